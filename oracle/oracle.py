@@ -1,0 +1,250 @@
+"""numpy/ctypes face of the CPU oracle.
+
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, ``__graft_entry__.smoke()`` and
+the CPU-baseline leg of bench.py, as the checker or the timed CPU baseline;
+never by the ye3t_b200 product path.
+
+``lib()`` loads the restatement (``ye3t_oracle.cpp``, built by ``make`` in this
+directory on first use); ``refcore()`` loads the reference's own runtime core
+compiled from its sources into ``_ref/`` (absent where the reference tree was
+not available at build time).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+_REF = None
+
+I64 = ctypes.c_int64
+VP = ctypes.c_void_p
+
+_DT = {np.dtype(np.float32): 0, np.dtype(np.float64): 1, np.dtype(np.complex64): 2,
+       np.dtype(np.complex128): 3}
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(VP)
+
+
+def build() -> str:
+    path = os.path.join(HERE, "_build", "libye3t_oracle.so")
+    src = os.path.join(HERE, "ye3t_oracle.cpp")
+    if not os.path.exists(path) or os.path.getmtime(path) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    return path
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        _LIB = ctypes.CDLL(build())
+        _LIB.yo_neighbor_list_bruteforce.restype = I64
+    return _LIB
+
+
+def refcore() -> Optional[ctypes.CDLL]:
+    """The reference core library, or None if it was not built."""
+    global _REF
+    if _REF is None:
+        path = os.path.join(HERE, "_ref", "libye3t_refcore.so")
+        if not os.path.exists(path):
+            return None
+        _REF = ctypes.CDLL(path)
+    return _REF
+
+
+def _c(a, dtype=None):
+    return np.ascontiguousarray(a if dtype is None else np.asarray(a, dtype=dtype))
+
+
+# -- schedule evaluation (factorized_runtime.cpp:252-287) -------------------
+def schedule_evaluate(block_values, component_offsets, component_label_index, block_m_indices, coeffs,
+                      component_count=None, threads=1):
+    bv = _c(block_values)
+    coeffs = _c(coeffs, bv.dtype)
+    off = _c(component_offsets, np.int64)
+    cli = _c(component_label_index, np.int64)
+    midx = _c(block_m_indices, np.int64)
+    comps = int(cli.shape[0]) if component_count is None else int(component_count)
+    batch, basis, blocks, mdim = bv.shape
+    out = np.zeros((batch, comps), dtype=bv.dtype)
+    lib().yo_factorized_schedule_evaluate(ctypes.c_int(_DT[bv.dtype]), _p(bv), I64(batch), I64(basis),
+                                          I64(blocks), I64(mdim), _p(off), _p(cli), _p(midx), _p(coeffs),
+                                          I64(comps), _p(out), ctypes.c_int(threads))
+    return out
+
+
+def schedule_evaluate_record(block_values, record, threads=1):
+    """Evaluate a ``ScheduleRecord`` with the reference's dtype rule (couplings.py:508-516)."""
+    bv = _c(block_values)
+    coeffs = record.coeffs
+    if not np.iscomplexobj(bv):
+        rc = record.real_coeffs()
+        if rc is None:
+            bv = bv.astype(np.complex128)
+        else:
+            coeffs = rc
+    return schedule_evaluate(bv, record.component_offsets, record.component_label_index,
+                             record.block_m_indices(), np.asarray(coeffs).astype(bv.dtype), threads=threads)
+
+
+# -- symmetric powers (ye3t_runtime_core.cpp:5279, :5392) -------------------
+def symmetric_power_monomial(x, monomial_counts, output_offsets, monomial_values):
+    x = _c(x)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    counts = _c(monomial_counts, np.int64)
+    off = _c(output_offsets, np.int64).reshape(-1)
+    vals = _c(monomial_values, x.dtype).reshape(-1)
+    out_dim = off.shape[0] - 1
+    out = np.zeros((x2.shape[0], out_dim), dtype=x.dtype)
+    lib().yo_symmetric_power_monomial(ctypes.c_int(_DT[x.dtype]), _p(x2), I64(x2.shape[0]), I64(x2.shape[1]),
+                                      _p(counts), _p(off), _p(vals), I64(out_dim), _p(out))
+    return out.reshape(*lead, out_dim)
+
+
+def symmetric_power_shared_monomial(x, monomial_counts, output_offsets, coefficient_terms, coefficient_values):
+    x = _c(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    counts = _c(monomial_counts, np.int64).reshape(-1, x.shape[-1])
+    off = _c(output_offsets, np.int64).reshape(-1)
+    terms = _c(coefficient_terms, np.int64)
+    vals = _c(coefficient_values, x.dtype)
+    out_dim = off.shape[0] - 1
+    out = np.zeros((x2.shape[0], out_dim), dtype=x.dtype)
+    lib().yo_symmetric_power_shared_monomial(ctypes.c_int(_DT[x.dtype]), _p(x2), I64(x2.shape[0]),
+                                             I64(x2.shape[1]), _p(counts), I64(counts.shape[0]), _p(off),
+                                             _p(terms), _p(vals), I64(out_dim), _p(out))
+    return out.reshape(*x.shape[:-1], out_dim)
+
+
+# -- edge tables (ye3t_runtime_core.cpp:320-392, 226-290, 843-948) ---------
+def radial_table(radii, cutoffs, lambdas, kmax):
+    r = _c(radii)
+    rc = _c(np.broadcast_to(cutoffs, r.shape), r.dtype)
+    lam = _c(np.broadcast_to(lambdas, r.shape), r.dtype)
+    E = r.shape[0]
+    val = np.zeros((E, kmax + 1), dtype=r.dtype)
+    der = np.zeros((E, kmax + 1), dtype=r.dtype)
+    lib().yo_cheb_exp_cos_radial_table(ctypes.c_int(_DT[r.dtype]), _p(r), _p(rc), _p(lam), I64(E), I64(kmax),
+                                       _p(val), _p(der))
+    return val, der
+
+
+def sh_table(vectors, lmax, real_output=False, epsilon=1e-12):
+    v = _c(vectors)
+    E = v.shape[0]
+    W = (lmax + 1) ** 2
+    dt = v.dtype if real_output else (np.complex128 if v.dtype == np.float64 else np.complex64)
+    val = np.zeros((E, W), dtype=dt)
+    der = np.zeros((E, W, 3), dtype=dt)
+    lib().yo_spherical_harmonics_table(ctypes.c_int(_DT[v.dtype]), _p(v), I64(E), I64(lmax),
+                                       ctypes.c_int(int(bool(real_output))), ctypes.c_double(epsilon),
+                                       _p(val), _p(der))
+    return val, der
+
+
+def density_accumulate(edge_values, centers, atom_count):
+    v = _c(edge_values)
+    c = _c(centers, np.int64)
+    E = v.shape[0]
+    C = int(np.prod(v.shape[1:])) if v.ndim > 1 else 1
+    out = np.zeros((atom_count,) + v.shape[1:], dtype=v.dtype)
+    lib().yo_density_accumulate(ctypes.c_int(_DT[v.dtype]), _p(v), _p(c), I64(E), I64(C), I64(atom_count), _p(out))
+    return out
+
+
+def density_accumulate_adjoint(atomic_adjoint, centers):
+    a = _c(atomic_adjoint)
+    c = _c(centers, np.int64)
+    C = int(np.prod(a.shape[1:]))
+    out = np.zeros((c.shape[0],) + a.shape[1:], dtype=a.dtype)
+    lib().yo_density_accumulate_adjoint(ctypes.c_int(_DT[a.dtype]), _p(a), _p(c), I64(c.shape[0]), I64(C), _p(out))
+    return out
+
+
+def neighbor_list(positions, box, cutoff):
+    pos = _c(positions, np.float64)
+    N = pos.shape[0]
+    cap = max(1024, N * 64)
+    while True:
+        off = np.zeros(N + 1, dtype=np.int64)
+        nbr = np.zeros(cap, dtype=np.int32)
+        disp = np.zeros((cap, 3), dtype=np.float64)
+        E = int(lib().yo_neighbor_list_bruteforce(_p(pos), I64(N), ctypes.c_double(box), ctypes.c_double(cutoff),
+                                                  _p(off), _p(nbr), _p(disp), I64(cap)))
+        if E >= 0:
+            return off, nbr[:E].copy(), disp[:E].copy()
+        cap *= 2
+
+
+def ace_density(disp, row_off, nbr, species, prefactor, nmax, lmax, cutoff, lam):
+    disp = _c(disp, np.float64)
+    off = _c(row_off, np.int64)
+    nbr = _c(nbr, np.int32)
+    sp = _c(species, np.int32)
+    pf = _c(prefactor, np.float64)
+    N = off.shape[0] - 1
+    A = np.zeros((N, nmax, (lmax + 1) ** 2), dtype=np.complex128)
+    lib().yo_ace_density(_p(disp), _p(off), _p(nbr), _p(sp), _p(pf), I64(N), I64(nmax), I64(lmax),
+                         ctypes.c_double(cutoff), ctypes.c_double(lam), _p(A))
+    return A
+
+
+# -- multi-word bundles ------------------------------------------------------
+def sym_block_values(bundle, A):
+    """``{(n, l, k, Lambda, mu): [N, 2 Lambda + 1]}`` for every symmetric block the bundle uses."""
+    out = {}
+    for key, table in bundle.sym_tables.items():
+        l, k, Lam, mu = key
+        for n in range(1, bundle.nmax + 1):
+            x = A[:, n - 1, l * l:(l + 1) * (l + 1)]
+            out[(n, l, k, Lam, mu)] = symmetric_power_monomial(x, table.monomial_counts, table.output_offsets,
+                                                               table.monomial_value.astype(A.dtype))
+    return out
+
+
+def bundle_word_block_values(bundle, w, A, sym=None):
+    """Block values ``[N, basis, B, mdim]`` of word ``w``, assembled as in workflows.py:636-661."""
+    rec = bundle.word_schedule(w)
+    mdim = rec.max_block_m_dim
+    N = A.shape[0]
+    bv = np.zeros((N, rec.basis_count, rec.block_count, mdim), dtype=A.dtype)
+    for a, label in enumerate(rec.block_specs):
+        for b, (kind, n, l, k, Lam, mu) in enumerate(label):
+            if kind == "sym":
+                if sym is not None and (n, l, k, Lam, mu) in sym:
+                    src = sym[(n, l, k, Lam, mu)]
+                else:
+                    t = bundle.sym_tables[(l, k, Lam, mu)]
+                    src = symmetric_power_monomial(A[:, n - 1, l * l:(l + 1) * (l + 1)], t.monomial_counts,
+                                                   t.output_offsets, t.monomial_value.astype(A.dtype))
+            else:
+                src = A[:, n - 1, l * l:(l + 1) * (l + 1)]
+            bv[:, a, b, :src.shape[1]] = src
+    return rec, bv
+
+
+def bundle_features(bundle, A, words=None, threads=1):
+    """Features ``[N, F]`` (words in bundle order, components in schedule order)."""
+    sym = sym_block_values(bundle, A)
+    outs = []
+    for w in (range(bundle.word_count) if words is None else words):
+        rec, bv = bundle_word_block_values(bundle, int(w), A, sym)
+        outs.append(schedule_evaluate_record(bv, rec, threads=threads))
+    return np.concatenate(outs, axis=1)
+
+
+def bundle_energy(bundle, A, species, weights, threads=1):
+    """Per-atom energies ``e_i = sum_f w[z_i, f] Re(B_if)``."""
+    B = bundle_features(bundle, A, threads=threads)
+    W = np.asarray(weights)[np.asarray(species)]
+    return (W * B.real).sum(axis=1)

@@ -1,0 +1,347 @@
+"""Generate the golden fixtures in this directory from the reference ye3t.
+
+Run only where the reference is importable and its torch-free runtime core has
+been compiled into oracle/_ref (``make -C oracle ref``):
+
+    PYTHONPATH=<ye3t checkout>:<this repo> python tests/golden/make_golden.py
+
+Every expected value below is produced by the reference's own public
+functions (cited per fixture); the inputs are seeded.  The GPU box never runs
+this script: tests read the committed ``.npz`` files.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+os.environ.setdefault("YE3T_ENABLE_CPP_RUNTIME_JIT", "1")
+os.environ.setdefault("TORCH_EXTENSIONS_DIR", os.path.join(REPO, "_work", "torch_ext"))
+
+from ye3t.couplings import compile_ace_factorized_schedules_by_L  # noqa: E402
+from ye3t import couplings  # noqa: E402
+from ye3t.runtime.execution_plan import (  # noqa: E402
+    cheb_exp_cos_radial_table_with_derivative, density_accumulate,
+    spherical_harmonics_table_with_derivative)
+from ye3t.runtime.symmetric_power import symmetric_power_product_plan_contraction  # noqa: E402
+
+from ye3t_b200.schedules import ACEBundle, ScheduleRecord  # noqa: E402
+
+REF_FIXTURE = os.path.join(os.environ.get("YE3T_REFERENCE", "/root/reference"), "tests", "fixtures",
+                           "shared_monomial_plan_v1.txt")
+
+
+def _record_arrays(prefix, rec: ScheduleRecord, out: dict):
+    out[prefix + "off"] = rec.component_offsets
+    out[prefix + "cli"] = rec.component_label_index
+    out[prefix + "bm"] = rec.block_m_tuples
+    out[prefix + "co"] = rec.coeffs
+    out[prefix + "bl"] = rec.block_L_by_label()
+    out[prefix + "specs"] = np.frombuffer(json.dumps(rec.block_specs).encode(), dtype=np.uint8)
+
+
+def schedules_fixture():
+    """``ACEFactorizedScheduleReport.evaluate`` (``couplings/__init__.py:2574``) on seeded blocks."""
+    cases = [((1, 1, 2), (1, 1, 0), 0), ((1, 1, 2), (1, 1, 0), 2), ((1, 1, 2, 3), (1, 1, 2, 2), 1),
+             ((1, 2, 3, 4), (3, 3, 3, 3), 0), ((1, 2, 3, 4), (3, 3, 3, 3), 2),
+             ((1, 1, 2, 2), (2, 2, 3, 3), 4), ((1, 1, 1, 1), (3, 3, 3, 3), 6),
+             ((1, 2, 2, 3), (0, 1, 2, 3), 0)]
+    out, meta = {}, []
+    g = torch.Generator().manual_seed(2026)
+    for i, (content, ls, L) in enumerate(cases):
+        rep = compile_ace_factorized_schedules_by_L(content=content, input_Ls=ls)
+        sched = rep.schedules_by_L[L]
+        rec = ScheduleRecord.from_schedule(sched, rep.convention_hash)
+        batch = 7
+        mdim = rec.max_block_m_dim
+        bl = rec.block_L_by_label()
+        re = torch.randn(batch, rec.basis_count, rec.block_count, mdim, dtype=torch.float64, generator=g)
+        im = torch.randn(batch, rec.basis_count, rec.block_count, mdim, dtype=torch.float64, generator=g)
+        mask = torch.zeros(rec.basis_count, rec.block_count, mdim, dtype=torch.bool)
+        for a in range(rec.basis_count):
+            for b in range(rec.block_count):
+                mask[a, b, : 2 * bl[a, b] + 1] = True
+        bv_c = torch.complex(re, im) * mask
+        bv_r = re * mask
+        outc_cpp = rep.evaluate(bv_c, target_L=L, backend="cpp")
+        outc_torch = rep.evaluate(bv_c, target_L=L, backend="torch")
+        outr_cpp = rep.evaluate(bv_r, target_L=L, backend="cpp")
+        bv_f = bv_r.to(torch.float32)
+        outf_cpp = rep.evaluate(bv_f, target_L=L, backend="cpp")
+        p = f"s{i}_"
+        _record_arrays(p, rec, out)
+        out[p + "bvc"] = bv_c.numpy()
+        out[p + "bvr"] = bv_r.numpy()
+        out[p + "outc_cpp"] = outc_cpp.numpy()
+        out[p + "outc_torch"] = outc_torch.numpy()
+        out[p + "outr_cpp"] = outr_cpp.numpy()
+        out[p + "outf_cpp"] = outf_cpp.numpy()
+        meta.append({"content": content, "input_Ls": ls, "L": L, "convention_hash": rep.convention_hash,
+                     "basis_count": rec.basis_count, "component_count": rec.component_count,
+                     "term_count": rec.term_count, "block_count": rec.block_count})
+    out["meta"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+    np.savez_compressed(os.path.join(HERE, "schedules.npz"), **out)
+    print("schedules.npz", len(cases), "cases")
+
+
+def quickstart_fixture():
+    """Config C1: README quickstart schedule applied to seeded factor arrays.
+
+    Block assembly follows ``ye3t/workflows.py:636-661``: channel ``(n, l)``
+    is ``multiplets[l][..., n-1, :]``; symmetric blocks go through
+    ``symmetric_power_product_plan_contraction`` with the plan built as in
+    ``workflows.py:544-556``.
+    """
+    rep = compile_ace_factorized_schedules_by_L(content=(1, 1, 2), input_Ls=(1, 1, 0))
+    g = torch.Generator().manual_seed(0)
+    A1 = torch.randn(4096, 8, 3, dtype=torch.float64, generator=g)
+    A0 = torch.randn(4096, 8, 1, dtype=torch.float64, generator=g)
+    multiplets = {1: A1, 0: A0}
+    sched = rep.schedules_by_L[0]
+    width = 2 * int(sched.block_L_by_label().max()) + 1
+    rows, prepared = [], {}
+    for blocks in sched.block_specs:
+        row = []
+        for block in blocks:
+            key = (block["n"], block["l"], block.get("k_b"), block.get("Lambda"), block.get("multiplicity_index"))
+            if key not in prepared:
+                src = multiplets[block["l"]][..., block["n"] - 1, :]
+                if block["kind"] == "sym":
+                    plan = couplings.symmetric_power_product_plan(
+                        [{"descriptor_index": m, "power": block["k_b"], "input_L": block["l"],
+                          "output_L": block["Lambda"], "multiplicity_index": block["multiplicity_index"],
+                          "component_index": m, "channel_indices": tuple(range(2 * block["l"] + 1))}
+                         for m in range(2 * block["Lambda"] + 1)],
+                        descriptor_count=2 * block["Lambda"] + 1, channel_count=2 * block["l"] + 1,
+                        basis_convention="complex_magnetic")
+                    src = symmetric_power_product_plan_contraction(src, plan)
+                prepared[key] = torch.nn.functional.pad(src, (0, width - src.shape[-1]))
+            row.append(prepared[key])
+        rows.append(torch.stack(row, dim=-2))
+    bv = torch.stack(rows, dim=-3)
+    out_cpp = rep.evaluate(bv, target_L=0, backend="cpp")
+    out_torch = rep.evaluate(bv, target_L=0, backend="torch")
+    rec = ScheduleRecord.from_schedule(sched, rep.convention_hash)
+    # A1/A0 are regenerated by the tests from the same seed; the first rows
+    # are kept to confirm the regeneration.
+    arrays = {"A1_head": A1[:16].numpy(), "A0_head": A0[:16].numpy(), "bv": bv.numpy(), "out_cpp": out_cpp.numpy(),
+              "out_torch": out_torch.numpy()}
+    _record_arrays("q_", rec, arrays)
+    arrays["convention_hash"] = np.frombuffer(rep.convention_hash.encode(), dtype=np.uint8)
+    np.savez_compressed(os.path.join(HERE, "quickstart.npz"), **arrays)
+    print("quickstart.npz hash", rep.convention_hash, "out[:3]", out_cpp[:3].flatten())
+
+
+def sympow_fixture():
+    """Each symmetric block kind of the nu<=4 bundle through ``symmetric_power_product_plan_contraction``."""
+    bundle = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu4_L0.npz"))
+    g = torch.Generator().manual_seed(7)
+    out = {}
+    keys = sorted(bundle.sym_tables)
+    for j, key in enumerate(keys):
+        l, k, Lam, mu = key
+        plan = couplings.symmetric_power_product_plan(
+            [{"descriptor_index": m, "power": k, "input_L": l, "output_L": Lam, "multiplicity_index": mu,
+              "component_index": m, "channel_indices": tuple(range(2 * l + 1))} for m in range(2 * Lam + 1)],
+            descriptor_count=2 * Lam + 1, channel_count=2 * l + 1, basis_convention="complex_magnetic")
+        x = torch.complex(torch.randn(33, 2 * l + 1, dtype=torch.float64, generator=g),
+                          torch.randn(33, 2 * l + 1, dtype=torch.float64, generator=g))
+        y = symmetric_power_product_plan_contraction(x, plan)
+        out[f"k{j}_x"] = x.numpy()
+        out[f"k{j}_y"] = y.numpy()
+        out[f"k{j}_key"] = np.asarray(key, dtype=np.int64)
+    # The reference's pinned shared-monomial fixture (real-tesseral, float64),
+    # read as text from its test tree.
+    fx = {}
+    with open(REF_FIXTURE) as fh:
+        for line in fh:
+            parts = line.split()
+            if not parts or parts[0] == "end":
+                continue
+            fx[parts[0]] = parts[1:]
+    for name in ("monomial_counts", "output_offsets", "coefficient_terms", "coefficient_outputs"):
+        out["fx_" + name] = np.asarray([int(v) for v in fx[name][1:]], dtype=np.int64)
+    for name in ("coefficient_values", "input", "expected_output"):
+        out["fx_" + name] = np.asarray([float(v) for v in fx[name][1:]], dtype=np.float64)
+    for name in ("batch_size", "input_dimension", "monomial_count", "output_dimension"):
+        out["fx_" + name] = np.asarray(int(fx[name][0]))
+    out["fx_convention_hash"] = np.frombuffer(fx["convention_hash"][0].encode(), dtype=np.uint8)
+    np.savez_compressed(os.path.join(HERE, "sympow.npz"), **out)
+    print("sympow.npz", len(keys), "kinds + reference fixture", fx["convention_hash"][0])
+
+
+def load_refcore():
+    path = os.path.join(REPO, "oracle", "_ref", "libye3t_refcore.so")
+    if not os.path.exists(path):
+        raise SystemExit("build the reference core first: make -C oracle ref")
+    return ctypes.CDLL(path)
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def radial_sh_density_fixture():
+    """Radial table (``execution_plan.py:7298``), harmonics (``:7479``) and density (``:7913``)."""
+    ref = load_refcore()
+    rng = np.random.default_rng(11)
+    E = 257
+    radii = np.concatenate([rng.uniform(0.0, 6.0, E - 5), [0.0, 5.0, 5.0 - 1e-12, 5.0 + 1e-12, 2.5]])
+    rc = np.full(E, 5.0)
+    lam = np.full(E, 5.0)
+    kmax = 12
+    val_t, der_t = cheb_exp_cos_radial_table_with_derivative(torch.tensor(radii), torch.tensor(rc),
+                                                             torch.tensor(lam), kmax, backend="reference")
+    val_n = np.zeros((E, kmax + 1))
+    der_n = np.zeros((E, kmax + 1))
+    ref.yr_cheb_exp_cos_radial_table_f64(_p(radii), _p(rc), _p(lam), ctypes.c_int64(E), ctypes.c_int64(kmax),
+                                         _p(val_n), _p(der_n), ctypes.c_int(1))
+    vec = rng.normal(size=(E, 3)) * rng.uniform(0.2, 5.0, size=(E, 1))
+    vec[0] = [0.0, 0.0, 1.3]
+    vec[1] = [0.0, 0.0, -0.7]
+    vec[2] = [0.0, 0.0, 0.0]
+    vec[3] = [1.2, -0.7, 0.5]
+    vec[4] = [-0.4, 0.9, 0.0]
+    vec[5] = [1e-13, 0.0, 0.0]
+    lmax = 4
+    W = (lmax + 1) ** 2
+    shr_v = np.zeros((E, W)); shr_d = np.zeros((E, W, 3))
+    ref.yr_real_spherical_harmonics_table_f64(_p(vec), ctypes.c_int64(E), ctypes.c_int64(lmax), ctypes.c_double(1e-12),
+                                              _p(shr_v), _p(shr_d), ctypes.c_int(1))
+    shc_v = np.zeros((E, W), dtype=np.complex128); shc_d = np.zeros((E, W, 3), dtype=np.complex128)
+    ref.yr_complex_spherical_harmonics_table_f64(_p(vec), ctypes.c_int64(E), ctypes.c_int64(lmax),
+                                                 ctypes.c_double(1e-12), _p(shc_v), _p(shc_d), ctypes.c_int(1))
+    tv = torch.tensor(vec[6:])
+    shc_t, shc_td = spherical_harmonics_table_with_derivative(tv, lmax, real_output=False, backend="reference")
+    shr_t, shr_td = spherical_harmonics_table_with_derivative(tv, lmax, real_output=True, backend="reference")
+    # density accumulation with the reference test's fixed centres
+    # (tests/test_execution_plan_native.py:1521-1540).
+    centers = np.asarray([0, 0, 2, 1, 2, 2, 3, 0, 3], dtype=np.int64)
+    g = torch.Generator().manual_seed(3)
+    ev_r = torch.randn(9, 7, dtype=torch.float64, generator=g)
+    ev_c = torch.complex(torch.randn(9, 7, dtype=torch.float64, generator=g),
+                         torch.randn(9, 7, dtype=torch.float64, generator=g))
+    acc_r = density_accumulate(ev_r, torch.tensor(centers), 4, backend="reference")
+    acc_c = density_accumulate(ev_c, torch.tensor(centers), 4, backend="reference")
+    np.savez_compressed(os.path.join(HERE, "edge_ops.npz"), radii=radii, rc=rc, lam=lam, kmax=np.asarray(kmax),
+                        rad_val_native=val_n, rad_der_native=der_n, rad_val_torch=val_t.detach().numpy(),
+                        rad_der_torch=der_t.detach().numpy(), vec=vec, lmax=np.asarray(lmax),
+                        shr_val_native=shr_v, shr_der_native=shr_d, shc_val_native=shc_v, shc_der_native=shc_d,
+                        shc_val_torch=shc_t.detach().numpy(), shc_der_torch=shc_td.detach().numpy(),
+                        shr_val_torch=shr_t.detach().numpy(), shr_der_torch=shr_td.detach().numpy(), centers=centers, ev_r=ev_r.numpy(), ev_c=ev_c.numpy(),
+                        acc_r=acc_r.numpy(), acc_c=acc_c.numpy())
+    print("edge_ops.npz")
+
+
+def minimum_image_csr(pos, box, rc):
+    N = pos.shape[0]
+    d = pos[None, :, :] - pos[:, None, :]
+    d -= box * np.round(d / box)
+    r2 = (d ** 2).sum(-1)
+    mask = (r2 <= rc * rc) & ~np.eye(N, dtype=bool)
+    rows, cols = np.nonzero(mask)
+    off = np.zeros(N + 1, dtype=np.int64)
+    np.add.at(off, rows + 1, 1)
+    off = np.cumsum(off)
+    return off, cols.astype(np.int32), d[rows, cols]
+
+
+def ace_fixture():
+    """A small periodic system through the reference ops and per-word schedules.
+
+    A-basis: reference radial table x complex harmonics x neighbour-species
+    prefactor, accumulated by ``density_accumulate``.  B-basis: for each word,
+    ``compile_ace_factorized_schedules_by_L`` on the word itself and the block
+    assembly of ``workflows.py:636-661``, evaluated with ``backend="cpp"``.
+    """
+    N, density, rc, lam, nmax, lmax = 96, 0.05, 5.0, 5.0, 8, 3
+    box = (N / density) ** (1.0 / 3.0)
+    pos = torch.rand(N, 3, dtype=torch.float64, generator=torch.Generator().manual_seed(0)).numpy() * box
+    species = torch.randint(0, 3, (N,), generator=torch.Generator().manual_seed(1)).numpy().astype(np.int32)
+    prefactor = np.asarray([1.0, 0.75, 1.25])
+    off, nbr, disp = minimum_image_csr(pos, box, rc)
+    E = nbr.shape[0]
+    r = np.sqrt((disp ** 2).sum(-1))
+    Rv, _ = cheb_exp_cos_radial_table_with_derivative(torch.tensor(r), torch.full((E,), rc), torch.full((E,), lam),
+                                                       nmax, backend="reference")
+    ref = load_refcore()
+    W = (lmax + 1) ** 2
+    Yv = np.zeros((E, W), dtype=np.complex128); Yd = np.zeros((E, W, 3), dtype=np.complex128)
+    ref.yr_complex_spherical_harmonics_table_f64(_p(np.ascontiguousarray(disp)), ctypes.c_int64(E),
+                                                 ctypes.c_int64(lmax), ctypes.c_double(1e-12), _p(Yv), _p(Yd),
+                                                 ctypes.c_int(1))
+    Rv = Rv.detach()
+    p = torch.tensor(prefactor[species[nbr]])
+    edge = (p[:, None, None] * Rv[:, 1:, None]).to(torch.complex128) * torch.tensor(Yv)[:, None, :]
+    centers = torch.tensor(np.repeat(np.arange(N), np.diff(off)))
+    A = density_accumulate(edge.reshape(E, -1), centers, N, backend="reference").reshape(N, nmax, W)
+    multiplets = {l: A[:, :, l * l:(l + 1) * (l + 1)] for l in range(lmax + 1)}
+
+    def word_features(words):
+        feats = []
+        for word in words:
+            rep = compile_ace_factorized_schedules_by_L(content=tuple(n for _, n in word),
+                                                        input_Ls=tuple(l for l, _ in word))
+            sched = rep.schedules_by_L[0]
+            width = 2 * int(sched.block_L_by_label().max()) + 1
+            rows, prepared = [], {}
+            for blocks in sched.block_specs:
+                row = []
+                for block in blocks:
+                    key = (block["n"], block["l"], block.get("k_b"), block.get("Lambda"),
+                           block.get("multiplicity_index"))
+                    if key not in prepared:
+                        src = multiplets[block["l"]][..., block["n"] - 1, :]
+                        if block["kind"] == "sym":
+                            plan = couplings.symmetric_power_product_plan(
+                                [{"descriptor_index": m, "power": block["k_b"], "input_L": block["l"],
+                                  "output_L": block["Lambda"], "multiplicity_index": block["multiplicity_index"],
+                                  "component_index": m, "channel_indices": tuple(range(2 * block["l"] + 1))}
+                                 for m in range(2 * block["Lambda"] + 1)],
+                                descriptor_count=2 * block["Lambda"] + 1, channel_count=2 * block["l"] + 1,
+                                basis_convention="complex_magnetic")
+                            src = symmetric_power_product_plan_contraction(src, plan)
+                        prepared[key] = torch.nn.functional.pad(src, (0, width - src.shape[-1]))
+                    row.append(prepared[key])
+                rows.append(torch.stack(row, dim=-2))
+            bv = torch.stack(rows, dim=-3)
+            feats.append(rep.evaluate(bv, target_L=0, backend="cpp"))
+        return torch.cat(feats, dim=1).numpy()
+
+    b3 = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu3_L0.npz"))
+    B3 = word_features(b3.words)
+    b4 = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu4_L0.npz"))
+    sample = np.arange(0, b4.word_count, 23, dtype=np.int64)
+    B4 = word_features([b4.words[int(w)] for w in sample])
+    rng = np.random.default_rng(2)
+    w3 = rng.normal(size=(3, B3.shape[1])) / np.sqrt(B3.shape[1])
+    energy3 = float(sum(np.dot(w3[species[i]], B3[i].real) for i in range(N)))
+    np.savez_compressed(os.path.join(HERE, "ace_small.npz"), pos=pos, box=np.asarray(box), species=species,
+                        prefactor=prefactor, rc=np.asarray(rc), lam=np.asarray(lam), nmax=np.asarray(nmax),
+                        lmax=np.asarray(lmax), row_off=off, nbr=nbr, disp=disp, A=A.numpy(), B3=B3[:40],
+                        B4=B4[:40], B4_words=sample, w3=w3, energy3=np.asarray(energy3))
+    # Features of the first 40 atoms are stored; the energy covers all atoms.
+    print("ace_small.npz N", N, "E", E, "B3", B3.shape, "B4", B4.shape, "energy3", energy3)
+
+
+if __name__ == "__main__":
+    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace"]
+    if "schedules" in which:
+        schedules_fixture()
+    if "quickstart" in which:
+        quickstart_fixture()
+    if "sympow" in which:
+        sympow_fixture()
+    if "edge" in which:
+        radial_sh_density_fixture()
+    if "ace" in which:
+        ace_fixture()
