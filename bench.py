@@ -1,0 +1,363 @@
+#!/usr/bin/env python
+"""ACE features atoms/s at nu <= 4, l_max = 3 on 1..8 B200 (config C5 of the build spec).
+
+One step = the whole hot path for one configuration of 2^20 atoms (periodic
+cubic box at 0.05 atoms/A^3, 3 species, n_max 8, l_max 3, cutoff 5 A):
+cell-list CSR neighbour list -> A-basis density (kernel 1) -> block pool with
+every symmetric block -> all 25,328 nu <= 4 words / 41,168 L = 0 features per
+atom evaluated from their compiled schedules and contracted with a per-species
+linear readout (kernel 2) -> total energy (NCCL all-reduce when N > 1).
+Atoms are block-partitioned across ranks (strong scaling of the fixed system).
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU
+path instead (the oracle restatement; see the cpu_baseline description).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "ACE features atoms/sec at nu=4,l_max=3"
+DENSITY = 0.05
+CUTOFF = 5.0
+LAMBDA = 5.0
+PREFACTOR = [1.0, 0.75, 1.25]
+SPECIES = 3
+BUNDLE = "ace_n8_l3_nu4_L0"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--atoms", type=int, default=1 << 20)
+    ap.add_argument("--bundle", default=BUNDLE)
+    ap.add_argument("--cpu-sample", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def make_system(N):
+    import torch
+    box = (N / DENSITY) ** (1.0 / 3.0)
+    pos = torch.rand(N, 3, dtype=torch.float64, generator=torch.Generator().manual_seed(0)) * box
+    species = torch.randint(0, SPECIES, (N,), generator=torch.Generator().manual_seed(1)).to(torch.int32)
+    return pos, species, box
+
+
+def make_weights(F):
+    import torch
+    return torch.randn(SPECIES, F, dtype=torch.float64, generator=torch.Generator().manual_seed(2)) / F ** 0.5
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                    power.append(float(parts[3]))
+                except ValueError:
+                    continue
+                for name, flag in zip(names, parts[5:9]):
+                    if flag.lower().startswith("active"):
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def measure_fp64_peak(torch, nat, device):
+    """FP64 FMA throughput of this GPU (TFLOP/s), best of 5 launches."""
+    blocks, threads, iters = 148 * 8, 256, 40000
+    sink = torch.empty(blocks * threads, dtype=torch.float64, device=device)
+    flops = nat.DBL(0.0)
+    s = nat.stream_of(device)
+    best = 0.0
+    for _ in range(6):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        nat.check(nat.lib().y3b_fma_peak_launch(nat.F64, blocks, threads, iters, sink.data_ptr(),
+                                                 nat.ctypes.byref(flops), s), "fma_peak")
+        b.record()
+        b.synchronize()
+        best = max(best, flops.value / (a.elapsed_time(b) * 1e-3) / 1e12)
+    return best
+
+
+def cpu_baseline(sample_atoms, bundle_stem):
+    """The reference CPU path restated (oracle) on a bounded sample, all host cores."""
+    import numpy as np
+
+    from oracle import oracle
+    from ye3t_b200.schedules import ACEBundle
+    cores = len(os.sched_getaffinity(0))
+    b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", bundle_stem + ".npz"))
+    M = int(sample_atoms)
+    rng = np.random.default_rng(0)
+    box = (M / DENSITY) ** (1 / 3)
+    pos = rng.uniform(0, box, (M, 3))
+    sp = rng.integers(0, SPECIES, M).astype(np.int32)
+    w = np.random.default_rng(2).normal(size=(SPECIES, 41168 if bundle_stem == BUNDLE else b.feature_count))
+    t0 = time.perf_counter()
+    off, nbr, disp = oracle.neighbor_list(pos, box, CUTOFF)
+    A = oracle.ace_density(disp, off, nbr, sp, np.asarray(PREFACTOR), b.nmax, b.lmax, CUTOFF, LAMBDA)
+    e = oracle.bundle_energy(b, A, sp, w, threads=cores)
+    dt = time.perf_counter() - t0
+    assert np.isfinite(e).all()
+    return {"value": M / dt, "unit": "atoms/s", "cores": cores, "kind": "port",
+            "sample": f"{M} atoms of the same density/species/cutoff in a {box:.1f} A periodic box; brute-force "
+                      f"neighbour list, A-basis, then per word the reference block assembly (workflows.py:636-661) "
+                      f"and schedule evaluation (factorized_runtime.cpp:252-287 restated, {cores} threads); "
+                      f"{dt:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    K, W = args.steps, args.warmup
+    base = None
+    times = []
+    for i in range(W + K):
+        cb = cpu_baseline(args.cpu_sample, args.bundle)
+        if i >= W:
+            times.append(cb)
+        base = cb
+    vals = [t["value"] for t in times]
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": args.gpus,
+            "steps": K, "warmup": W, "ms_per_step": 1e3 * args.cpu_sample / value,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "config": _config(args),
+            "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": base["cores"], "kind": "port",
+                             "sample": base["sample"]},
+            "e2e": {"value": value, "unit": "atoms/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _config(args):
+    return {"workload": "C5 scalar ACE energy: 2^20 atoms (periodic cubic box, 0.05/A^3, 3 species), "
+                        "n_max 8, l_max 3, nu<=4 (25,328 words / 41,168 L=0 features), fp64, per-species "
+                        "linear readout; forces not included",
+            "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
+            "parallelism": f"atom-block x{args.gpus}", "l2": "inputs larger than L2 (block pool >> 126 MB)"}
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from ye3t_b200 import _native as nat
+    from ye3t_b200.ace import ACEConfig, ACEEvaluator
+    from ye3t_b200.schedules import ACEBundle
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    N = int(args.atoms)
+    pos, species, box = make_system(N)
+    bundle = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", args.bundle + ".npz"))
+    weights = make_weights(bundle.feature_count)
+    ev = ACEEvaluator(bundle, device, config=ACEConfig(CUTOFF, LAMBDA), species_prefactor=PREFACTOR,
+                      weights=weights)
+    begin, end = (N * rank) // world, (N * (rank + 1)) // world
+    n_local = end - begin
+    pos_h = pos.pin_memory()
+    sp_h = species.pin_memory()
+    pos_d = pos.to(device)
+    sp_d = species.to(device)
+    pool_buf = torch.empty((ev.packed.pool_size, n_local), dtype=torch.complex128, device=device)
+    e_buf = torch.empty(n_local, dtype=torch.float64, device=device)
+    timers = {k: [] for k in ("neighbors", "density", "pool", "energy")}
+    launches_per_step = 10  # our kernels: 6 neighbour-count, 1 fill, density, pool, energy
+
+    def step(record):
+        ev_marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+        if record:
+            ev_marks[0].record()
+        row, nbr = ev.neighbor_list(pos_d, box, begin, end)
+        if record:
+            ev_marks[1].record()
+        A = ev.density(pos_d, sp_d, box, row, nbr, begin)
+        if record:
+            ev_marks[2].record()
+        pool = ev.pool(A, out=pool_buf)
+        if record:
+            ev_marks[3].record()
+        e_at = ev.energy_from_pool(pool, sp_d[begin:end], out=e_buf)
+        if record:
+            ev_marks[4].record()
+        total = e_at.sum()
+        if world > 1:
+            dist.all_reduce(total)
+        return total, ev_marks
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step(False)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = []
+    t0.record()
+    for _ in range(args.steps):
+        total, m = step(True)
+        marks.append(m)
+    t1.record()
+    barrier()
+    clock_info = clocks.stop()
+    dev_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    for m in marks:
+        for k, (a, b) in zip(timers, zip(m[:-1], m[1:])):
+            timers[k].append(a.elapsed_time(b))
+    energy = float(total.item())
+
+    # end to end through the public API with host buffers: H2D of positions
+    # and species every step, D2H of the total energy
+    for _ in range(max(1, args.warmup // 2)):
+        pos_d.copy_(pos_h, non_blocking=True)
+        sp_d.copy_(sp_h, non_blocking=True)
+        step(False)[0].to("cpu", non_blocking=False)
+    host_total = torch.empty(1, dtype=torch.float64).pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        pos_d.copy_(pos_h, non_blocking=True)
+        sp_d.copy_(sp_h, non_blocking=True)
+        tot, _ = step(False)
+        host_total.copy_(tot.reshape(1), non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    peak = measure_fp64_peak(torch, nat, device)
+    flops = ev.packed.flops_per_atom()
+    energy_ms = statistics.mean(timers["energy"])
+    sched_flops_launch = (flops["schedule"] + 2.0 * ev.feature_count) * n_local
+    achieved = sched_flops_launch / (energy_ms * 1e-3) / 1e12
+    W = (bundle.lmax + 1) ** 2
+    dens_ms = statistics.mean(timers["density"])
+    avg_deg = float(0.05 * 4.0 / 3.0 * 3.141592653589793 * CUTOFF ** 3)
+    dens_bytes_atom = 3 * 8 + 4 + 8 + 4 * avg_deg + bundle.nmax * W * 16
+    dens_gbs = dens_bytes_atom * n_local / (dens_ms * 1e-3) / 1e9
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
+            hbm_peak = float(json.load(fh)["hbm_gbs"])
+        hbm_src = "MEASURED_PEAKS.json hbm_gbs (measured copy)"
+    except (OSError, KeyError, ValueError):
+        hbm_peak, hbm_src = 6650.0, "fallback 6.65 TB/s"
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "ace_energy_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as fh:
+            t = json.load(fh)
+        traffic = t.get("dram_bytes_per_atom", 0) * n_local or None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_sample, args.bundle)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = N / (dev_ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded uniform positions, random readout)",
+        "config": _config(args),
+        "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
+                "d2h_bytes_per_step": 8},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "fp64", "kernel": "ace_eval_kernel<1> (B-basis energy)", "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                     "flops_per_launch": sched_flops_launch,
+                     "peak_source": "FP64 FMA microbenchmark (y3b_fma_peak_launch) measured in this run; "
+                                    "MEASURED_PEAKS.json has no FP64 figure"},
+        "roofline_density": {"bound": "hbm", "kernel": "ace_density_kernel<3>", "achieved": dens_gbs,
+                             "peak": hbm_peak, "unit": "GB/s", "frac": dens_gbs / hbm_peak,
+                             "bytes_per_atom": dens_bytes_atom, "peak_source": hbm_src},
+        "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
+        "energy_total": energy,
+        "clocks": clock_info,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,220 @@
+/*
+ * ye3t_b200: C ABI of the B200 (sm_100a) evaluator for ye3t's compiled ACE
+ * feature path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*), launches asynchronously on that stream and
+ * returns Y3B_OK or a negative error code; y3b_last_error() gives the message
+ * (thread-local).  Nothing here allocates device memory: callers pass outputs
+ * and, where an operation needs scratch, a workspace sized by the matching
+ * *_workspace_bytes() query.  Arrays are C-contiguous.  Complex arrays are
+ * interleaved (re, im) pairs, the layout of std::complex / numpy / torch.
+ *
+ * Each entry point cites the reference interface (file:line inside the ye3t
+ * project) that it replaces.
+ */
+#ifndef YE3T_B200_H
+#define YE3T_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Y3B_ABI_VERSION 1
+
+/* dtype codes */
+#define Y3B_F32 0
+#define Y3B_F64 1
+#define Y3B_C64 2
+#define Y3B_C128 3
+
+/* status codes */
+#define Y3B_OK 0
+#define Y3B_ERR_ARGUMENT (-1)
+#define Y3B_ERR_CUDA (-2)
+#define Y3B_ERR_WORKSPACE (-3)
+#define Y3B_ERR_UNSUPPORTED (-4)
+
+/* device status word bits written by kernels that detect bad input */
+#define Y3B_STATUS_INDEX_RANGE 1
+#define Y3B_STATUS_CAPACITY 2
+
+/* ABI version; the reference's gate is core_abi_version()
+ * (ye3t/runtime/csrc/execution_plan_torch.cpp:7925, checked at
+ * ye3t/runtime/execution_plan.py:253-291). */
+int32_t y3b_abi_version(void);
+const char* y3b_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Factorized coefficient schedule evaluation.
+ * Replaces evaluate_factorized_schedule_cpu
+ * (ye3t/core/csrc/factorized_runtime.cpp:426-548) and the torch
+ * gather/index_add path of evaluate_factorized_schedule_torch
+ * (ye3t/core/couplings.py:481-567):
+ *   out[b, c] = sum_{t in [off[c], off[c+1])} coeffs[t] *
+ *               prod_j block_values[b, label[c], j, m_idx[t, j]]
+ * block_values [batch, basis, blocks, mdim]; block_m_indices [terms, blocks]
+ * (int64, m + L_block); coeffs and out share dtype.  Out-of-range labels or m
+ * indices set Y3B_STATUS_INDEX_RANGE in *status (nullable) and contribute 0.
+ * ---------------------------------------------------------------------- */
+int y3b_factorized_schedule_evaluate(int dtype, const void* block_values, int64_t batch,
+                                     int64_t basis_count, int64_t block_count, int64_t magnetic_dim,
+                                     const int64_t* component_offsets,
+                                     const int64_t* component_label_index,
+                                     const int64_t* block_m_indices, const void* coeffs,
+                                     int64_t component_count, int64_t term_count, void* out,
+                                     int32_t* status, void* stream);
+
+/* Symmetric-power monomial contraction, grouped table.
+ * Replaces ye3t_runtime::symmetric_power_monomial
+ * (ye3t/runtime/csrc/execution_plan_torch.cpp:7528; CPU core
+ * ye3t_runtime_core.cpp:5279):
+ *   out[b, o] = sum_{t in [off[o], off[o+1])} values[t] prod_i x[b, i]^counts[t, i] */
+int y3b_symmetric_power_monomial(int dtype, const void* input, int64_t batch, int64_t input_dim,
+                                 const int64_t* monomial_counts, const int64_t* output_offsets,
+                                 const void* monomial_values, int64_t term_count,
+                                 int64_t output_dim, void* out, void* stream);
+
+/* ChebExpCos radial table with d/dr, radial indices 0..maximum_radial_index.
+ * Replaces ye3t_runtime::cheb_exp_cos_radial_table_with_derivative
+ * (ye3t/runtime/csrc/execution_plan_torch.cpp:7238). Real dtypes only. */
+int y3b_cheb_exp_cos_radial_table(int dtype, const void* radii, const void* cutoffs,
+                                  const void* lambdas, int64_t edge_count,
+                                  int64_t maximum_radial_index, void* values, void* derivatives,
+                                  void* stream);
+
+/* Packed spherical-harmonic table (all l <= lmax, columns [l^2, (l+1)^2))
+ * with Cartesian derivatives [E, W, 3].  Real tesseral when real_output != 0,
+ * else complex Condon-Shortley (values/derivatives then complex of the same
+ * precision).  Replaces ye3t_runtime::spherical_harmonics_table_with_derivative
+ * (ye3t/runtime/csrc/execution_plan_torch.cpp:7251). dtype is the real type
+ * of edge_vectors. */
+int y3b_spherical_harmonics_table(int dtype, const void* edge_vectors, int64_t edge_count,
+                                  int64_t maximum_angular_momentum, int real_output,
+                                  double epsilon, void* values, void* derivatives, void* stream);
+
+/* Density accumulation A[centers[e], c] += edge_values[e, c] without global
+ * floating-point atomics: centres are bucketed into CSR rows (integer
+ * counting), each row is ordered by edge index, and every output row is
+ * summed by one warp in edge order (deterministic).
+ * Replaces ye3t_runtime::density_accumulate
+ * (ye3t/runtime/csrc/execution_plan_torch.cpp:7285; CUDA atomics kernel
+ * execution_plan_cuda.cu:281). */
+int64_t y3b_density_accumulate_workspace_bytes(int64_t edge_count, int64_t atom_count);
+int y3b_density_accumulate(int dtype, const void* edge_values, const int64_t* centers,
+                           int64_t edge_count, int64_t channel_count, int64_t atom_count,
+                           void* workspace, int64_t workspace_bytes, void* out, int32_t* status,
+                           void* stream);
+
+/* CSR form: row i sums edges [row_offsets[i], row_offsets[i+1]) in order;
+ * edge_order (nullable) maps CSR slots to edge rows of edge_values. */
+int y3b_density_accumulate_csr(int dtype, const void* edge_values, const int64_t* row_offsets,
+                               const int64_t* edge_order, int64_t atom_count,
+                               int64_t channel_count, void* out, void* stream);
+
+/* edge_adjoint[e, c] = atomic_adjoint[centers[e], c].
+ * Replaces ye3t_runtime::density_accumulate_adjoint
+ * (execution_plan_torch.cpp, schema next to :7285; CUDA
+ * execution_plan_cuda.cu:9241). */
+int y3b_density_accumulate_adjoint(int dtype, const void* atomic_adjoint, const int64_t* centers,
+                                   int64_t edge_count, int64_t channel_count, int64_t atom_count,
+                                   void* edge_adjoint, int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Periodic cubic-box neighbour list (cell list) in CSR form for centres
+ * [center_begin, center_end).  The reference has no neighbour-list code; this
+ * builds the sorted CSR layout the A-basis kernel consumes.  Two passes:
+ * y3b_neighbor_count writes per-centre counts into row_offsets[1..] and the
+ * exclusive scan into row_offsets (row_offsets[0] = 0); the caller reads
+ * row_offsets[count] for the edge total, then y3b_neighbor_fill writes
+ * neighbour indices (int32), each row sorted by neighbour index.  Both
+ * passes need the cell-list workspace built by the first.
+ * ---------------------------------------------------------------------- */
+int64_t y3b_neighbor_workspace_bytes(int64_t atom_count, double box, double cutoff);
+int y3b_neighbor_count(const double* positions, int64_t atom_count, int64_t center_begin,
+                       int64_t center_end, double box, double cutoff, void* workspace,
+                       int64_t workspace_bytes, int64_t* row_offsets, void* stream);
+int y3b_neighbor_fill(const double* positions, int64_t atom_count, int64_t center_begin,
+                      int64_t center_end, double box, double cutoff, const void* workspace,
+                      int64_t workspace_bytes, const int64_t* row_offsets, int32_t* neighbors,
+                      void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused ACE evaluation over a packed multi-word bundle.
+ * ---------------------------------------------------------------------- */
+
+/* Device tables of one packed bundle (all arrays device-resident).  Built on
+ * the host from compiled schedules (compile_ace_factorized_schedules_by_L,
+ * ye3t/couplings/__init__.py:2617) and symmetric-power plans
+ * (ye3t/couplings/__init__.py:4112), see ye3t_b200/packing.py. */
+typedef struct {
+  int64_t nmax, lmax;             /* radial channels 1..nmax, l = 0..lmax */
+  int64_t pool_size;              /* complex entries per atom in the block pool */
+  int64_t word_count;
+  int64_t feature_count;
+  int64_t sym_kind_count;
+  int32_t max_blocks;
+  const int32_t* word_pattern;          /* [W] */
+  const int32_t* word_label_base;       /* [W] first row of label_bases */
+  const int64_t* word_feature_offset;   /* [W] */
+  const int32_t* pattern_comp_begin;    /* [P+1] */
+  const int32_t* pattern_block_count;   /* [P] */
+  const int32_t* comp_term_begin;       /* [C_total+1] */
+  const int32_t* comp_label;            /* [C_total] */
+  const uint32_t* term_m;               /* [T_total] 4 x uint8: m + L_block */
+  const double* term_coeff;             /* [T_total] real coefficients */
+  const int32_t* label_bases;           /* [rows, 4] pool index of m_idx = 0 */
+  const int32_t* sym_kind;              /* [K, 6]: l, k, Lambda, pool offset, term begin, term end */
+  const uint32_t* sym_term_factors;     /* [S] 4 x uint8 input components (255 = unused) */
+  const int32_t* sym_term_output;       /* [S] */
+  const double* sym_term_coeff;         /* [S] */
+} y3b_ace_tables;
+
+/* A-basis density for centres [center_begin, center_begin + center_count):
+ *   A[i, n-1, l^2 + l + m] = sum_{j in row i} p[z_j] R_n(r_ij) Yc_lm(r_ij)
+ * n = 1..nmax (ChebExpCos, ye3t/runtime/execution_plan.py:7298), complex
+ * Condon-Shortley harmonics (:7479), per-neighbour-species prefactor as in
+ * plain_site_basis_product (:7582), accumulated per centre over its sorted
+ * CSR row (density_accumulate, :7913) by one warp, without atomics.
+ * r_ij = minimum image of r_j - r_i in a cubic box.  A is complex128
+ * [center_count, nmax, (lmax+1)^2]; row_offsets are relative to the first
+ * centre's row (row_offsets[0] may be nonzero). */
+int y3b_ace_density(const double* positions, const int32_t* species, int64_t atom_count,
+                    int64_t center_begin, int64_t center_count, double box,
+                    const int64_t* row_offsets, const int32_t* neighbors,
+                    const double* species_prefactor, int64_t species_count, int64_t nmax,
+                    int64_t lmax, double cutoff, double lambda, void* A, int32_t* status,
+                    void* stream);
+
+/* Block pool [pool_size, atom_count] complex128 (atom-fastest): the A
+ * channels followed by every symmetric block Sym^k(V_l) -> V_Lambda of every
+ * radial channel (symmetric_power_product_plan_contraction,
+ * ye3t/runtime/symmetric_power.py:879). */
+int y3b_ace_pool(const y3b_ace_tables* tables, const void* A, int64_t atom_count, void* pool,
+                 void* stream);
+
+/* Features [atom_count, feature_count] complex128: every word's factorized
+ * schedule (ACEFactorizedScheduleReport.evaluate,
+ * ye3t/couplings/__init__.py:2574) on its blocks from the pool. */
+int y3b_ace_features(const y3b_ace_tables* tables, const void* pool, int64_t atom_count,
+                     void* features, void* stream);
+
+/* Per-atom energy e[i] = sum_f weights[species[i], f] Re(B[i, f]) with B
+ * evaluated in registers and never stored. */
+int y3b_ace_energy(const y3b_ace_tables* tables, const void* pool, int64_t atom_count,
+                   const int32_t* species, const double* weights, int64_t species_count,
+                   double* energy, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Measurement support: an FP64 / FP32 FMA throughput kernel used to measure
+ * the CUDA-core roofline.  Returns the flop count of one launch in *flops. */
+int y3b_fma_peak_launch(int dtype, int32_t blocks, int32_t threads, int32_t iterations,
+                        void* sink, double* flops, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* YE3T_B200_H */

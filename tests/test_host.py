@@ -1,0 +1,60 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every
+symbol include/ye3t_b200.h declares; bundle files round-trip; argument errors."""
+
+import os
+import re
+
+import numpy as np
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    src = open(os.path.join(REPO, "include", "ye3t_b200.h")).read()
+    return sorted(set(re.findall(r"\b(y3b_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from ye3t_b200 import _native
+    lib = _native.lib()
+    declared = _declared_symbols()
+    assert declared, "no declarations found"
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/ye3t_b200.h but not exported"
+    assert set(declared) == set(_native.exported_symbols())
+    assert lib.y3b_abi_version() == _native.ABI_VERSION
+
+
+def test_library_argument_errors_without_gpu():
+    from ye3t_b200 import _native
+    lib = _native.lib()
+    rc = lib.y3b_cheb_exp_cos_radial_table(_native.F64, 0, 0, 0, 10, -1, 0, 0, 0)
+    assert rc == -1 and b"maximum_radial_index" in lib.y3b_last_error()
+    assert lib.y3b_density_accumulate_workspace_bytes(100, 10) > 0
+    assert lib.y3b_density_accumulate_workspace_bytes(-1, 10) == -1
+    assert lib.y3b_neighbor_workspace_bytes(1000, 30.0, 5.0) > 0
+    rc = lib.y3b_ace_pool(None, 0, 10, 0, 0)
+    assert rc == -1
+
+
+def test_bundle_round_trip(tmp_path):
+    from ye3t_b200.schedules import ACEBundle
+    b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu3_L0.npz"))
+    p = tmp_path / "b.npz"
+    b.save(str(p))
+    c = ACEBundle.load(str(p))
+    assert c.table_hash() == b.table_hash()
+    assert c.word_count == b.word_count == 2344 and c.feature_count == 2344
+    np.testing.assert_array_equal(c.word_n_map, b.word_n_map)
+
+
+def test_runtime_rejects_reference_backend_and_cpu():
+    import torch
+    from ye3t_b200 import runtime
+    with pytest.raises(ValueError):
+        runtime.density_accumulate(torch.zeros(2, 2), torch.zeros(2, dtype=torch.int64), 1, backend="reference")
+    with pytest.raises(ValueError):
+        runtime.density_accumulate(torch.zeros(2, 2), torch.zeros(2, dtype=torch.int64), 1)
+    caps = runtime.native_execution_plan_capabilities()
+    assert caps["loaded"] and caps["cpu"] is False

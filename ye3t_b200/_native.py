@@ -1,0 +1,145 @@
+"""ctypes binding of the C-ABI library ``ye3t_b200/lib/libye3t_b200.so``.
+
+The declarations mirror ``include/ye3t_b200.h``.  There is no fallback: if the
+library is missing or fails to load, every native operation raises
+:class:`NativeUnavailable` naming the build command.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libye3t_b200.so")
+
+ABI_VERSION = 1
+F32, F64, C64, C128 = 0, 1, 2, 3
+STATUS_INDEX_RANGE = 1
+STATUS_CAPACITY = 2
+
+_DTYPE_CODE = {torch.float32: F32, torch.float64: F64, torch.complex64: C64, torch.complex128: C128}
+
+I64 = ctypes.c_int64
+I32 = ctypes.c_int32
+VP = ctypes.c_void_p
+P64 = ctypes.POINTER(ctypes.c_int64)
+DBL = ctypes.c_double
+
+
+class NativeUnavailable(RuntimeError):
+    pass
+
+
+class NativeError(RuntimeError):
+    pass
+
+
+class AceTables(ctypes.Structure):
+    """``y3b_ace_tables`` (include/ye3t_b200.h)."""
+
+    _fields_ = [
+        ("nmax", I64), ("lmax", I64), ("pool_size", I64), ("word_count", I64), ("feature_count", I64),
+        ("sym_kind_count", I64), ("max_blocks", I32),
+        ("word_pattern", VP), ("word_label_base", VP), ("word_feature_offset", VP),
+        ("pattern_comp_begin", VP), ("pattern_block_count", VP), ("comp_term_begin", VP),
+        ("comp_label", VP), ("term_m", VP), ("term_coeff", VP), ("label_bases", VP),
+        ("sym_kind", VP), ("sym_term_factors", VP), ("sym_term_output", VP), ("sym_term_coeff", VP),
+    ]
+
+
+_SIGS = {
+    "y3b_abi_version": (I32, []),
+    "y3b_last_error": (ctypes.c_char_p, []),
+    "y3b_factorized_schedule_evaluate": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, I64, I64, VP, VP, VP, VP,
+                                                        I64, I64, VP, VP, VP]),
+    "y3b_symmetric_power_monomial": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, VP, VP, VP, I64, I64, VP, VP]),
+    "y3b_cheb_exp_cos_radial_table": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, VP, VP, VP]),
+    "y3b_spherical_harmonics_table": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, ctypes.c_int, DBL, VP, VP,
+                                                     VP]),
+    "y3b_density_accumulate_workspace_bytes": (I64, [I64, I64]),
+    "y3b_density_accumulate": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, VP, I64, VP, VP, VP]),
+    "y3b_density_accumulate_csr": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, VP, VP]),
+    "y3b_density_accumulate_adjoint": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, VP, VP, VP]),
+    "y3b_neighbor_workspace_bytes": (I64, [I64, DBL, DBL]),
+    "y3b_neighbor_count": (ctypes.c_int, [VP, I64, I64, I64, DBL, DBL, VP, I64, VP, VP]),
+    "y3b_neighbor_fill": (ctypes.c_int, [VP, I64, I64, I64, DBL, DBL, VP, I64, VP, VP, VP]),
+    "y3b_ace_density": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
+                                       VP]),
+    "y3b_ace_pool": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
+    "y3b_ace_features": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
+    "y3b_ace_energy": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP]),
+    "y3b_fma_peak_launch": (ctypes.c_int, [ctypes.c_int, I32, I32, I32, VP, ctypes.POINTER(DBL), VP]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library once; raise NativeUnavailable when it cannot be used."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise NativeUnavailable(
+                f"{LIB_PATH} is missing; build it with `make -C ye3t_b200/csrc` "
+                "(or __graft_entry__.build()). ye3t_b200 has no CPU fallback.")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        abi = handle.y3b_abi_version()
+        if abi != ABI_VERSION:
+            raise NativeUnavailable(f"{LIB_PATH}: ABI {abi}, expected {ABI_VERSION}; rebuild the library")
+        _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().y3b_last_error().decode(errors="replace")
+        raise NativeError(f"{what} failed ({rc}): {msg}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}") from None
+
+
+def ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors, what: str) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise ValueError(f"{what}: ye3t_b200 evaluates on CUDA devices only (got a {t.device} tensor); "
+                             "there is no CPU path")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{what}: tensors are on different devices ({dev}, {t.device})")
+    if dev is None:
+        raise ValueError(f"{what}: no tensor argument")
+    return dev
+
+
+def exported_symbols():
+    return sorted(_SIGS)

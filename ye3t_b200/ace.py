@@ -1,0 +1,154 @@
+"""Fused ACE descriptor / energy evaluation on one GPU (or one atom block).
+
+Pipeline for the centres ``[begin, end)`` of a periodic cubic box:
+
+1. cell-list neighbour list in sorted CSR form (``y3b_neighbor_count`` /
+   ``y3b_neighbor_fill``);
+2. A-basis density (kernel 1, ``y3b_ace_density``): per centre
+   ``A[n, lm] = sum_j p[z_j] R_n(r_ij) Yc_lm(r_ij)`` -- the composition of the
+   reference's radial table (``ye3t/runtime/execution_plan.py:7298``), complex
+   harmonics (``:7479``), per-neighbour prefactor (``:7582``) and
+   ``density_accumulate`` (``:7913``), fused;
+3. block pool (``y3b_ace_pool``): A plus every symmetric block
+   (``symmetric_power_product_plan_contraction``,
+   ``ye3t/runtime/symmetric_power.py:879``);
+4. B-basis (kernel 2): every word's factorized schedule
+   (``ACEFactorizedScheduleReport.evaluate``,
+   ``ye3t/couplings/__init__.py:2574``) -- either written out as features or
+   contracted with a per-species linear readout into per-atom energies.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+
+from . import _native as nat
+from .packing import PackedBundle, pack_bundle
+from .schedules import ACEBundle
+
+__all__ = ["ACEConfig", "ACEEvaluator"]
+
+
+@dataclass(frozen=True)
+class ACEConfig:
+    cutoff: float = 5.0
+    radial_lambda: float = 5.0
+
+
+class ACEEvaluator:
+    """Evaluates one :class:`ACEBundle` on one CUDA device."""
+
+    def __init__(self, bundle: ACEBundle, device, *, config: ACEConfig = ACEConfig(),
+                 species_prefactor=None, weights=None):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("ACEEvaluator runs on CUDA devices only")
+        nat.lib()
+        self.bundle = bundle
+        self.config = config
+        self.packed: PackedBundle = pack_bundle(bundle, self.device)
+        self._tables = self.packed.tables()
+        self.W = (bundle.lmax + 1) ** 2
+        self.species_prefactor = None if species_prefactor is None else torch.as_tensor(
+            species_prefactor, dtype=torch.float64, device=self.device).contiguous()
+        self.weights = None if weights is None else torch.as_tensor(
+            weights, dtype=torch.float64, device=self.device).contiguous()
+        if self.weights is not None and self.weights.shape[-1] != self.packed.feature_count:
+            raise ValueError(f"weights need {self.packed.feature_count} features per species")
+
+    @property
+    def feature_count(self) -> int:
+        return self.packed.feature_count
+
+    def _stream(self):
+        return nat.stream_of(self.device)
+
+    # -- neighbour list --------------------------------------------------------
+    def neighbor_list(self, positions: torch.Tensor, box: float, begin: int = 0,
+                      end: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """CSR rows ``(row_offsets [n+1] int64, neighbors [E] int32)`` for centres [begin, end)."""
+        pos = positions.to(self.device, torch.float64).contiguous()
+        N = pos.shape[0]
+        end = N if end is None else int(end)
+        lib = nat.lib()
+        rc = float(self.config.cutoff)
+        ws_bytes = int(lib.y3b_neighbor_workspace_bytes(N, float(box), rc))
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=self.device)
+        row = torch.empty(end - begin + 1, dtype=torch.int64, device=self.device)
+        s = self._stream()
+        nat.check(lib.y3b_neighbor_count(pos.data_ptr(), N, begin, end, float(box), rc, ws.data_ptr(), ws_bytes,
+                                         row.data_ptr(), s), "neighbor_count")
+        E = int(row[-1].item())
+        nbr = torch.empty(max(E, 1), dtype=torch.int32, device=self.device)
+        nat.check(lib.y3b_neighbor_fill(pos.data_ptr(), N, begin, end, float(box), rc, ws.data_ptr(), ws_bytes,
+                                        row.data_ptr(), nbr.data_ptr(), s), "neighbor_fill")
+        return row, nbr[:E]
+
+    # -- kernel 1 ----------------------------------------------------------------
+    def density(self, positions, species, box, row_offsets, neighbors, begin: int = 0,
+                status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """A-basis ``[n_centres, nmax, (lmax+1)^2]`` complex128."""
+        if self.species_prefactor is None:
+            raise ValueError("species_prefactor is required for the density")
+        pos = positions.to(self.device, torch.float64).contiguous()
+        sp = species.to(self.device, torch.int32).contiguous()
+        count = int(row_offsets.shape[0]) - 1
+        A = torch.empty((count, self.bundle.nmax, self.W), dtype=torch.complex128, device=self.device)
+        nat.check(nat.lib().y3b_ace_density(
+            pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box), row_offsets.data_ptr(),
+            neighbors.data_ptr(), self.species_prefactor.data_ptr(), self.species_prefactor.numel(),
+            self.bundle.nmax, self.bundle.lmax, float(self.config.cutoff), float(self.config.radial_lambda),
+            A.data_ptr(), nat.ptr(status), self._stream()), "ace_density")
+        return A
+
+    # -- kernel 2 ----------------------------------------------------------------
+    def pool(self, A: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        A = A.to(self.device, torch.complex128).contiguous()
+        n = A.shape[0]
+        if out is None:
+            out = torch.empty((self.packed.pool_size, n), dtype=torch.complex128, device=self.device)
+        nat.check(nat.lib().y3b_ace_pool(ctypes_ref(self._tables), A.data_ptr(), n, out.data_ptr(),
+                                         self._stream()), "ace_pool")
+        return out
+
+    def features_from_pool(self, pool: torch.Tensor) -> torch.Tensor:
+        n = pool.shape[1]
+        out = torch.empty((n, self.packed.feature_count), dtype=torch.complex128, device=self.device)
+        nat.check(nat.lib().y3b_ace_features(ctypes_ref(self._tables), pool.data_ptr(), n, out.data_ptr(),
+                                             self._stream()), "ace_features")
+        return out
+
+    def energy_from_pool(self, pool: torch.Tensor, species_centres: torch.Tensor,
+                         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.weights is None:
+            raise ValueError("weights are required for the energy")
+        n = pool.shape[1]
+        sp = species_centres.to(self.device, torch.int32).contiguous()
+        if out is None:
+            out = torch.empty(n, dtype=torch.float64, device=self.device)
+        nat.check(nat.lib().y3b_ace_energy(ctypes_ref(self._tables), pool.data_ptr(), n, sp.data_ptr(),
+                                           self.weights.data_ptr(), self.weights.shape[0], out.data_ptr(),
+                                           self._stream()), "ace_energy")
+        return out
+
+    def features(self, A: torch.Tensor) -> torch.Tensor:
+        return self.features_from_pool(self.pool(A))
+
+    # -- end to end ----------------------------------------------------------------
+    def energy(self, positions, species, box, begin: int = 0, end: Optional[int] = None):
+        """Per-atom energies of centres [begin, end) from positions."""
+        N = positions.shape[0]
+        end = N if end is None else int(end)
+        row, nbr = self.neighbor_list(positions, box, begin, end)
+        A = self.density(positions, species, box, row, nbr, begin)
+        pool = self.pool(A)
+        sp = species.to(self.device, torch.int32)[begin:end]
+        return self.energy_from_pool(pool, sp)
+
+
+def ctypes_ref(tables):
+    import ctypes
+    return ctypes.byref(tables)

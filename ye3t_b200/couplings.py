@@ -1,0 +1,130 @@
+"""Drop-in evaluation of compiled ACE factorized schedules on B200.
+
+``evaluate_factorized_schedule_torch`` keeps the signature and result of the
+reference function ``ye3t/core/couplings.py:481-567``; ``evaluate_report``
+is ``ACEFactorizedScheduleReport.evaluate`` (``ye3t/couplings/__init__.py:2574``).
+Schedules are accepted as the reference's ``FactorizedCoefficientSchedule`` /
+``TorchFactorizedCoefficientSchedule`` records (duck-typed) or as
+:class:`~ye3t_b200.schedules.ScheduleRecord`; their device tables are packed
+once per (schedule, device, dtype) and cached.
+"""
+
+from __future__ import annotations
+
+import threading
+import weakref
+
+import numpy as np
+import torch
+
+from . import _native as nat
+from .schedules import ScheduleRecord
+
+__all__ = ["evaluate_factorized_schedule_torch", "evaluate_report", "packed_schedule_tables"]
+
+_CACHE = {}
+_CACHE_LOCK = threading.Lock()
+
+
+def _schedule_arrays(schedule):
+    """(offsets, labels, block_m_indices, coeffs, component_count, block_count, basis_count, max_m)."""
+    if hasattr(schedule, "block_m_indices") and hasattr(schedule, "term_component_index"):
+        # TorchFactorizedCoefficientSchedule (couplings.py:259-335)
+        off = schedule.component_offsets.detach().cpu().numpy().astype(np.int64)
+        cli = schedule.component_label_index.detach().cpu().numpy().astype(np.int64)
+        midx = schedule.block_m_indices.detach().cpu().numpy().astype(np.int64)
+        coeffs = schedule.coeffs.detach().cpu().numpy()
+        return (off, cli, midx, coeffs, int(schedule.component_count), int(schedule.block_count),
+                int(schedule.basis_count), int(schedule.max_block_m_dim))
+    rec = schedule if isinstance(schedule, ScheduleRecord) else ScheduleRecord.from_schedule(schedule)
+    return (rec.component_offsets, rec.component_label_index, rec.block_m_indices(), np.asarray(rec.coeffs),
+            rec.component_count, rec.block_count, rec.basis_count, rec.max_block_m_dim)
+
+
+class _PackedSchedule:
+    __slots__ = ("off", "cli", "midx", "coeffs_c", "coeffs_r", "comps", "blocks", "basis", "max_m", "terms",
+                 "imag_max")
+
+
+def packed_schedule_tables(schedule, device):
+    """Device tables of one schedule, cached per (schedule object, device)."""
+    key = (id(schedule), str(device))
+    with _CACHE_LOCK:
+        hit = _CACHE.get(key)
+        if hit is not None and hit[0]() is schedule:
+            return hit[1]
+    off, cli, midx, coeffs, comps, blocks, basis, max_m = _schedule_arrays(schedule)
+    p = _PackedSchedule()
+    p.off = torch.as_tensor(off, dtype=torch.int64).to(device)
+    p.cli = torch.as_tensor(cli, dtype=torch.int64).to(device)
+    p.midx = torch.as_tensor(np.ascontiguousarray(midx).reshape(-1, blocks), dtype=torch.int64).to(device)
+    c = np.asarray(coeffs)
+    p.imag_max = float(np.max(np.abs(c.imag))) if (np.iscomplexobj(c) and c.size) else 0.0
+    p.coeffs_c = torch.as_tensor(c.astype(np.complex128)).to(device)
+    p.coeffs_r = torch.as_tensor(np.ascontiguousarray(c.real, dtype=np.float64)).to(device)
+    p.comps, p.blocks, p.basis, p.max_m, p.terms = comps, blocks, basis, max_m, int(c.shape[0])
+    try:
+        ref = weakref.ref(schedule)
+    except TypeError:  # objects without weakref support: keep them alive in the cache
+        ref = (lambda obj: (lambda: obj))(schedule)
+    with _CACHE_LOCK:
+        _CACHE[key] = (ref, p)
+    return p
+
+
+def evaluate_factorized_schedule_torch(block_values, schedule, *, backend="auto", validate=False):
+    """Evaluate a factorized coefficient schedule on CUDA block values.
+
+    ``block_values``: ``[batch, basis_count, block_count, max_block_m_dim]``
+    with padded magnetic positions zero.  Returns ``[batch, component_count]``
+    in the reference's value dtype: coefficients whose imaginary parts are all
+    within 1e-12 are used as real numbers for real block values
+    (``ye3t/core/couplings.py:508-516``).
+    """
+    backend = str(backend or "auto").strip().lower()
+    if backend in ("cpp", "c++", "torch-cpp", "cpu-cpp", "torch", "pytorch", "reference"):
+        raise ValueError(f"backend {backend!r} is a ye3t reference path; ye3t_b200 evaluates on CUDA only")
+    if backend not in ("auto", "native", "cuda"):
+        raise ValueError(f"Unknown factorized runtime backend: {backend!r}")
+    bv = torch.as_tensor(block_values)
+    dev = nat.require_cuda(bv, what="evaluate_factorized_schedule_torch")
+    if bv.requires_grad and torch.is_grad_enabled():
+        raise NotImplementedError("ye3t_b200 schedule evaluation is forward-only; use the fused force path")
+    p = packed_schedule_tables(schedule, dev)
+    if bv.ndim != 4:
+        raise ValueError("block_values must have shape [batch, basis_count, block_count, max_block_m_dim].")
+    if int(bv.shape[1]) < p.basis:
+        raise ValueError("block_values basis dimension is smaller than schedule.basis_count.")
+    if int(bv.shape[2]) != p.blocks:
+        raise ValueError("block_values block dimension must equal schedule.block_count.")
+    if int(bv.shape[3]) < p.max_m:
+        raise ValueError("block_values magnetic dimension is smaller than schedule.max_block_m_dim.")
+    if torch.is_complex(bv):
+        value_dtype = bv.dtype
+        coeffs = p.coeffs_c.to(value_dtype)
+    elif p.imag_max > 1e-12:
+        value_dtype = torch.complex128 if bv.dtype == torch.float64 else torch.complex64
+        coeffs = p.coeffs_c.to(value_dtype)
+    else:
+        value_dtype = bv.dtype
+        coeffs = p.coeffs_r.to(value_dtype)
+    values = bv.to(value_dtype).contiguous()
+    batch, basis, blocks, mdim = (int(s) for s in values.shape)
+    out = torch.empty((batch, p.comps), dtype=value_dtype, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if validate else None
+    nat.check(nat.lib().y3b_factorized_schedule_evaluate(
+        nat.dtype_code(value_dtype), values.data_ptr(), batch, basis, blocks, mdim, p.off.data_ptr(),
+        p.cli.data_ptr(), p.midx.data_ptr() if p.terms else 0, coeffs.data_ptr() if p.terms else 0, p.comps,
+        p.terms, out.data_ptr(), nat.ptr(status), nat.stream_of(dev)), "evaluate_factorized_schedule_torch")
+    if validate and int(status.item()):
+        raise IndexError("evaluate_factorized_schedule_torch: schedule index out of range")
+    return out
+
+
+def evaluate_report(report, block_values, *, target_L, backend="auto"):
+    """``ACEFactorizedScheduleReport.evaluate`` on CUDA (``ye3t/couplings/__init__.py:2574-2591``)."""
+    target_L = int(target_L)
+    schedules = getattr(report, "schedules_by_target", None) or getattr(report, "schedules_by_L")
+    if target_L not in schedules:
+        raise ValueError("target_L is not present in this ACE schedule report.")
+    return evaluate_factorized_schedule_torch(block_values, schedules[target_L], backend=backend)

@@ -1,0 +1,248 @@
+// Cubic periodic cell-list neighbour builder producing sorted CSR rows.
+//
+// The reference has no neighbour-list code (applications supply the density
+// factors); this is the builder the fused A-basis path consumes.  The
+// minimum-image displacement and the r^2 <= rc^2 test use non-contracting
+// intrinsics so every pair decision and displacement is bit-identical to the
+// serial CPU oracle.
+#include "common.cuh"
+#include "neighbors.cuh"
+
+namespace y3b {
+
+namespace {
+
+struct CellWorkspace {
+  int64_t* cell_start;  // [nc + 1]
+  int32_t* cursor;      // [nc]
+  int32_t* atom_cell;   // [N]
+  int32_t* cell_atoms;  // [N]
+  int64_t bytes;
+};
+
+inline int64_t al(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+inline CellWorkspace carve_cells(void* base, int64_t N, int64_t nc) {
+  CellWorkspace w;
+  char* p = static_cast<char*>(base);
+  int64_t o = 0;
+  w.cell_start = reinterpret_cast<int64_t*>(p + o); o += al((nc + 1) * 8);
+  w.cursor = reinterpret_cast<int32_t*>(p + o); o += al(nc * 4);
+  w.atom_cell = reinterpret_cast<int32_t*>(p + o); o += al(N * 4);
+  w.cell_atoms = reinterpret_cast<int32_t*>(p + o); o += al(N * 4);
+  w.bytes = o;
+  return w;
+}
+
+__device__ __forceinline__ int cell_coord(double x, double box, int n) {
+  double f = x / box;
+  f -= floor(f);
+  int c = int(f * n);
+  return c < 0 ? 0 : (c >= n ? n - 1 : c);
+}
+
+__global__ void assign_cells_kernel(const double* __restrict__ pos, int64_t N, double box, int n,
+                                    int32_t* __restrict__ atom_cell,
+                                    unsigned long long* __restrict__ counts) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < N;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int cx = cell_coord(pos[3 * i], box, n), cy = cell_coord(pos[3 * i + 1], box, n),
+              cz = cell_coord(pos[3 * i + 2], box, n);
+    const int c = (cz * n + cy) * n + cx;
+    atom_cell[i] = c;
+    atomicAdd(counts + c + 1, 1ull);
+  }
+}
+
+__global__ void fill_cells_kernel(int64_t N, const int32_t* __restrict__ atom_cell,
+                                  const int64_t* __restrict__ cell_start, int32_t* __restrict__ cursor,
+                                  int32_t* __restrict__ cell_atoms) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < N;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int c = atom_cell[i];
+    const int slot = atomicAdd(cursor + c, 1);
+    cell_atoms[cell_start[c] + slot] = int32_t(i);
+  }
+}
+
+// Insertion sort of each cell's members (cells hold a handful of atoms).
+__global__ void sort_cells_kernel(int64_t nc, const int64_t* __restrict__ cell_start,
+                                  int32_t* __restrict__ cell_atoms) {
+  for (int64_t c = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; c < nc;
+       c += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = cell_start[c], e = cell_start[c + 1];
+    for (int64_t k = b + 1; k < e; ++k) {
+      const int32_t v = cell_atoms[k];
+      int64_t j = k - 1;
+      while (j >= b && cell_atoms[j] > v) {
+        cell_atoms[j + 1] = cell_atoms[j];
+        --j;
+      }
+      cell_atoms[j + 1] = v;
+    }
+  }
+}
+
+// Visit every candidate neighbour j of centre i exactly once.
+template <typename F>
+__device__ __forceinline__ void for_each_neighbor(const double* __restrict__ pos, int64_t i, double box,
+                                                  double rc2, int n, const int64_t* __restrict__ cell_start,
+                                                  const int32_t* __restrict__ cell_atoms, F&& f) {
+  const double xi = pos[3 * i], yi = pos[3 * i + 1], zi = pos[3 * i + 2];
+  const int span = n >= 3 ? 1 : 0;
+  const int cx = cell_coord(xi, box, n), cy = cell_coord(yi, box, n), cz = cell_coord(zi, box, n);
+  for (int dz = -span; dz <= span; ++dz)
+    for (int dy = -span; dy <= span; ++dy)
+      for (int dx = -span; dx <= span; ++dx) {
+        const int x = (cx + dx + n) % n, y = (cy + dy + n) % n, z = (cz + dz + n) % n;
+        const int c = (z * n + y) * n + x;
+        for (int64_t k = cell_start[c]; k < cell_start[c + 1]; ++k) {
+          const int32_t j = cell_atoms[k];
+          if (j == i) continue;
+          double d[3];
+          min_image(pos, i, j, box, d);
+          if (dist2(d) <= rc2) f(j);
+        }
+      }
+}
+
+__global__ void count_neighbors_kernel(const double* __restrict__ pos, int64_t begin, int64_t end,
+                                       double box, double rc2, int n,
+                                       const int64_t* __restrict__ cell_start,
+                                       const int32_t* __restrict__ cell_atoms,
+                                       int64_t* __restrict__ row_offsets) {
+  for (int64_t i = begin + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < end;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t cnt = 0;
+    for_each_neighbor(pos, i, box, rc2, n, cell_start, cell_atoms, [&](int32_t) { ++cnt; });
+    row_offsets[i - begin + 1] = cnt;
+    if (i == begin) row_offsets[0] = 0;
+  }
+}
+
+__global__ void fill_neighbors_kernel(const double* __restrict__ pos, int64_t begin, int64_t end,
+                                      double box, double rc2, int n,
+                                      const int64_t* __restrict__ cell_start,
+                                      const int32_t* __restrict__ cell_atoms,
+                                      const int64_t* __restrict__ row_offsets,
+                                      int32_t* __restrict__ nbr) {
+  for (int64_t i = begin + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < end;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = row_offsets[i - begin], e = row_offsets[i - begin + 1];
+    int64_t k = b;
+    for_each_neighbor(pos, i, box, rc2, n, cell_start, cell_atoms, [&](int32_t j) {
+      if (k < e) nbr[k] = j;
+      ++k;
+    });
+    for (int64_t a = b + 1; a < e; ++a) {  // rows in increasing neighbour index
+      const int32_t v = nbr[a];
+      int64_t q = a - 1;
+      while (q >= b && nbr[q] > v) {
+        nbr[q + 1] = nbr[q];
+        --q;
+      }
+      nbr[q + 1] = v;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(1024) scan_i64_kernel(int64_t* __restrict__ a, int64_t n) {
+  __shared__ int64_t sums[1024];
+  const int t = threadIdx.x;
+  const int64_t chunk = (n + 1023) / 1024;
+  const int64_t b = t * chunk, e = min(n, b + chunk);
+  int64_t s = 0;
+  for (int64_t i = b; i < e; ++i) s += a[i];
+  sums[t] = s;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int64_t v = t >= off ? sums[t - off] : 0;
+    __syncthreads();
+    sums[t] += v;
+    __syncthreads();
+  }
+  int64_t run = t > 0 ? sums[t - 1] : 0;
+  for (int64_t i = b; i < e; ++i) {
+    run += a[i];
+    a[i] = run;
+  }
+}
+
+}  // namespace
+
+int cells_per_side(double box, double cutoff) {
+  if (!(box > 0) || !(cutoff > 0)) return 1;
+  const double r = box / cutoff;
+  if (r < 3.0) return 1;
+  return int(r > 1024.0 ? 1024.0 : r);
+}
+
+}  // namespace y3b
+
+using namespace y3b;
+
+extern "C" int64_t y3b_neighbor_workspace_bytes(int64_t atom_count, double box, double cutoff) {
+  const int64_t n = cells_per_side(box, cutoff);
+  return carve_cells(nullptr, atom_count, n * n * n).bytes;
+}
+
+extern "C" int y3b_neighbor_count(const double* positions, int64_t atom_count, int64_t center_begin,
+                                  int64_t center_end, double box, double cutoff, void* workspace,
+                                  int64_t workspace_bytes, int64_t* row_offsets, void* stream) {
+  Y3B_CHECK_ARG(atom_count >= 0 && atom_count < (int64_t(1) << 31), "atom count out of range");
+  Y3B_CHECK_ARG(0 <= center_begin && center_begin <= center_end && center_end <= atom_count,
+                "bad centre range [%lld, %lld)", (long long)center_begin, (long long)center_end);
+  Y3B_CHECK_ARG(box > 0 && cutoff > 0, "box and cutoff must be positive");
+  Y3B_CHECK_ARG(row_offsets != nullptr, "null row_offsets");
+  cudaStream_t s = as_stream(stream);
+  if (center_end == center_begin) {
+    Y3B_CUDA_TRY(cudaMemsetAsync(row_offsets, 0, 8, s));
+    return Y3B_OK;
+  }
+  Y3B_CHECK_ARG(positions != nullptr, "null positions");
+  const int n = cells_per_side(box, cutoff);
+  const int64_t nc = int64_t(n) * n * n;
+  const CellWorkspace w = carve_cells(workspace, atom_count, nc);
+  Y3B_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "neighbour workspace too small: need %lld",
+                (long long)w.bytes);
+  Y3B_CUDA_TRY(cudaMemsetAsync(w.cell_start, 0, (nc + 1) * 8, s));
+  Y3B_CUDA_TRY(cudaMemsetAsync(w.cursor, 0, nc * 4, s));
+  assign_cells_kernel<<<grid_for(atom_count, 256), 256, 0, s>>>(
+      positions, atom_count, box, n, w.atom_cell, reinterpret_cast<unsigned long long*>(w.cell_start));
+  Y3B_LAUNCH_CHECK();
+  scan_i64_kernel<<<1, 1024, 0, s>>>(w.cell_start, nc + 1);
+  Y3B_LAUNCH_CHECK();
+  fill_cells_kernel<<<grid_for(atom_count, 256), 256, 0, s>>>(atom_count, w.atom_cell, w.cell_start,
+                                                              w.cursor, w.cell_atoms);
+  Y3B_LAUNCH_CHECK();
+  sort_cells_kernel<<<grid_for(nc, 256), 256, 0, s>>>(nc, w.cell_start, w.cell_atoms);
+  Y3B_LAUNCH_CHECK();
+  const int64_t count = center_end - center_begin;
+  count_neighbors_kernel<<<grid_for(count, 128), 128, 0, s>>>(
+      positions, center_begin, center_end, box, cutoff * cutoff, n, w.cell_start, w.cell_atoms,
+      row_offsets);
+  Y3B_LAUNCH_CHECK();
+  scan_i64_kernel<<<1, 1024, 0, s>>>(row_offsets, count + 1);
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+extern "C" int y3b_neighbor_fill(const double* positions, int64_t atom_count, int64_t center_begin,
+                                 int64_t center_end, double box, double cutoff, const void* workspace,
+                                 int64_t workspace_bytes, const int64_t* row_offsets, int32_t* neighbors,
+                                 void* stream) {
+  Y3B_CHECK_ARG(0 <= center_begin && center_begin <= center_end && center_end <= atom_count,
+                "bad centre range");
+  if (center_end == center_begin) return Y3B_OK;
+  Y3B_CHECK_ARG(positions && row_offsets && neighbors, "null pointer argument");
+  const int n = cells_per_side(box, cutoff);
+  const int64_t nc = int64_t(n) * n * n;
+  const CellWorkspace w = carve_cells(const_cast<void*>(workspace), atom_count, nc);
+  Y3B_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "neighbour workspace too small");
+  const int64_t count = center_end - center_begin;
+  fill_neighbors_kernel<<<grid_for(count, 128), 128, 0, as_stream(stream)>>>(
+      positions, center_begin, center_end, box, cutoff * cutoff, n, w.cell_start, w.cell_atoms,
+      row_offsets, neighbors);
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}

@@ -1,0 +1,139 @@
+// Generic factorized-schedule evaluation and symmetric-power contraction.
+//
+// These are the drop-in kernels behind evaluate_factorized_schedule_torch and
+// symmetric_power_monomial for arbitrary caller-supplied block arrays.  The
+// fused bundle path (ace.cu) evaluates the same schedules from an on-device
+// block pool.
+#include "common.cuh"
+
+namespace y3b {
+
+// One thread per (batch row, component), component fastest, grid-stride.
+// Consecutive threads read the same batch row (L1-resident) and write
+// consecutive outputs.  Terms run in table order from the coefficient, as in
+// factorized_runtime.cpp:268-283.
+template <typename T>
+__global__ void __launch_bounds__(256) schedule_eval_kernel(
+    const T* __restrict__ bv, int64_t batch, int64_t basis, int64_t blocks, int64_t mdim,
+    const int64_t* __restrict__ off, const int64_t* __restrict__ labels,
+    const int64_t* __restrict__ midx, const T* __restrict__ coeffs, int64_t comps,
+    T* __restrict__ out, int32_t* status) {
+  const int64_t total = batch * comps;
+  for (int64_t lin = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; lin < total;
+       lin += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = lin / comps;
+    const int64_t c = lin - b * comps;
+    const int64_t label = __ldg(labels + c);
+    T acc = zero<T>();
+    if (label < 0 || label >= basis) {
+      if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+    } else {
+      const T* row = bv + (b * basis + label) * blocks * mdim;
+      const int64_t t0 = __ldg(off + c), t1 = __ldg(off + c + 1);
+      for (int64_t t = t0; t < t1; ++t) {
+        T v = coeffs[t];
+        const int64_t* mt = midx + t * blocks;
+        for (int64_t j = 0; j < blocks; ++j) {
+          const int64_t m = __ldg(mt + j);
+          if (m < 0 || m >= mdim) {
+            if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+            v = zero<T>();
+            break;
+          }
+          v = mul(v, row[j * mdim + m]);
+        }
+        acc = add(acc, v);
+      }
+    }
+    out[lin] = acc;
+  }
+}
+
+// Integer power by repeated multiplication, as ye3t_runtime_core's
+// integer_power; an exponent of 0 yields exactly 1.
+template <typename T>
+__device__ __forceinline__ T ipow(T x, int64_t e) {
+  T r = one<T>();
+  for (int64_t k = 0; k < e; ++k) r = mul(r, x);
+  return r;
+}
+
+// One thread per (batch row, output component).
+template <typename T>
+__global__ void __launch_bounds__(256) sympow_kernel(
+    const T* __restrict__ x, int64_t batch, int64_t in_dim, const int64_t* __restrict__ counts,
+    const int64_t* __restrict__ off, const T* __restrict__ vals, int64_t out_dim,
+    T* __restrict__ out) {
+  const int64_t total = batch * out_dim;
+  for (int64_t lin = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; lin < total;
+       lin += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = lin / out_dim;
+    const int64_t o = lin - b * out_dim;
+    const T* xr = x + b * in_dim;
+    T acc = zero<T>();
+    for (int64_t t = __ldg(off + o); t < __ldg(off + o + 1); ++t) {
+      T m = vals[t];
+      for (int64_t i = 0; i < in_dim; ++i) {
+        const int64_t e = __ldg(counts + t * in_dim + i);
+        if (e) m = mul(m, ipow(xr[i], e));
+      }
+      acc = add(acc, m);
+    }
+    out[lin] = acc;
+  }
+}
+
+}  // namespace y3b
+
+using namespace y3b;
+
+extern "C" int y3b_factorized_schedule_evaluate(int dtype, const void* block_values, int64_t batch,
+                                                int64_t basis_count, int64_t block_count,
+                                                int64_t magnetic_dim,
+                                                const int64_t* component_offsets,
+                                                const int64_t* component_label_index,
+                                                const int64_t* block_m_indices, const void* coeffs,
+                                                int64_t component_count, int64_t term_count,
+                                                void* out, int32_t* status, void* stream) {
+  Y3B_CHECK_ARG(batch >= 0 && basis_count >= 0 && block_count >= 0 && magnetic_dim >= 0,
+                "negative size");
+  Y3B_CHECK_ARG(component_count >= 0 && term_count >= 0, "negative component/term count");
+  const int64_t total = batch * component_count;
+  if (total == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(block_values && component_offsets && component_label_index && out,
+                "null pointer argument");
+  Y3B_CHECK_ARG(term_count == 0 || (coeffs && (block_count == 0 || block_m_indices)),
+                "null coefficient or index table");
+  const int threads = 256;
+  const int grid = grid_for(total, threads);
+  Y3B_DISPATCH(dtype, T, {
+    schedule_eval_kernel<T><<<grid, threads, 0, as_stream(stream)>>>(
+        static_cast<const T*>(block_values), batch, basis_count, block_count, magnetic_dim,
+        component_offsets, component_label_index, block_m_indices, static_cast<const T*>(coeffs),
+        component_count, static_cast<T*>(out), status);
+  });
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+extern "C" int y3b_symmetric_power_monomial(int dtype, const void* input, int64_t batch,
+                                            int64_t input_dim, const int64_t* monomial_counts,
+                                            const int64_t* output_offsets,
+                                            const void* monomial_values, int64_t term_count,
+                                            int64_t output_dim, void* out, void* stream) {
+  Y3B_CHECK_ARG(batch >= 0 && input_dim >= 0 && output_dim >= 0 && term_count >= 0,
+                "negative size");
+  const int64_t total = batch * output_dim;
+  if (total == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(input && output_offsets && out && (term_count == 0 || (monomial_counts && monomial_values)),
+                "null pointer argument");
+  const int threads = 256;
+  const int grid = grid_for(total, threads);
+  Y3B_DISPATCH(dtype, T, {
+    sympow_kernel<T><<<grid, threads, 0, as_stream(stream)>>>(
+        static_cast<const T*>(input), batch, input_dim, monomial_counts, output_offsets,
+        static_cast<const T*>(monomial_values), output_dim, static_cast<T*>(out));
+  });
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}

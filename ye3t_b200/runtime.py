@@ -1,0 +1,271 @@
+"""``ye3t.runtime``-shaped operators backed by the sm_100a library.
+
+Same names, argument meanings and result layouts as the reference wrappers in
+``ye3t/runtime/execution_plan.py`` (cited per function).  ``backend`` accepts
+``"auto"`` and ``"native"`` (both run the CUDA library) and rejects
+``"reference"``: this package has no CPU or pure-torch fallback, and tensors
+must live on a CUDA device.
+
+Index checks run on the device: out-of-range centres or indices set a status
+word and contribute zero.  With ``YE3T_B200_VALIDATE=1`` (or
+``validate=True``) each call synchronises and raises ``IndexError`` when the
+status word is set, matching the reference CPU path's eager checks
+(``execution_plan_torch.cpp:1511-1515``).
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _native as nat
+
+__all__ = [
+    "cheb_exp_cos_radial_table_with_derivative",
+    "spherical_harmonics_table_with_derivative",
+    "density_accumulate",
+    "density_accumulate_adjoint",
+    "symmetric_power_monomial_contraction",
+    "symmetric_power_table_contraction",
+    "native_execution_plan_capabilities",
+]
+
+
+def _check_backend(backend, allowed=("auto", "native")):
+    backend = str(backend)
+    if backend == "reference":
+        raise ValueError("ye3t_b200 has no reference (CPU / pure torch) path; backend='reference' is the "
+                         "ye3t package's own implementation")
+    if backend not in allowed:
+        raise ValueError(f"backend must be one of {allowed}, got {backend!r}")
+
+
+def _validate_default(validate):
+    if validate is None:
+        return os.environ.get("YE3T_B200_VALIDATE", "0") not in ("", "0", "false", "False")
+    return bool(validate)
+
+
+def _status(device):
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def _raise_on_status(status, what):
+    v = int(status.item())
+    if v & nat.STATUS_INDEX_RANGE:
+        raise IndexError(f"{what}: index out of range")
+    if v:
+        raise RuntimeError(f"{what}: device status {v}")
+
+
+# ---------------------------------------------------------------------------
+def cheb_exp_cos_radial_table_with_derivative(radii, cutoffs, lambdas, maximum_radial_index, backend="auto"):
+    """ChebExpCos radial table and d/dr; ``ye3t/runtime/execution_plan.py:7298``.
+
+    Returns ``(values, derivatives)`` of shape ``[E, maximum_radial_index + 1]``.
+    """
+    _check_backend(backend)
+    kmax = int(maximum_radial_index)
+    if kmax < 0:
+        raise ValueError("maximum_radial_index must be non-negative")
+    radii = torch.as_tensor(radii)
+    dev = nat.require_cuda(radii, what="cheb_exp_cos_radial_table_with_derivative")
+    if radii.dtype not in (torch.float32, torch.float64):
+        raise TypeError("radii must be float32 or float64")
+    cutoffs = torch.as_tensor(cutoffs, dtype=radii.dtype, device=dev).expand_as(radii).contiguous()
+    lambdas = torch.as_tensor(lambdas, dtype=radii.dtype, device=dev).expand_as(radii).contiguous()
+    r = radii.contiguous().reshape(-1)
+    E = r.numel()
+    val = torch.empty((E, kmax + 1), dtype=radii.dtype, device=dev)
+    der = torch.empty_like(val)
+    nat.check(nat.lib().y3b_cheb_exp_cos_radial_table(nat.dtype_code(radii.dtype), r.data_ptr(),
+                                                       cutoffs.data_ptr(), lambdas.data_ptr(), E, kmax,
+                                                       val.data_ptr(), der.data_ptr(), nat.stream_of(dev)),
+              "cheb_exp_cos_radial_table_with_derivative")
+    return val, der
+
+
+def spherical_harmonics_table_with_derivative(edge_vectors, maximum_angular_momentum, *, real_output=False,
+                                              epsilon=1.0e-12, backend="auto"):
+    """Packed harmonics for all ``l <= lmax`` and Cartesian derivatives.
+
+    ``ye3t/runtime/execution_plan.py:7479``: values ``[E, (lmax+1)^2]``,
+    derivatives ``[E, (lmax+1)^2, 3]``; complex Condon-Shortley unless
+    ``real_output``.
+    """
+    _check_backend(backend)
+    lmax = int(maximum_angular_momentum)
+    if lmax < 0:
+        raise ValueError("maximum_angular_momentum must be non-negative")
+    v = torch.as_tensor(edge_vectors)
+    dev = nat.require_cuda(v, what="spherical_harmonics_table_with_derivative")
+    if v.dtype not in (torch.float32, torch.float64) or v.shape[-1] != 3:
+        raise ValueError("edge_vectors must be real [E, 3]")
+    v = v.contiguous().reshape(-1, 3)
+    E = v.shape[0]
+    W = (lmax + 1) ** 2
+    out_dtype = v.dtype if real_output else (torch.complex128 if v.dtype == torch.float64 else torch.complex64)
+    val = torch.empty((E, W), dtype=out_dtype, device=dev)
+    der = torch.empty((E, W, 3), dtype=out_dtype, device=dev)
+    nat.check(nat.lib().y3b_spherical_harmonics_table(nat.dtype_code(v.dtype), v.data_ptr(), E, lmax,
+                                                       int(bool(real_output)), float(epsilon), val.data_ptr(),
+                                                       der.data_ptr(), nat.stream_of(dev)),
+              "spherical_harmonics_table_with_derivative")
+    return val, der
+
+
+# ---------------------------------------------------------------------------
+def _density_forward(edge_values, centers, atom_count, validate):
+    dev = nat.require_cuda(edge_values, centers, what="density_accumulate")
+    ev = edge_values.contiguous()
+    E = ev.shape[0]
+    C = 1
+    for extent in ev.shape[1:]:
+        C *= int(extent)
+    centers = centers.to(device=dev, dtype=torch.int64).contiguous().reshape(-1)
+    if centers.numel() != E:
+        raise ValueError("centers must have one entry per edge row")
+    out = torch.empty((int(atom_count),) + tuple(ev.shape[1:]), dtype=ev.dtype, device=dev)
+    lib = nat.lib()
+    ws_bytes = int(lib.y3b_density_accumulate_workspace_bytes(E, int(atom_count)))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    status = _status(dev)
+    nat.check(lib.y3b_density_accumulate(nat.dtype_code(ev.dtype), ev.data_ptr(), centers.data_ptr(), E, C,
+                                         int(atom_count), ws.data_ptr(), ws_bytes, out.data_ptr(),
+                                         status.data_ptr(), nat.stream_of(dev)), "density_accumulate")
+    if validate:
+        _raise_on_status(status, "density_accumulate")
+    return out
+
+
+def _density_adjoint(atomic_adjoint, centers, validate):
+    dev = nat.require_cuda(atomic_adjoint, centers, what="density_accumulate_adjoint")
+    adj = atomic_adjoint.contiguous()
+    centers = centers.to(device=dev, dtype=torch.int64).contiguous().reshape(-1)
+    E = centers.numel()
+    C = 1
+    for extent in adj.shape[1:]:
+        C *= int(extent)
+    out = torch.empty((E,) + tuple(adj.shape[1:]), dtype=adj.dtype, device=dev)
+    status = _status(dev)
+    nat.check(nat.lib().y3b_density_accumulate_adjoint(nat.dtype_code(adj.dtype), adj.data_ptr(),
+                                                        centers.data_ptr(), E, C, adj.shape[0], out.data_ptr(),
+                                                        status.data_ptr(), nat.stream_of(dev)),
+              "density_accumulate_adjoint")
+    if validate:
+        _raise_on_status(status, "density_accumulate_adjoint")
+    return out
+
+
+class _DensityAccumulate(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, edge_values, centers, atom_count, validate):
+        ctx.save_for_backward(centers)
+        ctx.validate = validate
+        return _density_forward(edge_values, centers, atom_count, validate)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (centers,) = ctx.saved_tensors
+        return _density_adjoint(grad, centers, ctx.validate), None, None, None
+
+
+def density_accumulate(edge_values, centers, atom_count, *, backend="auto", validate=None):
+    """``A[centers[e]] += edge_values[e]``; ``ye3t/runtime/execution_plan.py:7913``.
+
+    Deterministic (no floating-point atomics).  Differentiable in
+    ``edge_values`` through :func:`density_accumulate_adjoint`.
+    """
+    _check_backend(backend, ("auto", "native", "deterministic"))
+    edge_values = torch.as_tensor(edge_values)
+    centers = torch.as_tensor(centers, device=edge_values.device)
+    validate = _validate_default(validate)
+    if edge_values.requires_grad and torch.is_grad_enabled():
+        return _DensityAccumulate.apply(edge_values, centers, int(atom_count), validate)
+    return _density_forward(edge_values, centers, int(atom_count), validate)
+
+
+def density_accumulate_adjoint(atomic_adjoint, centers, *, backend="auto", validate=None):
+    """Gather centre rows back to edge rows; ``ye3t/runtime/execution_plan.py:7987``."""
+    _check_backend(backend, ("auto", "native", "deterministic"))
+    atomic_adjoint = torch.as_tensor(atomic_adjoint)
+    centers = torch.as_tensor(centers, device=atomic_adjoint.device)
+    return _density_adjoint(atomic_adjoint, centers, _validate_default(validate))
+
+
+# ---------------------------------------------------------------------------
+def symmetric_power_monomial_contraction(input, monomial_counts, output_offsets, output_indices,
+                                         monomial_values, *, backend="auto"):
+    """Grouped symmetric-power table contraction; ``ye3t/runtime/execution_plan.py:11998``."""
+    _check_backend(backend)
+    x = torch.as_tensor(input)
+    dev = nat.require_cuda(x, what="symmetric_power_monomial_contraction")
+    if x.ndim < 1:
+        raise ValueError("symmetric-power input requires a feature axis")
+    in_dim = int(x.shape[-1])
+    counts = torch.as_tensor(monomial_counts, dtype=torch.int64, device=dev).contiguous()
+    offsets = torch.as_tensor(output_offsets, dtype=torch.int64, device=dev).reshape(-1).contiguous()
+    indices = torch.as_tensor(output_indices, dtype=torch.int64, device=dev).reshape(-1)
+    values = torch.as_tensor(monomial_values, dtype=x.dtype, device=dev).reshape(-1).contiguous()
+    if counts.ndim != 2 or int(counts.shape[1]) != in_dim:
+        raise ValueError("monomial_counts must have shape [term, input_dimension]")
+    if int(indices.numel()) != int(counts.shape[0]) or int(values.numel()) != int(counts.shape[0]):
+        raise ValueError("output_indices / monomial_values length must match the term count")
+    out_dim = int(offsets.numel()) - 1
+    x2 = x.contiguous().reshape(-1, in_dim)
+    out = torch.empty((x2.shape[0], out_dim), dtype=x.dtype, device=dev)
+    nat.check(nat.lib().y3b_symmetric_power_monomial(nat.dtype_code(x.dtype), x2.data_ptr(), x2.shape[0], in_dim,
+                                                      counts.data_ptr(), offsets.data_ptr(), values.data_ptr(),
+                                                      int(counts.shape[0]), out_dim, out.data_ptr(),
+                                                      nat.stream_of(dev)),
+              "symmetric_power_monomial_contraction")
+    return out.reshape(*x.shape[:-1], out_dim)
+
+
+def symmetric_power_table_contraction(input, table, *, backend="auto"):
+    """Contract with a :class:`~ye3t_b200.schedules.SymPowerTable` (grouped plan table).
+
+    Same role as ``symmetric_power_product_plan_contraction``
+    (``ye3t/runtime/symmetric_power.py:879``) once the plan has been lowered.
+    """
+    x = torch.as_tensor(input)
+    vals = torch.as_tensor(table.monomial_value)
+    if not torch.is_complex(x) and torch.is_complex(vals):
+        if vals.numel() and float(vals.imag.abs().max()) > 1e-12:
+            x = x.to(torch.complex128 if x.dtype == torch.float64 else torch.complex64)
+        else:
+            vals = vals.real
+    return symmetric_power_monomial_contraction(x, table.monomial_counts, table.output_offsets,
+                                                table.output_index, vals, backend=backend)
+
+
+def native_execution_plan_capabilities():
+    """Capability report; the analogue of ``ye3t/runtime/execution_plan.py:6118``."""
+    try:
+        lib = nat.lib()
+        loaded, abi, err = True, int(lib.y3b_abi_version()), None
+    except Exception as exc:  # noqa: BLE001 - report, do not hide
+        loaded, abi, err = False, None, str(exc)
+    return {
+        "library": nat.LIB_PATH,
+        "loaded": loaded,
+        "abi_version": abi,
+        "error": err,
+        "cuda": True,
+        "cpu": False,
+        "architecture": "sm_100a",
+        "ops": {
+            "cheb_exp_cos_radial_table_with_derivative": ["float32", "float64"],
+            "spherical_harmonics_table_with_derivative": ["float32", "float64"],
+            "density_accumulate": ["float32", "float64", "complex64", "complex128"],
+            "density_accumulate_adjoint": ["float32", "float64", "complex64", "complex128"],
+            "symmetric_power_monomial": ["float32", "float64", "complex64", "complex128"],
+            "factorized_schedule": ["float32", "float64", "complex64", "complex128"],
+            "ace_density": ["float64 -> complex128"],
+            "ace_bundle": ["complex128"],
+        },
+        "density_accumulate_deterministic": True,
+        "max_spherical_lmax": 8,
+        "fused_ace_lmax": 4,
+    }
