@@ -30,7 +30,9 @@ def test_radial_table_matches_reference(golden):
     np.testing.assert_allclose(v.cpu().numpy(), g["rad_val_native"], rtol=2e-13, atol=2e-13)
     np.testing.assert_allclose(d.cpu().numpy(), g["rad_der_native"], rtol=2e-12, atol=2e-12)
     v32, _ = radial(_t(g["radii"].astype(np.float32)), 5.0, 5.0, int(g["kmax"]))
-    np.testing.assert_allclose(v32.cpu().numpy(), g["rad_val_native"], rtol=1e-5, atol=1e-5)
+    # radii within fp32 rounding of the cutoff can land on the other side of it
+    ok = np.abs(g["radii"] - 5.0) > 1e-5
+    np.testing.assert_allclose(v32.cpu().numpy()[ok], g["rad_val_native"][ok], rtol=1e-5, atol=1e-5)
 
 
 @pytest.mark.parametrize("real_output", [True, False])
