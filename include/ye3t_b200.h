@@ -114,6 +114,24 @@ int y3b_density_accumulate_csr(int dtype, const void* edge_values, const int64_t
                                const int64_t* edge_order, int64_t atom_count,
                                int64_t channel_count, void* out, void* stream);
 
+/* Same result as y3b_density_accumulate, for callers that cannot allocate
+ * device memory (no counterpart in the reference).  A host that owns all
+ * device memory and forbids allocation while it runs -- an MD engine calling
+ * the density from its per-timestep force loop, a server that reserves its
+ * memory at start-up -- cannot hand this library a workspace per call, since
+ * cudaMalloc would synchronise the device and may fail or be disallowed
+ * mid-run.  This entry point allocates nothing: its scratch is a fixed
+ * Y3B_NOALLOC_SCRATCH_BYTES array that every GPU loading the library keeps
+ * until exit, enough when y3b_density_accumulate_workspace_bytes(E, N) is at
+ * most that size; larger problems are rejected with Y3B_ERR_WORKSPACE.  The
+ * first call on a device looks up the array's device address (make it before
+ * any stream capture).  All calls on a device share the array: calls that
+ * overlap on the GPU race and must be serialised by the caller. */
+#define Y3B_NOALLOC_SCRATCH_BYTES (16ll * 1024 * 1024)
+int y3b_density_accumulate_noalloc(int dtype, const void* edge_values, const int64_t* centers,
+                                   int64_t edge_count, int64_t channel_count, int64_t atom_count,
+                                   void* out, int32_t* status, void* stream);
+
 /* edge_adjoint[e, c] = atomic_adjoint[centers[e], c].
  * Replaces ye3t_runtime::density_accumulate_adjoint
  * (execution_plan_torch.cpp, schema next to :7285; CUDA

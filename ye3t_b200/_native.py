@@ -62,6 +62,7 @@ _SIGS = {
                                                      VP]),
     "y3b_density_accumulate_workspace_bytes": (I64, [I64, I64]),
     "y3b_density_accumulate": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, VP, I64, VP, VP, VP]),
+    "y3b_density_accumulate_noalloc": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, VP, VP, VP]),
     "y3b_density_accumulate_csr": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, VP, VP]),
     "y3b_density_accumulate_adjoint": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, VP, VP, VP]),
     "y3b_neighbor_workspace_bytes": (I64, [I64, DBL, DBL]),
