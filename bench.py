@@ -3,10 +3,10 @@
 
 One step = the whole hot path for one configuration of 2^20 atoms (periodic
 cubic box at 0.05 atoms/A^3, 3 species, n_max 8, l_max 3, cutoff 5 A):
-cell-list CSR neighbour list -> A-basis density (kernel 1) -> block pool with
-every symmetric block -> all 25,328 nu <= 4 words / 41,168 L = 0 features per
-atom evaluated from their compiled schedules and contracted with a per-species
-linear readout (kernel 2) -> total energy (NCCL all-reduce when N > 1).
+cell-list CSR neighbour list -> A-basis density (kernel 1) -> symmetric blocks
+and all 25,328 nu <= 4 words / 41,168 L = 0 features per atom evaluated from
+their compiled schedules on chip and contracted with a per-species linear
+readout (kernel 2) -> total energy (NCCL all-reduce when N > 1).
 Atoms are block-partitioned across ranks (strong scaling of the fixed system).
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU
@@ -188,7 +188,8 @@ def _config(args):
                         "n_max 8, l_max 3, nu<=4 (25,328 words / 41,168 L=0 features), fp64, per-species "
                         "linear readout; forces not included",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
-            "parallelism": f"atom-block x{args.gpus}", "l2": "inputs larger than L2 (block pool >> 126 MB)"}
+            "parallelism": f"atom-block x{args.gpus}",
+            "l2": "inputs larger than L2 (A-basis 2 GB, neighbour list 110 MB at 2^20 atoms)"}
 
 
 def run_b200(args):
@@ -219,13 +220,12 @@ def run_b200(args):
     sp_h = species.pin_memory()
     pos_d = pos.to(device)
     sp_d = species.to(device)
-    pool_buf = torch.empty((ev.packed.pool_size, n_local), dtype=torch.complex128, device=device)
     e_buf = torch.empty(n_local, dtype=torch.float64, device=device)
-    timers = {k: [] for k in ("neighbors", "density", "pool", "energy")}
-    launches_per_step = 10  # our kernels: 6 neighbour-count, 1 fill, density, pool, energy
+    timers = {k: [] for k in ("neighbors", "density", "energy")}
+    launches_per_step = 9  # our kernels: 6 neighbour-count, 1 fill, density, B-basis energy
 
     def step(record):
-        ev_marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+        ev_marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
         if record:
             ev_marks[0].record()
         row, nbr = ev.neighbor_list(pos_d, box, begin, end)
@@ -234,12 +234,9 @@ def run_b200(args):
         A = ev.density(pos_d, sp_d, box, row, nbr, begin)
         if record:
             ev_marks[2].record()
-        pool = ev.pool(A, out=pool_buf)
+        e_at = ev.energy_from_density(A, sp_d[begin:end], out=e_buf)
         if record:
             ev_marks[3].record()
-        e_at = ev.energy_from_pool(pool, sp_d[begin:end], out=e_buf)
-        if record:
-            ev_marks[4].record()
         total = e_at.sum()
         if world > 1:
             dist.all_reduce(total)
@@ -298,7 +295,8 @@ def run_b200(args):
     peak = measure_fp64_peak(torch, nat, device)
     flops = ev.packed.flops_per_atom()
     energy_ms = statistics.mean(timers["energy"])
-    sched_flops_launch = (flops["schedule"] + 2.0 * ev.feature_count) * n_local
+    sched_flops_launch = (flops["items"] + 2.0 * ev.feature_count) * n_local
+    term_flops_launch = (flops["terms"] + 2.0 * ev.feature_count) * n_local
     achieved = sched_flops_launch / (energy_ms * 1e-3) / 1e12
     W = (bundle.lmax + 1) ** 2
     dens_ms = statistics.mean(timers["density"])
@@ -335,9 +333,13 @@ def run_b200(args):
         "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
                 "d2h_bytes_per_step": 8},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": {"bound": "fp64", "kernel": "ace_eval_kernel<1> (B-basis energy)", "achieved": achieved,
+        "roofline": {"bound": "fp64", "kernel": "ace_eval_kernel<1> (B-basis energy, symmetric blocks on chip)", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "flops_per_launch": sched_flops_launch,
+                     "flops_note": "FP64 flops the item walk executes on valid tuples (2 complex multiplies "
+                                   "per tuple + 4 per component) plus the readout; the reference's "
+                                   "term-by-term count for the same features is "
+                                   f"{term_flops_launch:.4g} per launch",
                      "peak_source": "FP64 FMA microbenchmark (y3b_fma_peak_launch) measured in this run; "
                                     "MEASURED_PEAKS.json has no FP64 figure"},
         "roofline_density": {"bound": "hbm", "kernel": "ace_density_kernel<3>", "achieved": dens_gbs,

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define Y3B_ABI_VERSION 1
+#define Y3B_ABI_VERSION 3
 
 /* dtype codes */
 #define Y3B_F32 0
@@ -169,25 +169,20 @@ int y3b_neighbor_fill(const double* positions, int64_t atom_count, int64_t cente
  * (ye3t/couplings/__init__.py:4112), see ye3t_b200/packing.py. */
 typedef struct {
   int64_t nmax, lmax;             /* radial channels 1..nmax, l = 0..lmax */
-  int64_t pool_size;              /* complex entries per atom in the block pool */
-  int64_t word_count;
+  int64_t smem_entries;           /* complex entries per atom held in shared memory */
   int64_t feature_count;
-  int64_t sym_kind_count;
-  int32_t max_blocks;
-  const int32_t* word_pattern;          /* [W] */
-  const int32_t* word_label_base;       /* [W] first row of label_bases */
-  const int64_t* word_feature_offset;   /* [W] */
-  const int32_t* pattern_comp_begin;    /* [P+1] */
-  const int32_t* pattern_block_count;   /* [P] */
-  const int32_t* comp_term_begin;       /* [C_total+1] */
-  const int32_t* comp_label;            /* [C_total] */
-  const uint32_t* term_m;               /* [T_total] 4 x uint8: m + L_block */
-  const double* term_coeff;             /* [T_total] real coefficients */
-  const int32_t* label_bases;           /* [rows, 4] pool index of m_idx = 0 */
-  const int32_t* sym_kind;              /* [K, 6]: l, k, Lambda, pool offset, term begin, term end */
-  const uint32_t* sym_term_factors;     /* [S] 4 x uint8 input components (255 = unused) */
-  const int32_t* sym_term_output;       /* [S] */
-  const double* sym_term_coeff;         /* [S] */
+  int64_t item_count;
+  int64_t phase_count;
+  int64_t sym_output_count;       /* symmetric outputs of one radial channel */
+  const int32_t* items;           /* [item_count, 16] evaluation items grouped by phase: dispatch
+                                     code, loop extents, K, coefficient offset, two feature
+                                     indices, four shared-memory block bases */
+  const double* item_coef;        /* dense coefficient tables of the items */
+  const int32_t* phases;          /* [phase_count, 4]: slot-0 channel, slot-1 channel (-1 none),
+                                     item begin, item end */
+  const int32_t* sym_outputs;     /* [sym_output_count, 4]: l^2, term begin, term end, 0 */
+  const uint32_t* sym_term_factors; /* [S] 4 x uint8 input components (255 = unused) */
+  const double* sym_term_coeff;     /* [S] */
 } y3b_ace_tables;
 
 /* A-basis density for centres [center_begin, center_begin + center_count):
@@ -206,22 +201,18 @@ int y3b_ace_density(const double* positions, const int32_t* species, int64_t ato
                     int64_t lmax, double cutoff, double lambda, void* A, int32_t* status,
                     void* stream);
 
-/* Block pool [pool_size, atom_count] complex128 (atom-fastest): the A
- * channels followed by every symmetric block Sym^k(V_l) -> V_Lambda of every
- * radial channel (symmetric_power_product_plan_contraction,
- * ye3t/runtime/symmetric_power.py:879). */
-int y3b_ace_pool(const y3b_ace_tables* tables, const void* A, int64_t atom_count, void* pool,
-                 void* stream);
-
-/* Features [atom_count, feature_count] complex128: every word's factorized
+/* Features [atom_count, feature_count] complex128 of every word's factorized
  * schedule (ACEFactorizedScheduleReport.evaluate,
- * ye3t/couplings/__init__.py:2574) on its blocks from the pool. */
-int y3b_ace_features(const y3b_ace_tables* tables, const void* pool, int64_t atom_count,
-                     void* features, void* stream);
+ * ye3t/couplings/__init__.py:2574) from the A-basis, with every symmetric
+ * block Sym^k(V_l) -> V_Lambda (symmetric_power_product_plan_contraction,
+ * ye3t/runtime/symmetric_power.py:879) formed on chip.  A is the complex128
+ * [atom_count, nmax, (lmax+1)^2] output of y3b_ace_density. */
+int y3b_ace_features(const y3b_ace_tables* tables, const void* A, int64_t atom_count, void* features,
+                     void* stream);
 
 /* Per-atom energy e[i] = sum_f weights[species[i], f] Re(B[i, f]) with B
- * evaluated in registers and never stored. */
-int y3b_ace_energy(const y3b_ace_tables* tables, const void* pool, int64_t atom_count,
+ * evaluated on chip and never stored (species/energy indexed like A). */
+int y3b_ace_energy(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
                    const int32_t* species, const double* weights, int64_t species_count,
                    double* energy, void* stream);
 

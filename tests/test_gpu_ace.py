@@ -1,4 +1,4 @@
-"""Fused ACE path (neighbour list, A-basis, block pool, bundle) against the
+"""Fused ACE path (neighbour list, A-basis, on-chip symmetric blocks, bundle) against the
 reference golden vectors and the oracle."""
 
 import os
@@ -106,8 +106,7 @@ def test_energy_equals_readout_of_features_nu4(ev4):
     sp = torch.as_tensor(rng.integers(0, 3, size=N), device=DEV)
     row, nbr = ev4.neighbor_list(pos, box)
     A = ev4.density(pos, sp, box, row, nbr)
-    pool = ev4.pool(A)
-    e = ev4.energy_from_pool(pool, sp)
+    e = ev4.energy_from_density(A, sp)
     sel = torch.arange(0, N, 61, device=DEV)
     Bs = ev4.features(A[sel])
     e_ref = (ev4.weights[sp[sel].long()] * Bs.real).sum(1)

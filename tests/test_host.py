@@ -34,7 +34,7 @@ def test_library_argument_errors_without_gpu():
     assert lib.y3b_density_accumulate_workspace_bytes(100, 10) > 0
     assert lib.y3b_density_accumulate_workspace_bytes(-1, 10) == -1
     assert lib.y3b_neighbor_workspace_bytes(1000, 30.0, 5.0) > 0
-    rc = lib.y3b_ace_pool(None, 0, 10, 0, 0)
+    rc = lib.y3b_ace_features(None, 0, 10, 0, 0)
     assert rc == -1
 
 

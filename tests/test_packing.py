@@ -18,15 +18,22 @@ def _bundle(stem):
     return ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", stem + ".npz"))
 
 
-def emulate_pool(pb, A):
+def emulate_features(pb, A):
+    """numpy walk of the packed phases and items, in the kernel's order."""
+    from ye3t_b200.packing import ITEM_INTS
     a = {k: v.cpu().numpy() for k, v in pb.arrays.items()}
     N, nmax, W = A.shape
-    pool = np.zeros((pb.pool_size, N), dtype=np.complex128)
-    pool[: nmax * W] = A.reshape(N, nmax * W).T
-    for l, k, Lam, off, tb, te in a["sym_kind"]:
-        dimo = 2 * Lam + 1
-        for n in range(nmax):
-            x = A[:, n, l * l:(l + 1) * (l + 1)]
+    na = nmax * W
+    so = a["sym_outputs"].shape[0]
+    sm = np.zeros((na + 2 * so, N), dtype=np.complex128)
+    sm[:na] = A.reshape(N, na).T
+    coef = a["item_coef"]
+    out = np.zeros((N, pb.feature_count), dtype=np.complex128)
+
+    def fill(slot, ch):
+        for o, (l2, tb, te, _) in enumerate(a["sym_outputs"]):
+            x = sm[ch * W + l2: ch * W + l2 + 16]
+            acc = np.zeros(N, dtype=np.complex128)
             for q in range(tb, te):
                 f = int(np.uint32(a["sym_term_factors"][q]))
                 m = np.full(N, a["sym_term_coeff"][q], dtype=np.complex128)
@@ -34,31 +41,51 @@ def emulate_pool(pb, A):
                     ci = (f >> (8 * kk)) & 255
                     if ci == 255:
                         break
-                    m = m * x[:, ci]
-                pool[off + n * dimo + a["sym_term_output"][q]] += m
-    return pool
+                    m = m * x[ci]
+                acc += m
+            sm[na + slot * so + o] = acc
 
-
-def emulate_features(pb, pool):
-    a = {k: v.cpu().numpy() for k, v in pb.arrays.items()}
-    N = pool.shape[1]
-    out = np.zeros((N, pb.feature_count), dtype=np.complex128)
-    for w in range(pb.bundle.word_count):
-        p = a["word_pattern"][w]
-        B = a["pattern_block_count"][p]
-        lb = a["word_label_base"][w]
-        fo = a["word_feature_offset"][w]
-        c0, c1 = a["pattern_comp_begin"][p], a["pattern_comp_begin"][p + 1]
-        for c in range(c0, c1):
-            base = a["label_bases"][lb + a["comp_label"][c]]
-            acc = np.zeros(N, dtype=np.complex128)
-            for q in range(a["comp_term_begin"][c], a["comp_term_begin"][c + 1]):
-                mm = int(np.uint32(a["term_m"][q]))
-                v = a["term_coeff"][q] * pool[base[0] + (mm & 255)]
-                for b in range(1, B):
-                    v = v * pool[base[b] + ((mm >> (8 * b)) & 255)]
-                acc += v
-            out[:, fo + c - c0] = acc
+    cur = (None, None)
+    for c0, c1, ib, ie in a["phases"]:
+        if c0 != cur[0]:
+            fill(0, c0)
+        if c1 >= 0 and c1 != cur[1]:
+            fill(1, c1)
+        cur = (c0, c1)
+        for row in a["items"][ib:ie]:
+            sel, d0, d1, dl, K, co, f0, f1 = (int(v) for v in row[:8])
+            bases = [int(v) for v in row[8:12]]
+            nc = sel % 2 + 1
+            B = (sel // 2) // 7 + 1
+            ds = 2 * ((sel // 2) % 7) + 1
+            acc = [np.zeros(N, dtype=np.complex128) for _ in range(nc)]
+            rw = 2 * ds if nc == 2 else (ds + 1) & ~1
+            if B == 1:
+                for k in range(nc):
+                    acc[k] += coef[co + k] * sm[bases[0] + K]
+            else:
+                prefixes = [((), 0, np.ones(N, dtype=np.complex128))]
+                if B == 3:
+                    prefixes = [((i0,), i0 * rw, sm[bases[0] + i0]) for i0 in range(d0)]
+                elif B == 4:
+                    prefixes = [((i0, i1), (i0 * d1 + i1) * rw, sm[bases[0] + i0] * sm[bases[1] + i1])
+                                for i0 in range(d0) for i1 in range(d1)]
+                bs, bl = bases[B - 2], bases[B - 1]
+                for pre, crow, x in prefixes:
+                    S = sum(pre)
+                    t = [np.zeros(N, dtype=np.complex128) for _ in range(nc)]
+                    for j in range(ds):
+                        li = K - S - j
+                        if 0 <= li < dl:
+                            q = sm[bs + j] * sm[bl + li]
+                            for k in range(nc):
+                                t[k] += coef[co + crow + j * nc + k] * q
+                    for k in range(nc):
+                        acc[k] += x * t[k]
+            out[:, f0] = acc[0]
+            if f1 >= 0:
+                out[:, f1] = acc[1]
+    assert a["items"].shape[1] == ITEM_INTS
     return out
 
 
@@ -68,8 +95,11 @@ def test_packing_layout_and_counts():
     assert pb.feature_count == 41168
     assert pb.term_count_per_atom == 1332116
     assert pb.term_block_count_per_atom == 5163248
-    assert pb.pool_size == 8 * 16 + 8 * 89
+    assert pb.pool_size == 8 * 16 + 2 * 89  # shared-memory entries per atom
+    assert pb.arrays["phases"].shape[0] == 28
     assert pb.max_blocks == 4
+    flops = pb.flops_per_atom()
+    assert 0 < flops["items"] < flops["terms"]
 
 
 @pytest.mark.parametrize("stem", ["ace_n8_l3_nu3_L0"])
@@ -78,8 +108,7 @@ def test_packed_tables_reproduce_oracle_features(golden, stem):
     A = g["A"][:6]
     b = _bundle(stem)
     pb = pack_bundle(b, "cpu")
-    pool = emulate_pool(pb, A)
-    got = emulate_features(pb, pool)
+    got = emulate_features(pb, A)
     ref = oracle.bundle_features(b, A)
     np.testing.assert_allclose(got, ref, rtol=1e-12, atol=1e-12 * np.abs(ref).max())
     np.testing.assert_allclose(got, g["B3"][:6], rtol=1e-11, atol=1e-12 * np.abs(ref).max())

@@ -16,7 +16,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libye3t_b200.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 3
 F32, F64, C64, C128 = 0, 1, 2, 3
 STATUS_INDEX_RANGE = 1
 STATUS_CAPACITY = 2
@@ -42,12 +42,9 @@ class AceTables(ctypes.Structure):
     """``y3b_ace_tables`` (include/ye3t_b200.h)."""
 
     _fields_ = [
-        ("nmax", I64), ("lmax", I64), ("pool_size", I64), ("word_count", I64), ("feature_count", I64),
-        ("sym_kind_count", I64), ("max_blocks", I32),
-        ("word_pattern", VP), ("word_label_base", VP), ("word_feature_offset", VP),
-        ("pattern_comp_begin", VP), ("pattern_block_count", VP), ("comp_term_begin", VP),
-        ("comp_label", VP), ("term_m", VP), ("term_coeff", VP), ("label_bases", VP),
-        ("sym_kind", VP), ("sym_term_factors", VP), ("sym_term_output", VP), ("sym_term_coeff", VP),
+        ("nmax", I64), ("lmax", I64), ("smem_entries", I64), ("feature_count", I64), ("item_count", I64),
+        ("phase_count", I64), ("sym_output_count", I64), ("items", VP), ("item_coef", VP), ("phases", VP),
+        ("sym_outputs", VP), ("sym_term_factors", VP), ("sym_term_coeff", VP),
     ]
 
 
@@ -70,7 +67,6 @@ _SIGS = {
     "y3b_neighbor_fill": (ctypes.c_int, [VP, I64, I64, I64, DBL, DBL, VP, I64, VP, VP, VP]),
     "y3b_ace_density": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                        VP]),
-    "y3b_ace_pool": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
     "y3b_ace_features": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
     "y3b_ace_energy": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP]),
     "y3b_fma_peak_launch": (ctypes.c_int, [ctypes.c_int, I32, I32, I32, VP, ctypes.POINTER(DBL), VP]),

@@ -9,10 +9,10 @@ Pipeline for the centres ``[begin, end)`` of a periodic cubic box:
    reference's radial table (``ye3t/runtime/execution_plan.py:7298``), complex
    harmonics (``:7479``), per-neighbour prefactor (``:7582``) and
    ``density_accumulate`` (``:7913``), fused;
-3. block pool (``y3b_ace_pool``): A plus every symmetric block
-   (``symmetric_power_product_plan_contraction``,
-   ``ye3t/runtime/symmetric_power.py:879``);
-4. B-basis (kernel 2): every word's factorized schedule
+3. B-basis (kernel 2, ``y3b_ace_features`` / ``y3b_ace_energy``): the
+   symmetric blocks (``symmetric_power_product_plan_contraction``,
+   ``ye3t/runtime/symmetric_power.py:879``) formed on chip, then every word's
+   factorized schedule
    (``ACEFactorizedScheduleReport.evaluate``,
    ``ye3t/couplings/__init__.py:2574``) -- either written out as features or
    contracted with a per-species linear readout into per-atom energies.
@@ -105,37 +105,30 @@ class ACEEvaluator:
         return A
 
     # -- kernel 2 ----------------------------------------------------------------
-    def pool(self, A: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def features(self, A: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """B-basis features ``[n, feature_count]`` complex128 from the A-basis."""
         A = A.to(self.device, torch.complex128).contiguous()
         n = A.shape[0]
         if out is None:
-            out = torch.empty((self.packed.pool_size, n), dtype=torch.complex128, device=self.device)
-        nat.check(nat.lib().y3b_ace_pool(ctypes_ref(self._tables), A.data_ptr(), n, out.data_ptr(),
-                                         self._stream()), "ace_pool")
-        return out
-
-    def features_from_pool(self, pool: torch.Tensor) -> torch.Tensor:
-        n = pool.shape[1]
-        out = torch.empty((n, self.packed.feature_count), dtype=torch.complex128, device=self.device)
-        nat.check(nat.lib().y3b_ace_features(ctypes_ref(self._tables), pool.data_ptr(), n, out.data_ptr(),
+            out = torch.empty((n, self.packed.feature_count), dtype=torch.complex128, device=self.device)
+        nat.check(nat.lib().y3b_ace_features(ctypes_ref(self._tables), A.data_ptr(), n, out.data_ptr(),
                                              self._stream()), "ace_features")
         return out
 
-    def energy_from_pool(self, pool: torch.Tensor, species_centres: torch.Tensor,
-                         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def energy_from_density(self, A: torch.Tensor, species_centres: torch.Tensor,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Per-atom energies ``sum_f w[z, f] Re(B_f)`` from the A-basis (B never stored)."""
         if self.weights is None:
             raise ValueError("weights are required for the energy")
-        n = pool.shape[1]
+        A = A.to(self.device, torch.complex128).contiguous()
+        n = A.shape[0]
         sp = species_centres.to(self.device, torch.int32).contiguous()
         if out is None:
             out = torch.empty(n, dtype=torch.float64, device=self.device)
-        nat.check(nat.lib().y3b_ace_energy(ctypes_ref(self._tables), pool.data_ptr(), n, sp.data_ptr(),
+        nat.check(nat.lib().y3b_ace_energy(ctypes_ref(self._tables), A.data_ptr(), n, sp.data_ptr(),
                                            self.weights.data_ptr(), self.weights.shape[0], out.data_ptr(),
                                            self._stream()), "ace_energy")
         return out
-
-    def features(self, A: torch.Tensor) -> torch.Tensor:
-        return self.features_from_pool(self.pool(A))
 
     # -- end to end ----------------------------------------------------------------
     def energy(self, positions, species, box, begin: int = 0, end: Optional[int] = None):
@@ -144,9 +137,8 @@ class ACEEvaluator:
         end = N if end is None else int(end)
         row, nbr = self.neighbor_list(positions, box, begin, end)
         A = self.density(positions, species, box, row, nbr, begin)
-        pool = self.pool(A)
         sp = species.to(self.device, torch.int32)[begin:end]
-        return self.energy_from_pool(pool, sp)
+        return self.energy_from_density(A, sp)
 
 
 def ctypes_ref(tables):

@@ -108,112 +108,300 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX>::value) ace_density_ke
 }
 
 // ---------------------------------------------------------------------------
-// Block pool: pool[idx][atom] (atom fastest) holding the A channels and every
-// symmetric block of every radial channel.  One thread per atom.
-// Symmetric terms multiply the coefficient by x_i^{k_i} for each distinct
-// input component in increasing order, as ye3t_runtime_core.cpp:5279.
+// Kernel 2: the B-basis of every word, from shared memory.
+//
+// A CTA owns 32 atoms (lane = atom).  Its shared memory holds, per entry, one
+// complex value for each of the 32 atoms ([entry][lane]: a warp reads an
+// entry as one conflict-free 512-byte row):
+//   * the A channels of all radial channels (entries 0 .. nmax W - 1);
+//   * two slots, each holding every symmetric block Sym^k(A[n, l]) -> V_Lambda
+//     of one radial channel n (symmetric_power_product_plan_contraction,
+//     ye3t/runtime/symmetric_power.py:879), recomputed here when a phase
+//     changes the slot's channel.
+// Words are grouped in phases by the radial channels of their symmetric
+// blocks (at most two per word).  Inside a phase the CTA's warps share the
+// items round robin.  An item is one pass (<= 2 components) over one group
+// of a word: components whose labels bind the same blocks and share M.  Its
+// coefficients form a dense table over the magnetic indices of blocks
+// 0..B-2; the last block's index follows from M conservation,
+//   i_last = K - sum_{b < B-1} i_b,  K = M + sum_b L_b,
+// and the sum is evaluated in nested order
+//   B_c = sum_{i0} v0 ( sum_{i1} v1 ( sum_j C[i0, i1, j, c] vs[j] v_last ) )
+// with block B-2 (vs) unrolled at compile time and held in registers.
+// MODE 0 writes features [N, F]; MODE 1 reduces to per-atom energy.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) ace_pool_kernel(y3b_ace_tables t, const double2* __restrict__ A,
-                                                       int64_t N, double2* __restrict__ pool) {
-  const int W = int((t.lmax + 1) * (t.lmax + 1));
-  const int na = int(t.nmax) * W;
-  for (int64_t a = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; a < N;
-       a += int64_t(gridDim.x) * blockDim.x) {
-    const double2* Aa = A + a * na;
-    for (int idx = 0; idx < na; ++idx) pool[idx * N + a] = Aa[idx];
-    for (int s = 0; s < t.sym_kind_count; ++s) {
-      const int l = __ldg(t.sym_kind + 6 * s + 0);
-      const int Lam = __ldg(t.sym_kind + 6 * s + 2);
-      const int off = __ldg(t.sym_kind + 6 * s + 3);
-      const int tb = __ldg(t.sym_kind + 6 * s + 4), te = __ldg(t.sym_kind + 6 * s + 5);
-      const int dimo = 2 * Lam + 1;
-      for (int n = 0; n < t.nmax; ++n) {
-        const double2* x = Aa + n * W + l * l;
-        for (int o = 0; o < dimo; ++o) pool[int64_t(off + n * dimo + o) * N + a] = make_double2(0.0, 0.0);
-        for (int q = tb; q < te; ++q) {
-          const int o = __ldg(t.sym_term_output + q);
-          const uint32_t f = __ldg(t.sym_term_factors + q);
-          const double c = __ldg(t.sym_term_coeff + q);
-          double2 m = make_double2(c, 0.0);
-          int k = 0;
-          while (k < 4) {
-            const int ci = (f >> (8 * k)) & 255;
-            if (ci == 255) break;
-            double2 r = x[ci];
-            ++k;
-            while (k < 4 && int((f >> (8 * k)) & 255) == ci) {
-              r = mul(r, x[ci]);
-              ++k;
-            }
-            m = mul(m, r);
-          }
-          double2* dst = pool + int64_t(off + n * dimo + o) * N + a;
-          *dst = add(*dst, m);
-        }
+constexpr int kLanes = 32;
+constexpr int kEvalWarps = 16;
+
+struct Item {
+  int sel, d0, d1, dl, K, coef, f0, f1;
+  int b0, b1, b2, b3;
+};
+
+__device__ __forceinline__ Item load_item(const int4* __restrict__ items, int64_t i) {
+  const int4 a = __ldg(items + 4 * i), b = __ldg(items + 4 * i + 1), c = __ldg(items + 4 * i + 2);
+  Item it;
+  it.sel = a.x; it.d0 = a.y; it.d1 = a.z; it.dl = a.w;
+  it.K = b.x; it.coef = b.y; it.f0 = b.z; it.f1 = b.w;
+  it.b0 = c.x; it.b1 = c.y; it.b2 = c.z; it.b3 = c.w;
+  return it;
+}
+
+__device__ __forceinline__ void cmac(double2& acc, double c, double2 v) {
+  acc.x = fma(c, v.x, acc.x);
+  acc.y = fma(c, v.y, acc.y);
+}
+
+// acc += x * t (complex multiply-add)
+__device__ __forceinline__ void cfma(double2& acc, double2 x, double2 t) {
+  acc.x = fma(x.x, t.x, fma(-x.y, t.y, acc.x));
+  acc.y = fma(x.x, t.y, fma(x.y, t.x, acc.y));
+}
+
+// B = 1: a single tuple, i_0 = K.
+template <int NC>
+__device__ __forceinline__ void eval_b1(const double2* __restrict__ P, const Item& it,
+                                        const double* __restrict__ coef, double2& a0, double2& a1) {
+  const double2 v = P[(it.b0 + it.K) * kLanes];
+  cmac(a0, __ldg(coef + it.coef), v);
+  if (NC == 2) cmac(a1, __ldg(coef + it.coef + 1), v);
+}
+
+// Coefficient row of one prefix: NC doubles per j, padded to an even count so
+// that a 16-byte load returns two coefficients (packing.py lays rows out so).
+template <int DS, int NC>
+struct RowWidth {
+  static constexpr int value = NC == 2 ? 2 * DS : ((DS + 1) & ~1);
+};
+
+// T_c += C[j, c] * (vs[j] * v_last[kS - j]) for j in [jlo, jhi], the j whose
+// last index lies in the block.  Pk points at v_last[kS], so every j reads
+// at a compile-time offset from it.  Odd and even j accumulate separately
+// (two independent FMA chains).
+template <int DS, int NC>
+__device__ __forceinline__ void row_sum(const double2* __restrict__ Pk, int jlo, int jhi,
+                                        const double2 (&vs)[DS], const double* __restrict__ crow,
+                                        double2& t0, double2& t1) {
+  const double2* cr2 = reinterpret_cast<const double2*>(crow);
+  double2 o0 = make_double2(0.0, 0.0), o1 = o0;
+#pragma unroll
+  for (int j = 0; j < DS; ++j) {
+    if (j >= jlo && j <= jhi) {
+      double c0, c1 = 0.0;
+      if (NC == 2) {
+        const double2 cc = __ldg(cr2 + j);
+        c0 = cc.x;
+        c1 = cc.y;
+      } else {
+        const double2 cc = __ldg(cr2 + (j >> 1));
+        c0 = (j & 1) ? cc.y : cc.x;
       }
+      const double2 q = mul(vs[j], Pk[-j * kLanes]);
+      if (j & 1) {
+        cmac(o0, c0, q);
+        if (NC == 2) cmac(o1, c1, q);
+      } else {
+        cmac(t0, c0, q);
+        if (NC == 2) cmac(t1, c1, q);
+      }
+    }
+  }
+  t0 = add(t0, o0);
+  if (NC == 2) t1 = add(t1, o1);
+}
+
+template <int B, int DS, int NC>
+__device__ __forceinline__ void eval_item(const double2* __restrict__ P, const Item& it,
+                                          const double* __restrict__ coef, double2& a0, double2& a1) {
+  constexpr int RW = RowWidth<DS, NC>::value;
+  const int bs = B == 2 ? it.b0 : (B == 3 ? it.b1 : it.b2);  // block held in registers
+  const int bl = B == 2 ? it.b1 : (B == 3 ? it.b2 : it.b3);  // last block
+  double2 vs[DS];
+#pragma unroll
+  for (int j = 0; j < DS; ++j) vs[j] = P[(bs + j) * kLanes];
+  const double2* Pl = P + bl * kLanes;
+  const double* c = coef + it.coef;
+  const int dl = it.dl;
+  // a prefix with index sum S has tuples only for S in [smin, smax]
+  const int smin = it.K - (DS - 1) - (dl - 1), smax = it.K;
+  if (B == 2) {
+    const int kS = it.K;
+    row_sum<DS, NC>(Pl + kS * kLanes, max(0, kS - dl + 1), min(DS - 1, kS), vs, c, a0, a1);
+  } else if (B == 3) {
+    for (int i0 = max(0, smin); i0 < it.d0 && i0 <= smax; ++i0) {
+      const int kS = it.K - i0;
+      double2 t0 = make_double2(0.0, 0.0), t1 = t0;
+      row_sum<DS, NC>(Pl + kS * kLanes, max(0, kS - dl + 1), min(DS - 1, kS), vs, c + i0 * RW, t0, t1);
+      const double2 x0 = P[(it.b0 + i0) * kLanes];
+      cfma(a0, x0, t0);
+      if (NC == 2) cfma(a1, x0, t1);
+    }
+  } else {
+    for (int i0 = 0; i0 < it.d0 && i0 <= smax; ++i0) {
+      double2 u0 = make_double2(0.0, 0.0), u1 = u0;
+      const int i1lo = max(0, smin - i0), i1hi = min(it.d1 - 1, smax - i0);
+      for (int i1 = i1lo; i1 <= i1hi; ++i1) {
+        const int kS = it.K - i0 - i1;
+        double2 t0 = make_double2(0.0, 0.0), t1 = t0;
+        row_sum<DS, NC>(Pl + kS * kLanes, max(0, kS - dl + 1), min(DS - 1, kS), vs,
+                        c + (i0 * it.d1 + i1) * RW, t0, t1);
+        const double2 x1 = P[(it.b1 + i1) * kLanes];
+        cfma(u0, x1, t0);
+        if (NC == 2) cfma(u1, x1, t1);
+      }
+      const double2 x0 = P[(it.b0 + i0) * kLanes];
+      cfma(a0, x0, u0);
+      if (NC == 2) cfma(a1, x0, u1);
     }
   }
 }
 
-// ---------------------------------------------------------------------------
-// Kernel 2: every word's schedule on blocks from the pool.  One thread per
-// atom; the whole warp walks the same word/component/term sequence, so all
-// table reads are uniform and every pool read is a coalesced 512-byte row
-// segment.  MODE 0 writes features [N, F]; MODE 1 reduces to per-atom energy.
-// ---------------------------------------------------------------------------
-template <int MODE>
-__global__ void __launch_bounds__(128) ace_eval_kernel(y3b_ace_tables t, const double2* __restrict__ pool,
-                                                       int64_t N, double2* __restrict__ feats,
-                                                       const int32_t* __restrict__ species,
-                                                       const double* __restrict__ weights, int64_t S,
-                                                       double* __restrict__ energy) {
-  const int64_t a = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
-  const bool live = a < N;
-  const int64_t aa = live ? a : 0;
-  const double2* P = pool + aa;
-  int z = 0;
-  if (MODE == 1 && live) {
-    z = species[aa];
-    if (z < 0 || z >= S) z = 0;
+__device__ __forceinline__ void eval_dispatch(const double2* __restrict__ P, const Item& it,
+                                              const double* __restrict__ coef, double2& a0, double2& a1) {
+#define Y3B_ITEM_CASE(B, DS, NC)                                          \
+  case ((B - 1) * 7 + (DS - 1) / 2) * 2 + (NC - 1):                      \
+    eval_item<B, DS, NC>(P, it, coef, a0, a1);                           \
+    break;
+#define Y3B_ITEM_DS(B, DS) Y3B_ITEM_CASE(B, DS, 1) Y3B_ITEM_CASE(B, DS, 2)
+#define Y3B_ITEM_B(B) \
+  Y3B_ITEM_DS(B, 1) Y3B_ITEM_DS(B, 3) Y3B_ITEM_DS(B, 5) Y3B_ITEM_DS(B, 7) Y3B_ITEM_DS(B, 9) \
+  Y3B_ITEM_DS(B, 11) Y3B_ITEM_DS(B, 13)
+  switch (it.sel) {
+    case 0: eval_b1<1>(P, it, coef, a0, a1); break;
+    case 1: eval_b1<2>(P, it, coef, a0, a1); break;
+    Y3B_ITEM_B(2)
+    Y3B_ITEM_B(3)
+    Y3B_ITEM_B(4)
+    default: break;
   }
-  double e_acc = 0.0;
-  for (int64_t w = 0; w < t.word_count; ++w) {
-    const int p = __ldg(t.word_pattern + w);
-    const int B = __ldg(t.pattern_block_count + p);
-    const int c0 = __ldg(t.pattern_comp_begin + p), c1 = __ldg(t.pattern_comp_begin + p + 1);
-    const int lb = __ldg(t.word_label_base + w);
-    const int64_t fo = __ldg(t.word_feature_offset + w);
-    for (int c = c0; c < c1; ++c) {
-      const int label = __ldg(t.comp_label + c);
-      const int4 base = __ldg(reinterpret_cast<const int4*>(t.label_bases) + (lb + label));
-      double2 acc = make_double2(0.0, 0.0);
-      const int tb = __ldg(t.comp_term_begin + c), te = __ldg(t.comp_term_begin + c + 1);
-      for (int q = tb; q < te; ++q) {
-        const uint32_t mm = __ldg(t.term_m + q);
-        const double cf = __ldg(t.term_coeff + q);
-        double2 v = P[int64_t(base.x + int(mm & 255)) * N];
-        v = make_double2(cf * v.x, cf * v.y);
-        if (B > 1) v = mul(v, P[int64_t(base.y + int((mm >> 8) & 255)) * N]);
-        if (B > 2) v = mul(v, P[int64_t(base.z + int((mm >> 16) & 255)) * N]);
-        if (B > 3) v = mul(v, P[int64_t(base.w + int(mm >> 24)) * N]);
-        acc = add(acc, v);
+#undef Y3B_ITEM_B
+#undef Y3B_ITEM_DS
+#undef Y3B_ITEM_CASE
+}
+
+// Fill shared-memory slot `slot` with every symmetric output of radial
+// channel `ch`: out = sum_q coeff_q prod_i x_i^{k_qi}, the powers of each
+// distinct input component multiplied in increasing component order as in
+// ye3t_runtime_core.cpp:5279.
+__device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, double2* __restrict__ sm, int W, int slot,
+                                          int ch, int lane, int warp) {
+  const int na = int(t.nmax) * W;
+  const int so = int(t.sym_output_count);
+  const int4* outs = reinterpret_cast<const int4*>(t.sym_outputs);
+  for (int o = warp; o < so; o += kEvalWarps) {
+    const int4 r = __ldg(outs + o);  // (l^2, term begin, term end, -)
+    const double2* x = sm + (ch * W + r.x) * kLanes + lane;
+    double2 acc = make_double2(0.0, 0.0);
+    for (int q = r.y; q < r.z; ++q) {
+      const uint32_t f = __ldg(t.sym_term_factors + q);
+      double2 m = make_double2(__ldg(t.sym_term_coeff + q), 0.0);
+      int k = 0;
+      while (k < 4) {
+        const int ci = (f >> (8 * k)) & 255;
+        if (ci == 255) break;
+        const double2 xv = x[ci * kLanes];
+        double2 pw = xv;
+        ++k;
+        while (k < 4 && int((f >> (8 * k)) & 255) == ci) {
+          pw = mul(pw, xv);
+          ++k;
+        }
+        m = mul(m, pw);
       }
+      acc = add(acc, m);
+    }
+    sm[(na + slot * so + o) * kLanes + lane] = acc;
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
+    y3b_ace_tables t, const double2* __restrict__ A, int64_t N, double2* __restrict__ feats,
+    const int32_t* __restrict__ species, const double* __restrict__ weights, int64_t S,
+    double* __restrict__ energy) {
+  extern __shared__ double2 sm[];
+  __shared__ double red[kEvalWarps][kLanes];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int W = int((t.lmax + 1) * (t.lmax + 1));
+  const int na = int(t.nmax) * W;
+  const int64_t a = blockIdx.x * int64_t(kLanes) + lane;
+  const bool live = a < N;
+  for (int e = warp; e < na; e += kEvalWarps)
+    sm[e * kLanes + lane] = live ? A[a * na + e] : make_double2(0.0, 0.0);
+  const double* wz = weights;
+  if (MODE == 1) {
+    int z = live ? species[a] : 0;
+    if (z < 0 || z >= S) z = 0;
+    wz = weights + int64_t(z) * t.feature_count;
+  }
+  const double2* P = sm + lane;
+  const int4* items = reinterpret_cast<const int4*>(t.items);
+  const int4* phases = reinterpret_cast<const int4*>(t.phases);
+  int cur0 = -2, cur1 = -2;
+  double e_acc = 0.0;
+  for (int ph = 0; ph < t.phase_count; ++ph) {
+    const int4 pr = __ldg(phases + ph);
+    if (pr.x != cur0 || pr.y != cur1) {
+      __syncthreads();  // previous phase's items are done with the slots (and A is loaded)
+      if (pr.x != cur0) fill_slot(t, sm, W, 0, pr.x, lane, warp);
+      if (pr.y != cur1 && pr.y >= 0) fill_slot(t, sm, W, 1, pr.y, lane, warp);
+      __syncthreads();
+      cur0 = pr.x;
+      cur1 = pr.y;
+    }
+    for (int i = pr.z + warp; i < pr.w; i += kEvalWarps) {
+      const Item it = load_item(items, i);
+      double2 a0 = make_double2(0.0, 0.0), a1 = a0;
+      eval_dispatch(P, it, t.item_coef, a0, a1);
       if (MODE == 0) {
-        if (live) feats[aa * t.feature_count + fo + (c - c0)] = acc;
+        if (live) {
+          feats[a * t.feature_count + it.f0] = a0;
+          if (it.f1 >= 0) feats[a * t.feature_count + it.f1] = a1;
+        }
       } else {
-        e_acc += __ldg(weights + int64_t(z) * t.feature_count + fo + (c - c0)) * acc.x;
+        e_acc = fma(__ldg(wz + it.f0), a0.x, e_acc);
+        if (it.f1 >= 0) e_acc = fma(__ldg(wz + it.f1), a1.x, e_acc);
       }
     }
   }
-  if (MODE == 1 && live) energy[aa] = e_acc;
+  if (MODE == 1) {
+    red[warp][lane] = e_acc;
+    __syncthreads();
+    if (warp == 0 && live) {
+      double s = 0.0;
+      for (int w = 0; w < kEvalWarps; ++w) s += red[w][lane];
+      energy[a] = s;
+    }
+  }
+}
+
+inline size_t eval_smem_bytes(const y3b_ace_tables& t) {
+  return size_t(t.smem_entries) * kLanes * sizeof(double2);
 }
 
 int check_tables(const y3b_ace_tables* t) {
   Y3B_CHECK_ARG(t != nullptr, "null tables");
   Y3B_CHECK_ARG(t->nmax >= 1 && t->nmax <= kMaxNmax, "nmax must be in [1, %d]", kMaxNmax);
   Y3B_CHECK_ARG(t->lmax >= 0 && t->lmax <= 6, "lmax must be in [0, 6]");
-  Y3B_CHECK_ARG(t->max_blocks >= 1 && t->max_blocks <= 4, "bundles with more than 4 blocks per word are not supported");
-  Y3B_CHECK_ARG(t->word_count >= 0 && t->feature_count >= 0 && t->pool_size >= 0, "negative table size");
+  Y3B_CHECK_ARG(t->item_count >= 0 && t->feature_count >= 0 && t->phase_count >= 1, "bad table sizes");
+  Y3B_CHECK_ARG(t->item_count == 0 || (t->items && t->item_coef && t->phases), "null item tables");
+  Y3B_CHECK_ARG(t->smem_entries >= t->nmax * (t->lmax + 1) * (t->lmax + 1) + 2 * t->sym_output_count,
+                "shared-memory entry count too small");
+  Y3B_CHECK_ARG(eval_smem_bytes(*t) <= 200 * 1024, "bundle needs %lld bytes of shared memory per CTA (max 200 KB)",
+                (long long)eval_smem_bytes(*t));
+  return Y3B_OK;
+}
+
+template <int MODE>
+int launch_eval(const y3b_ace_tables* t, const void* A, int64_t n, double2* feats, const int32_t* species,
+                const double* weights, int64_t S, double* energy, cudaStream_t s) {
+  const size_t smem = eval_smem_bytes(*t);
+  Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_eval_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int64_t grid = (n + kLanes - 1) / kLanes;
+  Y3B_CHECK_ARG(grid < (int64_t(1) << 31), "too many atoms");
+  ace_eval_kernel<MODE><<<int(grid), kLanes * kEvalWarps, smem, s>>>(*t, static_cast<const double2*>(A), n,
+                                                                      feats, species, weights, S, energy);
+  Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }
 
@@ -260,43 +448,23 @@ extern "C" int y3b_ace_density(const double* positions, const int32_t* species, 
   return Y3B_OK;
 }
 
-extern "C" int y3b_ace_pool(const y3b_ace_tables* tables, const void* A, int64_t atom_count, void* pool,
-                            void* stream) {
+extern "C" int y3b_ace_features(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
+                                void* features, void* stream) {
   if (int rc = check_tables(tables)) return rc;
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
-  Y3B_CHECK_ARG(A && pool, "null pointer argument");
-  ace_pool_kernel<<<grid_for(atom_count, 128), 128, 0, as_stream(stream)>>>(
-      *tables, static_cast<const double2*>(A), atom_count, static_cast<double2*>(pool));
-  Y3B_LAUNCH_CHECK();
-  return Y3B_OK;
+  Y3B_CHECK_ARG(A && features, "null pointer argument");
+  return launch_eval<0>(tables, A, atom_count, static_cast<double2*>(features), nullptr, nullptr, 0, nullptr,
+                        as_stream(stream));
 }
 
-extern "C" int y3b_ace_features(const y3b_ace_tables* tables, const void* pool, int64_t atom_count,
-                                void* features, void* stream) {
-  if (int rc = check_tables(tables)) return rc;
-  if (atom_count == 0) return Y3B_OK;
-  Y3B_CHECK_ARG(pool && features, "null pointer argument");
-  const int threads = 128;
-  const int64_t grid = (atom_count + threads - 1) / threads;
-  ace_eval_kernel<0><<<int(grid), threads, 0, as_stream(stream)>>>(
-      *tables, static_cast<const double2*>(pool), atom_count, static_cast<double2*>(features),
-      nullptr, nullptr, 0, nullptr);
-  Y3B_LAUNCH_CHECK();
-  return Y3B_OK;
-}
-
-extern "C" int y3b_ace_energy(const y3b_ace_tables* tables, const void* pool, int64_t atom_count,
+extern "C" int y3b_ace_energy(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
                               const int32_t* species, const double* weights, int64_t species_count,
                               double* energy, void* stream) {
   if (int rc = check_tables(tables)) return rc;
+  Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
-  Y3B_CHECK_ARG(pool && species && weights && energy && species_count > 0, "null pointer argument");
-  const int threads = 128;
-  const int64_t grid = (atom_count + threads - 1) / threads;
-  ace_eval_kernel<1><<<int(grid), threads, 0, as_stream(stream)>>>(
-      *tables, static_cast<const double2*>(pool), atom_count, nullptr, species, weights, species_count,
-      energy);
-  Y3B_LAUNCH_CHECK();
-  return Y3B_OK;
+  Y3B_CHECK_ARG(A && species && weights && energy && species_count > 0, "null pointer argument");
+  return launch_eval<1>(tables, A, atom_count, nullptr, species, weights, species_count, energy,
+                        as_stream(stream));
 }

@@ -3,24 +3,25 @@
 Turns an :class:`~ye3t_b200.schedules.ACEBundle` into the flat arrays of
 ``y3b_ace_tables`` (include/ye3t_b200.h).
 
-Per-atom block pool (complex entries, atom-fastest on the device):
+Per-CTA shared-memory block entries (complex, 32 atoms per entry):
 
 * A channels: ``(n-1) * (lmax+1)^2 + l^2 + (m + l)`` for ``n = 1..nmax``;
-* then, for every symmetric block kind ``(l, k, Lambda, mu)`` in sorted
-  order and every radial channel ``n``, the ``2 Lambda + 1`` outputs of
+* two slots, each holding, for one radial channel, every symmetric block
+  kind ``(l, k, Lambda, mu)`` (sorted) as the ``2 Lambda + 1`` outputs of
   ``Sym^k(A[n, l]) -> V_Lambda``.
 
-A term of word ``w``, label ``a`` reads block ``b`` at
-``pool[label_bases[word_label_base[w] + a][b] + m_idx]`` with
-``m_idx = m + L_block`` exactly as ``TorchFactorizedCoefficientSchedule``'s
-``block_m_indices`` (``ye3t/core/couplings.py:216-240``).
+Words are scheduled in phases, one per pair of radial channels resident in
+the two slots; a word's symmetric blocks read at most two radial channels.
+A block's magnetic index is ``m + L_block`` exactly as
+``TorchFactorizedCoefficientSchedule``'s ``block_m_indices``
+(``ye3t/core/couplings.py:216-240``).
 """
 
 from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
-from typing import Dict
+from typing import Dict, Optional
 
 import numpy as np
 import torch
@@ -44,20 +45,19 @@ class PackedBundle:
     term_block_count_per_atom: int
     sym_term_count_per_atom: int
     sym_flops_per_atom: float = 0.0
+    item_flops: Optional[float] = None
 
     def tables(self) -> nat.AceTables:
         a = self.arrays
         b = self.bundle
         t = nat.AceTables()
         t.nmax, t.lmax = b.nmax, b.lmax
-        t.pool_size = self.pool_size
-        t.word_count = b.word_count
+        t.smem_entries = self.pool_size
         t.feature_count = self.feature_count
-        t.sym_kind_count = int(a["sym_kind"].shape[0])
-        t.max_blocks = self.max_blocks
-        for name in ("word_pattern", "word_label_base", "word_feature_offset", "pattern_comp_begin",
-                     "pattern_block_count", "comp_term_begin", "comp_label", "term_m", "term_coeff",
-                     "label_bases", "sym_kind", "sym_term_factors", "sym_term_output", "sym_term_coeff"):
+        t.item_count = int(a["items"].shape[0])
+        t.phase_count = int(a["phases"].shape[0])
+        t.sym_output_count = int(a["sym_outputs"].shape[0])
+        for name in ("items", "item_coef", "phases", "sym_outputs", "sym_term_factors", "sym_term_coeff"):
             setattr(t, name, ctypes.c_void_p(a[name].data_ptr()))
         return t
 
@@ -66,17 +66,20 @@ class PackedBundle:
         return (n - 1) * W + l * l + l + m
 
     def flops_per_atom(self) -> Dict[str, float]:
-        """Algorithmic complex-arithmetic counts of the bundle stage per atom (real flops).
+        """FP64 flop counts of the bundle stage per atom.
 
-        A term with B blocks costs one real x complex scaling (2 flops),
-        B - 1 complex multiplies (6 flops each) and one complex add (2 flops);
-        a symmetric-power term of degree k costs k complex multiplies
-        (including the coefficient) plus one complex add.
+        ``items``: what the item walk executes on valid tuples
+        (:func:`item_flops_per_atom`).  ``terms``: the reference's
+        term-by-term product count, sum over terms of (6 B - 2) flops (one
+        real x complex scaling, B - 1 complex multiplies, one complex add).
+        ``sym``: symmetric-block monomials.
         """
         terms = self.term_count_per_atom
         tb = self.term_block_count_per_atom
         sched = 2.0 * terms + 6.0 * (tb - terms) + 2.0 * terms
-        return {"schedule": sched, "sym": float(self.sym_flops_per_atom)}
+        if self.item_flops is None:
+            self.item_flops = item_flops_per_atom(self.arrays["items"].cpu().numpy())
+        return {"items": self.item_flops, "terms": sched, "sym": float(self.sym_flops_per_atom)}
 
 
 def _factors(row):
@@ -92,100 +95,287 @@ def _factors(row):
     return packed
 
 
+# ---------------------------------------------------------------------------
+# Evaluation items for the B-basis kernel.
+#
+# Within a pattern, components whose labels bind identical blocks and that
+# share the same M form a group; the group's coefficients are laid out as a
+# dense table over the magnetic index box of blocks 0..B-2 (the last block's
+# index follows from M: i_last = K - sum_{b < B-1} i_b with
+# K = M + sum_b L_b).  Blocks 0..B-3 are walked by runtime loops, block B-2
+# by a loop unrolled at compile time (its values stay in registers), and the
+# last block is read once per tuple.  A pass covers at most ITEM_MAX_NC
+# components of a group; every word contributes one item per pass.
+# ---------------------------------------------------------------------------
+ITEM_MAX_NC = 2
+ITEM_INTS = 16
+MAX_STATIC_DIM = 13
+
+
+def item_selector(B: int, ds: int, nc: int) -> int:
+    """Kernel dispatch code of an item (mirrors ace.cu)."""
+    return ((B - 1) * 7 + (ds - 1) // 2) * 2 + (nc - 1)
+
+
+def _pattern_groups(p):
+    """[(spec, M, [components])] in first-component order."""
+    order, groups = [], {}
+    for c in range(p.component_count):
+        key = (p.block_specs[int(p.component_label_index[c])], int(p.component_M_R[c]))
+        if key not in groups:
+            groups[key] = []
+            order.append(key)
+        groups[key].append(c)
+    return [(k[0], k[1], groups[k]) for k in order]
+
+
+def _row_width(ds: int, nc: int) -> int:
+    """Doubles per coefficient row (one prefix): nc per j, padded to even."""
+    return 2 * ds if nc == 2 else (ds + 1) & ~1
+
+
+def _group_pass_table(p, rc, spec, M, comps):
+    """Coefficient table of one pass: rows (one per prefix of blocks 0..B-3) of
+    ``_row_width`` doubles holding ``C[prefix, j, c]`` at ``j * nc + c``."""
+    B = len(spec)
+    lam = [s[4] if s[0] == "sym" else s[2] for s in spec]
+    dims = [2 * L + 1 for L in lam]
+    K = M + sum(lam)
+    nc = len(comps)
+    if B == 1:
+        table = np.zeros((1, nc), dtype=np.float64)
+    else:
+        prefix_box = dims[:-2]
+        ds = dims[-2]
+        rows = int(np.prod(prefix_box)) if prefix_box else 1
+        table = np.zeros((rows, _row_width(ds, nc)), dtype=np.float64)
+    for k, c in enumerate(comps):
+        for q in range(int(p.component_offsets[c]), int(p.component_offsets[c + 1])):
+            idx = [int(p.block_m_tuples[q, b]) + lam[b] for b in range(B)]
+            if idx[-1] != K - sum(idx[:-1]):
+                raise ValueError("term violates magnetic conservation")
+            if B == 1:
+                table[0, k] += float(rc[q])
+            else:
+                row = int(np.ravel_multi_index(tuple(idx[:-2]), dims[:-2])) if B > 2 else 0
+                table[row, idx[-2] * nc + k] += float(rc[q])
+    return dims, K, table
+
+
+def _phase_pairs(nmax):
+    """Channel pairs (slot 0, slot 1) visited by the kernel, in order."""
+    if nmax == 1:
+        return [(0, -1)]
+    return [(a, b) for a in range(nmax) for b in range(a + 1, nmax)]
+
+
+def _word_phase(sym_channels, nmax):
+    """Phase pair holding every radial channel that a word's symmetric blocks read."""
+    S = sorted(sym_channels)
+    if nmax == 1:
+        return (0, -1)
+    if len(S) == 2:
+        return (S[0], S[1])
+    if len(S) == 1:
+        a = S[0]
+        return (a, a + 1) if a + 1 < nmax else (a - 1, a)
+    return None
+
+
+def _build_items(bundle, sym_local, sym_out_count, W):
+    """Items grouped by phase, the coefficient array and the phase table.
+
+    Shared-memory entries of a CTA: A channels ``(n-1) W + l^2 + (m + l)``,
+    then two slots of ``sym_out_count`` symmetric outputs, each slot holding
+    every symmetric block of one radial channel (``sym_local`` gives a
+    block's first output inside a slot).
+    """
+    nmax = bundle.nmax
+    coef_chunks, coef_len = [], 0
+    pattern_passes = []
+    for p in bundle.patterns:
+        rc = p.real_coeffs()
+        if rc is None:
+            raise ValueError("fused kernel needs real schedule coefficients")
+        passes = []
+        for spec, M, comps in _pattern_groups(p):
+            for s0 in range(0, len(comps), ITEM_MAX_NC):
+                chunk = comps[s0:s0 + ITEM_MAX_NC]
+                dims, K, table = _group_pass_table(p, rc, spec, M, chunk)
+                if len(dims) > 4:
+                    raise ValueError("fused kernel supports at most 4 blocks per word")
+                if len(dims) >= 2 and dims[-2] > MAX_STATIC_DIM:
+                    raise ValueError("block magnetic dimension above 13 is not supported")
+                passes.append((dims, K, coef_len, chunk, spec))
+                flat = table.reshape(-1)
+                if flat.size % 2:
+                    flat = np.concatenate([flat, [0.0]])
+                coef_chunks.append(flat)
+                coef_len += flat.size
+        pattern_passes.append(passes)
+    pairs = _phase_pairs(nmax)
+    phase_of = {pr: i for i, pr in enumerate(pairs)}
+    phase_items = [[] for _ in pairs]
+    phase_work = [0.0] * len(pairs)
+    free_words = []
+    fo = 0
+    A_entries = nmax * W
+    for w in range(bundle.word_count):
+        pi = int(bundle.word_pattern_index[w])
+        p = bundle.patterns[pi]
+        n_map = {r: int(bundle.word_n_map[w, r]) for r in range(1, bundle.word_n_map.shape[1])
+                 if bundle.word_n_map[w, r] > 0}
+        sym_ch = {n_map[s[1]] - 1 for label in p.block_specs for s in label if s[0] == "sym"}
+        pair = _word_phase(sym_ch, nmax)
+        rows = []
+        work = 0.0
+        for dims, K, coff, chunk, spec in pattern_passes[pi]:
+            B = len(dims)
+            row = [0] * ITEM_INTS
+            ds = dims[-2] if B >= 2 else 1
+            row[0] = item_selector(B, ds, len(chunk))
+            row[1] = dims[0] if B >= 3 else 1
+            row[2] = dims[1] if B >= 4 else 1
+            row[3] = dims[-1]
+            row[4] = K
+            row[5] = coff
+            row[6] = fo + chunk[0]
+            row[7] = fo + chunk[1] if len(chunk) > 1 else -1
+            for b, (kind, n, l, k, Lam, mu) in enumerate(spec):
+                n = n_map[n]
+                if kind == "sym":
+                    row[8 + b] = -1 - (n - 1)  # resolved once the phase is known
+                    row[12 + b] = sym_local[(l, k, Lam, mu)]
+                else:
+                    row[8 + b] = (n - 1) * W + l * l
+            rows.append(row)
+            work += float(np.prod(dims[:-1])) if B > 1 else 1.0
+        fo += p.component_count
+        if pair is None:
+            free_words.append((work, rows))
+        else:
+            phase_items[phase_of[pair]].append(rows)
+            phase_work[phase_of[pair]] += work
+    # words without symmetric blocks balance the phases (largest first)
+    for work, rows in sorted(free_words, key=lambda x: -x[0]):
+        i = int(np.argmin(phase_work))
+        phase_items[i].append(rows)
+        phase_work[i] += work
+    items, phases = [], []
+    for i, (a, b2) in enumerate(pairs):
+        begin = len(items)
+        for rows in phase_items[i]:
+            for row in rows:
+                row = list(row)
+                for blk in range(4):
+                    if row[8 + blk] < 0:
+                        ch = -1 - row[8 + blk]
+                        slot = 0 if ch == a else 1
+                        if (slot == 1 and ch != b2) or (slot == 0 and ch != a):
+                            raise AssertionError("word scheduled in a phase without its channels")
+                        row[8 + blk] = A_entries + slot * sym_out_count + row[12 + blk]
+                    row[12 + blk] = 0
+                items.append(row)
+        phases.append([a, b2, begin, len(items)])
+    coef = np.concatenate(coef_chunks) if coef_chunks else np.zeros(0)
+    return (np.asarray(items, dtype=np.int32).reshape(-1, ITEM_INTS), coef,
+            np.asarray(phases, dtype=np.int32).reshape(-1, 4))
+
+
+def item_flops_per_atom(items: np.ndarray) -> float:
+    """FP64 flops per atom of the item walk (valid tuples only).
+
+    Nested order: per tuple one complex multiply (6 flops) and a real x
+    complex multiply-add per component (4); per runtime prefix row of a 3- or
+    4-block item a complex multiply-add per component (8); per outer index of
+    a 4-block item another (8 per component).
+    """
+    flops = 0.0
+    cache = {}
+    for row in items:
+        key = tuple(int(v) for v in row[:5])
+        if key in cache:
+            flops += cache[key]
+            continue
+        before = flops
+        sel = int(row[0])
+        nc = sel % 2 + 1
+        B = (sel // 2) // 7 + 1
+        ds = 2 * ((sel // 2) % 7) + 1
+        D0, D1, Dl, K = int(row[1]), int(row[2]), int(row[3]), int(row[4])
+        if B == 1:
+            flops += 4.0 * nc
+            cache[key] = flops - before
+            continue
+        prefixes = [(0,)] if B == 2 else ([(i,) for i in range(D0)] if B == 3 else
+                                          [(i, j) for i in range(D0) for j in range(D1)])
+        smin, smax = K - (ds - 1) - (Dl - 1), K
+        outer = set()
+        for pre in prefixes:
+            S = sum(pre) if B > 2 else 0
+            if B > 2 and not smin <= S <= smax:
+                continue
+            valid = sum(1 for j in range(ds) if 0 <= K - S - j < Dl)
+            flops += valid * (6.0 + 4.0 * nc) + (8.0 * nc if B > 2 else 0.0)
+            if B == 4:
+                outer.add(pre[0])
+        flops += 8.0 * nc * len(outer)
+        cache[key] = flops - before
+    return flops
+
+
 def pack_bundle(bundle: ACEBundle, device) -> PackedBundle:
     device = torch.device(device)
     nmax, lmax = bundle.nmax, bundle.lmax
     W = (lmax + 1) ** 2
-    # symmetric pool layout
+    # symmetric outputs of one radial channel (one shared-memory slot)
     sym_keys = sorted(bundle.sym_tables)
-    sym_off = {}
-    off = nmax * W
-    sym_kind_rows, s_fac, s_out, s_co = [], [], [], []
+    sym_local, sym_out_rows, s_fac, s_co = {}, [], [], []
     sym_flops = 0.0
     for key in sym_keys:
         t = bundle.sym_tables[key]
         l, k, Lam, mu = key
-        sym_off[key] = off
+        sym_local[key] = len(sym_out_rows)
         vals = np.asarray(t.monomial_value)
         if np.iscomplexobj(vals) and vals.size and np.max(np.abs(vals.imag)) > 1e-12:
             raise ValueError(f"symmetric table {key} has complex coefficients; not supported by the fused kernel")
-        tb = len(s_fac)
         offsets = np.asarray(t.output_offsets, dtype=np.int64)
         for o in range(2 * Lam + 1):
+            tb = len(s_fac)
             for q in range(int(offsets[o]), int(offsets[o + 1])):
                 s_fac.append(_factors(t.monomial_counts[q]))
-                s_out.append(o)
                 s_co.append(float(np.real(vals[q])))
                 sym_flops += 6.0 * int(np.sum(t.monomial_counts[q])) + 2.0
-        sym_kind_rows.append([l, k, Lam, off, tb, len(s_fac)])
-        off += nmax * (2 * Lam + 1)
-    sym_flops *= nmax
-    pool_size = off
-    # pattern tables
-    pcb, pbc, ctb, clab, tm, tco = [0], [], [0], [], [], []
-    max_blocks = 1
-    for p in bundle.patterns:
-        if p.block_count > 4:
-            raise ValueError("fused kernel supports at most 4 blocks per word")
-        max_blocks = max(max_blocks, p.block_count)
-        rc = p.real_coeffs()
-        if rc is None:
-            raise ValueError("fused kernel needs real schedule coefficients")
-        bmi = p.block_m_indices()
-        for c in range(p.component_count):
-            t0, t1 = int(p.component_offsets[c]), int(p.component_offsets[c + 1])
-            for q in range(t0, t1):
-                packed = 0
-                for b in range(p.block_count):
-                    v = int(bmi[q, b])
-                    if not 0 <= v < 255:
-                        raise ValueError("magnetic index out of packable range")
-                    packed |= v << (8 * b)
-                tm.append(packed)
-                tco.append(float(rc[q]))
-            ctb.append(len(tm))
-            clab.append(int(p.component_label_index[c]))
-        pcb.append(len(clab))
-        pbc.append(p.block_count)
-    # per-word bindings
-    wlb, lbases, wfo = [], [], []
+            sym_out_rows.append([l * l, tb, len(s_fac), 0])
+    sym_out_count = len(sym_out_rows)
+    items, item_coef, phases = _build_items(bundle, sym_local, sym_out_count, W)
+    max_blocks = max([p.block_count for p in bundle.patterns] + [1])
     fo = 0
     terms_per_atom = 0
     term_blocks_per_atom = 0
     for w in range(bundle.word_count):
-        rec = bundle.word_schedule(w)
-        wlb.append(len(lbases))
-        for label in rec.block_specs:
-            row = [0, 0, 0, 0]
-            for b, (kind, n, l, k, Lam, mu) in enumerate(label):
-                if kind == "sym":
-                    row[b] = sym_off[(l, k, Lam, mu)] + (n - 1) * (2 * Lam + 1)
-                else:
-                    row[b] = (n - 1) * W + l * l
-            lbases.append(row)
-        wfo.append(fo)
-        fo += rec.component_count
-        terms_per_atom += rec.term_count
-        term_blocks_per_atom += rec.term_count * rec.block_count
+        p = bundle.patterns[int(bundle.word_pattern_index[w])]
+        fo += p.component_count
+        terms_per_atom += p.term_count
+        term_blocks_per_atom += p.term_count * p.block_count
     arrays_np = {
-        "word_pattern": np.asarray(bundle.word_pattern_index, dtype=np.int32),
-        "word_label_base": np.asarray(wlb, dtype=np.int32),
-        "word_feature_offset": np.asarray(wfo, dtype=np.int64),
-        "pattern_comp_begin": np.asarray(pcb, dtype=np.int32),
-        "pattern_block_count": np.asarray(pbc, dtype=np.int32),
-        "comp_term_begin": np.asarray(ctb, dtype=np.int32),
-        "comp_label": np.asarray(clab, dtype=np.int32),
-        "term_m": np.asarray(tm, dtype=np.uint32).view(np.int32),
-        "term_coeff": np.asarray(tco, dtype=np.float64),
-        "label_bases": np.asarray(lbases, dtype=np.int32).reshape(-1, 4),
-        "sym_kind": np.asarray(sym_kind_rows, dtype=np.int32).reshape(-1, 6),
+        "items": items,
+        "item_coef": item_coef,
+        "phases": phases,
+        "sym_outputs": np.asarray(sym_out_rows, dtype=np.int32).reshape(-1, 4),
         "sym_term_factors": np.asarray(s_fac, dtype=np.uint32).view(np.int32),
-        "sym_term_output": np.asarray(s_out, dtype=np.int32),
         "sym_term_coeff": np.asarray(s_co, dtype=np.float64),
     }
     arrays = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device) for k, v in arrays_np.items()}
-    pb = PackedBundle(bundle=bundle, device=device, arrays=arrays, pool_size=pool_size, feature_count=fo,
-                      max_blocks=max_blocks, sym_offsets=sym_off, term_count_per_atom=terms_per_atom,
-                      term_block_count_per_atom=term_blocks_per_atom,
-                      sym_term_count_per_atom=len(s_fac) * nmax, sym_flops_per_atom=sym_flops)
+    # symmetric blocks of each visited slot channel are recomputed per phase change
+    loads = 0
+    prev = (None, None)
+    for a, b2, _, _ in phases.tolist():
+        loads += int(a != prev[0]) + int(b2 >= 0 and b2 != prev[1])
+        prev = (a, b2)
+    pb = PackedBundle(bundle=bundle, device=device, arrays=arrays, pool_size=nmax * W + 2 * sym_out_count,
+                      feature_count=fo, max_blocks=max_blocks, sym_offsets=sym_local,
+                      term_count_per_atom=terms_per_atom, term_block_count_per_atom=term_blocks_per_atom,
+                      sym_term_count_per_atom=len(s_fac) * loads,
+                      sym_flops_per_atom=sym_flops * loads)
     return pb
