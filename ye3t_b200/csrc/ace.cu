@@ -126,12 +126,15 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX>::value) ace_density_ke
 // 0..B-2; the last block's index follows from M conservation,
 //   i_last = K - sum_{b < B-1} i_b,  K = M + sum_b L_b,
 // and the sum is evaluated in nested order
-//   B_c = sum_{i0} v0 ( sum_{i1} v1 ( sum_j C[i0, i1, j, c] vs[j] v_last ) )
+//   B_c = sum_{i0} v0 ( sum_j C[i0, j, c] vs[j] v_last )                (B = 3)
+//   B_c = sum_S sum_{i0 + i1 = S} v0 v1 ( sum_j C[i0, i1, j, c] q_j ),
+//         q_j = vs[j] v_last[K - S - j]                                 (B = 4)
 // with block B-2 (vs) unrolled at compile time and held in registers.
 // MODE 0 writes features [N, F]; MODE 1 reduces to per-atom energy.
 // ---------------------------------------------------------------------------
 constexpr int kLanes = 32;
 constexpr int kEvalWarps = 16;
+constexpr int kPadEntries = 16;  // zero entries before and after the block entries
 
 struct Item {
   int sel, d0, d1, dl, K, coef, f0, f1;
@@ -174,36 +177,36 @@ struct RowWidth {
   static constexpr int value = NC == 2 ? 2 * DS : ((DS + 1) & ~1);
 };
 
-// T_c += C[j, c] * (vs[j] * v_last[kS - j]) for j in [jlo, jhi], the j whose
-// last index lies in the block.  Pk points at v_last[kS], so every j reads
-// at a compile-time offset from it.  Odd and even j accumulate separately
-// (two independent FMA chains).
+// T_c += C[j, c] * (vs[j] * v_last[kS - j]) for every j < DS.  Pk points at
+// v_last[kS], so each j reads at a compile-time offset from it.  Slots whose
+// last index falls outside the block have an exact-zero coefficient in the
+// dense row and read a finite neighbouring entry (or the zero padding around
+// the shared-memory array), so they add exactly zero and need no branch.
+// Odd and even j accumulate separately (two independent FMA chains).
 template <int DS, int NC>
-__device__ __forceinline__ void row_sum(const double2* __restrict__ Pk, int jlo, int jhi,
-                                        const double2 (&vs)[DS], const double* __restrict__ crow,
-                                        double2& t0, double2& t1) {
+__device__ __forceinline__ void row_sum(const double2* __restrict__ Pk, const double2 (&vs)[DS],
+                                        const double* __restrict__ crow, double2& t0, double2& t1) {
   const double2* cr2 = reinterpret_cast<const double2*>(crow);
   double2 o0 = make_double2(0.0, 0.0), o1 = o0;
+  double2 cc = make_double2(0.0, 0.0);
 #pragma unroll
   for (int j = 0; j < DS; ++j) {
-    if (j >= jlo && j <= jhi) {
-      double c0, c1 = 0.0;
-      if (NC == 2) {
-        const double2 cc = __ldg(cr2 + j);
-        c0 = cc.x;
-        c1 = cc.y;
-      } else {
-        const double2 cc = __ldg(cr2 + (j >> 1));
-        c0 = (j & 1) ? cc.y : cc.x;
-      }
-      const double2 q = mul(vs[j], Pk[-j * kLanes]);
-      if (j & 1) {
-        cmac(o0, c0, q);
-        if (NC == 2) cmac(o1, c1, q);
-      } else {
-        cmac(t0, c0, q);
-        if (NC == 2) cmac(t1, c1, q);
-      }
+    double c0, c1 = 0.0;
+    if (NC == 2) {
+      cc = __ldg(cr2 + j);
+      c0 = cc.x;
+      c1 = cc.y;
+    } else {
+      if ((j & 1) == 0) cc = __ldg(cr2 + (j >> 1));
+      c0 = (j & 1) ? cc.y : cc.x;
+    }
+    const double2 q = mul(vs[j], Pk[-j * kLanes]);
+    if (j & 1) {
+      cmac(o0, c0, q);
+      if (NC == 2) cmac(o1, c1, q);
+    } else {
+      cmac(t0, c0, q);
+      if (NC == 2) cmac(t1, c1, q);
     }
   }
   t0 = add(t0, o0);
@@ -225,26 +228,25 @@ __device__ __forceinline__ void eval_item(const double2* __restrict__ P, const I
   // a prefix with index sum S has tuples only for S in [smin, smax]
   const int smin = it.K - (DS - 1) - (dl - 1), smax = it.K;
   if (B == 2) {
-    const int kS = it.K;
-    row_sum<DS, NC>(Pl + kS * kLanes, max(0, kS - dl + 1), min(DS - 1, kS), vs, c, a0, a1);
+    row_sum<DS, NC>(Pl + it.K * kLanes, vs, c, a0, a1);
   } else if (B == 3) {
     for (int i0 = max(0, smin); i0 < it.d0 && i0 <= smax; ++i0) {
       const int kS = it.K - i0;
       double2 t0 = make_double2(0.0, 0.0), t1 = t0;
-      row_sum<DS, NC>(Pl + kS * kLanes, max(0, kS - dl + 1), min(DS - 1, kS), vs, c + i0 * RW, t0, t1);
+      row_sum<DS, NC>(Pl + kS * kLanes, vs, c + i0 * RW, t0, t1);
       const double2 x0 = P[(it.b0 + i0) * kLanes];
       cfma(a0, x0, t0);
       if (NC == 2) cfma(a1, x0, t1);
     }
-  } else {
+  } else if (DS > 7) {
+    // B = 4 with a wide register block: row by row (keeps register use low)
     for (int i0 = 0; i0 < it.d0 && i0 <= smax; ++i0) {
       double2 u0 = make_double2(0.0, 0.0), u1 = u0;
       const int i1lo = max(0, smin - i0), i1hi = min(it.d1 - 1, smax - i0);
       for (int i1 = i1lo; i1 <= i1hi; ++i1) {
         const int kS = it.K - i0 - i1;
         double2 t0 = make_double2(0.0, 0.0), t1 = t0;
-        row_sum<DS, NC>(Pl + kS * kLanes, max(0, kS - dl + 1), min(DS - 1, kS), vs,
-                        c + (i0 * it.d1 + i1) * RW, t0, t1);
+        row_sum<DS, NC>(Pl + kS * kLanes, vs, c + (i0 * it.d1 + i1) * RW, t0, t1);
         const double2 x1 = P[(it.b1 + i1) * kLanes];
         cfma(u0, x1, t0);
         if (NC == 2) cfma(u1, x1, t1);
@@ -252,6 +254,48 @@ __device__ __forceinline__ void eval_item(const double2* __restrict__ P, const I
       const double2 x0 = P[(it.b0 + i0) * kLanes];
       cfma(a0, x0, u0);
       if (NC == 2) cfma(a1, x0, u1);
+    }
+  } else {
+    // B = 4: prefixes (i0, i1) with the same index sum S read the same last-
+    // block window, so loop over S: form q_j = vs[j] v_last[K - S - j] once,
+    // then every prefix on the anti-diagonal only contracts its coefficient
+    // row with q:  B_c += v0[i0] v1[i1] sum_j C[i0, i1, j, c] q_j.
+    constexpr int DQ = DS <= 7 ? DS : 1;  // (this branch only runs for DS <= 7)
+    const int s_lo = max(0, smin), s_hi = min(it.d0 - 1 + it.d1 - 1, smax);
+    for (int S = s_lo; S <= s_hi; ++S) {
+      const double2* Pk = Pl + (it.K - S) * kLanes;
+      double2 q[DQ];
+#pragma unroll
+      for (int j = 0; j < DQ; ++j) q[j] = mul(vs[j], Pk[-j * kLanes]);
+      const int i0lo = max(0, S - (it.d1 - 1)), i0hi = min(it.d0 - 1, S);
+      for (int i0 = i0lo; i0 <= i0hi; ++i0) {
+        const int i1 = S - i0;
+        const double2* cr2 = reinterpret_cast<const double2*>(c + (i0 * it.d1 + i1) * RW);
+        double2 t0 = make_double2(0.0, 0.0), t1 = t0, o0 = t0, o1 = t0;
+        double2 cc = t0;
+#pragma unroll
+        for (int j = 0; j < DQ; ++j) {
+          double c0, c1 = 0.0;
+          if (NC == 2) {
+            cc = __ldg(cr2 + j);
+            c0 = cc.x;
+            c1 = cc.y;
+          } else {
+            if ((j & 1) == 0) cc = __ldg(cr2 + (j >> 1));
+            c0 = (j & 1) ? cc.y : cc.x;
+          }
+          if (j & 1) {
+            cmac(o0, c0, q[j]);
+            if (NC == 2) cmac(o1, c1, q[j]);
+          } else {
+            cmac(t0, c0, q[j]);
+            if (NC == 2) cmac(t1, c1, q[j]);
+          }
+        }
+        const double2 x01 = mul(P[(it.b0 + i0) * kLanes], P[(it.b1 + i1) * kLanes]);
+        cfma(a0, x01, add(t0, o0));
+        if (NC == 2) cfma(a1, x01, add(t1, o1));
+      }
     }
   }
 }
@@ -319,13 +363,18 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
     y3b_ace_tables t, const double2* __restrict__ A, int64_t N, double2* __restrict__ feats,
     const int32_t* __restrict__ species, const double* __restrict__ weights, int64_t S,
     double* __restrict__ energy) {
-  extern __shared__ double2 sm[];
+  extern __shared__ double2 smem_all[];
   __shared__ double red[kEvalWarps][kLanes];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int W = int((t.lmax + 1) * (t.lmax + 1));
   const int na = int(t.nmax) * W;
   const int64_t a = blockIdx.x * int64_t(kLanes) + lane;
   const bool live = a < N;
+  // zero everything (padding and slots), then the A channels
+  const int total = (int(t.smem_entries) + 2 * kPadEntries) * kLanes;
+  for (int e = threadIdx.x; e < total; e += blockDim.x) smem_all[e] = make_double2(0.0, 0.0);
+  __syncthreads();
+  double2* sm = smem_all + kPadEntries * kLanes;
   for (int e = warp; e < na; e += kEvalWarps)
     sm[e * kLanes + lane] = live ? A[a * na + e] : make_double2(0.0, 0.0);
   const double* wz = weights;
@@ -376,7 +425,7 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
 }
 
 inline size_t eval_smem_bytes(const y3b_ace_tables& t) {
-  return size_t(t.smem_entries) * kLanes * sizeof(double2);
+  return size_t(t.smem_entries + 2 * kPadEntries) * kLanes * sizeof(double2);
 }
 
 int check_tables(const y3b_ace_tables* t) {
