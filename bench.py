@@ -200,21 +200,20 @@ def run_b200(args):
     from ye3t_b200.ace import ACEConfig, ACEEvaluator
     from ye3t_b200.schedules import ACEBundle
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
+    from ye3t_b200.distributed import atom_block, init_from_env, max_over_ranks as _max_over_ranks
+    from ye3t_b200.distributed import sum_over_ranks
+
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    rank, world = init_from_env("nccl", 300.0, device)
     N = int(args.atoms)
     pos, species, box = make_system(N)
     bundle = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", args.bundle + ".npz"))
     weights = make_weights(bundle.feature_count)
     ev = ACEEvaluator(bundle, device, config=ACEConfig(CUTOFF, LAMBDA), species_prefactor=PREFACTOR,
                       weights=weights)
-    begin, end = (N * rank) // world, (N * (rank + 1)) // world
+    begin, end = atom_block(rank, world, N)
     n_local = end - begin
     pos_h = pos.pin_memory()
     sp_h = species.pin_memory()
@@ -237,9 +236,7 @@ def run_b200(args):
         e_at = ev.energy_from_density(A, sp_d[begin:end], out=e_buf)
         if record:
             ev_marks[3].record()
-        total = e_at.sum()
-        if world > 1:
-            dist.all_reduce(total)
+        total = sum_over_ranks(e_at.sum())
         return total, ev_marks
 
     def barrier():
@@ -248,10 +245,7 @@ def run_b200(args):
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max_over_ranks(x, device)
 
     for _ in range(args.warmup):
         step(False)
@@ -336,9 +330,9 @@ def run_b200(args):
         "roofline": {"bound": "fp64", "kernel": "ace_eval_kernel<1> (B-basis energy, symmetric blocks on chip)", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "flops_per_launch": sched_flops_launch,
-                     "flops_note": "FP64 flops the item walk executes on valid tuples (2 complex multiplies "
-                                   "per tuple + 4 per component) plus the readout; the reference's "
-                                   "term-by-term count for the same features is "
+                     "flops_note": "FP64 flops the nested item walk needs on valid tuples "
+                                   "(ye3t_b200.packing.item_flops_per_atom) plus the readout; the "
+                                   "reference's term-by-term count for the same features is "
                                    f"{term_flops_launch:.4g} per launch",
                      "peak_source": "FP64 FMA microbenchmark (y3b_fma_peak_launch) measured in this run; "
                                     "MEASURED_PEAKS.json has no FP64 figure"},

@@ -1,0 +1,67 @@
+"""Atom-block partition and the energy reduction, as 2 gloo ranks on CPU.
+
+Each rank evaluates its centre block with the CPU oracle (the GPU kernels are
+covered by the gpu tests); the summed energy must equal the single-process
+energy, and the blocks must tile the system."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from ye3t_b200.distributed import atom_block
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_atom_blocks_tile_the_system():
+    for N in (0, 1, 7, 96, 1 << 20):
+        for P in (1, 2, 3, 4, 8):
+            spans = [atom_block(r, P, N) for r in range(P)]
+            assert spans[0][0] == 0 and spans[-1][1] == N
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert max(e - b for b, e in spans) - min(e - b for b, e in spans) <= 1
+    with pytest.raises(ValueError):
+        atom_block(2, 2, 10)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, out_path):
+    import sys
+    sys.path.insert(0, REPO)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    from oracle import oracle
+    from ye3t_b200.distributed import atom_block, init_from_env, sum_over_ranks
+    from ye3t_b200.schedules import ACEBundle
+    import torch.distributed as dist
+    r, w = init_from_env("gloo", 60.0)
+    g = dict(np.load(os.path.join(REPO, "tests", "golden", "ace_small.npz")))
+    b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu3_L0.npz"))
+    N = g["pos"].shape[0]
+    lo, hi = atom_block(r, w, N)
+    A = oracle.ace_density(g["disp"], g["row_off"], g["nbr"], g["species"], g["prefactor"], 8, 3,
+                           float(g["rc"]), float(g["lam"]))
+    e = oracle.bundle_energy(b, A[lo:hi], g["species"][lo:hi], g["w3"], threads=2).sum()
+    total = sum_over_ranks(torch.tensor([e], dtype=torch.float64))
+    if r == 0:
+        np.save(out_path, total.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_energy_equals_single_process(tmp_path, golden):
+    out = str(tmp_path / "total.npy")
+    mp.start_processes(_rank_main, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
+    total = float(np.load(out)[0])
+    ref = float(golden("ace_small")["energy3"])
+    assert abs(total - ref) <= 1e-12 * abs(ref)

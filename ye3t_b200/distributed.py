@@ -1,0 +1,51 @@
+"""Atom-block partition across ranks (one process per GPU).
+
+Each atom's A- and B-basis depend only on its own neighbour row, so rank r of
+P evaluates the centres ``[r N / P, (r + 1) N / P)`` from the replicated
+positions and the only collective is a sum of the per-rank energies.  The
+reference has no distributed code; this is new.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+from typing import Tuple
+
+import torch
+import torch.distributed as dist
+
+__all__ = ["atom_block", "init_from_env", "sum_over_ranks", "max_over_ranks"]
+
+
+def atom_block(rank: int, world: int, atom_count: int) -> Tuple[int, int]:
+    """Contiguous centre range of ``rank``; blocks differ in size by at most one."""
+    if not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    return (atom_count * rank) // world, (atom_count * (rank + 1)) // world
+
+
+def init_from_env(backend: str = "nccl", timeout_s: float = 300.0, device=None):
+    """Initialise the default group from torchrun's environment; returns (rank, world)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
+        if backend == "nccl" and device is not None:
+            kwargs["device_id"] = device
+        dist.init_process_group(backend, **kwargs)
+    return rank, world
+
+
+def sum_over_ranks(value: torch.Tensor) -> torch.Tensor:
+    """In-place sum across ranks (no-op on one rank)."""
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(value, op=dist.ReduceOp.SUM)
+    return value
+
+
+def max_over_ranks(x: float, device) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
