@@ -277,7 +277,10 @@ def _build_items(bundle, sym_local, sym_out_count, W):
     items, phases = [], []
     for i, (a, b2) in enumerate(pairs):
         begin = len(items)
-        for rows in phase_items[i]:
+        # items sharing a coefficient table run next to each other, so the
+        # CTA's warps (which take items round robin) read it from L1 together
+        flat = sorted((row for rows in phase_items[i] for row in rows), key=lambda r: (r[5], r[6]))
+        for rows in [flat]:
             for row in rows:
                 row = list(row)
                 for blk in range(4):
@@ -544,7 +547,10 @@ def _build_items(bundle, sym_local, sym_out_count, W):
     items, phases = [], []
     for i, (a, b2) in enumerate(pairs):
         begin = len(items)
-        for rows in phase_items[i]:
+        # items sharing a coefficient table run next to each other, so the
+        # CTA's warps (which take items round robin) read it from L1 together
+        flat = sorted((row for rows in phase_items[i] for row in rows), key=lambda r: (r[5], r[6]))
+        for rows in [flat]:
             for row in rows:
                 row = list(row)
                 for blk in range(4):
