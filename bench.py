@@ -6,7 +6,9 @@ cubic box at 0.05 atoms/A^3, 3 species, n_max 8, l_max 3, cutoff 5 A):
 cell-list CSR neighbour list -> A-basis density (kernel 1) -> symmetric blocks
 and all 25,328 nu <= 4 words / 41,168 L = 0 features per atom evaluated from
 their compiled schedules on chip and contracted with a per-species linear
-readout (kernel 2) -> total energy (NCCL all-reduce when N > 1).
+readout, together with dE/dA (kernel 2 and its adjoint) -> per-edge
+gradients -> forces on every atom; total energy and forces are summed over
+ranks with NCCL when N > 1.  --energy-only times the energy alone.
 Atoms are block-partitioned across ranks (strong scaling of the fixed system).
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU
@@ -46,6 +48,8 @@ def parse():
     ap.add_argument("--bundle", default=BUNDLE)
     ap.add_argument("--cpu-sample", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--energy-only", action="store_true",
+                    help="time the energy step alone (no adjoint, no forces)")
     return ap.parse_args()
 
 
@@ -184,9 +188,10 @@ def run_reference(args):
 
 
 def _config(args):
-    return {"workload": "C5 scalar ACE energy: 2^20 atoms (periodic cubic box, 0.05/A^3, 3 species), "
+    what = "energy" if getattr(args, "energy_only", False) else "energy + forces"
+    return {"workload": f"C5 scalar ACE {what}: 2^20 atoms (periodic cubic box, 0.05/A^3, 3 species), "
                         "n_max 8, l_max 3, nu<=4 (25,328 words / 41,168 L=0 features), fp64, per-species "
-                        "linear readout; forces not included",
+                        "linear readout",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
             "parallelism": f"atom-block x{args.gpus}",
             "l2": "inputs larger than L2 (A-basis 2 GB, neighbour list 110 MB at 2^20 atoms)"}
@@ -220,24 +225,41 @@ def run_b200(args):
     pos_d = pos.to(device)
     sp_d = species.to(device)
     e_buf = torch.empty(n_local, dtype=torch.float64, device=device)
-    timers = {k: [] for k in ("neighbors", "density", "energy")}
-    launches_per_step = 9  # our kernels: 6 neighbour-count, 1 fill, density, B-basis energy
+    F_buf = torch.empty((N, 3), dtype=torch.float64, device=device)
+    forces = not args.energy_only
+    stages = ("neighbors", "density", "energy_grad", "edge_grad", "forces") if forces else \
+        ("neighbors", "density", "energy")
+    timers = {k: [] for k in stages}
+    # our kernels per step: 6 neighbour-count, 1 fill, density, then the
+    # B-basis energy, or the B-basis adjoint + edge gradients + force gather/scatter
+    launches_per_step = 8 + (3 if forces else 1)
 
     def step(record):
-        ev_marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
-        if record:
-            ev_marks[0].record()
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] if record else None
+
+        def mark(i):
+            if record:
+                marks[i].record()
+        mark(0)
         row, nbr = ev.neighbor_list(pos_d, box, begin, end)
-        if record:
-            ev_marks[1].record()
+        mark(1)
         A = ev.density(pos_d, sp_d, box, row, nbr, begin)
-        if record:
-            ev_marks[2].record()
-        e_at = ev.energy_from_density(A, sp_d[begin:end], out=e_buf)
-        if record:
-            ev_marks[3].record()
-        total = sum_over_ranks(e_at.sum())
-        return total, ev_marks
+        mark(2)
+        if not forces:
+            e_at = ev.energy_from_density(A, sp_d[begin:end], out=e_buf)
+            mark(3)
+            return sum_over_ranks(e_at.sum()), None, marks
+        e_at, G = ev.energy_grad(A, sp_d[begin:end])
+        mark(3)
+        g = ev.edge_grad(pos_d, sp_d, box, row, nbr, G, begin=begin)
+        mark(4)
+        if world == 1:
+            F = ev.forces_from_edges(row, nbr, g)
+        else:
+            F_buf.zero_()
+            F = sum_over_ranks(ev.partial_forces_from_edges(row, nbr, g, begin, N, out=F_buf))
+        mark(5)
+        return sum_over_ranks(e_at.sum()), F, marks
 
     def barrier():
         if world > 1:
@@ -256,42 +278,46 @@ def run_b200(args):
     marks = []
     t0.record()
     for _ in range(args.steps):
-        total, m = step(True)
+        total, F_last, m = step(True)
         marks.append(m)
     t1.record()
     barrier()
     clock_info = clocks.stop()
     dev_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
     for m in marks:
-        for k, (a, b) in zip(timers, zip(m[:-1], m[1:])):
+        for k, a, b in zip(stages, m[:-1], m[1:]):
             timers[k].append(a.elapsed_time(b))
     energy = float(total.item())
 
     # end to end through the public API with host buffers: H2D of positions
-    # and species every step, D2H of the total energy
+    # and species every step, D2H of the total energy (and the forces)
     for _ in range(max(1, args.warmup // 2)):
         pos_d.copy_(pos_h, non_blocking=True)
         sp_d.copy_(sp_h, non_blocking=True)
         step(False)[0].to("cpu", non_blocking=False)
     host_total = torch.empty(1, dtype=torch.float64).pin_memory()
+    host_forces = torch.empty((N, 3), dtype=torch.float64).pin_memory() if forces else None
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         pos_d.copy_(pos_h, non_blocking=True)
         sp_d.copy_(sp_h, non_blocking=True)
-        tot, _ = step(False)
+        tot, Fd, _ = step(False)
         host_total.copy_(tot.reshape(1), non_blocking=True)
+        if forces:
+            host_forces.copy_(Fd, non_blocking=True)
     e1.record()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
     peak = measure_fp64_peak(torch, nat, device)
     flops = ev.packed.flops_per_atom()
-    energy_ms = statistics.mean(timers["energy"])
-    sched_flops_launch = (flops["items"] + 2.0 * ev.feature_count) * n_local
+    kern_ms = statistics.mean(timers["energy_grad" if forces else "energy"])
+    kern_flops = (flops["items_grad"] if forces else flops["items"]) + 2.0 * ev.feature_count
+    sched_flops_launch = kern_flops * n_local
     term_flops_launch = (flops["terms"] + 2.0 * ev.feature_count) * n_local
-    achieved = sched_flops_launch / (energy_ms * 1e-3) / 1e12
+    achieved = sched_flops_launch / (kern_ms * 1e-3) / 1e12
     W = (bundle.lmax + 1) ** 2
     dens_ms = statistics.mean(timers["density"])
     avg_deg = float(0.05 * 4.0 / 3.0 * 3.141592653589793 * CUTOFF ** 3)
@@ -304,7 +330,7 @@ def run_b200(args):
     except (OSError, KeyError, ValueError):
         hbm_peak, hbm_src = 6650.0, "fallback 6.65 TB/s"
     traffic = None
-    tpath = os.path.join(REPO, "profiles", "ace_energy_traffic.json")
+    tpath = os.path.join(REPO, "profiles", "ace_grad_traffic.json" if forces else "ace_energy_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as fh:
             t = json.load(fh)
@@ -325,14 +351,18 @@ def run_b200(args):
         "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded uniform positions, random readout)",
         "config": _config(args),
         "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
-                "d2h_bytes_per_step": 8},
+                "d2h_bytes_per_step": 8 + (N * 24 if forces else 0)},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": {"bound": "fp64", "kernel": "ace_eval_kernel<1> (B-basis energy, symmetric blocks on chip)", "achieved": achieved,
+        "roofline": {"bound": "fp64",
+                     "kernel": ("ace_grad_kernel (B-basis energy + dE/dA)" if forces
+                                else "ace_eval_kernel<1> (B-basis energy, symmetric blocks on chip)"),
+                     "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "flops_per_launch": sched_flops_launch,
-                     "flops_note": "FP64 flops the nested item walk needs on valid tuples "
-                                   "(ye3t_b200.packing.item_flops_per_atom) plus the readout; the "
-                                   "reference's term-by-term count for the same features is "
+                     "flops_note": "FP64 flops the item walk needs on valid tuples "
+                                   "(ye3t_b200.packing.item_grad_flops_per_atom with forces, "
+                                   "item_flops_per_atom without) plus the readout; the reference's "
+                                   "forward term-by-term count for the same features is "
                                    f"{term_flops_launch:.4g} per launch",
                      "peak_source": "FP64 FMA microbenchmark (y3b_fma_peak_launch) measured in this run; "
                                     "MEASURED_PEAKS.json has no FP64 figure"},
@@ -341,6 +371,7 @@ def run_b200(args):
                              "bytes_per_atom": dens_bytes_atom, "peak_source": hbm_src},
         "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
         "energy_total": energy,
+        "forces_abs_sum": float(F_last.abs().sum().item()) if forces else None,
         "clocks": clock_info,
         "cpu_baseline": cpu,
     }

@@ -217,6 +217,44 @@ int y3b_ace_energy(const y3b_ace_tables* tables, const void* A, int64_t atom_cou
                    double* energy, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Force path (the reverse of the two kernels above).  E = sum_i sum_f
+ * w[z_i, f] Re(B_if); the reference obtains its gradient by torch autograd
+ * through evaluate_factorized_schedule_torch (ye3t/core/couplings.py:552-567),
+ * the symmetric-power adjoint (execution_plan_cuda.cu:5272) and
+ * density_accumulate_adjoint (ye3t/runtime/execution_plan.py:7987).
+ * ---------------------------------------------------------------------- */
+
+/* Per-atom energies and G = dE/dA (complex128, A's layout; B is holomorphic
+ * in A so dE = Re(sum G dA)). */
+int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
+                        const int32_t* species, const double* weights, int64_t species_count,
+                        double* energy, void* dEdA, void* stream);
+
+/* Per-edge g_e = dE_i/dd_e (f64 [E, 3], d_e = r_j - r_i minimum image) for the
+ * rows of centres [center_begin, center_begin + center_count), from dEdA of
+ * those centres (plain_site_basis_product_adjoint,
+ * ye3t/runtime/execution_plan.py:7790, fused with the radial/harmonic
+ * derivatives). */
+int y3b_ace_edge_grad(const double* positions, const int32_t* species, int64_t atom_count,
+                      int64_t center_begin, int64_t center_count, double box,
+                      const int64_t* row_offsets, const int32_t* neighbors,
+                      const double* species_prefactor, int64_t species_count, int64_t nmax,
+                      int64_t lmax, double cutoff, double lambda, const void* dEdA,
+                      double* edge_grad, int32_t* status, void* stream);
+
+/* Forces F_k = -dE/dr_k = sum_{e in row k} (g_e - g_rev(e)) from the rows of
+ * all atoms (deterministic gather; rev(e) is the reverse edge). */
+int y3b_forces_gather(const int64_t* row_offsets, const int32_t* neighbors, int64_t atom_count,
+                      const double* edge_grad, double* forces, int32_t* status, void* stream);
+
+/* Partial forces of local rows added into forces [atom_count, 3] (caller
+ * zeroes it): F[k] += g_e, F[nbr] -= g_e (atomics).  Summing the partial
+ * arrays of all atom blocks gives the forces. */
+int y3b_forces_scatter(const int64_t* row_offsets, const int32_t* neighbors, int64_t center_begin,
+                       int64_t center_count, int64_t atom_count, const double* edge_grad,
+                       double* forces, void* stream);
+
+/* ------------------------------------------------------------------------
  * Measurement support: an FP64 / FP32 FMA throughput kernel used to measure
  * the CUDA-core roofline.  Returns the flop count of one launch in *flops. */
 int y3b_fma_peak_launch(int dtype, int32_t blocks, int32_t threads, int32_t iterations,

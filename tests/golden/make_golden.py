@@ -333,8 +333,75 @@ def ace_fixture():
     print("ace_small.npz N", N, "E", E, "B3", B3.shape, "B4", B4.shape, "energy3", energy3)
 
 
+def forces_fixture():
+    """Energy and forces of the 96-atom system through the reference's torch ops with autograd.
+
+    Displacements are the minimum image of the CSR pairs with the image shift
+    held fixed; the radial table (``execution_plan.py:6862`` reference
+    formula), complex harmonics (``:6919``), ``density_accumulate`` and, per
+    word, the symmetric-power contraction and ``evaluate(backend="torch")``
+    are all differentiable torch code in the reference.  F = -dE/dr.
+    """
+    g = dict(np.load(os.path.join(HERE, "ace_small.npz")))
+    N = g["pos"].shape[0]
+    box = float(g["box"])
+    rc, lam, nmax, lmax = float(g["rc"]), float(g["lam"]), int(g["nmax"]), int(g["lmax"])
+    off, nbr = g["row_off"], g["nbr"]
+    E = nbr.shape[0]
+    centers = torch.tensor(np.repeat(np.arange(N), np.diff(off)))
+    nbr_t = torch.tensor(nbr, dtype=torch.long)
+    pos = torch.tensor(g["pos"], requires_grad=True)
+    raw = (pos[nbr_t] - pos[centers]).detach()
+    shift = box * torch.round(raw / box)
+    disp = pos[nbr_t] - pos[centers] - shift
+    r = torch.linalg.norm(disp, dim=-1)
+    Rv, _ = cheb_exp_cos_radial_table_with_derivative(r, torch.full((E,), rc, dtype=torch.float64),
+                                                       torch.full((E,), lam, dtype=torch.float64), nmax,
+                                                       backend="reference")
+    Yv, _ = spherical_harmonics_table_with_derivative(disp, lmax, real_output=False, backend="reference")
+    p = torch.tensor(g["prefactor"][g["species"][nbr]])
+    edge = (p[:, None, None] * Rv[:, 1:, None]).to(torch.complex128) * Yv[:, None, :]
+    A = density_accumulate(edge.reshape(E, -1), centers, N, backend="reference").reshape(N, nmax, -1)
+    multiplets = {l: A[:, :, l * l:(l + 1) * (l + 1)] for l in range(lmax + 1)}
+    b3 = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu3_L0.npz"))
+    feats = []
+    for word in b3.words:
+        rep = compile_ace_factorized_schedules_by_L(content=tuple(n for _, n in word),
+                                                    input_Ls=tuple(l for l, _ in word))
+        sched = rep.schedules_by_L[0]
+        width = 2 * int(sched.block_L_by_label().max()) + 1
+        rows, prepared = [], {}
+        for blocks in sched.block_specs:
+            row = []
+            for block in blocks:
+                key = (block["n"], block["l"], block.get("k_b"), block.get("Lambda"), block.get("multiplicity_index"))
+                if key not in prepared:
+                    src = multiplets[block["l"]][..., block["n"] - 1, :]
+                    if block["kind"] == "sym":
+                        plan = couplings.symmetric_power_product_plan(
+                            [{"descriptor_index": m, "power": block["k_b"], "input_L": block["l"],
+                              "output_L": block["Lambda"], "multiplicity_index": block["multiplicity_index"],
+                              "component_index": m, "channel_indices": tuple(range(2 * block["l"] + 1))}
+                             for m in range(2 * block["Lambda"] + 1)],
+                            descriptor_count=2 * block["Lambda"] + 1, channel_count=2 * block["l"] + 1,
+                            basis_convention="complex_magnetic")
+                        src = symmetric_power_product_plan_contraction(src, plan, backend="reference")
+                    prepared[key] = torch.nn.functional.pad(src, (0, width - src.shape[-1]))
+                row.append(prepared[key])
+            rows.append(torch.stack(row, dim=-2))
+        bv = torch.stack(rows, dim=-3)
+        feats.append(rep.evaluate(bv, target_L=0, backend="torch"))
+    B = torch.cat(feats, dim=1)
+    w = torch.tensor(g["w3"])[torch.tensor(g["species"], dtype=torch.long)]
+    energy = (w * B.real).sum()
+    (grad,) = torch.autograd.grad(energy, pos)
+    np.savez_compressed(os.path.join(HERE, "forces_small.npz"), energy=np.asarray(float(energy)),
+                        forces=(-grad).numpy())
+    print("forces_small.npz energy", float(energy), "|F| max", float(grad.abs().max()))
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace"]
+    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -345,3 +412,5 @@ if __name__ == "__main__":
         radial_sh_density_fixture()
     if "ace" in which:
         ace_fixture()
+    if "forces" in which:
+        forces_fixture()

@@ -1,0 +1,98 @@
+"""Force path (B-basis adjoint, edge gradients, reverse-edge gather) against
+reference forces from torch autograd through the reference ops."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bundle(stem):
+    from ye3t_b200.schedules import ACEBundle
+    return ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", stem + ".npz"))
+
+
+def _evaluator(small, stem, weights):
+    from ye3t_b200.ace import ACEConfig, ACEEvaluator
+    return ACEEvaluator(_bundle(stem), DEV, config=ACEConfig(float(small["rc"]), float(small["lam"])),
+                        species_prefactor=small["prefactor"], weights=weights)
+
+
+def test_forces_match_reference_autograd(golden):
+    small = golden("ace_small")
+    ref = golden("forces_small")
+    ev = _evaluator(small, "ace_n8_l3_nu3_L0", small["w3"])
+    pos = torch.as_tensor(small["pos"], device=DEV)
+    sp = torch.as_tensor(small["species"], device=DEV)
+    E, F = ev.energy_forces(pos, sp, float(small["box"]))
+    assert abs(float(E) - float(ref["energy"])) <= 1e-12 * abs(float(ref["energy"]))
+    Fr = ref["forces"]
+    err = np.abs(F.cpu().numpy() - Fr).max() / np.abs(Fr).max()
+    assert err <= 1e-10, err
+
+
+def test_energy_grad_energy_equals_forward_and_gradient_is_exact(golden):
+    small = golden("ace_small")
+    rng = np.random.default_rng(4)
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    N = 1024
+    box = (N / 0.05) ** (1 / 3)
+    pos = torch.as_tensor(rng.uniform(0, box, size=(N, 3)), device=DEV)
+    sp = torch.as_tensor(rng.integers(0, 3, size=N), device=DEV)
+    row, nbr = ev.neighbor_list(pos, box)
+    A = ev.density(pos, sp, box, row, nbr)
+    e_fwd = ev.energy_from_density(A, sp)
+    e_adj, G = ev.energy_grad(A, sp)
+    np.testing.assert_allclose(e_adj.cpu().numpy(), e_fwd.cpu().numpy(), rtol=1e-11, atol=1e-12)
+    # dE/dA against a central difference along a random complex direction (B is a polynomial in A)
+    dA = torch.complex(torch.randn_like(A.real), torch.randn_like(A.real)) * 1e-6
+    ep = ev.energy_from_density(A + dA, sp).sum().item()
+    em = ev.energy_from_density(A - dA, sp).sum().item()
+    lin = (G * dA).real.sum().item()
+    assert abs((ep - em) / 2 - lin) <= 1e-6 * abs(lin) + 1e-12
+
+
+def test_forces_sum_to_zero_and_match_finite_differences(golden):
+    small = golden("ace_small")
+    rng = np.random.default_rng(5)
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    N = 512
+    box = (N / 0.05) ** (1 / 3)
+    pos0 = rng.uniform(0, box, size=(N, 3))
+    sp = torch.as_tensor(rng.integers(0, 3, size=N), device=DEV)
+    E, F = ev.energy_forces(torch.as_tensor(pos0, device=DEV), sp, box)
+    F = F.cpu().numpy()
+    assert np.abs(F.sum(0)).max() <= 1e-9 * np.abs(F).max()  # momentum conservation
+    h = 1e-5
+    for k, ax in ((3, 0), (100, 1), (400, 2)):
+        p = pos0.copy()
+        p[k, ax] += h
+        ep = float(ev.energy_forces(torch.as_tensor(p, device=DEV), sp, box)[0])
+        p[k, ax] -= 2 * h
+        em = float(ev.energy_forces(torch.as_tensor(p, device=DEV), sp, box)[0])
+        fd = -(ep - em) / (2 * h)
+        assert abs(fd - F[k, ax]) <= 1e-6 * max(1.0, abs(F[k, ax])), (k, ax, fd, F[k, ax])
+
+
+def test_partial_forces_sum_to_gather_forces(golden):
+    small = golden("ace_small")
+    ev = _evaluator(small, "ace_n8_l3_nu3_L0", small["w3"])
+    pos = torch.as_tensor(small["pos"], device=DEV)
+    sp = torch.as_tensor(small["species"], device=DEV)
+    box = float(small["box"])
+    _, F = ev.energy_forces(pos, sp, box)
+    N = pos.shape[0]
+    acc = torch.zeros((N, 3), dtype=torch.float64, device=DEV)
+    for b, e in ((0, 40), (40, 96)):  # two atom blocks, as two ranks would
+        row, nbr = ev.neighbor_list(pos, box, b, e)
+        A = ev.density(pos, sp, box, row, nbr, b)
+        _, G = ev.energy_grad(A, sp[b:e])
+        g = ev.edge_grad(pos, sp, box, row, nbr, G, begin=b)
+        ev.partial_forces_from_edges(row, nbr, g, b, N, out=acc)
+    np.testing.assert_allclose(acc.cpu().numpy(), F.cpu().numpy(), rtol=1e-10, atol=1e-12)

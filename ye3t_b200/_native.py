@@ -69,6 +69,11 @@ _SIGS = {
                                        VP]),
     "y3b_ace_features": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
     "y3b_ace_energy": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP]),
+    "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP]),
+    "y3b_ace_edge_grad": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
+                                         VP, VP]),
+    "y3b_forces_gather": (ctypes.c_int, [VP, VP, I64, VP, VP, VP, VP]),
+    "y3b_forces_scatter": (ctypes.c_int, [VP, VP, I64, I64, I64, VP, VP, VP]),
     "y3b_fma_peak_launch": (ctypes.c_int, [ctypes.c_int, I32, I32, I32, VP, ctypes.POINTER(DBL), VP]),
 }
 

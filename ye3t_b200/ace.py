@@ -130,6 +130,64 @@ class ACEEvaluator:
                                            self._stream()), "ace_energy")
         return out
 
+    # -- force path ------------------------------------------------------------------
+    def energy_grad(self, A: torch.Tensor, species_centres: torch.Tensor):
+        """(per-atom energies, G = dE/dA) from the A-basis (B is holomorphic in A: dE = Re(sum G dA))."""
+        if self.weights is None:
+            raise ValueError("weights are required for the energy")
+        A = A.to(self.device, torch.complex128).contiguous()
+        n = A.shape[0]
+        sp = species_centres.to(self.device, torch.int32).contiguous()
+        e = torch.empty(n, dtype=torch.float64, device=self.device)
+        G = torch.empty_like(A)
+        nat.check(nat.lib().y3b_ace_energy_grad(ctypes_ref(self._tables), A.data_ptr(), n, sp.data_ptr(),
+                                                self.weights.data_ptr(), self.weights.shape[0], e.data_ptr(),
+                                                G.data_ptr(), self._stream()), "ace_energy_grad")
+        return e, G
+
+    def edge_grad(self, positions, species, box, row_offsets, neighbors, dEdA, begin: int = 0,
+                  status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """g_e = dE_i/dd_e [E, 3] for the rows of centres [begin, begin + n)."""
+        pos = positions.to(self.device, torch.float64).contiguous()
+        sp = species.to(self.device, torch.int32).contiguous()
+        count = int(row_offsets.shape[0]) - 1
+        E = int(neighbors.shape[0])
+        g = torch.empty((max(E, 1), 3), dtype=torch.float64, device=self.device)
+        nat.check(nat.lib().y3b_ace_edge_grad(
+            pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box), row_offsets.data_ptr(),
+            neighbors.data_ptr(), self.species_prefactor.data_ptr(), self.species_prefactor.numel(),
+            self.bundle.nmax, self.bundle.lmax, float(self.config.cutoff), float(self.config.radial_lambda),
+            dEdA.data_ptr(), g.data_ptr(), nat.ptr(status), self._stream()), "ace_edge_grad")
+        return g[:E]
+
+    def forces_from_edges(self, row_offsets, neighbors, edge_grad, status: Optional[torch.Tensor] = None):
+        """F = -dE/dr for every atom from the rows of all atoms (deterministic gather)."""
+        N = int(row_offsets.shape[0]) - 1
+        F = torch.empty((N, 3), dtype=torch.float64, device=self.device)
+        nat.check(nat.lib().y3b_forces_gather(row_offsets.data_ptr(), neighbors.data_ptr(), N,
+                                              edge_grad.data_ptr(), F.data_ptr(), nat.ptr(status),
+                                              self._stream()), "forces_gather")
+        return F
+
+    def partial_forces_from_edges(self, row_offsets, neighbors, edge_grad, begin: int, atom_count: int,
+                                  out: Optional[torch.Tensor] = None):
+        """This atom block's contribution to every atom's force (the sum over blocks is F)."""
+        count = int(row_offsets.shape[0]) - 1
+        if out is None:
+            out = torch.zeros((atom_count, 3), dtype=torch.float64, device=self.device)
+        nat.check(nat.lib().y3b_forces_scatter(row_offsets.data_ptr(), neighbors.data_ptr(), int(begin), count,
+                                               int(atom_count), edge_grad.data_ptr(), out.data_ptr(),
+                                               self._stream()), "forces_scatter")
+        return out
+
+    def energy_forces(self, positions, species, box):
+        """(total energy, forces [N, 3]) of the whole system on this device."""
+        row, nbr = self.neighbor_list(positions, box)
+        A = self.density(positions, species, box, row, nbr)
+        e, G = self.energy_grad(A, species.to(self.device, torch.int32))
+        g = self.edge_grad(positions, species, box, row, nbr, G)
+        return e.sum(), self.forces_from_edges(row, nbr, g)
+
     # -- end to end ----------------------------------------------------------------
     def energy(self, positions, species, box, begin: int = 0, end: Optional[int] = None):
         """Per-atom energies of centres [begin, end) from positions."""

@@ -2,6 +2,7 @@
 // schedule bundle (kernel 2).
 #include "edge_math.cuh"
 #include "neighbors.cuh"
+#include "ace_common.cuh"
 
 namespace y3b {
 
@@ -132,34 +133,9 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX>::value) ace_density_ke
 // with block B-2 (vs) unrolled at compile time and held in registers.
 // MODE 0 writes features [N, F]; MODE 1 reduces to per-atom energy.
 // ---------------------------------------------------------------------------
-constexpr int kLanes = 32;
+constexpr int kLanes = 32;  // atoms per B-basis CTA (one per lane)
 constexpr int kEvalWarps = 16;
 constexpr int kPadEntries = 16;  // zero entries before and after the block entries
-
-struct Item {
-  int sel, d0, d1, dl, K, coef, f0, f1;
-  int b0, b1, b2, b3;
-};
-
-__device__ __forceinline__ Item load_item(const int4* __restrict__ items, int64_t i) {
-  const int4 a = __ldg(items + 4 * i), b = __ldg(items + 4 * i + 1), c = __ldg(items + 4 * i + 2);
-  Item it;
-  it.sel = a.x; it.d0 = a.y; it.d1 = a.z; it.dl = a.w;
-  it.K = b.x; it.coef = b.y; it.f0 = b.z; it.f1 = b.w;
-  it.b0 = c.x; it.b1 = c.y; it.b2 = c.z; it.b3 = c.w;
-  return it;
-}
-
-__device__ __forceinline__ void cmac(double2& acc, double c, double2 v) {
-  acc.x = fma(c, v.x, acc.x);
-  acc.y = fma(c, v.y, acc.y);
-}
-
-// acc += x * t (complex multiply-add)
-__device__ __forceinline__ void cfma(double2& acc, double2 x, double2 t) {
-  acc.x = fma(x.x, t.x, fma(-x.y, t.y, acc.x));
-  acc.y = fma(x.x, t.y, fma(x.y, t.x, acc.y));
-}
 
 // B = 1: a single tuple, i_0 = K.
 template <int NC>
@@ -169,13 +145,6 @@ __device__ __forceinline__ void eval_b1(const double2* __restrict__ P, const Ite
   cmac(a0, __ldg(coef + it.coef), v);
   if (NC == 2) cmac(a1, __ldg(coef + it.coef + 1), v);
 }
-
-// Coefficient row of one prefix: NC doubles per j, padded to an even count so
-// that a 16-byte load returns two coefficients (packing.py lays rows out so).
-template <int DS, int NC>
-struct RowWidth {
-  static constexpr int value = NC == 2 ? 2 * DS : ((DS + 1) & ~1);
-};
 
 // T_c += C[j, c] * (vs[j] * v_last[kS - j]) for every j < DS.  Pk points at
 // v_last[kS], so each j reads at a compile-time offset from it.  Slots whose
@@ -324,9 +293,7 @@ __device__ __forceinline__ void eval_dispatch(const double2* __restrict__ P, con
 }
 
 // Fill shared-memory slot `slot` with every symmetric output of radial
-// channel `ch`: out = sum_q coeff_q prod_i x_i^{k_qi}, the powers of each
-// distinct input component multiplied in increasing component order as in
-// ye3t_runtime_core.cpp:5279.
+// channel `ch` (sym_output, ace_common.cuh).
 __device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, double2* __restrict__ sm, int W, int slot,
                                           int ch, int lane, int warp) {
   const int na = int(t.nmax) * W;
@@ -334,27 +301,7 @@ __device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, double2* __re
   const int4* outs = reinterpret_cast<const int4*>(t.sym_outputs);
   for (int o = warp; o < so; o += kEvalWarps) {
     const int4 r = __ldg(outs + o);  // (l^2, term begin, term end, -)
-    const double2* x = sm + (ch * W + r.x) * kLanes + lane;
-    double2 acc = make_double2(0.0, 0.0);
-    for (int q = r.y; q < r.z; ++q) {
-      const uint32_t f = __ldg(t.sym_term_factors + q);
-      double2 m = make_double2(__ldg(t.sym_term_coeff + q), 0.0);
-      int k = 0;
-      while (k < 4) {
-        const int ci = (f >> (8 * k)) & 255;
-        if (ci == 255) break;
-        const double2 xv = x[ci * kLanes];
-        double2 pw = xv;
-        ++k;
-        while (k < 4 && int((f >> (8 * k)) & 255) == ci) {
-          pw = mul(pw, xv);
-          ++k;
-        }
-        m = mul(m, pw);
-      }
-      acc = add(acc, m);
-    }
-    sm[(na + slot * so + o) * kLanes + lane] = acc;
+    sm[(na + slot * so + o) * kLanes + lane] = sym_output(t, r.y, r.z, sm + (ch * W + r.x) * kLanes + lane, kLanes);
   }
 }
 

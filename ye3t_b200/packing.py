@@ -46,6 +46,7 @@ class PackedBundle:
     sym_term_count_per_atom: int
     sym_flops_per_atom: float = 0.0
     item_flops: Optional[float] = None
+    item_grad_flops: Optional[float] = None
 
     def tables(self) -> nat.AceTables:
         a = self.arrays
@@ -78,8 +79,62 @@ class PackedBundle:
         tb = self.term_block_count_per_atom
         sched = 2.0 * terms + 6.0 * (tb - terms) + 2.0 * terms
         if self.item_flops is None:
-            self.item_flops = item_flops_per_atom(self.arrays["items"].cpu().numpy())
-        return {"items": self.item_flops, "terms": sched, "sym": float(self.sym_flops_per_atom)}
+            items = self.arrays["items"].cpu().numpy()
+            self.item_flops = item_flops_per_atom(items)
+            self.item_grad_flops = item_grad_flops_per_atom(items)
+        return {"items": self.item_flops, "items_grad": self.item_grad_flops, "terms": sched,
+                "sym": float(self.sym_flops_per_atom)}
+
+
+def item_grad_flops_per_atom(items: np.ndarray) -> float:
+    """FP64 flops per atom of the energy-and-gradient walk (valid tuples only).
+
+    Mirrors ace_grad.cu: per valid slot of a row the weighted coefficient
+    (2 nc - 1), the product q (6), T += c q (4), x c (2), gvs += (x c) vl (8)
+    and the last-block gradient (x c) vs (8); per row the energy (4) and the
+    prefix gradients (8 or 14).  4-block items with a register block <= 7
+    share q per anti-diagonal: per valid j there q (6), gvs (8) and the
+    last-block gradient (8); per prefix x0 x1 (6), per j the weighted
+    coefficient and the T and R multiply-adds (2 nc - 1 + 8), the energy (4)
+    and two gradients (6 + 8).
+    """
+    flops = 0.0
+    cache = {}
+    for row in items:
+        key = tuple(int(v) for v in row[:5])
+        if key not in cache:
+            sel, D0, D1, Dl, K = key
+            nc = sel % 2 + 1
+            B = (sel // 2) // 7 + 1
+            ds = 2 * ((sel // 2) % 7) + 1
+            wc = 2 * nc - 1
+            smin, smax = K - (ds - 1) - (Dl - 1), K
+
+            def valid(S):
+                return sum(1 for j in range(ds) if 0 <= K - S - j < Dl)
+            f = 0.0
+            if B == 1:
+                f = 4.0 * nc
+            elif B == 2:
+                f = valid(0) * (wc + 28.0) + 2.0
+            elif B == 3:
+                for i0 in range(D0):
+                    if smin <= i0 <= smax:
+                        f += valid(i0) * (wc + 28.0) + 4.0
+            elif ds <= 7:
+                for S in range(max(0, smin), min(D0 - 1 + D1 - 1, smax) + 1):
+                    v = valid(S)
+                    rows = sum(1 for i0 in range(D0) if 0 <= S - i0 < D1)
+                    f += 22.0 * v + rows * (6.0 + ds * (wc + 8.0) + 18.0)
+            else:
+                for i0 in range(D0):
+                    for i1 in range(D1):
+                        S = i0 + i1
+                        if smin <= S <= smax:
+                            f += valid(S) * (wc + 28.0) + 6.0 + 4.0 + 14.0
+            cache[key] = f
+        flops += cache[key]
+    return flops
 
 
 def _factors(row):
@@ -347,6 +402,57 @@ def item_flops_per_atom(items: np.ndarray) -> float:
                             f += valid(S) * (6.0 + 4.0 * nc) + 8.0 * nc
                             outer.add(i0)
                 f += 8.0 * nc * len(outer)
+            cache[key] = f
+        flops += cache[key]
+    return flops
+
+
+def item_grad_flops_per_atom(items: np.ndarray) -> float:
+    """FP64 flops per atom of the energy-and-gradient walk (valid tuples only).
+
+    Mirrors ace_grad.cu: per valid slot of a row the weighted coefficient
+    (2 nc - 1), the product q (6), T += c q (4), x c (2), gvs += (x c) vl (8)
+    and the last-block gradient (x c) vs (8); per row the energy (4) and the
+    prefix gradients (8 or 14).  4-block items with a register block <= 7
+    share q per anti-diagonal: per valid j there q (6), gvs (8) and the
+    last-block gradient (8); per prefix x0 x1 (6), per j the weighted
+    coefficient and the T and R multiply-adds (2 nc - 1 + 8), the energy (4)
+    and two gradients (6 + 8).
+    """
+    flops = 0.0
+    cache = {}
+    for row in items:
+        key = tuple(int(v) for v in row[:5])
+        if key not in cache:
+            sel, D0, D1, Dl, K = key
+            nc = sel % 2 + 1
+            B = (sel // 2) // 7 + 1
+            ds = 2 * ((sel // 2) % 7) + 1
+            wc = 2 * nc - 1
+            smin, smax = K - (ds - 1) - (Dl - 1), K
+
+            def valid(S):
+                return sum(1 for j in range(ds) if 0 <= K - S - j < Dl)
+            f = 0.0
+            if B == 1:
+                f = 4.0 * nc
+            elif B == 2:
+                f = valid(0) * (wc + 28.0) + 2.0
+            elif B == 3:
+                for i0 in range(D0):
+                    if smin <= i0 <= smax:
+                        f += valid(i0) * (wc + 28.0) + 4.0
+            elif ds <= 7:
+                for S in range(max(0, smin), min(D0 - 1 + D1 - 1, smax) + 1):
+                    v = valid(S)
+                    rows = sum(1 for i0 in range(D0) if 0 <= S - i0 < D1)
+                    f += 22.0 * v + rows * (6.0 + ds * (wc + 8.0) + 18.0)
+            else:
+                for i0 in range(D0):
+                    for i1 in range(D1):
+                        S = i0 + i1
+                        if smin <= S <= smax:
+                            f += valid(S) * (wc + 28.0) + 6.0 + 4.0 + 14.0
             cache[key] = f
         flops += cache[key]
     return flops
