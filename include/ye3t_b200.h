@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define Y3B_ABI_VERSION 3
+#define Y3B_ABI_VERSION 4
 
 /* dtype codes */
 #define Y3B_F32 0
@@ -183,6 +183,16 @@ typedef struct {
   const int32_t* sym_outputs;     /* [sym_output_count, 4]: l^2, term begin, term end, 0 */
   const uint32_t* sym_term_factors; /* [S] 4 x uint8 input components (255 = unused) */
   const double* sym_term_coeff;     /* [S] */
+  /* adjoint only: items of one shape paired per phase (one per half-warp) */
+  int64_t group_count;
+  const int32_t* groups;          /* [group_count, 2] item indices (second -1: odd item out) */
+  const int32_t* group_offsets;   /* [phase_count + 1] */
+  /* adjoint only: derivatives of the symmetric outputs listed per input
+     component (l^2 + m + l inside a radial channel) */
+  int64_t sym_grad_count;
+  const int32_t* sym_grad_offsets; /* [(lmax+1)^2 + 1] */
+  const int32_t* sym_grad_index;   /* [sym_grad_count, 2]: output, 4 x u8 remaining factors (255 unused) */
+  const double* sym_grad_coeff;    /* [sym_grad_count]: multiplicity x monomial coefficient */
 } y3b_ace_tables;
 
 /* A-basis density for centres [center_begin, center_begin + center_count):
@@ -225,10 +235,11 @@ int y3b_ace_energy(const y3b_ace_tables* tables, const void* A, int64_t atom_cou
  * ---------------------------------------------------------------------- */
 
 /* Per-atom energies and G = dE/dA (complex128, A's layout; B is holomorphic
- * in A so dE = Re(sum G dA)). */
+ * in A so dE = Re(sum G dA)).  Species outside [0, species_count) set
+ * Y3B_STATUS_INDEX_RANGE in *status (nullable) and use species 0. */
 int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
                         const int32_t* species, const double* weights, int64_t species_count,
-                        double* energy, void* dEdA, void* stream);
+                        double* energy, void* dEdA, int32_t* status, void* stream);
 
 /* Per-edge g_e = dE_i/dd_e (f64 [E, 3], d_e = r_j - r_i minimum image) for the
  * rows of centres [center_begin, center_begin + center_count), from dEdA of

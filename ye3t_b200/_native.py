@@ -16,7 +16,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libye3t_b200.so")
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 F32, F64, C64, C128 = 0, 1, 2, 3
 STATUS_INDEX_RANGE = 1
 STATUS_CAPACITY = 2
@@ -45,6 +45,8 @@ class AceTables(ctypes.Structure):
         ("nmax", I64), ("lmax", I64), ("smem_entries", I64), ("feature_count", I64), ("item_count", I64),
         ("phase_count", I64), ("sym_output_count", I64), ("items", VP), ("item_coef", VP), ("phases", VP),
         ("sym_outputs", VP), ("sym_term_factors", VP), ("sym_term_coeff", VP),
+        ("group_count", I64), ("groups", VP), ("group_offsets", VP),
+        ("sym_grad_count", I64), ("sym_grad_offsets", VP), ("sym_grad_index", VP), ("sym_grad_coeff", VP),
     ]
 
 
@@ -69,7 +71,7 @@ _SIGS = {
                                        VP]),
     "y3b_ace_features": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
     "y3b_ace_energy": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP]),
-    "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP]),
+    "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP, VP]),
     "y3b_ace_edge_grad": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                          VP, VP]),
     "y3b_forces_gather": (ctypes.c_int, [VP, VP, I64, VP, VP, VP, VP]),

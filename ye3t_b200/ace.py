@@ -131,7 +131,7 @@ class ACEEvaluator:
         return out
 
     # -- force path ------------------------------------------------------------------
-    def energy_grad(self, A: torch.Tensor, species_centres: torch.Tensor):
+    def energy_grad(self, A: torch.Tensor, species_centres: torch.Tensor, status: Optional[torch.Tensor] = None):
         """(per-atom energies, G = dE/dA) from the A-basis (B is holomorphic in A: dE = Re(sum G dA))."""
         if self.weights is None:
             raise ValueError("weights are required for the energy")
@@ -142,7 +142,7 @@ class ACEEvaluator:
         G = torch.empty_like(A)
         nat.check(nat.lib().y3b_ace_energy_grad(ctypes_ref(self._tables), A.data_ptr(), n, sp.data_ptr(),
                                                 self.weights.data_ptr(), self.weights.shape[0], e.data_ptr(),
-                                                G.data_ptr(), self._stream()), "ace_energy_grad")
+                                                G.data_ptr(), nat.ptr(status), self._stream()), "ace_energy_grad")
         return e, G
 
     def edge_grad(self, positions, species, box, row_offsets, neighbors, dEdA, begin: int = 0,

@@ -21,241 +21,449 @@ namespace y3b {
 
 namespace {
 
-// A CTA holds values and gradient accumulators of 16 atoms in shared memory
-// ([entry][atom]); lanes l and l + 16 of a warp work on atom l and split each
-// item's outer iterations between them.
+// A CTA holds 16 atoms.  Values V ([entry][atom] complex, with zero entries
+// before and after) and gradients G (real and imaginary planes, [entry][atom])
+// live in shared memory.  Lanes l and l + 16 of a warp both work on atom l,
+// each half-warp on its own item; the two items of a warp have the same shape
+// (packing pairs them), so both halves follow one control flow.
+//
+// Every item accumulates its gradients in registers and adds each block's
+// gradient to G once.  Entries that leave a register window early go to a
+// small per-lane staging area first.  The additions to G are batched
+// compare-and-swaps: all old values are loaded, all swaps issued, and only the
+// ones that lost a race against another warp are retried.
 constexpr int kGA = 16;
 constexpr int kGWarps = 8;
-constexpr int kGPad = 16;  // zero entries before and after the block entries
+constexpr int kGPad = 16;
+constexpr int kStage = 14;  // staged gradient entries per lane (two blocks of <= 7)
+#ifndef Y3B_GRAD_BATCH
+#define Y3B_GRAD_BATCH 2
+#endif
 
-struct Tile {
-  const double2* V;  // V[e * kGA]: value of entry e for this lane's atom
-  double2* G;        // G[e * kGA]: its gradient accumulator
+// Shared-window (32-bit) byte addresses of this lane's data.
+struct Ctx {
+  uint32_t V;        // entry e of this lane's atom at V + e * kGA * 16
+  uint32_t Gr, Gi;   // its gradient planes, entry e at + e * kGA * 8
+  uint32_t stage;    // this lane's staged entry k at stage + k * 32 * 16
 };
 
-__device__ __forceinline__ double2 vat(const Tile& tl, int e) { return tl.V[e * kGA]; }
-
-// Gradient entries are shared by the CTA's warps, so accumulation is atomic
-// (the order of these partial sums is not fixed; forces agree run to run to
-// rounding).
-__device__ __forceinline__ void gacc(const Tile& tl, int e, double2 v) {
-  atomicAdd(&tl.G[e * kGA].x, v.x);
-  atomicAdd(&tl.G[e * kGA].y, v.y);
+__device__ __forceinline__ double2 lds128(uint32_t a) {
+  double2 v;
+  asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "r"(a));
+  return v;
 }
 
-__device__ __forceinline__ double2 cscale(double c, double2 v) { return make_double2(c * v.x, c * v.y); }
-
-__device__ __forceinline__ double2 shfl_half(double2 v) {
-  return make_double2(__shfl_xor_sync(0xffffffffu, v.x, 16), __shfl_xor_sync(0xffffffffu, v.y, 16));
+__device__ __forceinline__ void sts128(uint32_t a, double2 v) {
+  asm volatile("st.shared.v2.f64 [%0], {%1, %2};" ::"r"(a), "d"(v.x), "d"(v.y));
 }
 
-// Readout-weighted coefficient j of a row: w0 C[j, 0] + w1 C[j, 1].
-template <int NC>
-__device__ __forceinline__ double wcoef(const double* __restrict__ crow, int j, double w0, double w1) {
-  if (NC == 2) {
-    const double2 c = __ldg(reinterpret_cast<const double2*>(crow) + j);
-    return w0 * c.x + w1 * c.y;
+__device__ __forceinline__ double2 vat(const Ctx& c, int e) { return lds128(c.V + e * (kGA * 16)); }
+
+__device__ __forceinline__ double2 cscale(double s, double2 v) { return make_double2(s * v.x, s * v.y); }
+
+__device__ __forceinline__ unsigned long long dbits(double x) {
+  return static_cast<unsigned long long>(__double_as_longlong(x));
+}
+
+__device__ __forceinline__ unsigned long long lds64(uint32_t a) {
+  unsigned long long v;
+  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long cas64(uint32_t a, unsigned long long cmp, unsigned long long val) {
+  unsigned long long old;
+  asm volatile("atom.shared.cas.b64 %0, [%1], %2, %3;" : "=l"(old) : "r"(a), "l"(cmp), "l"(val));
+  return old;
+}
+
+__device__ __forceinline__ void red_add64(uint32_t a, double v) {
+  asm volatile("red.shared.add.f64 [%0], %1;" ::"r"(a), "d"(v));
+}
+
+// G[base + STEP * k] += v[k] for K0 <= k < K0 + NB, lo <= k < hi: loads the
+// old values, then issues every compare-and-swap at once; the few that lost a
+// race against another warp are redone as single atomic additions.  The loads
+// and swaps are volatile asm, so successive batches stay in program order.
+template <int NB, int STEP, int K0, int N>
+__device__ __forceinline__ void g_add_batch_lanes(uint32_t ar, uint32_t ai, int lo, int hi, const double2 (&v)[N]) {
+  constexpr int kStride = STEP * kGA * 8;
+  unsigned long long o[2 * NB];
+#pragma unroll
+  for (int b = 0; b < 2 * NB; ++b) {
+    const int k = K0 + (b >> 1);
+    const double x = k < N ? ((b & 1) ? v[k < N ? k : 0].y : v[k < N ? k : 0].x) : 0.0;
+    if (k < N && k >= lo && k < hi && x != 0.0) o[b] = lds64(((b & 1) ? ai : ar) + k * kStride);
   }
-  return w0 * __ldg(crow + j);
-}
-
-// Register window over the last block's gradient: a[t] belongs to index
-// base - t.  A half-warp's bases fall by 2 per outer step, so each step
-// flushes the two entries that no later step can reach and shifts by two.
-template <int DS>
-__device__ __forceinline__ void win_step2(const Tile& tl, int bl, int dl, int base, double2 (&a)[DS]) {
 #pragma unroll
-  for (int t = 0; t < 2 && t < DS; ++t) {
-    const int li = base - t;
-    if (li >= 0 && li < dl && (a[t].x != 0.0 || a[t].y != 0.0)) gacc(tl, bl + li, a[t]);
-  }
-#pragma unroll
-  for (int t = 0; t < DS; ++t) a[t] = t + 2 < DS ? a[t + 2] : make_double2(0.0, 0.0);
-}
-
-template <int DS>
-__device__ __forceinline__ void win_flush(const Tile& tl, int bl, int dl, int base, const double2 (&a)[DS]) {
-#pragma unroll
-  for (int t = 0; t < DS; ++t) {
-    const int li = base - t;
-    if (li >= 0 && li < dl && (a[t].x != 0.0 || a[t].y != 0.0)) gacc(tl, bl + li, a[t]);
-  }
-}
-
-// Half-warp partial sums of register gradients are combined, then flushed once.
-template <int D>
-__device__ __forceinline__ void flush_pair(const Tile& tl, int base, int count, double2 (&g)[D], int half) {
-#pragma unroll
-  for (int j = 0; j < D; ++j) {
-    const double2 s = add(g[j], shfl_half(g[j]));
-    if (half == 0 && j < count && (s.x != 0.0 || s.y != 0.0)) gacc(tl, base + j, s);
-  }
-}
-
-template <int NC>
-__device__ __forceinline__ void adj_b1(const Tile& tl, const Item& it, const double* __restrict__ coef, double w0,
-                                       double w1, int half, double& e) {
-  if (half) return;
-  const double c = w0 * __ldg(coef + it.coef) + (NC == 2 ? w1 * __ldg(coef + it.coef + 1) : 0.0);
-  const double2 v = vat(tl, it.b0 + it.K);
-  e += c * v.x;
-  gacc(tl, it.b0 + it.K, make_double2(c, 0.0));
-}
-
-// One row with prefix value x:  F += x sum_j c_j vs_j vl[kS - j].  Returns
-// T = sum_j c_j vs_j vl_j; adds x c_j vl_j to gvs[j] and x c_j vs_j to the
-// last block's window (win[j] belongs to index kS - j).
-template <int DS, int NC>
-__device__ __forceinline__ double2 adj_row(const Tile& tl, int bl, int kS, int dl, const double2 (&vs)[DS],
-                                           double2 (&gvs)[DS], double2 (&win)[DS], const double* __restrict__ crow,
-                                           double w0, double w1, double2 x) {
-  double2 T = make_double2(0.0, 0.0);
-#pragma unroll
-  for (int j = 0; j < DS; ++j) {
-    const int li = kS - j;
-    if (li >= 0 && li < dl) {
-      const double c = wcoef<NC>(crow, j, w0, w1);
-      const double2 vl = vat(tl, bl + li);
-      cmac(T, c, mul(vs[j], vl));
-      const double2 xc = cscale(c, x);
-      cfma(gvs[j], xc, vl);
-      cfma(win[j], xc, vs[j]);
+  for (int b = 0; b < 2 * NB; ++b) {
+    const int k = K0 + (b >> 1);
+    const double x = k < N ? ((b & 1) ? v[k < N ? k : 0].y : v[k < N ? k : 0].x) : 0.0;
+    if (k < N && k >= lo && k < hi && x != 0.0) {
+      const uint32_t a = ((b & 1) ? ai : ar) + k * kStride;
+      const unsigned long long want = dbits(__longlong_as_double(static_cast<long long>(o[b])) + x);
+      o[b] = cas64(a, o[b], want) ^ o[b];  // 0 when the swap took effect
     }
   }
-  return T;
+#pragma unroll
+  for (int b = 0; b < 2 * NB; ++b) {
+    const int k = K0 + (b >> 1);
+    const double x = k < N ? ((b & 1) ? v[k < N ? k : 0].y : v[k < N ? k : 0].x) : 0.0;
+    if (k < N && k >= lo && k < hi && x != 0.0 && o[b] != 0) red_add64(((b & 1) ? ai : ar) + k * kStride, x);
+  }
 }
 
-template <int B, int DS, int NC>
-__device__ __forceinline__ void adj_item(const Tile& tl, const Item& it, const double* __restrict__ coef,
-                                         double w0, double w1, int half, double& e) {
-  constexpr int RW = RowWidth<DS, NC>::value;
-  const int bs = B == 2 ? it.b0 : (B == 3 ? it.b1 : it.b2);
-  const int bl = B == 2 ? it.b1 : (B == 3 ? it.b2 : it.b3);
-  double2 vs[DS], gvs[DS], win[DS];
-#pragma unroll
-  for (int j = 0; j < DS; ++j) {
-    vs[j] = vat(tl, bs + j);
-    gvs[j] = make_double2(0.0, 0.0);
-    win[j] = make_double2(0.0, 0.0);
+template <int NB, int STEP, int K0, int N>
+__device__ __forceinline__ void g_add_batch(const Ctx& c, uint32_t ar, uint32_t ai, int lo, int hi,
+                                            const double2 (&v)[N]) {
+  g_add_batch_lanes<NB, STEP, K0, N>(ar, ai, lo, hi, v);
+}
+
+constexpr int kBatch = Y3B_GRAD_BATCH;
+
+template <int STEP, int K0, int N>
+struct GAddChunks {
+  static __device__ __forceinline__ void run(const Ctx& c, uint32_t ar, uint32_t ai, int lo, int hi,
+                                             const double2 (&v)[N]) {
+    g_add_batch<kBatch, STEP, K0, N>(c, ar, ai, lo, hi, v);
+    if constexpr (K0 + kBatch < N) GAddChunks<STEP, K0 + kBatch, N>::run(c, ar, ai, lo, hi, v);
   }
-  const double* c = coef + it.coef;
-  const int dl = it.dl;
-  const int smin = it.K - (DS - 1) - (dl - 1), smax = it.K;
-  if (B == 2) {
-    if (half == 0) {
-      const double2 T = adj_row<DS, NC>(tl, bl, it.K, dl, vs, gvs, win, c, w0, w1, make_double2(1.0, 0.0));
-      e += T.x;
-      win_flush<DS>(tl, bl, dl, it.K, win);
-    }
-  } else if (B == 3) {
-    int i0 = max(0, smin) + half;
-    for (; i0 < it.d0 && i0 <= smax; i0 += 2) {
-      const double2 x0 = vat(tl, it.b0 + i0);
-      const double2 T = adj_row<DS, NC>(tl, bl, it.K - i0, dl, vs, gvs, win, c + i0 * RW, w0, w1, x0);
-      e += x0.x * T.x - x0.y * T.y;
-      gacc(tl, it.b0 + i0, T);
-      win_step2<DS>(tl, bl, dl, it.K - i0, win);
-    }
-    win_flush<DS>(tl, bl, dl, it.K - i0, win);
-  } else if (DS > 7) {
-    // 4 blocks with a wide register block: rows in (i0, i1) order, last-block
-    // gradients added directly
-    for (int i0 = half; i0 < it.d0 && i0 <= smax; i0 += 2) {
-      const double2 x0 = vat(tl, it.b0 + i0);
-      double2 gx0 = make_double2(0.0, 0.0);
-      const int i1lo = max(0, smin - i0), i1hi = min(it.d1 - 1, smax - i0);
-      for (int i1 = i1lo; i1 <= i1hi; ++i1) {
-        const double2 x1 = vat(tl, it.b1 + i1);
-        const double2 x01 = mul(x0, x1);
-        const int kS = it.K - i0 - i1;
+};
+
+// G[base + STEP * k] += v[k] for lo <= k < hi (zero parts are skipped).
+template <int N, int STEP>
+__device__ __forceinline__ void g_add(const Ctx& c, int base, int lo, int hi, const double2 (&v)[N]) {
+  const uint32_t ar = c.Gr + base * (kGA * 8), ai = c.Gi + base * (kGA * 8);
+  GAddChunks<STEP, 0, N>::run(c, ar, ai, lo, hi, v);
+}
+
+__device__ __forceinline__ void g_add1(const Ctx& c, int e, double2 v) {
+  const double2 a[1] = {v};
+  g_add<1, 1>(c, e, 0, 1, a);
+}
+
+
+// G[base + STEP * k] += staged entry off + k for lo <= k < hi, kBatch entries
+// at a time.
+template <int STEP>
+__device__ __forceinline__ void stage_flush_impl(const Ctx& c, int base, int off, int lo, int hi) {
+  const uint32_t ar = c.Gr + base * (kGA * 8), ai = c.Gi + base * (kGA * 8);
 #pragma unroll
-        for (int j = 0; j < DS; ++j) win[j] = make_double2(0.0, 0.0);
-        const double2 T = adj_row<DS, NC>(tl, bl, kS, dl, vs, gvs, win, c + (i0 * it.d1 + i1) * RW, w0, w1, x01);
-        win_flush<DS>(tl, bl, dl, kS, win);
-        e += x01.x * T.x - x01.y * T.y;
-        cfma(gx0, x1, T);
-        gacc(tl, it.b1 + i1, mul(x0, T));
+  for (int k0 = 0; k0 < kStage; k0 += kBatch) {
+    if (k0 < hi && k0 + kBatch > lo) {
+      double2 v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int k = k0 + u;
+        v[u] = (k + off < kStage && k >= lo && k < hi) ? lds128(c.stage + (off + k) * (32 * 16))
+                                                       : make_double2(0.0, 0.0);
       }
-      gacc(tl, it.b0 + i0, gx0);
+      g_add_batch<kBatch, STEP, 0, kBatch>(c, ar + STEP * k0 * (kGA * 8), ai + STEP * k0 * (kGA * 8), lo - k0,
+                                           hi - k0, v);
+    }
+  }
+}
+
+__device__ __forceinline__ void stage_flush(const Ctx& c, int base, int lo, int hi) {
+  stage_flush_impl<1>(c, base, 0, lo, hi);
+}
+__device__ __forceinline__ void stage_flush_off(const Ctx& c, int base, int off, int lo, int hi) {
+  stage_flush_impl<1>(c, base, off, lo, hi);
+}
+
+// Staged accumulation: entry k of this lane's staging area += v (private to
+// the lane, so a plain read-modify-write).
+__device__ __forceinline__ void stage_acc(const Ctx& c, int k, double2 v) {
+  const uint32_t a = c.stage + k * (32 * 16);
+  sts128(a, add(lds128(a), v));
+}
+
+__device__ __forceinline__ void stage_zero(const Ctx& c, int lo, int hi) {
+#pragma unroll 1
+  for (int k = lo; k < hi; ++k) sts128(c.stage + k * (32 * 16), make_double2(0.0, 0.0));
+}
+
+// The register block is walked in chunks of kCh indices j (runtime width jn
+// <= kCh); every item shape then runs through one code path per block count,
+// which keeps the kernel's register demand within the register file.
+constexpr int kCh = 4;
+
+// Readout-weighted coefficients j0 .. j0 + kCh - 1 of a row (zero past jn):
+// wc[u] = w0 C[j0 + u, 0] + w1 C[j0 + u, 1]; rows are 16-byte aligned and j0
+// is a multiple of kCh, so pairs are read with 16-byte loads.
+__device__ __forceinline__ void wchunk(const double* __restrict__ crow, int nc, int j0, int jn, double w0, double w1,
+                                       double (&wc)[kCh]) {
+  const double2* c2 = reinterpret_cast<const double2*>(crow);
+  if (nc == 2) {
+#pragma unroll
+    for (int u = 0; u < kCh; ++u) {
+      const double2 cc = u < jn ? __ldg(c2 + j0 + u) : make_double2(0.0, 0.0);
+      wc[u] = fma(w1, cc.y, w0 * cc.x);
     }
   } else {
-    // 4 blocks, register block <= 7: anti-diagonals S = i0 + i1 share
-    // q_j = vs_j vl[K - S - j].  Both half-warps take the same S and split its
-    // rows (alternate i0); R_j = sum_rows x0 x1 C[.., j] is combined across
-    // the halves, and half 0 adds the register-block and last-block
-    // gradients (the last block through a window that slides by one per S).
-    constexpr int DQ = DS <= 7 ? DS : 1;
-    double2 wq[DQ];
 #pragma unroll
-    for (int j = 0; j < DQ; ++j) wq[j] = make_double2(0.0, 0.0);
-    const int s_lo = max(0, smin), s_hi = min(it.d0 - 1 + it.d1 - 1, smax);
-    int S = s_lo;
-    for (; S <= s_hi; ++S) {
-      const int kS = it.K - S;
-      double2 q[DQ], R[DQ];
-#pragma unroll
-      for (int j = 0; j < DQ; ++j) {
-        q[j] = mul(vs[j], vat(tl, bl + kS - j));  // out-of-block slots read finite padding; their coefficients are 0
-        R[j] = make_double2(0.0, 0.0);
-      }
-      const int i0lo = max(0, S - (it.d1 - 1)), i0hi = min(it.d0 - 1, S);
-      for (int i0 = i0lo + half; i0 <= i0hi; i0 += 2) {
-        const int i1 = S - i0;
-        const double* crow = c + (i0 * it.d1 + i1) * RW;
-        const double2 x0 = vat(tl, it.b0 + i0), x1 = vat(tl, it.b1 + i1);
-        const double2 x01 = mul(x0, x1);
-        double2 T = make_double2(0.0, 0.0);
-#pragma unroll
-        for (int j = 0; j < DQ; ++j) {
-          const double cj = wcoef<NC>(crow, j, w0, w1);
-          cmac(T, cj, q[j]);
-          cmac(R[j], cj, x01);
-        }
-        e += x01.x * T.x - x01.y * T.y;
-        gacc(tl, it.b0 + i0, mul(x1, T));
-        gacc(tl, it.b1 + i1, mul(x0, T));
-      }
-#pragma unroll
-      for (int j = 0; j < DQ; ++j) {
-        R[j] = add(R[j], shfl_half(R[j]));
-        if (half == 0) {
-          cfma(gvs[j], R[j], vat(tl, bl + kS - j));
-          cfma(wq[j], R[j], vs[j]);
-        }
-      }
-      if (half == 0) {
-        // entry kS is final: later diagonals reach only indices below it
-        if (kS >= 0 && kS < dl && (wq[0].x != 0.0 || wq[0].y != 0.0)) gacc(tl, bl + kS, wq[0]);
-#pragma unroll
-        for (int j = 0; j < DQ; ++j) wq[j] = j + 1 < DQ ? wq[j + 1] : make_double2(0.0, 0.0);
-      }
+    for (int u = 0; u < kCh; u += 2) {
+      const double2 cc = u < jn ? __ldg(c2 + (j0 + u) / 2) : make_double2(0.0, 0.0);
+      wc[u] = w0 * cc.x;
+      wc[u + 1] = u + 1 < jn ? w0 * cc.y : 0.0;
     }
-    if (half == 0) win_flush<DQ>(tl, bl, dl, it.K - S, wq);
   }
-  flush_pair<DS>(tl, bs, DS, gvs, half);
 }
 
-__device__ __forceinline__ void adj_dispatch(const Tile& tl, const Item& it, const double* __restrict__ coef,
-                                             double w0, double w1, int half, double& e) {
-#define Y3B_ADJ_CASE(B, DS, NC)                         \
-  case ((B - 1) * 7 + (DS - 1) / 2) * 2 + (NC - 1):     \
-    adj_item<B, DS, NC>(tl, it, coef, w0, w1, half, e); \
-    break;
-#define Y3B_ADJ_DS(B, DS) Y3B_ADJ_CASE(B, DS, 1) Y3B_ADJ_CASE(B, DS, 2)
-#define Y3B_ADJ_B(B) \
-  Y3B_ADJ_DS(B, 1) Y3B_ADJ_DS(B, 3) Y3B_ADJ_DS(B, 5) Y3B_ADJ_DS(B, 7) Y3B_ADJ_DS(B, 9) \
-  Y3B_ADJ_DS(B, 11) Y3B_ADJ_DS(B, 13)
-  switch (it.sel) {
-    case 0: adj_b1<1>(tl, it, coef, w0, w1, half, e); break;
-    case 1: adj_b1<2>(tl, it, coef, w0, w1, half, e); break;
-    Y3B_ADJ_B(2)
-    Y3B_ADJ_B(3)
-    Y3B_ADJ_B(4)
-    default: break;
+__device__ __forceinline__ double adj1(const Ctx& c, const Item& it, int nc, const double* __restrict__ coef,
+                                       double w0, double w1, bool mute) {
+  const double* cr = coef + it.coef;
+  const double wc = nc == 2 ? fma(w1, __ldg(cr + 1), w0 * __ldg(cr)) : w0 * __ldg(cr);
+  if (!mute) g_add1(c, it.b0 + it.K, make_double2(wc, 0.0));
+  return wc * vat(c, it.b0 + it.K).x;
+}
+
+// Two blocks (register block s of ds indices, last block l = K - j): one
+// row.  Per chunk, gs is staged at [0, kCh) and gl at [7, 7 + kCh).
+__device__ __forceinline__ double adj2(const Ctx& c, const Item& it, int ds, int nc, const double* __restrict__ coef,
+                                       double w0, double w1, bool mute) {
+  double e = 0.0;
+  const int bs = it.b0, bl = it.b1, K = it.K, dl = it.dl;
+  const double* cr = coef + it.coef;
+#pragma unroll 1
+  for (int j0 = 0; j0 < ds; j0 += kCh) {
+    const int jn = min(kCh, ds - j0);
+    double wc[kCh];
+    wchunk(cr, nc, j0, jn, w0, w1, wc);
+    double2 gs[kCh], gl[kCh];
+#pragma unroll
+    for (int u = 0; u < kCh; ++u) {
+      gs[u] = gl[u] = make_double2(0.0, 0.0);
+      if (u < jn) {
+        // out-of-block last indices read finite neighbours; their coefficient is 0
+        const double2 xs = vat(c, bs + j0 + u), xl = vat(c, bl + K - j0 - u);
+        e += wc[u] * (xs.x * xl.x - xs.y * xl.y);
+        gs[u] = cscale(wc[u], xl);
+        gl[u] = cscale(wc[u], xs);
+      }
+    }
+    if (!mute) {
+      g_add<kCh, 1>(c, bs + j0, 0, jn, gs);
+      // gl[u] belongs to last-block index K - j0 - u
+      g_add<kCh, -1>(c, bl + K - j0, max(0, K - j0 - dl + 1), min(jn, K - j0 + 1), gl);
+    }
   }
-#undef Y3B_ADJ_B
-#undef Y3B_ADJ_DS
-#undef Y3B_ADJ_CASE
+  return e;
+}
+
+// Three blocks: rows i0 (prefix block 0), register block s, last block
+// l = K - i0 - j (dl <= kStage, gl accumulates in the staging area).  The
+// prefix gradient of a row is T_i0, added to G per row and chunk.
+__device__ __forceinline__ double adj3(const Ctx& c, const Item& it, int ds, int nc, const double* __restrict__ coef,
+                                       double w0, double w1, bool mute) {
+  double e = 0.0;
+  const int rw = nc == 2 ? 2 * ds : ((ds + 1) & ~1);
+  const int b0 = it.b0, bs = it.b1, bl = it.b2, K = it.K, dl = it.dl;
+  const int r_lo = max(0, K - (ds - 1) - (dl - 1)), r_hi = min(it.d0 - 1, K);
+  if (r_lo > r_hi) return e;
+  const double* cb = coef + it.coef;
+  stage_zero(c, 0, dl);
+#pragma unroll 1
+  for (int j0 = 0; j0 < ds; j0 += kCh) {
+    const int jn = min(kCh, ds - j0);
+    double2 vs[kCh], gs[kCh];
+#pragma unroll
+    for (int u = 0; u < kCh; ++u) {
+      vs[u] = u < jn ? vat(c, bs + j0 + u) : make_double2(0.0, 0.0);
+      gs[u] = make_double2(0.0, 0.0);
+    }
+    // w[u] belongs to last-block index K - r - j0 - u (moves by one per row)
+    double2 w[kCh];
+#pragma unroll
+    for (int u = 0; u < kCh; ++u) w[u] = make_double2(0.0, 0.0);
+#pragma unroll 1
+    for (int r = r_lo; r <= r_hi; ++r) {
+      double wc[kCh];
+      wchunk(cb + r * rw, nc, j0, jn, w0, w1, wc);
+      const double2 x0 = vat(c, b0 + r);
+      double2 T = make_double2(0.0, 0.0);
+#pragma unroll
+      for (int u = 0; u < kCh; ++u) {
+        // out-of-block last indices read finite neighbours; their coefficient is 0
+        const double2 vl = vat(c, bl + K - r - j0 - u);
+        cmac(T, wc[u], mul(vs[u], vl));
+        const double2 xw = cscale(wc[u], x0);
+        cfma(gs[u], xw, vl);
+        cfma(w[u], xw, vs[u]);
+      }
+      e += x0.x * T.x - x0.y * T.y;
+      if (!mute) g_add1(c, b0 + r, T);
+      const int kf = K - r - j0;
+      if (kf >= 0 && kf < dl) stage_acc(c, kf, w[0]);
+#pragma unroll
+      for (int u = 0; u + 1 < kCh; ++u) w[u] = w[u + 1];
+      w[kCh - 1] = make_double2(0.0, 0.0);
+    }
+#pragma unroll
+    for (int u = 0; u + 1 < kCh; ++u) {
+      const int k = K - r_hi - 1 - j0 - u;
+      if (k >= 0 && k < dl) stage_acc(c, k, w[u]);
+    }
+    if (!mute) g_add<kCh, 1>(c, bs + j0, 0, jn, gs);
+  }
+  if (!mute) stage_flush(c, bl, 0, dl);
+  return e;
+}
+
+// Four blocks: rows (i0, i1) of prefix blocks 0 and 1 (d0 <= d1 <= 7), the
+// register block s and the last block l = K - S - j with S = i0 + i1 (dl <=
+// 14).  Rows of one anti-diagonal S share q_j = vs_j vl_{K-S-j}.  Two passes
+// over the anti-diagonals, each chunk of j in turn:
+//   A: T per row; g0[i0] += x1 T and g1[i1] += x0 T accumulate in the
+//      staging area ([0, 7) and [7, 14));
+//   B: R_j = sum over the diagonal's rows of c_j x0 x1; gs[j] += R_j vl
+//      (registers, per chunk) and gl[K - S - j] += R_j vs_j (staged at [0, dl)).
+__device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int nc, const double* __restrict__ coef,
+                                       double w0, double w1, bool mute) {
+  double e = 0.0;
+  const int rw = nc == 2 ? 2 * ds : ((ds + 1) & ~1);
+  const int b0 = it.b0, b1 = it.b1, bs = it.b2, bl = it.b3;
+  const int d0 = it.d0, d1 = it.d1, dl = it.dl, K = it.K;
+  const int s_lo = max(0, K - (ds - 1) - (dl - 1)), s_hi = min(d0 + d1 - 2, K);
+  if (s_lo > s_hi) return e;
+  const double* cb = coef + it.coef;
+  stage_zero(c, 0, d0);
+  stage_zero(c, 7, 7 + d1);
+#pragma unroll 1
+  for (int j0 = 0; j0 < ds; j0 += kCh) {
+    const int jn = min(kCh, ds - j0);
+    double2 vs[kCh];
+#pragma unroll
+    for (int u = 0; u < kCh; ++u) vs[u] = u < jn ? vat(c, bs + j0 + u) : make_double2(0.0, 0.0);
+#pragma unroll 1
+    for (int S = s_lo; S <= s_hi; ++S) {
+      double2 q[kCh];
+#pragma unroll
+      for (int u = 0; u < kCh; ++u) q[u] = mul(vs[u], vat(c, bl + K - S - j0 - u));
+      const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
+#pragma unroll 1
+      for (int i0 = i0a; i0 <= i0b; ++i0) {
+        const int i1 = S - i0;
+        double wc[kCh];
+        wchunk(cb + (i0 * d1 + i1) * rw, nc, j0, jn, w0, w1, wc);
+        double2 T = make_double2(0.0, 0.0);
+#pragma unroll
+        for (int u = 0; u < kCh; ++u) cmac(T, wc[u], q[u]);
+        const double2 x0 = vat(c, b0 + i0), x1 = vat(c, b1 + i1);
+        const double2 x01 = mul(x0, x1);
+        e += x01.x * T.x - x01.y * T.y;
+        stage_acc(c, i0, mul(x1, T));
+        stage_acc(c, 7 + i1, mul(x0, T));
+      }
+    }
+  }
+  if (!mute) {
+    stage_flush(c, b0, 0, d0);
+    stage_flush_off(c, b1, 7, 0, d1);
+  }
+  stage_zero(c, 0, dl);
+#pragma unroll 1
+  for (int j0 = 0; j0 < ds; j0 += kCh) {
+    const int jn = min(kCh, ds - j0);
+    double2 vs[kCh], gs[kCh];
+#pragma unroll
+    for (int u = 0; u < kCh; ++u) {
+      vs[u] = u < jn ? vat(c, bs + j0 + u) : make_double2(0.0, 0.0);
+      gs[u] = make_double2(0.0, 0.0);
+    }
+    // w[u] belongs to last-block index K - S - j0 - u; after diagonal S no
+    // later one reaches index K - S - j0, which is added to the staging area
+    double2 w[kCh];
+#pragma unroll
+    for (int u = 0; u < kCh; ++u) w[u] = make_double2(0.0, 0.0);
+#pragma unroll 1
+    for (int S = s_lo; S <= s_hi; ++S) {
+      double2 R[kCh];
+#pragma unroll
+      for (int u = 0; u < kCh; ++u) R[u] = make_double2(0.0, 0.0);
+      const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
+#pragma unroll 1
+      for (int i0 = i0a; i0 <= i0b; ++i0) {
+        const int i1 = S - i0;
+        double wc[kCh];
+        wchunk(cb + (i0 * d1 + i1) * rw, nc, j0, jn, w0, w1, wc);
+        const double2 x01 = mul(vat(c, b0 + i0), vat(c, b1 + i1));
+#pragma unroll
+        for (int u = 0; u < kCh; ++u) cmac(R[u], wc[u], x01);
+      }
+#pragma unroll
+      for (int u = 0; u < kCh; ++u) {
+        cfma(gs[u], R[u], vat(c, bl + K - S - j0 - u));
+        cfma(w[u], R[u], vs[u]);
+      }
+      const int kf = K - S - j0;
+      if (kf >= 0 && kf < dl) stage_acc(c, kf, w[0]);
+#pragma unroll
+      for (int u = 0; u + 1 < kCh; ++u) w[u] = w[u + 1];
+      w[kCh - 1] = make_double2(0.0, 0.0);
+    }
+#pragma unroll
+    for (int u = 0; u + 1 < kCh; ++u) {
+      const int k = K - s_hi - 1 - j0 - u;
+      if (k >= 0 && k < dl) stage_acc(c, k, w[u]);
+    }
+    if (!mute) g_add<kCh, 1>(c, bs + j0, 0, jn, gs);
+  }
+  if (!mute) stage_flush(c, bl, 0, dl);
+  return e;
+}
+
+// Any item shape, one tuple at a time with single additions (for shapes the
+// unrolled paths do not cover: wide register blocks, long last blocks).
+__device__ __noinline__ double adj_generic(const Ctx c, const Item it, int B, int DS, int NC,
+                                           const double* __restrict__ coef, double w0, double w1, bool mute) {
+  double e = 0.0;
+  const int RW = NC == 2 ? 2 * DS : ((DS + 1) & ~1);
+  const int n0 = B >= 3 ? it.d0 : 1, n1 = B == 4 ? it.d1 : 1;
+  const int bs = B == 2 ? it.b0 : (B == 3 ? it.b1 : it.b2);
+  const int bl = B == 2 ? it.b1 : (B == 3 ? it.b2 : it.b3);
+  const double2 one = make_double2(1.0, 0.0);
+  for (int i0 = 0; i0 < n0; ++i0) {
+    for (int i1 = 0; i1 < n1; ++i1) {
+      const int row = B == 4 ? i0 * it.d1 + i1 : (B == 3 ? i0 : 0);
+      const double* cr = coef + it.coef + row * RW;
+      const double2 x0 = B >= 3 ? vat(c, it.b0 + i0) : one;
+      const double2 x1 = B == 4 ? vat(c, it.b1 + i1) : one;
+      const double2 p01 = mul(x0, x1);
+      for (int j = 0; j < DS; ++j) {
+        const int k = it.K - i0 - i1 - j;
+        if (k < 0 || k >= it.dl) continue;
+        const double wc = NC == 2 ? fma(w1, __ldg(cr + 2 * j + 1), w0 * __ldg(cr + 2 * j)) : w0 * __ldg(cr + j);
+        if (wc == 0.0) continue;
+        const double2 xs = vat(c, bs + j), xl = vat(c, bl + k);
+        const double2 psl = mul(xs, xl);
+        e += wc * (p01.x * psl.x - p01.y * psl.y);
+        if (mute) continue;
+        if (B >= 3) g_add1(c, it.b0 + i0, cscale(wc, mul(x1, psl)));
+        if (B == 4) g_add1(c, it.b1 + i1, cscale(wc, mul(x0, psl)));
+        g_add1(c, bs + j, cscale(wc, mul(p01, xl)));
+        g_add1(c, bl + k, cscale(wc, mul(p01, xs)));
+      }
+    }
+  }
+  return e;
+}
+
+__device__ __forceinline__ double adj_dispatch(const Ctx& c, const Item& it, const double* __restrict__ coef,
+                                               double w0, double w1, bool mute) {
+  const int nc = (it.sel & 1) + 1, ds = 2 * ((it.sel >> 1) % 7) + 1, B = (it.sel >> 1) / 7 + 1;
+  switch (B) {
+    case 1: return adj1(c, it, nc, coef, w0, w1, mute);
+    case 2: return adj2(c, it, ds, nc, coef, w0, w1, mute);
+    case 3:
+      if (it.dl <= kStage) return adj3(c, it, ds, nc, coef, w0, w1, mute);
+      break;
+    case 4:
+      if (it.d0 <= 7 && it.d1 <= 7 && it.dl <= kStage) return adj4(c, it, ds, nc, coef, w0, w1, mute);
+      break;
+    default: return 0.0;
+  }
+  return adj_generic(c, it, B, ds, nc, coef, w0, w1, mute);
 }
 
 // Symmetric slot: fill values from A.  Threads cover (atom, output) pairs.
@@ -270,61 +478,66 @@ __device__ __forceinline__ void grad_fill_slot(const y3b_ace_tables& t, double2*
   }
 }
 
-// Pull a slot's gradients back to the A entries of its radial channel:
-// d/dx_c of coeff prod_k x_{f_k} is, for each distinct component c (first
-// occurrence p), multiplicity(c) coeff prod_{k != p} x_{f_k}.  Clears the slot.
+// Chain rule from a slot's gradients to the A entries of its radial channel:
+// dE/dx_p += sum over monomials containing p of g_o * m * c * prod(other
+// factors), from the component-major derivative table.  Each thread owns
+// (atom, component) pairs, so the additions need no atomics.
 __device__ __forceinline__ void grad_pull_slot(const y3b_ace_tables& t, const double2* __restrict__ val,
-                                               double2* __restrict__ grad, int W, int slot, int ch) {
+                                               double* __restrict__ Gr, double* __restrict__ Gi, int W, int slot,
+                                               int ch) {
   const int na = int(t.nmax) * W, so = int(t.sym_output_count);
-  const int4* outs = reinterpret_cast<const int4*>(t.sym_outputs);
-  const int atom = threadIdx.x % kGA;
-  for (int o = threadIdx.x / kGA; o < so; o += blockDim.x / kGA) {
-    double2* gslot = grad + (na + slot * so + o) * kGA + atom;
-    const double2 g = *gslot;
-    *gslot = make_double2(0.0, 0.0);
-    if (g.x == 0.0 && g.y == 0.0) continue;
-    const int4 r = __ldg(outs + o);
-    const double2* x = val + (ch * W + r.x) * kGA + atom;
-    double2* gx = grad + (ch * W + r.x) * kGA + atom;
-    for (int q = r.y; q < r.z; ++q) {
-      const uint32_t f = __ldg(t.sym_term_factors + q);
-      const double cq = __ldg(t.sym_term_coeff + q);
-      int fk[4], nf = 0;
+  const int2* gidx = reinterpret_cast<const int2*>(t.sym_grad_index);
+  for (int task = threadIdx.x; task < kGA * W; task += blockDim.x) {
+    const int atom = task % kGA, comp = task / kGA;
+    const double2* x = val + ch * W * kGA + atom;
+    const int gb = (na + slot * so) * kGA + atom;
+    double ar = 0.0, ai = 0.0;
+    const int qe = __ldg(t.sym_grad_offsets + comp + 1);
+    for (int q = __ldg(t.sym_grad_offsets + comp); q < qe; ++q) {
+      const int2 r = __ldg(gidx + q);
+      const double gr = Gr[gb + r.x * kGA], gi = Gi[gb + r.x * kGA];
+      if (gr == 0.0 && gi == 0.0) continue;
+      double2 m = make_double2(__ldg(t.sym_grad_coeff + q), 0.0);
+      const uint32_t f = uint32_t(r.y);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 3; ++k) {
         const int ci = (f >> (8 * k)) & 255;
-        if (ci != 255 && nf == k) fk[nf++] = ci;
+        if (ci != 255) m = mul(m, x[ci * kGA]);
       }
-      for (int p = 0; p < nf; ++p) {
-        if (p > 0 && fk[p] == fk[p - 1]) continue;
-        int mult = 0;
-        double2 prod = make_double2(cq, 0.0);
-        for (int k = 0; k < nf; ++k) {
-          if (fk[k] == fk[p]) ++mult;
-          if (k != p) prod = mul(prod, x[fk[k] * kGA]);
-        }
-        const double2 d = mul(g, cscale(double(mult), prod));
-        atomicAdd(&gx[fk[p] * kGA].x, d.x);
-        atomicAdd(&gx[fk[p] * kGA].y, d.y);
-      }
+      ar += gr * m.x - gi * m.y;
+      ai += gr * m.y + gi * m.x;
     }
+    const int e = (ch * W + comp) * kGA + atom;
+    Gr[e] += ar;
+    Gi[e] += ai;
   }
 }
 
-__global__ void __launch_bounds__(32 * kGWarps) ace_grad_kernel(y3b_ace_tables t, const double2* __restrict__ A,
-                                                                int64_t N, const int32_t* __restrict__ species,
-                                                                const double* __restrict__ weights, int64_t S,
-                                                                double* __restrict__ energy,
-                                                                double2* __restrict__ dEdA) {
+__device__ __forceinline__ void grad_clear_slot(double* __restrict__ Gr, double* __restrict__ Gi, int na, int so,
+                                                int slot) {
+  for (int e = (na + slot * so) * kGA + threadIdx.x; e < (na + (slot + 1) * so) * kGA; e += blockDim.x)
+    Gr[e] = Gi[e] = 0.0;
+}
+
+__global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_tables t, const double2* __restrict__ A,
+                                                                   int64_t N, const int32_t* __restrict__ species,
+                                                                   const double* __restrict__ weights, int64_t S,
+                                                                   double* __restrict__ energy,
+                                                                   double2* __restrict__ dEdA,
+                                                                   int32_t* __restrict__ status) {
   extern __shared__ double2 gsm[];
   __shared__ double red[kGWarps][kGA];
   const int W = int((t.lmax + 1) * (t.lmax + 1));
-  const int na = int(t.nmax) * W;
-  const int rows = int(t.smem_entries) + 2 * kGPad;
-  for (int e = threadIdx.x; e < 2 * rows * kGA; e += blockDim.x) gsm[e] = make_double2(0.0, 0.0);
+  const int na = int(t.nmax) * W, so = int(t.sym_output_count);
+  const int E = int(t.smem_entries);
+  const int rows = E + 2 * kGPad;
+  double* Gr = reinterpret_cast<double*>(gsm + rows * kGA);
+  double* Gi = Gr + E * kGA;
+  double2* stg = reinterpret_cast<double2*>(Gi + E * kGA);
+  for (int e = threadIdx.x; e < rows * kGA; e += blockDim.x) gsm[e] = make_double2(0.0, 0.0);
+  for (int e = threadIdx.x; e < 2 * E * kGA; e += blockDim.x) Gr[e] = 0.0;
   __syncthreads();
   double2* val = gsm + kGPad * kGA;
-  double2* grad = gsm + (rows + kGPad) * kGA;
   {
     const int la = threadIdx.x % kGA;  // loader thread's atom
     const int64_t aa = blockIdx.x * int64_t(kGA) + la;
@@ -332,42 +545,60 @@ __global__ void __launch_bounds__(32 * kGWarps) ace_grad_kernel(y3b_ace_tables t
       val[e * kGA + la] = aa < N ? A[aa * na + e] : make_double2(0.0, 0.0);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int atom = lane & (kGA - 1), half = lane >> 4;
+  const int atom = lane & (kGA - 1), grp = lane / kGA;
   const int64_t a = blockIdx.x * int64_t(kGA) + atom;
-  const bool live = a < N;
-  int z = live ? species[a] : 0;
-  if (z < 0 || z >= S) z = 0;
+  int z = a < N ? species[a] : 0;
+  if (z < 0 || z >= S) {
+    if (status && grp == 0) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+    z = 0;
+  }
   const double* wz = weights + int64_t(z) * t.feature_count;
-  const Tile tl{val + atom, grad + atom};
+  const Ctx c{static_cast<uint32_t>(__cvta_generic_to_shared(val + atom)),
+        static_cast<uint32_t>(__cvta_generic_to_shared(Gr + atom)),
+        static_cast<uint32_t>(__cvta_generic_to_shared(Gi + atom)),
+        static_cast<uint32_t>(__cvta_generic_to_shared(stg + warp * kStage * 32 + lane))};
   const int4* items = reinterpret_cast<const int4*>(t.items);
   const int4* phases = reinterpret_cast<const int4*>(t.phases);
+  const int2* groups = reinterpret_cast<const int2*>(t.groups);
   int cur0 = -2, cur1 = -2;
   double e_acc = 0.0;
+#pragma unroll 1
   for (int ph = 0; ph < t.phase_count; ++ph) {
     const int4 pr = __ldg(phases + ph);
     if (pr.x != cur0 || pr.y != cur1) {
       __syncthreads();  // the previous phase is done with the slots (and A is loaded)
-      if (pr.x != cur0 && cur0 >= 0) grad_pull_slot(t, val, grad, W, 0, cur0);
-      if (pr.y != cur1 && cur1 >= 0) grad_pull_slot(t, val, grad, W, 1, cur1);
+      if (pr.x != cur0 && cur0 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 0, cur0);
+      if (pr.y != cur1 && cur1 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 1, cur1);
       __syncthreads();
-      if (pr.x != cur0) grad_fill_slot(t, val, W, 0, pr.x);
-      if (pr.y != cur1 && pr.y >= 0) grad_fill_slot(t, val, W, 1, pr.y);
+      if (pr.x != cur0) {
+        grad_clear_slot(Gr, Gi, na, so, 0);
+        grad_fill_slot(t, val, W, 0, pr.x);
+      }
+      if (pr.y != cur1) {
+        grad_clear_slot(Gr, Gi, na, so, 1);
+        if (pr.y >= 0) grad_fill_slot(t, val, W, 1, pr.y);
+      }
       __syncthreads();
       cur0 = pr.x;
       cur1 = pr.y;
     }
-    for (int i = pr.z + warp; i < pr.w; i += kGWarps) {
-      const Item it = load_item(items, i);
-      const double w0 = __ldg(wz + it.f0);
-      const double w1 = it.f1 >= 0 ? __ldg(wz + it.f1) : 0.0;
-      adj_dispatch(tl, it, t.item_coef, w0, w1, half, e_acc);
+    const int ge = __ldg(t.group_offsets + ph + 1);
+#pragma unroll 1
+    for (int g = __ldg(t.group_offsets + ph) + warp; g < ge; g += kGWarps) {
+      const int2 ig = __ldg(groups + g);
+      const int mine = grp == 0 ? ig.x : ig.y;
+      const bool mute = mine < 0;  // odd item out: the second half runs the first item unweighted, adding nothing
+      const Item it = load_item(items, mute ? ig.x : mine);
+      const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
+      const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
+      e_acc += adj_dispatch(c, it, t.item_coef, w0, w1, mute);
     }
   }
   __syncthreads();
-  if (cur0 >= 0) grad_pull_slot(t, val, grad, W, 0, cur0);
-  if (cur1 >= 0) grad_pull_slot(t, val, grad, W, 1, cur1);
+  if (cur0 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 0, cur0);
+  if (cur1 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 1, cur1);
   e_acc += __shfl_xor_sync(0xffffffffu, e_acc, 16);
-  if (half == 0) red[warp][atom] = e_acc;
+  if (grp == 0) red[warp][atom] = e_acc;
   __syncthreads();
   if (threadIdx.x < kGA) {
     const int64_t aa = blockIdx.x * int64_t(kGA) + threadIdx.x;
@@ -379,7 +610,7 @@ __global__ void __launch_bounds__(32 * kGWarps) ace_grad_kernel(y3b_ace_tables t
     const int la = threadIdx.x % kGA;
     const int64_t aa = blockIdx.x * int64_t(kGA) + la;
     for (int e = threadIdx.x / kGA; e < na; e += blockDim.x / kGA)
-      if (aa < N) dEdA[aa * na + e] = grad[e * kGA + la];
+      if (aa < N) dEdA[aa * na + e] = make_double2(Gr[e * kGA + la], Gi[e * kGA + la]);
   }
 }
 
@@ -554,6 +785,9 @@ int check_grad_tables(const y3b_ace_tables* t) {
   Y3B_CHECK_ARG(t->nmax >= 1 && t->nmax <= 16 && t->lmax >= 0 && t->lmax <= 6, "bad nmax / lmax");
   Y3B_CHECK_ARG(t->item_count >= 0 && t->phase_count >= 1, "bad table sizes");
   Y3B_CHECK_ARG(t->item_count == 0 || (t->items && t->item_coef && t->phases), "null item tables");
+  Y3B_CHECK_ARG(t->group_offsets && (t->group_count == 0 || t->groups), "null adjoint item groups");
+  Y3B_CHECK_ARG(t->sym_grad_offsets && (t->sym_grad_count == 0 || (t->sym_grad_index && t->sym_grad_coeff)),
+                "null symmetric derivative tables");
   return Y3B_OK;
 }
 
@@ -564,20 +798,22 @@ using namespace y3b;
 
 extern "C" int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
                                    const int32_t* species, const double* weights, int64_t species_count,
-                                   double* energy, void* dEdA, void* stream) {
+                                   double* energy, void* dEdA, int32_t* status, void* stream) {
   if (int rc = check_grad_tables(tables)) return rc;
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && weights && energy && dEdA && species_count > 0, "null pointer argument");
-  const size_t smem = size_t(2) * size_t(tables->smem_entries + 2 * kGPad) * kGA * sizeof(double2);
-  Y3B_CHECK_ARG(smem <= 200 * 1024, "bundle needs %lld bytes of shared memory for the adjoint (max 200 KB)",
+  const size_t smem = size_t(tables->smem_entries + 2 * kGPad) * kGA * sizeof(double2) +
+                      size_t(2) * size_t(tables->smem_entries) * kGA * sizeof(double) +
+                      size_t(kGWarps) * kStage * 32 * sizeof(double2);
+  Y3B_CHECK_ARG(smem <= 224 * 1024, "bundle needs %lld bytes of shared memory for the adjoint (max 224 KB)",
                 (long long)smem);
   Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   const int64_t grid = (atom_count + kGA - 1) / kGA;
   Y3B_CHECK_ARG(grid < (int64_t(1) << 31), "too many atoms");
   ace_grad_kernel<<<int(grid), 32 * kGWarps, smem, as_stream(stream)>>>(
       *tables, static_cast<const double2*>(A), atom_count, species, weights, species_count, energy,
-      static_cast<double2*>(dEdA));
+      static_cast<double2*>(dEdA), status);
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }

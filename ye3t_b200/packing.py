@@ -58,7 +58,10 @@ class PackedBundle:
         t.item_count = int(a["items"].shape[0])
         t.phase_count = int(a["phases"].shape[0])
         t.sym_output_count = int(a["sym_outputs"].shape[0])
-        for name in ("items", "item_coef", "phases", "sym_outputs", "sym_term_factors", "sym_term_coeff"):
+        t.group_count = int(a["groups"].shape[0])
+        t.sym_grad_count = int(a["sym_grad_coeff"].shape[0])
+        for name in ("items", "item_coef", "phases", "sym_outputs", "sym_term_factors", "sym_term_coeff", "groups",
+                     "group_offsets", "sym_grad_offsets", "sym_grad_index", "sym_grad_coeff"):
             setattr(t, name, ctypes.c_void_p(a[name].data_ptr()))
         return t
 
@@ -84,327 +87,6 @@ class PackedBundle:
             self.item_grad_flops = item_grad_flops_per_atom(items)
         return {"items": self.item_flops, "items_grad": self.item_grad_flops, "terms": sched,
                 "sym": float(self.sym_flops_per_atom)}
-
-
-def item_grad_flops_per_atom(items: np.ndarray) -> float:
-    """FP64 flops per atom of the energy-and-gradient walk (valid tuples only).
-
-    Mirrors ace_grad.cu: per valid slot of a row the weighted coefficient
-    (2 nc - 1), the product q (6), T += c q (4), x c (2), gvs += (x c) vl (8)
-    and the last-block gradient (x c) vs (8); per row the energy (4) and the
-    prefix gradients (8 or 14).  4-block items with a register block <= 7
-    share q per anti-diagonal: per valid j there q (6), gvs (8) and the
-    last-block gradient (8); per prefix x0 x1 (6), per j the weighted
-    coefficient and the T and R multiply-adds (2 nc - 1 + 8), the energy (4)
-    and two gradients (6 + 8).
-    """
-    flops = 0.0
-    cache = {}
-    for row in items:
-        key = tuple(int(v) for v in row[:5])
-        if key not in cache:
-            sel, D0, D1, Dl, K = key
-            nc = sel % 2 + 1
-            B = (sel // 2) // 7 + 1
-            ds = 2 * ((sel // 2) % 7) + 1
-            wc = 2 * nc - 1
-            smin, smax = K - (ds - 1) - (Dl - 1), K
-
-            def valid(S):
-                return sum(1 for j in range(ds) if 0 <= K - S - j < Dl)
-            f = 0.0
-            if B == 1:
-                f = 4.0 * nc
-            elif B == 2:
-                f = valid(0) * (wc + 28.0) + 2.0
-            elif B == 3:
-                for i0 in range(D0):
-                    if smin <= i0 <= smax:
-                        f += valid(i0) * (wc + 28.0) + 4.0
-            elif ds <= 7:
-                for S in range(max(0, smin), min(D0 - 1 + D1 - 1, smax) + 1):
-                    v = valid(S)
-                    rows = sum(1 for i0 in range(D0) if 0 <= S - i0 < D1)
-                    f += 22.0 * v + rows * (6.0 + ds * (wc + 8.0) + 18.0)
-            else:
-                for i0 in range(D0):
-                    for i1 in range(D1):
-                        S = i0 + i1
-                        if smin <= S <= smax:
-                            f += valid(S) * (wc + 28.0) + 6.0 + 4.0 + 14.0
-            cache[key] = f
-        flops += cache[key]
-    return flops
-
-
-def _factors(row):
-    out = []
-    for comp, cnt in enumerate(row):
-        out.extend([comp] * int(cnt))
-    if len(out) > 4:
-        raise ValueError("symmetric block degree above 4 is not supported by the fused kernel")
-    packed = 0
-    for k in range(4):
-        v = out[k] if k < len(out) else 255
-        packed |= int(v) << (8 * k)
-    return packed
-
-
-# ---------------------------------------------------------------------------
-# Evaluation items for the B-basis kernel.
-#
-# Within a pattern, components whose labels bind identical blocks and that
-# share the same M form a group; the group's coefficients are laid out as a
-# dense table over the magnetic index box of blocks 0..B-2 (the last block's
-# index follows from M: i_last = K - sum_{b < B-1} i_b with
-# K = M + sum_b L_b).  Blocks 0..B-3 are walked by runtime loops, block B-2
-# by a loop unrolled at compile time (its values stay in registers), and the
-# last block is read once per tuple.  A pass covers at most ITEM_MAX_NC
-# components of a group; every word contributes one item per pass.
-# ---------------------------------------------------------------------------
-ITEM_MAX_NC = 2
-ITEM_INTS = 16
-MAX_STATIC_DIM = 13
-
-
-def item_selector(B: int, ds: int, nc: int) -> int:
-    """Kernel dispatch code of an item (mirrors ace.cu)."""
-    return ((B - 1) * 7 + (ds - 1) // 2) * 2 + (nc - 1)
-
-
-def _pattern_groups(p):
-    """[(spec, M, [components])] in first-component order."""
-    order, groups = [], {}
-    for c in range(p.component_count):
-        key = (p.block_specs[int(p.component_label_index[c])], int(p.component_M_R[c]))
-        if key not in groups:
-            groups[key] = []
-            order.append(key)
-        groups[key].append(c)
-    return [(k[0], k[1], groups[k]) for k in order]
-
-
-def _row_width(ds: int, nc: int) -> int:
-    """Doubles per coefficient row (one prefix): nc per j, padded to even."""
-    return 2 * ds if nc == 2 else (ds + 1) & ~1
-
-
-def _block_order(spec):
-    """Evaluation order of a group's blocks: ascending magnetic dimension
-    (stable), so the two largest become the register-held and the implied
-    last block and the short ones run as the outer loops."""
-    dims = [2 * (s[4] if s[0] == "sym" else s[2]) + 1 for s in spec]
-    return sorted(range(len(spec)), key=lambda b: dims[b])
-
-
-def _group_pass_table(p, rc, spec, M, comps):
-    """Coefficient table of one pass: rows (one per prefix of blocks 0..B-3) of
-    ``_row_width`` doubles holding ``C[prefix, j, c]`` at ``j * nc + c``.
-
-    ``spec`` is the group's block list already in evaluation order; term
-    indices are permuted to it with ``order`` (original block of each slot)."""
-    order = _block_order(spec)
-    spec = [spec[b] for b in order]
-    B = len(spec)
-    lam = [s[4] if s[0] == "sym" else s[2] for s in spec]
-    dims = [2 * L + 1 for L in lam]
-    K = M + sum(lam)
-    nc = len(comps)
-    if B == 1:
-        table = np.zeros((1, nc), dtype=np.float64)
-    else:
-        prefix_box = dims[:-2]
-        ds = dims[-2]
-        rows = int(np.prod(prefix_box)) if prefix_box else 1
-        table = np.zeros((rows, _row_width(ds, nc)), dtype=np.float64)
-    for k, c in enumerate(comps):
-        for q in range(int(p.component_offsets[c]), int(p.component_offsets[c + 1])):
-            idx = [int(p.block_m_tuples[q, order[b]]) + lam[b] for b in range(B)]
-            if idx[-1] != K - sum(idx[:-1]):
-                raise ValueError("term violates magnetic conservation")
-            if B == 1:
-                table[0, k] += float(rc[q])
-            else:
-                row = int(np.ravel_multi_index(tuple(idx[:-2]), dims[:-2])) if B > 2 else 0
-                table[row, idx[-2] * nc + k] += float(rc[q])
-    return dims, K, table, tuple(spec)
-
-
-def _phase_pairs(nmax):
-    """Channel pairs (slot 0, slot 1) visited by the kernel, in order."""
-    if nmax == 1:
-        return [(0, -1)]
-    return [(a, b) for a in range(nmax) for b in range(a + 1, nmax)]
-
-
-def _word_phase(sym_channels, nmax):
-    """Phase pair holding every radial channel that a word's symmetric blocks read."""
-    S = sorted(sym_channels)
-    if nmax == 1:
-        return (0, -1)
-    if len(S) == 2:
-        return (S[0], S[1])
-    if len(S) == 1:
-        a = S[0]
-        return (a, a + 1) if a + 1 < nmax else (a - 1, a)
-    return None
-
-
-def _build_items(bundle, sym_local, sym_out_count, W):
-    """Items grouped by phase, the coefficient array and the phase table.
-
-    Shared-memory entries of a CTA: A channels ``(n-1) W + l^2 + (m + l)``,
-    then two slots of ``sym_out_count`` symmetric outputs, each slot holding
-    every symmetric block of one radial channel (``sym_local`` gives a
-    block's first output inside a slot).
-    """
-    nmax = bundle.nmax
-    coef_chunks, coef_len = [], 0
-    pattern_passes = []
-    for p in bundle.patterns:
-        rc = p.real_coeffs()
-        if rc is None:
-            raise ValueError("fused kernel needs real schedule coefficients")
-        passes = []
-        for spec, M, comps in _pattern_groups(p):
-            for s0 in range(0, len(comps), ITEM_MAX_NC):
-                chunk = comps[s0:s0 + ITEM_MAX_NC]
-                dims, K, table, spec_eval = _group_pass_table(p, rc, spec, M, chunk)
-                if len(dims) > 4:
-                    raise ValueError("fused kernel supports at most 4 blocks per word")
-                if len(dims) >= 2 and dims[-2] > MAX_STATIC_DIM:
-                    raise ValueError("block magnetic dimension above 13 is not supported")
-                passes.append((dims, K, coef_len, chunk, spec_eval))
-                flat = table.reshape(-1)
-                if flat.size % 2:
-                    flat = np.concatenate([flat, [0.0]])
-                coef_chunks.append(flat)
-                coef_len += flat.size
-        pattern_passes.append(passes)
-    pairs = _phase_pairs(nmax)
-    phase_of = {pr: i for i, pr in enumerate(pairs)}
-    phase_items = [[] for _ in pairs]
-    phase_work = [0.0] * len(pairs)
-    free_words = []
-    fo = 0
-    A_entries = nmax * W
-    for w in range(bundle.word_count):
-        pi = int(bundle.word_pattern_index[w])
-        p = bundle.patterns[pi]
-        n_map = {r: int(bundle.word_n_map[w, r]) for r in range(1, bundle.word_n_map.shape[1])
-                 if bundle.word_n_map[w, r] > 0}
-        sym_ch = {n_map[s[1]] - 1 for label in p.block_specs for s in label if s[0] == "sym"}
-        pair = _word_phase(sym_ch, nmax)
-        rows = []
-        work = 0.0
-        for dims, K, coff, chunk, spec in pattern_passes[pi]:
-            B = len(dims)
-            row = [0] * ITEM_INTS
-            ds = dims[-2] if B >= 2 else 1
-            row[0] = item_selector(B, ds, len(chunk))
-            row[1] = dims[0] if B >= 3 else 1
-            row[2] = dims[1] if B >= 4 else 1
-            row[3] = dims[-1]
-            row[4] = K
-            row[5] = coff
-            row[6] = fo + chunk[0]
-            row[7] = fo + chunk[1] if len(chunk) > 1 else -1
-            for b, (kind, n, l, k, Lam, mu) in enumerate(spec):
-                n = n_map[n]
-                if kind == "sym":
-                    row[8 + b] = -1 - (n - 1)  # resolved once the phase is known
-                    row[12 + b] = sym_local[(l, k, Lam, mu)]
-                else:
-                    row[8 + b] = (n - 1) * W + l * l
-            rows.append(row)
-            work += float(np.prod(dims[:-1])) if B > 1 else 1.0
-        fo += p.component_count
-        if pair is None:
-            free_words.append((work, rows))
-        else:
-            phase_items[phase_of[pair]].append(rows)
-            phase_work[phase_of[pair]] += work
-    # words without symmetric blocks balance the phases (largest first)
-    for work, rows in sorted(free_words, key=lambda x: -x[0]):
-        i = int(np.argmin(phase_work))
-        phase_items[i].append(rows)
-        phase_work[i] += work
-    items, phases = [], []
-    for i, (a, b2) in enumerate(pairs):
-        begin = len(items)
-        # items sharing a coefficient table run next to each other, so the
-        # CTA's warps (which take items round robin) read it from L1 together
-        flat = sorted((row for rows in phase_items[i] for row in rows), key=lambda r: (r[5], r[6]))
-        for rows in [flat]:
-            for row in rows:
-                row = list(row)
-                for blk in range(4):
-                    if row[8 + blk] < 0:
-                        ch = -1 - row[8 + blk]
-                        slot = 0 if ch == a else 1
-                        if (slot == 1 and ch != b2) or (slot == 0 and ch != a):
-                            raise AssertionError("word scheduled in a phase without its channels")
-                        row[8 + blk] = A_entries + slot * sym_out_count + row[12 + blk]
-                    row[12 + blk] = 0
-                items.append(row)
-        phases.append([a, b2, begin, len(items)])
-    coef = np.concatenate(coef_chunks) if coef_chunks else np.zeros(0)
-    return (np.asarray(items, dtype=np.int32).reshape(-1, ITEM_INTS), coef,
-            np.asarray(phases, dtype=np.int32).reshape(-1, 4))
-
-
-def item_flops_per_atom(items: np.ndarray) -> float:
-    """FP64 flops per atom the item walk needs (valid tuples only).
-
-    Complex multiply = 6 flops, real x complex multiply-add = 4, complex
-    multiply-add = 8.  Per item shape (nc components, dims, K):
-
-    * B = 1: 4 nc;
-    * B = 2: per valid tuple 6 + 4 nc;
-    * B = 3: per valid tuple 6 + 4 nc, per prefix row 8 nc;
-    * B = 4 (register block <= 7): per index sum S one complex multiply per
-      valid j (q_j), per prefix row 4 nc per valid j plus 6 + 8 nc;
-    * B = 4 (register block > 7): as B = 3 plus 8 nc per outer index.
-    """
-    flops = 0.0
-    cache = {}
-    for row in items:
-        key = tuple(int(v) for v in row[:5])
-        if key not in cache:
-            sel, D0, D1, Dl, K = key
-            nc = sel % 2 + 1
-            B = (sel // 2) // 7 + 1
-            ds = 2 * ((sel // 2) % 7) + 1
-            f = 0.0
-            smin, smax = K - (ds - 1) - (Dl - 1), K
-
-            def valid(S):
-                return sum(1 for j in range(ds) if 0 <= K - S - j < Dl)
-            if B == 1:
-                f = 4.0 * nc
-            elif B == 2:
-                f = valid(0) * (6.0 + 4.0 * nc)
-            elif B == 3:
-                for i0 in range(D0):
-                    if smin <= i0 <= smax:
-                        f += valid(i0) * (6.0 + 4.0 * nc) + 8.0 * nc
-            elif ds <= 7:
-                for S in range(max(0, smin), min(D0 - 1 + D1 - 1, smax) + 1):
-                    v = valid(S)
-                    rows = sum(1 for i0 in range(D0) if 0 <= S - i0 < D1)
-                    f += 6.0 * v + rows * (4.0 * nc * v + 6.0 + 8.0 * nc)
-            else:
-                outer = set()
-                for i0 in range(D0):
-                    for i1 in range(D1):
-                        S = i0 + i1
-                        if smin <= S <= smax:
-                            f += valid(S) * (6.0 + 4.0 * nc) + 8.0 * nc
-                            outer.add(i0)
-                f += 8.0 * nc * len(outer)
-            cache[key] = f
-        flops += cache[key]
-    return flops
 
 
 def item_grad_flops_per_atom(items: np.ndarray) -> float:
@@ -716,6 +398,64 @@ def item_flops_per_atom(items: np.ndarray) -> float:
     return flops
 
 
+GRAD_GROUP = 2
+
+
+def _grad_groups(items: np.ndarray, phases: np.ndarray):
+    """Item pairs of the adjoint kernel, per phase.
+
+    Each half-warp runs one item; pairing two items of one shape (dispatch
+    code, loop extents, K) keeps the warp's control flow identical.  Within a
+    shape, items sharing a coefficient table stay adjacent.  Returns
+    ``groups [P, 2]`` (-1 for a shape's odd item out) and
+    ``group_offsets [phase_count + 1]``.
+    """
+    groups, offsets = [], [0]
+    for _, _, begin, end in phases.tolist():
+        shapes = {}
+        for i in range(begin, end):
+            shapes.setdefault(tuple(int(v) for v in items[i, :5]), []).append(i)
+        for key in sorted(shapes):
+            idx = sorted(shapes[key], key=lambda i: (int(items[i, 5]), int(items[i, 6])))
+            for u in range(0, len(idx), GRAD_GROUP):
+                g = idx[u:u + GRAD_GROUP]
+                groups.append(g + [-1] * (GRAD_GROUP - len(g)))
+        offsets.append(len(groups))
+    return (np.asarray(groups, dtype=np.int32).reshape(-1, GRAD_GROUP), np.asarray(offsets, dtype=np.int32))
+
+
+def _sym_grad_terms(sym_out_rows, s_fac, s_co, W):
+    """Component-major derivative table of the symmetric outputs.
+
+    For a monomial ``c prod_k x_{f_k}`` of output ``o`` and each distinct
+    component ``p`` among its factors (multiplicity ``m``), the derivative
+    ``m c prod_{k != one p} x_{f_k}`` is listed under ``p`` (the component's
+    index inside its radial channel, ``l^2 + m + l``).  Returns offsets
+    ``[W + 1]``, ``index [T, 2]`` (output, 4 x u8 remaining factors with
+    255 unused) and ``coeff [T]``.
+    """
+    per = [[] for _ in range(W)]
+    for o, (base, tb, te, _) in enumerate(sym_out_rows):
+        for q in range(tb, te):
+            comps = [base + ci for ci in s_fac[q] if ci != 255]
+            for p in sorted(set(comps)):
+                rest = list(comps)
+                rest.remove(p)
+                packed = 0
+                for k in range(4):
+                    packed |= (rest[k] if k < len(rest) else 255) << (8 * k)
+                per[p].append((o, packed, comps.count(p) * s_co[q]))
+    offsets = np.zeros(W + 1, dtype=np.int32)
+    index, coeff = [], []
+    for p in range(W):
+        for o, packed, c in per[p]:
+            index.append((o, np.uint32(packed).view(np.int32)))
+            coeff.append(c)
+        offsets[p + 1] = len(index)
+    return (offsets, np.asarray(index, dtype=np.int32).reshape(-1, 2),
+            np.asarray(coeff, dtype=np.float64))
+
+
 def pack_bundle(bundle: ACEBundle, device) -> PackedBundle:
     device = torch.device(device)
     nmax, lmax = bundle.nmax, bundle.lmax
@@ -750,7 +490,15 @@ def pack_bundle(bundle: ACEBundle, device) -> PackedBundle:
         fo += p.component_count
         terms_per_atom += p.term_count
         term_blocks_per_atom += p.term_count * p.block_count
+    groups, group_offsets = _grad_groups(items, phases)
+    unpacked = [[(f >> (8 * k)) & 255 for k in range(4)] for f in np.asarray(s_fac, dtype=np.uint32).tolist()]
+    sg_off, sg_index, sg_coeff = _sym_grad_terms(sym_out_rows, unpacked, s_co, W)
     arrays_np = {
+        "groups": groups,
+        "group_offsets": group_offsets,
+        "sym_grad_offsets": sg_off,
+        "sym_grad_index": sg_index,
+        "sym_grad_coeff": sg_coeff,
         "items": items,
         "item_coef": item_coef,
         "phases": phases,
