@@ -46,7 +46,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--atoms", type=int, default=1 << 20)
     ap.add_argument("--bundle", default=BUNDLE)
-    ap.add_argument("--cpu-sample", type=int, default=1024)
+    ap.add_argument("--cpu-sample", type=int, default=None,
+                    help="atoms in the CPU baseline sample (default 256 with forces, 1024 energy only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--energy-only", action="store_true",
                     help="time the energy step alone (no adjoint, no forces)")
@@ -136,7 +137,7 @@ def measure_fp64_peak(torch, nat, device):
     return best
 
 
-def cpu_baseline(sample_atoms, bundle_stem):
+def cpu_baseline(sample_atoms, bundle_stem, forces=True):
     """The reference CPU path restated (oracle) on a bounded sample, all host cores."""
     import numpy as np
 
@@ -151,16 +152,23 @@ def cpu_baseline(sample_atoms, bundle_stem):
     sp = rng.integers(0, SPECIES, M).astype(np.int32)
     w = np.random.default_rng(2).normal(size=(SPECIES, 41168 if bundle_stem == BUNDLE else b.feature_count))
     t0 = time.perf_counter()
-    off, nbr, disp = oracle.neighbor_list(pos, box, CUTOFF)
-    A = oracle.ace_density(disp, off, nbr, sp, np.asarray(PREFACTOR), b.nmax, b.lmax, CUTOFF, LAMBDA)
-    e = oracle.bundle_energy(b, A, sp, w, threads=cores)
+    if forces:
+        e, F = oracle.energy_forces(b, pos, box, sp, np.asarray(PREFACTOR), w, CUTOFF, LAMBDA, threads=cores)
+        assert np.isfinite(e) and np.isfinite(F).all()
+        what = ("then per word the reference block assembly (workflows.py:636-661), schedule evaluation "
+                "(factorized_runtime.cpp:252-287 restated) and its adjoint (autograd of couplings.py:552-567), the "
+                "symmetric-power adjoint, per-edge gradients and the force scatter")
+    else:
+        off, nbr, disp = oracle.neighbor_list(pos, box, CUTOFF)
+        A = oracle.ace_density(disp, off, nbr, sp, np.asarray(PREFACTOR), b.nmax, b.lmax, CUTOFF, LAMBDA)
+        e = oracle.bundle_energy(b, A, sp, w, threads=cores)
+        assert np.isfinite(e).all()
+        what = ("then per word the reference block assembly (workflows.py:636-661) and schedule evaluation "
+                "(factorized_runtime.cpp:252-287 restated)")
     dt = time.perf_counter() - t0
-    assert np.isfinite(e).all()
     return {"value": M / dt, "unit": "atoms/s", "cores": cores, "kind": "port",
             "sample": f"{M} atoms of the same density/species/cutoff in a {box:.1f} A periodic box; brute-force "
-                      f"neighbour list, A-basis, then per word the reference block assembly (workflows.py:636-661) "
-                      f"and schedule evaluation (factorized_runtime.cpp:252-287 restated, {cores} threads); "
-                      f"{dt:.1f} s"}
+                      f"neighbour list, A-basis, {what} ({cores} threads); {dt:.1f} s"}
 
 
 def run_reference(args):
@@ -171,7 +179,7 @@ def run_reference(args):
     base = None
     times = []
     for i in range(W + K):
-        cb = cpu_baseline(args.cpu_sample, args.bundle)
+        cb = cpu_baseline(args.cpu_sample, args.bundle, forces=not args.energy_only)
         if i >= W:
             times.append(cb)
         base = cb
@@ -338,7 +346,7 @@ def run_b200(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.cpu_sample, args.bundle)
+        cpu = cpu_baseline(args.cpu_sample, args.bundle, forces=not args.energy_only)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -380,6 +388,8 @@ def run_b200(args):
 
 def main():
     args = parse()
+    if args.cpu_sample is None:
+        args.cpu_sample = 1024 if args.energy_only else 256
     if args.impl == "reference":
         run_reference(args)
     else:

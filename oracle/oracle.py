@@ -248,3 +248,100 @@ def bundle_energy(bundle, A, species, weights, threads=1):
     B = bundle_features(bundle, A, threads=threads)
     W = np.asarray(weights)[np.asarray(species)]
     return (W * B.real).sum(axis=1)
+
+
+# -- force path ----------------------------------------------------------------
+def schedule_adjoint(block_values, record, gout, threads=1):
+    """Holomorphic ``dL/dbv`` of the schedule evaluation given ``gout = dL/dout`` (complex128)."""
+    bv = _c(block_values, np.complex128)
+    go = _c(gout, np.complex128)
+    batch, basis, blocks, mdim = bv.shape
+    gbv = np.zeros_like(bv)
+    off = _c(record.component_offsets, np.int64)
+    lab = _c(record.component_label_index, np.int64)
+    mi = _c(record.block_m_indices(), np.int64)
+    co = _c(record.coeffs, np.complex128)
+    lib().yo_factorized_schedule_adjoint(_p(bv), I64(batch), I64(basis), I64(blocks), I64(mdim), _p(off), _p(lab),
+                                         _p(mi), _p(co), I64(go.shape[1]), _p(go), _p(gbv), ctypes.c_int(threads))
+    return gbv
+
+
+def symmetric_power_monomial_adjoint(x, monomial_counts, output_offsets, monomial_values, gout):
+    """Holomorphic ``dL/dx`` of :func:`symmetric_power_monomial` given ``gout = dL/dout``."""
+    xc = _c(x, np.complex128)
+    cnt = _c(monomial_counts, np.int64)
+    off = _c(output_offsets, np.int64)
+    val = _c(monomial_values, np.complex128)
+    go = _c(gout, np.complex128)
+    gx = np.zeros_like(xc)
+    lib().yo_symmetric_power_monomial_adjoint(_p(xc), I64(xc.shape[0]), I64(xc.shape[1]), _p(cnt), _p(off),
+                                              _p(val), I64(go.shape[1]), _p(go), _p(gx))
+    return gx
+
+
+def bundle_energy_grad(bundle, A, species, weights, threads=1):
+    """Per-atom energies and the holomorphic ``G = dE/dA`` (E = sum_i w[z_i] . Re(B_i))."""
+    A = _c(A, np.complex128)
+    N = A.shape[0]
+    W = np.asarray(weights, dtype=np.float64)[np.asarray(species)]
+    sym = sym_block_values(bundle, A)
+    G = np.zeros_like(A)
+    gsym = {}
+    e = np.zeros(N)
+    fo = 0
+    for w in range(bundle.word_count):
+        rec, bv = bundle_word_block_values(bundle, w, A, sym)
+        out = schedule_evaluate_record(bv, rec, threads=threads)
+        C = out.shape[1]
+        wf = W[:, fo:fo + C]
+        e += (wf * out.real).sum(axis=1)
+        gbv = schedule_adjoint(bv, rec, wf.astype(np.complex128), threads=threads)
+        for a, label in enumerate(rec.block_specs):
+            for b, (kind, n, l, k, Lam, mu) in enumerate(label):
+                if kind == "sym":
+                    key = (n, l, k, Lam, mu)
+                    g = gbv[:, a, b, :2 * Lam + 1]
+                    gsym[key] = gsym[key] + g if key in gsym else g.copy()
+                else:
+                    G[:, n - 1, l * l:(l + 1) * (l + 1)] += gbv[:, a, b, :2 * l + 1]
+        fo += C
+    for (n, l, k, Lam, mu), g in gsym.items():
+        t = bundle.sym_tables[(l, k, Lam, mu)]
+        G[:, n - 1, l * l:(l + 1) * (l + 1)] += symmetric_power_monomial_adjoint(
+            A[:, n - 1, l * l:(l + 1) * (l + 1)], t.monomial_counts, t.output_offsets,
+            t.monomial_value.astype(np.complex128), g)
+    return e, G
+
+
+def ace_edge_grad(disp, row_off, nbr, species, prefactor, nmax, lmax, cutoff, lam, G):
+    """``g_e = dE_i/dd_e`` [E, 3] for the CSR rows, from ``G = dE/dA``."""
+    disp = _c(disp, np.float64)
+    off = _c(row_off, np.int64)
+    nb = _c(nbr, np.int32)
+    sp = _c(species, np.int32)
+    pf = _c(prefactor, np.float64)
+    Gc = _c(G, np.complex128)
+    g = np.zeros((nb.shape[0], 3))
+    lib().yo_ace_edge_grad(_p(disp), _p(off), _p(nb), _p(sp), _p(pf), I64(off.shape[0] - 1), I64(nmax), I64(lmax),
+                           ctypes.c_double(cutoff), ctypes.c_double(lam), _p(Gc), _p(g))
+    return g
+
+
+def forces_from_edges(row_off, nbr, g):
+    """``F = -dE/dr`` from per-edge gradients of a full (all-centre) CSR list."""
+    off = _c(row_off, np.int64)
+    nb = _c(nbr, np.int32)
+    gg = _c(g, np.float64)
+    N = off.shape[0] - 1
+    F = np.zeros((N, 3))
+    lib().yo_forces_from_edges(_p(off), _p(nb), I64(N), _p(gg), _p(F))
+    return F
+
+
+def energy_forces(bundle, positions, box, species, prefactor, weights, cutoff, lam, threads=1):
+    """Total energy and forces of a periodic system (brute-force neighbour list)."""
+    off, nbr, disp = neighbor_list(positions, box, cutoff)
+    A = ace_density(disp, off, nbr, species, prefactor, bundle.nmax, bundle.lmax, cutoff, lam)
+    e, G = bundle_energy_grad(bundle, A, species, weights, threads=threads)
+    g = ace_edge_grad(disp, off, nbr, species, prefactor, bundle.nmax, bundle.lmax, cutoff, lam, G)
+    return float(e.sum()), forces_from_edges(off, nbr, g)

@@ -448,4 +448,120 @@ void yo_ace_density(const double* disp, const i64* row_off, const int* nbr, cons
   }
 }
 
+// ---------------------------------------------------------------------------
+// Force path (complex128 only).  The reference obtains these by torch
+// autograd: through the gather-and-product schedule evaluator
+// (ye3t/core/couplings.py:552-567), the symmetric-power contraction
+// (ye3t/runtime/execution_plan.py:11998) and the edge products
+// (plain_site_basis_product, :7582; density_accumulate, :7913).  All
+// gradients are holomorphic: for a real loss L of complex z, G = dL/dz with
+// dL = Re(sum G dz).
+// ---------------------------------------------------------------------------
+
+// gbv[b, label[c], j, m_idx[t, j]] += gout[b, c] coeff[t] prod_{j' != j} bv[b, label[c], j', m_idx[t, j']]
+void yo_factorized_schedule_adjoint(const void* bv_in, i64 batch, i64 basis, i64 blocks, i64 mdim,
+                                    const i64* off, const i64* labels, const i64* midx, const void* coeffs_in,
+                                    i64 comps, const void* gout_in, void* gbv_out, int threads) {
+  const c128* bv = static_cast<const c128*>(bv_in);
+  const c128* coeffs = static_cast<const c128*>(coeffs_in);
+  const c128* gout = static_cast<const c128*>(gout_in);
+  c128* gbv = static_cast<c128*>(gbv_out);
+  parallel_chunks(batch, threads, [&](i64 lo, i64 hi) {
+    std::vector<c128> f(blocks);
+    for (i64 b = lo; b < hi; ++b) {
+      for (i64 c = 0; c < comps; ++c) {
+        const c128 g = gout[b * comps + c];
+        if (g == c128(0, 0)) continue;
+        const c128* row = bv + (b * basis + labels[c]) * blocks * mdim;
+        c128* grow = gbv + (b * basis + labels[c]) * blocks * mdim;
+        for (i64 t = off[c]; t < off[c + 1]; ++t) {
+          for (i64 j = 0; j < blocks; ++j) f[j] = row[j * mdim + midx[t * blocks + j]];
+          for (i64 j = 0; j < blocks; ++j) {
+            c128 p = g * coeffs[t];
+            for (i64 k = 0; k < blocks; ++k)
+              if (k != j) p *= f[k];
+            grow[j * mdim + midx[t * blocks + j]] += p;
+          }
+        }
+      }
+    }
+  });
+}
+
+// Adjoint of out[b, o] = sum_{t in [off[o], off[o+1])} val[t] prod_i x[b, i]^{k[t, i]}:
+//   gx[b, i] += gout[b, o] val[t] k[t, i] x_i^{k[t, i] - 1} prod_{i' != i} x_{i'}^{k[t, i']}
+void yo_symmetric_power_monomial_adjoint(const void* x_in, i64 batch, i64 in_dim, const i64* counts,
+                                         const i64* offsets, const void* values_in, i64 out_dim,
+                                         const void* gout_in, void* gx_out) {
+  const c128* x = static_cast<const c128*>(x_in);
+  const c128* values = static_cast<const c128*>(values_in);
+  const c128* gout = static_cast<const c128*>(gout_in);
+  c128* gx = static_cast<c128*>(gx_out);
+  for (i64 b = 0; b < batch; ++b) {
+    const c128* xb = x + b * in_dim;
+    for (i64 o = 0; o < out_dim; ++o) {
+      const c128 g = gout[b * out_dim + o];
+      if (g == c128(0, 0)) continue;
+      for (i64 t = offsets[o]; t < offsets[o + 1]; ++t) {
+        const i64* kt = counts + t * in_dim;
+        for (i64 i = 0; i < in_dim; ++i) {
+          if (kt[i] == 0) continue;
+          c128 p = g * values[t] * double(kt[i]);
+          for (i64 i2 = 0; i2 < in_dim; ++i2) {
+            const i64 pw = kt[i2] - (i2 == i ? 1 : 0);
+            for (i64 q = 0; q < pw; ++q) p *= xb[i2];
+          }
+          gx[b * in_dim + i] += p;
+        }
+      }
+    }
+  }
+}
+
+// g_e = dE_i / dd_e for every edge e = (i -> nbr[e]) of the rows, from the
+// holomorphic G = dE/dA of the density above:
+//   dA[n, lm] = p (R'_n(r) (d/r) Yc_lm + R_n grad Yc_lm) . dd
+//   g_e = p Re( sum_{n, lm} G[n, lm] (R'_n (d/r) Yc_lm + R_n grad Yc_lm) )
+void yo_ace_edge_grad(const double* disp, const i64* row_off, const int* nbr, const int* species,
+                      const double* prefactor, i64 N, i64 nmax, i64 lmax, double rc, double lam,
+                      const double* G_in /* complex128 [N, nmax, W] */, double* g /* [E, 3] */) {
+  const i64 W = (lmax + 1) * (lmax + 1);
+  const c128* G = reinterpret_cast<const c128*>(G_in);
+  std::vector<double> rv(nmax + 1), rd(nmax + 1);
+  std::vector<c128> yv(W), yd(3 * W);
+  for (i64 i = 0; i < N; ++i) {
+    const c128* Gi = G + i * nmax * W;
+    for (i64 e = row_off[i]; e < row_off[i + 1]; ++e) {
+      const double* d = disp + 3 * e;
+      const double r = std::sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+      radial_one<double>(r, rc, lam, nmax, rv.data(), rd.data());
+      sh_table<double>(d, 1, lmax, false, 1e-12, yv.data(), yd.data());
+      const double p = prefactor[species[nbr[e]]];
+      const double sr = std::max(r, 1e-12);
+      double acc[3] = {0.0, 0.0, 0.0};
+      for (i64 n = 1; n <= nmax; ++n) {
+        for (i64 k = 0; k < W; ++k) {
+          const c128 gk = Gi[(n - 1) * W + k];
+          for (int a = 0; a < 3; ++a) {
+            const c128 dA = rd[n] * (d[a] / sr) * yv[k] + rv[n] * yd[3 * k + a];
+            acc[a] += (gk * dA).real();
+          }
+        }
+      }
+      for (int a = 0; a < 3; ++a) g[3 * e + a] = p * acc[a];
+    }
+  }
+}
+
+// F_k = -dE/dr_k = sum_{e in row k} g_e - sum_{e : nbr[e] = k} g_e  (d_e = r_nbr - r_row)
+void yo_forces_from_edges(const i64* row_off, const int* nbr, i64 N, const double* g, double* F) {
+  std::fill(F, F + 3 * N, 0.0);
+  for (i64 i = 0; i < N; ++i)
+    for (i64 e = row_off[i]; e < row_off[i + 1]; ++e)
+      for (int a = 0; a < 3; ++a) {
+        F[3 * i + a] += g[3 * e + a];
+        F[3 * nbr[e] + a] -= g[3 * e + a];
+      }
+}
+
 }  // extern "C"
