@@ -160,6 +160,35 @@ int y3b_neighbor_fill(const double* positions, int64_t atom_count, int64_t cente
                       void* stream);
 
 /* ------------------------------------------------------------------------
+ * Radial channel mixing.
+ * ---------------------------------------------------------------------- */
+
+/* out[p, o] = sum_i W[o, i] in[p, i] and dout[p, o] = sum_i W[o, i] din[p, i]
+ * (pace_radial_channel_contraction_with_derivative,
+ * ye3t/runtime/csrc/ye3t_runtime_core.h:74-85, .cpp:651): W row-major
+ * [output][input], points [point][input] -> [point][output]; products and
+ * sums in input order without contraction, as the reference loop.  Real
+ * dtypes.  Empty points are a no-op; zero input/output counts are an error. */
+int y3b_radial_channel_contraction(int dtype, const void* input_values, const void* input_derivatives,
+                                   const void* coefficients, int64_t point_count, int64_t input_count,
+                                   int64_t output_count, void* output_values, void* output_derivatives,
+                                   void* stream);
+
+/* A-basis with radial channels mixed per species pair:
+ *   A[i, c, l^2 + l + m] = sum_{j in row i} sum_n W[z_i, z_j, c, n-1] R_n(r_ij) Yc_lm(r_ij)
+ * for n = 1..nmax (ChebExpCos), c < channel_count, complex Condon-Shortley
+ * harmonics: the reference's radial table, the contraction above with the
+ * pair's table and density_accumulate, fused.  mixing is [S, S, C, nmax]
+ * in dtype (F32 or F64, which is also the compute and output type: A is
+ * complex64 / complex128 [center_count, C, (lmax+1)^2]); positions are f64.
+ * Bad species or neighbour indices set Y3B_STATUS_INDEX_RANGE and contribute 0. */
+int y3b_ace_density_mixed(int dtype, const double* positions, const int32_t* species, int64_t atom_count,
+                          int64_t center_begin, int64_t center_count, double box,
+                          const int64_t* row_offsets, const int32_t* neighbors, const void* mixing,
+                          int64_t species_count, int64_t channel_count, int64_t nmax, int64_t lmax,
+                          double cutoff, double lambda, void* A, int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------
  * Fused ACE evaluation over a packed multi-word bundle.
  * ---------------------------------------------------------------------- */
 

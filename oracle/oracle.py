@@ -345,3 +345,34 @@ def energy_forces(bundle, positions, box, species, prefactor, weights, cutoff, l
     e, G = bundle_energy_grad(bundle, A, species, weights, threads=threads)
     g = ace_edge_grad(disp, off, nbr, species, prefactor, bundle.nmax, bundle.lmax, cutoff, lam, G)
     return float(e.sum()), forces_from_edges(off, nbr, g)
+
+
+# -- radial channel mixing ------------------------------------------------------
+def radial_channel_contraction(values, derivatives, coefficients):
+    """``(values @ W.T, derivatives @ W.T)`` in input order (ye3t_runtime_core.cpp:651); f32 or f64."""
+    x = _c(values)
+    dt = x.dtype
+    dx = _c(derivatives, dt)
+    W = _c(coefficients, dt)
+    P, I = x.shape
+    O = W.shape[0]
+    out = np.zeros((P, O), dtype=dt)
+    dout = np.zeros((P, O), dtype=dt)
+    lib().yo_radial_channel_contraction(ctypes.c_int(0 if dt == np.float32 else 1), _p(x), _p(dx), _p(W), I64(P),
+                                        I64(I), I64(O), _p(out), _p(dout))
+    return out, dout
+
+
+def ace_density_mixed(disp, row_off, nbr, species, mixing, nmax, lmax, cutoff, lam):
+    """A-basis ``[N, C, (lmax+1)^2]`` complex128 with channels mixed by ``mixing [S, S, C, nmax]``."""
+    disp = _c(disp, np.float64)
+    off = _c(row_off, np.int64)
+    nb = _c(nbr, np.int32)
+    sp = _c(species, np.int32)
+    W = _c(mixing, np.float64)
+    S, _, C, _ = W.shape
+    N = off.shape[0] - 1
+    A = np.zeros((N, C, (lmax + 1) ** 2), dtype=np.complex128)
+    lib().yo_ace_density_mixed(_p(disp), _p(off), _p(nb), _p(sp), _p(W), I64(N), I64(S), I64(C), I64(nmax),
+                               I64(lmax), ctypes.c_double(cutoff), ctypes.c_double(lam), _p(A))
+    return A

@@ -101,4 +101,15 @@ void yr_symmetric_power_monomial_f64(const double* x, i64 batch, i64 in_dim, con
   });
 }
 
+
+// ye3t_runtime_core.h:76 pace_radial_channel_contraction_with_derivative (serial: one call)
+void yr_pace_radial_channel_contraction_f64(const double* in, const double* din, const double* W, i64 P, i64 I,
+                                            i64 O, double* out, double* dout) {
+  rt::pace_radial_channel_contraction_with_derivative<double>(in, din, W, P, I, O, out, dout);
+}
+
+void yr_pace_radial_channel_contraction_f32(const float* in, const float* din, const float* W, i64 P, i64 I,
+                                            i64 O, float* out, float* dout) {
+  rt::pace_radial_channel_contraction_with_derivative<float>(in, din, W, P, I, O, out, dout);
+}
 }  // extern "C"

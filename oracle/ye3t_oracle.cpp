@@ -309,6 +309,23 @@ void density_adjoint(const S* adj, const i64* centers, i64 E, i64 C, S* out) {
     for (i64 c = 0; c < C; ++c) out[e * C + c] = adj[centers[e] * C + c];
 }
 
+template <typename R>
+void contraction(const R* in, const R* din, const R* W, i64 P, i64 I, i64 O, R* out, R* dout) {
+  for (i64 p = 0; p < P; ++p)
+    for (i64 o = 0; o < O; ++o) {
+      R v = R(0), d = R(0);
+      for (i64 i = 0; i < I; ++i) {
+        const R c = W[o * I + i];
+        const R a = c * in[p * I + i];
+        const R b = c * din[p * I + i];
+        v = v + a;
+        d = d + b;
+      }
+      out[p * O + o] = v;
+      dout[p * O + o] = d;
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -562,6 +579,50 @@ void yo_forces_from_edges(const i64* row_off, const int* nbr, i64 N, const doubl
         F[3 * i + a] += g[3 * e + a];
         F[3 * nbr[e] + a] -= g[3 * e + a];
       }
+}
+
+// ---------------------------------------------------------------------------
+// Radial channel mixing (pace_radial_channel_contraction_with_derivative,
+// ye3t/runtime/csrc/ye3t_runtime_core.cpp:651): out[p, o] = sum_i W[o, i] in[p, i]
+// and the same for the derivatives, inputs in order, multiply then add.
+// ---------------------------------------------------------------------------
+void yo_radial_channel_contraction(int dtype, const void* in, const void* din, const void* W, i64 P, i64 I, i64 O,
+                                   void* out, void* dout) {
+  if (dtype == 0)
+    contraction<float>(static_cast<const float*>(in), static_cast<const float*>(din),
+                       static_cast<const float*>(W), P, I, O, static_cast<float*>(out), static_cast<float*>(dout));
+  else
+    contraction<double>(static_cast<const double*>(in), static_cast<const double*>(din),
+                        static_cast<const double*>(W), P, I, O, static_cast<double*>(out),
+                        static_cast<double*>(dout));
+}
+
+// A-basis with channels mixed per species pair (fp64): the composition of the
+// radial table (execution_plan.py:7298, indices 1..nmax), the contraction
+// above with the table W[z_i, z_j] (row-major [channel][n]), the complex
+// harmonics (:7479) and density_accumulate (:7913), edges in CSR order:
+//   A[i, c, lm] = sum_{e in row i} Rm_c(e) Yc_lm(d_e),  Rm_c = sum_n W[z_i, z_j, c, n-1] R_n(r)
+void yo_ace_density_mixed(const double* disp, const i64* row_off, const int* nbr, const int* species,
+                          const double* mixing, i64 N, i64 S, i64 C, i64 nmax, i64 lmax, double rc, double lam,
+                          double* A_out /* complex128 [N, C, (lmax+1)^2] */) {
+  const i64 W = (lmax + 1) * (lmax + 1);
+  c128* A = reinterpret_cast<c128*>(A_out);
+  std::vector<double> rv(nmax + 1), rd(nmax + 1), rm(C), dm(C);
+  std::vector<c128> yv(W), yd(3 * W);
+  for (i64 i = 0; i < N; ++i) {
+    c128* Ai = A + i * C * W;
+    for (i64 k = 0; k < C * W; ++k) Ai[k] = c128(0, 0);
+    for (i64 e = row_off[i]; e < row_off[i + 1]; ++e) {
+      const double* d = disp + 3 * e;
+      const double r = std::sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+      radial_one<double>(r, rc, lam, nmax, rv.data(), rd.data());
+      const double* Wp = mixing + (i64(species[i]) * S + species[nbr[e]]) * C * nmax;
+      contraction<double>(rv.data() + 1, rd.data() + 1, Wp, 1, nmax, C, rm.data(), dm.data());
+      sh_table<double>(d, 1, lmax, false, 1e-12, yv.data(), yd.data());
+      for (i64 c = 0; c < C; ++c)
+        for (i64 k = 0; k < W; ++k) Ai[c * W + k] += rm[c] * yv[k];
+    }
+  }
 }
 
 }  // extern "C"

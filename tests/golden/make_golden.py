@@ -400,8 +400,66 @@ def forces_fixture():
     print("forces_small.npz energy", float(energy), "|F| max", float(grad.abs().max()))
 
 
+def mixing_fixture():
+    """Radial channel mixing through the reference core, and the mixed A-basis.
+
+    Contraction: random inputs, derivatives and a [output][input] table through
+    ``pace_radial_channel_contraction_with_derivative`` (the reference core,
+    f64 and f32).  Mixed A-basis (4 species, n_max 12, 8 channels, l_max 4): the
+    reference radial table, per edge the contraction with the table of the
+    pair (z_i, z_j), the reference complex harmonics and ``density_accumulate``.
+    """
+    ref = load_refcore()
+    rng = np.random.default_rng(5)
+    out = {}
+    for tag, dt, fn in (("f64", np.float64, ref.yr_pace_radial_channel_contraction_f64),
+                        ("f32", np.float32, ref.yr_pace_radial_channel_contraction_f32)):
+        P, I, O = 257, 12, 32
+        x = rng.normal(size=(P, I)).astype(dt)
+        dx = rng.normal(size=(P, I)).astype(dt)
+        Wt = (rng.normal(size=(O, I)) / np.sqrt(I)).astype(dt)
+        y = np.zeros((P, O), dtype=dt)
+        dy = np.zeros((P, O), dtype=dt)
+        fn(_p(x), _p(dx), _p(Wt), ctypes.c_int64(P), ctypes.c_int64(I), ctypes.c_int64(O), _p(y), _p(dy))
+        out.update({f"c_{tag}_x": x, f"c_{tag}_dx": dx, f"c_{tag}_w": Wt, f"c_{tag}_y": y, f"c_{tag}_dy": dy})
+    N, density, rc, lam, nmax, lmax, S, C = 64, 0.05, 5.0, 5.0, 12, 4, 4, 8
+    box = (N / density) ** (1.0 / 3.0)
+    pos = torch.rand(N, 3, dtype=torch.float64, generator=torch.Generator().manual_seed(0)).numpy() * box
+    species = torch.randint(0, S, (N,), generator=torch.Generator().manual_seed(1)).numpy().astype(np.int32)
+    mix = torch.randn(S, S, C, nmax, dtype=torch.float64, generator=torch.Generator().manual_seed(2)).numpy()
+    mix /= np.sqrt(nmax)
+    off, nbr, disp = minimum_image_csr(pos, box, rc)
+    E = nbr.shape[0]
+    r = np.sqrt((disp ** 2).sum(-1))
+    Rv, Rd = cheb_exp_cos_radial_table_with_derivative(torch.tensor(r), torch.full((E,), rc), torch.full((E,), lam),
+                                                        nmax, backend="reference")
+    Rv = np.ascontiguousarray(Rv.detach().numpy()[:, 1:])
+    Rd = np.ascontiguousarray(Rd.detach().numpy()[:, 1:])
+    centers = np.repeat(np.arange(N), np.diff(off))
+    Rm = np.zeros((E, C))
+    scratch = np.zeros((1, C))
+    for e in range(E):
+        Wp = np.ascontiguousarray(mix[species[centers[e]], species[nbr[e]]])
+        ref.yr_pace_radial_channel_contraction_f64(_p(Rv[e:e + 1]), _p(Rd[e:e + 1]), _p(Wp), ctypes.c_int64(1),
+                                                   ctypes.c_int64(nmax), ctypes.c_int64(C), _p(Rm[e:e + 1]),
+                                                   _p(scratch))
+    W = (lmax + 1) ** 2
+    Yv = np.zeros((E, W), dtype=np.complex128)
+    Yd = np.zeros((E, W, 3), dtype=np.complex128)
+    ref.yr_complex_spherical_harmonics_table_f64(_p(np.ascontiguousarray(disp)), ctypes.c_int64(E),
+                                                 ctypes.c_int64(lmax), ctypes.c_double(1e-12), _p(Yv), _p(Yd),
+                                                 ctypes.c_int(1))
+    edge = torch.tensor(Rm)[:, :, None].to(torch.complex128) * torch.tensor(Yv)[:, None, :]
+    A = density_accumulate(edge.reshape(E, -1), torch.tensor(centers), N, backend="reference").reshape(N, C, W)
+    out.update({"pos": pos, "box": np.asarray(box), "species": species, "mixing": mix, "row_off": off, "nbr": nbr,
+                "rc": np.asarray(rc), "lam": np.asarray(lam), "nmax": np.asarray(nmax), "lmax": np.asarray(lmax),
+                "A": A.numpy()})
+    np.savez_compressed(os.path.join(HERE, "mixing_small.npz"), **out)
+    print("mixing_small.npz", N, "atoms", E, "edges", "A norm", float(np.abs(A.numpy()).sum()))
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces"]
+    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -414,3 +472,5 @@ if __name__ == "__main__":
         ace_fixture()
     if "forces" in which:
         forces_fixture()
+    if "mixing" in which:
+        mixing_fixture()

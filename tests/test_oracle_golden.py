@@ -189,3 +189,22 @@ def test_oracle_schedule_adjoint_is_the_holomorphic_derivative():
         lm = (gout * oracle.schedule_evaluate_record(bv - d, rec)).real.sum()
         lin = (gbv * d).real.sum()
         assert abs((lp - lm) / 2 - lin) <= 1e-7 * abs(lin) + 1e-14
+
+
+def test_oracle_radial_channel_contraction_matches_reference_core(golden):
+    """Bit-exact against pace_radial_channel_contraction_with_derivative (reference core, f64 and f32)."""
+    g = golden("mixing_small")
+    for tag in ("f64", "f32"):
+        y, dy = oracle.radial_channel_contraction(g[f"c_{tag}_x"], g[f"c_{tag}_dx"], g[f"c_{tag}_w"])
+        assert np.array_equal(y, g[f"c_{tag}_y"]) and np.array_equal(dy, g[f"c_{tag}_dy"])
+
+
+def test_oracle_mixed_density_matches_reference_composition(golden):
+    """Mixed A-basis against the reference radial table, contraction, harmonics and density_accumulate."""
+    g = golden("mixing_small")
+    off, nbr, disp = oracle.neighbor_list(g["pos"], float(g["box"]), float(g["rc"]))
+    assert np.array_equal(off, g["row_off"]) and np.array_equal(nbr, g["nbr"])
+    A = oracle.ace_density_mixed(disp, off, nbr, g["species"], g["mixing"], int(g["nmax"]), int(g["lmax"]),
+                                 float(g["rc"]), float(g["lam"]))
+    err = np.abs(A - g["A"]).max() / np.abs(g["A"]).max()
+    assert err <= 1e-13, err

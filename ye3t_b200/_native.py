@@ -71,6 +71,9 @@ _SIGS = {
                                        VP]),
     "y3b_ace_features": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
     "y3b_ace_energy": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP]),
+    "y3b_radial_channel_contraction": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, I64, VP, VP, VP]),
+    "y3b_ace_density_mixed": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64,
+                                             I64, DBL, DBL, VP, VP, VP]),
     "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP, VP]),
     "y3b_ace_edge_grad": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                          VP, VP]),

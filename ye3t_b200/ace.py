@@ -104,6 +104,29 @@ class ACEEvaluator:
             A.data_ptr(), nat.ptr(status), self._stream()), "ace_density")
         return A
 
+    def density_mixed(self, positions, species, box, row_offsets, neighbors, mixing, begin: int = 0,
+                      dtype=torch.float64, status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """A-basis ``[n_centres, C, (lmax+1)^2]`` with radial channels mixed per species pair.
+
+        ``mixing [S, S, C, nmax]``: channel c of a pair (z_i, z_j) is
+        ``sum_n mixing[z_i, z_j, c, n-1] R_n``.  ``dtype`` float64 gives
+        complex128, float32 complex64 (computed in that precision).
+        """
+        pos = positions.to(self.device, torch.float64).contiguous()
+        sp = species.to(self.device, torch.int32).contiguous()
+        W = torch.as_tensor(mixing, dtype=dtype, device=self.device).contiguous()
+        if W.dim() != 4 or W.shape[0] != W.shape[1]:
+            raise ValueError("mixing must be [S, S, C, nmax]")
+        count = int(row_offsets.shape[0]) - 1
+        cdt = torch.complex128 if dtype == torch.float64 else torch.complex64
+        A = torch.empty((count, W.shape[2], self.W), dtype=cdt, device=self.device)
+        nat.check(nat.lib().y3b_ace_density_mixed(
+            nat.dtype_code(dtype), pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box),
+            row_offsets.data_ptr(), neighbors.data_ptr(), W.data_ptr(), W.shape[0], W.shape[2], W.shape[3],
+            self.bundle.lmax, float(self.config.cutoff), float(self.config.radial_lambda), A.data_ptr(),
+            nat.ptr(status), self._stream()), "ace_density_mixed")
+        return A
+
     # -- kernel 2 ----------------------------------------------------------------
     def features(self, A: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """B-basis features ``[n, feature_count]`` complex128 from the A-basis."""
@@ -114,6 +137,19 @@ class ACEEvaluator:
         nat.check(nat.lib().y3b_ace_features(ctypes_ref(self._tables), A.data_ptr(), n, out.data_ptr(),
                                              self._stream()), "ace_features")
         return out
+
+    def channel_features(self, A: torch.Tensor) -> torch.Tensor:
+        """Channel-diagonal features ``[n, C * feature_count]`` from mixed channels ``A [n, C, W]``.
+
+        The bundle's words read a single radial channel (``nmax == 1``); every
+        channel is evaluated with the same items, channel c's features at
+        ``[c * F, (c + 1) * F)``.
+        """
+        if self.bundle.nmax != 1:
+            raise ValueError("channel_features needs a channel-diagonal bundle (nmax == 1)")
+        n, C, W = A.shape
+        out = self.features(A.reshape(n * C, 1, W))
+        return out.reshape(n, C * self.packed.feature_count)
 
     def energy_from_density(self, A: torch.Tensor, species_centres: torch.Tensor,
                             out: Optional[torch.Tensor] = None) -> torch.Tensor:

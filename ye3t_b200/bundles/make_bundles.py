@@ -31,14 +31,23 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 from ye3t_b200.schedules import (ACEBundle, ScheduleRecord, SymPowerTable,  # noqa: E402
                                  enumerate_ace_words, schedule_table_hash)
 
-# Word sets shipped with the package: (file stem, nmax, lmax, numax, target_L).
+# Word sets shipped with the package: (file stem, nmax, lmax, numax, target_L, parity).
+# Symmetric-power tables are materialised exactly; Sym^4(V_4) (l_max 4) is
+# over the reference's exact-symbolic resource limit and takes its "auto"
+# policy (the reference's own advice), recorded in the bundle meta.
+# The channel-diagonal sets (nmax 1) are evaluated once per mixed radial
+# channel: every block of a word reads the same channel.
 BUNDLES = [
-    ("ace_n8_l3_nu4_L0", 8, 3, 4, 0),  # large-scale scalar ACE (nu <= 4, l_max 3)
-    ("ace_n8_l3_nu3_L0", 8, 3, 3, 0),  # single-species scalar descriptor (nu <= 3)
+    ("ace_n8_l3_nu4_L0", 8, 3, 4, 0, "even"),  # large-scale scalar ACE (nu <= 4, l_max 3)
+    ("ace_n8_l3_nu3_L0", 8, 3, 3, 0, "even"),  # single-species scalar descriptor (nu <= 3)
+    ("ace_diag_l4_nu4_L0", 1, 4, 4, 0, "even"),  # multi-species, mixed channels (l_max 4, nu <= 4)
+    ("ace_diag_l3_nu3_L0", 1, 3, 3, 0, "all"),  # equivariant couplings, L = 0 outputs
+    ("ace_diag_l3_nu3_L1", 1, 3, 3, 1, "all"),  # ... L = 1 outputs
+    ("ace_diag_l3_nu3_L2", 1, 3, 3, 2, "all"),  # ... L = 2 outputs
 ]
 
 
-def reference_compilers(target_L: int):
+def reference_compilers(target_L: int, materialization: str = "exact"):
     import torch
     from ye3t import couplings
     from ye3t.couplings import compile_ace_factorized_schedules_by_L
@@ -54,7 +63,7 @@ def reference_compilers(target_L: int):
               "multiplicity_index": mu, "component_index": m,
               "channel_indices": tuple(range(2 * l + 1))} for m in range(2 * Lam + 1)],
             descriptor_count=2 * Lam + 1, channel_count=2 * l + 1,
-            basis_convention="complex_magnetic")
+            basis_convention="complex_magnetic", coefficient_materialization=materialization)
         grouped, _shared, _dt = _symmetric_power_product_plan_count_table(
             plan, device="cpu", dtype=torch.complex128, imag_tol=1e-12)
         counts, offsets, index, values = grouped
@@ -89,15 +98,18 @@ def main(argv=None):
     ap.add_argument("--out", default=HERE)
     ap.add_argument("--only", default=None)
     args = ap.parse_args(argv)
-    for stem, nmax, lmax, numax, L in BUNDLES:
+    for stem, nmax, lmax, numax, L, parity in BUNDLES:
         if args.only and stem != args.only:
             continue
         t0 = time.time()
-        words = enumerate_ace_words(nmax, lmax, numax)
-        cp, st = reference_compilers(L)
+        words = enumerate_ace_words(nmax, lmax, numax, parity=parity)
+        materialization = "auto" if lmax >= 4 else "exact"
+        cp, st = reference_compilers(L, materialization)
+        rule = "even sum(l)" if parity == "even" else "any sum(l) with a basis at target_L"
         b = ACEBundle.from_words(words, nmax, lmax, L, cp, st, meta={
-            "word_rule": "all multisets of (n,l), n in 1..nmax, l in 0..lmax, size 1..numax, even sum(l)",
-            "nmax": nmax, "lmax": lmax, "numax": numax, "target_L": L,
+            "word_rule": f"all multisets of (n,l), n in 1..nmax, l in 0..lmax, size 1..numax, {rule}",
+            "nmax": nmax, "lmax": lmax, "numax": numax, "target_L": L, "parity": parity,
+            "symmetric_power_materialization": materialization,
             "compiler": "ye3t.couplings.compile_ace_factorized_schedules_by_L (defaults)"})
         n_checked = check_rebinding(b, args.check_every)
         path = os.path.join(args.out, stem + ".npz")

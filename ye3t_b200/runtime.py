@@ -28,6 +28,7 @@ __all__ = [
     "density_accumulate_adjoint",
     "symmetric_power_monomial_contraction",
     "symmetric_power_table_contraction",
+    "pace_radial_channel_contraction_with_derivative",
     "native_execution_plan_capabilities",
 ]
 
@@ -240,6 +241,36 @@ def symmetric_power_table_contraction(input, table, *, backend="auto"):
                                                 table.output_index, vals, backend=backend)
 
 
+def pace_radial_channel_contraction_with_derivative(values, derivatives, coefficients, backend="auto"):
+    """Dense radial channel mixing; ``ye3t/runtime/csrc/ye3t_runtime_core.h:74-85``.
+
+    ``values``/``derivatives`` ``[P, I]``, ``coefficients`` row-major ``[O, I]``;
+    returns ``(values @ W^T, derivatives @ W^T)`` as ``[P, O]`` (products and
+    sums in input order, as the reference loop).  float32 or float64.
+    """
+    _check_backend(backend)
+    x = torch.as_tensor(values)
+    dev = nat.require_cuda(x, what="pace_radial_channel_contraction_with_derivative")
+    if x.dtype not in (torch.float32, torch.float64) or x.dim() != 2:
+        raise ValueError("values must be real [P, I]")
+    dx = torch.as_tensor(derivatives, device=dev)
+    W = torch.as_tensor(coefficients, device=dev)
+    if dx.shape != x.shape or dx.dtype != x.dtype or W.dtype != x.dtype or W.dim() != 2 or W.shape[1] != x.shape[1]:
+        raise ValueError("derivatives must match values and coefficients must be [O, I] of the same dtype")
+    if W.shape[0] <= 0 or x.shape[1] <= 0:
+        raise ValueError("empty radial contraction")
+    x, dx, W = x.contiguous(), dx.contiguous(), W.contiguous()
+    P, I = x.shape
+    O = W.shape[0]
+    out = torch.empty((P, O), dtype=x.dtype, device=dev)
+    dout = torch.empty_like(out)
+    nat.check(nat.lib().y3b_radial_channel_contraction(nat.dtype_code(x.dtype), x.data_ptr(), dx.data_ptr(),
+                                                       W.data_ptr(), P, I, O, out.data_ptr(), dout.data_ptr(),
+                                                       nat.stream_of(dev)),
+              "pace_radial_channel_contraction_with_derivative")
+    return out, dout
+
+
 def native_execution_plan_capabilities():
     """Capability report; the analogue of ``ye3t/runtime/execution_plan.py:6118``."""
     try:
@@ -263,6 +294,8 @@ def native_execution_plan_capabilities():
             "symmetric_power_monomial": ["float32", "float64", "complex64", "complex128"],
             "factorized_schedule": ["float32", "float64", "complex64", "complex128"],
             "ace_density": ["float64 -> complex128"],
+            "ace_density_mixed": ["float32 -> complex64", "float64 -> complex128"],
+            "pace_radial_channel_contraction_with_derivative": ["float32", "float64"],
             "ace_bundle": ["complex128"],
         },
         "density_accumulate_deterministic": True,
