@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="atoms in the CPU baseline sample (default 256 with forces, 1024 energy only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="c5", choices=["c5", "c3", "c3f32", "c4"],
+                    help="c5 (default): the headline 2^20-atom energy + forces step; c3/c3f32/c4: the "
+                         "channel-diagonal descriptor configurations (mixed radial channels)")
     ap.add_argument("--energy-only", action="store_true",
                     help="time the energy step alone (no adjoint, no forces)")
     return ap.parse_args()
@@ -386,8 +389,227 @@ def run_b200(args):
     print(json.dumps(line), flush=True)
 
 
+# Channel-diagonal configurations: radial channels mixed per species pair,
+# every word reading one mixed channel (packing bundles with nmax 1).
+CHANNEL_CONFIGS = {
+    "c3": dict(atoms=65536, species=4, nmax=12, channels=32, lmax=4, bundles=["ace_diag_l4_nu4_L0"], dtype="f64",
+               workload="C3 multi-species scalar ACE: 65,536 atoms (periodic cubic box, 0.05/A^3), 4 species, "
+                        "ChebExpCos n_max 12 mixed per species pair to 32 channels, l_max 4, nu<=4 "
+                        "channel-diagonal words (53 words / 71 L=0 features per channel, 2,272 per atom)"),
+    "c3f32": dict(atoms=65536, species=4, nmax=12, channels=32, lmax=4, bundles=["ace_diag_l4_nu4_L0"],
+                  dtype="f32", workload="C3 as above, evaluated in fp32"),
+    "c4": dict(atoms=32768, species=2, nmax=8, channels=64, lmax=3,
+               bundles=["ace_diag_l3_nu3_L0", "ace_diag_l3_nu3_L1", "ace_diag_l3_nu3_L2"], dtype="f32",
+               workload="C4 equivariant couplings: 32,768 atoms, 2 species, n_max 8 mixed per species pair to "
+                        "64 channels, l_max 3, nu<=3 channel-diagonal words, outputs L = 0, 1, 2 (13 / 20 / 29 "
+                        "labels per channel, 13,952 components per atom)"),
+}
+
+
+def _channel_system(cfg):
+    import torch
+    N = cfg["atoms"]
+    box = (N / DENSITY) ** (1.0 / 3.0)
+    pos = torch.rand(N, 3, dtype=torch.float64, generator=torch.Generator().manual_seed(0)) * box
+    species = torch.randint(0, cfg["species"], (N,), generator=torch.Generator().manual_seed(1)).to(torch.int32)
+    mix = torch.randn(cfg["species"], cfg["species"], cfg["channels"], cfg["nmax"], dtype=torch.float64,
+                      generator=torch.Generator().manual_seed(2)) / cfg["nmax"] ** 0.5
+    return pos, species, box, mix
+
+
+def cpu_channels_baseline(cfg, sample_atoms):
+    """The reference CPU path restated (oracle) for a channel configuration on a bounded sample."""
+    import numpy as np
+
+    from oracle import oracle
+    from ye3t_b200.schedules import ACEBundle
+    cores = len(os.sched_getaffinity(0))
+    bundles = [ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", b + ".npz")) for b in cfg["bundles"]]
+    M = int(sample_atoms)
+    rng = np.random.default_rng(0)
+    box = (M / DENSITY) ** (1 / 3)
+    pos = rng.uniform(0, box, (M, 3))
+    sp = rng.integers(0, cfg["species"], M).astype(np.int32)
+    mix = rng.normal(size=(cfg["species"], cfg["species"], cfg["channels"], cfg["nmax"])) / cfg["nmax"] ** 0.5
+    t0 = time.perf_counter()
+    off, nbr, disp = oracle.neighbor_list(pos, box, CUTOFF)
+    A = oracle.ace_density_mixed(disp, off, nbr, sp, mix, cfg["nmax"], cfg["lmax"], CUTOFF, LAMBDA)
+    total = 0.0
+    for b in bundles:
+        for c in range(cfg["channels"]):
+            total += float(np.abs(oracle.bundle_features(b, A[:, c:c + 1, :], threads=cores).real).sum())
+    dt = time.perf_counter() - t0
+    assert np.isfinite(total)
+    return {"value": M / dt, "unit": "atoms/s", "cores": cores, "kind": "port",
+            "sample": f"{M} atoms of the same density/species/cutoff in a {box:.1f} A periodic box; brute-force "
+                      f"neighbour list, mixed A-basis (radial table, per-pair contraction as "
+                      f"ye3t_runtime_core.cpp:651, harmonics, density_accumulate), then per channel and word the "
+                      f"reference block assembly and schedule evaluation, fp64 ({cores} threads); {dt:.1f} s"}
+
+
+def run_channels(args):
+    import torch
+    import torch.distributed as dist
+
+    from ye3t_b200 import _native as nat
+    from ye3t_b200.ace import ACEConfig, ACEEvaluator
+    from ye3t_b200.distributed import atom_block, init_from_env, max_over_ranks as _max_over_ranks
+    from ye3t_b200.schedules import ACEBundle
+
+    cfg = CHANNEL_CONFIGS[args.config]
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    rank, world = init_from_env("nccl", 300.0, device)
+    pos, species, box, mix = _channel_system(cfg)
+    N = cfg["atoms"]
+    rdt = torch.float64 if cfg["dtype"] == "f64" else torch.float32
+    evs = [ACEEvaluator(ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", b + ".npz")), device,
+                        config=ACEConfig(CUTOFF, LAMBDA)) for b in cfg["bundles"]]
+    begin, end = atom_block(rank, world, N)
+    n_local = end - begin
+    pos_h, sp_h = pos.pin_memory(), species.pin_memory()
+    pos_d, sp_d = pos.to(device), species.to(device)
+    mix_d = mix.to(device, rdt)
+    stages = ("neighbors", "density", "features")
+    timers = {k: [] for k in stages}
+
+    def step(record):
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
+        if record:
+            marks[0].record()
+        row, nbr = evs[0].neighbor_list(pos_d, box, begin, end)
+        if record:
+            marks[1].record()
+        A = evs[0].density_mixed(pos_d, sp_d, box, row, nbr, mix_d, begin=begin, dtype=rdt)
+        if record:
+            marks[2].record()
+        check = torch.zeros((), dtype=torch.float64, device=device)
+        for ev in evs:
+            check += ev.channel_features(A).real.abs().sum().to(torch.float64)
+        if record:
+            marks[3].record()
+        return check, marks
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(False)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = []
+    t0.record()
+    for _ in range(args.steps):
+        check, m = step(True)
+        marks.append(m)
+    t1.record()
+    barrier()
+    clock_info = clocks.stop()
+    dev_ms = _max_over_ranks(t0.elapsed_time(t1) / args.steps, device)
+    for m in marks:
+        for k, a, b in zip(stages, m[:-1], m[1:]):
+            timers[k].append(a.elapsed_time(b))
+    host = torch.empty(1, dtype=torch.float64).pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        pos_d.copy_(pos_h, non_blocking=True)
+        sp_d.copy_(sp_h, non_blocking=True)
+        c, _ = step(False)
+        host.copy_(c.reshape(1), non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, device)
+    # roofline of the B-basis stage: algorithmic flops (needed item flops per
+    # atom and channel) against the FMA peak of the compute type, and the
+    # feature bytes written against HBM; the larger time is the bound
+    best = 0.0
+    sink = torch.empty(148 * 8 * 256, dtype=rdt, device=device)
+    fl = nat.DBL(0.0)
+    for _ in range(6):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        nat.check(nat.lib().y3b_fma_peak_launch(nat.dtype_code(rdt), 148 * 8, 256, 40000, sink.data_ptr(),
+                                                 nat.ctypes.byref(fl), nat.stream_of(device)), "fma_peak")
+        b.record()
+        b.synchronize()
+        best = max(best, fl.value / (a.elapsed_time(b) * 1e-3) / 1e12)
+    C = cfg["channels"]
+    feat_flops = sum(ev.packed.flops_per_atom()["items"] for ev in evs) * C * n_local
+    cplx = 16 if rdt == torch.float64 else 8
+    W = (cfg["lmax"] + 1) ** 2
+    feat_bytes = (sum(ev.feature_count for ev in evs) * C + len(evs) * C * W) * cplx * n_local
+    feat_ms = statistics.mean(timers["features"])
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
+            hbm_peak = float(json.load(fh)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        hbm_peak = 6650.0
+    t_fp = feat_flops / (best * 1e12)
+    t_hbm = feat_bytes / (hbm_peak * 1e9)
+    if t_fp >= t_hbm:
+        roof = {"bound": cfg["dtype"], "achieved": feat_flops / (feat_ms * 1e-3) / 1e12, "peak": best,
+                "unit": "TFLOP/s", "peak_source": f"{cfg['dtype']} FMA microbenchmark (y3b_fma_peak_launch) in "
+                                                  "this run"}
+    else:
+        roof = {"bound": "hbm", "achieved": feat_bytes / (feat_ms * 1e-3) / 1e9, "peak": hbm_peak,
+                "unit": "GB/s", "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy)"}
+    roof.update({"kernel": f"ace_eval_kernel<{'double' if rdt == torch.float64 else 'float'}, 0> (features, "
+                           "all channels of all bundles)",
+                 "frac": roof["achieved"] / roof["peak"], "traffic": None,
+                 "flops_per_step": feat_flops, "bytes_per_step": feat_bytes})
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_channels_baseline(cfg, 512)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": f"ACE channel-diagonal features atoms/sec ({args.config})", "value": N / (dev_ms * 1e-3),
+        "unit": "atoms/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded uniform positions, random mixing tables)",
+        "config": {"workload": cfg["workload"], "atoms": N, "bundles": cfg["bundles"], "cutoff_A": CUTOFF,
+                   "radial_lambda": LAMBDA, "parallelism": f"atom-block x{world}",
+                   "l2": "feature output larger than L2 (written to HBM every step)"},
+        "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
+                "d2h_bytes_per_step": 8,
+                "note": "features stay on the device (sharded descriptor); a checksum is read back"},
+        "gpu_launches": (9 + len(evs)) * args.steps,
+        "roofline": roof,
+        "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
+        "checksum": float(check.item()),
+        "clocks": clock_info,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.config != "c5":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                cfg = CHANNEL_CONFIGS[args.config]
+                vals = [cpu_channels_baseline(cfg, 512) for _ in range(args.warmup + args.steps)][args.warmup:]
+                v = statistics.median([x["value"] for x in vals])
+                print(json.dumps({"impl": "reference", "metric": f"ACE channel-diagonal features atoms/sec "
+                                                               f"({args.config})", "value": v, "unit": "atoms/s",
+                                  "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                                  "higher_is_better": True, "cpu_baseline": dict(vals[-1], value=v),
+                                  "e2e": {"value": v, "unit": "atoms/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}), flush=True)
+            return
+        run_channels(args)
+        return
     if args.cpu_sample is None:
         args.cpu_sample = 1024 if args.energy_only else 256
     if args.impl == "reference":

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define Y3B_ABI_VERSION 4
+#define Y3B_ABI_VERSION 5
 
 /* dtype codes */
 #define Y3B_F32 0
@@ -248,6 +248,12 @@ int y3b_ace_density(const double* positions, const int32_t* species, int64_t ato
  * [atom_count, nmax, (lmax+1)^2] output of y3b_ace_density. */
 int y3b_ace_features(const y3b_ace_tables* tables, const void* A, int64_t atom_count, void* features,
                      void* stream);
+
+/* As y3b_ace_features with A and features in dtype Y3B_C128 (as above) or
+ * Y3B_C64 (complex64, evaluated in fp32 with the fp64 coefficient tables
+ * rounded on load). */
+int y3b_ace_features_typed(int dtype, const y3b_ace_tables* tables, const void* A, int64_t atom_count,
+                           void* features, void* stream);
 
 /* Per-atom energy e[i] = sum_f weights[species[i], f] Re(B[i, f]) with B
  * evaluated on chip and never stored (species/energy indexed like A). */

@@ -112,3 +112,21 @@ def test_channel_diagonal_features_config4(golden, stem, count):
     assert B.shape == (A.shape[0], A.shape[1] * count)
     err = np.abs(B - ref).max() / np.abs(ref).max()
     assert err <= 1e-12, err
+
+
+@pytest.mark.parametrize("stem", ["ace_diag_l4_nu4_L0", "ace_diag_l3_nu3_L2"])
+def test_channel_diagonal_features_fp32(golden, stem):
+    """Mixed density and B-basis evaluated in fp32 against the fp64 oracle (1e-5 of the largest feature)."""
+    g = golden("mixing_small")
+    ev = _evaluator(stem, g)
+    pos = torch.as_tensor(g["pos"], device=DEV)
+    sp = torch.as_tensor(g["species"], device=DEV)
+    box = float(g["box"])
+    row, nbr = ev.neighbor_list(pos, box)
+    A64 = ev.density_mixed(pos, sp, box, row, nbr, g["mixing"], dtype=torch.float64)
+    A32 = ev.density_mixed(pos, sp, box, row, nbr, g["mixing"], dtype=torch.float32)
+    B = ev.channel_features(A32)
+    assert B.dtype == torch.complex64
+    ref = _oracle_channel_features(ev.bundle, A64.cpu().numpy())
+    err = np.abs(B.cpu().numpy().astype(np.complex128) - ref).max() / np.abs(ref).max()
+    assert err <= 1e-5, err

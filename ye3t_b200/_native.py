@@ -16,7 +16,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libye3t_b200.so")
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 F32, F64, C64, C128 = 0, 1, 2, 3
 STATUS_INDEX_RANGE = 1
 STATUS_CAPACITY = 2
@@ -70,6 +70,7 @@ _SIGS = {
     "y3b_ace_density": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                        VP]),
     "y3b_ace_features": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),
+    "y3b_ace_features_typed": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(AceTables), VP, I64, VP, VP]),
     "y3b_ace_energy": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP]),
     "y3b_radial_channel_contraction": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, I64, VP, VP, VP]),
     "y3b_ace_density_mixed": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64,

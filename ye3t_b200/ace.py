@@ -129,13 +129,19 @@ class ACEEvaluator:
 
     # -- kernel 2 ----------------------------------------------------------------
     def features(self, A: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """B-basis features ``[n, feature_count]`` complex128 from the A-basis."""
-        A = A.to(self.device, torch.complex128).contiguous()
+        """B-basis features ``[n, feature_count]`` from the A-basis.
+
+        complex128 A gives complex128 features; complex64 A is evaluated in
+        fp32 and gives complex64 features.
+        """
+        dt = torch.complex64 if A.dtype == torch.complex64 else torch.complex128
+        A = A.to(self.device, dt).contiguous()
         n = A.shape[0]
         if out is None:
-            out = torch.empty((n, self.packed.feature_count), dtype=torch.complex128, device=self.device)
-        nat.check(nat.lib().y3b_ace_features(ctypes_ref(self._tables), A.data_ptr(), n, out.data_ptr(),
-                                             self._stream()), "ace_features")
+            out = torch.empty((n, self.packed.feature_count), dtype=dt, device=self.device)
+        code = nat.C64 if dt == torch.complex64 else nat.C128
+        nat.check(nat.lib().y3b_ace_features_typed(code, ctypes_ref(self._tables), A.data_ptr(), n, out.data_ptr(),
+                                                   self._stream()), "ace_features")
         return out
 
     def channel_features(self, A: torch.Tensor) -> torch.Tensor:

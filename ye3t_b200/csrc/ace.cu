@@ -138,10 +138,11 @@ constexpr int kEvalWarps = 16;
 constexpr int kPadEntries = 16;  // zero entries before and after the block entries
 
 // B = 1: a single tuple, i_0 = K.
-template <int NC>
-__device__ __forceinline__ void eval_b1(const double2* __restrict__ P, const Item& it,
-                                        const double* __restrict__ coef, double2& a0, double2& a1) {
-  const double2 v = P[(it.b0 + it.K) * kLanes];
+template <typename R, int NC>
+__device__ __forceinline__ void eval_b1(const Cx2<R>* __restrict__ P, const Item& it,
+                                        const double* __restrict__ coef, Cx2<R>& a0, Cx2<R>& a1) {
+  using C2 = typename Cplx<R>::type;
+  const C2 v = P[(it.b0 + it.K) * kLanes];
   cmac(a0, __ldg(coef + it.coef), v);
   if (NC == 2) cmac(a1, __ldg(coef + it.coef + 1), v);
 }
@@ -152,24 +153,25 @@ __device__ __forceinline__ void eval_b1(const double2* __restrict__ P, const Ite
 // dense row and read a finite neighbouring entry (or the zero padding around
 // the shared-memory array), so they add exactly zero and need no branch.
 // Odd and even j accumulate separately (two independent FMA chains).
-template <int DS, int NC>
-__device__ __forceinline__ void row_sum(const double2* __restrict__ Pk, const double2 (&vs)[DS],
-                                        const double* __restrict__ crow, double2& t0, double2& t1) {
-  const double2* cr2 = reinterpret_cast<const double2*>(crow);
-  double2 o0 = make_double2(0.0, 0.0), o1 = o0;
-  double2 cc = make_double2(0.0, 0.0);
+template <typename R, int DS, int NC>
+__device__ __forceinline__ void row_sum(const Cx2<R>* __restrict__ Pk, const Cx2<R> (&vs)[DS],
+                                        const double* __restrict__ crow, Cx2<R>& t0, Cx2<R>& t1) {
+  using C2 = typename Cplx<R>::type;
+  const CoefPair* cr2 = reinterpret_cast<const CoefPair*>(crow);
+  C2 o0 = cz<C2>(), o1 = o0;
+  CoefPair cc = make_double2(0.0, 0.0);
 #pragma unroll
   for (int j = 0; j < DS; ++j) {
-    double c0, c1 = 0.0;
+    R c0, c1 = R(0);
     if (NC == 2) {
       cc = __ldg(cr2 + j);
-      c0 = cc.x;
-      c1 = cc.y;
+      c0 = R(cc.x);
+      c1 = R(cc.y);
     } else {
       if ((j & 1) == 0) cc = __ldg(cr2 + (j >> 1));
-      c0 = (j & 1) ? cc.y : cc.x;
+      c0 = R((j & 1) ? cc.y : cc.x);
     }
-    const double2 q = mul(vs[j], Pk[-j * kLanes]);
+    const C2 q = mul(vs[j], Pk[-j * kLanes]);
     if (j & 1) {
       cmac(o0, c0, q);
       if (NC == 2) cmac(o1, c1, q);
@@ -182,45 +184,46 @@ __device__ __forceinline__ void row_sum(const double2* __restrict__ Pk, const do
   if (NC == 2) t1 = add(t1, o1);
 }
 
-template <int B, int DS, int NC>
-__device__ __forceinline__ void eval_item(const double2* __restrict__ P, const Item& it,
-                                          const double* __restrict__ coef, double2& a0, double2& a1) {
+template <typename R, int B, int DS, int NC>
+__device__ __forceinline__ void eval_item(const Cx2<R>* __restrict__ P, const Item& it,
+                                          const double* __restrict__ coef, Cx2<R>& a0, Cx2<R>& a1) {
+  using C2 = typename Cplx<R>::type;
   constexpr int RW = RowWidth<DS, NC>::value;
   const int bs = B == 2 ? it.b0 : (B == 3 ? it.b1 : it.b2);  // block held in registers
   const int bl = B == 2 ? it.b1 : (B == 3 ? it.b2 : it.b3);  // last block
-  double2 vs[DS];
+  C2 vs[DS];
 #pragma unroll
   for (int j = 0; j < DS; ++j) vs[j] = P[(bs + j) * kLanes];
-  const double2* Pl = P + bl * kLanes;
+  const C2* Pl = P + bl * kLanes;
   const double* c = coef + it.coef;
   const int dl = it.dl;
   // a prefix with index sum S has tuples only for S in [smin, smax]
   const int smin = it.K - (DS - 1) - (dl - 1), smax = it.K;
   if (B == 2) {
-    row_sum<DS, NC>(Pl + it.K * kLanes, vs, c, a0, a1);
+    row_sum<R, DS, NC>(Pl + it.K * kLanes, vs, c, a0, a1);
   } else if (B == 3) {
     for (int i0 = max(0, smin); i0 < it.d0 && i0 <= smax; ++i0) {
       const int kS = it.K - i0;
-      double2 t0 = make_double2(0.0, 0.0), t1 = t0;
-      row_sum<DS, NC>(Pl + kS * kLanes, vs, c + i0 * RW, t0, t1);
-      const double2 x0 = P[(it.b0 + i0) * kLanes];
+      C2 t0 = cz<C2>(), t1 = t0;
+      row_sum<R, DS, NC>(Pl + kS * kLanes, vs, c + i0 * RW, t0, t1);
+      const C2 x0 = P[(it.b0 + i0) * kLanes];
       cfma(a0, x0, t0);
       if (NC == 2) cfma(a1, x0, t1);
     }
   } else if (DS > 7) {
     // B = 4 with a wide register block: row by row (keeps register use low)
     for (int i0 = 0; i0 < it.d0 && i0 <= smax; ++i0) {
-      double2 u0 = make_double2(0.0, 0.0), u1 = u0;
+      C2 u0 = cz<C2>(), u1 = u0;
       const int i1lo = max(0, smin - i0), i1hi = min(it.d1 - 1, smax - i0);
       for (int i1 = i1lo; i1 <= i1hi; ++i1) {
         const int kS = it.K - i0 - i1;
-        double2 t0 = make_double2(0.0, 0.0), t1 = t0;
-        row_sum<DS, NC>(Pl + kS * kLanes, vs, c + (i0 * it.d1 + i1) * RW, t0, t1);
-        const double2 x1 = P[(it.b1 + i1) * kLanes];
+        C2 t0 = cz<C2>(), t1 = t0;
+        row_sum<R, DS, NC>(Pl + kS * kLanes, vs, c + (i0 * it.d1 + i1) * RW, t0, t1);
+        const C2 x1 = P[(it.b1 + i1) * kLanes];
         cfma(u0, x1, t0);
         if (NC == 2) cfma(u1, x1, t1);
       }
-      const double2 x0 = P[(it.b0 + i0) * kLanes];
+      const C2 x0 = P[(it.b0 + i0) * kLanes];
       cfma(a0, x0, u0);
       if (NC == 2) cfma(a1, x0, u1);
     }
@@ -232,26 +235,26 @@ __device__ __forceinline__ void eval_item(const double2* __restrict__ P, const I
     constexpr int DQ = DS <= 7 ? DS : 1;  // (this branch only runs for DS <= 7)
     const int s_lo = max(0, smin), s_hi = min(it.d0 - 1 + it.d1 - 1, smax);
     for (int S = s_lo; S <= s_hi; ++S) {
-      const double2* Pk = Pl + (it.K - S) * kLanes;
-      double2 q[DQ];
+      const C2* Pk = Pl + (it.K - S) * kLanes;
+      C2 q[DQ];
 #pragma unroll
       for (int j = 0; j < DQ; ++j) q[j] = mul(vs[j], Pk[-j * kLanes]);
       const int i0lo = max(0, S - (it.d1 - 1)), i0hi = min(it.d0 - 1, S);
       for (int i0 = i0lo; i0 <= i0hi; ++i0) {
         const int i1 = S - i0;
-        const double2* cr2 = reinterpret_cast<const double2*>(c + (i0 * it.d1 + i1) * RW);
-        double2 t0 = make_double2(0.0, 0.0), t1 = t0, o0 = t0, o1 = t0;
-        double2 cc = t0;
+        const CoefPair* cr2 = reinterpret_cast<const CoefPair*>(c + (i0 * it.d1 + i1) * RW);
+        C2 t0 = cz<C2>(), t1 = t0, o0 = t0, o1 = t0;
+        CoefPair cc = make_double2(0.0, 0.0);
 #pragma unroll
         for (int j = 0; j < DQ; ++j) {
-          double c0, c1 = 0.0;
+          R c0, c1 = R(0);
           if (NC == 2) {
             cc = __ldg(cr2 + j);
-            c0 = cc.x;
-            c1 = cc.y;
+            c0 = R(cc.x);
+            c1 = R(cc.y);
           } else {
             if ((j & 1) == 0) cc = __ldg(cr2 + (j >> 1));
-            c0 = (j & 1) ? cc.y : cc.x;
+            c0 = R((j & 1) ? cc.y : cc.x);
           }
           if (j & 1) {
             cmac(o0, c0, q[j]);
@@ -261,7 +264,7 @@ __device__ __forceinline__ void eval_item(const double2* __restrict__ P, const I
             if (NC == 2) cmac(t1, c1, q[j]);
           }
         }
-        const double2 x01 = mul(P[(it.b0 + i0) * kLanes], P[(it.b1 + i1) * kLanes]);
+        const C2 x01 = mul(P[(it.b0 + i0) * kLanes], P[(it.b1 + i1) * kLanes]);
         cfma(a0, x01, add(t0, o0));
         if (NC == 2) cfma(a1, x01, add(t1, o1));
       }
@@ -269,19 +272,21 @@ __device__ __forceinline__ void eval_item(const double2* __restrict__ P, const I
   }
 }
 
-__device__ __forceinline__ void eval_dispatch(const double2* __restrict__ P, const Item& it,
-                                              const double* __restrict__ coef, double2& a0, double2& a1) {
+template <typename R>
+__device__ __forceinline__ void eval_dispatch(const Cx2<R>* __restrict__ P, const Item& it,
+                                              const double* __restrict__ coef, Cx2<R>& a0, Cx2<R>& a1) {
+  using C2 = typename Cplx<R>::type;
 #define Y3B_ITEM_CASE(B, DS, NC)                                          \
   case ((B - 1) * 7 + (DS - 1) / 2) * 2 + (NC - 1):                      \
-    eval_item<B, DS, NC>(P, it, coef, a0, a1);                           \
+    eval_item<R, B, DS, NC>(P, it, coef, a0, a1);                           \
     break;
 #define Y3B_ITEM_DS(B, DS) Y3B_ITEM_CASE(B, DS, 1) Y3B_ITEM_CASE(B, DS, 2)
 #define Y3B_ITEM_B(B) \
   Y3B_ITEM_DS(B, 1) Y3B_ITEM_DS(B, 3) Y3B_ITEM_DS(B, 5) Y3B_ITEM_DS(B, 7) Y3B_ITEM_DS(B, 9) \
   Y3B_ITEM_DS(B, 11) Y3B_ITEM_DS(B, 13)
   switch (it.sel) {
-    case 0: eval_b1<1>(P, it, coef, a0, a1); break;
-    case 1: eval_b1<2>(P, it, coef, a0, a1); break;
+    case 0: eval_b1<R, 1>(P, it, coef, a0, a1); break;
+    case 1: eval_b1<R, 2>(P, it, coef, a0, a1); break;
     Y3B_ITEM_B(2)
     Y3B_ITEM_B(3)
     Y3B_ITEM_B(4)
@@ -294,8 +299,10 @@ __device__ __forceinline__ void eval_dispatch(const double2* __restrict__ P, con
 
 // Fill shared-memory slot `slot` with every symmetric output of radial
 // channel `ch` (sym_output, ace_common.cuh).
-__device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, double2* __restrict__ sm, int W, int slot,
+template <typename R>
+__device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, Cx2<R>* __restrict__ sm, int W, int slot,
                                           int ch, int lane, int warp) {
+  using C2 = typename Cplx<R>::type;
   const int na = int(t.nmax) * W;
   const int so = int(t.sym_output_count);
   const int4* outs = reinterpret_cast<const int4*>(t.sym_outputs);
@@ -305,12 +312,14 @@ __device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, double2* __re
   }
 }
 
-template <int MODE>
+template <typename R, int MODE>
 __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
-    y3b_ace_tables t, const double2* __restrict__ A, int64_t N, double2* __restrict__ feats,
+    y3b_ace_tables t, const Cx2<R>* __restrict__ A, int64_t N, Cx2<R>* __restrict__ feats,
     const int32_t* __restrict__ species, const double* __restrict__ weights, int64_t S,
     double* __restrict__ energy) {
-  extern __shared__ double2 smem_all[];
+  using C2 = typename Cplx<R>::type;
+  extern __shared__ __align__(16) unsigned char eval_smem_raw[];
+  C2* smem_all = reinterpret_cast<C2*>(eval_smem_raw);
   __shared__ double red[kEvalWarps][kLanes];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int W = int((t.lmax + 1) * (t.lmax + 1));
@@ -319,18 +328,18 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
   const bool live = a < N;
   // zero everything (padding and slots), then the A channels
   const int total = (int(t.smem_entries) + 2 * kPadEntries) * kLanes;
-  for (int e = threadIdx.x; e < total; e += blockDim.x) smem_all[e] = make_double2(0.0, 0.0);
+  for (int e = threadIdx.x; e < total; e += blockDim.x) smem_all[e] = cz<C2>();
   __syncthreads();
-  double2* sm = smem_all + kPadEntries * kLanes;
+  C2* sm = smem_all + kPadEntries * kLanes;
   for (int e = warp; e < na; e += kEvalWarps)
-    sm[e * kLanes + lane] = live ? A[a * na + e] : make_double2(0.0, 0.0);
+    sm[e * kLanes + lane] = live ? A[a * na + e] : cz<C2>();
   const double* wz = weights;
   if (MODE == 1) {
     int z = live ? species[a] : 0;
     if (z < 0 || z >= S) z = 0;
     wz = weights + int64_t(z) * t.feature_count;
   }
-  const double2* P = sm + lane;
+  const C2* P = sm + lane;
   const int4* items = reinterpret_cast<const int4*>(t.items);
   const int4* phases = reinterpret_cast<const int4*>(t.phases);
   int cur0 = -2, cur1 = -2;
@@ -339,24 +348,24 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
     const int4 pr = __ldg(phases + ph);
     if (pr.x != cur0 || pr.y != cur1) {
       __syncthreads();  // previous phase's items are done with the slots (and A is loaded)
-      if (pr.x != cur0) fill_slot(t, sm, W, 0, pr.x, lane, warp);
-      if (pr.y != cur1 && pr.y >= 0) fill_slot(t, sm, W, 1, pr.y, lane, warp);
+      if (pr.x != cur0) fill_slot<R>(t, sm, W, 0, pr.x, lane, warp);
+      if (pr.y != cur1 && pr.y >= 0) fill_slot<R>(t, sm, W, 1, pr.y, lane, warp);
       __syncthreads();
       cur0 = pr.x;
       cur1 = pr.y;
     }
     for (int i = pr.z + warp; i < pr.w; i += kEvalWarps) {
       const Item it = load_item(items, i);
-      double2 a0 = make_double2(0.0, 0.0), a1 = a0;
-      eval_dispatch(P, it, t.item_coef, a0, a1);
+      C2 a0 = cz<C2>(), a1 = a0;
+      eval_dispatch<R>(P, it, t.item_coef, a0, a1);
       if (MODE == 0) {
         if (live) {
           feats[a * t.feature_count + it.f0] = a0;
           if (it.f1 >= 0) feats[a * t.feature_count + it.f1] = a1;
         }
       } else {
-        e_acc = fma(__ldg(wz + it.f0), a0.x, e_acc);
-        if (it.f1 >= 0) e_acc = fma(__ldg(wz + it.f1), a1.x, e_acc);
+        e_acc = fma(__ldg(wz + it.f0), double(a0.x), e_acc);
+        if (it.f1 >= 0) e_acc = fma(__ldg(wz + it.f1), double(a1.x), e_acc);
       }
     }
   }
@@ -371,8 +380,8 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
   }
 }
 
-inline size_t eval_smem_bytes(const y3b_ace_tables& t) {
-  return size_t(t.smem_entries + 2 * kPadEntries) * kLanes * sizeof(double2);
+inline size_t eval_smem_bytes(const y3b_ace_tables& t, size_t complex_size = sizeof(double2)) {
+  return size_t(t.smem_entries + 2 * kPadEntries) * kLanes * complex_size;
 }
 
 int check_tables(const y3b_ace_tables* t) {
@@ -388,15 +397,17 @@ int check_tables(const y3b_ace_tables* t) {
   return Y3B_OK;
 }
 
-template <int MODE>
-int launch_eval(const y3b_ace_tables* t, const void* A, int64_t n, double2* feats, const int32_t* species,
-                const double* weights, int64_t S, double* energy, cudaStream_t s) {
-  const size_t smem = eval_smem_bytes(*t);
-  Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_eval_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+template <typename R, int MODE>
+int launch_eval(const y3b_ace_tables* t, const void* A, int64_t n, typename Cplx<R>::type* feats,
+                const int32_t* species, const double* weights, int64_t S, double* energy, cudaStream_t s) {
+  using C2 = typename Cplx<R>::type;
+  const size_t smem = eval_smem_bytes(*t, sizeof(C2));
+  Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_eval_kernel<R, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
   const int64_t grid = (n + kLanes - 1) / kLanes;
   Y3B_CHECK_ARG(grid < (int64_t(1) << 31), "too many atoms");
-  ace_eval_kernel<MODE><<<int(grid), kLanes * kEvalWarps, smem, s>>>(*t, static_cast<const double2*>(A), n,
-                                                                      feats, species, weights, S, energy);
+  ace_eval_kernel<R, MODE><<<int(grid), kLanes * kEvalWarps, smem, s>>>(*t, static_cast<const C2*>(A), n, feats,
+                                                                       species, weights, S, energy);
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }
@@ -450,8 +461,23 @@ extern "C" int y3b_ace_features(const y3b_ace_tables* tables, const void* A, int
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && features, "null pointer argument");
-  return launch_eval<0>(tables, A, atom_count, static_cast<double2*>(features), nullptr, nullptr, 0, nullptr,
-                        as_stream(stream));
+  return launch_eval<double, 0>(tables, A, atom_count, static_cast<double2*>(features), nullptr, nullptr, 0,
+                                nullptr, as_stream(stream));
+}
+
+extern "C" int y3b_ace_features_typed(int dtype, const y3b_ace_tables* tables, const void* A, int64_t atom_count,
+                                      void* features, void* stream) {
+  if (int rc = check_tables(tables)) return rc;
+  Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
+  if (atom_count == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(A && features, "null pointer argument");
+  if (dtype == Y3B_C128)
+    return launch_eval<double, 0>(tables, A, atom_count, static_cast<double2*>(features), nullptr, nullptr, 0,
+                                  nullptr, as_stream(stream));
+  if (dtype == Y3B_C64)
+    return launch_eval<float, 0>(tables, A, atom_count, static_cast<float2*>(features), nullptr, nullptr, 0,
+                                 nullptr, as_stream(stream));
+  return fail(Y3B_ERR_ARGUMENT, "ace_features: dtype must be C64 or C128 (got %d)", dtype);
 }
 
 extern "C" int y3b_ace_energy(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
@@ -461,6 +487,6 @@ extern "C" int y3b_ace_energy(const y3b_ace_tables* tables, const void* A, int64
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && weights && energy && species_count > 0, "null pointer argument");
-  return launch_eval<1>(tables, A, atom_count, nullptr, species, weights, species_count, energy,
-                        as_stream(stream));
+  return launch_eval<double, 1>(tables, A, atom_count, nullptr, species, weights, species_count, energy,
+                                as_stream(stream));
 }

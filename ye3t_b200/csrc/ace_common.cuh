@@ -20,15 +20,34 @@ __device__ __forceinline__ Item load_item(const int4* __restrict__ items, int64_
   return it;
 }
 
+// Complex type of a real type, and its zero.
+template <typename R> struct Cplx;
+template <> struct Cplx<float> { using type = float2; };
+template <> struct Cplx<double> { using type = double2; };
+template <typename R> using Cx2 = typename Cplx<R>::type;
+using CoefPair = double2;  // two fp64 coefficients read with one 16-byte load
+
+template <typename C2> __device__ __forceinline__ C2 cz();
+template <> __device__ __forceinline__ float2 cz<float2>() { return make_float2(0.f, 0.f); }
+template <> __device__ __forceinline__ double2 cz<double2>() { return make_double2(0.0, 0.0); }
+
 __device__ __forceinline__ void cmac(double2& acc, double c, double2 v) {
   acc.x = fma(c, v.x, acc.x);
   acc.y = fma(c, v.y, acc.y);
+}
+__device__ __forceinline__ void cmac(float2& acc, float c, float2 v) {
+  acc.x = fmaf(c, v.x, acc.x);
+  acc.y = fmaf(c, v.y, acc.y);
 }
 
 // acc += x * t (complex multiply-add)
 __device__ __forceinline__ void cfma(double2& acc, double2 x, double2 t) {
   acc.x = fma(x.x, t.x, fma(-x.y, t.y, acc.x));
   acc.y = fma(x.x, t.y, fma(x.y, t.x, acc.y));
+}
+__device__ __forceinline__ void cfma(float2& acc, float2 x, float2 t) {
+  acc.x = fmaf(x.x, t.x, fmaf(-x.y, t.y, acc.x));
+  acc.y = fmaf(x.x, t.y, fmaf(x.y, t.x, acc.y));
 }
 
 // Coefficient row of one prefix: NC doubles per j, padded to an even count so
@@ -43,18 +62,20 @@ struct RowWidth {
 // input component multiplied in increasing component order
 // (ye3t_runtime_core.cpp:5279).  Factors are 4 x u8 component indices
 // (repeated for powers, 255 = unused).
-__device__ __forceinline__ double2 sym_output(const y3b_ace_tables& t, int tb, int te, const double2* x,
-                                              int stride) {
-  double2 acc = make_double2(0.0, 0.0);
+template <typename C2>
+__device__ __forceinline__ C2 sym_output(const y3b_ace_tables& t, int tb, int te, const C2* x, int stride) {
+  using R = decltype(C2{}.x);
+  C2 acc = cz<C2>();
   for (int q = tb; q < te; ++q) {
     const uint32_t f = __ldg(t.sym_term_factors + q);
-    double2 m = make_double2(__ldg(t.sym_term_coeff + q), 0.0);
+    C2 m = cz<C2>();
+    m.x = R(__ldg(t.sym_term_coeff + q));
     int k = 0;
     while (k < 4) {
       const int ci = (f >> (8 * k)) & 255;
       if (ci == 255) break;
-      const double2 xv = x[ci * stride];
-      double2 pw = xv;
+      const C2 xv = x[ci * stride];
+      C2 pw = xv;
       ++k;
       while (k < 4 && int((f >> (8 * k)) & 255) == ci) {
         pw = mul(pw, xv);
