@@ -96,3 +96,25 @@ def test_partial_forces_sum_to_gather_forces(golden):
         g = ev.edge_grad(pos, sp, box, row, nbr, G, begin=b)
         ev.partial_forces_from_edges(row, nbr, g, b, N, out=acc)
     np.testing.assert_allclose(acc.cpu().numpy(), F.cpu().numpy(), rtol=1e-10, atol=1e-12)
+
+
+def test_energy_grad_many_ctas_matches_forward_and_repeats(golden):
+    """Thousands of CTAs (races between loading A and the item walk, or between
+    warps adding to G, would show here): the adjoint's energies equal the
+    forward kernel's and a second run agrees with the first."""
+    small = golden("ace_small")
+    rng = np.random.default_rng(11)
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    N = 8192
+    box = (N / 0.05) ** (1 / 3)
+    pos = torch.as_tensor(rng.uniform(0, box, size=(N, 3)), device=DEV)
+    sp = torch.as_tensor(rng.integers(0, 3, size=N), device=DEV)
+    row, nbr = ev.neighbor_list(pos, box)
+    A = ev.density(pos, sp, box, row, nbr)
+    e_fwd = ev.energy_from_density(A, sp).cpu().numpy()
+    e1, G1 = ev.energy_grad(A, sp)
+    e2, G2 = ev.energy_grad(A, sp)
+    np.testing.assert_allclose(e1.cpu().numpy(), e_fwd, rtol=1e-11, atol=1e-11)
+    np.testing.assert_allclose(e2.cpu().numpy(), e_fwd, rtol=1e-11, atol=1e-11)
+    scale = G1.abs().max().item()
+    assert (G1 - G2).abs().max().item() <= 1e-12 * scale

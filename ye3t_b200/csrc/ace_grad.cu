@@ -183,30 +183,33 @@ __device__ __forceinline__ void stage_zero(const Ctx& c, int lo, int hi) {
   for (int k = lo; k < hi; ++k) sts128(c.stage + k * (32 * 16), make_double2(0.0, 0.0));
 }
 
-// The register block is walked in chunks of kCh indices j (runtime width jn
-// <= kCh); every item shape then runs through one code path per block count,
-// which keeps the kernel's register demand within the register file.
-constexpr int kCh = 4;
+// The register block is walked in chunks of CH indices j (runtime width jn <=
+// CH); the adjoint's item classes each run in their own kernel with CH equal
+// to the class's register-block size, so a chunk is the whole block.
 
-// Readout-weighted coefficients j0 .. j0 + kCh - 1 of a row (zero past jn):
-// wc[u] = w0 C[j0 + u, 0] + w1 C[j0 + u, 1]; rows are 16-byte aligned and j0
-// is a multiple of kCh, so pairs are read with 16-byte loads.
+// Readout-weighted coefficients j0 .. j0 + CH - 1 of a row (zero past jn):
+// wc[u] = w0 C[j0 + u, 0] + w1 C[j0 + u, 1]; rows are 16-byte aligned, so for
+// even j0 single-component pairs are read with 16-byte loads.
+template <int CH>
 __device__ __forceinline__ void wchunk(const double* __restrict__ crow, int nc, int j0, int jn, double w0, double w1,
-                                       double (&wc)[kCh]) {
+                                       double (&wc)[CH]) {
   const double2* c2 = reinterpret_cast<const double2*>(crow);
   if (nc == 2) {
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) {
+    for (int u = 0; u < CH; ++u) {
       const double2 cc = u < jn ? __ldg(c2 + j0 + u) : make_double2(0.0, 0.0);
       wc[u] = fma(w1, cc.y, w0 * cc.x);
     }
-  } else {
+  } else if ((j0 & 1) == 0) {
 #pragma unroll
-    for (int u = 0; u < kCh; u += 2) {
+    for (int u = 0; u < CH; u += 2) {
       const double2 cc = u < jn ? __ldg(c2 + (j0 + u) / 2) : make_double2(0.0, 0.0);
       wc[u] = w0 * cc.x;
-      wc[u + 1] = u + 1 < jn ? w0 * cc.y : 0.0;
+      if (u + 1 < CH) wc[u + 1] = u + 1 < jn ? w0 * cc.y : 0.0;
     }
+  } else {
+#pragma unroll
+    for (int u = 0; u < CH; ++u) wc[u] = u < jn ? w0 * __ldg(crow + j0 + u) : 0.0;
   }
 }
 
@@ -219,20 +222,21 @@ __device__ __forceinline__ double adj1(const Ctx& c, const Item& it, int nc, con
 }
 
 // Two blocks (register block s of ds indices, last block l = K - j): one
-// row.  Per chunk, gs is staged at [0, kCh) and gl at [7, 7 + kCh).
+// row.  Per chunk of CH indices, gs and gl are added to G from registers.
+template <int CH>
 __device__ __forceinline__ double adj2(const Ctx& c, const Item& it, int ds, int nc, const double* __restrict__ coef,
                                        double w0, double w1, bool mute) {
   double e = 0.0;
   const int bs = it.b0, bl = it.b1, K = it.K, dl = it.dl;
   const double* cr = coef + it.coef;
 #pragma unroll 1
-  for (int j0 = 0; j0 < ds; j0 += kCh) {
-    const int jn = min(kCh, ds - j0);
-    double wc[kCh];
-    wchunk(cr, nc, j0, jn, w0, w1, wc);
-    double2 gs[kCh], gl[kCh];
+  for (int j0 = 0; j0 < ds; j0 += CH) {
+    const int jn = min(CH, ds - j0);
+    double wc[CH];
+    wchunk<CH>(cr, nc, j0, jn, w0, w1, wc);
+    double2 gs[CH], gl[CH];
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) {
+    for (int u = 0; u < CH; ++u) {
       gs[u] = gl[u] = make_double2(0.0, 0.0);
       if (u < jn) {
         // out-of-block last indices read finite neighbours; their coefficient is 0
@@ -243,9 +247,9 @@ __device__ __forceinline__ double adj2(const Ctx& c, const Item& it, int ds, int
       }
     }
     if (!mute) {
-      g_add<kCh, 1>(c, bs + j0, 0, jn, gs);
+      g_add<CH, 1>(c, bs + j0, 0, jn, gs);
       // gl[u] belongs to last-block index K - j0 - u
-      g_add<kCh, -1>(c, bl + K - j0, max(0, K - j0 - dl + 1), min(jn, K - j0 + 1), gl);
+      g_add<CH, -1>(c, bl + K - j0, max(0, K - j0 - dl + 1), min(jn, K - j0 + 1), gl);
     }
   }
   return e;
@@ -254,6 +258,7 @@ __device__ __forceinline__ double adj2(const Ctx& c, const Item& it, int ds, int
 // Three blocks: rows i0 (prefix block 0), register block s, last block
 // l = K - i0 - j (dl <= kStage, gl accumulates in the staging area).  The
 // prefix gradient of a row is T_i0, added to G per row and chunk.
+template <int CH>
 __device__ __forceinline__ double adj3(const Ctx& c, const Item& it, int ds, int nc, const double* __restrict__ coef,
                                        double w0, double w1, bool mute) {
   double e = 0.0;
@@ -264,26 +269,26 @@ __device__ __forceinline__ double adj3(const Ctx& c, const Item& it, int ds, int
   const double* cb = coef + it.coef;
   stage_zero(c, 0, dl);
 #pragma unroll 1
-  for (int j0 = 0; j0 < ds; j0 += kCh) {
-    const int jn = min(kCh, ds - j0);
-    double2 vs[kCh], gs[kCh];
+  for (int j0 = 0; j0 < ds; j0 += CH) {
+    const int jn = min(CH, ds - j0);
+    double2 vs[CH], gs[CH];
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) {
+    for (int u = 0; u < CH; ++u) {
       vs[u] = u < jn ? vat(c, bs + j0 + u) : make_double2(0.0, 0.0);
       gs[u] = make_double2(0.0, 0.0);
     }
     // w[u] belongs to last-block index K - r - j0 - u (moves by one per row)
-    double2 w[kCh];
+    double2 w[CH];
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) w[u] = make_double2(0.0, 0.0);
+    for (int u = 0; u < CH; ++u) w[u] = make_double2(0.0, 0.0);
 #pragma unroll 1
     for (int r = r_lo; r <= r_hi; ++r) {
-      double wc[kCh];
-      wchunk(cb + r * rw, nc, j0, jn, w0, w1, wc);
+      double wc[CH];
+      wchunk<CH>(cb + r * rw, nc, j0, jn, w0, w1, wc);
       const double2 x0 = vat(c, b0 + r);
       double2 T = make_double2(0.0, 0.0);
 #pragma unroll
-      for (int u = 0; u < kCh; ++u) {
+      for (int u = 0; u < CH; ++u) {
         // out-of-block last indices read finite neighbours; their coefficient is 0
         const double2 vl = vat(c, bl + K - r - j0 - u);
         cmac(T, wc[u], mul(vs[u], vl));
@@ -296,15 +301,15 @@ __device__ __forceinline__ double adj3(const Ctx& c, const Item& it, int ds, int
       const int kf = K - r - j0;
       if (kf >= 0 && kf < dl) stage_acc(c, kf, w[0]);
 #pragma unroll
-      for (int u = 0; u + 1 < kCh; ++u) w[u] = w[u + 1];
-      w[kCh - 1] = make_double2(0.0, 0.0);
+      for (int u = 0; u + 1 < CH; ++u) w[u] = w[u + 1];
+      w[CH - 1] = make_double2(0.0, 0.0);
     }
 #pragma unroll
-    for (int u = 0; u + 1 < kCh; ++u) {
+    for (int u = 0; u + 1 < CH; ++u) {
       const int k = K - r_hi - 1 - j0 - u;
       if (k >= 0 && k < dl) stage_acc(c, k, w[u]);
     }
-    if (!mute) g_add<kCh, 1>(c, bs + j0, 0, jn, gs);
+    if (!mute) g_add<CH, 1>(c, bs + j0, 0, jn, gs);
   }
   if (!mute) stage_flush(c, bl, 0, dl);
   return e;
@@ -318,6 +323,7 @@ __device__ __forceinline__ double adj3(const Ctx& c, const Item& it, int ds, int
 //      staging area ([0, 7) and [7, 14));
 //   B: R_j = sum over the diagonal's rows of c_j x0 x1; gs[j] += R_j vl
 //      (registers, per chunk) and gl[K - S - j] += R_j vs_j (staged at [0, dl)).
+template <int CH>
 __device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int nc, const double* __restrict__ coef,
                                        double w0, double w1, bool mute) {
   double e = 0.0;
@@ -330,25 +336,25 @@ __device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int
   stage_zero(c, 0, d0);
   stage_zero(c, 7, 7 + d1);
 #pragma unroll 1
-  for (int j0 = 0; j0 < ds; j0 += kCh) {
-    const int jn = min(kCh, ds - j0);
-    double2 vs[kCh];
+  for (int j0 = 0; j0 < ds; j0 += CH) {
+    const int jn = min(CH, ds - j0);
+    double2 vs[CH];
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) vs[u] = u < jn ? vat(c, bs + j0 + u) : make_double2(0.0, 0.0);
+    for (int u = 0; u < CH; ++u) vs[u] = u < jn ? vat(c, bs + j0 + u) : make_double2(0.0, 0.0);
 #pragma unroll 1
     for (int S = s_lo; S <= s_hi; ++S) {
-      double2 q[kCh];
+      double2 q[CH];
 #pragma unroll
-      for (int u = 0; u < kCh; ++u) q[u] = mul(vs[u], vat(c, bl + K - S - j0 - u));
+      for (int u = 0; u < CH; ++u) q[u] = mul(vs[u], vat(c, bl + K - S - j0 - u));
       const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
 #pragma unroll 1
       for (int i0 = i0a; i0 <= i0b; ++i0) {
         const int i1 = S - i0;
-        double wc[kCh];
-        wchunk(cb + (i0 * d1 + i1) * rw, nc, j0, jn, w0, w1, wc);
+        double wc[CH];
+        wchunk<CH>(cb + (i0 * d1 + i1) * rw, nc, j0, jn, w0, w1, wc);
         double2 T = make_double2(0.0, 0.0);
 #pragma unroll
-        for (int u = 0; u < kCh; ++u) cmac(T, wc[u], q[u]);
+        for (int u = 0; u < CH; ++u) cmac(T, wc[u], q[u]);
         const double2 x0 = vat(c, b0 + i0), x1 = vat(c, b1 + i1);
         const double2 x01 = mul(x0, x1);
         e += x01.x * T.x - x01.y * T.y;
@@ -363,51 +369,51 @@ __device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int
   }
   stage_zero(c, 0, dl);
 #pragma unroll 1
-  for (int j0 = 0; j0 < ds; j0 += kCh) {
-    const int jn = min(kCh, ds - j0);
-    double2 vs[kCh], gs[kCh];
+  for (int j0 = 0; j0 < ds; j0 += CH) {
+    const int jn = min(CH, ds - j0);
+    double2 vs[CH], gs[CH];
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) {
+    for (int u = 0; u < CH; ++u) {
       vs[u] = u < jn ? vat(c, bs + j0 + u) : make_double2(0.0, 0.0);
       gs[u] = make_double2(0.0, 0.0);
     }
     // w[u] belongs to last-block index K - S - j0 - u; after diagonal S no
     // later one reaches index K - S - j0, which is added to the staging area
-    double2 w[kCh];
+    double2 w[CH];
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) w[u] = make_double2(0.0, 0.0);
+    for (int u = 0; u < CH; ++u) w[u] = make_double2(0.0, 0.0);
 #pragma unroll 1
     for (int S = s_lo; S <= s_hi; ++S) {
-      double2 R[kCh];
+      double2 R[CH];
 #pragma unroll
-      for (int u = 0; u < kCh; ++u) R[u] = make_double2(0.0, 0.0);
+      for (int u = 0; u < CH; ++u) R[u] = make_double2(0.0, 0.0);
       const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
 #pragma unroll 1
       for (int i0 = i0a; i0 <= i0b; ++i0) {
         const int i1 = S - i0;
-        double wc[kCh];
-        wchunk(cb + (i0 * d1 + i1) * rw, nc, j0, jn, w0, w1, wc);
+        double wc[CH];
+        wchunk<CH>(cb + (i0 * d1 + i1) * rw, nc, j0, jn, w0, w1, wc);
         const double2 x01 = mul(vat(c, b0 + i0), vat(c, b1 + i1));
 #pragma unroll
-        for (int u = 0; u < kCh; ++u) cmac(R[u], wc[u], x01);
+        for (int u = 0; u < CH; ++u) cmac(R[u], wc[u], x01);
       }
 #pragma unroll
-      for (int u = 0; u < kCh; ++u) {
+      for (int u = 0; u < CH; ++u) {
         cfma(gs[u], R[u], vat(c, bl + K - S - j0 - u));
         cfma(w[u], R[u], vs[u]);
       }
       const int kf = K - S - j0;
       if (kf >= 0 && kf < dl) stage_acc(c, kf, w[0]);
 #pragma unroll
-      for (int u = 0; u + 1 < kCh; ++u) w[u] = w[u + 1];
-      w[kCh - 1] = make_double2(0.0, 0.0);
+      for (int u = 0; u + 1 < CH; ++u) w[u] = w[u + 1];
+      w[CH - 1] = make_double2(0.0, 0.0);
     }
 #pragma unroll
-    for (int u = 0; u + 1 < kCh; ++u) {
+    for (int u = 0; u + 1 < CH; ++u) {
       const int k = K - s_hi - 1 - j0 - u;
       if (k >= 0 && k < dl) stage_acc(c, k, w[u]);
     }
-    if (!mute) g_add<kCh, 1>(c, bs + j0, 0, jn, gs);
+    if (!mute) g_add<CH, 1>(c, bs + j0, 0, jn, gs);
   }
   if (!mute) stage_flush(c, bl, 0, dl);
   return e;
@@ -449,19 +455,32 @@ __device__ __noinline__ double adj_generic(const Ctx c, const Item it, int B, in
   return e;
 }
 
-__device__ __forceinline__ double adj_dispatch(const Ctx& c, const Item& it, const double* __restrict__ coef,
-                                               double w0, double w1, bool mute) {
+// Item classes of the adjoint (packing.grad_class assigns them); each class
+// runs in its own kernel so that its item paths keep the register file, and
+// a chunk of the register block is the whole block for the large classes.
+// Every launch reloads A and redoes the symmetric slots of the phases it
+// touches, so the small item shapes share one class:
+//   0: 1 and 2 blocks, 3 and 4 blocks with a register block of <= 3, and
+//      anything the unrolled paths do not cover (generic path);
+//   1 / 2: 3 blocks with a register block of 5 / 7;
+//   3 / 4: 4 blocks with a register block of 5 / 7.
+constexpr int kGradClasses = 5;
+
+template <int CLS>
+__device__ __forceinline__ double adj_class(const Ctx& c, const Item& it, const double* __restrict__ coef,
+                                            double w0, double w1, bool mute) {
   const int nc = (it.sel & 1) + 1, ds = 2 * ((it.sel >> 1) % 7) + 1, B = (it.sel >> 1) / 7 + 1;
-  switch (B) {
-    case 1: return adj1(c, it, nc, coef, w0, w1, mute);
-    case 2: return adj2(c, it, ds, nc, coef, w0, w1, mute);
-    case 3:
-      if (it.dl <= kStage) return adj3(c, it, ds, nc, coef, w0, w1, mute);
-      break;
-    case 4:
-      if (it.d0 <= 7 && it.d1 <= 7 && it.dl <= kStage) return adj4(c, it, ds, nc, coef, w0, w1, mute);
-      break;
-    default: return 0.0;
+  const bool fits3 = B == 3 && it.dl <= kStage;
+  const bool fits4 = B == 4 && it.d0 <= 7 && it.d1 <= 7 && it.dl <= kStage;
+  if (CLS == 0) {
+    if (B == 1) return adj1(c, it, nc, coef, w0, w1, mute);
+    if (B == 2) return adj2<8>(c, it, ds, nc, coef, w0, w1, mute);
+    if (fits3 && ds <= 3) return adj3<3>(c, it, ds, nc, coef, w0, w1, mute);
+    if (fits4 && ds <= 3) return adj4<3>(c, it, ds, nc, coef, w0, w1, mute);
+  } else {
+    constexpr int CH = (CLS == 1 || CLS == 3) ? 5 : 7;
+    if ((CLS == 1 || CLS == 2) && fits3 && ds <= CH) return adj3<CH>(c, it, ds, nc, coef, w0, w1, mute);
+    if ((CLS == 3 || CLS == 4) && fits4 && ds <= CH) return adj4<CH>(c, it, ds, nc, coef, w0, w1, mute);
   }
   return adj_generic(c, it, B, ds, nc, coef, w0, w1, mute);
 }
@@ -519,17 +538,20 @@ __device__ __forceinline__ void grad_clear_slot(double* __restrict__ Gr, double*
     Gr[e] = Gi[e] = 0.0;
 }
 
+template <int CLS>
 __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_tables t, const double2* __restrict__ A,
                                                                    int64_t N, const int32_t* __restrict__ species,
                                                                    const double* __restrict__ weights, int64_t S,
                                                                    double* __restrict__ energy,
                                                                    double2* __restrict__ dEdA,
-                                                                   int32_t* __restrict__ status) {
+                                                                   int32_t* __restrict__ status, int accumulate) {
   extern __shared__ double2 gsm[];
   __shared__ double red[kGWarps][kGA];
+  // classes 3 and 4 (4-block items) read A entries only: no symmetric slots
+  constexpr bool kSlots = CLS <= 2;
   const int W = int((t.lmax + 1) * (t.lmax + 1));
   const int na = int(t.nmax) * W, so = int(t.sym_output_count);
-  const int E = int(t.smem_entries);
+  const int E = kSlots ? int(t.smem_entries) : na;
   const int rows = E + 2 * kGPad;
   double* Gr = reinterpret_cast<double*>(gsm + rows * kGA);
   double* Gi = Gr + E * kGA;
@@ -544,6 +566,7 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
     for (int e = threadIdx.x / kGA; e < na; e += blockDim.x / kGA)
       val[e * kGA + la] = aa < N ? A[aa * na + e] : make_double2(0.0, 0.0);
   }
+  __syncthreads();  // A is in shared memory before any item reads it
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int atom = lane & (kGA - 1), grp = lane / kGA;
   const int64_t a = blockIdx.x * int64_t(kGA) + atom;
@@ -565,7 +588,10 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
 #pragma unroll 1
   for (int ph = 0; ph < t.phase_count; ++ph) {
     const int4 pr = __ldg(phases + ph);
-    if (pr.x != cur0 || pr.y != cur1) {
+    const int* goff = t.group_offsets + CLS * (t.phase_count + 1);
+    const int gb = __ldg(goff + ph), ge = __ldg(goff + ph + 1);
+    if (gb == ge) continue;  // no items of this class in the phase
+    if (kSlots && (pr.x != cur0 || pr.y != cur1)) {
       __syncthreads();  // the previous phase is done with the slots (and A is loaded)
       if (pr.x != cur0 && cur0 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 0, cur0);
       if (pr.y != cur1 && cur1 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 1, cur1);
@@ -582,21 +608,20 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
       cur0 = pr.x;
       cur1 = pr.y;
     }
-    const int ge = __ldg(t.group_offsets + ph + 1);
 #pragma unroll 1
-    for (int g = __ldg(t.group_offsets + ph) + warp; g < ge; g += kGWarps) {
+    for (int g = gb + warp; g < ge; g += kGWarps) {
       const int2 ig = __ldg(groups + g);
       const int mine = grp == 0 ? ig.x : ig.y;
       const bool mute = mine < 0;  // odd item out: the second half runs the first item unweighted, adding nothing
       const Item it = load_item(items, mute ? ig.x : mine);
       const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
       const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
-      e_acc += adj_dispatch(c, it, t.item_coef, w0, w1, mute);
+      e_acc += adj_class<CLS>(c, it, t.item_coef, w0, w1, mute);
     }
   }
   __syncthreads();
-  if (cur0 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 0, cur0);
-  if (cur1 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 1, cur1);
+  if (kSlots && cur0 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 0, cur0);
+  if (kSlots && cur1 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 1, cur1);
   e_acc += __shfl_xor_sync(0xffffffffu, e_acc, 16);
   if (grp == 0) red[warp][atom] = e_acc;
   __syncthreads();
@@ -604,13 +629,17 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
     const int64_t aa = blockIdx.x * int64_t(kGA) + threadIdx.x;
     double s = 0.0;
     for (int w = 0; w < kGWarps; ++w) s += red[w][threadIdx.x];
-    if (aa < N) energy[aa] = s;
+    if (aa < N) energy[aa] = accumulate ? energy[aa] + s : s;
   }
   {
     const int la = threadIdx.x % kGA;
     const int64_t aa = blockIdx.x * int64_t(kGA) + la;
     for (int e = threadIdx.x / kGA; e < na; e += blockDim.x / kGA)
-      if (aa < N) dEdA[aa * na + e] = make_double2(Gr[e * kGA + la], Gi[e * kGA + la]);
+      if (aa < N) {
+        double2 g = make_double2(Gr[e * kGA + la], Gi[e * kGA + la]);
+        if (accumulate) g = add(g, dEdA[aa * na + e]);
+        dEdA[aa * na + e] = g;
+      }
   }
 }
 
@@ -803,18 +832,35 @@ extern "C" int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, 
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && weights && energy && dEdA && species_count > 0, "null pointer argument");
-  const size_t smem = size_t(tables->smem_entries + 2 * kGPad) * kGA * sizeof(double2) +
-                      size_t(2) * size_t(tables->smem_entries) * kGA * sizeof(double) +
-                      size_t(kGWarps) * kStage * 32 * sizeof(double2);
+  auto smem_for = [&](int64_t entries) {
+    return size_t(entries + 2 * kGPad) * kGA * sizeof(double2) + size_t(2) * size_t(entries) * kGA * sizeof(double) +
+           size_t(kGWarps) * kStage * 32 * sizeof(double2);
+  };
+  const size_t smem = smem_for(tables->smem_entries);
+  const size_t smem_a = smem_for(tables->nmax * (tables->lmax + 1) * (tables->lmax + 1));
   Y3B_CHECK_ARG(smem <= 224 * 1024, "bundle needs %lld bytes of shared memory for the adjoint (max 224 KB)",
                 (long long)smem);
-  Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   const int64_t grid = (atom_count + kGA - 1) / kGA;
   Y3B_CHECK_ARG(grid < (int64_t(1) << 31), "too many atoms");
-  ace_grad_kernel<<<int(grid), 32 * kGWarps, smem, as_stream(stream)>>>(
-      *tables, static_cast<const double2*>(A), atom_count, species, weights, species_count, energy,
-      static_cast<double2*>(dEdA), status);
+  cudaStream_t s = as_stream(stream);
+  // one launch per item class (stream-ordered); the first writes dE/dA and
+  // the energies, the others add to them
+#define Y3B_GRAD_LAUNCH(CLS)                                                                              \
+  Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_grad_kernel<CLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                    int(CLS <= 2 ? smem : smem_a)));                                      \
+  ace_grad_kernel<CLS><<<int(grid), 32 * kGWarps, CLS <= 2 ? smem : smem_a, s>>>(                         \
+      *tables, static_cast<const double2*>(A),                                                            \
+                                                             atom_count, species, weights, species_count, \
+                                                             energy, static_cast<double2*>(dEdA), status, \
+                                                             CLS > 0);                                    \
   Y3B_LAUNCH_CHECK();
+  Y3B_GRAD_LAUNCH(0)
+  Y3B_GRAD_LAUNCH(1)
+  Y3B_GRAD_LAUNCH(2)
+  Y3B_GRAD_LAUNCH(3)
+  Y3B_GRAD_LAUNCH(4)
+#undef Y3B_GRAD_LAUNCH
+  static_assert(kGradClasses == 5, "one launch per class");
   return Y3B_OK;
 }
 

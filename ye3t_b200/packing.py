@@ -399,29 +399,55 @@ def item_flops_per_atom(items: np.ndarray) -> float:
 
 
 GRAD_GROUP = 2
+GRAD_CLASSES = 5
+GRAD_STAGE = 14  # staged gradient entries per lane in the adjoint kernel
 
 
-def _grad_groups(items: np.ndarray, phases: np.ndarray):
-    """Item pairs of the adjoint kernel, per phase.
+def grad_class(row, a_entries: Optional[int] = None) -> int:
+    """Adjoint item class (one kernel launch each, csrc/ace_grad.cu adj_class).
+
+    0: one and two blocks, three and four blocks with a register block of at
+    most 3 indices, and shapes the unrolled paths do not cover (wide register
+    blocks, long last blocks); 1 / 2: three blocks with a register block of 5
+    / 7; 3 / 4: four blocks with a register block of 5 / 7 whose blocks are
+    all A entries (``< a_entries``; those kernels hold no symmetric slots).
+    """
+    sel, d0, d1, dl = int(row[0]), int(row[1]), int(row[2]), int(row[3])
+    B = (sel // 2) // 7 + 1
+    ds = 2 * ((sel // 2) % 7) + 1
+    if B <= 2 or ds <= 3 or ds > 7 or dl > GRAD_STAGE or (B == 4 and (d0 > 7 or d1 > 7)):
+        return 0
+    if B == 4 and a_entries is not None and any(int(row[8 + b]) + dim > a_entries
+                                                for b, dim in enumerate((d0, d1, ds, dl))):
+        return 0
+    return (1 if B == 3 else 3) + (0 if ds <= 5 else 1)
+
+
+def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
+    """Item pairs of the adjoint kernel, per item class and phase.
 
     Each half-warp runs one item; pairing two items of one shape (dispatch
     code, loop extents, K) keeps the warp's control flow identical.  Within a
     shape, items sharing a coefficient table stay adjacent.  Returns
-    ``groups [P, 2]`` (-1 for a shape's odd item out) and
-    ``group_offsets [phase_count + 1]``.
+    ``groups [P, 2]`` (-1 for a shape's odd item out), ordered by class then
+    phase, and ``group_offsets [GRAD_CLASSES, phase_count + 1]`` (flattened).
     """
-    groups, offsets = [], [0]
-    for _, _, begin, end in phases.tolist():
-        shapes = {}
-        for i in range(begin, end):
-            shapes.setdefault(tuple(int(v) for v in items[i, :5]), []).append(i)
-        for key in sorted(shapes):
-            idx = sorted(shapes[key], key=lambda i: (int(items[i, 5]), int(items[i, 6])))
-            for u in range(0, len(idx), GRAD_GROUP):
-                g = idx[u:u + GRAD_GROUP]
-                groups.append(g + [-1] * (GRAD_GROUP - len(g)))
-        offsets.append(len(groups))
-    return (np.asarray(groups, dtype=np.int32).reshape(-1, GRAD_GROUP), np.asarray(offsets, dtype=np.int32))
+    groups = []
+    offsets = np.zeros((GRAD_CLASSES, phases.shape[0] + 1), dtype=np.int32)
+    for cls in range(GRAD_CLASSES):
+        for ph, (_, _, begin, end) in enumerate(phases.tolist()):
+            offsets[cls, ph] = len(groups)
+            shapes = {}
+            for i in range(begin, end):
+                if grad_class(items[i], a_entries) == cls:
+                    shapes.setdefault(tuple(int(v) for v in items[i, :5]), []).append(i)
+            for key in sorted(shapes):
+                idx = sorted(shapes[key], key=lambda i: (int(items[i, 5]), int(items[i, 6])))
+                for u in range(0, len(idx), GRAD_GROUP):
+                    g = idx[u:u + GRAD_GROUP]
+                    groups.append(g + [-1] * (GRAD_GROUP - len(g)))
+        offsets[cls, -1] = len(groups)
+    return np.asarray(groups, dtype=np.int32).reshape(-1, GRAD_GROUP), offsets.reshape(-1)
 
 
 def _sym_grad_terms(sym_out_rows, s_fac, s_co, W):
@@ -490,7 +516,7 @@ def pack_bundle(bundle: ACEBundle, device) -> PackedBundle:
         fo += p.component_count
         terms_per_atom += p.term_count
         term_blocks_per_atom += p.term_count * p.block_count
-    groups, group_offsets = _grad_groups(items, phases)
+    groups, group_offsets = _grad_groups(items, phases, nmax * W)
     unpacked = [[(f >> (8 * k)) & 255 for k in range(4)] for f in np.asarray(s_fac, dtype=np.uint32).tolist()]
     sg_off, sg_index, sg_coeff = _sym_grad_terms(sym_out_rows, unpacked, s_co, W)
     arrays_np = {
