@@ -40,24 +40,18 @@ constexpr int kStage = 14;  // staged gradient entries per lane (two blocks of <
 #define Y3B_GRAD_BATCH 2
 #endif
 
-// Shared-window (32-bit) byte addresses of this lane's data.
+// This lane's data in shared memory.  V and the staging area are read and
+// written with ordinary loads and stores (V is read-only during the item walk,
+// the staging area is private to the lane), so the compiler schedules them
+// freely; G is only touched by the compare-and-swap batches, through
+// shared-window (32-bit) byte addresses.
 struct Ctx {
-  uint32_t V;        // entry e of this lane's atom at V + e * kGA * 16
+  const double2* V;  // V[e * kGA]: entry e of this lane's atom
   uint32_t Gr, Gi;   // its gradient planes, entry e at + e * kGA * 8
-  uint32_t stage;    // this lane's staged entry k at stage + k * 32 * 16
+  double2* stage;    // stage[k * 32]: this lane's staged entry k
 };
 
-__device__ __forceinline__ double2 lds128(uint32_t a) {
-  double2 v;
-  asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "r"(a));
-  return v;
-}
-
-__device__ __forceinline__ void sts128(uint32_t a, double2 v) {
-  asm volatile("st.shared.v2.f64 [%0], {%1, %2};" ::"r"(a), "d"(v.x), "d"(v.y));
-}
-
-__device__ __forceinline__ double2 vat(const Ctx& c, int e) { return lds128(c.V + e * (kGA * 16)); }
+__device__ __forceinline__ double2 vat(const Ctx& c, int e) { return c.V[e * kGA]; }
 
 __device__ __forceinline__ double2 cscale(double s, double2 v) { return make_double2(s * v.x, s * v.y); }
 
@@ -155,8 +149,7 @@ __device__ __forceinline__ void stage_flush_impl(const Ctx& c, int base, int off
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const int k = k0 + u;
-        v[u] = (k + off < kStage && k >= lo && k < hi) ? lds128(c.stage + (off + k) * (32 * 16))
-                                                       : make_double2(0.0, 0.0);
+        v[u] = (k + off < kStage && k >= lo && k < hi) ? c.stage[(off + k) * 32] : make_double2(0.0, 0.0);
       }
       g_add_batch<kBatch, STEP, 0, kBatch>(c, ar + STEP * k0 * (kGA * 8), ai + STEP * k0 * (kGA * 8), lo - k0,
                                            hi - k0, v);
@@ -174,13 +167,13 @@ __device__ __forceinline__ void stage_flush_off(const Ctx& c, int base, int off,
 // Staged accumulation: entry k of this lane's staging area += v (private to
 // the lane, so a plain read-modify-write).
 __device__ __forceinline__ void stage_acc(const Ctx& c, int k, double2 v) {
-  const uint32_t a = c.stage + k * (32 * 16);
-  sts128(a, add(lds128(a), v));
+  double2* a = c.stage + k * 32;
+  *a = add(*a, v);
 }
 
 __device__ __forceinline__ void stage_zero(const Ctx& c, int lo, int hi) {
 #pragma unroll 1
-  for (int k = lo; k < hi; ++k) sts128(c.stage + k * (32 * 16), make_double2(0.0, 0.0));
+  for (int k = lo; k < hi; ++k) c.stage[k * 32] = make_double2(0.0, 0.0);
 }
 
 // The register block is walked in chunks of CH indices j (runtime width jn <=
@@ -352,9 +345,10 @@ __device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int
         const int i1 = S - i0;
         double wc[CH];
         wchunk<CH>(cb + (i0 * d1 + i1) * rw, nc, j0, jn, w0, w1, wc);
-        double2 T = make_double2(0.0, 0.0);
+        double2 T = make_double2(0.0, 0.0), To = T;  // even and odd u: two independent chains
 #pragma unroll
-        for (int u = 0; u < CH; ++u) cmac(T, wc[u], q[u]);
+        for (int u = 0; u < CH; ++u) cmac((u & 1) ? To : T, wc[u], q[u]);
+        T = add(T, To);
         const double2 x0 = vat(c, b0 + i0), x1 = vat(c, b1 + i1);
         const double2 x01 = mul(x0, x1);
         e += x01.x * T.x - x01.y * T.y;
@@ -576,10 +570,8 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
     z = 0;
   }
   const double* wz = weights + int64_t(z) * t.feature_count;
-  const Ctx c{static_cast<uint32_t>(__cvta_generic_to_shared(val + atom)),
-        static_cast<uint32_t>(__cvta_generic_to_shared(Gr + atom)),
-        static_cast<uint32_t>(__cvta_generic_to_shared(Gi + atom)),
-        static_cast<uint32_t>(__cvta_generic_to_shared(stg + warp * kStage * 32 + lane))};
+  const Ctx c{val + atom, static_cast<uint32_t>(__cvta_generic_to_shared(Gr + atom)),
+              static_cast<uint32_t>(__cvta_generic_to_shared(Gi + atom)), stg + warp * kStage * 32 + lane};
   const int4* items = reinterpret_cast<const int4*>(t.items);
   const int4* phases = reinterpret_cast<const int4*>(t.phases);
   const int2* groups = reinterpret_cast<const int2*>(t.groups);
