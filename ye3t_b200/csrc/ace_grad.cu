@@ -35,7 +35,8 @@ namespace {
 constexpr int kGA = 16;
 constexpr int kGWarps = 8;
 constexpr int kGPad = 16;
-constexpr int kStage = 14;  // staged gradient entries per lane (two blocks of <= 7)
+constexpr int kStage = 14;     // staged gradient entries per lane (two blocks of <= 7)
+constexpr int kStageRun = 21;  // the same for the four-block run path (three blocks of <= 7)
 #ifndef Y3B_GRAD_BATCH
 #define Y3B_GRAD_BATCH 2
 #endif
@@ -137,19 +138,19 @@ __device__ __forceinline__ void g_add1(const Ctx& c, int e, double2 v) {
 }
 
 
-// G[base + STEP * k] += staged entry off + k for lo <= k < hi, kBatch entries
-// at a time.
-template <int STEP>
+// G[base + STEP * k] += staged entry off + k for lo <= k < hi (< NMAX),
+// kBatch entries at a time.
+template <int STEP, int NMAX = kStage>
 __device__ __forceinline__ void stage_flush_impl(const Ctx& c, int base, int off, int lo, int hi) {
   const uint32_t ar = c.Gr + base * (kGA * 8), ai = c.Gi + base * (kGA * 8);
 #pragma unroll
-  for (int k0 = 0; k0 < kStage; k0 += kBatch) {
+  for (int k0 = 0; k0 < NMAX; k0 += kBatch) {
     if (k0 < hi && k0 + kBatch > lo) {
       double2 v[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const int k = k0 + u;
-        v[u] = (k + off < kStage && k >= lo && k < hi) ? c.stage[(off + k) * 32] : make_double2(0.0, 0.0);
+        v[u] = (k < NMAX && k >= lo && k < hi) ? c.stage[(off + k) * 32] : make_double2(0.0, 0.0);
       }
       g_add_batch<kBatch, STEP, 0, kBatch>(c, ar + STEP * k0 * (kGA * 8), ai + STEP * k0 * (kGA * 8), lo - k0,
                                            hi - k0, v);
@@ -413,6 +414,139 @@ __device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int
   return e;
 }
 
+// Four-block item, register block of exactly CH indices, accumulating into
+// state that persists over a run of items: g0 and g1 in staging regions
+// [0, 7) and [7, 14), g_last in [14, 21), g_s in gs.  Same two passes as adj4.
+template <int CH>
+__device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc, const double* __restrict__ coef,
+                                            double w0, double w1, double2 (&gs)[CH]) {
+  double e = 0.0;
+  constexpr int rw_1 = (CH + 1) & ~1;
+  const int rw = nc == 2 ? 2 * CH : rw_1;
+  const int b0 = it.b0, b1 = it.b1, bs = it.b2, bl = it.b3;
+  const int d0 = it.d0, d1 = it.d1, dl = it.dl, K = it.K;
+  const int s_lo = max(0, K - (CH - 1) - (dl - 1)), s_hi = min(d0 + d1 - 2, K);
+  if (s_lo > s_hi) return e;
+  const double* cb = coef + it.coef;
+  double2 vs[CH];
+#pragma unroll
+  for (int u = 0; u < CH; ++u) vs[u] = vat(c, bs + u);
+#pragma unroll 1
+  for (int S = s_lo; S <= s_hi; ++S) {
+    double2 q[CH];
+#pragma unroll
+    for (int u = 0; u < CH; ++u) q[u] = mul(vs[u], vat(c, bl + K - S - u));
+    const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
+#pragma unroll 1
+    for (int i0 = i0a; i0 <= i0b; ++i0) {
+      const int i1 = S - i0;
+      double wc[CH];
+      wchunk<CH>(cb + (i0 * d1 + i1) * rw, nc, 0, CH, w0, w1, wc);
+      double2 T = make_double2(0.0, 0.0), To = T;  // even and odd u: two independent chains
+#pragma unroll
+      for (int u = 0; u < CH; ++u) cmac((u & 1) ? To : T, wc[u], q[u]);
+      T = add(T, To);
+      const double2 x0 = vat(c, b0 + i0), x1 = vat(c, b1 + i1);
+      const double2 x01 = mul(x0, x1);
+      e += x01.x * T.x - x01.y * T.y;
+      stage_acc(c, i0, mul(x1, T));
+      stage_acc(c, 7 + i1, mul(x0, T));
+    }
+  }
+  // w[u] belongs to last-block index K - S - u; after diagonal S no later one
+  // reaches index K - S, which is added to the staging area
+  double2 w[CH];
+#pragma unroll
+  for (int u = 0; u < CH; ++u) w[u] = make_double2(0.0, 0.0);
+#pragma unroll 1
+  for (int S = s_lo; S <= s_hi; ++S) {
+    double2 R[CH];
+#pragma unroll
+    for (int u = 0; u < CH; ++u) R[u] = make_double2(0.0, 0.0);
+    const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
+#pragma unroll 1
+    for (int i0 = i0a; i0 <= i0b; ++i0) {
+      const int i1 = S - i0;
+      double wc[CH];
+      wchunk<CH>(cb + (i0 * d1 + i1) * rw, nc, 0, CH, w0, w1, wc);
+      const double2 x01 = mul(vat(c, b0 + i0), vat(c, b1 + i1));
+#pragma unroll
+      for (int u = 0; u < CH; ++u) cmac(R[u], wc[u], x01);
+    }
+#pragma unroll
+    for (int u = 0; u < CH; ++u) {
+      cfma(gs[u], R[u], vat(c, bl + K - S - u));
+      cfma(w[u], R[u], vs[u]);
+    }
+    const int kf = K - S;
+    if (kf >= 0 && kf < dl) stage_acc(c, 14 + kf, w[0]);
+#pragma unroll
+    for (int u = 0; u + 1 < CH; ++u) w[u] = w[u + 1];
+    w[CH - 1] = make_double2(0.0, 0.0);
+  }
+#pragma unroll
+  for (int u = 0; u + 1 < CH; ++u) {
+    const int k = K - s_hi - 1 - u;
+    if (k >= 0 && k < dl) stage_acc(c, 14 + k, w[u]);
+  }
+  return e;
+}
+
+// A warp's contiguous run of four-block item pairs [g, ge) (classes 3, 4).
+// Packing sorts each shape's items by (register block, last block, prefix
+// blocks) and gives each half-warp a sorted half, so consecutive items of a
+// lane mostly share blocks: a target's gradient is added to G only when the
+// next item's block differs (a muted lane adds zeros, which changes nothing).
+template <int CH>
+__device__ __forceinline__ double adj4_run(const Ctx& c, const int2* __restrict__ pairs, int g, int ge, int grp,
+                                           const int4* __restrict__ items, const double* __restrict__ coef,
+                                           const double* __restrict__ wz) {
+  double e = 0.0;
+  double2 gs[CH];
+#pragma unroll
+  for (int u = 0; u < CH; ++u) gs[u] = make_double2(0.0, 0.0);
+  int p0 = -1, p1 = -1, ps = -1, pl = -1, n0 = 0, n1 = 0, nl = 0;
+#pragma unroll 1
+  for (; g < ge; ++g) {
+    const int2 ig = __ldg(pairs + g);
+    const int mine = grp == 0 ? ig.x : ig.y;
+    const bool mute = mine < 0;
+    const Item it = load_item(items, mute ? ig.x : mine);
+    const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
+    const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
+    if (it.b0 != p0) {
+      if (p0 >= 0) stage_flush_impl<1, 7>(c, p0, 0, 0, n0);
+      stage_zero(c, 0, it.d0);
+      p0 = it.b0;
+      n0 = it.d0;
+    }
+    if (it.b1 != p1) {
+      if (p1 >= 0) stage_flush_impl<1, 7>(c, p1, 7, 0, n1);
+      stage_zero(c, 7, 7 + it.d1);
+      p1 = it.b1;
+      n1 = it.d1;
+    }
+    if (it.b2 != ps) {
+      if (ps >= 0) g_add<CH, 1>(c, ps, 0, CH, gs);
+#pragma unroll
+      for (int u = 0; u < CH; ++u) gs[u] = make_double2(0.0, 0.0);
+      ps = it.b2;
+    }
+    if (it.b3 != pl) {
+      if (pl >= 0) stage_flush_impl<1, 7>(c, pl, 14, 0, nl);
+      stage_zero(c, 14, 14 + it.dl);
+      pl = it.b3;
+      nl = it.dl;
+    }
+    e += adj4_body<CH>(c, it, (it.sel & 1) + 1, coef, w0, w1, gs);
+  }
+  if (p0 >= 0) stage_flush_impl<1, 7>(c, p0, 0, 0, n0);
+  if (p1 >= 0) stage_flush_impl<1, 7>(c, p1, 7, 0, n1);
+  if (ps >= 0) g_add<CH, 1>(c, ps, 0, CH, gs);
+  if (pl >= 0) stage_flush_impl<1, 7>(c, pl, 14, 0, nl);
+  return e;
+}
+
 // Any item shape, one tuple at a time with single additions (for shapes the
 // unrolled paths do not cover: wide register blocks, long last blocks).
 __device__ __noinline__ double adj_generic(const Ctx c, const Item it, int B, int DS, int NC,
@@ -550,6 +684,7 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
   double* Gr = reinterpret_cast<double*>(gsm + rows * kGA);
   double* Gi = Gr + E * kGA;
   double2* stg = reinterpret_cast<double2*>(Gi + E * kGA);
+  constexpr int kStageLanes = kSlots ? kStage : kStageRun;  // staged entries per lane
   for (int e = threadIdx.x; e < rows * kGA; e += blockDim.x) gsm[e] = make_double2(0.0, 0.0);
   for (int e = threadIdx.x; e < 2 * E * kGA; e += blockDim.x) Gr[e] = 0.0;
   __syncthreads();
@@ -571,14 +706,23 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
   }
   const double* wz = weights + int64_t(z) * t.feature_count;
   const Ctx c{val + atom, static_cast<uint32_t>(__cvta_generic_to_shared(Gr + atom)),
-              static_cast<uint32_t>(__cvta_generic_to_shared(Gi + atom)), stg + warp * kStage * 32 + lane};
+              static_cast<uint32_t>(__cvta_generic_to_shared(Gi + atom)), stg + warp * kStageLanes * 32 + lane};
   const int4* items = reinterpret_cast<const int4*>(t.items);
   const int4* phases = reinterpret_cast<const int4*>(t.phases);
   const int2* groups = reinterpret_cast<const int2*>(t.groups);
   int cur0 = -2, cur1 = -2;
   double e_acc = 0.0;
+  if (!kSlots) {
+    // four-block classes: all pairs sit in phase 0's range (no slots), one
+    // contiguous run per warp
+    const int gb = __ldg(t.group_offsets + CLS * (t.phase_count + 1));
+    const int ge = __ldg(t.group_offsets + CLS * (t.phase_count + 1) + 1);
+    const int per = (ge - gb + kGWarps - 1) / kGWarps;
+    const int g0 = gb + warp * per, g1 = min(ge, g0 + per);
+    e_acc = adj4_run<(CLS == 3 ? 5 : 7)>(c, groups, g0, g1, grp, items, t.item_coef, wz);
+  }
 #pragma unroll 1
-  for (int ph = 0; ph < t.phase_count; ++ph) {
+  for (int ph = 0; kSlots && ph < t.phase_count; ++ph) {
     const int4 pr = __ldg(phases + ph);
     const int* goff = t.group_offsets + CLS * (t.phase_count + 1);
     const int gb = __ldg(goff + ph), ge = __ldg(goff + ph + 1);
@@ -824,12 +968,14 @@ extern "C" int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, 
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && weights && energy && dEdA && species_count > 0, "null pointer argument");
-  auto smem_for = [&](int64_t entries) {
+  auto smem_for = [&](int64_t entries, int stage) {
     return size_t(entries + 2 * kGPad) * kGA * sizeof(double2) + size_t(2) * size_t(entries) * kGA * sizeof(double) +
-           size_t(kGWarps) * kStage * 32 * sizeof(double2);
+           size_t(kGWarps) * stage * 32 * sizeof(double2);
   };
-  const size_t smem = smem_for(tables->smem_entries);
-  const size_t smem_a = smem_for(tables->nmax * (tables->lmax + 1) * (tables->lmax + 1));
+  const size_t smem = smem_for(tables->smem_entries, kStage);
+  const size_t smem_a = smem_for(tables->nmax * (tables->lmax + 1) * (tables->lmax + 1), kStageRun);
+  Y3B_CHECK_ARG(smem_a <= 224 * 1024, "adjoint run path needs %lld bytes of shared memory (max 224 KB)",
+                (long long)smem_a);
   Y3B_CHECK_ARG(smem <= 224 * 1024, "bundle needs %lld bytes of shared memory for the adjoint (max 224 KB)",
                 (long long)smem);
   const int64_t grid = (atom_count + kGA - 1) / kGA;

@@ -401,6 +401,7 @@ def item_flops_per_atom(items: np.ndarray) -> float:
 GRAD_GROUP = 2
 GRAD_CLASSES = 5
 GRAD_STAGE = 14  # staged gradient entries per lane in the adjoint kernel
+GRAD_RUN_CLASSES = (3, 4)  # four-block classes: A entries only, one sorted run per warp
 
 
 def grad_class(row, a_entries: Optional[int] = None) -> int:
@@ -435,6 +436,25 @@ def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
     groups = []
     offsets = np.zeros((GRAD_CLASSES, phases.shape[0] + 1), dtype=np.int32)
     for cls in range(GRAD_CLASSES):
+        if cls in GRAD_RUN_CLASSES:
+            # A-entry-only classes ignore phases: every pair goes to phase 0's
+            # range.  Each shape's items are sorted by (register block, last
+            # block, prefix blocks) and split in two halves, one per half-warp,
+            # so that consecutive items of a lane share blocks (the kernel adds
+            # a block's gradient to G only when the block changes).
+            offsets[cls, 0] = len(groups)
+            shapes = {}
+            for i in range(items.shape[0]):
+                if grad_class(items[i], a_entries) == cls:
+                    shapes.setdefault(tuple(int(v) for v in items[i, :5]), []).append(i)
+            for key in sorted(shapes):
+                idx = sorted(shapes[key], key=lambda i: (int(items[i, 10]), int(items[i, 11]), int(items[i, 8]),
+                                                         int(items[i, 9]), int(items[i, 5])))
+                h = (len(idx) + 1) // 2
+                for u in range(h):
+                    groups.append([idx[u], idx[u + h] if u + h < len(idx) else -1])
+            offsets[cls, 1:] = len(groups)
+            continue
         for ph, (_, _, begin, end) in enumerate(phases.tolist()):
             offsets[cls, ph] = len(groups)
             shapes = {}
