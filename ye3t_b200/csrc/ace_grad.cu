@@ -33,7 +33,16 @@ namespace {
 // compare-and-swaps: all old values are loaded, all swaps issued, and only the
 // ones that lost a race against another warp are retried.
 constexpr int kGA = 16;
-constexpr int kGWarps = 8;
+#ifndef Y3B_RUN_WARPS
+#define Y3B_RUN_WARPS 8
+#endif
+constexpr int kGWarps = 8;       // warps per CTA of the classes with symmetric slots
+constexpr int kGWarpsRun = Y3B_RUN_WARPS;  // and of the four-block (A-only) classes
+
+template <int CLS>
+struct ClassWarps {
+  static constexpr int value = CLS >= 3 ? kGWarpsRun : kGWarps;
+};
 constexpr int kGPad = 16;
 constexpr int kStage = 14;     // staged gradient entries per lane (two blocks of <= 7)
 constexpr int kStageRun = 21;  // the same for the four-block run path (three blocks of <= 7)
@@ -667,14 +676,15 @@ __device__ __forceinline__ void grad_clear_slot(double* __restrict__ Gr, double*
 }
 
 template <int CLS>
-__global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_tables t, const double2* __restrict__ A,
+__global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kernel(y3b_ace_tables t, const double2* __restrict__ A,
                                                                    int64_t N, const int32_t* __restrict__ species,
                                                                    const double* __restrict__ weights, int64_t S,
                                                                    double* __restrict__ energy,
                                                                    double2* __restrict__ dEdA,
                                                                    int32_t* __restrict__ status, int accumulate) {
   extern __shared__ double2 gsm[];
-  __shared__ double red[kGWarps][kGA];
+  constexpr int kWarps = ClassWarps<CLS>::value;
+  __shared__ double red[kWarps][kGA];
   // classes 3 and 4 (4-block items) read A entries only: no symmetric slots
   constexpr bool kSlots = CLS <= 2;
   const int W = int((t.lmax + 1) * (t.lmax + 1));
@@ -717,7 +727,7 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
     // contiguous run per warp
     const int gb = __ldg(t.group_offsets + CLS * (t.phase_count + 1));
     const int ge = __ldg(t.group_offsets + CLS * (t.phase_count + 1) + 1);
-    const int per = (ge - gb + kGWarps - 1) / kGWarps;
+    const int per = (ge - gb + kWarps - 1) / kWarps;
     const int g0 = gb + warp * per, g1 = min(ge, g0 + per);
     e_acc = adj4_run<(CLS == 3 ? 5 : 7)>(c, groups, g0, g1, grp, items, t.item_coef, wz);
   }
@@ -745,7 +755,7 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
       cur1 = pr.y;
     }
 #pragma unroll 1
-    for (int g = gb + warp; g < ge; g += kGWarps) {
+    for (int g = gb + warp; g < ge; g += kWarps) {
       const int2 ig = __ldg(groups + g);
       const int mine = grp == 0 ? ig.x : ig.y;
       const bool mute = mine < 0;  // odd item out: the second half runs the first item unweighted, adding nothing
@@ -764,7 +774,7 @@ __global__ void __launch_bounds__(32 * kGWarps, 1) ace_grad_kernel(y3b_ace_table
   if (threadIdx.x < kGA) {
     const int64_t aa = blockIdx.x * int64_t(kGA) + threadIdx.x;
     double s = 0.0;
-    for (int w = 0; w < kGWarps; ++w) s += red[w][threadIdx.x];
+    for (int w = 0; w < kWarps; ++w) s += red[w][threadIdx.x];
     if (aa < N) energy[aa] = accumulate ? energy[aa] + s : s;
   }
   {
@@ -968,12 +978,12 @@ extern "C" int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, 
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && weights && energy && dEdA && species_count > 0, "null pointer argument");
-  auto smem_for = [&](int64_t entries, int stage) {
+  auto smem_for = [&](int64_t entries, int stage, int warps) {
     return size_t(entries + 2 * kGPad) * kGA * sizeof(double2) + size_t(2) * size_t(entries) * kGA * sizeof(double) +
-           size_t(kGWarps) * stage * 32 * sizeof(double2);
+           size_t(warps) * stage * 32 * sizeof(double2);
   };
-  const size_t smem = smem_for(tables->smem_entries, kStage);
-  const size_t smem_a = smem_for(tables->nmax * (tables->lmax + 1) * (tables->lmax + 1), kStageRun);
+  const size_t smem = smem_for(tables->smem_entries, kStage, kGWarps);
+  const size_t smem_a = smem_for(tables->nmax * (tables->lmax + 1) * (tables->lmax + 1), kStageRun, kGWarpsRun);
   Y3B_CHECK_ARG(smem_a <= 224 * 1024, "adjoint run path needs %lld bytes of shared memory (max 224 KB)",
                 (long long)smem_a);
   Y3B_CHECK_ARG(smem <= 224 * 1024, "bundle needs %lld bytes of shared memory for the adjoint (max 224 KB)",
@@ -986,7 +996,7 @@ extern "C" int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, 
 #define Y3B_GRAD_LAUNCH(CLS)                                                                              \
   Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_grad_kernel<CLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
                                     int(CLS <= 2 ? smem : smem_a)));                                      \
-  ace_grad_kernel<CLS><<<int(grid), 32 * kGWarps, CLS <= 2 ? smem : smem_a, s>>>(                         \
+  ace_grad_kernel<CLS><<<int(grid), 32 * ClassWarps<CLS>::value, CLS <= 2 ? smem : smem_a, s>>>(       \
       *tables, static_cast<const double2*>(A),                                                            \
                                                              atom_count, species, weights, species_count, \
                                                              energy, static_cast<double2*>(dEdA), status, \
