@@ -299,28 +299,28 @@ __device__ __forceinline__ void eval_dispatch(const Cx2<R>* __restrict__ P, cons
 
 // Fill shared-memory slot `slot` with every symmetric output of radial
 // channel `ch` (sym_output, ace_common.cuh).
-template <typename R>
+template <typename R, int WARPS>
 __device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, Cx2<R>* __restrict__ sm, int W, int slot,
                                           int ch, int lane, int warp) {
   using C2 = typename Cplx<R>::type;
   const int na = int(t.nmax) * W;
   const int so = int(t.sym_output_count);
   const int4* outs = reinterpret_cast<const int4*>(t.sym_outputs);
-  for (int o = warp; o < so; o += kEvalWarps) {
+  for (int o = warp; o < so; o += WARPS) {
     const int4 r = __ldg(outs + o);  // (l^2, term begin, term end, -)
     sm[(na + slot * so + o) * kLanes + lane] = sym_output(t, r.y, r.z, sm + (ch * W + r.x) * kLanes + lane, kLanes);
   }
 }
 
-template <typename R, int MODE>
-__global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
+template <typename R, int MODE, int WARPS>
+__global__ void __launch_bounds__(kLanes * WARPS) ace_eval_kernel(
     y3b_ace_tables t, const Cx2<R>* __restrict__ A, int64_t N, Cx2<R>* __restrict__ feats,
     const int32_t* __restrict__ species, const double* __restrict__ weights, int64_t S,
     double* __restrict__ energy) {
   using C2 = typename Cplx<R>::type;
   extern __shared__ __align__(16) unsigned char eval_smem_raw[];
   C2* smem_all = reinterpret_cast<C2*>(eval_smem_raw);
-  __shared__ double red[kEvalWarps][kLanes];
+  __shared__ double red[WARPS][kLanes];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int W = int((t.lmax + 1) * (t.lmax + 1));
   const int na = int(t.nmax) * W;
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
   for (int e = threadIdx.x; e < total; e += blockDim.x) smem_all[e] = cz<C2>();
   __syncthreads();
   C2* sm = smem_all + kPadEntries * kLanes;
-  for (int e = warp; e < na; e += kEvalWarps)
+  for (int e = warp; e < na; e += WARPS)
     sm[e * kLanes + lane] = live ? A[a * na + e] : cz<C2>();
   const double* wz = weights;
   if (MODE == 1) {
@@ -348,13 +348,15 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
     const int4 pr = __ldg(phases + ph);
     if (pr.x != cur0 || pr.y != cur1) {
       __syncthreads();  // previous phase's items are done with the slots (and A is loaded)
-      if (pr.x != cur0) fill_slot<R>(t, sm, W, 0, pr.x, lane, warp);
-      if (pr.y != cur1 && pr.y >= 0) fill_slot<R>(t, sm, W, 1, pr.y, lane, warp);
+      if (pr.x != cur0) fill_slot<R, WARPS>(t, sm, W, 0, pr.x, lane, warp);
+      // (the second slot exists only in pools sized for it)
+      if (pr.y != cur1 && pr.y >= 0 && t.smem_entries >= na + 2 * t.sym_output_count)
+        fill_slot<R, WARPS>(t, sm, W, 1, pr.y, lane, warp);
       __syncthreads();
       cur0 = pr.x;
       cur1 = pr.y;
     }
-    for (int i = pr.z + warp; i < pr.w; i += kEvalWarps) {
+    for (int i = pr.z + warp; i < pr.w; i += WARPS) {
       const Item it = load_item(items, i);
       C2 a0 = cz<C2>(), a1 = a0;
       eval_dispatch<R>(P, it, t.item_coef, a0, a1);
@@ -374,7 +376,7 @@ __global__ void __launch_bounds__(kLanes * kEvalWarps) ace_eval_kernel(
     __syncthreads();
     if (warp == 0 && live) {
       double s = 0.0;
-      for (int w = 0; w < kEvalWarps; ++w) s += red[w][lane];
+      for (int w = 0; w < WARPS; ++w) s += red[w][lane];
       energy[a] = s;
     }
   }
@@ -390,26 +392,39 @@ int check_tables(const y3b_ace_tables* t) {
   Y3B_CHECK_ARG(t->lmax >= 0 && t->lmax <= 6, "lmax must be in [0, 6]");
   Y3B_CHECK_ARG(t->item_count >= 0 && t->feature_count >= 0 && t->phase_count >= 1, "bad table sizes");
   Y3B_CHECK_ARG(t->item_count == 0 || (t->items && t->item_coef && t->phases), "null item tables");
-  Y3B_CHECK_ARG(t->smem_entries >= t->nmax * (t->lmax + 1) * (t->lmax + 1) + 2 * t->sym_output_count,
+  Y3B_CHECK_ARG(t->smem_entries >= t->nmax * (t->lmax + 1) * (t->lmax + 1) + t->sym_output_count,
                 "shared-memory entry count too small");
   Y3B_CHECK_ARG(eval_smem_bytes(*t) <= 200 * 1024, "bundle needs %lld bytes of shared memory per CTA (max 200 KB)",
                 (long long)eval_smem_bytes(*t));
   return Y3B_OK;
 }
 
+template <typename R, int MODE, int WARPS>
+int launch_eval_w(const y3b_ace_tables* t, const void* A, int64_t n, typename Cplx<R>::type* feats,
+                  const int32_t* species, const double* weights, int64_t S, double* energy, cudaStream_t s,
+                  size_t smem) {
+  using C2 = typename Cplx<R>::type;
+  Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_eval_kernel<R, MODE, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
+  const int64_t grid = (n + kLanes - 1) / kLanes;
+  Y3B_CHECK_ARG(grid < (int64_t(1) << 31), "too many atoms");
+  ace_eval_kernel<R, MODE, WARPS><<<int(grid), kLanes * WARPS, smem, s>>>(*t, static_cast<const C2*>(A), n, feats,
+                                                                          species, weights, S, energy);
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+// Pools small enough for two CTAs per SM run 8-warp CTAs (two of them share
+// an SM, so one's phase barriers overlap the other's items); larger pools run
+// one 16-warp CTA per SM.
 template <typename R, int MODE>
 int launch_eval(const y3b_ace_tables* t, const void* A, int64_t n, typename Cplx<R>::type* feats,
                 const int32_t* species, const double* weights, int64_t S, double* energy, cudaStream_t s) {
   using C2 = typename Cplx<R>::type;
   const size_t smem = eval_smem_bytes(*t, sizeof(C2));
-  Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_eval_kernel<R, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(smem)));
-  const int64_t grid = (n + kLanes - 1) / kLanes;
-  Y3B_CHECK_ARG(grid < (int64_t(1) << 31), "too many atoms");
-  ace_eval_kernel<R, MODE><<<int(grid), kLanes * kEvalWarps, smem, s>>>(*t, static_cast<const C2*>(A), n, feats,
-                                                                       species, weights, S, energy);
-  Y3B_LAUNCH_CHECK();
-  return Y3B_OK;
+  if (2 * (smem + 2048) <= 227 * 1024)
+    return launch_eval_w<R, MODE, 8>(t, A, n, feats, species, weights, S, energy, s, smem);
+  return launch_eval_w<R, MODE, kEvalWarps>(t, A, n, feats, species, weights, S, energy, s, smem);
 }
 
 }  // namespace y3b

@@ -747,8 +747,8 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
         grad_fill_slot(t, val, W, 0, pr.x);
       }
       if (pr.y != cur1) {
-        grad_clear_slot(Gr, Gi, na, so, 1);
-        if (pr.y >= 0) grad_fill_slot(t, val, W, 1, pr.y);
+        if (t.smem_entries >= na + 2 * so) grad_clear_slot(Gr, Gi, na, so, 1);
+        if (pr.y >= 0 && t.smem_entries >= na + 2 * so) grad_fill_slot(t, val, W, 1, pr.y);
       }
       __syncthreads();
       cur0 = pr.x;

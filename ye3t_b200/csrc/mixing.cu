@@ -71,11 +71,17 @@ __global__ void __launch_bounds__(32 * kMixWarps) ace_density_mixed_kernel(
   using C2 = typename Cx<T>::type;
   constexpr int W = (LMAX + 1) * (LMAX + 1);
   extern __shared__ __align__(16) unsigned char msm[];
-  const int mixn = S * S * C * nmax;
+  // pair tables one element apart, so lanes reading the tables of different
+  // neighbour species hit different banks
+  const int pstride = C * nmax + 1;
+  const int mixn = S * S * pstride;
   T* s_mix = reinterpret_cast<T*>(msm);
   C2* s_y = reinterpret_cast<C2*>(msm + ((size_t(mixn) * sizeof(T) + 15) & ~size_t(15)));  // [warp][32][W]
   T* s_rm = reinterpret_cast<T*>(s_y + kMixWarps * 32 * W);                                   // [warp][32][C]
-  for (int k = threadIdx.x; k < mixn; k += blockDim.x) s_mix[k] = mix[k];
+  for (int k = threadIdx.x; k < S * S * C * nmax; k += blockDim.x) {
+    const int pr = k / (C * nmax);
+    s_mix[pr * pstride + (k - pr * C * nmax)] = mix[k];
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   C2* y_w = s_y + wib * 32 * W;
@@ -110,7 +116,7 @@ __global__ void __launch_bounds__(32 * kMixWarps) ace_density_mixed_kernel(
           const T r = sqrt(T(r2));
           T rv[kMaxRadial + 1];
           radial_basis<T>(r, rc, lam, nmax, rv, nullptr);
-          const T* wp = s_mix + (size_t(zi) * S + zj) * C * nmax;
+          const T* wp = s_mix + (size_t(zi) * S + zj) * pstride;
           for (int c = 0; c < C; ++c) {
             T s = T(0);
             for (int n = 0; n < nmax; ++n) s = add_rn(s, mul_rn(wp[c * nmax + n], rv[n + 1]));
@@ -209,7 +215,7 @@ extern "C" int y3b_ace_density_mixed(int dtype, const double* positions, const i
   cudaStream_t s = as_stream(stream);
   const size_t W = size_t(lmax + 1) * size_t(lmax + 1);
   auto smem_for = [&](size_t real_size) {
-    return ((size_t(S) * S * C * nmax * real_size + 15) & ~size_t(15)) + kMixWarps * 32 * W * 2 * real_size +
+    return ((size_t(S) * S * (C * nmax + 1) * real_size + 15) & ~size_t(15)) + kMixWarps * 32 * W * 2 * real_size +
            kMixWarps * 32 * size_t(C) * real_size;
   };
 #define Y3B_MIX_CASE(T, L)                                                                                    \

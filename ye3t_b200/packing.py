@@ -559,7 +559,9 @@ def pack_bundle(bundle: ACEBundle, device) -> PackedBundle:
     for a, b2, _, _ in phases.tolist():
         loads += int(a != prev[0]) + int(b2 >= 0 and b2 != prev[1])
         prev = (a, b2)
-    pb = PackedBundle(bundle=bundle, device=device, arrays=arrays, pool_size=nmax * W + 2 * sym_out_count,
+    # a second symmetric slot only when some phase pairs two radial channels
+    n_slots = 2 if any(int(ph[1]) >= 0 for ph in phases.tolist()) else 1
+    pb = PackedBundle(bundle=bundle, device=device, arrays=arrays, pool_size=nmax * W + n_slots * sym_out_count,
                       feature_count=fo, max_blocks=max_blocks, sym_offsets=sym_local,
                       term_count_per_atom=terms_per_atom, term_block_count_per_atom=term_blocks_per_atom,
                       sym_term_count_per_atom=len(s_fac) * loads,
