@@ -458,8 +458,36 @@ def mixing_fixture():
     print("mixing_small.npz", N, "atoms", E, "edges", "A norm", float(np.abs(A.numpy()).sum()))
 
 
+def real_schedules_fixture():
+    """Real-tesseral schedules (``generate_real_factorized_coefficient_schedule_for_labels``) of a few
+    words and targets, random real blocks and the reference's ``evaluate_real_factorized_schedule_torch``."""
+    from ye3t.core.basis import ExactACELabeler
+    from ye3t.core.couplings import (evaluate_real_factorized_schedule_torch,
+                                     generate_real_factorized_coefficient_schedule_for_labels)
+    cases = [((1, 2), (1, 1), 0), ((1, 2, 3), (1, 1, 2), 0), ((1, 1, 2, 3), (2, 2, 1, 3), 0), ((1, 2), (2, 3), 4),
+             ((1, 2, 3), (1, 2, 3), 2)]
+    out = {"count": np.asarray(len(cases))}
+    g = torch.Generator().manual_seed(2040)
+    for k, (n_tuple, l_tuple, L) in enumerate(cases):
+        labels = ExactACELabeler(list(n_tuple), list(l_tuple), strict_target_validation=False) \
+            .compact_labels_for_target(L)
+        sch = generate_real_factorized_coefficient_schedule_for_labels(labels, component_indices=range(2 * L + 1))
+        ts = sch.to_torch(dtype=torch.float64)
+        bv = torch.randn(7, ts.basis_count, ts.block_count, ts.max_block_m_dim, dtype=torch.float64, generator=g)
+        y = evaluate_real_factorized_schedule_torch(bv, ts)
+        p = f"r{k}_"
+        out.update({p + "off": np.asarray(sch.component_offsets, dtype=np.int64),
+                    p + "cli": np.asarray(sch.component_label_index, dtype=np.int64),
+                    p + "idx": np.asarray(sch.block_real_tuples, dtype=np.int64).reshape(-1, int(sch.block_count)),
+                    p + "co": np.asarray(sch.coeffs, dtype=np.float64),
+                    p + "bL": np.asarray(sch.block_L_by_label(dtype=np.int64)),
+                    p + "basis": np.asarray(int(sch.basis_count)), p + "bv": bv.numpy(), p + "y": y.numpy()})
+    np.savez_compressed(os.path.join(HERE, "real_schedules.npz"), **out)
+    print("real_schedules.npz", len(cases), "schedules")
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing"]
+    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing", "real"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -474,3 +502,5 @@ if __name__ == "__main__":
         forces_fixture()
     if "mixing" in which:
         mixing_fixture()
+    if "real" in which:
+        real_schedules_fixture()

@@ -208,3 +208,13 @@ def test_oracle_mixed_density_matches_reference_composition(golden):
                                  float(g["rc"]), float(g["lam"]))
     err = np.abs(A - g["A"]).max() / np.abs(g["A"]).max()
     assert err <= 1e-13, err
+
+
+def test_oracle_real_tesseral_schedules(golden):
+    """Real-tesseral schedules (generate_real_factorized_coefficient_schedule_for_labels) through the
+    oracle's schedule evaluator against the reference's evaluate_real_factorized_schedule_torch."""
+    g = golden("real_schedules")
+    for k in range(int(g["count"])):
+        p = f"r{k}_"
+        y = oracle.schedule_evaluate(g[p + "bv"], g[p + "off"], g[p + "cli"], g[p + "idx"], g[p + "co"])
+        np.testing.assert_allclose(y, g[p + "y"], rtol=1e-13, atol=1e-13)

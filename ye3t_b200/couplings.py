@@ -20,7 +20,8 @@ import torch
 from . import _native as nat
 from .schedules import ScheduleRecord
 
-__all__ = ["evaluate_factorized_schedule_torch", "evaluate_report", "packed_schedule_tables"]
+__all__ = ["evaluate_factorized_schedule_torch", "evaluate_real_factorized_schedule_torch", "evaluate_report",
+           "packed_schedule_tables"]
 
 _CACHE = {}
 _CACHE_LOCK = threading.Lock()
@@ -128,3 +129,94 @@ def evaluate_report(report, block_values, *, target_L, backend="auto"):
     if target_L not in schedules:
         raise ValueError("target_L is not present in this ACE schedule report.")
     return evaluate_factorized_schedule_torch(block_values, schedules[target_L], backend=backend)
+
+
+# ---------------------------------------------------------------------------
+# Real-tesseral schedules (ye3t/core/couplings.py:337-478, 570-610): the same
+# contraction with real block values, real coefficients and real component
+# indices (block_real_tuples), so the same native evaluator runs it in f32/f64.
+# ---------------------------------------------------------------------------
+def _real_schedule_arrays(schedule):
+    """(offsets, labels, block_real_indices, coeffs, component_count, block_count, basis_count, max_dim)."""
+    if hasattr(schedule, "block_real_indices") and hasattr(schedule, "term_component_index"):
+        # TorchRealFactorizedCoefficientSchedule (couplings.py:398-478)
+        off = schedule.component_offsets.detach().cpu().numpy().astype(np.int64)
+        cli = schedule.component_label_index.detach().cpu().numpy().astype(np.int64)
+        ridx = schedule.block_real_indices.detach().cpu().numpy().astype(np.int64)
+        coeffs = schedule.coeffs.detach().cpu().numpy().astype(np.float64)
+        return (off, cli, ridx, coeffs, int(schedule.component_count), int(schedule.block_count),
+                int(schedule.basis_count), int(schedule.max_block_m_dim))
+    # RealFactorizedCoefficientSchedule (couplings.py:337-397) or a record with its fields
+    off = np.asarray(schedule.component_offsets, dtype=np.int64)
+    cli = np.asarray(schedule.component_label_index, dtype=np.int64)
+    blocks = int(schedule.block_count)
+    ridx = np.asarray(schedule.block_real_tuples, dtype=np.int64).reshape(-1, blocks)
+    coeffs = np.asarray(schedule.coeffs, dtype=np.float64)
+    block_L = np.asarray(schedule.block_L_by_label(dtype=np.int64)) if hasattr(schedule, "block_L_by_label") \
+        else np.asarray(schedule.block_L, dtype=np.int64)
+    max_dim = int(2 * int(block_L.max()) + 1) if block_L.size else 0
+    basis = int(schedule.basis_count)
+    return off, cli, ridx, coeffs, int(cli.shape[0]), blocks, basis, max_dim
+
+
+_REAL_CACHE = {}
+
+
+def evaluate_real_factorized_schedule_torch(block_values, schedule, *, backend="auto", validate=False):
+    """Evaluate a real-tesseral factorized schedule on CUDA block values.
+
+    Mirrors ``ye3t/core/couplings.py:570-610``: ``block_values`` are real
+    ``[batch, basis_count, block_count, max_block_m_dim]``; the result is
+    ``[batch, component_count]`` in the block dtype (float32 or float64),
+    ``out[b, c] = sum_t coeff_t prod_j bv[b, label_c, j, real_idx[t, j]]``
+    with products in block order and sums in term order.
+    """
+    selected = str(backend or "auto").strip().lower()
+    if selected in ("torch", "pytorch", "reference"):
+        raise ValueError(f"backend {backend!r} is a ye3t reference path; ye3t_b200 evaluates on CUDA only")
+    if selected not in ("auto", "native", "cuda", ""):
+        raise ValueError(f"Unknown real factorized runtime backend: {backend!r}")
+    bv = torch.as_tensor(block_values)
+    if torch.is_complex(bv):
+        raise ValueError("Real factorized schedule evaluation requires real block values.")
+    dev = nat.require_cuda(bv, what="evaluate_real_factorized_schedule_torch")
+    if bv.ndim != 4:
+        raise ValueError("block_values must have shape [batch, basis_count, block_count, max_block_m_dim].")
+    key = (id(schedule), str(dev))
+    with _CACHE_LOCK:
+        hit = _REAL_CACHE.get(key)
+    if hit is None or hit[0]() is not schedule:
+        off, cli, ridx, coeffs, comps, blocks, basis, max_dim = _real_schedule_arrays(schedule)
+        tab = {"off": torch.as_tensor(off).to(dev), "cli": torch.as_tensor(cli).to(dev),
+               "ridx": torch.as_tensor(np.ascontiguousarray(ridx)).to(dev),
+               "coeffs": torch.as_tensor(np.ascontiguousarray(coeffs)).to(dev), "comps": comps, "blocks": blocks,
+               "basis": basis, "max_dim": max_dim, "terms": int(coeffs.shape[0])}
+        try:
+            ref = weakref.ref(schedule)
+        except TypeError:
+            ref = (lambda obj: (lambda: obj))(schedule)
+        with _CACHE_LOCK:
+            _REAL_CACHE[key] = (ref, tab)
+    else:
+        tab = hit[1]
+    if int(bv.shape[1]) < tab["basis"]:
+        raise ValueError("block_values basis dimension is smaller than schedule.basis_count.")
+    if int(bv.shape[2]) != tab["blocks"]:
+        raise ValueError("block_values block dimension must equal schedule.block_count.")
+    if int(bv.shape[3]) < tab["max_dim"]:
+        raise ValueError("block_values real-component dimension is smaller than schedule.max_block_m_dim.")
+    if bv.dtype not in (torch.float32, torch.float64):
+        raise TypeError("block_values must be float32 or float64")
+    values = bv.contiguous()
+    coeffs = tab["coeffs"].to(values.dtype)
+    batch, basis, blocks, mdim = (int(v) for v in values.shape)
+    out = torch.empty((batch, tab["comps"]), dtype=values.dtype, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if validate else None
+    nat.check(nat.lib().y3b_factorized_schedule_evaluate(
+        nat.dtype_code(values.dtype), values.data_ptr(), batch, basis, blocks, mdim, tab["off"].data_ptr(),
+        tab["cli"].data_ptr(), tab["ridx"].data_ptr() if tab["terms"] else 0,
+        coeffs.data_ptr() if tab["terms"] else 0, tab["comps"], tab["terms"], out.data_ptr(), nat.ptr(status),
+        nat.stream_of(dev)), "evaluate_real_factorized_schedule_torch")
+    if validate and int(status.item()):
+        raise IndexError("evaluate_real_factorized_schedule_torch: schedule index out of range")
+    return out
