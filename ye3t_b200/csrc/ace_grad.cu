@@ -425,7 +425,11 @@ __device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int
 
 // Four-block item, register block of exactly CH indices, accumulating into
 // state that persists over a run of items: g0 and g1 in staging regions
-// [0, 7) and [7, 14), g_last in [14, 21), g_s in gs.  Same two passes as adj4.
+// [0, 7) and [7, 14), g_last in [14, 21), g_s in gs.  One pass over the
+// anti-diagonals S: q_u = vs_u vl[K-S-u]; per row T = sum_u c_u q_u gives the
+// energy and the prefix gradients, and R_u += c_u x0 x1; per diagonal
+// gs_u += R_u vl[K-S-u] and g_last[K-S-u] += R_u vs_u (through a window that
+// moves by one per diagonal).
 template <int CH>
 __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc, const double* __restrict__ coef,
                                             double w0, double w1, double2 (&gs)[CH]) {
@@ -437,14 +441,21 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
   const int s_lo = max(0, K - (CH - 1) - (dl - 1)), s_hi = min(d0 + d1 - 2, K);
   if (s_lo > s_hi) return e;
   const double* cb = coef + it.coef;
-  double2 vs[CH];
+  double2 vs[CH], w[CH];
 #pragma unroll
-  for (int u = 0; u < CH; ++u) vs[u] = vat(c, bs + u);
+  for (int u = 0; u < CH; ++u) {
+    vs[u] = vat(c, bs + u);
+    w[u] = make_double2(0.0, 0.0);
+  }
 #pragma unroll 1
   for (int S = s_lo; S <= s_hi; ++S) {
-    double2 q[CH];
+    double2 vl[CH], q[CH], R[CH];
 #pragma unroll
-    for (int u = 0; u < CH; ++u) q[u] = mul(vs[u], vat(c, bl + K - S - u));
+    for (int u = 0; u < CH; ++u) {
+      vl[u] = vat(c, bl + K - S - u);  // out-of-block indices read finite neighbours; their coefficient is 0
+      q[u] = mul(vs[u], vl[u]);
+      R[u] = make_double2(0.0, 0.0);
+    }
     const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
 #pragma unroll 1
     for (int i0 = i0a; i0 <= i0b; ++i0) {
@@ -460,33 +471,15 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
       e += x01.x * T.x - x01.y * T.y;
       stage_acc(c, i0, mul(x1, T));
       stage_acc(c, 7 + i1, mul(x0, T));
-    }
-  }
-  // w[u] belongs to last-block index K - S - u; after diagonal S no later one
-  // reaches index K - S, which is added to the staging area
-  double2 w[CH];
-#pragma unroll
-  for (int u = 0; u < CH; ++u) w[u] = make_double2(0.0, 0.0);
-#pragma unroll 1
-  for (int S = s_lo; S <= s_hi; ++S) {
-    double2 R[CH];
-#pragma unroll
-    for (int u = 0; u < CH; ++u) R[u] = make_double2(0.0, 0.0);
-    const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
-#pragma unroll 1
-    for (int i0 = i0a; i0 <= i0b; ++i0) {
-      const int i1 = S - i0;
-      double wc[CH];
-      wchunk<CH>(cb + (i0 * d1 + i1) * rw, nc, 0, CH, w0, w1, wc);
-      const double2 x01 = mul(vat(c, b0 + i0), vat(c, b1 + i1));
 #pragma unroll
       for (int u = 0; u < CH; ++u) cmac(R[u], wc[u], x01);
     }
 #pragma unroll
     for (int u = 0; u < CH; ++u) {
-      cfma(gs[u], R[u], vat(c, bl + K - S - u));
+      cfma(gs[u], R[u], vl[u]);
       cfma(w[u], R[u], vs[u]);
     }
+    // w[u] belongs to last-block index K - S - u; no later diagonal reaches K - S
     const int kf = K - S;
     if (kf >= 0 && kf < dl) stage_acc(c, 14 + kf, w[0]);
 #pragma unroll
