@@ -449,11 +449,15 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
   }
 #pragma unroll 1
   for (int S = s_lo; S <= s_hi; ++S) {
-    double2 vl[CH], q[CH], R[CH];
+    // last-block values: held over the diagonal's rows for the smaller block,
+    // read again after them for the 7-index block (register budget)
+    constexpr int NV = CH <= 5 ? CH : 1;
+    double2 vl[NV], q[CH], R[CH];
 #pragma unroll
     for (int u = 0; u < CH; ++u) {
-      vl[u] = vat(c, bl + K - S - u);  // out-of-block indices read finite neighbours; their coefficient is 0
-      q[u] = mul(vs[u], vl[u]);
+      const double2 v = vat(c, bl + K - S - u);  // out-of-block indices read finite neighbours; their coefficient is 0
+      if (CH <= 5) vl[u < NV ? u : 0] = v;
+      q[u] = mul(vs[u], v);
       R[u] = make_double2(0.0, 0.0);
     }
     const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
@@ -476,7 +480,7 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
     }
 #pragma unroll
     for (int u = 0; u < CH; ++u) {
-      cfma(gs[u], R[u], vl[u]);
+      cfma(gs[u], R[u], CH <= 5 ? vl[u < NV ? u : 0] : vat(c, bl + K - S - u));
       cfma(w[u], R[u], vs[u]);
     }
     // w[u] belongs to last-block index K - S - u; no later diagonal reaches K - S
