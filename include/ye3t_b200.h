@@ -214,8 +214,9 @@ typedef struct {
   const double* sym_term_coeff;     /* [S] */
   /* adjoint only: items of one shape paired per phase (one per half-warp) */
   int64_t group_count;
-  const int32_t* groups;          /* [group_count, 2] item indices (second -1: odd item out), by item
-                                     class (one adjoint launch each) then phase */
+  const int32_t* groups;          /* [group_count, 2] item indices (second -1: odd item out; both -1:
+                                     null pair, skipped), by item class (one adjoint launch each)
+                                     then phase; classes 3 and 4 are cut into equal runs, one per warp */
   const int32_t* group_offsets;   /* [5, phase_count + 1]: first group of each (class, phase) */
   /* adjoint only: derivatives of the symmetric outputs listed per input
      component (l^2 + m + l inside a radial channel) */

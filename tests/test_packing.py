@@ -112,3 +112,44 @@ def test_packed_tables_reproduce_oracle_features(golden, stem):
     ref = oracle.bundle_features(b, A)
     np.testing.assert_allclose(got, ref, rtol=1e-12, atol=1e-12 * np.abs(ref).max())
     np.testing.assert_allclose(got, g["B3"][:6], rtol=1e-11, atol=1e-12 * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("stem", ["ace_n8_l3_nu4_L0", "ace_diag_l3_nu3_L2"])
+def test_adjoint_groups_cover_items_once(stem):
+    """Every item sits in exactly one adjoint pair of its class; the four-block
+    run classes hold no phases, split into equal per-warp runs whose costs
+    differ by at most one item per shape."""
+    from ye3t_b200.packing import (GRAD_CLASSES, GRAD_RUN_CLASSES, GRAD_RUN_WARPS, grad_class,
+                                   item_grad_flops_per_atom)
+    b = _bundle(stem)
+    pb = pack_bundle(b, "cpu")
+    items = pb.arrays["items"].numpy()
+    groups = pb.arrays["groups"].numpy()
+    P = pb.arrays["phases"].shape[0]
+    off = pb.arrays["group_offsets"].numpy().reshape(GRAD_CLASSES, P + 1)
+    na = b.nmax * (b.lmax + 1) ** 2
+    seen = np.zeros(items.shape[0], dtype=np.int64)
+    for cls in range(GRAD_CLASSES):
+        assert off[cls, 0] == (off[cls - 1, -1] if cls else 0)
+        assert np.all(np.diff(off[cls]) >= 0)
+        rng = groups[off[cls, 0]:off[cls, -1]]
+        real = rng[rng[:, 0] >= 0]
+        if cls not in GRAD_RUN_CLASSES:
+            assert len(real) == len(rng)  # null pairs pad the run classes only
+        for x, y in real:
+            for i in (x, y):
+                if i >= 0:
+                    seen[i] += 1
+                    assert grad_class(items[i], na) == cls
+            if y >= 0:
+                assert np.array_equal(items[x, :5], items[y, :5])  # one shape per pair
+        if cls in GRAD_RUN_CLASSES and len(rng):
+            assert np.all(off[cls, 1:] == off[cls, -1])
+            assert len(rng) % GRAD_RUN_WARPS == 0
+            per = len(rng) // GRAD_RUN_WARPS
+            costs = [item_grad_flops_per_atom(items[[x for x, _ in rng[w * per:(w + 1) * per] if x >= 0]])
+                     for w in range(GRAD_RUN_WARPS)]
+            worst = max(item_grad_flops_per_atom(items[x:x + 1]) for x, _ in real)
+            shapes = len({tuple(items[x, :5]) for x, _ in real})
+            assert max(costs) - min(costs) <= shapes * worst
+    assert np.all(seen == 1)

@@ -515,6 +515,7 @@ __device__ __forceinline__ double adj4_run(const Ctx& c, const int2* __restrict_
 #pragma unroll 1
   for (; g < ge; ++g) {
     const int2 ig = __ldg(pairs + g);
+    if (ig.x < 0) continue;  // null pair padding a run (the whole warp skips it)
     const int mine = grp == 0 ? ig.x : ig.y;
     const bool mute = mine < 0;
     const Item it = load_item(items, mute ? ig.x : mine);
@@ -754,6 +755,7 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
 #pragma unroll 1
     for (int g = gb + warp; g < ge; g += kWarps) {
       const int2 ig = __ldg(groups + g);
+      if (ig.x < 0) continue;  // null pair
       const int mine = grp == 0 ? ig.x : ig.y;
       const bool mute = mine < 0;  // odd item out: the second half runs the first item unweighted, adding nothing
       const Item it = load_item(items, mute ? ig.x : mine);

@@ -402,6 +402,7 @@ GRAD_GROUP = 2
 GRAD_CLASSES = 5
 GRAD_STAGE = 14  # staged gradient entries per lane in the adjoint kernel
 GRAD_RUN_CLASSES = (3, 4)  # four-block classes: A entries only, one sorted run per warp
+GRAD_RUN_WARPS = 8  # warps of a run-class CTA (csrc/ace_grad.cu Y3B_RUN_WARPS)
 
 
 def grad_class(row, a_entries: Optional[int] = None) -> int:
@@ -441,18 +442,31 @@ def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
             # range.  Each shape's items are sorted by (register block, last
             # block, prefix blocks) and split in two halves, one per half-warp,
             # so that consecutive items of a lane share blocks (the kernel adds
-            # a block's gradient to G only when the block changes).
+            # a block's gradient to G only when the block changes).  The kernel
+            # cuts the range into GRAD_RUN_WARPS equal runs; item costs differ
+            # by shape, so each run holds an equal share of every shape, padded
+            # with null pairs (-1, -1) that the kernel skips.
             offsets[cls, 0] = len(groups)
             shapes = {}
             for i in range(items.shape[0]):
                 if grad_class(items[i], a_entries) == cls:
                     shapes.setdefault(tuple(int(v) for v in items[i, :5]), []).append(i)
+            runs = [[] for _ in range(GRAD_RUN_WARPS)]
             for key in sorted(shapes):
                 idx = sorted(shapes[key], key=lambda i: (int(items[i, 10]), int(items[i, 11]), int(items[i, 8]),
                                                          int(items[i, 9]), int(items[i, 5])))
                 h = (len(idx) + 1) // 2
-                for u in range(h):
-                    groups.append([idx[u], idx[u + h] if u + h < len(idx) else -1])
+                pairs = [[idx[u], idx[u + h] if u + h < len(idx) else -1] for u in range(h)]
+                # the longest runs so far take the smaller shares of this shape
+                order = sorted(range(GRAD_RUN_WARPS), key=lambda w: (len(runs[w]), w))
+                cut = np.linspace(0, h, GRAD_RUN_WARPS + 1).round().astype(int)
+                shares = sorted((pairs[cut[k]:cut[k + 1]] for k in range(GRAD_RUN_WARPS)), key=len, reverse=True)
+                for w, share in zip(order, shares):
+                    runs[w].extend(share)
+            if any(runs):
+                per = max(len(r) for r in runs)
+                for r in runs:
+                    groups.extend(r + [[-1, -1]] * (per - len(r)))
             offsets[cls, 1:] = len(groups)
             continue
         for ph, (_, _, begin, end) in enumerate(phases.tolist()):
