@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define Y3B_ABI_VERSION 5
+#define Y3B_ABI_VERSION 6
 
 /* dtype codes */
 #define Y3B_F32 0
@@ -40,6 +40,7 @@ extern "C" {
 /* device status word bits written by kernels that detect bad input */
 #define Y3B_STATUS_INDEX_RANGE 1
 #define Y3B_STATUS_CAPACITY 2
+#define Y3B_STATUS_TABLE 4 /* a table entry outside the kernel's bounds was skipped */
 
 /* ABI version; the reference's gate is core_abi_version()
  * (ye3t/runtime/csrc/execution_plan_torch.cpp:7925, checked at
@@ -216,8 +217,8 @@ typedef struct {
   int64_t group_count;
   const int32_t* groups;          /* [group_count, 2] item indices (second -1: odd item out; both -1:
                                      null pair, skipped), by item class (one adjoint launch each)
-                                     then phase; classes 3 and 4 are cut into equal runs, one per warp */
-  const int32_t* group_offsets;   /* [5, phase_count + 1]: first group of each (class, phase) */
+                                     then phase; classes 2 and 3 are cut into equal runs, one per warp */
+  const int32_t* group_offsets;   /* [4, phase_count + 1]: first group of each (class, phase) */
   /* adjoint only: derivatives of the symmetric outputs listed per input
      component (l^2 + m + l inside a radial channel) */
   int64_t sym_grad_count;
@@ -273,7 +274,9 @@ int y3b_ace_energy(const y3b_ace_tables* tables, const void* A, int64_t atom_cou
 
 /* Per-atom energies and G = dE/dA (complex128, A's layout; B is holomorphic
  * in A so dE = Re(sum G dA)).  Species outside [0, species_count) set
- * Y3B_STATUS_INDEX_RANGE in *status (nullable) and use species 0. */
+ * Y3B_STATUS_INDEX_RANGE in *status (nullable) and use species 0; an adjoint
+ * item grouped into a class whose bounds it exceeds sets Y3B_STATUS_TABLE
+ * and is skipped. */
 int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, int64_t atom_count,
                         const int32_t* species, const double* weights, int64_t species_count,
                         double* energy, void* dEdA, int32_t* status, void* stream);

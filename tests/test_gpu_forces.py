@@ -120,21 +120,27 @@ def test_energy_grad_many_ctas_matches_forward_and_repeats(golden):
     assert (G1 - G2).abs().max().item() <= 1e-12 * scale
 
 
-def test_energy_grad_single_slot_pool(golden):
-    """A channel-diagonal bundle (one radial channel, so one symmetric slot in the pool):
-    energies equal the forward kernel's and G is the derivative of the energy."""
+@pytest.mark.parametrize("stem", ["ace_diag_l3_nu3_L0", "ace_diag_l4_nu4_L0"])
+def test_energy_grad_single_slot_pool(golden, stem):
+    """Channel-diagonal bundles (one radial channel, so one symmetric slot in the pool;
+    l_max 4 adds four-block items whose last block of 9 indices exceeds the run path's
+    staging windows and must take the general path): energies equal the forward
+    kernel's, no status bit is set and G is the derivative of the energy."""
     small = golden("ace_small")
     from ye3t_b200.ace import ACEConfig, ACEEvaluator
-    b = _bundle("ace_diag_l3_nu3_L0")
+    b = _bundle(stem)
     rng = np.random.default_rng(5)
     ev = ACEEvaluator(b, DEV, config=ACEConfig(float(small["rc"]), float(small["lam"])),
                       weights=rng.normal(size=(2, b.feature_count)))
     N = 2048
-    A = torch.complex(torch.randn(N, 1, 16, dtype=torch.float64, device=DEV),
-                      torch.randn(N, 1, 16, dtype=torch.float64, device=DEV)) * 0.5
+    W = (b.lmax + 1) ** 2
+    A = torch.complex(torch.randn(N, 1, W, dtype=torch.float64, device=DEV),
+                      torch.randn(N, 1, W, dtype=torch.float64, device=DEV)) * 0.5
     sp = torch.as_tensor(rng.integers(0, 2, size=N), device=DEV, dtype=torch.int32)
     e_fwd = ev.energy_from_density(A, sp).cpu().numpy()
-    e_adj, G = ev.energy_grad(A, sp)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    e_adj, G = ev.energy_grad(A, sp, status=status)
+    assert int(status.item()) == 0
     np.testing.assert_allclose(e_adj.cpu().numpy(), e_fwd, rtol=1e-11, atol=1e-12)
     dA = torch.complex(torch.randn_like(A.real), torch.randn_like(A.real)) * 1e-6
     ep = ev.energy_from_density(A + dA, sp).sum().item()

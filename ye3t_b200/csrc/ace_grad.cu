@@ -39,9 +39,21 @@ constexpr int kGA = 16;
 constexpr int kGWarps = 8;       // warps per CTA of the classes with symmetric slots
 constexpr int kGWarpsRun = Y3B_RUN_WARPS;  // and of the four-block (A-only) classes
 
+// Item classes of the adjoint (packing.grad_class assigns them); each class
+// runs in its own kernel so that its item paths keep the register file.
+// Every slot-class launch reloads A and redoes the symmetric slots of the
+// phases it touches, so the slot items share two classes:
+//   0: 1 and 2 blocks, 3 and 4 blocks with a register block of <= 3, and
+//      anything the unrolled paths do not cover (generic path);
+//   1: 3 blocks with a register block of 5 or 7;
+//   2 / 3 (run classes): 4 blocks of A entries with a register block of 3 or
+//      5 / 7 and prefix and last blocks of at most 7, no symmetric slots.
+constexpr int kGradClasses = 4;
+constexpr int kFirstRunClass = 2;
+
 template <int CLS>
 struct ClassWarps {
-  static constexpr int value = CLS >= 3 ? kGWarpsRun : kGWarps;
+  static constexpr int value = CLS >= kFirstRunClass ? kGWarpsRun : kGWarps;
 };
 constexpr int kGPad = 16;
 constexpr int kStage = 14;     // staged gradient entries per lane (two blocks of <= 7)
@@ -430,9 +442,10 @@ __device__ __forceinline__ double adj4(const Ctx& c, const Item& it, int ds, int
 // energy and the prefix gradients, and R_u += c_u x0 x1; per diagonal
 // gs_u += R_u vl[K-S-u] and g_last[K-S-u] += R_u vs_u (through a window that
 // moves by one per diagonal).
-template <int CH>
+template <int CH, int NG>
 __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc, const double* __restrict__ coef,
-                                            double w0, double w1, double2 (&gs)[CH]) {
+                                            double w0, double w1, double2 (&gs)[NG]) {
+  static_assert(CH <= NG, "register-block gradient shorter than the block");
   double e = 0.0;
   constexpr int rw_1 = (CH + 1) & ~1;
   const int rw = nc == 2 ? 2 * CH : rw_1;
@@ -498,20 +511,26 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
   return e;
 }
 
-// A warp's contiguous run of four-block item pairs [g, ge) (classes 3, 4).
-// Packing sorts each shape's items by (register block, last block, prefix
-// blocks) and gives each half-warp a sorted half, so consecutive items of a
-// lane mostly share blocks: a target's gradient is added to G only when the
-// next item's block differs (a muted lane adds zeros, which changes nothing).
-template <int CH>
+// A warp's contiguous run of four-block item pairs [g, ge) (run classes 2, 3;
+// register blocks of 3 or 5 indices in class 2, 7 in class 3).  Packing sorts
+// each shape's items by (register block, last block, prefix blocks) and gives
+// each half-warp a sorted half, so consecutive items of a lane mostly share
+// blocks: a target's gradient is added to G only when the next item's block
+// differs (a muted lane adds zeros, which changes nothing).  Both half-warps
+// run items of one shape, so the per-item branches are warp-uniform.  An item
+// outside the run path's bounds (blocks longer than the 7-entry staging
+// windows, another register block) is skipped and reported in *bad.
+template <int CLS>
 __device__ __forceinline__ double adj4_run(const Ctx& c, const int2* __restrict__ pairs, int g, int ge, int grp,
                                            const int4* __restrict__ items, const double* __restrict__ coef,
-                                           const double* __restrict__ wz) {
+                                           const double* __restrict__ wz, bool& bad) {
+  constexpr bool kSmall = CLS == kFirstRunClass;  // register blocks of 3 or 5
+  constexpr int NG = kSmall ? 5 : 7;
   double e = 0.0;
-  double2 gs[CH];
+  double2 gs[NG];
 #pragma unroll
-  for (int u = 0; u < CH; ++u) gs[u] = make_double2(0.0, 0.0);
-  int p0 = -1, p1 = -1, ps = -1, pl = -1, n0 = 0, n1 = 0, nl = 0;
+  for (int u = 0; u < NG; ++u) gs[u] = make_double2(0.0, 0.0);
+  int p0 = -1, p1 = -1, ps = -1, pl = -1, n0 = 0, n1 = 0, ns = 0, nl = 0;
 #pragma unroll 1
   for (; g < ge; ++g) {
     const int2 ig = __ldg(pairs + g);
@@ -519,6 +538,11 @@ __device__ __forceinline__ double adj4_run(const Ctx& c, const int2* __restrict_
     const int mine = grp == 0 ? ig.x : ig.y;
     const bool mute = mine < 0;
     const Item it = load_item(items, mute ? ig.x : mine);
+    const int ds = 2 * ((it.sel >> 1) % 7) + 1;
+    if (it.d0 > 7 || it.d1 > 7 || it.dl > 7 || (kSmall ? (ds != 3 && ds != 5) : ds != 7)) {
+      bad = true;
+      continue;
+    }
     const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
     const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
     if (it.b0 != p0) {
@@ -533,11 +557,12 @@ __device__ __forceinline__ double adj4_run(const Ctx& c, const int2* __restrict_
       p1 = it.b1;
       n1 = it.d1;
     }
-    if (it.b2 != ps) {
-      if (ps >= 0) g_add<CH, 1>(c, ps, 0, CH, gs);
+    if (it.b2 != ps || (kSmall && ds != ns)) {
+      if (ps >= 0) g_add<NG, 1>(c, ps, 0, kSmall ? ns : NG, gs);
 #pragma unroll
-      for (int u = 0; u < CH; ++u) gs[u] = make_double2(0.0, 0.0);
+      for (int u = 0; u < NG; ++u) gs[u] = make_double2(0.0, 0.0);
       ps = it.b2;
+      ns = ds;
     }
     if (it.b3 != pl) {
       if (pl >= 0) stage_flush_impl<1, 7>(c, pl, 14, 0, nl);
@@ -545,11 +570,15 @@ __device__ __forceinline__ double adj4_run(const Ctx& c, const int2* __restrict_
       pl = it.b3;
       nl = it.dl;
     }
-    e += adj4_body<CH>(c, it, (it.sel & 1) + 1, coef, w0, w1, gs);
+    const int nc = (it.sel & 1) + 1;
+    if (kSmall && ds == 3)
+      e += adj4_body<3>(c, it, nc, coef, w0, w1, gs);
+    else
+      e += adj4_body<NG>(c, it, nc, coef, w0, w1, gs);
   }
   if (p0 >= 0) stage_flush_impl<1, 7>(c, p0, 0, 0, n0);
   if (p1 >= 0) stage_flush_impl<1, 7>(c, p1, 7, 0, n1);
-  if (ps >= 0) g_add<CH, 1>(c, ps, 0, CH, gs);
+  if (ps >= 0) g_add<NG, 1>(c, ps, 0, kSmall ? ns : NG, gs);
   if (pl >= 0) stage_flush_impl<1, 7>(c, pl, 14, 0, nl);
   return e;
 }
@@ -590,32 +619,21 @@ __device__ __noinline__ double adj_generic(const Ctx c, const Item it, int B, in
   return e;
 }
 
-// Item classes of the adjoint (packing.grad_class assigns them); each class
-// runs in its own kernel so that its item paths keep the register file, and
-// a chunk of the register block is the whole block for the large classes.
-// Every launch reloads A and redoes the symmetric slots of the phases it
-// touches, so the small item shapes share one class:
-//   0: 1 and 2 blocks, 3 and 4 blocks with a register block of <= 3, and
-//      anything the unrolled paths do not cover (generic path);
-//   1 / 2: 3 blocks with a register block of 5 / 7;
-//   3 / 4: 4 blocks with a register block of 5 / 7.
-constexpr int kGradClasses = 5;
-
 template <int CLS>
 __device__ __forceinline__ double adj_class(const Ctx& c, const Item& it, const double* __restrict__ coef,
                                             double w0, double w1, bool mute) {
   const int nc = (it.sel & 1) + 1, ds = 2 * ((it.sel >> 1) % 7) + 1, B = (it.sel >> 1) / 7 + 1;
   const bool fits3 = B == 3 && it.dl <= kStage;
   const bool fits4 = B == 4 && it.d0 <= 7 && it.d1 <= 7 && it.dl <= kStage;
+  static_assert(CLS < kFirstRunClass, "slot classes only");
   if (CLS == 0) {
     if (B == 1) return adj1(c, it, nc, coef, w0, w1, mute);
     if (B == 2) return adj2<8>(c, it, ds, nc, coef, w0, w1, mute);
     if (fits3 && ds <= 3) return adj3<3>(c, it, ds, nc, coef, w0, w1, mute);
     if (fits4 && ds <= 3) return adj4<3>(c, it, ds, nc, coef, w0, w1, mute);
   } else {
-    constexpr int CH = (CLS == 1 || CLS == 3) ? 5 : 7;
-    if ((CLS == 1 || CLS == 2) && fits3 && ds <= CH) return adj3<CH>(c, it, ds, nc, coef, w0, w1, mute);
-    if ((CLS == 3 || CLS == 4) && fits4 && ds <= CH) return adj4<CH>(c, it, ds, nc, coef, w0, w1, mute);
+    if (fits3 && ds == 7) return adj3<7>(c, it, ds, nc, coef, w0, w1, mute);
+    if (fits3 && ds <= 5) return adj3<5>(c, it, ds, nc, coef, w0, w1, mute);
   }
   return adj_generic(c, it, B, ds, nc, coef, w0, w1, mute);
 }
@@ -683,8 +701,8 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
   extern __shared__ double2 gsm[];
   constexpr int kWarps = ClassWarps<CLS>::value;
   __shared__ double red[kWarps][kGA];
-  // classes 3 and 4 (4-block items) read A entries only: no symmetric slots
-  constexpr bool kSlots = CLS <= 2;
+  // the run classes (4-block items) read A entries only: no symmetric slots
+  constexpr bool kSlots = CLS < kFirstRunClass;
   const int W = int((t.lmax + 1) * (t.lmax + 1));
   const int na = int(t.nmax) * W, so = int(t.sym_output_count);
   const int E = kSlots ? int(t.smem_entries) : na;
@@ -727,7 +745,9 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
     const int ge = __ldg(t.group_offsets + CLS * (t.phase_count + 1) + 1);
     const int per = (ge - gb + kWarps - 1) / kWarps;
     const int g0 = gb + warp * per, g1 = min(ge, g0 + per);
-    e_acc = adj4_run<(CLS == 3 ? 5 : 7)>(c, groups, g0, g1, grp, items, t.item_coef, wz);
+    bool bad = false;
+    e_acc = adj4_run<CLS>(c, groups, g0, g1, grp, items, t.item_coef, wz, bad);
+    if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
   }
 #pragma unroll 1
   for (int ph = 0; kSlots && ph < t.phase_count; ++ph) {
@@ -761,7 +781,7 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
       const Item it = load_item(items, mute ? ig.x : mine);
       const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
       const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
-      e_acc += adj_class<CLS>(c, it, t.item_coef, w0, w1, mute);
+      e_acc += adj_class<kSlots ? CLS : 0>(c, it, t.item_coef, w0, w1, mute);
     }
   }
   __syncthreads();
@@ -994,8 +1014,8 @@ extern "C" int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, 
   // the energies, the others add to them
 #define Y3B_GRAD_LAUNCH(CLS)                                                                              \
   Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_grad_kernel<CLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
-                                    int(CLS <= 2 ? smem : smem_a)));                                      \
-  ace_grad_kernel<CLS><<<int(grid), 32 * ClassWarps<CLS>::value, CLS <= 2 ? smem : smem_a, s>>>(       \
+                                    int(CLS < kFirstRunClass ? smem : smem_a)));                          \
+  ace_grad_kernel<CLS><<<int(grid), 32 * ClassWarps<CLS>::value, CLS < kFirstRunClass ? smem : smem_a, s>>>( \
       *tables, static_cast<const double2*>(A),                                                            \
                                                              atom_count, species, weights, species_count, \
                                                              energy, static_cast<double2*>(dEdA), status, \
@@ -1005,9 +1025,8 @@ extern "C" int y3b_ace_energy_grad(const y3b_ace_tables* tables, const void* A, 
   Y3B_GRAD_LAUNCH(1)
   Y3B_GRAD_LAUNCH(2)
   Y3B_GRAD_LAUNCH(3)
-  Y3B_GRAD_LAUNCH(4)
 #undef Y3B_GRAD_LAUNCH
-  static_assert(kGradClasses == 5, "one launch per class");
+  static_assert(kGradClasses == 4, "one launch per class");
   return Y3B_OK;
 }
 

@@ -399,30 +399,33 @@ def item_flops_per_atom(items: np.ndarray) -> float:
 
 
 GRAD_GROUP = 2
-GRAD_CLASSES = 5
+GRAD_CLASSES = 4
 GRAD_STAGE = 14  # staged gradient entries per lane in the adjoint kernel
-GRAD_RUN_CLASSES = (3, 4)  # four-block classes: A entries only, one sorted run per warp
+GRAD_RUN_CLASSES = (2, 3)  # four-block classes: A entries only, one sorted run per warp
 GRAD_RUN_WARPS = 8  # warps of a run-class CTA (csrc/ace_grad.cu Y3B_RUN_WARPS)
+GRAD_RUN_BLOCK = 7  # longest prefix / last block of a run-class item (staging windows of 7 entries)
 
 
-def grad_class(row, a_entries: Optional[int] = None) -> int:
+def grad_class(row, a_entries: int) -> int:
     """Adjoint item class (one kernel launch each, csrc/ace_grad.cu adj_class).
 
-    0: one and two blocks, three and four blocks with a register block of at
-    most 3 indices, and shapes the unrolled paths do not cover (wide register
-    blocks, long last blocks); 1 / 2: three blocks with a register block of 5
-    / 7; 3 / 4: four blocks with a register block of 5 / 7 whose blocks are
-    all A entries (``< a_entries``; those kernels hold no symmetric slots).
+    2 / 3: four blocks with a register block of 3 or 5 / 7 indices whose
+    blocks are all A entries (``< a_entries``; those kernels hold no
+    symmetric slots) and fit the run path's staging windows (prefix and last
+    blocks of at most GRAD_RUN_BLOCK indices); 1: three blocks with a
+    register block of 5 or 7; 0: everything else (one and two blocks, small
+    register blocks, four-block items reading symmetric outputs, and shapes
+    the unrolled paths do not cover: wide register blocks, long last blocks).
     """
     sel, d0, d1, dl = int(row[0]), int(row[1]), int(row[2]), int(row[3])
     B = (sel // 2) // 7 + 1
     ds = 2 * ((sel // 2) % 7) + 1
-    if B <= 2 or ds <= 3 or ds > 7 or dl > GRAD_STAGE or (B == 4 and (d0 > 7 or d1 > 7)):
-        return 0
-    if B == 4 and a_entries is not None and any(int(row[8 + b]) + dim > a_entries
-                                                for b, dim in enumerate((d0, d1, ds, dl))):
-        return 0
-    return (1 if B == 3 else 3) + (0 if ds <= 5 else 1)
+    if (B == 4 and 3 <= ds <= 7 and max(d0, d1, dl) <= GRAD_RUN_BLOCK
+            and all(int(row[8 + b]) + dim <= a_entries for b, dim in enumerate((d0, d1, ds, dl)))):
+        return 2 if ds <= 5 else 3
+    if B == 3 and 5 <= ds <= 7 and dl <= GRAD_STAGE:
+        return 1
+    return 0
 
 
 def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
