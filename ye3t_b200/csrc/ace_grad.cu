@@ -330,6 +330,111 @@ __device__ __forceinline__ double adj3(const Ctx& c, const Item& it, int ds, int
   return e;
 }
 
+// Three-block item (register block of ds <= CH indices) accumulating into
+// state that persists over a run of items: g_s in gs, g_last staged at
+// [0, dl).  The prefix gradient T_r of a row is added to G per row (a muted
+// lane has zero weights and adds zeros).
+template <int CH, int NG>
+__device__ __forceinline__ double adj3_acc(const Ctx& c, const Item& it, int ds, int nc,
+                                           const double* __restrict__ coef, double w0, double w1,
+                                           double2 (&gs)[NG]) {
+  static_assert(CH <= NG, "register-block gradient shorter than the block");
+  double e = 0.0;
+  const int rw = nc == 2 ? 2 * ds : ((ds + 1) & ~1);
+  const int b0 = it.b0, bs = it.b1, bl = it.b2, K = it.K, dl = it.dl;
+  const int r_lo = max(0, K - (ds - 1) - (dl - 1)), r_hi = min(it.d0 - 1, K);
+  if (r_lo > r_hi) return e;
+  const double* cb = coef + it.coef;
+  double2 vs[CH], w[CH];
+#pragma unroll
+  for (int u = 0; u < CH; ++u) {
+    vs[u] = u < ds ? vat(c, bs + u) : make_double2(0.0, 0.0);
+    w[u] = make_double2(0.0, 0.0);
+  }
+  // w[u] belongs to last-block index K - r - u (moves by one per row)
+#pragma unroll 1
+  for (int r = r_lo; r <= r_hi; ++r) {
+    double wc[CH];
+    wchunk<CH>(cb + r * rw, nc, 0, ds, w0, w1, wc);
+    const double2 x0 = vat(c, b0 + r);
+    double2 T = make_double2(0.0, 0.0);
+#pragma unroll
+    for (int u = 0; u < CH; ++u) {
+      // out-of-block last indices read finite neighbours; their coefficient is 0
+      const double2 vl = vat(c, bl + K - r - u);
+      cmac(T, wc[u], mul(vs[u], vl));
+      const double2 xw = cscale(wc[u], x0);
+      cfma(gs[u], xw, vl);
+      cfma(w[u], xw, vs[u]);
+    }
+    e += x0.x * T.x - x0.y * T.y;
+    g_add1(c, b0 + r, T);
+    const int kf = K - r;
+    if (kf >= 0 && kf < dl) stage_acc(c, kf, w[0]);
+#pragma unroll
+    for (int u = 0; u + 1 < CH; ++u) w[u] = w[u + 1];
+    w[CH - 1] = make_double2(0.0, 0.0);
+  }
+#pragma unroll
+  for (int u = 0; u + 1 < CH; ++u) {
+    const int k = K - r_hi - 1 - u;
+    if (k >= 0 && k < dl) stage_acc(c, k, w[u]);
+  }
+  return e;
+}
+
+// A warp's sorted run of three-block item pairs [g, ge) inside one phase
+// (class 1: register blocks of 5 or 7 indices).  As in the four-block run
+// path, the register block's gradient stays in registers and the last
+// block's in the staging area until the next item's block differs.  An item
+// outside the path's bounds is skipped and reported in *bad.
+__device__ __forceinline__ double adj3_run(const Ctx& c, const int2* __restrict__ pairs, int g, int ge, int grp,
+                                           const int4* __restrict__ items, const double* __restrict__ coef,
+                                           const double* __restrict__ wz, bool& bad) {
+  constexpr int NG = 7;
+  double e = 0.0;
+  double2 gs[NG];
+#pragma unroll
+  for (int u = 0; u < NG; ++u) gs[u] = make_double2(0.0, 0.0);
+  int ps = -1, ns = 0, pl = -1, nl = 0;
+#pragma unroll 1
+  for (; g < ge; ++g) {
+    const int2 ig = __ldg(pairs + g);
+    if (ig.x < 0) continue;  // null pair padding a run (the whole warp skips it)
+    const int mine = grp == 0 ? ig.x : ig.y;
+    const bool mute = mine < 0;
+    const Item it = load_item(items, mute ? ig.x : mine);
+    const int ds = 2 * ((it.sel >> 1) % 7) + 1, B = (it.sel >> 1) / 7 + 1;
+    if (B != 3 || it.dl > kStage || (ds != 5 && ds != 7)) {
+      bad = true;
+      continue;
+    }
+    const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
+    const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
+    if (it.b1 != ps || ds != ns) {
+      if (ps >= 0) g_add<NG, 1>(c, ps, 0, ns, gs);
+#pragma unroll
+      for (int u = 0; u < NG; ++u) gs[u] = make_double2(0.0, 0.0);
+      ps = it.b1;
+      ns = ds;
+    }
+    if (it.b2 != pl || it.dl != nl) {
+      if (pl >= 0) stage_flush_impl<1, kStage>(c, pl, 0, 0, nl);
+      stage_zero(c, 0, it.dl);
+      pl = it.b2;
+      nl = it.dl;
+    }
+    const int nc = (it.sel & 1) + 1;
+    if (ds == 5)
+      e += adj3_acc<5>(c, it, ds, nc, coef, w0, w1, gs);
+    else
+      e += adj3_acc<7>(c, it, ds, nc, coef, w0, w1, gs);
+  }
+  if (ps >= 0) g_add<NG, 1>(c, ps, 0, ns, gs);
+  if (pl >= 0) stage_flush_impl<1, kStage>(c, pl, 0, 0, nl);
+  return e;
+}
+
 // Four blocks: rows (i0, i1) of prefix blocks 0 and 1 (d0 <= d1 <= 7), the
 // register block s and the last block l = K - S - j with S = i0 + i1 (dl <=
 // 14).  Rows of one anti-diagonal S share q_j = vs_j vl_{K-S-j}.  Two passes
@@ -625,16 +730,11 @@ __device__ __forceinline__ double adj_class(const Ctx& c, const Item& it, const 
   const int nc = (it.sel & 1) + 1, ds = 2 * ((it.sel >> 1) % 7) + 1, B = (it.sel >> 1) / 7 + 1;
   const bool fits3 = B == 3 && it.dl <= kStage;
   const bool fits4 = B == 4 && it.d0 <= 7 && it.d1 <= 7 && it.dl <= kStage;
-  static_assert(CLS < kFirstRunClass, "slot classes only");
-  if (CLS == 0) {
-    if (B == 1) return adj1(c, it, nc, coef, w0, w1, mute);
-    if (B == 2) return adj2<8>(c, it, ds, nc, coef, w0, w1, mute);
-    if (fits3 && ds <= 3) return adj3<3>(c, it, ds, nc, coef, w0, w1, mute);
-    if (fits4 && ds <= 3) return adj4<3>(c, it, ds, nc, coef, w0, w1, mute);
-  } else {
-    if (fits3 && ds == 7) return adj3<7>(c, it, ds, nc, coef, w0, w1, mute);
-    if (fits3 && ds <= 5) return adj3<5>(c, it, ds, nc, coef, w0, w1, mute);
-  }
+  static_assert(CLS == 0, "class 0 only (class 1 and the run classes walk sorted runs)");
+  if (B == 1) return adj1(c, it, nc, coef, w0, w1, mute);
+  if (B == 2) return adj2<8>(c, it, ds, nc, coef, w0, w1, mute);
+  if (fits3 && ds <= 3) return adj3<3>(c, it, ds, nc, coef, w0, w1, mute);
+  if (fits4 && ds <= 3) return adj4<3>(c, it, ds, nc, coef, w0, w1, mute);
   return adj_generic(c, it, B, ds, nc, coef, w0, w1, mute);
 }
 
@@ -772,6 +872,15 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
       cur0 = pr.x;
       cur1 = pr.y;
     }
+    if (CLS == 1) {
+      // one sorted run per warp (packing pads the phase's range to equal runs)
+      const int per = (ge - gb + kWarps - 1) / kWarps;
+      const int g0 = gb + warp * per, g1 = min(ge, g0 + per);
+      bool bad = false;
+      e_acc += adj3_run(c, groups, g0, g1, grp, items, t.item_coef, wz, bad);
+      if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
+      continue;
+    }
 #pragma unroll 1
     for (int g = gb + warp; g < ge; g += kWarps) {
       const int2 ig = __ldg(groups + g);
@@ -781,7 +890,7 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
       const Item it = load_item(items, mute ? ig.x : mine);
       const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
       const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
-      e_acc += adj_class<kSlots ? CLS : 0>(c, it, t.item_coef, w0, w1, mute);
+      e_acc += adj_class<0>(c, it, t.item_coef, w0, w1, mute);
     }
   }
   __syncthreads();

@@ -402,7 +402,8 @@ GRAD_GROUP = 2
 GRAD_CLASSES = 4
 GRAD_STAGE = 14  # staged gradient entries per lane in the adjoint kernel
 GRAD_RUN_CLASSES = (2, 3)  # four-block classes: A entries only, one sorted run per warp
-GRAD_RUN_WARPS = 8  # warps of a run-class CTA (csrc/ace_grad.cu Y3B_RUN_WARPS)
+GRAD_RUN_WARPS = 8  # warps of a run-class CTA (csrc/ace_grad.cu Y3B_RUN_WARPS) and of a slot-class CTA
+GRAD_SLOT_RUN_CLASS = 1  # three-block class: one sorted run per warp and phase
 GRAD_RUN_BLOCK = 7  # longest prefix / last block of a run-class item (staging windows of 7 entries)
 
 
@@ -428,48 +429,60 @@ def grad_class(row, a_entries: int) -> int:
     return 0
 
 
+def _balanced_runs(shapes: Dict[tuple, list], items: np.ndarray, key) -> list:
+    """Item pairs of one (class, phase) range laid out as GRAD_RUN_WARPS equal runs.
+
+    Each shape's items are sorted by ``key`` (blocks first, so that
+    consecutive items of a lane share blocks and the kernel adds a block's
+    gradient to G only when the block changes) and split in two halves, one
+    per half-warp.  The kernel cuts the range into GRAD_RUN_WARPS equal runs;
+    item costs differ by shape, so each run holds an equal share of every
+    shape, padded with null pairs (-1, -1) that the kernel skips.
+    """
+    runs = [[] for _ in range(GRAD_RUN_WARPS)]
+    for shape in sorted(shapes):
+        idx = sorted(shapes[shape], key=key)
+        h = (len(idx) + 1) // 2
+        pairs = [[idx[u], idx[u + h] if u + h < len(idx) else -1] for u in range(h)]
+        # the longest runs so far take the smaller shares of this shape
+        order = sorted(range(GRAD_RUN_WARPS), key=lambda w: (len(runs[w]), w))
+        cut = np.linspace(0, h, GRAD_RUN_WARPS + 1).round().astype(int)
+        shares = sorted((pairs[cut[k]:cut[k + 1]] for k in range(GRAD_RUN_WARPS)), key=len, reverse=True)
+        for w, share in zip(order, shares):
+            runs[w].extend(share)
+    out = []
+    if any(runs):
+        per = max(len(r) for r in runs)
+        for r in runs:
+            out.extend(r + [[-1, -1]] * (per - len(r)))
+    return out
+
+
 def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
     """Item pairs of the adjoint kernel, per item class and phase.
 
     Each half-warp runs one item; pairing two items of one shape (dispatch
-    code, loop extents, K) keeps the warp's control flow identical.  Within a
-    shape, items sharing a coefficient table stay adjacent.  Returns
-    ``groups [P, 2]`` (-1 for a shape's odd item out), ordered by class then
+    code, loop extents, K) keeps the warp's control flow identical.  Class 0
+    takes a phase's pairs round robin over the warps (items sharing a
+    coefficient table adjacent); class 1 gives each warp a sorted run of the
+    phase (register block, last block, prefix); the A-entry-only run classes
+    ignore phases (every pair in phase 0's range) and sort by (register
+    block, last block, prefix blocks).  Returns ``groups [P, 2]`` (-1 for a
+    shape's odd item out, (-1, -1) for run padding), ordered by class then
     phase, and ``group_offsets [GRAD_CLASSES, phase_count + 1]`` (flattened).
     """
     groups = []
     offsets = np.zeros((GRAD_CLASSES, phases.shape[0] + 1), dtype=np.int32)
     for cls in range(GRAD_CLASSES):
         if cls in GRAD_RUN_CLASSES:
-            # A-entry-only classes ignore phases: every pair goes to phase 0's
-            # range.  Each shape's items are sorted by (register block, last
-            # block, prefix blocks) and split in two halves, one per half-warp,
-            # so that consecutive items of a lane share blocks (the kernel adds
-            # a block's gradient to G only when the block changes).  The kernel
-            # cuts the range into GRAD_RUN_WARPS equal runs; item costs differ
-            # by shape, so each run holds an equal share of every shape, padded
-            # with null pairs (-1, -1) that the kernel skips.
             offsets[cls, 0] = len(groups)
             shapes = {}
             for i in range(items.shape[0]):
                 if grad_class(items[i], a_entries) == cls:
                     shapes.setdefault(tuple(int(v) for v in items[i, :5]), []).append(i)
-            runs = [[] for _ in range(GRAD_RUN_WARPS)]
-            for key in sorted(shapes):
-                idx = sorted(shapes[key], key=lambda i: (int(items[i, 10]), int(items[i, 11]), int(items[i, 8]),
-                                                         int(items[i, 9]), int(items[i, 5])))
-                h = (len(idx) + 1) // 2
-                pairs = [[idx[u], idx[u + h] if u + h < len(idx) else -1] for u in range(h)]
-                # the longest runs so far take the smaller shares of this shape
-                order = sorted(range(GRAD_RUN_WARPS), key=lambda w: (len(runs[w]), w))
-                cut = np.linspace(0, h, GRAD_RUN_WARPS + 1).round().astype(int)
-                shares = sorted((pairs[cut[k]:cut[k + 1]] for k in range(GRAD_RUN_WARPS)), key=len, reverse=True)
-                for w, share in zip(order, shares):
-                    runs[w].extend(share)
-            if any(runs):
-                per = max(len(r) for r in runs)
-                for r in runs:
-                    groups.extend(r + [[-1, -1]] * (per - len(r)))
+            groups.extend(_balanced_runs(shapes, items, lambda i: (int(items[i, 10]), int(items[i, 11]),
+                                                                   int(items[i, 8]), int(items[i, 9]),
+                                                                   int(items[i, 5]))))
             offsets[cls, 1:] = len(groups)
             continue
         for ph, (_, _, begin, end) in enumerate(phases.tolist()):
@@ -478,6 +491,10 @@ def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
             for i in range(begin, end):
                 if grad_class(items[i], a_entries) == cls:
                     shapes.setdefault(tuple(int(v) for v in items[i, :5]), []).append(i)
+            if cls == GRAD_SLOT_RUN_CLASS:
+                groups.extend(_balanced_runs(shapes, items, lambda i: (int(items[i, 9]), int(items[i, 10]),
+                                                                       int(items[i, 8]), int(items[i, 5]))))
+                continue
             for key in sorted(shapes):
                 idx = sorted(shapes[key], key=lambda i: (int(items[i, 5]), int(items[i, 6])))
                 for u in range(0, len(idx), GRAD_GROUP):
