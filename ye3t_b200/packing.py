@@ -429,6 +429,33 @@ def grad_class(row, a_entries: int) -> int:
     return 0
 
 
+GRAD_ITEM_OVERHEAD = 200.0  # flop-equivalents of an item's fixed work (loads, flushes), for balancing only
+
+
+def _pair_cost(items: np.ndarray, i: int) -> float:
+    """Balancing weight of one item pair (both halves run the same shape):
+    its adjoint flops plus a fixed per-item charge."""
+    return item_grad_flops_per_atom(items[i:i + 1]) + GRAD_ITEM_OVERHEAD
+
+
+def _round_robin_balanced(pairs: list, costs: list) -> list:
+    """Pairs ordered so that the kernel's round robin (pair g to warp g mod
+    GRAD_RUN_WARPS) gives every warp a near-equal cost: longest first to the
+    least loaded warp, then interleaved, null pairs filling the short warps."""
+    sets = [[] for _ in range(GRAD_RUN_WARPS)]
+    load = [0.0] * GRAD_RUN_WARPS
+    for k in sorted(range(len(pairs)), key=lambda k: -costs[k]):
+        w = min(range(GRAD_RUN_WARPS), key=lambda v: (load[v], len(sets[v]), v))
+        sets[w].append(pairs[k])
+        load[w] += costs[k]
+    rounds = max((len(x) for x in sets), default=0)
+    out = []
+    for r in range(rounds):
+        for w in range(GRAD_RUN_WARPS):
+            out.append(sets[w][r] if r < len(sets[w]) else [-1, -1])
+    return out
+
+
 def _balanced_runs(shapes: Dict[tuple, list], items: np.ndarray, key) -> list:
     """Item pairs of one (class, phase) range laid out as GRAD_RUN_WARPS equal runs.
 
@@ -444,7 +471,8 @@ def _balanced_runs(shapes: Dict[tuple, list], items: np.ndarray, key) -> list:
         idx = sorted(shapes[shape], key=key)
         h = (len(idx) + 1) // 2
         pairs = [[idx[u], idx[u + h] if u + h < len(idx) else -1] for u in range(h)]
-        # the longest runs so far take the smaller shares of this shape
+        # the longest runs so far take the smaller shares of this shape (a
+        # cost-ordered assignment measured slower: it breaks block sharing)
         order = sorted(range(GRAD_RUN_WARPS), key=lambda w: (len(runs[w]), w))
         cut = np.linspace(0, h, GRAD_RUN_WARPS + 1).round().astype(int)
         shares = sorted((pairs[cut[k]:cut[k + 1]] for k in range(GRAD_RUN_WARPS)), key=len, reverse=True)
@@ -463,13 +491,14 @@ def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
 
     Each half-warp runs one item; pairing two items of one shape (dispatch
     code, loop extents, K) keeps the warp's control flow identical.  Class 0
-    takes a phase's pairs round robin over the warps (items sharing a
-    coefficient table adjacent); class 1 gives each warp a sorted run of the
+    takes a phase's pairs round robin over the warps; class 1 gives each warp a sorted run of the
     phase (register block, last block, prefix); the A-entry-only run classes
     ignore phases (every pair in phase 0's range) and sort by (register
     block, last block, prefix blocks).  Returns ``groups [P, 2]`` (-1 for a
     shape's odd item out, (-1, -1) for run padding), ordered by class then
     phase, and ``group_offsets [GRAD_CLASSES, phase_count + 1]`` (flattened).
+    Class 0's pairs are spread over the warps by cost (``_round_robin_balanced``),
+    since a phase ends in a barrier that waits for its slowest warp.
     """
     groups = []
     offsets = np.zeros((GRAD_CLASSES, phases.shape[0] + 1), dtype=np.int32)
@@ -495,11 +524,15 @@ def _grad_groups(items: np.ndarray, phases: np.ndarray, a_entries: int):
                 groups.extend(_balanced_runs(shapes, items, lambda i: (int(items[i, 9]), int(items[i, 10]),
                                                                        int(items[i, 8]), int(items[i, 5]))))
                 continue
+            pairs, costs = [], []
             for key in sorted(shapes):
                 idx = sorted(shapes[key], key=lambda i: (int(items[i, 5]), int(items[i, 6])))
+                c = _pair_cost(items, idx[0])
                 for u in range(0, len(idx), GRAD_GROUP):
                     g = idx[u:u + GRAD_GROUP]
-                    groups.append(g + [-1] * (GRAD_GROUP - len(g)))
+                    pairs.append(g + [-1] * (GRAD_GROUP - len(g)))
+                    costs.append(c)
+            groups.extend(_round_robin_balanced(pairs, costs))
         offsets[cls, -1] = len(groups)
     return np.asarray(groups, dtype=np.int32).reshape(-1, GRAD_GROUP), offsets.reshape(-1)
 
