@@ -738,15 +738,70 @@ __device__ __forceinline__ double adj_class(const Ctx& c, const Item& it, const 
   return adj_generic(c, it, B, ds, nc, coef, w0, w1, mute);
 }
 
+// Fill and pull-back tables of the symmetric slots.  At a phase change no
+// item is running, so the per-lane staging area is free: the CTA copies the
+// tables there (about 16 KB for l_max 3) and the fill and the pull read them
+// from shared memory instead of through chains of L2 reads; tables larger
+// than the staging area are read from global memory.
+struct SymTabs {
+  const int4* outs;     // [so]: l^2, term begin, term end
+  const uint32_t* fac;  // [nterm] 4 x u8 factors
+  const double* co;     // [nterm]
+  int nterm;
+  const int32_t* goff;  // [W + 1]
+  const int2* gidx;     // [T]: output, 4 x u8 remaining factors
+  const double* gco;    // [T]
+};
+
+__device__ __forceinline__ int sym_term_total(const y3b_ace_tables& t) {
+  const int so = int(t.sym_output_count);
+  return so > 0 ? __ldg(t.sym_outputs + 4 * (so - 1) + 2) : 0;  // terms are packed in output order
+}
+
+__device__ __forceinline__ SymTabs sym_tabs_global(const y3b_ace_tables& t, int nterm) {
+  return SymTabs{reinterpret_cast<const int4*>(t.sym_outputs), t.sym_term_factors, t.sym_term_coeff, nterm,
+                 t.sym_grad_offsets, reinterpret_cast<const int2*>(t.sym_grad_index), t.sym_grad_coeff};
+}
+
+__host__ __device__ __forceinline__ size_t sym_tabs_bytes(int so, int nterm, int W, int64_t T) {
+  const size_t a = size_t(16) * so, b = (size_t(4) * nterm + 15) & ~size_t(15), c = size_t(8) * nterm;
+  const size_t d = (size_t(4) * (W + 1) + 15) & ~size_t(15);
+  return a + b + ((c + 15) & ~size_t(15)) + d + size_t(16) * T;
+}
+
+// All threads copy; the caller synchronises before reading.  base is 16-byte aligned.
+__device__ __forceinline__ SymTabs sym_tabs_stage(const y3b_ace_tables& t, char* base, int nterm, int W) {
+  const int so = int(t.sym_output_count), T = int(t.sym_grad_count);
+  int4* outs = reinterpret_cast<int4*>(base);
+  uint32_t* fac = reinterpret_cast<uint32_t*>(base + size_t(16) * so);
+  double* co = reinterpret_cast<double*>(reinterpret_cast<char*>(fac) + ((size_t(4) * nterm + 15) & ~size_t(15)));
+  int32_t* goff = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(co) + ((size_t(8) * nterm + 15) & ~size_t(15)));
+  int2* gidx = reinterpret_cast<int2*>(reinterpret_cast<char*>(goff) + ((size_t(4) * (W + 1) + 15) & ~size_t(15)));
+  double* gco = reinterpret_cast<double*>(gidx + T);
+  const int4* g_outs = reinterpret_cast<const int4*>(t.sym_outputs);
+  const int2* g_gidx = reinterpret_cast<const int2*>(t.sym_grad_index);
+  for (int i = threadIdx.x; i < so; i += blockDim.x) outs[i] = __ldg(g_outs + i);
+  for (int i = threadIdx.x; i < nterm; i += blockDim.x) {
+    fac[i] = __ldg(t.sym_term_factors + i);
+    co[i] = __ldg(t.sym_term_coeff + i);
+  }
+  for (int i = threadIdx.x; i <= W; i += blockDim.x) goff[i] = __ldg(t.sym_grad_offsets + i);
+  for (int i = threadIdx.x; i < T; i += blockDim.x) {
+    gidx[i] = __ldg(g_gidx + i);
+    gco[i] = __ldg(t.sym_grad_coeff + i);
+  }
+  return SymTabs{outs, fac, co, nterm, goff, gidx, gco};
+}
+
 // Symmetric slot: fill values from A.  Threads cover (atom, output) pairs.
-__device__ __forceinline__ void grad_fill_slot(const y3b_ace_tables& t, double2* __restrict__ val, int W, int slot,
-                                               int ch) {
+__device__ __forceinline__ void grad_fill_slot(const y3b_ace_tables& t, const SymTabs& tb, double2* __restrict__ val,
+                                               int W, int slot, int ch) {
   const int na = int(t.nmax) * W, so = int(t.sym_output_count);
-  const int4* outs = reinterpret_cast<const int4*>(t.sym_outputs);
   const int atom = threadIdx.x % kGA;
   for (int o = threadIdx.x / kGA; o < so; o += blockDim.x / kGA) {
-    const int4 r = __ldg(outs + o);
-    val[(na + slot * so + o) * kGA + atom] = sym_output(t, r.y, r.z, val + (ch * W + r.x) * kGA + atom, kGA);
+    const int4 r = tb.outs[o];
+    val[(na + slot * so + o) * kGA + atom] =
+        sym_output_tab(tb.fac, tb.co, r.y, min(r.z, tb.nterm), val + (ch * W + r.x) * kGA + atom, kGA);
   }
 }
 
@@ -754,22 +809,21 @@ __device__ __forceinline__ void grad_fill_slot(const y3b_ace_tables& t, double2*
 // dE/dx_p += sum over monomials containing p of g_o * m * c * prod(other
 // factors), from the component-major derivative table.  Each thread owns
 // (atom, component) pairs, so the additions need no atomics.
-__device__ __forceinline__ void grad_pull_slot(const y3b_ace_tables& t, const double2* __restrict__ val,
-                                               double* __restrict__ Gr, double* __restrict__ Gi, int W, int slot,
-                                               int ch) {
+__device__ __forceinline__ void grad_pull_slot(const y3b_ace_tables& t, const SymTabs& tb,
+                                               const double2* __restrict__ val, double* __restrict__ Gr,
+                                               double* __restrict__ Gi, int W, int slot, int ch) {
   const int na = int(t.nmax) * W, so = int(t.sym_output_count);
-  const int2* gidx = reinterpret_cast<const int2*>(t.sym_grad_index);
   for (int task = threadIdx.x; task < kGA * W; task += blockDim.x) {
     const int atom = task % kGA, comp = task / kGA;
     const double2* x = val + ch * W * kGA + atom;
     const int gb = (na + slot * so) * kGA + atom;
     double ar = 0.0, ai = 0.0;
-    const int qe = __ldg(t.sym_grad_offsets + comp + 1);
-    for (int q = __ldg(t.sym_grad_offsets + comp); q < qe; ++q) {
-      const int2 r = __ldg(gidx + q);
+    const int qe = tb.goff[comp + 1];
+    for (int q = tb.goff[comp]; q < qe; ++q) {
+      const int2 r = tb.gidx[q];
       const double gr = Gr[gb + r.x * kGA], gi = Gi[gb + r.x * kGA];
       if (gr == 0.0 && gi == 0.0) continue;
-      double2 m = make_double2(__ldg(t.sym_grad_coeff + q), 0.0);
+      double2 m = make_double2(tb.gco[q], 0.0);
       const uint32_t f = uint32_t(r.y);
 #pragma unroll
       for (int k = 0; k < 3; ++k) {
@@ -838,6 +892,11 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
   const int2* groups = reinterpret_cast<const int2*>(t.groups);
   int cur0 = -2, cur1 = -2;
   double e_acc = 0.0;
+  // slot tables staged in the staging area at phase changes when they fit
+  const int nterm = kSlots ? sym_term_total(t) : 0;
+  const bool tabs_staged =
+      kSlots && sym_tabs_bytes(so, nterm, W, t.sym_grad_count) <= size_t(kWarps) * kStageLanes * 32 * sizeof(double2);
+  const SymTabs tg = sym_tabs_global(t, nterm);
   if (!kSlots) {
     // four-block classes: all pairs sit in phase 0's range (no slots), one
     // contiguous run per warp
@@ -856,17 +915,19 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
     const int gb = __ldg(goff + ph), ge = __ldg(goff + ph + 1);
     if (gb == ge) continue;  // no items of this class in the phase
     if (kSlots && (pr.x != cur0 || pr.y != cur1)) {
-      __syncthreads();  // the previous phase is done with the slots (and A is loaded)
-      if (pr.x != cur0 && cur0 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 0, cur0);
-      if (pr.y != cur1 && cur1 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 1, cur1);
+      __syncthreads();  // the previous phase is done with the slots and the staging area
+      const SymTabs tb = tabs_staged ? sym_tabs_stage(t, reinterpret_cast<char*>(stg), nterm, W) : tg;
+      if (tabs_staged) __syncthreads();
+      if (pr.x != cur0 && cur0 >= 0) grad_pull_slot(t, tb, val, Gr, Gi, W, 0, cur0);
+      if (pr.y != cur1 && cur1 >= 0) grad_pull_slot(t, tb, val, Gr, Gi, W, 1, cur1);
       __syncthreads();
       if (pr.x != cur0) {
         grad_clear_slot(Gr, Gi, na, so, 0);
-        grad_fill_slot(t, val, W, 0, pr.x);
+        grad_fill_slot(t, tb, val, W, 0, pr.x);
       }
       if (pr.y != cur1) {
         if (t.smem_entries >= na + 2 * so) grad_clear_slot(Gr, Gi, na, so, 1);
-        if (pr.y >= 0 && t.smem_entries >= na + 2 * so) grad_fill_slot(t, val, W, 1, pr.y);
+        if (pr.y >= 0 && t.smem_entries >= na + 2 * so) grad_fill_slot(t, tb, val, W, 1, pr.y);
       }
       __syncthreads();
       cur0 = pr.x;
@@ -894,8 +955,12 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
     }
   }
   __syncthreads();
-  if (kSlots && cur0 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 0, cur0);
-  if (kSlots && cur1 >= 0) grad_pull_slot(t, val, Gr, Gi, W, 1, cur1);
+  if (kSlots && (cur0 >= 0 || cur1 >= 0)) {
+    const SymTabs tb = tabs_staged ? sym_tabs_stage(t, reinterpret_cast<char*>(stg), nterm, W) : tg;
+    if (tabs_staged) __syncthreads();
+    if (cur0 >= 0) grad_pull_slot(t, tb, val, Gr, Gi, W, 0, cur0);
+    if (cur1 >= 0) grad_pull_slot(t, tb, val, Gr, Gi, W, 1, cur1);
+  }
   e_acc += __shfl_xor_sync(0xffffffffu, e_acc, 16);
   if (grp == 0) red[warp][atom] = e_acc;
   __syncthreads();
