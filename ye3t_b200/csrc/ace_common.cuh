@@ -62,34 +62,6 @@ struct RowWidth {
 // input component multiplied in increasing component order
 // (ye3t_runtime_core.cpp:5279).  Factors are 4 x u8 component indices
 // (repeated for powers, 255 = unused).
-// The same sum with the term tables at given addresses (shared-memory copies).
-template <typename C2>
-__device__ __forceinline__ C2 sym_output_tab(const uint32_t* fac, const double* co, int tb, int te, const C2* x,
-                                             int stride) {
-  using R = decltype(C2{}.x);
-  C2 acc = cz<C2>();
-  for (int q = tb; q < te; ++q) {
-    const uint32_t f = fac[q];
-    C2 m = cz<C2>();
-    m.x = R(co[q]);
-    int k = 0;
-    while (k < 4) {
-      const int ci = (f >> (8 * k)) & 255;
-      if (ci == 255) break;
-      const C2 xv = x[ci * stride];
-      C2 pw = xv;
-      ++k;
-      while (k < 4 && int((f >> (8 * k)) & 255) == ci) {
-        pw = mul(pw, xv);
-        ++k;
-      }
-      m = mul(m, pw);
-    }
-    acc = add(acc, m);
-  }
-  return acc;
-}
-
 template <typename C2>
 __device__ __forceinline__ C2 sym_output(const y3b_ace_tables& t, int tb, int te, const C2* x, int stride) {
   using R = decltype(C2{}.x);

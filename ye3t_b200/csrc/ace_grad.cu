@@ -559,23 +559,25 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
   const int s_lo = max(0, K - (CH - 1) - (dl - 1)), s_hi = min(d0 + d1 - 2, K);
   if (s_lo > s_hi) return e;
   const double* cb = coef + it.coef;
-  double2 vs[CH], w[CH];
+  // register-block values: held in registers for the smaller blocks, read
+  // from shared memory at each use for the 7-index block (register budget)
+  constexpr int NS = CH <= 5 ? CH : 1;
+  double2 vs[NS], w[CH];
+  auto vsu = [&](int u) { return CH <= 5 ? vs[u < NS ? u : 0] : vat(c, bs + u); };
 #pragma unroll
   for (int u = 0; u < CH; ++u) {
-    vs[u] = vat(c, bs + u);
+    if (CH <= 5) vs[u < NS ? u : 0] = vat(c, bs + u);
     w[u] = make_double2(0.0, 0.0);
   }
 #pragma unroll 1
   for (int S = s_lo; S <= s_hi; ++S) {
-    // last-block values: held over the diagonal's rows for the smaller block,
-    // read again after them for the 7-index block (register budget)
-    constexpr int NV = CH <= 5 ? CH : 1;
-    double2 vl[NV], q[CH], R[CH];
+    // last-block values of the diagonal, held over its rows
+    double2 vl[CH], q[CH], R[CH];
 #pragma unroll
     for (int u = 0; u < CH; ++u) {
       const double2 v = vat(c, bl + K - S - u);  // out-of-block indices read finite neighbours; their coefficient is 0
-      if (CH <= 5) vl[u < NV ? u : 0] = v;
-      q[u] = mul(vs[u], v);
+      vl[u] = v;
+      q[u] = mul(vsu(u), v);
       R[u] = make_double2(0.0, 0.0);
     }
     const int i0a = max(0, S - (d1 - 1)), i0b = min(d0 - 1, S);
@@ -598,8 +600,8 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
     }
 #pragma unroll
     for (int u = 0; u < CH; ++u) {
-      cfma(gs[u], R[u], CH <= 5 ? vl[u < NV ? u : 0] : vat(c, bl + K - S - u));
-      cfma(w[u], R[u], vs[u]);
+      cfma(gs[u], R[u], vl[u]);
+      cfma(w[u], R[u], vsu(u));
     }
     // w[u] belongs to last-block index K - S - u; no later diagonal reaches K - S
     const int kf = K - S;
@@ -794,14 +796,35 @@ __device__ __forceinline__ SymTabs sym_tabs_stage(const y3b_ace_tables& t, char*
 }
 
 // Symmetric slot: fill values from A.  Threads cover (atom, output) pairs.
+// Each monomial is its coefficient times up to four factors, multiplied in
+// order with no data-dependent loop (the two outputs of a warp have different
+// factor patterns), two terms per iteration into separate sums.  The forward
+// kernel forms repeated factors as powers first; the values agree to rounding.
 __device__ __forceinline__ void grad_fill_slot(const y3b_ace_tables& t, const SymTabs& tb, double2* __restrict__ val,
                                                int W, int slot, int ch) {
   const int na = int(t.nmax) * W, so = int(t.sym_output_count);
   const int atom = threadIdx.x % kGA;
   for (int o = threadIdx.x / kGA; o < so; o += blockDim.x / kGA) {
     const int4 r = tb.outs[o];
-    val[(na + slot * so + o) * kGA + atom] =
-        sym_output_tab(tb.fac, tb.co, r.y, min(r.z, tb.nterm), val + (ch * W + r.x) * kGA + atom, kGA);
+    const double2* x = val + (ch * W + r.x) * kGA + atom;
+    const int te = min(r.z, tb.nterm);
+    double2 acc[2] = {make_double2(0.0, 0.0), make_double2(0.0, 0.0)};
+#pragma unroll 1
+    for (int q0 = r.y; q0 < te; q0 += 2) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int q = q0 + h < te ? q0 + h : q0;  // a lone last term runs twice, the copy with weight 0
+        const uint32_t f = tb.fac[q];
+        double2 m = make_double2(q0 + h < te ? tb.co[q] : 0.0, 0.0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int ci = (f >> (8 * k)) & 255;
+          if (ci != 255) m = mul(m, x[ci * kGA]);
+        }
+        acc[h] = add(acc[h], m);
+      }
+    }
+    val[(na + slot * so + o) * kGA + atom] = add(acc[0], acc[1]);
   }
 }
 
