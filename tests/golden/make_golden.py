@@ -486,8 +486,68 @@ def real_schedules_fixture():
     print("real_schedules.npz", len(cases), "schedules")
 
 
+def hierarchical_fixture():
+    """``block_symmetric_power`` execution plans and the reference module's outputs.
+
+    Plans come from the reference's own test builders (``tests/test_execution_plan.py``,
+    ``tests/test_hierarchical_runtime.py``: one to three blocks, schemas v1 and v2, target_L 0
+    and 1, up to 1,430 tableaux) and from its scalar-ACE LAMMPS export example
+    (``examples/compile_scalar_ace_lammps_plans.py``, ``ye3t/scalar_ace_export.py``: the
+    manifest and every exported plan file, ranks 1-8 and 16).  Expected values are
+    ``YE3THierarchicalRepeatedBlockModule(plan, backend="reference").forward`` on seeded
+    complex block inputs (``ye3t/runtime/hierarchical.py:514``)."""
+    import importlib.util
+    import tempfile
+    ref = os.environ.get("YE3T_REFERENCE", "/root/reference")
+    sys.path.insert(0, os.path.join(ref, "tests"))
+    import test_execution_plan as te
+    import test_hierarchical_runtime as th
+    from ye3t.runtime import YE3THierarchicalRepeatedBlockModule
+
+    builders = [("h4", lambda: te._ordinary_homogeneous_scalar_plan(4)), ("r3L1", lambda: th._rank3_plan(1)),
+                ("r4", th._ordinary_rank4_plan), ("r6", lambda: th._ordinary_rank6_three_block_case()[0]),
+                ("r6u", lambda: th._ordinary_rank6_uneven_three_block_case()[0]), ("r9", th._rank9_plan),
+                ("r12", th._rank12_plan), ("r16", th._rank16_plan), ("r32", th._rank32_plan)]
+    plans = [(name, build().to_json(), None) for name, build in builders]
+    spec = importlib.util.spec_from_file_location(
+        "compile_scalar_ace_lammps_plans", os.path.join(ref, "examples", "compile_scalar_ace_lammps_plans.py"))
+    example = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(example)
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        manifest = example.run_compile_scalar_ace_lammps_plans(
+            config={"runtime": {"output_dir": os.path.join(tmp, "plans")}})
+        text = open(manifest, encoding="utf-8").read()
+        out["lammps_manifest"] = np.asarray(text)
+        for case in json.loads(text)["cases"]:
+            name = case["execution_plan"]["file"]
+            body = open(os.path.join(tmp, "plans", name), encoding="utf-8").read()
+            out["lammps_file_" + name] = np.asarray(body)
+            plans.append(("lammps_" + case["name"], body, name))
+    g = torch.Generator().manual_seed(7319)
+    names = []
+    for name, js, file in plans:
+        module = YE3THierarchicalRepeatedBlockModule(json.loads(js), backend="reference", dtype=torch.complex128)
+        inputs = [torch.complex(torch.randn(5, 2 * int(b["input_L"]) + 1, dtype=torch.float64, generator=g),
+                                torch.randn(5, 2 * int(b["input_L"]) + 1, dtype=torch.float64, generator=g)) * 0.7
+                  for b in module._blocks]
+        y = module(*inputs)
+        if file is None:
+            out["plan_" + name] = np.asarray(js)
+        else:  # an exported plan: stored once, under its file name
+            out["planfile_" + name] = np.asarray(file)
+        for b, x in enumerate(inputs):
+            out[f"x{b}_{name}"] = x.numpy()
+        out["y_" + name] = y.detach().numpy()
+        names.append(name)
+    out["names"] = np.asarray(names)
+    np.savez_compressed(os.path.join(HERE, "hierarchical.npz"), **out)
+    print("hierarchical.npz", len(names), "plans")
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing", "real"]
+    which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing", "real",
+                             "hierarchical"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -504,3 +564,5 @@ if __name__ == "__main__":
         mixing_fixture()
     if "real" in which:
         real_schedules_fixture()
+    if "hierarchical" in which:
+        hierarchical_fixture()
