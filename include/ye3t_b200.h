@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define Y3B_ABI_VERSION 6
+#define Y3B_ABI_VERSION 7
 
 /* dtype codes */
 #define Y3B_F32 0
@@ -225,6 +225,7 @@ typedef struct {
   const int32_t* sym_grad_offsets; /* [(lmax+1)^2 + 1] */
   const int32_t* sym_grad_index;   /* [sym_grad_count, 2]: output, 4 x u8 remaining factors (255 unused) */
   const double* sym_grad_coeff;    /* [sym_grad_count]: multiplicity x monomial coefficient */
+  int64_t sym_term_count;          /* S: entries of sym_term_factors / sym_term_coeff */
 } y3b_ace_tables;
 
 /* A-basis density for centres [center_begin, center_begin + center_count):

@@ -16,7 +16,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libye3t_b200.so")
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 F32, F64, C64, C128 = 0, 1, 2, 3
 STATUS_INDEX_RANGE = 1
 STATUS_CAPACITY = 2
@@ -48,6 +48,7 @@ class AceTables(ctypes.Structure):
         ("sym_outputs", VP), ("sym_term_factors", VP), ("sym_term_coeff", VP),
         ("group_count", I64), ("groups", VP), ("group_offsets", VP),
         ("sym_grad_count", I64), ("sym_grad_offsets", VP), ("sym_grad_index", VP), ("sym_grad_coeff", VP),
+        ("sym_term_count", I64),
     ]
 
 

@@ -297,18 +297,48 @@ __device__ __forceinline__ void eval_dispatch(const Cx2<R>* __restrict__ P, cons
 #undef Y3B_ITEM_CASE
 }
 
+// The symmetric-output tables (outputs, term factors, term coefficients) sit
+// in shared memory after the pool: a fill reads them there instead of through
+// chains of L2 reads (about 5 KB for l_max 3).
+struct FillTabs {
+  const int4* outs;     // [so]: l^2, term begin, term end, -
+  const uint32_t* fac;  // [nterm]
+  const double* co;     // [nterm]
+  int nterm;
+};
+
+inline size_t fill_tabs_bytes(const y3b_ace_tables& t) {
+  const size_t S = size_t(t.sym_term_count);
+  return size_t(16) * t.sym_output_count + ((4 * S + 15) & ~size_t(15)) + ((8 * S + 15) & ~size_t(15));
+}
+
+// All threads copy; the caller synchronises before a fill.  base is 16-byte aligned.
+__device__ __forceinline__ FillTabs fill_tabs_stage(const y3b_ace_tables& t, unsigned char* base) {
+  const int so = int(t.sym_output_count), S = int(t.sym_term_count);
+  int4* outs = reinterpret_cast<int4*>(base);
+  uint32_t* fac = reinterpret_cast<uint32_t*>(base + size_t(16) * so);
+  double* co = reinterpret_cast<double*>(reinterpret_cast<unsigned char*>(fac) + ((size_t(4) * S + 15) & ~size_t(15)));
+  const int4* g_outs = reinterpret_cast<const int4*>(t.sym_outputs);
+  for (int i = threadIdx.x; i < so; i += blockDim.x) outs[i] = __ldg(g_outs + i);
+  for (int i = threadIdx.x; i < S; i += blockDim.x) {
+    fac[i] = __ldg(t.sym_term_factors + i);
+    co[i] = __ldg(t.sym_term_coeff + i);
+  }
+  return FillTabs{outs, fac, co, S};
+}
+
 // Fill shared-memory slot `slot` with every symmetric output of radial
-// channel `ch` (sym_output, ace_common.cuh).
+// channel `ch` (sym_output_tab, ace_common.cuh); a warp fills one output for
+// its 32 atoms.
 template <typename R, int WARPS>
-__device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, Cx2<R>* __restrict__ sm, int W, int slot,
-                                          int ch, int lane, int warp) {
-  using C2 = typename Cplx<R>::type;
+__device__ __forceinline__ void fill_slot(const y3b_ace_tables& t, const FillTabs& tb, Cx2<R>* __restrict__ sm,
+                                          int W, int slot, int ch, int lane, int warp) {
   const int na = int(t.nmax) * W;
   const int so = int(t.sym_output_count);
-  const int4* outs = reinterpret_cast<const int4*>(t.sym_outputs);
   for (int o = warp; o < so; o += WARPS) {
-    const int4 r = __ldg(outs + o);  // (l^2, term begin, term end, -)
-    sm[(na + slot * so + o) * kLanes + lane] = sym_output(t, r.y, r.z, sm + (ch * W + r.x) * kLanes + lane, kLanes);
+    const int4 r = tb.outs[o];
+    sm[(na + slot * so + o) * kLanes + lane] =
+        sym_output_tab(tb.fac, tb.co, r.y, min(r.z, tb.nterm), sm + (ch * W + r.x) * kLanes + lane, kLanes);
   }
 }
 
@@ -329,6 +359,7 @@ __global__ void __launch_bounds__(kLanes * WARPS) ace_eval_kernel(
   // zero everything (padding and slots), then the A channels
   const int total = (int(t.smem_entries) + 2 * kPadEntries) * kLanes;
   for (int e = threadIdx.x; e < total; e += blockDim.x) smem_all[e] = cz<C2>();
+  const FillTabs tb = fill_tabs_stage(t, eval_smem_raw + size_t(total) * sizeof(C2));
   __syncthreads();
   C2* sm = smem_all + kPadEntries * kLanes;
   for (int e = warp; e < na; e += WARPS)
@@ -348,10 +379,10 @@ __global__ void __launch_bounds__(kLanes * WARPS) ace_eval_kernel(
     const int4 pr = __ldg(phases + ph);
     if (pr.x != cur0 || pr.y != cur1) {
       __syncthreads();  // previous phase's items are done with the slots (and A is loaded)
-      if (pr.x != cur0) fill_slot<R, WARPS>(t, sm, W, 0, pr.x, lane, warp);
+      if (pr.x != cur0) fill_slot<R, WARPS>(t, tb, sm, W, 0, pr.x, lane, warp);
       // (the second slot exists only in pools sized for it)
       if (pr.y != cur1 && pr.y >= 0 && t.smem_entries >= na + 2 * t.sym_output_count)
-        fill_slot<R, WARPS>(t, sm, W, 1, pr.y, lane, warp);
+        fill_slot<R, WARPS>(t, tb, sm, W, 1, pr.y, lane, warp);
       __syncthreads();
       cur0 = pr.x;
       cur1 = pr.y;
@@ -383,7 +414,7 @@ __global__ void __launch_bounds__(kLanes * WARPS) ace_eval_kernel(
 }
 
 inline size_t eval_smem_bytes(const y3b_ace_tables& t, size_t complex_size = sizeof(double2)) {
-  return size_t(t.smem_entries + 2 * kPadEntries) * kLanes * complex_size;
+  return size_t(t.smem_entries + 2 * kPadEntries) * kLanes * complex_size + fill_tabs_bytes(t);
 }
 
 int check_tables(const y3b_ace_tables* t) {
@@ -394,6 +425,8 @@ int check_tables(const y3b_ace_tables* t) {
   Y3B_CHECK_ARG(t->item_count == 0 || (t->items && t->item_coef && t->phases), "null item tables");
   Y3B_CHECK_ARG(t->smem_entries >= t->nmax * (t->lmax + 1) * (t->lmax + 1) + t->sym_output_count,
                 "shared-memory entry count too small");
+  Y3B_CHECK_ARG(t->sym_term_count >= 0 && (t->sym_output_count == 0 || t->sym_term_count > 0),
+                "symmetric term count missing");
   Y3B_CHECK_ARG(eval_smem_bytes(*t) <= 200 * 1024, "bundle needs %lld bytes of shared memory per CTA (max 200 KB)",
                 (long long)eval_smem_bytes(*t));
   return Y3B_OK;

@@ -58,34 +58,35 @@ struct RowWidth {
 };
 
 // Symmetric output of radial channel values x (x[i * stride] = component i
-// of A[n, l]): sum_q coeff_q prod_i x_i^{k_qi}, the powers of each distinct
-// input component multiplied in increasing component order
-// (ye3t_runtime_core.cpp:5279).  Factors are 4 x u8 component indices
-// (repeated for powers, 255 = unused).
+// of A[n, l]): sum_q coeff_q prod_i x_i^{k_qi} (the grouped monomial tables
+// of ye3t_runtime_core.cpp:5279).  Factors are 4 x u8 component indices
+// (repeated for powers, 255 = unused), read with the coefficients from the
+// given addresses (shared-memory copies of the tables).  Each monomial is its
+// coefficient times its factors multiplied in order, with no data-dependent
+// loop (threads of one warp may follow different factor patterns), two terms
+// per iteration into separate sums.
 template <typename C2>
-__device__ __forceinline__ C2 sym_output(const y3b_ace_tables& t, int tb, int te, const C2* x, int stride) {
+__device__ __forceinline__ C2 sym_output_tab(const uint32_t* fac, const double* co, int tb, int te, const C2* x,
+                                             int stride) {
   using R = decltype(C2{}.x);
-  C2 acc = cz<C2>();
-  for (int q = tb; q < te; ++q) {
-    const uint32_t f = __ldg(t.sym_term_factors + q);
-    C2 m = cz<C2>();
-    m.x = R(__ldg(t.sym_term_coeff + q));
-    int k = 0;
-    while (k < 4) {
-      const int ci = (f >> (8 * k)) & 255;
-      if (ci == 255) break;
-      const C2 xv = x[ci * stride];
-      C2 pw = xv;
-      ++k;
-      while (k < 4 && int((f >> (8 * k)) & 255) == ci) {
-        pw = mul(pw, xv);
-        ++k;
+  C2 acc[2] = {cz<C2>(), cz<C2>()};
+#pragma unroll 1
+  for (int q0 = tb; q0 < te; q0 += 2) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int q = q0 + h < te ? q0 + h : q0;  // a lone last term runs twice, the copy with weight 0
+      const uint32_t f = fac[q];
+      C2 m = cz<C2>();
+      m.x = q0 + h < te ? R(co[q]) : R(0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int ci = (f >> (8 * k)) & 255;
+        if (ci != 255) m = mul(m, x[ci * stride]);
       }
-      m = mul(m, pw);
+      acc[h] = add(acc[h], m);
     }
-    acc = add(acc, m);
   }
-  return acc;
+  return add(acc[0], acc[1]);
 }
 
 }  // namespace y3b

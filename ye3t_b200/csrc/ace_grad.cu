@@ -562,7 +562,7 @@ __device__ __forceinline__ double adj4_body(const Ctx& c, const Item& it, int nc
   // register-block values: held in registers for the smaller blocks, read
   // from shared memory at each use for the 7-index block (register budget)
   constexpr int NS = CH <= 5 ? CH : 1;
-  double2 vs[NS], w[CH];
+  double2 vs[NS] = {}, w[CH];
   auto vsu = [&](int u) { return CH <= 5 ? vs[u < NS ? u : 0] : vat(c, bs + u); };
 #pragma unroll
   for (int u = 0; u < CH; ++u) {
@@ -755,10 +755,7 @@ struct SymTabs {
   const double* gco;    // [T]
 };
 
-__device__ __forceinline__ int sym_term_total(const y3b_ace_tables& t) {
-  const int so = int(t.sym_output_count);
-  return so > 0 ? __ldg(t.sym_outputs + 4 * (so - 1) + 2) : 0;  // terms are packed in output order
-}
+__device__ __forceinline__ int sym_term_total(const y3b_ace_tables& t) { return int(t.sym_term_count); }
 
 __device__ __forceinline__ SymTabs sym_tabs_global(const y3b_ace_tables& t, int nterm) {
   return SymTabs{reinterpret_cast<const int4*>(t.sym_outputs), t.sym_term_factors, t.sym_term_coeff, nterm,
@@ -795,36 +792,17 @@ __device__ __forceinline__ SymTabs sym_tabs_stage(const y3b_ace_tables& t, char*
   return SymTabs{outs, fac, co, nterm, goff, gidx, gco};
 }
 
-// Symmetric slot: fill values from A.  Threads cover (atom, output) pairs.
-// Each monomial is its coefficient times up to four factors, multiplied in
-// order with no data-dependent loop (the two outputs of a warp have different
-// factor patterns), two terms per iteration into separate sums.  The forward
-// kernel forms repeated factors as powers first; the values agree to rounding.
+// Symmetric slot: fill values from A.  Threads cover (atom, output) pairs, so
+// the two half-warps of a warp fill different outputs (sym_output_tab has no
+// data-dependent loop).
 __device__ __forceinline__ void grad_fill_slot(const y3b_ace_tables& t, const SymTabs& tb, double2* __restrict__ val,
                                                int W, int slot, int ch) {
   const int na = int(t.nmax) * W, so = int(t.sym_output_count);
   const int atom = threadIdx.x % kGA;
   for (int o = threadIdx.x / kGA; o < so; o += blockDim.x / kGA) {
     const int4 r = tb.outs[o];
-    const double2* x = val + (ch * W + r.x) * kGA + atom;
-    const int te = min(r.z, tb.nterm);
-    double2 acc[2] = {make_double2(0.0, 0.0), make_double2(0.0, 0.0)};
-#pragma unroll 1
-    for (int q0 = r.y; q0 < te; q0 += 2) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int q = q0 + h < te ? q0 + h : q0;  // a lone last term runs twice, the copy with weight 0
-        const uint32_t f = tb.fac[q];
-        double2 m = make_double2(q0 + h < te ? tb.co[q] : 0.0, 0.0);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int ci = (f >> (8 * k)) & 255;
-          if (ci != 255) m = mul(m, x[ci * kGA]);
-        }
-        acc[h] = add(acc[h], m);
-      }
-    }
-    val[(na + slot * so + o) * kGA + atom] = add(acc[0], acc[1]);
+    val[(na + slot * so + o) * kGA + atom] =
+        sym_output_tab(tb.fac, tb.co, r.y, min(r.z, tb.nterm), val + (ch * W + r.x) * kGA + atom, kGA);
   }
 }
 
@@ -956,25 +934,25 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
       cur0 = pr.x;
       cur1 = pr.y;
     }
-    if (CLS == 1) {
+    if constexpr (CLS == 1) {
       // one sorted run per warp (packing pads the phase's range to equal runs)
       const int per = (ge - gb + kWarps - 1) / kWarps;
       const int g0 = gb + warp * per, g1 = min(ge, g0 + per);
       bool bad = false;
       e_acc += adj3_run(c, groups, g0, g1, grp, items, t.item_coef, wz, bad);
       if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
-      continue;
-    }
+    } else {
 #pragma unroll 1
-    for (int g = gb + warp; g < ge; g += kWarps) {
-      const int2 ig = __ldg(groups + g);
-      if (ig.x < 0) continue;  // null pair
-      const int mine = grp == 0 ? ig.x : ig.y;
-      const bool mute = mine < 0;  // odd item out: the second half runs the first item unweighted, adding nothing
-      const Item it = load_item(items, mute ? ig.x : mine);
-      const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
-      const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
-      e_acc += adj_class<0>(c, it, t.item_coef, w0, w1, mute);
+      for (int g = gb + warp; g < ge; g += kWarps) {
+        const int2 ig = __ldg(groups + g);
+        if (ig.x < 0) continue;  // null pair
+        const int mine = grp == 0 ? ig.x : ig.y;
+        const bool mute = mine < 0;  // odd item out: the second half runs the first item unweighted, adding nothing
+        const Item it = load_item(items, mute ? ig.x : mine);
+        const double w0 = mute ? 0.0 : __ldg(wz + it.f0);
+        const double w1 = (!mute && it.f1 >= 0) ? __ldg(wz + it.f1) : 0.0;
+        e_acc += adj_class<0>(c, it, t.item_coef, w0, w1, mute);
+      }
     }
   }
   __syncthreads();
@@ -1179,6 +1157,8 @@ int check_grad_tables(const y3b_ace_tables* t) {
   Y3B_CHECK_ARG(t->group_offsets && (t->group_count == 0 || t->groups), "null adjoint item groups");
   Y3B_CHECK_ARG(t->sym_grad_offsets && (t->sym_grad_count == 0 || (t->sym_grad_index && t->sym_grad_coeff)),
                 "null symmetric derivative tables");
+  Y3B_CHECK_ARG(t->sym_term_count >= 0 && (t->sym_output_count == 0 || t->sym_term_count > 0),
+                "symmetric term count missing");
   return Y3B_OK;
 }
 

@@ -60,6 +60,7 @@ class PackedBundle:
         t.sym_output_count = int(a["sym_outputs"].shape[0])
         t.group_count = int(a["groups"].shape[0])
         t.sym_grad_count = int(a["sym_grad_coeff"].shape[0])
+        t.sym_term_count = int(a["sym_term_coeff"].shape[0])
         for name in ("items", "item_coef", "phases", "sym_outputs", "sym_term_factors", "sym_term_coeff", "groups",
                      "group_offsets", "sym_grad_offsets", "sym_grad_index", "sym_grad_coeff"):
             setattr(t, name, ctypes.c_void_p(a[name].data_ptr()))
