@@ -2,8 +2,10 @@
 
 Each atom's A- and B-basis depend only on its own neighbour row, so rank r of
 P evaluates the centres ``[r N / P, (r + 1) N / P)`` from the replicated
-positions and the only collective is a sum of the per-rank energies.  The
-reference has no distributed code; this is new.
+positions; the collectives are sums of the per-rank energies and, with forces,
+of the per-rank partial force arrays (each rank scatters its rows' edge
+gradients into a full ``[N, 3]`` array).  The reference has no distributed
+code; this is new.
 """
 
 from __future__ import annotations
