@@ -27,11 +27,13 @@ namespace {
 // each half-warp on its own item; the two items of a warp have the same shape
 // (packing pairs them), so both halves follow one control flow.
 //
-// Every item accumulates its gradients in registers and adds each block's
-// gradient to G once.  Entries that leave a register window early go to a
-// small per-lane staging area first.  The additions to G are batched
-// compare-and-swaps: all old values are loaded, all swaps issued, and only the
-// ones that lost a race against another warp are retried.
+// Gradients accumulate in registers and, for entries that leave a register
+// window early, in a small per-lane staging area.  Class-0 items add each
+// block's gradient to G once per item; the run paths (classes 1-3) keep a
+// block's gradient over consecutive items of a lane and add it when the block
+// changes.  The additions to G are batched compare-and-swaps: all old values
+// are loaded, all swaps issued, and the ones that lost a race against another
+// warp are added with red.shared.add.f64.
 constexpr int kGA = 16;
 #ifndef Y3B_RUN_WARPS
 #define Y3B_RUN_WARPS 8
