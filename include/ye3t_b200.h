@@ -78,6 +78,20 @@ int y3b_symmetric_power_monomial(int dtype, const void* input, int64_t batch, in
                                  const void* monomial_values, int64_t term_count,
                                  int64_t output_dim, void* out, void* stream);
 
+/* Symmetric-power contraction, shared-monomial table: each of monomial_count
+ * unique monomials prod_i x[b, i]^counts[m, i] is weighted per coefficient.
+ * Replaces ye3t_runtime::symmetric_power_shared_monomial
+ * (ye3t/runtime/csrc/execution_plan_torch.cpp:7541; CPU core
+ * ye3t_runtime_core.cpp:5392; Python entry execution_plan.py:12502):
+ *   out[b, o] = sum_{t in [off[o], off[o+1])} values[t] monomial[b, terms[t]]
+ * Monomial indices outside [0, monomial_count) set Y3B_STATUS_INDEX_RANGE in
+ * *status (nullable) and contribute 0. */
+int y3b_symmetric_power_shared_monomial(int dtype, const void* input, int64_t batch, int64_t input_dim,
+                                        const int64_t* monomial_counts, int64_t monomial_count,
+                                        const int64_t* output_offsets, int64_t output_dim,
+                                        const int64_t* coefficient_terms, const void* coefficient_values,
+                                        int64_t coefficient_count, void* out, int32_t* status, void* stream);
+
 /* ChebExpCos radial table with d/dr, radial indices 0..maximum_radial_index.
  * Replaces ye3t_runtime::cheb_exp_cos_radial_table_with_derivative
  * (ye3t/runtime/csrc/execution_plan_torch.cpp:7238). Real dtypes only. */

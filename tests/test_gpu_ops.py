@@ -115,6 +115,44 @@ def test_symmetric_power_matches_reference(golden):
     np.testing.assert_allclose(y.cpu().numpy().reshape(-1), g["fx_expected_output"], rtol=1e-13, atol=1e-13)
 
 
+def test_symmetric_power_shared_monomial_matches_reference(golden):
+    """The shared-monomial form (execution_plan.py:12502): the reference's pinned fixture as is,
+    then every symmetric block kind of the nu<=4 word set lowered to unique monomials against the
+    oracle (complex128 and complex64), and the table checks."""
+    from oracle import oracle
+    from ye3t_b200.runtime import symmetric_power_shared_monomial_contraction as op
+    from ye3t_b200.schedules import ACEBundle
+    import os
+    g = golden("sympow")
+    dim = int(g["fx_input_dimension"])
+    x = g["fx_input"].reshape(int(g["fx_batch_size"]), dim)
+    y = op(_t(x), _t(g["fx_monomial_counts"].reshape(-1, dim)), _t(g["fx_output_offsets"]),
+           _t(g["fx_coefficient_terms"]), _t(g["fx_coefficient_outputs"]), _t(g["fx_coefficient_values"]))
+    np.testing.assert_allclose(y.cpu().numpy().reshape(-1), g["fx_expected_output"], rtol=1e-13, atol=1e-13)
+    b = ACEBundle.load(os.path.join(os.path.dirname(os.path.dirname(__file__)), "ye3t_b200", "bundles",
+                                    "ace_n8_l3_nu4_L0.npz"))
+    rng = np.random.default_rng(3)
+    for key in sorted(b.sym_tables):
+        t = b.sym_tables[key]
+        unique, terms = np.unique(t.monomial_counts, axis=0, return_inverse=True)
+        outs = np.repeat(np.arange(t.output_offsets.shape[0] - 1), np.diff(t.output_offsets))
+        xs = rng.normal(size=(40, t.monomial_counts.shape[1])) + 1j * rng.normal(size=(40, t.monomial_counts.shape[1]))
+        ref = oracle.symmetric_power_shared_monomial(xs, unique, t.output_offsets, terms.reshape(-1),
+                                                     t.monomial_value)
+        for dt, tol in ((torch.complex128, 1e-12), (torch.complex64, 1e-5)):
+            y = op(torch.as_tensor(xs, device=DEV).to(dt), unique, t.output_offsets, terms.reshape(-1), outs,
+                   torch.as_tensor(t.monomial_value).to(dt))
+            err = np.abs(y.cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1.0)
+            assert err <= tol, (key, dt, err)
+    counts = g["fx_monomial_counts"].reshape(-1, dim)
+    with pytest.raises(ValueError, match="invalid monomial"):
+        op(_t(x), _t(counts), _t(g["fx_output_offsets"]), _t(g["fx_coefficient_terms"] + 3),
+           _t(g["fx_coefficient_outputs"]), _t(g["fx_coefficient_values"]))
+    with pytest.raises(ValueError, match="length must match"):
+        op(_t(x), _t(counts), _t(g["fx_output_offsets"]), _t(g["fx_coefficient_terms"]),
+           _t(g["fx_coefficient_outputs"][:-1]), _t(g["fx_coefficient_values"]))
+
+
 def _record(g, p):
     from ye3t_b200.schedules import ScheduleRecord
     specs = json.loads(bytes(g[p + "specs"]).decode())

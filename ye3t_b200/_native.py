@@ -58,6 +58,8 @@ _SIGS = {
     "y3b_factorized_schedule_evaluate": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, I64, I64, VP, VP, VP, VP,
                                                         I64, I64, VP, VP, VP]),
     "y3b_symmetric_power_monomial": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, VP, VP, VP, I64, I64, VP, VP]),
+    "y3b_symmetric_power_shared_monomial": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, VP, I64, VP, I64, VP, VP, I64,
+                                                           VP, VP, VP]),
     "y3b_cheb_exp_cos_radial_table": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, VP, VP, VP]),
     "y3b_spherical_harmonics_table": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, ctypes.c_int, DBL, VP, VP,
                                                      VP]),

@@ -49,12 +49,17 @@ __global__ void __launch_bounds__(256) schedule_eval_kernel(
   }
 }
 
-// Integer power by repeated multiplication, as ye3t_runtime_core's
-// integer_power; an exponent of 0 yields exactly 1.
+// Integer power by square-and-multiply, the evaluation order of
+// ye3t_runtime_core's integer_power (ye3t_runtime_core.cpp:98), so that
+// powers round as the reference's do; an exponent of 0 yields exactly 1.
 template <typename T>
 __device__ __forceinline__ T ipow(T x, int64_t e) {
   T r = one<T>();
-  for (int64_t k = 0; k < e; ++k) r = mul(r, x);
+  while (e > 0) {
+    if (e & 1) r = mul(r, x);
+    e >>= 1;
+    if (e > 0) x = mul(x, x);
+  }
   return r;
 }
 
@@ -78,6 +83,38 @@ __global__ void __launch_bounds__(256) sympow_kernel(
         if (e) m = mul(m, ipow(xr[i], e));
       }
       acc = add(acc, m);
+    }
+    out[lin] = acc;
+  }
+}
+
+// Shared-monomial form: out[b, o] = sum over the output's coefficients t of
+// values[t] * monomial[terms[t]], each monomial the product over all input
+// components of x^count (ye3t_runtime_core.cpp:5392).  One thread per
+// (batch row, output); a monomial is formed where a coefficient uses it.
+// Monomial indices outside [0, monomial_count) set Y3B_STATUS_INDEX_RANGE and
+// contribute 0.
+template <typename T>
+__global__ void __launch_bounds__(256) sympow_shared_kernel(
+    const T* __restrict__ x, int64_t batch, int64_t in_dim, const int64_t* __restrict__ counts,
+    int64_t monomials, const int64_t* __restrict__ off, const int64_t* __restrict__ terms,
+    const T* __restrict__ vals, int64_t out_dim, T* __restrict__ out, int32_t* __restrict__ status) {
+  const int64_t total = batch * out_dim;
+  for (int64_t lin = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; lin < total;
+       lin += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = lin / out_dim;
+    const int64_t o = lin - b * out_dim;
+    const T* xr = x + b * in_dim;
+    T acc = zero<T>();
+    for (int64_t t = __ldg(off + o); t < __ldg(off + o + 1); ++t) {
+      const int64_t m = __ldg(terms + t);
+      if (m < 0 || m >= monomials) {
+        if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        continue;
+      }
+      T mono = one<T>();
+      for (int64_t i = 0; i < in_dim; ++i) mono = mul(mono, ipow(xr[i], __ldg(counts + m * in_dim + i)));
+      acc = add(acc, mul(vals[t], mono));
     }
     out[lin] = acc;
   }
@@ -133,6 +170,31 @@ extern "C" int y3b_symmetric_power_monomial(int dtype, const void* input, int64_
     sympow_kernel<T><<<grid, threads, 0, as_stream(stream)>>>(
         static_cast<const T*>(input), batch, input_dim, monomial_counts, output_offsets,
         static_cast<const T*>(monomial_values), output_dim, static_cast<T*>(out));
+  });
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+extern "C" int y3b_symmetric_power_shared_monomial(int dtype, const void* input, int64_t batch,
+                                                   int64_t input_dim, const int64_t* monomial_counts,
+                                                   int64_t monomial_count, const int64_t* output_offsets,
+                                                   int64_t output_dim, const int64_t* coefficient_terms,
+                                                   const void* coefficient_values, int64_t coefficient_count,
+                                                   void* out, int32_t* status, void* stream) {
+  Y3B_CHECK_ARG(batch >= 0 && input_dim >= 0 && output_dim >= 0 && monomial_count >= 0 && coefficient_count >= 0,
+                "negative size");
+  const int64_t total = batch * output_dim;
+  if (total == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(input && output_offsets && out &&
+                    (coefficient_count == 0 || (coefficient_terms && coefficient_values)) &&
+                    (monomial_count == 0 || monomial_counts),
+                "null pointer argument");
+  const int threads = 256;
+  const int grid = grid_for(total, threads);
+  Y3B_DISPATCH(dtype, T, {
+    sympow_shared_kernel<T><<<grid, threads, 0, as_stream(stream)>>>(
+        static_cast<const T*>(input), batch, input_dim, monomial_counts, monomial_count, output_offsets,
+        coefficient_terms, static_cast<const T*>(coefficient_values), output_dim, static_cast<T*>(out), status);
   });
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;

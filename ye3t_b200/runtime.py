@@ -27,6 +27,7 @@ __all__ = [
     "density_accumulate",
     "density_accumulate_adjoint",
     "symmetric_power_monomial_contraction",
+    "symmetric_power_shared_monomial_contraction",
     "symmetric_power_table_contraction",
     "pace_radial_channel_contraction_with_derivative",
     "native_execution_plan_capabilities",
@@ -224,6 +225,58 @@ def symmetric_power_monomial_contraction(input, monomial_counts, output_offsets,
     return out.reshape(*x.shape[:-1], out_dim)
 
 
+def symmetric_power_shared_monomial_contraction(input, monomial_counts, output_offsets, coefficient_terms,
+                                                coefficient_outputs, coefficient_values, *, backend="auto"):
+    """Shared-monomial symmetric-power contraction; ``ye3t/runtime/execution_plan.py:12502``.
+
+    Unique monomials ``prod_i x_i^counts[m, i]`` weighted by sparse
+    coefficients: ``out[..., o] = sum_{t in [offsets[o], offsets[o+1])}
+    values[t] * monomial[terms[t]]``.  The table checks (lengths, index
+    ranges) and their messages follow the reference's
+    ``symmetric_power_shared_monomial_reference`` (:12100-12160).
+    """
+    _check_backend(backend)
+    x = torch.as_tensor(input)
+    dev = nat.require_cuda(x, what="symmetric_power_shared_monomial_contraction")
+    if x.ndim < 1:
+        raise ValueError("symmetric-power input requires a feature axis")
+    in_dim = int(x.shape[-1])
+    counts = torch.as_tensor(monomial_counts, dtype=torch.int64, device=dev).contiguous()
+    offsets = torch.as_tensor(output_offsets, dtype=torch.int64, device=dev).reshape(-1).contiguous()
+    terms = torch.as_tensor(coefficient_terms, dtype=torch.int64, device=dev).reshape(-1).contiguous()
+    outputs = torch.as_tensor(coefficient_outputs, dtype=torch.int64, device=dev).reshape(-1)
+    values = torch.as_tensor(coefficient_values, dtype=x.dtype, device=dev).reshape(-1).contiguous()
+    if counts.ndim != 2 or int(counts.shape[1]) != in_dim:
+        raise ValueError("monomial_counts must have shape [monomial, input_dimension]")
+    n_coef = int(terms.numel())
+    if int(outputs.numel()) != n_coef:
+        raise ValueError("coefficient_outputs length must match coefficient_terms")
+    if int(values.numel()) != n_coef:
+        raise ValueError("coefficient_values length must match coefficient_terms")
+    if int(offsets.numel()) < 1:
+        raise ValueError("output_offsets must contain at least one entry")
+    out_dim = int(offsets.numel()) - 1
+    if n_coef:
+        if int(terms.min()) < 0:
+            raise ValueError("coefficient_terms must be nonnegative")
+        if int(terms.max()) >= int(counts.shape[0]):
+            raise ValueError("coefficient_terms contains an invalid monomial")
+        if int(outputs.min()) < 0:
+            raise ValueError("coefficient_outputs must be nonnegative")
+        if int(outputs.max()) >= out_dim:
+            raise ValueError("coefficient_outputs contains an invalid output")
+    x2 = x.contiguous().reshape(-1, in_dim)
+    out = torch.empty((x2.shape[0], out_dim), dtype=x.dtype, device=dev)
+    status = _status(dev)
+    nat.check(nat.lib().y3b_symmetric_power_shared_monomial(
+        nat.dtype_code(x.dtype), x2.data_ptr(), x2.shape[0], in_dim, counts.data_ptr() if counts.numel() else 0,
+        int(counts.shape[0]), offsets.data_ptr(), out_dim, terms.data_ptr() if n_coef else 0,
+        values.data_ptr() if n_coef else 0, n_coef, out.data_ptr(), status.data_ptr(), nat.stream_of(dev)),
+        "symmetric_power_shared_monomial_contraction")
+    _raise_on_status(status, "symmetric_power_shared_monomial_contraction")
+    return out.reshape(*x.shape[:-1], out_dim)
+
+
 def symmetric_power_table_contraction(input, table, *, backend="auto"):
     """Contract with a :class:`~ye3t_b200.schedules.SymPowerTable` (grouped plan table).
 
@@ -292,6 +345,7 @@ def native_execution_plan_capabilities():
             "density_accumulate": ["float32", "float64", "complex64", "complex128"],
             "density_accumulate_adjoint": ["float32", "float64", "complex64", "complex128"],
             "symmetric_power_monomial": ["float32", "float64", "complex64", "complex128"],
+            "symmetric_power_shared_monomial": ["float32", "float64", "complex64", "complex128"],
             "factorized_schedule": ["float32", "float64", "complex64", "complex128"],
             "ace_density": ["float64 -> complex128"],
             "ace_density_mixed": ["float32 -> complex64", "float64 -> complex128"],
