@@ -110,6 +110,45 @@ int y3b_spherical_harmonics_table(int dtype, const void* edge_vectors, int64_t e
                                   int64_t maximum_angular_momentum, int real_output,
                                   double epsilon, void* values, void* derivatives, void* stream);
 
+/* Scheduled radial x angular channels with Cartesian derivatives (real dtypes):
+ *   values[e, c] = R[e, rad_c] Y[e, ang_c] s_c
+ *   derivatives[e, c, :] = s_c (R'[e, rad_c] d[e, :] Y[e, ang_c] + R[e, rad_c] dY[e, ang_c, :])
+ * for channels whose type is negative or equals the edge's type, else 0.
+ * R, R' [E, radial_count]; Y [E, angular_count]; dY [E, angular_count, 3];
+ * d [E, 3] (unit edge directions).  Replaces
+ * ye3t_runtime::scheduled_radial_angular_channels_with_derivative
+ * (ye3t/runtime/csrc/execution_plan_torch.cpp:7268; Python entry
+ * execution_plan.py:7675).  Radial / angular indices outside their tables set
+ * Y3B_STATUS_INDEX_RANGE in *status (nullable) and give 0. */
+int y3b_scheduled_radial_angular_channels(int dtype, const void* radial_values, const void* radial_derivatives,
+                                          int64_t radial_count, const void* angular_values,
+                                          const void* angular_derivatives, int64_t angular_count,
+                                          const void* radial_directions, const int64_t* edge_types,
+                                          int64_t edge_count, const int64_t* channel_radial_indices,
+                                          const int64_t* channel_angular_indices, const int64_t* channel_types,
+                                          const void* channel_scales, int64_t channel_count, void* values,
+                                          void* derivatives, int32_t* status, void* stream);
+
+/* Plain site-basis product with per-edge group prefactors (real or complex):
+ * term t (group g_t, channel ch_t) of edge e gives
+ *   edge_values[e, ch_t] = p[g_t, e] R[g_t, e] Y[t, e]
+ *   edge_derivatives[e, ch_t, :] = p[g_t, e] (R'[g_t, e] d[e, :] Y[t, e] + R[g_t, e] dY[t, e, :])
+ *   charge_center / charge_neighbor [e, ch_t] = pc / pn [g_t, e] R[g_t, e] Y[t, e]
+ * and channels no term names are 0.  R, R', p, pc, pn [group_count, E];
+ * Y [term_count, E]; dY [term_count, E, 3]; d [E, 3]; outputs [E, channel_count]
+ * ([E, channel_count, 3] for the derivatives).  Term channels are distinct.
+ * Replaces ye3t_runtime::plain_site_basis_product_with_derivative
+ * (execution_plan_torch.cpp, schema beside :7268; Python entry
+ * execution_plan.py:7582).  Groups or channels out of range set
+ * Y3B_STATUS_INDEX_RANGE and write nothing. */
+int y3b_plain_site_basis_product(int dtype, const void* radial_values, const void* radial_derivatives,
+                                 int64_t group_count, const void* angular_values, const void* angular_derivatives,
+                                 int64_t term_count, const void* prefactors, const void* prefactor_derivatives_center,
+                                 const void* prefactor_derivatives_neighbor, const void* radial_directions,
+                                 int64_t edge_count, const int64_t* term_groups, const int64_t* term_channels,
+                                 int64_t channel_count, void* edge_values, void* edge_derivatives,
+                                 void* charge_center, void* charge_neighbor, int32_t* status, void* stream);
+
 /* Density accumulation A[centers[e], c] += edge_values[e, c] without global
  * floating-point atomics: centres are bucketed into CSR rows (integer
  * counting), each row is ordered by edge index, and every output row is

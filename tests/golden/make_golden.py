@@ -545,9 +545,57 @@ def hierarchical_fixture():
     print("hierarchical.npz", len(names), "plans")
 
 
+def edge_products_fixture():
+    """``scheduled_radial_angular_channels_with_derivative`` (execution_plan.py:7675) and
+    ``plain_site_basis_product_with_derivative`` (:7582) through the reference's own composition
+    (``backend="reference"``) on seeded inputs."""
+    from ye3t.runtime.execution_plan import (plain_site_basis_product_with_derivative,
+                                             scheduled_radial_angular_channels_with_derivative)
+    g = torch.Generator().manual_seed(5150)
+    out = {}
+    for tag, dt in (("f64", torch.float64), ("f32", torch.float32)):
+        E, K, A, C = 37, 9, 16, 20
+        d = torch.randn(E, 3, dtype=dt, generator=g)
+        d = d / d.norm(dim=1, keepdim=True)
+        args = dict(radial_values=torch.randn(E, K, dtype=dt, generator=g),
+                    radial_derivatives=torch.randn(E, K, dtype=dt, generator=g),
+                    angular_values=torch.randn(E, A, dtype=dt, generator=g),
+                    angular_derivatives=torch.randn(E, A, 3, dtype=dt, generator=g), radial_directions=d,
+                    edge_types=torch.randint(0, 3, (E,), generator=g),
+                    channel_radial_indices=torch.randint(0, K, (C,), generator=g),
+                    channel_angular_indices=torch.randint(0, A, (C,), generator=g),
+                    channel_types=torch.randint(-1, 3, (C,), generator=g),
+                    channel_scales=torch.randn(C, dtype=dt, generator=g))
+        v, dv = scheduled_radial_angular_channels_with_derivative(**args, backend="reference")
+        for k, x in args.items():
+            out[f"s_{tag}_{k}"] = x.numpy()
+        out[f"s_{tag}_values"], out[f"s_{tag}_derivatives"] = v.numpy(), dv.numpy()
+    for tag, dt in (("f64", torch.float64), ("c128", torch.complex128), ("c64", torch.complex64)):
+        G, T, E, C = 3, 10, 29, 14
+        rdt = torch.float64 if dt != torch.float32 and dt != torch.complex64 else torch.float32
+
+        def rnd(*shape):
+            x = torch.randn(*shape, dtype=rdt, generator=g)
+            return torch.complex(x, torch.randn(*shape, dtype=rdt, generator=g)) if dt.is_complex else x
+        d = torch.randn(E, 3, dtype=rdt, generator=g)
+        d = (d / d.norm(dim=1, keepdim=True)).to(dt)
+        channels = torch.randperm(C, generator=g)[:T]
+        args = dict(radial_values=rnd(G, E), radial_derivatives=rnd(G, E), angular_values=rnd(T, E),
+                    angular_derivatives=rnd(T, E, 3), prefactors=rnd(G, E), prefactor_derivatives_center=rnd(G, E),
+                    prefactor_derivatives_neighbor=rnd(G, E), radial_directions=d,
+                    term_groups=torch.randint(0, G, (T,), generator=g), term_channels=channels, channel_count=C)
+        res = plain_site_basis_product_with_derivative(**args, backend="reference")
+        for k, x in args.items():
+            out[f"p_{tag}_{k}"] = x.numpy() if torch.is_tensor(x) else np.asarray(x)
+        for k, x in zip(("edge_values", "edge_derivatives", "charge_center", "charge_neighbor"), res):
+            out[f"p_{tag}_{k}"] = x.numpy()
+    np.savez_compressed(os.path.join(HERE, "edge_products.npz"), **out)
+    print("edge_products.npz", len(out), "arrays")
+
+
 if __name__ == "__main__":
     which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing", "real",
-                             "hierarchical"]
+                             "hierarchical", "edge_products"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -566,3 +614,5 @@ if __name__ == "__main__":
         real_schedules_fixture()
     if "hierarchical" in which:
         hierarchical_fixture()
+    if "edge_products" in which:
+        edge_products_fixture()

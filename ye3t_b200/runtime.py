@@ -28,6 +28,8 @@ __all__ = [
     "density_accumulate_adjoint",
     "symmetric_power_monomial_contraction",
     "symmetric_power_shared_monomial_contraction",
+    "scheduled_radial_angular_channels_with_derivative",
+    "plain_site_basis_product_with_derivative",
     "symmetric_power_table_contraction",
     "pace_radial_channel_contraction_with_derivative",
     "native_execution_plan_capabilities",
@@ -115,6 +117,91 @@ def spherical_harmonics_table_with_derivative(edge_vectors, maximum_angular_mome
                                                        der.data_ptr(), nat.stream_of(dev)),
               "spherical_harmonics_table_with_derivative")
     return val, der
+
+
+def _index_range(t, n, what):
+    if t.numel() and (int(t.min()) < 0 or int(t.max()) >= n):
+        raise IndexError(f"{what}: index out of range")
+
+
+def scheduled_radial_angular_channels_with_derivative(radial_values, radial_derivatives, angular_values,
+                                                      angular_derivatives, radial_directions, edge_types,
+                                                      channel_radial_indices, channel_angular_indices,
+                                                      channel_types, channel_scales, backend="auto"):
+    """Fixed radial x angular channel schedule and its analytic derivatives.
+
+    ``ye3t/runtime/execution_plan.py:7675`` (composition :7036-7080): returns
+    ``values [E, C]`` and ``derivatives [E, C, 3]`` with the reference's
+    operation order and rounding (real dtypes).
+    """
+    _check_backend(backend)
+    rv = torch.as_tensor(radial_values)
+    dev = nat.require_cuda(rv, what="scheduled_radial_angular_channels_with_derivative")
+    if rv.dtype not in (torch.float32, torch.float64):
+        raise ValueError("scheduled radial-angular channels are real")
+    rd, av, ad, dr, cs = (torch.as_tensor(v, dtype=rv.dtype, device=dev).contiguous()
+                          for v in (radial_derivatives, angular_values, angular_derivatives, radial_directions,
+                                    channel_scales))
+    et, cr, ca, ct = (torch.as_tensor(v, dtype=torch.int64, device=dev).reshape(-1).contiguous()
+                      for v in (edge_types, channel_radial_indices, channel_angular_indices, channel_types))
+    rv = rv.contiguous()
+    if rv.ndim != 2 or rd.shape != rv.shape or av.ndim != 2 or ad.shape != (*av.shape, 3):
+        raise ValueError("radial tables must be [E, K] and angular tables [E, A] / [E, A, 3]")
+    E, K, A, C = int(rv.shape[0]), int(rv.shape[1]), int(av.shape[1]), int(cr.numel())
+    if av.shape[0] != E or dr.shape != (E, 3) or et.numel() != E:
+        raise ValueError("edge tables disagree on the edge count")
+    if ca.numel() != C or ct.numel() != C or cs.numel() != C:
+        raise ValueError("channel tables must have one entry per channel")
+    _index_range(cr, K, "channel_radial_indices")
+    _index_range(ca, A, "channel_angular_indices")
+    val = torch.empty((E, C), dtype=rv.dtype, device=dev)
+    der = torch.empty((E, C, 3), dtype=rv.dtype, device=dev)
+    nat.check(nat.lib().y3b_scheduled_radial_angular_channels(
+        nat.dtype_code(rv.dtype), rv.data_ptr(), rd.data_ptr(), K, av.data_ptr(), ad.data_ptr(), A, dr.data_ptr(),
+        et.data_ptr(), E, cr.data_ptr(), ca.data_ptr(), ct.data_ptr(), cs.data_ptr(), C, val.data_ptr(),
+        der.data_ptr(), None, nat.stream_of(dev)), "scheduled_radial_angular_channels_with_derivative")
+    return val, der
+
+
+def plain_site_basis_product_with_derivative(radial_values, radial_derivatives, angular_values,
+                                             angular_derivatives, prefactors, prefactor_derivatives_center,
+                                             prefactor_derivatives_neighbor, radial_directions, term_groups,
+                                             term_channels, channel_count, backend="auto"):
+    """Grouped plain source channels and analytic edge derivatives.
+
+    ``ye3t/runtime/execution_plan.py:7582`` (composition :7082-7155): returns
+    ``(edge_values [E, C], edge_derivatives [E, C, 3], charge_center [E, C],
+    charge_neighbor [E, C])`` in the dtype of ``radial_values`` (real or
+    complex); term channels must be distinct.
+    """
+    _check_backend(backend)
+    rv = torch.as_tensor(radial_values)
+    dev = nat.require_cuda(rv, what="plain_site_basis_product_with_derivative")
+    rd, av, ad, p, pc, pn, dr = (torch.as_tensor(v, dtype=rv.dtype, device=dev).contiguous()
+                                 for v in (radial_derivatives, angular_values, angular_derivatives, prefactors,
+                                           prefactor_derivatives_center, prefactor_derivatives_neighbor,
+                                           radial_directions))
+    tg, tc = (torch.as_tensor(v, dtype=torch.int64, device=dev).reshape(-1).contiguous()
+              for v in (term_groups, term_channels))
+    rv = rv.contiguous()
+    C = int(channel_count)
+    if rv.ndim != 2:
+        raise ValueError("radial_values must be [group, E]")
+    G, E = int(rv.shape[0]), int(rv.shape[1])
+    T = int(tg.numel())
+    if rd.shape != rv.shape or p.shape != rv.shape or pc.shape != rv.shape or pn.shape != rv.shape:
+        raise ValueError("radial and prefactor tables must be [group, E]")
+    if av.shape != (T, E) or ad.shape != (T, E, 3) or dr.shape != (E, 3) or tc.numel() != T:
+        raise ValueError("angular tables must be [term, E] / [term, E, 3] and directions [E, 3]")
+    _index_range(tg, G, "term_groups")
+    _index_range(tc, C, "term_channels")
+    outs = (torch.empty((E, C), dtype=rv.dtype, device=dev), torch.empty((E, C, 3), dtype=rv.dtype, device=dev),
+            torch.empty((E, C), dtype=rv.dtype, device=dev), torch.empty((E, C), dtype=rv.dtype, device=dev))
+    nat.check(nat.lib().y3b_plain_site_basis_product(
+        nat.dtype_code(rv.dtype), rv.data_ptr(), rd.data_ptr(), G, av.data_ptr(), ad.data_ptr(), T, p.data_ptr(),
+        pc.data_ptr(), pn.data_ptr(), dr.data_ptr(), E, tg.data_ptr(), tc.data_ptr(), C,
+        *(o.data_ptr() for o in outs), None, nat.stream_of(dev)), "plain_site_basis_product_with_derivative")
+    return outs
 
 
 # ---------------------------------------------------------------------------
@@ -346,6 +433,8 @@ def native_execution_plan_capabilities():
             "density_accumulate_adjoint": ["float32", "float64", "complex64", "complex128"],
             "symmetric_power_monomial": ["float32", "float64", "complex64", "complex128"],
             "symmetric_power_shared_monomial": ["float32", "float64", "complex64", "complex128"],
+            "scheduled_radial_angular_channels_with_derivative": ["float32", "float64"],
+            "plain_site_basis_product_with_derivative": ["float32", "float64", "complex64", "complex128"],
             "factorized_schedule": ["float32", "float64", "complex64", "complex128"],
             "ace_density": ["float64 -> complex128"],
             "ace_density_mixed": ["float32 -> complex64", "float64 -> complex128"],
