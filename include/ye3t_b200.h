@@ -86,6 +86,17 @@ int y3b_symmetric_power_monomial(int dtype, const void* input, int64_t batch, in
  *   out[b, o] = sum_{t in [off[o], off[o+1])} values[t] monomial[b, terms[t]]
  * Monomial indices outside [0, monomial_count) set Y3B_STATUS_INDEX_RANGE in
  * *status (nullable) and contribute 0. */
+/* Vector-Jacobian product of the grouped table (autograd of
+ * symmetric_power_monomial, execution_plan.py:4970-4990; CPU core
+ * symmetric_power_monomial_adjoint): input_adjoint[b, i] = sum over terms t of
+ * output_adjoint[b, output_indices[t]] conj(d term_t / d x_i).  Output indices
+ * outside [0, output_dim) set Y3B_STATUS_INDEX_RANGE and contribute 0. */
+int y3b_symmetric_power_monomial_adjoint(int dtype, const void* output_adjoint, const void* input, int64_t batch,
+                                         int64_t input_dim, const int64_t* monomial_counts,
+                                         const int64_t* output_indices, const void* monomial_values,
+                                         int64_t term_count, int64_t output_dim, void* input_adjoint,
+                                         int32_t* status, void* stream);
+
 int y3b_symmetric_power_shared_monomial(int dtype, const void* input, int64_t batch, int64_t input_dim,
                                         const int64_t* monomial_counts, int64_t monomial_count,
                                         const int64_t* output_offsets, int64_t output_dim,
@@ -141,6 +152,25 @@ int y3b_scheduled_radial_angular_channels(int dtype, const void* radial_values, 
  * (execution_plan_torch.cpp, schema beside :7268; Python entry
  * execution_plan.py:7582).  Groups or channels out of range set
  * Y3B_STATUS_INDEX_RANGE and write nothing. */
+/* Adjoint of the plain site-basis product with edge weights w [E] and their
+ * derivatives dw [E, 3] against edge-channel adjoints a [E, channel_count]:
+ *   position_adjoint[e, :] = sum_t a[e, ch_t] (td[t, e, :] w[e] + tv[t, e] dw[e, :])
+ *   charge_center / charge_neighbor _adjoint[e] = sum_t a[e, ch_t] pc / pn[g_t, e] R[g_t, e] Y[t, e] w[e]
+ * (tv, td: the forward term values and derivatives above).  Replaces
+ * ye3t_runtime::plain_site_basis_product_adjoint (Python entry
+ * execution_plan.py:7790).  One thread per edge; no atomics. */
+int y3b_plain_site_basis_product_adjoint(int dtype, const void* radial_values, const void* radial_derivatives,
+                                         int64_t group_count, const void* angular_values,
+                                         const void* angular_derivatives, int64_t term_count, const void* prefactors,
+                                         const void* prefactor_derivatives_center,
+                                         const void* prefactor_derivatives_neighbor, const void* radial_directions,
+                                         const void* edge_weights, const void* edge_weight_derivatives,
+                                         int64_t edge_count, const int64_t* term_groups,
+                                         const int64_t* term_channels, int64_t channel_count,
+                                         const void* edge_adjoint, void* position_adjoint,
+                                         void* charge_center_adjoint, void* charge_neighbor_adjoint,
+                                         int32_t* status, void* stream);
+
 int y3b_plain_site_basis_product(int dtype, const void* radial_values, const void* radial_derivatives,
                                  int64_t group_count, const void* angular_values, const void* angular_derivatives,
                                  int64_t term_count, const void* prefactors, const void* prefactor_derivatives_center,

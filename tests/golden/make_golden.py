@@ -593,9 +593,53 @@ def edge_products_fixture():
     print("edge_products.npz", len(out), "arrays")
 
 
+def adjoints_fixture():
+    """Standalone adjoints through the reference: ``plain_site_basis_product_adjoint``
+    (execution_plan.py:7790, ``backend="reference"``) and the input gradient of
+    ``symmetric_power_monomial_contraction`` (:11998) by torch autograd, for every symmetric
+    block kind of the nu<=4 word set."""
+    from ye3t.runtime.execution_plan import plain_site_basis_product_adjoint, symmetric_power_monomial_contraction
+    g = torch.Generator().manual_seed(6021)
+    out = {}
+    for tag, dt in (("f64", torch.float64), ("c128", torch.complex128)):
+        G, T, E, C = 3, 10, 29, 14
+
+        def rnd(*shape):
+            x = torch.randn(*shape, dtype=torch.float64, generator=g)
+            return torch.complex(x, torch.randn(*shape, dtype=torch.float64, generator=g)) if dt.is_complex else x
+        d = torch.randn(E, 3, dtype=torch.float64, generator=g)
+        d = (d / d.norm(dim=1, keepdim=True)).to(dt)
+        args = dict(radial_values=rnd(G, E), radial_derivatives=rnd(G, E), angular_values=rnd(T, E),
+                    angular_derivatives=rnd(T, E, 3), prefactors=rnd(G, E), prefactor_derivatives_center=rnd(G, E),
+                    prefactor_derivatives_neighbor=rnd(G, E), radial_directions=d, edge_weights=rnd(E),
+                    edge_weight_derivatives=rnd(E, 3), term_groups=torch.randint(0, G, (T,), generator=g),
+                    term_channels=torch.randperm(C, generator=g)[:T], edge_adjoint=rnd(E, C))
+        res = plain_site_basis_product_adjoint(**args, backend="reference")
+        for k, x in args.items():
+            out[f"pa_{tag}_{k}"] = x.numpy()
+        for k, x in zip(("position", "charge_center", "charge_neighbor"), res):
+            out[f"pa_{tag}_{k}"] = x.numpy()
+    bundle = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu4_L0.npz"))
+    for j, key in enumerate(sorted(bundle.sym_tables)):
+        t = bundle.sym_tables[key]
+        width = t.monomial_counts.shape[1]
+        x = torch.complex(torch.randn(33, width, dtype=torch.float64, generator=g),
+                          torch.randn(33, width, dtype=torch.float64, generator=g)).requires_grad_(True)
+        y = symmetric_power_monomial_contraction(x, torch.as_tensor(t.monomial_counts),
+                                                 torch.as_tensor(t.output_offsets), torch.as_tensor(t.output_index),
+                                                 torch.as_tensor(t.monomial_value), backend="reference")
+        adj = torch.complex(torch.randn(*y.shape, dtype=torch.float64, generator=g),
+                            torch.randn(*y.shape, dtype=torch.float64, generator=g))
+        (grad,) = torch.autograd.grad(y, x, adj)
+        out[f"sp{j}_key"] = np.asarray(key, dtype=np.int64)
+        out[f"sp{j}_x"], out[f"sp{j}_adj"], out[f"sp{j}_grad"] = x.detach().numpy(), adj.numpy(), grad.numpy()
+    np.savez_compressed(os.path.join(HERE, "adjoints.npz"), **out)
+    print("adjoints.npz", len(out), "arrays")
+
+
 if __name__ == "__main__":
     which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing", "real",
-                             "hierarchical", "edge_products"]
+                             "hierarchical", "edge_products", "adjoints"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -616,3 +660,5 @@ if __name__ == "__main__":
         hierarchical_fixture()
     if "edge_products" in which:
         edge_products_fixture()
+    if "adjoints" in which:
+        adjoints_fixture()

@@ -54,3 +54,42 @@ def test_edge_products_reject_bad_indices(golden):
     args = [torch.as_tensor(g[f"p_f64_{k}"], device=DEV) for k in P_ARGS]
     with pytest.raises(IndexError):
         plain_site_basis_product_with_derivative(*args, 3)  # channels beyond a 3-channel output
+
+
+PA_ARGS = ("radial_values", "radial_derivatives", "angular_values", "angular_derivatives", "prefactors",
+           "prefactor_derivatives_center", "prefactor_derivatives_neighbor", "radial_directions", "edge_weights",
+           "edge_weight_derivatives", "term_groups", "term_channels", "edge_adjoint")
+
+
+@pytest.mark.parametrize("tag,tol", [("f64", 1e-13), ("c128", 1e-12)])
+def test_plain_site_basis_product_adjoint_matches_reference(golden, tag, tol):
+    from ye3t_b200.runtime import plain_site_basis_product_adjoint as op
+    g = golden("adjoints")
+    outs = op(*(torch.as_tensor(g[f"pa_{tag}_{k}"], device=DEV) for k in PA_ARGS))
+    for name, y in zip(("position", "charge_center", "charge_neighbor"), outs):
+        ref = g[f"pa_{tag}_{name}"]
+        assert tuple(y.shape) == ref.shape
+        err = np.abs(y.cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1.0)
+        assert err <= tol, (name, err)
+
+
+def test_symmetric_power_backward_matches_reference_autograd(golden):
+    """Every symmetric block kind of the nu<=4 word set: the input gradient of the grouped
+    contraction (GPU vector-Jacobian product) against torch autograd through the reference."""
+    import os
+    from ye3t_b200.runtime import symmetric_power_table_contraction
+    from ye3t_b200.schedules import ACEBundle
+    g = golden("adjoints")
+    b = ACEBundle.load(os.path.join(os.path.dirname(os.path.dirname(__file__)), "ye3t_b200", "bundles",
+                                    "ace_n8_l3_nu4_L0.npz"))
+    j = 0
+    while f"sp{j}_key" in g:
+        t = b.sym_tables[tuple(int(v) for v in g[f"sp{j}_key"])]
+        x = torch.as_tensor(g[f"sp{j}_x"], device=DEV).requires_grad_(True)
+        y = symmetric_power_table_contraction(x, t)
+        (grad,) = torch.autograd.grad(y, x, torch.as_tensor(g[f"sp{j}_adj"], device=DEV))
+        ref = g[f"sp{j}_grad"]
+        err = np.abs(grad.cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1.0)
+        assert err <= 1e-12, (j, err)
+        j += 1
+    assert j == 23

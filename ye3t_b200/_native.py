@@ -62,6 +62,10 @@ _SIGS = {
                                                            VP, VP, VP]),
     "y3b_scheduled_radial_angular_channels": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, VP, VP, I64, VP, VP, I64, VP,
                                                              VP, VP, VP, I64, VP, VP, VP, VP]),
+    "y3b_symmetric_power_monomial_adjoint": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, VP, VP, VP, I64, I64, VP,
+                                                            VP, VP]),
+    "y3b_plain_site_basis_product_adjoint": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, VP, VP, I64, VP, VP, VP, VP, VP,
+                                                            VP, I64, VP, VP, I64, VP, VP, VP, VP, VP, VP]),
     "y3b_plain_site_basis_product": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, VP, VP, I64, VP, VP, VP, VP, I64, VP,
                                                     VP, I64, VP, VP, VP, VP, VP, VP]),
     "y3b_cheb_exp_cos_radial_table": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, VP, VP, VP]),

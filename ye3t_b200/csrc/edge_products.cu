@@ -5,7 +5,8 @@
 //    ye3t/runtime/execution_plan.py:7675, reference composition :7036-7080);
 //  * the plain site-basis product with per-edge group prefactors, complex
 //    capable (plain_site_basis_product_with_derivative, :7582, reference
-//    composition :7082-7155).
+//    composition :7082-7155), and its adjoint against edge-channel adjoints
+//    (plain_site_basis_product_adjoint, :7790, composition :7158-7220).
 // Each output entry is formed with the reference's operation order; the real
 // operator rounds every product and sum separately (no contraction), as the
 // reference's elementwise tensor operations do.
@@ -88,6 +89,49 @@ __global__ void __launch_bounds__(256) plain_product_kernel(
   }
 }
 
+// Adjoint of the plain site-basis product with edge weights w[e] (and their
+// Cartesian derivatives dw[e, :]) against edge-channel adjoints a[e, ch]
+// (execution_plan.py:7790, composition :7158-7220): per edge,
+//   position[e, :] = sum_t a[e, ch_t] (td[t, e, :] w[e] + tv[t, e] dw[e, :])
+//   charge_center / neighbor[e] = sum_t a[e, ch_t] pc / pn[g_t, e] R[g_t, e] Y[t, e] w[e]
+// with tv, td the term values and derivatives of the forward product.  One
+// thread per edge, terms in order (no atomics).
+template <typename T>
+__global__ void __launch_bounds__(256) plain_product_adjoint_kernel(
+    const T* __restrict__ rv, const T* __restrict__ rd, int64_t G, const T* __restrict__ av,
+    const T* __restrict__ ad, int64_t Tn, const T* __restrict__ pref, const T* __restrict__ pc,
+    const T* __restrict__ pn, const T* __restrict__ dir, const T* __restrict__ w, const T* __restrict__ dw,
+    int64_t E, const int64_t* __restrict__ groups, const int64_t* __restrict__ channels, int64_t C,
+    const T* __restrict__ adj, T* __restrict__ pos, T* __restrict__ charge_c, T* __restrict__ charge_n,
+    int32_t* __restrict__ status) {
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < E; e += int64_t(gridDim.x) * blockDim.x) {
+    T acc[3] = {zero<T>(), zero<T>(), zero<T>()}, cc = zero<T>(), cn = zero<T>();
+    const T we = w[e];
+    for (int64_t t = 0; t < Tn; ++t) {
+      const int64_t g = __ldg(groups + t), ch = __ldg(channels + t);
+      if (g < 0 || g >= G || ch < 0 || ch >= C) {
+        if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        continue;
+      }
+      const T r = rv[g * E + e], r1 = rd[g * E + e], p = pref[g * E + e], y = av[t * E + e];
+      const T a = adj[e * C + ch];
+      const T tv = mul(mul(p, r), y);
+#pragma unroll
+      for (int x = 0; x < 3; ++x) {
+        const T td = mul(p, add(mul(mul(r1, dir[3 * e + x]), y), mul(r, ad[(t * E + e) * 3 + x])));
+        acc[x] = add(acc[x], mul(a, add(mul(td, we), mul(tv, dw[3 * e + x]))));
+      }
+      const T common = mul(mul(r, y), we);
+      cc = add(cc, mul(mul(a, pc[g * E + e]), common));
+      cn = add(cn, mul(mul(a, pn[g * E + e]), common));
+    }
+#pragma unroll
+    for (int x = 0; x < 3; ++x) pos[3 * e + x] = acc[x];
+    charge_c[e] = cc;
+    charge_n[e] = cn;
+  }
+}
+
 }  // namespace
 }  // namespace y3b
 
@@ -154,6 +198,38 @@ extern "C" int y3b_plain_site_basis_product(
         edge_count, term_groups, term_channels, channel_count, static_cast<T*>(edge_values),
         static_cast<T*>(edge_derivatives), static_cast<T*>(charge_center), static_cast<T*>(charge_neighbor),
         status);
+  });
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+extern "C" int y3b_plain_site_basis_product_adjoint(
+    int dtype, const void* radial_values, const void* radial_derivatives, int64_t group_count,
+    const void* angular_values, const void* angular_derivatives, int64_t term_count, const void* prefactors,
+    const void* prefactor_derivatives_center, const void* prefactor_derivatives_neighbor,
+    const void* radial_directions, const void* edge_weights, const void* edge_weight_derivatives, int64_t edge_count,
+    const int64_t* term_groups, const int64_t* term_channels, int64_t channel_count, const void* edge_adjoint,
+    void* position_adjoint, void* charge_center_adjoint, void* charge_neighbor_adjoint, int32_t* status,
+    void* stream) {
+  Y3B_CHECK_ARG(group_count >= 0 && term_count >= 0 && edge_count >= 0 && channel_count >= 0, "negative size");
+  if (edge_count == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(edge_weights && edge_weight_derivatives && position_adjoint && charge_center_adjoint &&
+                    charge_neighbor_adjoint && radial_directions &&
+                    (term_count == 0 || (radial_values && radial_derivatives && angular_values &&
+                                         angular_derivatives && prefactors && prefactor_derivatives_center &&
+                                         prefactor_derivatives_neighbor && term_groups && term_channels &&
+                                         edge_adjoint)),
+                "null pointer argument");
+  const int threads = 256;
+  Y3B_DISPATCH(dtype, T, {
+    plain_product_adjoint_kernel<T><<<grid_for(edge_count, threads), threads, 0, as_stream(stream)>>>(
+        static_cast<const T*>(radial_values), static_cast<const T*>(radial_derivatives), group_count,
+        static_cast<const T*>(angular_values), static_cast<const T*>(angular_derivatives), term_count,
+        static_cast<const T*>(prefactors), static_cast<const T*>(prefactor_derivatives_center),
+        static_cast<const T*>(prefactor_derivatives_neighbor), static_cast<const T*>(radial_directions),
+        static_cast<const T*>(edge_weights), static_cast<const T*>(edge_weight_derivatives), edge_count, term_groups,
+        term_channels, channel_count, static_cast<const T*>(edge_adjoint), static_cast<T*>(position_adjoint),
+        static_cast<T*>(charge_center_adjoint), static_cast<T*>(charge_neighbor_adjoint), status);
   });
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;

@@ -120,6 +120,51 @@ __global__ void __launch_bounds__(256) sympow_shared_kernel(
   }
 }
 
+// Conjugate-transposed derivative of the grouped table (the vector-Jacobian
+// product autograd forms, execution_plan.py:4970-4990 / ye3t_runtime_core
+// symmetric_power_monomial_adjoint): grad[b, i] = sum over terms t with
+// counts[t, i] = e > 0 of adj[b, o_t] conj(e c_t x_i^(e-1) prod_{j != i}
+// x_j^(e_j)).  One thread per (batch row, input component), so every entry has
+// one owner; the derivative is formed without dividing by x_i.
+template <typename T>
+__device__ __forceinline__ T cconj(T a) { return a; }
+template <>
+__device__ __forceinline__ float2 cconj(float2 a) { return make_float2(a.x, -a.y); }
+template <>
+__device__ __forceinline__ double2 cconj(double2 a) { return make_double2(a.x, -a.y); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) sympow_adjoint_kernel(
+    const T* __restrict__ adj, const T* __restrict__ x, int64_t batch, int64_t in_dim,
+    const int64_t* __restrict__ counts, const int64_t* __restrict__ oidx, const T* __restrict__ vals,
+    int64_t terms, int64_t out_dim, T* __restrict__ grad, int32_t* __restrict__ status) {
+  const int64_t total = batch * in_dim;
+  for (int64_t lin = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; lin < total;
+       lin += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = lin / in_dim, i = lin - b * in_dim;
+    const T* xr = x + b * in_dim;
+    T acc = zero<T>();
+    for (int64_t t = 0; t < terms; ++t) {
+      const int64_t e = __ldg(counts + t * in_dim + i);
+      if (e <= 0) continue;
+      const int64_t o = __ldg(oidx + t);
+      if (o < 0 || o >= out_dim) {
+        if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        continue;
+      }
+      T d = vals[t];
+      for (int64_t j = 0; j < in_dim; ++j) {
+        const int64_t ej = __ldg(counts + t * in_dim + j);
+        d = mul(d, ipow(xr[j], j == i ? ej - 1 : ej));
+      }
+      using R = typename Real<T>::type;
+      d = scale(R(e), d);
+      acc = add(acc, mul(adj[b * out_dim + o], cconj(d)));
+    }
+    grad[lin] = acc;
+  }
+}
+
 }  // namespace y3b
 
 using namespace y3b;
@@ -195,6 +240,28 @@ extern "C" int y3b_symmetric_power_shared_monomial(int dtype, const void* input,
     sympow_shared_kernel<T><<<grid, threads, 0, as_stream(stream)>>>(
         static_cast<const T*>(input), batch, input_dim, monomial_counts, monomial_count, output_offsets,
         coefficient_terms, static_cast<const T*>(coefficient_values), output_dim, static_cast<T*>(out), status);
+  });
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+extern "C" int y3b_symmetric_power_monomial_adjoint(int dtype, const void* output_adjoint, const void* input,
+                                                    int64_t batch, int64_t input_dim, const int64_t* monomial_counts,
+                                                    const int64_t* output_indices, const void* monomial_values,
+                                                    int64_t term_count, int64_t output_dim, void* input_adjoint,
+                                                    int32_t* status, void* stream) {
+  Y3B_CHECK_ARG(batch >= 0 && input_dim >= 0 && output_dim >= 0 && term_count >= 0, "negative size");
+  const int64_t total = batch * input_dim;
+  if (total == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(output_adjoint && input && input_adjoint &&
+                    (term_count == 0 || (monomial_counts && output_indices && monomial_values)),
+                "null pointer argument");
+  const int threads = 256;
+  Y3B_DISPATCH(dtype, T, {
+    sympow_adjoint_kernel<T><<<grid_for(total, threads), threads, 0, as_stream(stream)>>>(
+        static_cast<const T*>(output_adjoint), static_cast<const T*>(input), batch, input_dim, monomial_counts,
+        output_indices, static_cast<const T*>(monomial_values), term_count, output_dim,
+        static_cast<T*>(input_adjoint), status);
   });
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;

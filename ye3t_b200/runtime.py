@@ -30,6 +30,7 @@ __all__ = [
     "symmetric_power_shared_monomial_contraction",
     "scheduled_radial_angular_channels_with_derivative",
     "plain_site_basis_product_with_derivative",
+    "plain_site_basis_product_adjoint",
     "symmetric_power_table_contraction",
     "pace_radial_channel_contraction_with_derivative",
     "native_execution_plan_capabilities",
@@ -204,6 +205,50 @@ def plain_site_basis_product_with_derivative(radial_values, radial_derivatives, 
     return outs
 
 
+def plain_site_basis_product_adjoint(radial_values, radial_derivatives, angular_values, angular_derivatives,
+                                     prefactors, prefactor_derivatives_center, prefactor_derivatives_neighbor,
+                                     radial_directions, edge_weights, edge_weight_derivatives, term_groups,
+                                     term_channels, edge_adjoint, backend="auto"):
+    """Edge adjoints of the plain site-basis product; ``ye3t/runtime/execution_plan.py:7790``.
+
+    Returns ``(edge_position_adjoint [E, 3], edge_charge_center [E],
+    edge_charge_neighbor [E])`` (composition :7158-7220), one thread per edge.
+    """
+    _check_backend(backend)
+    rv = torch.as_tensor(radial_values)
+    dev = nat.require_cuda(rv, what="plain_site_basis_product_adjoint")
+    rd, av, ad, p, pc, pn, dr, w, dw, adj = (
+        torch.as_tensor(v, dtype=rv.dtype, device=dev).contiguous()
+        for v in (radial_derivatives, angular_values, angular_derivatives, prefactors, prefactor_derivatives_center,
+                  prefactor_derivatives_neighbor, radial_directions, edge_weights, edge_weight_derivatives,
+                  edge_adjoint))
+    tg, tc = (torch.as_tensor(v, dtype=torch.int64, device=dev).reshape(-1).contiguous()
+              for v in (term_groups, term_channels))
+    rv = rv.contiguous()
+    if rv.ndim != 2:
+        raise ValueError("radial_values must be [group, E]")
+    G, E = int(rv.shape[0]), int(rv.shape[1])
+    T = int(tg.numel())
+    if rd.shape != rv.shape or p.shape != rv.shape or pc.shape != rv.shape or pn.shape != rv.shape:
+        raise ValueError("radial and prefactor tables must be [group, E]")
+    if av.shape != (T, E) or ad.shape != (T, E, 3) or dr.shape != (E, 3) or tc.numel() != T:
+        raise ValueError("angular tables must be [term, E] / [term, E, 3] and directions [E, 3]")
+    if w.reshape(-1).numel() != E or dw.shape != (E, 3) or adj.ndim != 2 or adj.shape[0] != E:
+        raise ValueError("edge weights must be [E] / [E, 3] and the edge adjoint [E, channels]")
+    C = int(adj.shape[1])
+    _index_range(tg, G, "term_groups")
+    _index_range(tc, C, "term_channels")
+    pos = torch.empty((E, 3), dtype=rv.dtype, device=dev)
+    cc = torch.empty((E,), dtype=rv.dtype, device=dev)
+    cn = torch.empty((E,), dtype=rv.dtype, device=dev)
+    nat.check(nat.lib().y3b_plain_site_basis_product_adjoint(
+        nat.dtype_code(rv.dtype), rv.data_ptr(), rd.data_ptr(), G, av.data_ptr(), ad.data_ptr(), T, p.data_ptr(),
+        pc.data_ptr(), pn.data_ptr(), dr.data_ptr(), w.data_ptr(), dw.data_ptr(), E, tg.data_ptr(), tc.data_ptr(),
+        C, adj.data_ptr(), pos.data_ptr(), cc.data_ptr(), cn.data_ptr(), None, nat.stream_of(dev)),
+        "plain_site_basis_product_adjoint")
+    return pos, cc, cn
+
+
 # ---------------------------------------------------------------------------
 def _density_forward(edge_values, centers, atom_count, validate):
     dev = nat.require_cuda(edge_values, centers, what="density_accumulate")
@@ -284,9 +329,51 @@ def density_accumulate_adjoint(atomic_adjoint, centers, *, backend="auto", valid
 
 
 # ---------------------------------------------------------------------------
+def _sympow_forward(x2, counts, offsets, values, out_dim):
+    out = torch.empty((x2.shape[0], out_dim), dtype=x2.dtype, device=x2.device)
+    nat.check(nat.lib().y3b_symmetric_power_monomial(nat.dtype_code(x2.dtype), x2.data_ptr(), x2.shape[0],
+                                                      x2.shape[1], counts.data_ptr(), offsets.data_ptr(),
+                                                      values.data_ptr(), int(counts.shape[0]), out_dim,
+                                                      out.data_ptr(), nat.stream_of(x2.device)),
+              "symmetric_power_monomial_contraction")
+    return out
+
+
+def _sympow_adjoint(adj, x2, counts, indices, values, out_dim):
+    grad = torch.empty_like(x2)
+    status = _status(x2.device)
+    nat.check(nat.lib().y3b_symmetric_power_monomial_adjoint(
+        nat.dtype_code(x2.dtype), adj.data_ptr(), x2.data_ptr(), x2.shape[0], x2.shape[1], counts.data_ptr(),
+        indices.data_ptr(), values.data_ptr(), int(counts.shape[0]), out_dim, grad.data_ptr(), status.data_ptr(),
+        nat.stream_of(x2.device)), "symmetric_power_monomial_adjoint")
+    _raise_on_status(status, "symmetric_power_monomial_adjoint")
+    return grad
+
+
+class _SymmetricPowerMonomial(torch.autograd.Function):
+    """First-order autograd of the grouped table (execution_plan.py:4960-4990)."""
+
+    @staticmethod
+    def forward(ctx, x2, counts, offsets, indices, values, out_dim):
+        ctx.save_for_backward(x2, counts, indices, values)
+        ctx.out_dim = out_dim
+        return _sympow_forward(x2, counts, offsets, values, out_dim)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, adj):
+        x2, counts, indices, values = ctx.saved_tensors
+        return _sympow_adjoint(adj.contiguous(), x2, counts, indices, values, ctx.out_dim), None, None, None, None, None
+
+
 def symmetric_power_monomial_contraction(input, monomial_counts, output_offsets, output_indices,
                                          monomial_values, *, backend="auto"):
-    """Grouped symmetric-power table contraction; ``ye3t/runtime/execution_plan.py:11998``."""
+    """Grouped symmetric-power table contraction; ``ye3t/runtime/execution_plan.py:11998``.
+
+    Differentiable with respect to ``input`` (first order): the backward is
+    the table's vector-Jacobian product on the GPU
+    (``y3b_symmetric_power_monomial_adjoint``).
+    """
     _check_backend(backend)
     x = torch.as_tensor(input)
     dev = nat.require_cuda(x, what="symmetric_power_monomial_contraction")
@@ -295,7 +382,7 @@ def symmetric_power_monomial_contraction(input, monomial_counts, output_offsets,
     in_dim = int(x.shape[-1])
     counts = torch.as_tensor(monomial_counts, dtype=torch.int64, device=dev).contiguous()
     offsets = torch.as_tensor(output_offsets, dtype=torch.int64, device=dev).reshape(-1).contiguous()
-    indices = torch.as_tensor(output_indices, dtype=torch.int64, device=dev).reshape(-1)
+    indices = torch.as_tensor(output_indices, dtype=torch.int64, device=dev).reshape(-1).contiguous()
     values = torch.as_tensor(monomial_values, dtype=x.dtype, device=dev).reshape(-1).contiguous()
     if counts.ndim != 2 or int(counts.shape[1]) != in_dim:
         raise ValueError("monomial_counts must have shape [term, input_dimension]")
@@ -303,12 +390,10 @@ def symmetric_power_monomial_contraction(input, monomial_counts, output_offsets,
         raise ValueError("output_indices / monomial_values length must match the term count")
     out_dim = int(offsets.numel()) - 1
     x2 = x.contiguous().reshape(-1, in_dim)
-    out = torch.empty((x2.shape[0], out_dim), dtype=x.dtype, device=dev)
-    nat.check(nat.lib().y3b_symmetric_power_monomial(nat.dtype_code(x.dtype), x2.data_ptr(), x2.shape[0], in_dim,
-                                                      counts.data_ptr(), offsets.data_ptr(), values.data_ptr(),
-                                                      int(counts.shape[0]), out_dim, out.data_ptr(),
-                                                      nat.stream_of(dev)),
-              "symmetric_power_monomial_contraction")
+    if x2.requires_grad and torch.is_grad_enabled():
+        out = _SymmetricPowerMonomial.apply(x2, counts, offsets, indices, values, out_dim)
+    else:
+        out = _sympow_forward(x2, counts, offsets, values, out_dim)
     return out.reshape(*x.shape[:-1], out_dim)
 
 
@@ -435,6 +520,8 @@ def native_execution_plan_capabilities():
             "symmetric_power_shared_monomial": ["float32", "float64", "complex64", "complex128"],
             "scheduled_radial_angular_channels_with_derivative": ["float32", "float64"],
             "plain_site_basis_product_with_derivative": ["float32", "float64", "complex64", "complex128"],
+            "plain_site_basis_product_adjoint": ["float32", "float64", "complex64", "complex128"],
+            "symmetric_power_monomial_adjoint": ["float32", "float64", "complex64", "complex128"],
             "factorized_schedule": ["float32", "float64", "complex64", "complex128"],
             "ace_density": ["float64 -> complex128"],
             "ace_density_mixed": ["float32 -> complex64", "float64 -> complex128"],
