@@ -68,6 +68,23 @@ int y3b_factorized_schedule_evaluate(int dtype, const void* block_values, int64_
                                      int64_t component_count, int64_t term_count, void* out,
                                      int32_t* status, void* stream);
 
+/* Vector-Jacobian product of the evaluation above (the backward torch autograd
+ * forms through evaluate_factorized_schedule_torch, core/couplings.py:481-567):
+ *   grad[b, label, j, m] = sum over (t, c) reading slot (label, j, m) of
+ *                          adj[b, c] conj(coeffs[t] prod_{k != j} bv[b, label, k, m_idx[t, k]])
+ * block_values and the gradient are [batch, basis, blocks, magnetic_dim];
+ * slot s = (label * blocks + j) * magnetic_dim + m lists its (term,
+ * component) pairs in slot_terms / slot_components[slot_offsets[s] ..
+ * slot_offsets[s+1]) (host-built transposed table; ye3t_b200/couplings.py).
+ * One thread per gradient entry: no atomics.  Indices out of range set
+ * Y3B_STATUS_INDEX_RANGE in *status (nullable) and contribute 0. */
+int y3b_factorized_schedule_adjoint(int dtype, const void* output_adjoint, const void* block_values, int64_t batch,
+                                    int64_t basis_count, int64_t block_count, int64_t magnetic_dim,
+                                    const int64_t* block_m_indices, const void* coeffs, int64_t component_count,
+                                    int64_t term_count, const int64_t* slot_offsets, const int64_t* slot_terms,
+                                    const int64_t* slot_components, void* block_values_adjoint, int32_t* status,
+                                    void* stream);
+
 /* Symmetric-power monomial contraction, grouped table.
  * Replaces ye3t_runtime::symmetric_power_monomial
  * (ye3t/runtime/csrc/execution_plan_torch.cpp:7528; CPU core

@@ -49,12 +49,15 @@ def _record_arrays(prefix, rec: ScheduleRecord, out: dict):
     out[prefix + "specs"] = np.frombuffer(json.dumps(rec.block_specs).encode(), dtype=np.uint8)
 
 
+SCHEDULE_CASES = [((1, 1, 2), (1, 1, 0), 0), ((1, 1, 2), (1, 1, 0), 2), ((1, 1, 2, 3), (1, 1, 2, 2), 1),
+                  ((1, 2, 3, 4), (3, 3, 3, 3), 0), ((1, 2, 3, 4), (3, 3, 3, 3), 2),
+                  ((1, 1, 2, 2), (2, 2, 3, 3), 4), ((1, 1, 1, 1), (3, 3, 3, 3), 6),
+                  ((1, 2, 2, 3), (0, 1, 2, 3), 0)]
+
+
 def schedules_fixture():
     """``ACEFactorizedScheduleReport.evaluate`` (``couplings/__init__.py:2574``) on seeded blocks."""
-    cases = [((1, 1, 2), (1, 1, 0), 0), ((1, 1, 2), (1, 1, 0), 2), ((1, 1, 2, 3), (1, 1, 2, 2), 1),
-             ((1, 2, 3, 4), (3, 3, 3, 3), 0), ((1, 2, 3, 4), (3, 3, 3, 3), 2),
-             ((1, 1, 2, 2), (2, 2, 3, 3), 4), ((1, 1, 1, 1), (3, 3, 3, 3), 6),
-             ((1, 2, 2, 3), (0, 1, 2, 3), 0)]
+    cases = SCHEDULE_CASES
     out, meta = {}, []
     g = torch.Generator().manual_seed(2026)
     for i, (content, ls, L) in enumerate(cases):
@@ -637,9 +640,71 @@ def adjoints_fixture():
     print("adjoints.npz", len(out), "arrays")
 
 
+def schedule_grads_fixture():
+    """Gradients of the reference's torch schedule evaluator (``evaluate_factorized_schedule_torch``,
+    ``core/couplings.py:481-567``, by torch autograd) for the schedules of ``schedules.npz``, complex and
+    real block values, on seeded blocks and output adjoints."""
+    g = torch.Generator().manual_seed(3141)
+    out = {}
+    for i, (content, ls, L) in enumerate(SCHEDULE_CASES):
+        rep = compile_ace_factorized_schedules_by_L(content=content, input_Ls=ls)
+        rec = ScheduleRecord.from_schedule(rep.schedules_by_L[L], rep.convention_hash)
+        bl = rec.block_L_by_label()
+        mdim = rec.max_block_m_dim
+        mask = torch.zeros(rec.basis_count, rec.block_count, mdim, dtype=torch.bool)
+        for a in range(rec.basis_count):
+            for b in range(rec.block_count):
+                mask[a, b, : 2 * bl[a, b] + 1] = True
+        shape = (5, rec.basis_count, rec.block_count, mdim)
+        re, im = torch.randn(*shape, dtype=torch.float64, generator=g), torch.randn(*shape, dtype=torch.float64,
+                                                                                    generator=g)
+        for tag, bv in (("c", torch.complex(re, im) * mask), ("r", re * mask)):
+            x = bv.clone().requires_grad_(True)
+            y = rep.evaluate(x, target_L=L, backend="torch")
+            adj = torch.randn(*y.shape, dtype=torch.float64, generator=g)
+            if y.is_complex():
+                adj = torch.complex(adj, torch.randn(*y.shape, dtype=torch.float64, generator=g))
+            (grad,) = torch.autograd.grad(y, x, adj)
+            p = f"s{i}_{tag}_"
+            out[p + "bv"], out[p + "adj"], out[p + "grad"] = bv.numpy(), adj.numpy(), grad.numpy()
+    np.savez_compressed(os.path.join(HERE, "schedule_grads.npz"), **out)
+    print("schedule_grads.npz", len(SCHEDULE_CASES), "schedules")
+
+
+def hierarchical_grads_fixture():
+    """Input gradients of ``YE3THierarchicalRepeatedBlockModule(backend="reference")`` by torch
+    autograd (``ye3t/runtime/hierarchical.py:514``) for plans of ``hierarchical.npz``, on its
+    inputs and seeded output adjoints."""
+    from ye3t.runtime import YE3THierarchicalRepeatedBlockModule
+    src = np.load(os.path.join(HERE, "hierarchical.npz"))
+    g = torch.Generator().manual_seed(8080)
+    out = {}
+    names = ["h4", "r3L1", "r4", "r6", "r6u", "r9", "r12", "lammps_ta_r04_block_2_2_a1", "lammps_ta_r08_block_4_4_a2"]
+    for name in names:
+        js = str(src["plan_" + name]) if "plan_" + name in src.files else \
+            str(src["lammps_file_" + str(src["planfile_" + name])])
+        module = YE3THierarchicalRepeatedBlockModule(json.loads(js), backend="reference", dtype=torch.complex128)
+        xs = []
+        b = 0
+        while f"x{b}_{name}" in src.files:
+            xs.append(torch.as_tensor(src[f"x{b}_{name}"]).clone().requires_grad_(True))
+            b += 1
+        y = module(*xs)
+        adj = torch.complex(torch.randn(*y.shape, dtype=torch.float64, generator=g),
+                            torch.randn(*y.shape, dtype=torch.float64, generator=g))
+        grads = torch.autograd.grad(y, xs, adj)
+        out["adj_" + name] = adj.numpy()
+        for k, gr in enumerate(grads):
+            out[f"g{k}_{name}"] = gr.numpy()
+    out["names"] = np.asarray(names)
+    np.savez_compressed(os.path.join(HERE, "hierarchical_grads.npz"), **out)
+    print("hierarchical_grads.npz", len(names), "plans")
+
+
 if __name__ == "__main__":
     which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing", "real",
-                             "hierarchical", "edge_products", "adjoints"]
+                             "hierarchical", "edge_products", "adjoints", "schedule_grads",
+                             "hierarchical_grads"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -662,3 +727,7 @@ if __name__ == "__main__":
         edge_products_fixture()
     if "adjoints" in which:
         adjoints_fixture()
+    if "schedule_grads" in which:
+        schedule_grads_fixture()
+    if "hierarchical_grads" in which:
+        hierarchical_grads_fixture()

@@ -79,3 +79,19 @@ def test_linear_readout_and_input_checks(golden):
     # unbatched inputs keep the reference's shapes
     y = module(xs[0][0], xs[1][0])
     assert tuple(y.shape) == (module.channel_count, module.tableau_count, module.magnetic_count)
+
+
+def test_input_gradients_match_reference_autograd(golden):
+    """First-order autograd through the module (the symmetric-power and schedule
+    vector-Jacobian products on the GPU) against the reference module's autograd."""
+    g = golden("hierarchical")
+    gg = golden("hierarchical_grads")
+    for name in map(str, gg["names"]):
+        module = YE3THierarchicalRepeatedBlockModule(_text(g, name), device=DEV)
+        xs = [x.requires_grad_(True) for x in _inputs(g, name)]
+        y = module(*xs)
+        grads = torch.autograd.grad(y, xs, torch.as_tensor(gg["adj_" + name], device=DEV))
+        for k, gr in enumerate(grads):
+            ref = gg[f"g{k}_{name}"]
+            err = np.abs(gr.cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1.0)
+            assert err <= 1e-12, (name, k, err)

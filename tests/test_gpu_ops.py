@@ -180,6 +180,27 @@ def test_factorized_schedule_matches_reference(golden):
         np.testing.assert_allclose(outc64, ref, rtol=1e-5, atol=1e-4)
 
 
+@pytest.mark.parametrize("tag", ["c", "r"])
+def test_factorized_schedule_backward_matches_reference_autograd(golden, tag):
+    """Block-value gradients of evaluate_factorized_schedule_torch (GPU vector-Jacobian product)
+    against torch autograd through the reference's torch evaluator."""
+    from ye3t_b200.couplings import evaluate_factorized_schedule_torch
+    g = golden("schedules")
+    gg = golden("schedule_grads")
+    i = 0
+    while f"s{i}_off" in g:
+        rec = _record(g, f"s{i}_")
+        p = f"s{i}_{tag}_"
+        x = _t(gg[p + "bv"]).requires_grad_(True)
+        y = evaluate_factorized_schedule_torch(x, rec)
+        (grad,) = torch.autograd.grad(y, x, _t(gg[p + "adj"]))
+        ref = gg[p + "grad"]
+        err = np.abs(grad.cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1.0)
+        assert err <= 1e-12, (i, err)
+        i += 1
+    assert i == 8
+
+
 def test_quickstart_config1(golden):
     from ye3t_b200.couplings import evaluate_factorized_schedule_torch as ev
     g = golden("quickstart")

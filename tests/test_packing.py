@@ -156,3 +156,36 @@ def test_adjoint_groups_cover_items_once(stem):
             shapes = len({tuple(items[x, :5]) for x, _ in real})
             assert max(costs) - min(costs) <= shapes * worst
     assert np.all(seen == 1)
+
+
+def test_schedule_adjoint_slot_table(golden):
+    """The transposed (slot -> term, component) table of the schedule adjoint, against a
+    brute-force listing, for every schedule of the reference fixture."""
+    import json as _json
+    from ye3t_b200.couplings import packed_schedule_tables
+    from ye3t_b200.schedules import ScheduleRecord
+    g = golden("schedules")
+    i = 0
+    while f"s{i}_off" in g:
+        p = f"s{i}_"
+        specs = _json.loads(bytes(g[p + "specs"]).decode())
+        rec = ScheduleRecord(rank=0, block_count=int(g[p + "bm"].shape[1]), L_R=0, n_tuple=(), l_tuple=(),
+                             block_specs=tuple(tuple(tuple(s) for s in label) for label in specs),
+                             component_offsets=g[p + "off"], component_label_index=g[p + "cli"],
+                             component_M_R=np.zeros_like(g[p + "cli"]), block_m_tuples=g[p + "bm"],
+                             coeffs=g[p + "co"])
+        pk = packed_schedule_tables(rec, "cpu")
+        mdim = rec.max_block_m_dim + 1  # wider than needed, as a caller's padded array may be
+        off, terms, comps = (x.numpy() for x in pk.slot_table(mdim, "cpu"))
+        midx = rec.block_m_indices()
+        expect = {}
+        for c in range(rec.component_count):
+            for t in range(rec.component_offsets[c], rec.component_offsets[c + 1]):
+                for j in range(rec.block_count):
+                    s = (rec.component_label_index[c] * rec.block_count + j) * mdim + midx[t, j]
+                    expect.setdefault(int(s), []).append((t, c))
+        assert off.shape[0] == rec.basis_count * rec.block_count * mdim + 1
+        for s in range(off.shape[0] - 1):
+            got = list(zip(terms[off[s]:off[s + 1]].tolist(), comps[off[s]:off[s + 1]].tolist()))
+            assert got == expect.get(s, []), (i, s)
+        i += 1

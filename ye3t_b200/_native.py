@@ -57,6 +57,8 @@ _SIGS = {
     "y3b_last_error": (ctypes.c_char_p, []),
     "y3b_factorized_schedule_evaluate": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, I64, I64, VP, VP, VP, VP,
                                                         I64, I64, VP, VP, VP]),
+    "y3b_factorized_schedule_adjoint": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, I64, VP, VP, I64, I64,
+                                                       VP, VP, VP, VP, VP, VP]),
     "y3b_symmetric_power_monomial": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, VP, VP, VP, I64, I64, VP, VP]),
     "y3b_symmetric_power_shared_monomial": (ctypes.c_int, [ctypes.c_int, VP, I64, I64, VP, I64, VP, I64, VP, VP, I64,
                                                            VP, VP, VP]),

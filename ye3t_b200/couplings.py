@@ -44,7 +44,27 @@ def _schedule_arrays(schedule):
 
 class _PackedSchedule:
     __slots__ = ("off", "cli", "midx", "coeffs_c", "coeffs_r", "comps", "blocks", "basis", "max_m", "terms",
-                 "imag_max")
+                 "imag_max", "host", "slots")
+
+    def slot_table(self, mdim, device):
+        """Transposed table of the adjoint for block arrays of magnetic width
+        ``mdim``: for every slot ``(label * blocks + j) * mdim + m`` the
+        (term, component) pairs reading it, terms in order.  Built once per width."""
+        hit = self.slots.get(mdim)
+        if hit is None:
+            off, cli, midx = self.host
+            comp_of_term = np.repeat(np.arange(self.comps, dtype=np.int64), np.diff(off))
+            T, B = midx.shape[0], self.blocks
+            slot = ((cli[comp_of_term][:, None] * B + np.arange(B)[None, :]) * mdim + midx).reshape(-1)
+            order = np.argsort(slot, kind="stable")  # by slot, then term
+            S = self.basis * B * mdim
+            counts = np.bincount(slot, minlength=S) if slot.size else np.zeros(S, dtype=np.int64)
+            offsets = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+            terms = np.repeat(np.arange(T, dtype=np.int64), B)[order]
+            hit = (torch.as_tensor(offsets).to(device), torch.as_tensor(terms).to(device),
+                   torch.as_tensor(comp_of_term[terms]).to(device))
+            self.slots[mdim] = hit
+        return hit
 
 
 def packed_schedule_tables(schedule, device):
@@ -64,6 +84,9 @@ def packed_schedule_tables(schedule, device):
     p.coeffs_c = torch.as_tensor(c.astype(np.complex128)).to(device)
     p.coeffs_r = torch.as_tensor(np.ascontiguousarray(c.real, dtype=np.float64)).to(device)
     p.comps, p.blocks, p.basis, p.max_m, p.terms = comps, blocks, basis, max_m, int(c.shape[0])
+    p.host = (np.asarray(off, dtype=np.int64), np.asarray(cli, dtype=np.int64),
+              np.ascontiguousarray(midx, dtype=np.int64).reshape(-1, blocks))
+    p.slots = {}
     try:
         ref = weakref.ref(schedule)
     except TypeError:  # objects without weakref support: keep them alive in the cache
@@ -89,8 +112,6 @@ def evaluate_factorized_schedule_torch(block_values, schedule, *, backend="auto"
         raise ValueError(f"Unknown factorized runtime backend: {backend!r}")
     bv = torch.as_tensor(block_values)
     dev = nat.require_cuda(bv, what="evaluate_factorized_schedule_torch")
-    if bv.requires_grad and torch.is_grad_enabled():
-        raise NotImplementedError("ye3t_b200 schedule evaluation is forward-only; use the fused force path")
     p = packed_schedule_tables(schedule, dev)
     if bv.ndim != 4:
         raise ValueError("block_values must have shape [batch, basis_count, block_count, max_block_m_dim].")
@@ -109,17 +130,53 @@ def evaluate_factorized_schedule_torch(block_values, schedule, *, backend="auto"
     else:
         value_dtype = bv.dtype
         coeffs = p.coeffs_r.to(value_dtype)
-    values = bv.to(value_dtype).contiguous()
+    values = bv.to(value_dtype)
+    if values.requires_grad and torch.is_grad_enabled():
+        return _ScheduleEvaluate.apply(values, p, coeffs, bool(validate))
+    return _schedule_forward(values.contiguous(), p, coeffs, validate)
+
+
+def _schedule_forward(values, p, coeffs, validate):
+    dev = values.device
     batch, basis, blocks, mdim = (int(s) for s in values.shape)
-    out = torch.empty((batch, p.comps), dtype=value_dtype, device=dev)
+    out = torch.empty((batch, p.comps), dtype=values.dtype, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev) if validate else None
     nat.check(nat.lib().y3b_factorized_schedule_evaluate(
-        nat.dtype_code(value_dtype), values.data_ptr(), batch, basis, blocks, mdim, p.off.data_ptr(),
+        nat.dtype_code(values.dtype), values.data_ptr(), batch, basis, blocks, mdim, p.off.data_ptr(),
         p.cli.data_ptr(), p.midx.data_ptr() if p.terms else 0, coeffs.data_ptr() if p.terms else 0, p.comps,
         p.terms, out.data_ptr(), nat.ptr(status), nat.stream_of(dev)), "evaluate_factorized_schedule_torch")
     if validate and int(status.item()):
         raise IndexError("evaluate_factorized_schedule_torch: schedule index out of range")
     return out
+
+
+class _ScheduleEvaluate(torch.autograd.Function):
+    """First-order autograd of the schedule evaluation: the backward is the
+    vector-Jacobian product on the GPU (``y3b_factorized_schedule_adjoint``),
+    gathered per block-value slot through the transposed table."""
+
+    @staticmethod
+    def forward(ctx, values, p, coeffs, validate):
+        values = values.contiguous()
+        ctx.save_for_backward(values, coeffs)
+        ctx.p = p
+        return _schedule_forward(values, p, coeffs, validate)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, adj):
+        values, coeffs = ctx.saved_tensors
+        p = ctx.p
+        batch, basis, blocks, mdim = (int(s) for s in values.shape)
+        slot_off, slot_term, slot_comp = p.slot_table(mdim, values.device)
+        grad = torch.empty_like(values)
+        adj = adj.to(values.dtype).contiguous()
+        nat.check(nat.lib().y3b_factorized_schedule_adjoint(
+            nat.dtype_code(values.dtype), adj.data_ptr(), values.data_ptr(), batch, basis, blocks, mdim,
+            p.midx.data_ptr() if p.terms else 0, coeffs.data_ptr() if p.terms else 0, p.comps, p.terms,
+            slot_off.data_ptr(), slot_term.data_ptr() if p.terms else 0, slot_comp.data_ptr() if p.terms else 0,
+            grad.data_ptr(), None, nat.stream_of(values.device)), "evaluate_factorized_schedule_torch backward")
+        return grad, None, None, None
 
 
 def evaluate_report(report, block_values, *, target_L, backend="auto"):

@@ -165,6 +165,56 @@ __global__ void __launch_bounds__(256) sympow_adjoint_kernel(
   }
 }
 
+// Vector-Jacobian product of the schedule evaluation (what torch autograd
+// forms through evaluate_factorized_schedule_torch, core/couplings.py:481-567):
+//   grad[b, label, j, m] = sum over (t, c) reading slot (label, j, m) of
+//                          adj[b, c] conj(coeff_t prod_{k != j} bv[b, label, k, midx[t, k]]).
+// The (term, component) pairs of every slot s = (label * blocks + j) * mdim + m
+// come from a transposed table built once per schedule on the host
+// (slot_offsets [S + 1], slot_terms / slot_components [P]), so each gradient
+// entry has one owning thread: no atomics, a fixed summation order.
+template <typename T>
+__global__ void __launch_bounds__(256) schedule_adjoint_kernel(
+    const T* __restrict__ adj, const T* __restrict__ bv, int64_t batch, int64_t basis, int64_t blocks,
+    int64_t mdim, const int64_t* __restrict__ midx, const T* __restrict__ coeffs, int64_t comps, int64_t terms,
+    const int64_t* __restrict__ slot_off, const int64_t* __restrict__ slot_term,
+    const int64_t* __restrict__ slot_comp, T* __restrict__ grad, int32_t* status) {
+  const int64_t S = basis * blocks * mdim;
+  const int64_t total = batch * S;
+  for (int64_t lin = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; lin < total;
+       lin += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = lin / S, s = lin - b * S;
+    const int64_t label = s / (blocks * mdim), j = (s / mdim) % blocks;
+    const T* row = bv + (b * basis + label) * blocks * mdim;
+    T acc = zero<T>();
+    for (int64_t p = __ldg(slot_off + s); p < __ldg(slot_off + s + 1); ++p) {
+      const int64_t t = __ldg(slot_term + p), c = __ldg(slot_comp + p);
+      if (t < 0 || t >= terms || c < 0 || c >= comps) {
+        if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        continue;
+      }
+      T v = coeffs[t];
+      const int64_t* mt = midx + t * blocks;
+      bool ok = true;
+      for (int64_t k = 0; k < blocks; ++k) {
+        if (k == j) continue;
+        const int64_t m = __ldg(mt + k);
+        if (m < 0 || m >= mdim) {
+          ok = false;
+          break;
+        }
+        v = mul(v, row[k * mdim + m]);
+      }
+      if (!ok) {
+        if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        continue;
+      }
+      acc = add(acc, mul(adj[b * comps + c], cconj(v)));
+    }
+    grad[lin] = acc;
+  }
+}
+
 }  // namespace y3b
 
 using namespace y3b;
@@ -262,6 +312,32 @@ extern "C" int y3b_symmetric_power_monomial_adjoint(int dtype, const void* outpu
         static_cast<const T*>(output_adjoint), static_cast<const T*>(input), batch, input_dim, monomial_counts,
         output_indices, static_cast<const T*>(monomial_values), term_count, output_dim,
         static_cast<T*>(input_adjoint), status);
+  });
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+extern "C" int y3b_factorized_schedule_adjoint(int dtype, const void* output_adjoint, const void* block_values,
+                                               int64_t batch, int64_t basis_count, int64_t block_count,
+                                               int64_t magnetic_dim, const int64_t* block_m_indices,
+                                               const void* coeffs, int64_t component_count, int64_t term_count,
+                                               const int64_t* slot_offsets, const int64_t* slot_terms,
+                                               const int64_t* slot_components, void* block_values_adjoint,
+                                               int32_t* status, void* stream) {
+  Y3B_CHECK_ARG(batch >= 0 && basis_count >= 0 && block_count >= 0 && magnetic_dim >= 0 && component_count >= 0 &&
+                    term_count >= 0,
+                "negative size");
+  const int64_t total = batch * basis_count * block_count * magnetic_dim;
+  if (total == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(output_adjoint && block_values && slot_offsets && block_values_adjoint &&
+                    (term_count == 0 || (coeffs && block_m_indices && slot_terms && slot_components)),
+                "null pointer argument");
+  const int threads = 256;
+  Y3B_DISPATCH(dtype, T, {
+    schedule_adjoint_kernel<T><<<grid_for(total, threads), threads, 0, as_stream(stream)>>>(
+        static_cast<const T*>(output_adjoint), static_cast<const T*>(block_values), batch, basis_count, block_count,
+        magnetic_dim, block_m_indices, static_cast<const T*>(coeffs), component_count, term_count, slot_offsets,
+        slot_terms, slot_components, static_cast<T*>(block_values_adjoint), status);
   });
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;

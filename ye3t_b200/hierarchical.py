@@ -23,8 +23,9 @@ on the GPU:
    binary CG table (hierarchical.py:478-497), ``conj(value)`` for each entry
    of a schema-v2 sparse route (hierarchical.py:437-472).
 
-The module is forward-only: the force path of ACE energies runs through the
-fused adjoint (``ye3t_b200.ace``).  ``load_scalar_ace_plans`` reads the scalar
+Both GPU operations carry first-order autograd (their vector-Jacobian
+products run on the GPU), so the module is differentiable once with respect
+to its block inputs; second derivatives are not supported.  ``load_scalar_ace_plans`` reads the scalar
 ACE LAMMPS export (ye3t/scalar_ace_export.py:52-114): its manifest, each plan
 file checked against the recorded SHA-256 and plan hash, one module per
 exported coordinate.
@@ -384,6 +385,7 @@ class YE3THierarchicalRepeatedBlockModule(torch.nn.Module):
             "composition": "cuda_block_power_then_factorized_schedule_with_folded_LR",
             "schedule_terms": self.term_count,
             "supports_autograd_vjp_hvp": False,
+            "supports_autograd_vjp": True,
         }
 
 
