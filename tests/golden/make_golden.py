@@ -173,7 +173,7 @@ def sympow_fixture():
             fx[parts[0]] = parts[1:]
     for name in ("monomial_counts", "output_offsets", "coefficient_terms", "coefficient_outputs"):
         out["fx_" + name] = np.asarray([int(v) for v in fx[name][1:]], dtype=np.int64)
-    for name in ("coefficient_values", "input", "expected_output"):
+    for name in ("coefficient_values", "input", "expected_output", "output_adjoint", "expected_input_adjoint"):
         out["fx_" + name] = np.asarray([float(v) for v in fx[name][1:]], dtype=np.float64)
     for name in ("batch_size", "input_dimension", "monomial_count", "output_dimension"):
         out["fx_" + name] = np.asarray(int(fx[name][0]))

@@ -144,6 +144,13 @@ def test_symmetric_power_shared_monomial_matches_reference(golden):
                    torch.as_tensor(t.monomial_value).to(dt))
             err = np.abs(y.cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1.0)
             assert err <= tol, (key, dt, err)
+    # the pinned fixture's input adjoint (its autograd), through the GPU backward
+    xg = _t(x).requires_grad_(True)
+    y = op(xg, _t(g["fx_monomial_counts"].reshape(-1, dim)), _t(g["fx_output_offsets"]),
+           _t(g["fx_coefficient_terms"]), _t(g["fx_coefficient_outputs"]), _t(g["fx_coefficient_values"]))
+    (grad,) = torch.autograd.grad(y, xg, _t(g["fx_output_adjoint"].reshape(y.shape)))
+    np.testing.assert_allclose(grad.cpu().numpy().reshape(-1), g["fx_expected_input_adjoint"], rtol=1e-13,
+                               atol=1e-13)
     counts = g["fx_monomial_counts"].reshape(-1, dim)
     with pytest.raises(ValueError, match="invalid monomial"):
         op(_t(x), _t(counts), _t(g["fx_output_offsets"]), _t(g["fx_coefficient_terms"] + 3),

@@ -438,15 +438,44 @@ def symmetric_power_shared_monomial_contraction(input, monomial_counts, output_o
         if int(outputs.max()) >= out_dim:
             raise ValueError("coefficient_outputs contains an invalid output")
     x2 = x.contiguous().reshape(-1, in_dim)
-    out = torch.empty((x2.shape[0], out_dim), dtype=x.dtype, device=dev)
+    if x2.requires_grad and torch.is_grad_enabled():
+        out = _SharedMonomial.apply(x2, counts, offsets, terms, outputs, values, out_dim)
+    else:
+        out = _shared_forward(x2, counts, offsets, terms, values, out_dim)
+    return out.reshape(*x.shape[:-1], out_dim)
+
+
+def _shared_forward(x2, counts, offsets, terms, values, out_dim):
+    dev, n_coef = x2.device, int(terms.numel())
+    out = torch.empty((x2.shape[0], out_dim), dtype=x2.dtype, device=dev)
     status = _status(dev)
     nat.check(nat.lib().y3b_symmetric_power_shared_monomial(
-        nat.dtype_code(x.dtype), x2.data_ptr(), x2.shape[0], in_dim, counts.data_ptr() if counts.numel() else 0,
+        nat.dtype_code(x2.dtype), x2.data_ptr(), x2.shape[0], x2.shape[1], counts.data_ptr() if counts.numel() else 0,
         int(counts.shape[0]), offsets.data_ptr(), out_dim, terms.data_ptr() if n_coef else 0,
         values.data_ptr() if n_coef else 0, n_coef, out.data_ptr(), status.data_ptr(), nat.stream_of(dev)),
         "symmetric_power_shared_monomial_contraction")
     _raise_on_status(status, "symmetric_power_shared_monomial_contraction")
-    return out.reshape(*x.shape[:-1], out_dim)
+    return out
+
+
+class _SharedMonomial(torch.autograd.Function):
+    """First-order autograd of the shared-monomial form: its backward is the
+    grouped table's vector-Jacobian product with one row per coefficient (the
+    coefficient's monomial exponents, its output index)."""
+
+    @staticmethod
+    def forward(ctx, x2, counts, offsets, terms, outputs, values, out_dim):
+        ctx.save_for_backward(x2, counts, terms, outputs, values)
+        ctx.out_dim = out_dim
+        return _shared_forward(x2, counts, offsets, terms, values, out_dim)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, adj):
+        x2, counts, terms, outputs, values = ctx.saved_tensors
+        rows = counts.index_select(0, terms).contiguous()
+        grad = _sympow_adjoint(adj.contiguous(), x2, rows, outputs.contiguous(), values, ctx.out_dim)
+        return grad, None, None, None, None, None, None
 
 
 def symmetric_power_table_contraction(input, table, *, backend="auto"):
