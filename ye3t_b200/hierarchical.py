@@ -137,9 +137,12 @@ class HierarchicalLowering:
 
     ``power_tables``: per (block, L) ``(block, L, start, D, counts, offsets,
     output_index, values)``, the descriptors landing at ``[start, start + D)``
-    of the block's row; ``schedule``: per output component (channel, tableau,
-    magnetic, in the output's flat order) its terms' coefficients and
-    descriptor index per block (``offsets``, ``m_idx [T, blocks]``, ``coeffs``).
+    of the block's row (``block_width`` = the widest row).  The schedule, per
+    output component (channel, tableau, magnetic, in the output's flat order):
+    ``offsets [components + 1]`` into its terms, ``m_idx [T, blocks]`` the
+    descriptor each term reads from each block, ``coeffs [T]``.  The plan's
+    identity and layout fields (``plan_hash``, ``channel_count``, ...) are
+    copied as the reference module exposes them.
     """
 
 
