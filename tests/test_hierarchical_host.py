@@ -96,3 +96,42 @@ def test_scalar_ace_manifest_rejects_a_changed_plan(golden, tmp_path):
     (tmp_path / "manifest.json").write_text(json.dumps(manifest), encoding="utf-8")
     with pytest.raises(ValueError, match="manifest"):
         H.load_scalar_ace_plans(os.fspath(tmp_path / "manifest.json"))
+
+
+def test_block_power_lowering_checks_and_merges(golden):
+    """The grouped lowering merges terms with equal exponent rows, drops zero rows and rejects
+    indices outside the plan (symmetric_power.py:740-868)."""
+    g = golden("hierarchical")
+    plan = json.loads(_text(g, "r4"))["instructions"][0]["metadata"]["block_power_plans"][1]["plan"]
+    counts, offsets, index, values = H.lower_block_power_plan(plan)
+    assert offsets[0] == 0 and offsets[-1] == counts.shape[0] == index.shape[0] == values.shape[0]
+    assert np.all(np.diff(offsets) >= 0) and np.all(np.abs(values) > 1e-12)
+    for d in range(offsets.shape[0] - 1):
+        rows = [tuple(r) for r in counts[offsets[d]:offsets[d + 1]]]
+        assert rows == sorted(set(rows))  # merged and ordered per descriptor
+        assert np.all(index[offsets[d]:offsets[d + 1]] == d)
+    doubled = copy.deepcopy(plan)
+    for entry in doubled["entries"]:
+        entry["component_terms"] = entry["component_terms"] * 2
+    c2, o2, i2, v2 = H.lower_block_power_plan(doubled)
+    assert np.array_equal(c2, counts) and np.allclose(v2, 2 * values)
+    bad = copy.deepcopy(plan)
+    bad["entries"][0]["descriptor_index"] = int(plan["descriptor_count"])
+    with pytest.raises(ValueError, match="descriptor index"):
+        H.lower_block_power_plan(bad)
+    bad = copy.deepcopy(plan)
+    bad["entries"][0]["channel_indices"] = [int(plan["channel_count"])] * len(bad["entries"][0]["channel_indices"])
+    with pytest.raises(ValueError, match="channel index"):
+        H.lower_block_power_plan(bad)
+
+
+def test_scalar_ace_manifest_rejects_a_changed_plan_hash(golden, tmp_path):
+    g = golden("hierarchical")
+    manifest = json.loads(str(g["lammps_manifest"]))
+    for case in manifest["cases"]:
+        name = case["execution_plan"]["file"]
+        (tmp_path / name).write_text(str(g["lammps_file_" + name]), encoding="utf-8")
+    manifest["cases"][0]["execution_plan"]["plan_hash"] = "0" * 16
+    (tmp_path / "manifest.json").write_text(json.dumps(manifest), encoding="utf-8")
+    with pytest.raises(ValueError, match="plan hash"):
+        H.load_scalar_ace_plans(os.fspath(tmp_path / "manifest.json"))
