@@ -336,8 +336,10 @@ def ace_fixture():
     print("ace_small.npz N", N, "E", E, "B3", B3.shape, "B4", B4.shape, "energy3", energy3)
 
 
-def forces_fixture():
-    """Energy and forces of the 96-atom system through the reference's torch ops with autograd.
+def _reference_energy_forces(words, weights_of):
+    """Total energy and forces of the 96-atom system of ``ace_small.npz`` through the reference's
+    differentiable torch ops, for a word list; ``weights_of(F)`` gives the per-species readout
+    ``[3, F]`` over the words' L=0 features in order.
 
     Displacements are the minimum image of the CSR pairs with the image shift
     held fixed; the radial table (``execution_plan.py:6862`` reference
@@ -366,9 +368,8 @@ def forces_fixture():
     edge = (p[:, None, None] * Rv[:, 1:, None]).to(torch.complex128) * Yv[:, None, :]
     A = density_accumulate(edge.reshape(E, -1), centers, N, backend="reference").reshape(N, nmax, -1)
     multiplets = {l: A[:, :, l * l:(l + 1) * (l + 1)] for l in range(lmax + 1)}
-    b3 = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu3_L0.npz"))
     feats = []
-    for word in b3.words:
+    for word in words:
         rep = compile_ace_factorized_schedules_by_L(content=tuple(n for _, n in word),
                                                     input_Ls=tuple(l for l, _ in word))
         sched = rep.schedules_by_L[0]
@@ -395,12 +396,34 @@ def forces_fixture():
         bv = torch.stack(rows, dim=-3)
         feats.append(rep.evaluate(bv, target_L=0, backend="torch"))
     B = torch.cat(feats, dim=1)
-    w = torch.tensor(g["w3"])[torch.tensor(g["species"], dtype=torch.long)]
+    w_all = weights_of(B.shape[1])
+    w = torch.tensor(w_all)[torch.tensor(g["species"], dtype=torch.long)]
     energy = (w * B.real).sum()
     (grad,) = torch.autograd.grad(energy, pos)
-    np.savez_compressed(os.path.join(HERE, "forces_small.npz"), energy=np.asarray(float(energy)),
-                        forces=(-grad).numpy())
-    print("forces_small.npz energy", float(energy), "|F| max", float(grad.abs().max()))
+    return float(energy), (-grad).numpy(), w_all
+
+
+def forces_fixture():
+    """Energy and forces of the 96-atom system (nu <= 3, all 2,344 features) by reference autograd."""
+    g = dict(np.load(os.path.join(HERE, "ace_small.npz")))
+    b3 = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu3_L0.npz"))
+    energy, forces, _ = _reference_energy_forces(b3.words, lambda F: g["w3"])
+    np.savez_compressed(os.path.join(HERE, "forces_small.npz"), energy=np.asarray(energy), forces=forces)
+    print("forces_small.npz energy", energy, "|F| max", float(np.abs(forces).max()))
+
+
+def forces_nu4_fixture():
+    """Energy and forces of the 96-atom system over every 23rd word of the nu <= 4 set (the C5
+    bundle; 1,102 words with four-block words of every adjoint class) by reference autograd, with a
+    seeded readout over those words' features (every other feature of the bundle has weight 0)."""
+    b4 = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu4_L0.npz"))
+    sample = np.arange(0, b4.word_count, 23, dtype=np.int64)
+    rng = np.random.default_rng(44)
+    energy, forces, w = _reference_energy_forces([b4.words[int(k)] for k in sample],
+                                                 lambda F: rng.normal(size=(3, F)) / np.sqrt(F))
+    np.savez_compressed(os.path.join(HERE, "forces_nu4.npz"), energy=np.asarray(energy), forces=forces,
+                        words=sample, weights=w)
+    print("forces_nu4.npz words", sample.shape[0], "energy", energy, "|F| max", float(np.abs(forces).max()))
 
 
 def mixing_fixture():
@@ -704,7 +727,7 @@ def hierarchical_grads_fixture():
 if __name__ == "__main__":
     which = sys.argv[1:] or ["schedules", "quickstart", "sympow", "edge", "ace", "forces", "mixing", "real",
                              "hierarchical", "edge_products", "adjoints", "schedule_grads",
-                             "hierarchical_grads"]
+                             "hierarchical_grads", "forces_nu4"]
     if "schedules" in which:
         schedules_fixture()
     if "quickstart" in which:
@@ -731,3 +754,5 @@ if __name__ == "__main__":
         schedule_grads_fixture()
     if "hierarchical_grads" in which:
         hierarchical_grads_fixture()
+    if "forces_nu4" in which:
+        forces_nu4_fixture()

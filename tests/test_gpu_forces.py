@@ -37,6 +37,30 @@ def test_forces_match_reference_autograd(golden):
     assert err <= 1e-10, err
 
 
+def test_forces_nu4_bundle_match_reference_autograd(golden):
+    """The C5 bundle (nu <= 4, all four adjoint classes) with a readout on every 23rd word
+    (1,102 words; every other feature weighted 0): total energy and forces against torch
+    autograd through the reference ops on the 96-atom system."""
+    small = golden("ace_small")
+    ref = golden("forces_nu4")
+    bundle = _bundle("ace_n8_l3_nu4_L0")
+    offsets = bundle.feature_offsets()
+    W = np.zeros((3, bundle.feature_count))
+    col = 0
+    for w in ref["words"]:
+        lo, hi = int(offsets[w]), int(offsets[w + 1])
+        W[:, lo:hi] = ref["weights"][:, col:col + hi - lo]
+        col += hi - lo
+    assert col == ref["weights"].shape[1]
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", W)
+    pos = torch.as_tensor(small["pos"], device=DEV)
+    sp = torch.as_tensor(small["species"], device=DEV)
+    E, F = ev.energy_forces(pos, sp, float(small["box"]))
+    assert abs(float(E) - float(ref["energy"])) <= 1e-11 * abs(float(ref["energy"]))
+    err = np.abs(F.cpu().numpy() - ref["forces"]).max() / np.abs(ref["forces"]).max()
+    assert err <= 1e-10, err
+
+
 def test_energy_grad_energy_equals_forward_and_gradient_is_exact(golden):
     small = golden("ace_small")
     rng = np.random.default_rng(4)
