@@ -58,3 +58,46 @@ def test_runtime_rejects_reference_backend_and_cpu():
         runtime.density_accumulate(torch.zeros(2, 2), torch.zeros(2, dtype=torch.int64), 1)
     caps = runtime.native_execution_plan_capabilities()
     assert caps["loaded"] and caps["cpu"] is False
+
+
+def test_torch_ops_registered_with_fake_kernels():
+    """torch.ops.ye3t_b200.*: registered at import, with fake kernels that give the output
+    shapes and dtypes without running anything (what torch.compile tracing uses)."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import ye3t_b200.torch_ops  # noqa: F401
+    ops = torch.ops.ye3t_b200
+    with FakeTensorMode():
+        dev = "cuda"
+        ev = torch.empty(11, 16, device=dev, dtype=torch.complex128)
+        c = torch.empty(11, device=dev, dtype=torch.int64)
+        assert ops.density_accumulate(ev, c, 5).shape == (5, 16)
+        assert ops.density_accumulate_adjoint(torch.empty(5, 16, device=dev), c).shape == (11, 16)
+        r = torch.empty(9, device=dev, dtype=torch.float64)
+        v, d = ops.cheb_exp_cos_radial_table_with_derivative(r, r, r, 8)
+        assert v.shape == d.shape == (9, 9)
+        y, dy = ops.spherical_harmonics_table_with_derivative(torch.empty(9, 3, device=dev, dtype=torch.float64),
+                                                             3, False, 1e-12)
+        assert y.shape == (9, 16) and dy.shape == (9, 16, 3) and y.dtype == torch.complex128
+        x = torch.empty(4, 7, 3, device=dev, dtype=torch.complex128)
+        counts = torch.empty(6, 3, device=dev, dtype=torch.int64)
+        offs = torch.empty(4, device=dev, dtype=torch.int64)
+        idx = torch.empty(6, device=dev, dtype=torch.int64)
+        vals = torch.empty(6, device=dev, dtype=torch.complex128)
+        assert ops.symmetric_power_monomial(x, counts, offs, idx, vals).shape == (4, 7, 3)
+        assert ops.symmetric_power_monomial_adjoint(torch.empty(4, 7, 3, device=dev, dtype=torch.complex128), x,
+                                                    counts, offs, idx, vals).shape == x.shape
+        assert ops.symmetric_power_shared_monomial(x, counts, offs, idx, idx, vals).shape == (4, 7, 3)
+        bv = torch.empty(5, 2, 3, 7, device=dev, dtype=torch.complex128)
+        out = ops.factorized_schedule(bv, torch.empty(13, device=dev, dtype=torch.int64),
+                                      torch.empty(12, device=dev, dtype=torch.int64),
+                                      torch.empty(20, 3, device=dev, dtype=torch.int64),
+                                      torch.empty(20, device=dev, dtype=torch.complex128))
+        assert out.shape == (5, 12)
+        a, b = ops.scheduled_radial_angular_channels_with_derivative(
+            torch.empty(9, 4, device=dev), torch.empty(9, 4, device=dev), torch.empty(9, 16, device=dev),
+            torch.empty(9, 16, 3, device=dev), torch.empty(9, 3, device=dev),
+            torch.empty(9, device=dev, dtype=torch.int64), torch.empty(6, device=dev, dtype=torch.int64),
+            torch.empty(6, device=dev, dtype=torch.int64), torch.empty(6, device=dev, dtype=torch.int64),
+            torch.empty(6, device=dev))
+        assert a.shape == (9, 6) and b.shape == (9, 6, 3)
