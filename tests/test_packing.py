@@ -5,7 +5,6 @@ import os
 
 import numpy as np
 import pytest
-import torch
 
 from oracle import oracle
 from ye3t_b200.packing import pack_bundle
@@ -121,8 +120,7 @@ def test_adjoint_groups_cover_items_once(stem):
     each phase into equal per-warp runs; the four-block run
     classes hold no phases, split into equal per-warp runs whose costs differ
     by at most one item per shape."""
-    from ye3t_b200.packing import (GRAD_CLASSES, GRAD_RUN_CLASSES, GRAD_RUN_WARPS, GRAD_SLOT_RUN_CLASS,
-                                   grad_class, item_grad_flops_per_atom)
+    from ye3t_b200.packing import GRAD_CLASSES, GRAD_RUN_CLASSES, GRAD_RUN_WARPS, grad_class, item_grad_flops_per_atom
     b = _bundle(stem)
     pb = pack_bundle(b, "cpu")
     items = pb.arrays["items"].numpy()

@@ -8,7 +8,6 @@ y3b_density_accumulate, including on a second call that finds the previous
 call's data still in the shared scratch array.  This file is collected last.
 """
 
-import ctypes
 
 import numpy as np
 import pytest
