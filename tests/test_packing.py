@@ -187,3 +187,26 @@ def test_schedule_adjoint_slot_table(golden):
             got = list(zip(terms[off[s]:off[s + 1]].tolist(), comps[off[s]:off[s + 1]].tolist()))
             assert got == expect.get(s, []), (i, s)
         i += 1
+
+
+@pytest.mark.parametrize("stem", sorted(f[:-4] for f in os.listdir(os.path.join(REPO, "ye3t_b200", "bundles"))
+                                        if f.endswith(".npz")))
+def test_adjoint_classes_respect_kernel_bounds(stem):
+    """Every item of every shipped bundle sits in a class whose kernel path holds it: the run
+    classes (per-lane staging windows of 7 entries, A entries only) and class 1 (last block
+    staged in 14 entries, register block 5 or 7); everything else goes to class 0, whose general
+    path has no staging bound."""
+    from ye3t_b200.packing import GRAD_RUN_BLOCK, GRAD_STAGE, grad_class
+    b = _bundle(stem)
+    items = pack_bundle(b, "cpu").arrays["items"].numpy()
+    na = b.nmax * (b.lmax + 1) ** 2
+    for row in items:
+        sel, d0, d1, dl = int(row[0]), int(row[1]), int(row[2]), int(row[3])
+        B, ds = (sel // 2) // 7 + 1, 2 * ((sel // 2) % 7) + 1
+        cls = grad_class(row, na)
+        if cls in (2, 3):
+            assert B == 4 and max(d0, d1, dl) <= GRAD_RUN_BLOCK
+            assert ds in ((3, 5) if cls == 2 else (7,))
+            assert all(int(row[8 + k]) + dim <= na for k, dim in enumerate((d0, d1, ds, dl)))
+        elif cls == 1:
+            assert B == 3 and ds in (5, 7) and dl <= GRAD_STAGE
