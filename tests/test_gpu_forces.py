@@ -171,3 +171,34 @@ def test_energy_grad_single_slot_pool(golden, stem):
     em = ev.energy_from_density(A - dA, sp).sum().item()
     lin = (G * dA).real.sum().item()
     assert abs((ep - em) / 2 - lin) <= 1e-6 * abs(lin) + 1e-12
+
+
+def test_energy_grad_flags_a_run_item_outside_its_bounds(golden):
+    """A four-block item whose tables claim a last block longer than the run path's
+    7-entry staging window is skipped before any staging access and reported with
+    Y3B_STATUS_TABLE; with the table restored the flag stays clear."""
+    from ye3t_b200 import _native as nat
+    from ye3t_b200.packing import GRAD_CLASSES
+    small = golden("ace_small")
+    rng = np.random.default_rng(9)
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    items, groups = ev.packed.arrays["items"], ev.packed.arrays["groups"]
+    P = ev.packed.arrays["phases"].shape[0]
+    off = ev.packed.arrays["group_offsets"].cpu().numpy().reshape(GRAD_CLASSES, P + 1)
+    pairs = groups[int(off[3, 0]):int(off[3, 1])].cpu().numpy()
+    i = int(pairs[pairs[:, 0] >= 0][0, 0])
+    N = 64
+    A = torch.complex(torch.randn(N, 8, 16, dtype=torch.float64, device=DEV),
+                      torch.randn(N, 8, 16, dtype=torch.float64, device=DEV)) * 0.3
+    sp = torch.as_tensor(rng.integers(0, 3, size=N), device=DEV, dtype=torch.int32)
+    saved = int(items[i, 3])
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    try:
+        items[i, 3] = 9
+        ev.energy_grad(A, sp, status=status)
+        assert int(status.item()) & nat.STATUS_TABLE
+    finally:
+        items[i, 3] = saved
+    status.zero_()
+    ev.energy_grad(A, sp, status=status)
+    assert int(status.item()) == 0
