@@ -242,8 +242,10 @@ def run_b200(args):
         ("neighbors", "density", "energy")
     timers = {k: [] for k in stages}
     # our kernels per step: 6 neighbour-count, 1 fill, density, then the
-    # B-basis energy, or the B-basis adjoint + edge gradients + force gather/scatter
-    launches_per_step = 8 + (3 if forces else 1)
+    # B-basis energy, or the B-basis adjoint (one launch per item class) + edge
+    # gradients + force gather/scatter
+    from ye3t_b200.packing import GRAD_CLASSES
+    launches_per_step = 8 + (GRAD_CLASSES + 2 if forces else 1)
 
     def step(record):
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] if record else None
@@ -583,7 +585,7 @@ def run_channels(args):
         "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
                 "d2h_bytes_per_step": 8,
                 "note": "features stay on the device (sharded descriptor); a checksum is read back"},
-        "gpu_launches": (9 + len(evs)) * args.steps,
+        "gpu_launches": (8 + len(evs)) * args.steps,  # 7 neighbour-list, mixed density, one per bundle
         "roofline": roof,
         "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
         "checksum": float(check.item()),
