@@ -101,3 +101,42 @@ def test_torch_ops_registered_with_fake_kernels():
             torch.empty(6, device=dev, dtype=torch.int64), torch.empty(6, device=dev, dtype=torch.int64),
             torch.empty(6, device=dev))
         assert a.shape == (9, 6) and b.shape == (9, 6, 3)
+
+
+def test_tables_struct_layout_matches_header(tmp_path):
+    """The ctypes mirror of y3b_ace_tables (passed by value to every fused kernel) has the
+    C struct's size and field offsets, read from include/ye3t_b200.h by a small C program."""
+    import ctypes
+    import shutil
+    import subprocess
+    from ye3t_b200 import _native
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    fields = [name for name, _ in _native.AceTables._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"ye3t_b200.h\"\nint main(void) {\n"
+                   "  printf(\"%zu\\n\", sizeof(y3b_ace_tables));\n"
+                   + "".join(f"  printf(\"%zu\\n\", offsetof(y3b_ace_tables, {f}));\n" for f in fields)
+                   + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    include = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run([gcc, "-I", include, str(src), "-o", str(exe)], check=True)
+    out = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(_native.AceTables)
+    assert out[1:] == [getattr(_native.AceTables, f).offset for f in fields]
+
+
+def test_ctypes_signatures_match_header_parameter_counts():
+    """Every entry point's ctypes argument list has as many entries as its declaration in
+    include/ye3t_b200.h has parameters (a short or long list would pass arguments misaligned)."""
+    from ye3t_b200 import _native
+    src = open(os.path.join(REPO, "include", "ye3t_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    counts = {}
+    for m in re.finditer(r"\b(y3b_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", src):
+        params = m.group(2).strip()
+        counts[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    assert counts and set(counts) == set(_native._SIGS)
+    for name, (_, args) in _native._SIGS.items():
+        assert len(args) == counts[name], (name, len(args), counts[name])
