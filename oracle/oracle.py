@@ -376,3 +376,49 @@ def ace_density_mixed(disp, row_off, nbr, species, mixing, nmax, lmax, cutoff, l
     lib().yo_ace_density_mixed(_p(disp), _p(off), _p(nb), _p(sp), _p(W), I64(N), I64(S), I64(C), I64(nmax),
                                I64(lmax), ctypes.c_double(cutoff), ctypes.c_double(lam), _p(A))
     return A
+
+
+# -- edge products (ye3t/runtime/execution_plan.py:7036-7220), numpy ------------------------
+def scheduled_radial_angular_channels(rv, rd, av, ad, directions, edge_types, ch_rad, ch_ang, ch_type, ch_scale):
+    """``_scheduled_radial_angular_channels_reference`` (execution_plan.py:7036-7080):
+    values [E, C] and derivatives [E, C, 3], each elementwise operation rounded on its own."""
+    R, dR = rv[:, ch_rad], rd[:, ch_rad]
+    Y, dY = av[:, ch_ang], ad[:, ch_ang]
+    active = ((ch_type < 0)[None, :] | (edge_types[:, None] == ch_type[None, :])).astype(rv.dtype)
+    scale = active * ch_scale[None, :]
+    values = R * Y * scale
+    derivatives = scale[..., None] * (dR[..., None] * directions[:, None, :] * Y[..., None] + R[..., None] * dY)
+    return values, derivatives
+
+
+def _plain_terms(rv, rd, av, ad, pref, directions, groups):
+    R, dR, P = rv[groups], rd[groups], pref[groups]
+    values = P * R * av
+    derivatives = P[..., None] * (dR[..., None] * directions[None, :, :] * av[..., None] + R[..., None] * ad)
+    return R, values, derivatives
+
+
+def plain_site_basis_product(rv, rd, av, ad, pref, pc, pn, directions, groups, channels, channel_count):
+    """``_plain_site_basis_product_reference`` (execution_plan.py:7082-7155): edge values and
+    derivatives per channel, and the two prefactor-derivative channels."""
+    E = rv.shape[1]
+    R, tv, td = _plain_terms(rv, rd, av, ad, pref, directions, groups)
+    common = R * av
+    out = [np.zeros((E, channel_count), dtype=rv.dtype), np.zeros((E, channel_count, 3), dtype=rv.dtype),
+           np.zeros((E, channel_count), dtype=rv.dtype), np.zeros((E, channel_count), dtype=rv.dtype)]
+    out[0][:, channels] = tv.T
+    out[1][:, channels] = np.transpose(td, (1, 0, 2))
+    out[2][:, channels] = (pc[groups] * common).T
+    out[3][:, channels] = (pn[groups] * common).T
+    return tuple(out)
+
+
+def plain_site_basis_product_adjoint(rv, rd, av, ad, pref, pc, pn, directions, w, dw, groups, channels, adj):
+    """``_plain_site_basis_product_adjoint_reference`` (execution_plan.py:7158-7220): the edge
+    position adjoint [E, 3] and the two charge adjoints [E]."""
+    R, tv, td = _plain_terms(rv, rd, av, ad, pref, directions, groups)
+    a = adj[:, channels].T
+    weighted = td * w[None, :, None] + tv[..., None] * dw[None, :, :]
+    position = (a[..., None] * weighted).sum(axis=0)
+    common = R * av * w[None, :]
+    return position, (a * pc[groups] * common).sum(axis=0), (a * pn[groups] * common).sum(axis=0)

@@ -218,3 +218,61 @@ def test_oracle_real_tesseral_schedules(golden):
         p = f"r{k}_"
         y = oracle.schedule_evaluate(g[p + "bv"], g[p + "off"], g[p + "cli"], g[p + "idx"], g[p + "co"])
         np.testing.assert_allclose(y, g[p + "y"], rtol=1e-13, atol=1e-13)
+
+
+S_ARGS = ("radial_values", "radial_derivatives", "angular_values", "angular_derivatives", "radial_directions",
+          "edge_types", "channel_radial_indices", "channel_angular_indices", "channel_types", "channel_scales")
+P_ARGS = ("radial_values", "radial_derivatives", "angular_values", "angular_derivatives", "prefactors",
+          "prefactor_derivatives_center", "prefactor_derivatives_neighbor", "radial_directions", "term_groups",
+          "term_channels")
+
+
+def _rel(a, ref):
+    return np.abs(np.asarray(a) - ref).max() / max(np.abs(ref).max(), 1.0)
+
+
+def test_oracle_edge_products_match_reference(golden):
+    """Scheduled radial-angular channels and the plain site-basis product (and its adjoint)
+    restated in numpy, against the reference's compositions (execution_plan.py:7036-7220)."""
+    g = golden("edge_products")
+    for tag in ("f64", "f32"):
+        v, d = oracle.scheduled_radial_angular_channels(*(g[f"s_{tag}_{k}"] for k in S_ARGS))
+        assert np.array_equal(v, g[f"s_{tag}_values"]) and np.array_equal(d, g[f"s_{tag}_derivatives"])
+    for tag, tol in (("f64", 1e-14), ("c128", 1e-13), ("c64", 1e-5)):
+        outs = oracle.plain_site_basis_product(*(g[f"p_{tag}_{k}"] for k in P_ARGS), int(g[f"p_{tag}_channel_count"]))
+        for name, y in zip(("edge_values", "edge_derivatives", "charge_center", "charge_neighbor"), outs):
+            assert _rel(y, g[f"p_{tag}_{name}"]) <= tol, (tag, name)
+    ga = golden("adjoints")
+    for tag in ("f64", "c128"):
+        outs = oracle.plain_site_basis_product_adjoint(*(ga[f"pa_{tag}_{k}"] for k in P_ARGS[:8]),
+                                                       ga[f"pa_{tag}_edge_weights"],
+                                                       ga[f"pa_{tag}_edge_weight_derivatives"],
+                                                       ga[f"pa_{tag}_term_groups"], ga[f"pa_{tag}_term_channels"],
+                                                       ga[f"pa_{tag}_edge_adjoint"])
+        for name, y in zip(("position", "charge_center", "charge_neighbor"), outs):
+            assert _rel(y, ga[f"pa_{tag}_{name}"]) <= 1e-13, (tag, name)
+
+
+def test_oracle_adjoints_match_reference_autograd(golden):
+    """The oracle's holomorphic adjoints of the schedule evaluation and of the grouped symmetric
+    power, against torch autograd through the reference (which returns conj(J)^T adj, i.e.
+    conj(holomorphic adjoint of conj(adj)))."""
+    g, gg = golden("schedules"), golden("schedule_grads")
+    for i in range(8):
+        rec = _record(g, f"s{i}_")
+        for tag in ("c", "r"):
+            p = f"s{i}_{tag}_"
+            got = np.conj(oracle.schedule_adjoint(gg[p + "bv"], rec, np.conj(gg[p + "adj"])))
+            if tag == "r":
+                got = got.real
+            assert _rel(got, gg[p + "grad"]) <= 1e-13, (i, tag)
+    ga = golden("adjoints")
+    b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu4_L0.npz"))
+    j = 0
+    while f"sp{j}_key" in ga:
+        t = b.sym_tables[tuple(int(v) for v in ga[f"sp{j}_key"])]
+        got = np.conj(oracle.symmetric_power_monomial_adjoint(ga[f"sp{j}_x"], t.monomial_counts, t.output_offsets,
+                                                              t.monomial_value, np.conj(ga[f"sp{j}_adj"])))
+        assert _rel(got, ga[f"sp{j}_grad"]) <= 1e-13, j
+        j += 1
+    assert j == 23
