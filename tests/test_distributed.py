@@ -1,8 +1,9 @@
-"""Atom-block partition and the energy reduction, as 2 gloo ranks on CPU.
+"""Atom-block partition and the energy and force reductions, as 2 gloo ranks on CPU.
 
 Each rank evaluates its centre block with the CPU oracle (the GPU kernels are
 covered by the gpu tests); the summed energy must equal the single-process
-energy, and the blocks must tile the system."""
+energy, the summed partial forces must equal the reference's forces, and the
+blocks must tile the system."""
 
 import os
 import socket
@@ -65,3 +66,52 @@ def test_two_rank_energy_equals_single_process(tmp_path, golden):
     total = float(np.load(out)[0])
     ref = float(golden("ace_small")["energy3"])
     assert abs(total - ref) <= 1e-12 * abs(ref)
+
+
+def _rank_forces(rank, world, port, out_path):
+    """One rank of the force decomposition: ``G = dE/dA`` of its centre block, the
+    edge gradients of its CSR rows, and a full-length partial force array (each
+    edge i->j adds ``g`` to atom i and subtracts it from atom j, both global
+    indices); the ranks then sum the partial arrays."""
+    import sys
+    sys.path.insert(0, REPO)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    from oracle import oracle
+    from ye3t_b200.distributed import atom_block, init_from_env, sum_over_ranks
+    from ye3t_b200.schedules import ACEBundle
+    import torch.distributed as dist
+    r, w = init_from_env("gloo", 60.0)
+    g = dict(np.load(os.path.join(REPO, "tests", "golden", "ace_small.npz")))
+    b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", "ace_n8_l3_nu3_L0.npz"))
+    N = g["pos"].shape[0]
+    rc, lam = float(g["rc"]), float(g["lam"])
+    lo, hi = atom_block(r, w, N)
+    A = oracle.ace_density(g["disp"], g["row_off"], g["nbr"], g["species"], g["prefactor"], 8, 3, rc, lam)
+    e, G = oracle.bundle_energy_grad(b, A[lo:hi], g["species"][lo:hi], g["w3"], threads=2)
+    off = g["row_off"].astype(np.int64)
+    e0, e1 = int(off[lo]), int(off[hi])
+    rows = off[lo:hi + 1] - e0
+    nbr = g["nbr"][e0:e1]
+    ge = oracle.ace_edge_grad(g["disp"][e0:e1], rows, nbr, g["species"], g["prefactor"], 8, 3, rc, lam, G)
+    centre = np.repeat(np.arange(lo, hi), np.diff(rows))
+    F = np.zeros((N, 3))
+    np.add.at(F, centre, ge)
+    np.add.at(F, nbr.astype(np.int64), -ge)
+    total = sum_over_ranks(torch.tensor(np.concatenate([[e.sum()], F.reshape(-1)]), dtype=torch.float64))
+    if r == 0:
+        np.save(out_path, total.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_rank_partial_forces_sum_to_reference(tmp_path, golden, world):
+    out = str(tmp_path / "forces.npy")
+    mp.start_processes(_rank_forces, args=(world, _free_port(), out), nprocs=world, join=True,
+                       start_method="spawn")
+    total = np.load(out)
+    ref = golden("forces_small")
+    F_ref = np.asarray(ref["forces"])
+    assert abs(total[0] - float(ref["energy"])) <= 1e-12 * abs(float(ref["energy"]))
+    F = total[1:].reshape(-1, 3)
+    assert np.abs(F - F_ref).max() <= 1e-10 * max(1.0, np.abs(F_ref).max())
