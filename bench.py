@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--atoms", type=int, default=1 << 20)
     ap.add_argument("--bundle", default=BUNDLE)
     ap.add_argument("--cpu-sample", type=int, default=None,
-                    help="atoms in the CPU baseline sample (default 256 with forces, 1024 energy only)")
+                    help="atoms in the CPU baseline sample (default 512 with forces, 1024 energy only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="c5", choices=["c5", "c3", "c3f32", "c4"],
                     help="c5 (default): the headline 2^20-atom energy + forces step; c3/c3f32/c4: the "
@@ -613,7 +613,7 @@ def main():
         run_channels(args)
         return
     if args.cpu_sample is None:
-        args.cpu_sample = 1024 if args.energy_only else 256
+        args.cpu_sample = 1024 if args.energy_only else 512
     if args.impl == "reference":
         run_reference(args)
     else:

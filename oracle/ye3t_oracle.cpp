@@ -16,8 +16,11 @@
 #include <algorithm>
 #include <cmath>
 #include <complex>
+#include <condition_variable>
 #include <cstdint>
 #include <cstring>
+#include <functional>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -27,18 +30,75 @@ using c128 = std::complex<double>;
 
 namespace {
 
-// Runs body(begin, end) over [0, n) split into `threads` contiguous chunks.
+// Persistent worker pool behind parallel_chunks.  The reference's CPU
+// evaluator runs on at::parallel_for, whose threads live for the whole
+// process; starting threads per call instead would cost more than the work of
+// a small batch.  Workers sleep on a condition variable between calls; one
+// parallel call runs at a time (callers are serialised); the pool is never
+// destroyed, so process exit does not wait on it.
+class ChunkPool {
+ public:
+  static ChunkPool& get() {
+    static ChunkPool* pool = new ChunkPool();
+    return *pool;
+  }
+
+  // Runs job(0) .. job(T - 1), job(0) on the calling thread.
+  void run(int T, const std::function<void(int)>& job) {
+    std::lock_guard<std::mutex> call(call_mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    while (static_cast<int>(workers_.size()) < T - 1) {
+      const int index = static_cast<int>(workers_.size()) + 1;
+      const std::uint64_t seen = gen_;
+      workers_.emplace_back([this, index, seen] { loop(index, seen); });
+    }
+    job_ = &job;
+    participants_ = T - 1;
+    remaining_ = T - 1;
+    ++gen_;
+    lk.unlock();
+    wake_.notify_all();
+    job(0);
+    lk.lock();
+    done_.wait(lk, [&] { return remaining_ == 0; });
+    job_ = nullptr;
+  }
+
+ private:
+  void loop(int index, std::uint64_t seen) {
+    std::unique_lock<std::mutex> lk(mu_);
+    for (;;) {
+      wake_.wait(lk, [&] { return gen_ != seen; });
+      seen = gen_;
+      if (index > participants_) continue;
+      const std::function<void(int)>* job = job_;
+      lk.unlock();
+      (*job)(index);
+      lk.lock();
+      if (--remaining_ == 0) done_.notify_one();
+    }
+  }
+
+  std::mutex call_mu_, mu_;
+  std::condition_variable wake_, done_;
+  std::vector<std::thread> workers_;
+  const std::function<void(int)>* job_ = nullptr;
+  std::uint64_t gen_ = 0;
+  int participants_ = 0, remaining_ = 0;
+};
+
+// Runs body(begin, end) over [0, n) split into `threads` contiguous chunks
+// (one chunk per thread, as at::parallel_for with grain 0).
 template <typename F>
 void parallel_chunks(std::int64_t n, int threads, F body) {
   if (threads <= 1 || n < 2) { body(std::int64_t(0), n); return; }
-  std::vector<std::thread> pool;
-  const std::int64_t step = (n + threads - 1) / threads;
-  for (int t = 0; t < threads; ++t) {
+  const int T = static_cast<int>(std::min<std::int64_t>(threads, n));
+  const std::int64_t step = (n + T - 1) / T;
+  const std::function<void(int)> job = [&](int t) {
     const std::int64_t b = t * step, e = std::min<std::int64_t>(n, b + step);
-    if (b >= e) break;
-    pool.emplace_back([=] { body(b, e); });
-  }
-  for (auto& th : pool) th.join();
+    if (b < e) body(b, e);
+  };
+  ChunkPool::get().run(T, job);
 }
 
 // ---------------------------------------------------------------------------
