@@ -1,0 +1,94 @@
+"""Numpy restatement of the recoupled evaluation (test helper).
+
+Per atom: segment components, contractions, features; and the holomorphic
+``dE/dA`` of ``e = Re(sum_d k[z, d] T_d)`` by the chain rule through the
+contractions and the pair couplings.  The order of operations is the one a
+device kernel over ``RecoupledPlan`` follows (segments by L, contractions by
+L then first segment), so a kernel can be checked against it term by term."""
+
+import numpy as np
+
+from ye3t_b200.recoupling import SEG_CHANNEL, SEG_PAIR, SEG_UNIT, cg_table
+
+
+def _chan(plan, A, c):
+    l, n = plan.channel(int(c))
+    return A[:, n - 1, l * l:(l + 1) * (l + 1)]
+
+
+def segments(plan, A):
+    """``I [N, component_count]``."""
+    N = A.shape[0]
+    I = np.zeros((N, plan.component_count), dtype=np.complex128)
+    for s in range(plan.segment_count):
+        o0, o1 = int(plan.seg_offset[s]), int(plan.seg_offset[s + 1])
+        kind, L = int(plan.seg_kind[s]), int(plan.seg_L[s])
+        if kind == SEG_UNIT:
+            I[:, o0] = 1.0
+        elif kind == SEG_CHANNEL:
+            I[:, o0:o1] = _chan(plan, A, plan.seg_a[s])
+        else:
+            a, b = int(plan.seg_a[s]), int(plan.seg_b[s])
+            la, lb = plan.channel(a)[0], plan.channel(b)[0]
+            idx, val = cg_table(la, lb, L)
+            xa, xb = _chan(plan, A, a), _chan(plan, A, b)
+            np.add.at(I, (slice(None), o0 + idx[:, 2]), val * xa[:, idx[:, 0]] * xb[:, idx[:, 1]])
+    return I
+
+
+def contractions(plan, I):
+    """``T [N, dot_count]``."""
+    T = np.zeros((I.shape[0], plan.dot_count), dtype=np.complex128)
+    for L in np.unique(plan.dot_L):
+        sel = np.nonzero(plan.dot_L == L)[0]
+        M = np.arange(-L, L + 1)
+        oa = plan.seg_offset[plan.dot_a[sel]][:, None] + (M + L)[None, :]
+        ob = plan.seg_offset[plan.dot_b[sel]][:, None] + (L - M)[None, :]
+        T[:, sel] = ((-1.0) ** M * I[:, oa] * I[:, ob]).sum(axis=2)
+    return T
+
+
+def features(plan, A):
+    T = contractions(plan, segments(plan, A))
+    dot_of = np.repeat(np.arange(plan.dot_count), np.diff(plan.dot_feat_offset))
+    F = np.zeros((A.shape[0], plan.feature_count), dtype=np.complex128)
+    np.add.at(F, (slice(None), plan.feat_index), T[:, dot_of] * plan.feat_weight[None, :])
+    return F
+
+
+def energy_grad(plan, A, species, weights):
+    """Per-atom energies and the holomorphic ``G = dE/dA``."""
+    k = plan.energy_weights(weights)[np.asarray(species)]  # [N, D]
+    I = segments(plan, A)
+    T = contractions(plan, I)
+    e = (k * T).sum(axis=1).real
+    gI = np.zeros_like(I)
+    for L in np.unique(plan.dot_L):
+        sel = np.nonzero(plan.dot_L == L)[0]
+        M = np.arange(-L, L + 1)
+        oa = plan.seg_offset[plan.dot_a[sel]][:, None] + (M + L)[None, :]
+        ob = plan.seg_offset[plan.dot_b[sel]][:, None] + (L - M)[None, :]
+        sgn = (-1.0) ** M
+        kd = k[:, sel][:, :, None]
+        np.add.at(gI, (slice(None), oa), kd * sgn * I[:, ob])
+        np.add.at(gI, (slice(None), ob), kd * sgn * I[:, oa])
+    G = np.zeros_like(A)
+    for s in range(plan.segment_count):
+        o0, o1 = int(plan.seg_offset[s]), int(plan.seg_offset[s + 1])
+        kind, L = int(plan.seg_kind[s]), int(plan.seg_L[s])
+        if kind == SEG_CHANNEL:
+            l, n = plan.channel(int(plan.seg_a[s]))
+            G[:, n - 1, l * l:(l + 1) * (l + 1)] += gI[:, o0:o1]
+        elif kind == SEG_PAIR:
+            a, b = int(plan.seg_a[s]), int(plan.seg_b[s])
+            (la, na), (lb, nb) = plan.channel(a), plan.channel(b)
+            idx, val = cg_table(la, lb, L)
+            xa, xb = _chan(plan, A, a), _chan(plan, A, b)
+            g = gI[:, o0 + idx[:, 2]] * val
+            ga = np.zeros_like(xa)
+            gb = np.zeros_like(xb)
+            np.add.at(ga, (slice(None), idx[:, 0]), g * xb[:, idx[:, 1]])
+            np.add.at(gb, (slice(None), idx[:, 1]), g * xa[:, idx[:, 0]])
+            G[:, na - 1, la * la:(la + 1) * (la + 1)] += ga
+            G[:, nb - 1, lb * lb:(lb + 1) * (lb + 1)] += gb
+    return e, G

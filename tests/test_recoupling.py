@@ -1,0 +1,111 @@
+"""Recoupled plan of a scalar ACE bundle (host side, CPU).
+
+The plan rewrites every feature as a sum of contractions of coupled channel
+pairs with weights fitted per pattern; these tests pin it to the reference's
+own features (the golden B-basis of the 96-atom system, computed by the
+reference) and to the oracle's energy gradient, and check the plan's
+structure and its per-atom costs."""
+
+import math
+import os
+
+import numpy as np
+import pytest
+
+from ye3t_b200.recoupling import (SEG_CHANNEL, SEG_PAIR, SEG_UNIT, build_recoupled_plan, cg_table,
+                                  clebsch_gordan)
+from ye3t_b200.schedules import ACEBundle
+
+import recoupled_numpy as rn
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bundle(stem):
+    return ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", stem + ".npz"))
+
+
+@pytest.fixture(scope="module")
+def plan3():
+    return build_recoupled_plan(_bundle("ace_n8_l3_nu3_L0"))
+
+
+@pytest.fixture(scope="module")
+def plan5():
+    b = _bundle("ace_n8_l3_nu4_L0")
+    return b, build_recoupled_plan(b)
+
+
+def test_clebsch_gordan_values_and_orthonormality():
+    # tabulated values (Condon-Shortley phase)
+    assert clebsch_gordan(1, 0, 1, 0, 0, 0) == pytest.approx(-1 / math.sqrt(3), abs=1e-15)
+    assert clebsch_gordan(1, 1, 1, -1, 0, 0) == pytest.approx(1 / math.sqrt(3), abs=1e-15)
+    assert clebsch_gordan(1, 1, 1, 0, 2, 1) == pytest.approx(1 / math.sqrt(2), abs=1e-15)
+    assert clebsch_gordan(1, 0, 1, 0, 2, 0) == pytest.approx(math.sqrt(2 / 3), abs=1e-15)
+    assert clebsch_gordan(2, 1, 1, -1, 1, 0) == pytest.approx(math.sqrt(3 / 10), abs=1e-15)
+    assert clebsch_gordan(1, 0, 1, 0, 1, 0) == 0.0
+    # the coupling V_l1 x V_l2 -> sum_L V_L is orthogonal
+    for l1 in range(4):
+        for l2 in range(4):
+            Ls = range(abs(l1 - l2), l1 + l2 + 1)
+            U = np.zeros(((2 * l1 + 1) * (2 * l2 + 1), sum(2 * L + 1 for L in Ls)))
+            col = 0
+            for L in Ls:
+                idx, val = cg_table(l1, l2, L)
+                U[idx[:, 0] * (2 * l2 + 1) + idx[:, 1], col + idx[:, 2]] = val
+                col += 2 * L + 1
+            assert np.abs(U.T @ U - np.eye(U.shape[1])).max() < 1e-13
+
+
+def test_plan_reproduces_reference_features_nu3(plan3, golden):
+    g = golden("ace_small")
+    A = np.asarray(g["A"])[:40]
+    F = rn.features(plan3, A)
+    ref = np.asarray(g["B3"])
+    assert np.abs(F - ref).max() <= 1e-12 * np.abs(ref).max()
+
+
+def test_plan_reproduces_reference_features_nu4(plan5, golden):
+    b, plan = plan5
+    g = golden("ace_small")
+    A = np.asarray(g["A"])[:40]
+    F = rn.features(plan, A)
+    off = b.feature_offsets()
+    cols = np.concatenate([np.arange(off[w], off[w + 1]) for w in np.asarray(g["B4_words"])])
+    ref = np.asarray(g["B4"])
+    assert ref.shape[1] == cols.shape[0]
+    assert np.abs(F[:, cols] - ref).max() <= 1e-12 * np.abs(ref).max()
+
+
+def test_plan_energy_gradient_matches_oracle(plan5):
+    from oracle import oracle
+    b, plan = plan5
+    rng = np.random.default_rng(11)
+    A = rng.normal(size=(3, 8, 16)) + 1j * rng.normal(size=(3, 8, 16))
+    species = np.array([0, 2, 1], dtype=np.int32)
+    w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
+    e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=4)
+    e1, G1 = rn.energy_grad(plan, A, species, w)
+    assert np.abs(e1 - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G1 - G0).max() <= 1e-12 * np.abs(G0).max()
+
+
+def test_plan_structure_and_costs(plan3, plan5):
+    b, plan = plan5
+    for p in (plan3, plan):
+        assert np.all(np.diff(p.seg_L) >= 0)
+        assert np.array_equal(p.seg_offset, np.concatenate([[0], np.cumsum(2 * p.seg_L.astype(np.int64) + 1)]))
+        assert np.array_equal(p.seg_L[p.dot_a], p.dot_L) and np.array_equal(p.seg_L[p.dot_b], p.dot_L)
+        assert np.all(np.diff(p.dot_L) >= 0)
+        assert np.unique(p.feat_index).shape[0] == p.feature_count
+        assert p.feat_weight.dtype == np.float64
+        pairs = p.seg_kind == SEG_PAIR
+        assert np.all(p.seg_a[pairs] >= 0) and np.all(p.seg_b[pairs] >= 0)
+        chans = p.seg_kind == SEG_CHANNEL
+        ls = p.seg_a[chans] % (p.lmax + 1)
+        assert np.array_equal(ls, p.seg_L[chans]) and np.all(p.seg_b[chans] == -1)
+        assert int((p.seg_kind == SEG_UNIT).sum()) <= 1
+    # the nu <= 4 set: one contraction per feature, and the per-atom work it needs
+    assert plan.dot_count == plan.feature_count == 41168
+    assert plan.costs() == {"pair_couplings": 20539, "contractions": 166072, "feature_weights": 57104,
+                            "components": 6920}

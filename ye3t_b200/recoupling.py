@@ -1,0 +1,333 @@
+"""Recoupled plan of a scalar (L = 0) ACE bundle: every feature as a short sum of
+contractions of coupled channel pairs.
+
+A feature of the word ``((l_1, n_1), ..., (l_nu, n_nu))`` (nu <= 4, channels sorted) is a
+rotation-invariant polynomial in the word's channel vectors
+``a_i = A[n_i - 1, l_i^2 : (l_i + 1)^2]`` (complex Condon-Shortley components, ``m = -l .. l``).
+The compiled schedule (``ye3t/core/couplings.py:481-567``) evaluates it term by term:
+``F = sum_t c_t prod_j bv_j[m_tj]``, 1,332,116 terms per atom for the nu <= 4, l <= 3 word set.
+
+The invariant multilinear forms on ``V_l1 x V_l2 x V_l3 x V_l4`` are spanned by the coupling
+trees ``((l_1 l_2) L, (l_3 l_4) L) 0`` over the intermediate ``L`` in
+``[|l_1 - l_2|, l_1 + l_2] & [|l_3 - l_4|, l_3 + l_4]``; a feature with repeated channels is
+such a form evaluated on repeated arguments (the polarisation of an invariant polynomial is
+invariant).  Hence, exactly,
+
+    F_f = sum_L W[f, L] T_L,        T_L = sum_M (-1)^M I_A[M] I_B[-M],
+    I_(a,b)^L[M] = sum_{m_a + m_b = M} <l_a m_a l_b m_b | L M> a[m_a] b[m_b],
+
+with ``I_A`` the coupled first pair and ``I_B`` the coupled second pair.  Three-channel words
+use the coupled first pair against the third channel (``L = l_3``), two-channel words the two
+channels (``L = l_1 = l_2``), one-channel words the ``l = 0`` component.  The pair couplings
+are shared by every word that contains the pair: for the nu <= 4, l <= 3, n <= 8 word set
+(25,328 words, 41,168 features), 1,308 segments hold 6,920 coupled components per atom
+(20,539 complex multiply-adds), and 41,168 contractions of 166,072 multiply-adds give every
+feature, against the 1.33 M terms of the compiled schedules.
+
+``W`` depends only on the word's pattern (its angular momenta and which channels repeat).
+The builder fits it once per pattern on seeded random channel vectors: it evaluates the
+pattern's schedule (block assembly as ``ye3t/workflows.py:636-661``, symmetric blocks as
+``ye3t/runtime/symmetric_power.py:740-868``) and the candidate contractions, keeps the
+cheapest contractions that span the features, and solves least squares.  It then checks the
+fit on a second, independent sample.  ``W`` is therefore exact up to rounding (residuals
+are about 1e-14 relative on the C5 set), and a pattern that does not fit raises.
+
+The Clebsch-Gordan coefficients come from Racah's closed formula (G. Racah, Phys. Rev. 62,
+438 (1942), eq. 16'); any fixed normalisation would do, since ``W`` absorbs it, but the
+coupled components must be the irreducible ones so that only the needed ``L`` are stored.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from functools import lru_cache
+from typing import Dict, List, Sequence, Tuple
+
+import numpy as np
+
+from .schedules import ACEBundle, ScheduleRecord, SymPowerTable
+
+__all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "build_recoupled_plan", "SEG_UNIT", "SEG_CHANNEL",
+           "SEG_PAIR"]
+
+SEG_UNIT, SEG_CHANNEL, SEG_PAIR = 0, 1, 2
+_FIT_TOL = 1e-11
+
+
+def clebsch_gordan(l1: int, m1: int, l2: int, m2: int, L: int, M: int) -> float:
+    """``<l1 m1 l2 m2 | L M>`` for integer angular momenta (Racah's formula)."""
+    if m1 + m2 != M or abs(m1) > l1 or abs(m2) > l2 or abs(M) > L or not abs(l1 - l2) <= L <= l1 + l2:
+        return 0.0
+    f = math.factorial
+    pre = (2 * L + 1) * f(L + l1 - l2) * f(L - l1 + l2) * f(l1 + l2 - L) / f(l1 + l2 + L + 1)
+    pre *= f(L + M) * f(L - M) * f(l1 - m1) * f(l1 + m1) * f(l2 - m2) * f(l2 + m2)
+    s = 0.0
+    for k in range(l1 + l2 - L + 1):
+        d = (k, l1 + l2 - L - k, l1 - m1 - k, l2 + m2 - k, L - l2 + m1 + k, L - l1 - m2 + k)
+        if min(d) < 0:
+            continue
+        s += (-1) ** k / float(np.prod([f(x) for x in d], dtype=np.float64))
+    return math.sqrt(pre) * s
+
+
+@lru_cache(maxsize=None)
+def cg_table(l1: int, l2: int, L: int) -> Tuple[np.ndarray, np.ndarray]:
+    """Nonzero couplings of ``V_l1 x V_l2 -> V_L``: ``(idx [K, 3], value [K])`` with rows
+    ``(m1 + l1, m2 + l2, M + L)``, ordered by ``M`` then ``m1``."""
+    rows, vals = [], []
+    for M in range(-L, L + 1):
+        for m1 in range(-l1, l1 + 1):
+            m2 = M - m1
+            if abs(m2) > l2:
+                continue
+            c = clebsch_gordan(l1, m1, l2, m2, L, M)
+            if c != 0.0:
+                rows.append((m1 + l1, m2 + l2, M + L))
+                vals.append(c)
+    return np.asarray(rows, dtype=np.int64).reshape(-1, 3), np.asarray(vals, dtype=np.float64)
+
+
+def _couple(a: np.ndarray, la: int, b: np.ndarray, lb: int, L: int) -> np.ndarray:
+    idx, val = cg_table(la, lb, L)
+    out = np.zeros(a.shape[:-1] + (2 * L + 1,), dtype=np.result_type(a, b))
+    np.add.at(out, (Ellipsis, idx[:, 2]), (val * a[..., idx[:, 0]] * b[..., idx[:, 1]]))
+    return out
+
+
+def _contract(x: np.ndarray, y: np.ndarray) -> np.ndarray:
+    L = (x.shape[-1] - 1) // 2
+    sign = (-1.0) ** np.arange(-L, L + 1)
+    return (sign * x * y[..., ::-1]).sum(axis=-1)
+
+
+# -- the pattern's own features on sample channel vectors ------------------------------------
+def _sym_values(table: SymPowerTable, x: np.ndarray) -> np.ndarray:
+    """``out[s, o] = sum_t v_t prod_i x[s, i]^k[t, i]`` (grouped symmetric-power table)."""
+    k = np.asarray(table.monomial_counts, dtype=np.int64)
+    mono = np.prod(x[:, None, :] ** k[None, :, :], axis=2) * np.asarray(table.monomial_value)[None, :]
+    off = np.asarray(table.output_offsets, dtype=np.int64)
+    out = np.zeros((x.shape[0], off.shape[0] - 1), dtype=np.complex128)
+    for o in range(off.shape[0] - 1):
+        out[:, o] = mono[:, off[o]:off[o + 1]].sum(axis=1)
+    return out
+
+
+def _pattern_features(rec: ScheduleRecord, sym_tables: Dict, chan: Dict[Tuple[int, int], np.ndarray]) -> np.ndarray:
+    """Schedule features ``[S, C]`` of a pattern record on channel vectors keyed ``(l, rank)``."""
+    S = next(iter(chan.values())).shape[0]
+    mdim = rec.max_block_m_dim
+    bv = np.zeros((S, rec.basis_count, rec.block_count, mdim), dtype=np.complex128)
+    for a, label in enumerate(rec.block_specs):
+        for j, (kind, n, l, k, lam, mu) in enumerate(label):
+            src = _sym_values(sym_tables[(l, k, lam, mu)], chan[(l, n)]) if kind == "sym" else chan[(l, n)]
+            bv[:, a, j, :src.shape[1]] = src
+    midx = rec.block_m_indices()
+    counts = np.diff(rec.component_offsets)
+    term_comp = np.repeat(np.arange(rec.component_count), counts)
+    label = rec.component_label_index[term_comp]
+    prod = np.broadcast_to(np.asarray(rec.coeffs)[None, :], (S, rec.term_count)).copy()
+    for j in range(rec.block_count):
+        prod = prod * bv[:, label, j, midx[:, j]]
+    out = np.zeros((S, rec.component_count), dtype=np.complex128)
+    np.add.at(out, (slice(None), term_comp), prod)
+    return out
+
+
+def _candidates(key: Sequence[Tuple[int, int]]) -> List[Tuple[Tuple, Tuple, int]]:
+    """Candidate contractions of a word pattern: ``(segment A, segment B, L)`` with segments
+    ``("unit",)``, ``("chan", i)`` or ``("pair", i, j)`` over word positions."""
+    ls = [l for l, _ in key]
+    if len(key) == 1:
+        return [(("chan", 0), ("unit",), 0)] if ls[0] == 0 else []
+    if len(key) == 2:
+        return [(("chan", 0), ("chan", 1), ls[0])] if ls[0] == ls[1] else []
+    if len(key) == 3:
+        ok = abs(ls[0] - ls[1]) <= ls[2] <= ls[0] + ls[1]
+        return [(("pair", 0, 1), ("chan", 2), ls[2])] if ok else []
+    if len(key) == 4:
+        lo = max(abs(ls[0] - ls[1]), abs(ls[2] - ls[3]))
+        hi = min(ls[0] + ls[1], ls[2] + ls[3])
+        return [(("pair", 0, 1), ("pair", 2, 3), L) for L in range(lo, hi + 1)]
+    raise ValueError(f"words of {len(key)} channels are not supported (nu <= 4)")
+
+
+def _segment_values(seg, L, key, chan):
+    if seg[0] == "unit":
+        return np.ones((next(iter(chan.values())).shape[0], 1), dtype=np.complex128)
+    if seg[0] == "chan":
+        return chan[key[seg[1]]]
+    (la, ra), (lb, rb) = key[seg[1]], key[seg[2]]
+    return _couple(chan[(la, ra)], la, chan[(lb, rb)], lb, L)
+
+
+def _fit_pattern(rec: ScheduleRecord, key, sym_tables, seed: int):
+    """Cheapest contractions spanning the pattern's features and their weights ``W [k, C]``."""
+    cands = _candidates(key)
+    C = rec.component_count
+    ranks = sorted(set(key))
+
+    def sample(rng, S):
+        chan = {(l, r): rng.normal(size=(S, 2 * l + 1)) + 1j * rng.normal(size=(S, 2 * l + 1)) for l, r in ranks}
+        F = _pattern_features(rec, sym_tables, chan)
+        T = np.stack([_contract(_segment_values(a, L, key, chan), _segment_values(b, L, key, chan))
+                      for a, b, L in cands], axis=1) if cands else np.zeros((S, 0), dtype=np.complex128)
+        return F, T
+
+    S = 12 + 3 * len(cands)
+    F, T = sample(np.random.default_rng(seed), S)
+    Fscale = max(float(np.abs(F).max()), 1e-300)
+    order = sorted(range(len(cands)), key=lambda i: (cands[i][2], i))
+    chosen: List[int] = []
+    W = np.zeros((0, C), dtype=np.complex128)
+    resid = float(np.abs(F).max()) / Fscale
+    for i in order:
+        if resid <= _FIT_TOL:
+            break
+        trial = chosen + [i]
+        Tt = T[:, trial]
+        if np.linalg.matrix_rank(Tt, tol=1e-10 * max(float(np.abs(Tt).max()), 1e-300)) < len(trial):
+            continue
+        Wt = np.linalg.lstsq(Tt, F, rcond=None)[0]
+        chosen, W = trial, Wt
+        resid = float(np.abs(Tt @ Wt - F).max()) / Fscale
+    F2, T2 = sample(np.random.default_rng(seed + 1), S)
+    check = float(np.abs(T2[:, chosen] @ W - F2).max()) / max(float(np.abs(F2).max()), 1e-300)
+    if resid > _FIT_TOL or check > _FIT_TOL:
+        raise ArithmeticError(f"pattern {key}: features are not spanned by the coupling trees "
+                              f"(residual {max(resid, check):.3e})")
+    return [cands[i] for i in chosen], W
+
+
+@dataclass
+class RecoupledPlan:
+    """Segments, contractions and feature weights of a recoupled bundle.
+
+    Per atom the evaluator forms every segment's components (``seg_offset`` into a
+    ``[component_count]`` complex row, segments ordered by ``L``), then every contraction
+    ``T_d = sum_M (-1)^M I[seg_a[d]][M] I[seg_b[d]][-M]`` (both segments of order ``dot_L[d]``;
+    contractions ordered by ``L``, then first segment), then
+    ``F[feat_index[z]] += feat_weight[z] T_d`` for ``z`` in ``dot_feat_offset[d] ..``.
+    Channel ``c`` is ``(l, n) = (c % (lmax + 1), c // (lmax + 1) + 1)``; its components are
+    ``A[n - 1, l^2 : (l + 1)^2]``.  A pair segment couples channels ``seg_a`` and ``seg_b``
+    (``seg_a <= seg_b`` in the words' ``(l, n)`` order) through ``cg_table(l_a, l_b, L)``.
+    """
+
+    nmax: int
+    lmax: int
+    feature_count: int
+    seg_kind: np.ndarray    # int8 [S]: SEG_UNIT, SEG_CHANNEL, SEG_PAIR
+    seg_L: np.ndarray       # int32 [S]
+    seg_a: np.ndarray       # int32 [S] channel (SEG_CHANNEL, SEG_PAIR), -1 for the unit segment
+    seg_b: np.ndarray       # int32 [S] second channel of a pair, -1 otherwise
+    seg_offset: np.ndarray  # int64 [S + 1] component offsets (ordered by L)
+    dot_a: np.ndarray       # int32 [D]
+    dot_b: np.ndarray       # int32 [D]
+    dot_L: np.ndarray       # int32 [D]
+    dot_word: np.ndarray    # int32 [D]
+    dot_feat_offset: np.ndarray  # int64 [D + 1]
+    feat_index: np.ndarray  # int64 [Z] global feature index
+    feat_weight: np.ndarray  # float64 [Z] (real: the fitted weights of the C-S basis are real)
+
+    @property
+    def segment_count(self) -> int:
+        return int(self.seg_kind.shape[0])
+
+    @property
+    def component_count(self) -> int:
+        return int(self.seg_offset[-1])
+
+    @property
+    def dot_count(self) -> int:
+        return int(self.dot_a.shape[0])
+
+    def channel(self, c: int) -> Tuple[int, int]:
+        return c % (self.lmax + 1), c // (self.lmax + 1) + 1
+
+    def costs(self) -> Dict[str, int]:
+        """Complex multiply-adds per atom: pair couplings, contractions, feature weights."""
+        couple = 0
+        for s in np.nonzero(self.seg_kind == SEG_PAIR)[0]:
+            la, lb = self.channel(int(self.seg_a[s]))[0], self.channel(int(self.seg_b[s]))[0]
+            couple += int(cg_table(la, lb, int(self.seg_L[s]))[1].shape[0])
+        return {"pair_couplings": couple, "contractions": int((2 * self.dot_L + 1).sum()),
+                "feature_weights": int(self.feat_weight.shape[0]), "components": self.component_count}
+
+    def energy_weights(self, weights: np.ndarray) -> np.ndarray:
+        """Per species, the real contraction weights ``k[s, d] = sum_f w[s, f] W[f, d]`` of the
+        energy ``e = Re(sum_d k[z, d] T_d)`` (real readout ``w [species, feature_count]``)."""
+        w = np.asarray(weights, dtype=np.float64)
+        if w.ndim != 2 or w.shape[1] != self.feature_count:
+            raise ValueError(f"weights must have shape [species, {self.feature_count}]")
+        contrib = w[:, self.feat_index] * self.feat_weight[None, :]
+        dot_of = np.repeat(np.arange(self.dot_count), np.diff(self.dot_feat_offset))
+        k = np.zeros((w.shape[0], self.dot_count), dtype=np.float64)
+        np.add.at(k, (slice(None), dot_of), contrib)
+        return k
+
+
+def build_recoupled_plan(bundle: ACEBundle, seed: int = 20260) -> RecoupledPlan:
+    """Recoupled plan of an L = 0 bundle (weights fitted once per pattern)."""
+    if bundle.target_L != 0:
+        raise ValueError("the recoupled plan covers scalar (L = 0) bundles")
+    fits = {}
+    for p, (rec, key) in enumerate(zip(bundle.patterns, bundle.pattern_keys)):
+        fits[p] = _fit_pattern(rec, key, bundle.sym_tables, seed + 7919 * p)
+
+    L1 = bundle.lmax + 1
+    chan_id = lambda l, n: (n - 1) * L1 + l  # noqa: E731
+    seg_index: Dict[Tuple[int, int, int, int], int] = {}
+    segs: List[Tuple[int, int, int, int]] = []
+
+    def segment(kind: int, L: int, a: int, b: int) -> int:
+        k = (kind, L, a, b)
+        if k not in seg_index:
+            seg_index[k] = len(segs)
+            segs.append(k)
+        return seg_index[k]
+
+    dots = []  # (L, seg_a, seg_b, word, [(feature, weight)])
+    offsets = bundle.feature_offsets()
+    for w, word in enumerate(bundle.words):
+        chosen, W = fits[int(bundle.word_pattern_index[w])]
+        ch = [chan_id(l, n) for l, n in word]
+
+        def seg_of(s, L):
+            if s[0] == "unit":
+                return segment(SEG_UNIT, 0, -1, -1)
+            if s[0] == "chan":
+                return segment(SEG_CHANNEL, L, ch[s[1]], -1)
+            return segment(SEG_PAIR, L, ch[s[1]], ch[s[2]])
+
+        for d, (sa, sb, L) in enumerate(chosen):
+            feats = [(int(offsets[w]) + c, complex(W[d, c])) for c in range(W.shape[1])
+                     if abs(W[d, c]) > 1e-14 * max(float(np.abs(W).max()), 1e-300)]
+            dots.append((L, seg_of(sa, L), seg_of(sb, L), w, feats))
+
+    # segments ordered by L (then first appearance); contractions by L, then first segment
+    order = sorted(range(len(segs)), key=lambda s: (segs[s][1], s))
+    rank = np.empty(len(segs), dtype=np.int64)
+    rank[np.asarray(order, dtype=np.int64)] = np.arange(len(segs))
+    kinds = np.asarray([segs[s][0] for s in order], dtype=np.int8)
+    Ls = np.asarray([segs[s][1] for s in order], dtype=np.int32)
+    seg_offset = np.concatenate([[0], np.cumsum(2 * Ls.astype(np.int64) + 1)])
+    dots = [(L, int(rank[a]), int(rank[b]), w, f) for L, a, b, w, f in dots]
+    dots.sort(key=lambda t: (t[0], t[1], t[2], t[3]))
+    nz = np.concatenate([[0], np.cumsum([len(t[4]) for t in dots])]).astype(np.int64)
+    weights = np.asarray([v for t in dots for _, v in t[4]], dtype=np.complex128)
+    scale = max(float(np.abs(weights).max()), 1e-300) if weights.size else 1.0
+    if weights.size and float(np.abs(weights.imag).max()) > 1e-12 * scale:
+        raise ArithmeticError("recoupled feature weights are not real")
+    return RecoupledPlan(
+        nmax=bundle.nmax, lmax=bundle.lmax, feature_count=bundle.feature_count,
+        seg_kind=kinds, seg_L=Ls,
+        seg_a=np.asarray([segs[s][2] for s in order], dtype=np.int32),
+        seg_b=np.asarray([segs[s][3] for s in order], dtype=np.int32),
+        seg_offset=seg_offset,
+        dot_a=np.asarray([t[1] for t in dots], dtype=np.int32),
+        dot_b=np.asarray([t[2] for t in dots], dtype=np.int32),
+        dot_L=np.asarray([t[0] for t in dots], dtype=np.int32),
+        dot_word=np.asarray([t[3] for t in dots], dtype=np.int32),
+        dot_feat_offset=nz,
+        feat_index=np.asarray([f for t in dots for f, _ in t[4]], dtype=np.int64),
+        feat_weight=np.ascontiguousarray(weights.real))
