@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define Y3B_ABI_VERSION 7
+#define Y3B_ABI_VERSION 8
 
 /* dtype codes */
 #define Y3B_F32 0
@@ -393,6 +393,48 @@ int y3b_ace_edge_grad(const double* positions, const int32_t* species, int64_t a
                       const double* species_prefactor, int64_t species_count, int64_t nmax,
                       int64_t lmax, double cutoff, double lambda, const void* dEdA,
                       double* edge_grad, int32_t* status, void* stream);
+
+/* Recoupled form of the same adjoint (scalar bundles).  Each feature is a
+ * short sum over intermediate L of contractions of Clebsch-Gordan coupled
+ * channel pairs, F_f = sum_L W[f, L] sum_M (-1)^M I_A^L[M] I_B^L[-M], which
+ * replaces the term-by-term schedules of evaluate_factorized_schedule_torch
+ * (ye3t/core/couplings.py:552-567) for E = sum_i sum_f w[z_i, f] Re(B_if).
+ * The tables are the device form of ye3t_b200.recoupling.RecoupledDeviceTables
+ * (all arrays in device memory): per pass L the components
+ * [pass_begin[L], pass_begin[L + 1]); comp holds two int4 per component,
+ * (a, b, cg_begin, cg_count) and (m, own_begin, own_count, 0); own holds
+ * (partner's first component in the pass, contraction) pairs; bp_* the
+ * back-propagation entries of each A-row entry per pass. */
+typedef struct {
+  int32_t pass_count;          /* passes, one per intermediate L */
+  int32_t max_pass_components; /* largest pass (shared-memory sizing) */
+  int32_t row_width;           /* complex entries of one A row: nmax (lmax + 1)^2 */
+  int32_t dot_count;           /* contractions: length of one species' weight row */
+  int64_t component_count;     /* entries of comp / 8 */
+  int64_t cg_count;            /* entries of cg_index and cg_value */
+  int64_t own_count;           /* entries of own / 2 */
+  int64_t bp_count;            /* entries of bp_gi, bp_other, bp_value */
+  const int32_t* pass_begin;   /* [pass_count + 1] */
+  const int32_t* comp;         /* [component_count, 8], 16-byte aligned */
+  const int32_t* cg_index;     /* [cg_count]: m_a index | m_b index << 8 */
+  const double* cg_value;      /* [cg_count] */
+  const int32_t* own;          /* [own_count, 2], 8-byte aligned */
+  const int32_t* bp_begin;     /* [pass_count * row_width + 1] */
+  const int32_t* bp_gi;        /* [bp_count] component of the pass */
+  const int32_t* bp_other;     /* [bp_count] A-row entry of the partner, -1 for a copied channel */
+  const double* bp_value;      /* [bp_count] */
+} y3b_recoupled_tables;
+
+/* Per-atom energies e_i = Re(sum_d k[z_i, d] T_d) and G = dE/dA (complex128,
+ * A's layout [atom_count, row_width]), with contraction_weights k
+ * [species_count, dot_count] (RecoupledPlan.energy_weights of the readout).
+ * Species outside [0, species_count) set Y3B_STATUS_INDEX_RANGE and use
+ * species 0; a table entry outside its pass or array sets Y3B_STATUS_TABLE and
+ * is skipped.  Deterministic (fixed summation order, no atomics on data). */
+int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                                  const int32_t* species, const double* contraction_weights,
+                                  int64_t species_count, double* energy, void* dEdA, int32_t* status,
+                                  void* stream);
 
 /* Forces F_k = -dE/dr_k = sum_{e in row k} (g_e - g_rev(e)) from the rows of
  * all atoms (deterministic gather; rev(e) is the reverse edge). */

@@ -92,3 +92,42 @@ def energy_grad(plan, A, species, weights):
             G[:, na - 1, la * la:(la + 1) * (la + 1)] += ga
             G[:, nb - 1, lb * lb:(lb + 1) * (lb + 1)] += gb
     return e, G
+
+
+def walk_device_tables(tabs, A, species, k):
+    """The device pass over ``RecoupledDeviceTables``, restated loop for loop
+    (vectorised over atoms): per L, the components, their adjoints and the energy
+    share, then the back-propagation into the A row.  Returns (energies, G)."""
+    N = A.shape[0]
+    W = tabs.row_width
+    row = A.reshape(N, W)
+    kz = np.asarray(k)[np.asarray(species)]  # [N, D]
+    G = np.zeros((N, W), dtype=np.complex128)
+    e = np.zeros(N)
+    for L in range(tabs.pass_count):
+        c0, c1 = int(tabs.pass_begin[L]), int(tabs.pass_begin[L + 1])
+        I = np.zeros((N, c1 - c0), dtype=np.complex128)
+        for c in range(c0, c1):
+            a, b, q0, qn = (int(v) for v in tabs.comp[c, :4])
+            if a < 0:
+                I[:, c - c0] = 1.0
+            elif qn == 0:
+                I[:, c - c0] = row[:, a]
+            else:
+                q = tabs.cg_index[q0:q0 + qn]
+                I[:, c - c0] = (tabs.cg_value[q0:q0 + qn] * row[:, a + (q & 255)] * row[:, b + (q >> 8)]).sum(axis=1)
+        gI = np.zeros_like(I)
+        for c in range(c0, c1):
+            m, o0, on = (int(v) for v in tabs.comp[c, 4:7])
+            ent = tabs.own[o0:o0 + on]
+            acc = (kz[:, ent[:, 1]] * I[:, ent[:, 0] + 2 * L - m]).sum(axis=1)
+            gI[:, c - c0] = -acc if (m - L) & 1 else acc
+        e += 0.5 * (I * gI).sum(axis=1).real
+        for t in range(W):
+            b0, b1 = int(tabs.bp_begin[L * W + t]), int(tabs.bp_begin[L * W + t + 1])
+            if b1 == b0:
+                continue
+            gi, other, val = tabs.bp_gi[b0:b1], tabs.bp_other[b0:b1], tabs.bp_value[b0:b1]
+            partner = np.where(other[None, :] < 0, 1.0, row[:, np.maximum(other, 0)])
+            G[:, t] += (val * gI[:, gi] * partner).sum(axis=1)
+    return e, G.reshape(A.shape)

@@ -103,9 +103,12 @@ def test_torch_ops_registered_with_fake_kernels():
         assert a.shape == (9, 6) and b.shape == (9, 6, 3)
 
 
-def test_tables_struct_layout_matches_header(tmp_path):
-    """The ctypes mirror of y3b_ace_tables (passed by value to every fused kernel) has the
-    C struct's size and field offsets, read from include/ye3t_b200.h by a small C program."""
+@pytest.mark.parametrize("struct, c_name", [("AceTables", "y3b_ace_tables"),
+                                             ("RecoupledTables", "y3b_recoupled_tables")])
+def test_tables_struct_layout_matches_header(tmp_path, struct, c_name):
+    """The ctypes mirrors of the table structs (y3b_ace_tables is passed by value to every
+    fused kernel) have the C structs' sizes and field offsets, read from include/ye3t_b200.h
+    by a small C program."""
     import ctypes
     import shutil
     import subprocess
@@ -113,18 +116,19 @@ def test_tables_struct_layout_matches_header(tmp_path):
     gcc = shutil.which("gcc")
     if gcc is None:
         pytest.skip("no C compiler")
-    fields = [name for name, _ in _native.AceTables._fields_]
+    cls = getattr(_native, struct)
+    fields = [name for name, _ in cls._fields_]
     src = tmp_path / "layout.c"
     src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"ye3t_b200.h\"\nint main(void) {\n"
-                   "  printf(\"%zu\\n\", sizeof(y3b_ace_tables));\n"
-                   + "".join(f"  printf(\"%zu\\n\", offsetof(y3b_ace_tables, {f}));\n" for f in fields)
+                   f"  printf(\"%zu\\n\", sizeof({c_name}));\n"
+                   + "".join(f"  printf(\"%zu\\n\", offsetof({c_name}, {f}));\n" for f in fields)
                    + "  return 0;\n}\n")
     exe = tmp_path / "layout"
     include = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
     subprocess.run([gcc, "-I", include, str(src), "-o", str(exe)], check=True)
     out = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
-    assert out[0] == ctypes.sizeof(_native.AceTables)
-    assert out[1:] == [getattr(_native.AceTables, f).offset for f in fields]
+    assert out[0] == ctypes.sizeof(cls)
+    assert out[1:] == [getattr(cls, f).offset for f in fields]
 
 
 def test_ctypes_signatures_match_header_parameter_counts():

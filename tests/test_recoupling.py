@@ -109,3 +109,53 @@ def test_plan_structure_and_costs(plan3, plan5):
     assert plan.dot_count == plan.feature_count == 41168
     assert plan.costs() == {"pair_couplings": 20539, "contractions": 166072, "feature_weights": 57104,
                             "components": 6920}
+
+
+def test_device_tables_walk_matches_oracle_and_validation_catches_damage(plan5):
+    """The packed tables, walked loop for loop as the device pass walks them, give the
+    oracle's energies and dE/dA; a damaged index is refused before any upload."""
+    from oracle import oracle
+    b, plan = plan5
+    tabs = plan.device_tables()
+    assert (tabs.pass_count, tabs.max_pass_components, tabs.row_width, tabs.dot_count) == (7, 2184, 128, 41168)
+    assert tabs.smem_bytes() == 16 * (2 * 128 + 2 * 2184)
+    rng = np.random.default_rng(12)
+    A = rng.normal(size=(3, 8, 16)) + 1j * rng.normal(size=(3, 8, 16))
+    species = np.array([1, 0, 2], dtype=np.int32)
+    w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
+    e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=4)
+    e1, G1 = rn.walk_device_tables(tabs, A, species, plan.energy_weights(w))
+    assert np.abs(e1 - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G1 - G0).max() <= 1e-12 * np.abs(G0).max()
+    import copy
+    for field, row, col, value in (("own", 5, 0, 10 ** 6), ("bp_gi", 3, None, -2), ("comp", 0, 0, 10 ** 4)):
+        bad = copy.deepcopy(tabs)
+        arr = getattr(bad, field)
+        if col is None:
+            arr[row] = value
+        else:
+            arr[row, col] = value
+        with pytest.raises(ValueError):
+            bad.validate()
+
+
+def test_recoupled_entry_point_checks_arguments_without_gpu(plan3):
+    """The C entry point refuses null, misaligned and oversized tables before any CUDA call."""
+    import ctypes
+
+    import torch
+    from ye3t_b200 import _native
+    from ye3t_b200.recoupling import _TABLE_ARRAYS, ctypes_tables
+    tabs = plan3.device_tables()
+    arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(tabs, name))) for name in _TABLE_ARRAYS}
+    ct = ctypes_tables(arrays, tabs)
+    lib = _native.lib()
+    f = lib.y3b_ace_recoupled_energy_grad
+    assert f(ctypes.byref(ct), 0, 0, 0, 0, 1, 0, 0, 0, 0) == 0  # no atoms: nothing to do
+    assert f(None, 0, 0, 0, 0, 1, 0, 0, 0, 0) == -1
+    odd = ctypes_tables(arrays, tabs)
+    odd.comp = ct.comp + 4
+    assert f(ctypes.byref(odd), 0, 0, 0, 0, 1, 0, 0, 0, 0) == -1 and b"aligned" in lib.y3b_last_error()
+    big = ctypes_tables(arrays, tabs)
+    big.max_pass_components = 1 << 20
+    assert f(ctypes.byref(big), 1, 4, 1, 1, 1, 1, 1, 0, 0) == -1 and b"shared memory" in lib.y3b_last_error()

@@ -16,7 +16,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libye3t_b200.so")
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 F32, F64, C64, C128 = 0, 1, 2, 3
 STATUS_INDEX_RANGE = 1
 STATUS_CAPACITY = 2
@@ -49,6 +49,17 @@ class AceTables(ctypes.Structure):
         ("group_count", I64), ("groups", VP), ("group_offsets", VP),
         ("sym_grad_count", I64), ("sym_grad_offsets", VP), ("sym_grad_index", VP), ("sym_grad_coeff", VP),
         ("sym_term_count", I64),
+    ]
+
+
+class RecoupledTables(ctypes.Structure):
+    """``y3b_recoupled_tables`` (include/ye3t_b200.h)."""
+
+    _fields_ = [
+        ("pass_count", I32), ("max_pass_components", I32), ("row_width", I32), ("dot_count", I32),
+        ("component_count", I64), ("cg_count", I64), ("own_count", I64), ("bp_count", I64),
+        ("pass_begin", VP), ("comp", VP), ("cg_index", VP), ("cg_value", VP), ("own", VP),
+        ("bp_begin", VP), ("bp_gi", VP), ("bp_other", VP), ("bp_value", VP),
     ]
 
 
@@ -90,6 +101,8 @@ _SIGS = {
     "y3b_ace_density_mixed": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64,
                                              I64, DBL, DBL, VP, VP, VP]),
     "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP, VP]),
+    "y3b_ace_recoupled_energy_grad": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, I64, VP,
+                                                     VP, VP, VP]),
     "y3b_ace_edge_grad": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                          VP, VP]),
     "y3b_forces_gather": (ctypes.c_int, [VP, VP, I64, VP, VP, VP, VP]),

@@ -48,8 +48,8 @@ import numpy as np
 
 from .schedules import ACEBundle, ScheduleRecord, SymPowerTable
 
-__all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "build_recoupled_plan", "SEG_UNIT", "SEG_CHANNEL",
-           "SEG_PAIR"]
+__all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "RecoupledDeviceTables", "RecoupledEnergyGrad",
+           "build_recoupled_plan", "ctypes_tables", "SEG_UNIT", "SEG_CHANNEL", "SEG_PAIR"]
 
 SEG_UNIT, SEG_CHANNEL, SEG_PAIR = 0, 1, 2
 _FIT_TOL = 1e-11
@@ -265,6 +265,170 @@ class RecoupledPlan:
         np.add.at(k, (slice(None), dot_of), contrib)
         return k
 
+    def device_tables(self) -> "RecoupledDeviceTables":
+        """The plan packed for the device pass (validated)."""
+        return _device_tables(self)
+
+
+@dataclass
+class RecoupledDeviceTables:
+    """The plan packed for the device pass over one atom (``y3b_recoupled_tables``).
+
+    The kernel runs one pass per ``L``.  In pass ``L`` the components
+    ``pass_begin[L] .. pass_begin[L + 1]`` are formed in shared memory (local index
+    ``c - pass_begin[L]``), from the atom's A row of ``row_width`` complex entries:
+    ``comp[c] = (a, b, cg_begin, cg_count, m, own_begin, own_count, 0)``.  ``a < 0`` is the
+    unit; ``cg_count == 0`` copies ``A[a]``; otherwise
+    ``I = sum_q cg_value[q] A[a + (cg_index[q] & 255)] A[b + (cg_index[q] >> 8)]``.
+    Then each component's adjoint
+    ``gI[c] = (-1)^(m - L) sum_q k[own[q, 1]] I[own[q, 0] + 2L - m]``
+    (``q`` in ``own_begin .. + own_count``, ``own[q, 0]`` the partner segment's first local
+    component, ``own[q, 1]`` the contraction), and the pass's energy share
+    ``Re(I[c] gI[c]) / 2``.  Last, each A entry ``t`` adds
+    ``sum_q bp_value[q] gI[bp_gi[q]] (A[bp_other[q]] or 1 when bp_other[q] < 0)`` over
+    ``q`` in ``bp_begin[L * row_width + t] ..``."""
+
+    pass_count: int
+    max_pass_components: int
+    row_width: int
+    dot_count: int
+    pass_begin: np.ndarray  # int32 [pass_count + 1]
+    comp: np.ndarray        # int32 [C, 8]
+    cg_index: np.ndarray    # int32 [K]
+    cg_value: np.ndarray    # float64 [K]
+    own: np.ndarray         # int32 [O, 2]
+    bp_begin: np.ndarray    # int32 [pass_count * row_width + 1]
+    bp_gi: np.ndarray       # int32 [Bp]
+    bp_other: np.ndarray    # int32 [Bp]
+    bp_value: np.ndarray    # float64 [Bp]
+
+    def validate(self) -> None:
+        """Every index the device pass follows stays inside its array or its pass."""
+        P, W = self.pass_count, self.row_width
+        pb = self.pass_begin.astype(np.int64)
+        if pb.shape != (P + 1,) or pb[0] != 0 or np.any(np.diff(pb) < 0) or pb[-1] != self.comp.shape[0]:
+            raise ValueError("pass_begin does not partition the components")
+        if int(np.diff(pb).max(initial=0)) > self.max_pass_components:
+            raise ValueError("a pass holds more components than max_pass_components")
+        c = self.comp.astype(np.int64)
+        Lc = np.repeat(np.arange(P), np.diff(pb))
+        nc = np.diff(pb)[Lc]
+        a, b, cg0, cgn, m, o0, on = (c[:, i] for i in range(7))
+        unit, chan, pair = a < 0, (a >= 0) & (cgn == 0), cgn > 0
+        if np.any(unit & ((a != -1) | (m != 0) | (Lc != 0))):
+            raise ValueError("the unit component must be L = 0")
+        if np.any(chan & (a >= W)):
+            raise ValueError("channel component outside the A row")
+        if np.any((m < 0) | (m > 2 * Lc)):
+            raise ValueError("component m outside 0 .. 2L")
+        if np.any(cg0 < 0) or np.any(cg0 + cgn > self.cg_value.shape[0]):
+            raise ValueError("coupling range outside the coupling table")
+        K = self.cg_index.astype(np.int64)
+        for i in np.nonzero(pair)[0]:
+            q = K[cg0[i]:cg0[i] + cgn[i]]
+            if a[i] + (q & 255).max() >= W or b[i] < 0 or b[i] + (q >> 8).max() >= W:
+                raise ValueError("coupling term outside the A row")
+        if np.any(o0 < 0) or np.any(o0 + on > self.own.shape[0]):
+            raise ValueError("adjoint list outside the list table")
+        own = self.own.astype(np.int64)
+        if own.size:
+            idx = np.repeat(np.arange(c.shape[0]), on)
+            q = np.concatenate([np.arange(o0[i], o0[i] + on[i]) for i in range(c.shape[0])]) if on.sum() else \
+                np.zeros(0, dtype=np.int64)
+            rd = own[q, 0] + 2 * Lc[idx] - m[idx]
+            if np.any(own[q, 0] < 0) or np.any(rd >= nc[idx]) or np.any(rd < 0):
+                raise ValueError("adjoint partner outside its pass")
+            if np.any(own[q, 1] < 0) or np.any(own[q, 1] >= self.dot_count):
+                raise ValueError("adjoint contraction outside the weights")
+        bb = self.bp_begin.astype(np.int64)
+        if bb.shape != (P * W + 1,) or bb[0] != 0 or np.any(np.diff(bb) < 0) or bb[-1] != self.bp_gi.shape[0]:
+            raise ValueError("bp_begin does not partition the back-propagation entries")
+        Lq = np.repeat(np.arange(P * W) // W, np.diff(bb))
+        if np.any(self.bp_gi < 0) or np.any(self.bp_gi >= np.diff(pb)[Lq]):
+            raise ValueError("back-propagation entry outside its pass")
+        if np.any(self.bp_other >= W) or np.any(self.bp_other < -1):
+            raise ValueError("back-propagation partner outside the A row")
+
+    def smem_bytes(self) -> int:
+        """Dynamic shared memory of the device pass: the A row and its adjoint, the pass's
+        components and theirs."""
+        return 16 * (2 * self.row_width + 2 * self.max_pass_components)
+
+
+def _device_tables(plan: "RecoupledPlan") -> RecoupledDeviceTables:
+    L1 = plan.lmax + 1
+    W = L1 * L1
+    row_width = plan.nmax * W
+
+    def base(c):  # first A-row entry of channel c
+        l, n = c % L1, c // L1 + 1
+        return (n - 1) * W + l * l
+
+    P = int(plan.seg_L.max()) + 1 if plan.segment_count else 0
+    seg_off = plan.seg_offset.astype(np.int64)
+    pass_begin = np.zeros(P + 1, dtype=np.int64)
+    for L in range(P):
+        sel = np.nonzero(plan.seg_L == L)[0]
+        pass_begin[L + 1] = seg_off[sel[-1] + 1] if sel.size else pass_begin[L]
+    # coupling tables shared by (l_a, l_b, L, M)
+    cg_index, cg_value, cg_at = [], [], {}
+
+    def cg_range(la, lb, L, M):
+        key = (la, lb, L, M)
+        if key not in cg_at:
+            idx, val = cg_table(la, lb, L)
+            rows = np.nonzero(idx[:, 2] == M + L)[0]
+            cg_at[key] = (len(cg_value), rows.shape[0])
+            cg_index.extend(int(idx[r, 0]) | (int(idx[r, 1]) << 8) for r in rows)
+            cg_value.extend(float(val[r]) for r in rows)
+        return cg_at[key]
+
+    # adjoint lists per segment: partner segment (local first component) and contraction
+    lists: List[List[Tuple[int, int]]] = [[] for _ in range(plan.segment_count)]
+    for d in range(plan.dot_count):
+        a, b = int(plan.dot_a[d]), int(plan.dot_b[d])
+        L = int(plan.dot_L[d])
+        lists[a].append((int(seg_off[b] - pass_begin[L]), d))
+        lists[b].append((int(seg_off[a] - pass_begin[L]), d))
+    own, own_at = [], []
+    for s in range(plan.segment_count):
+        own_at.append(len(own))
+        own.extend(lists[s])
+    comp = np.zeros((int(seg_off[-1]), 8), dtype=np.int64)
+    bp = [[[] for _ in range(row_width)] for _ in range(P)]
+    for s in range(plan.segment_count):
+        L, kind = int(plan.seg_L[s]), int(plan.seg_kind[s])
+        for mi in range(2 * L + 1):
+            c = int(seg_off[s]) + mi
+            local = c - int(pass_begin[L])
+            row = [-1, -1, 0, 0, mi, own_at[s], len(lists[s]), 0]
+            if kind == SEG_CHANNEL:
+                row[0] = base(int(plan.seg_a[s])) + mi
+                bp[L][row[0]].append((local, -1, 1.0))
+            elif kind == SEG_PAIR:
+                ca, cb = int(plan.seg_a[s]), int(plan.seg_b[s])
+                la, lb = ca % L1, cb % L1
+                row[0], row[1] = base(ca), base(cb)
+                q0, qn = cg_range(la, lb, L, mi - L)
+                row[2], row[3] = q0, qn
+                for q in range(q0, q0 + qn):
+                    ia, ib, v = cg_index[q] & 255, cg_index[q] >> 8, cg_value[q]
+                    bp[L][row[0] + ia].append((local, row[1] + ib, v))
+                    bp[L][row[1] + ib].append((local, row[0] + ia, v))
+            comp[c] = row
+    bp_flat = [e for L in range(P) for t in range(row_width) for e in bp[L][t]]
+    bp_begin = np.concatenate([[0], np.cumsum([len(bp[L][t]) for L in range(P) for t in range(row_width)])])
+    tabs = RecoupledDeviceTables(
+        pass_count=P, max_pass_components=int(np.diff(pass_begin).max(initial=0)), row_width=row_width,
+        dot_count=plan.dot_count, pass_begin=pass_begin.astype(np.int32), comp=comp.astype(np.int32),
+        cg_index=np.asarray(cg_index, dtype=np.int32), cg_value=np.asarray(cg_value, dtype=np.float64),
+        own=np.asarray(own, dtype=np.int32).reshape(-1, 2), bp_begin=bp_begin.astype(np.int32),
+        bp_gi=np.asarray([e[0] for e in bp_flat], dtype=np.int32),
+        bp_other=np.asarray([e[1] for e in bp_flat], dtype=np.int32),
+        bp_value=np.asarray([e[2] for e in bp_flat], dtype=np.float64))
+    tabs.validate()
+    return tabs
+
 
 def build_recoupled_plan(bundle: ACEBundle, seed: int = 20260) -> RecoupledPlan:
     """Recoupled plan of an L = 0 bundle (weights fitted once per pattern)."""
@@ -331,3 +495,51 @@ def build_recoupled_plan(bundle: ACEBundle, seed: int = 20260) -> RecoupledPlan:
         dot_feat_offset=nz,
         feat_index=np.asarray([f for t in dots for f, _ in t[4]], dtype=np.int64),
         feat_weight=np.ascontiguousarray(weights.real))
+
+
+def ctypes_tables(arrays: Dict[str, "object"], tabs: RecoupledDeviceTables):
+    """``y3b_recoupled_tables`` over tensors holding ``tabs``' arrays (``arrays[name]``)."""
+    from . import _native as nat
+    return nat.RecoupledTables(
+        pass_count=tabs.pass_count, max_pass_components=tabs.max_pass_components, row_width=tabs.row_width,
+        dot_count=tabs.dot_count, component_count=int(tabs.comp.shape[0]), cg_count=int(tabs.cg_value.shape[0]),
+        own_count=int(tabs.own.shape[0]), bp_count=int(tabs.bp_gi.shape[0]),
+        **{name: arrays[name].data_ptr() for name in _TABLE_ARRAYS})
+
+
+_TABLE_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value")
+
+
+class RecoupledEnergyGrad:
+    """Per-atom energies and ``G = dE/dA`` through the recoupled plan on one GPU
+    (``y3b_ace_recoupled_energy_grad``): the tables and the per-species contraction
+    weights are uploaded once; each call takes ``A [n, nmax, (lmax+1)^2]`` complex128
+    and the atoms' species, like ``ACEEvaluator.energy_grad``."""
+
+    def __init__(self, bundle: ACEBundle, device, weights: np.ndarray, plan: "RecoupledPlan" = None):
+        import torch
+        self.device = torch.device(device)
+        self.plan = plan if plan is not None else build_recoupled_plan(bundle)
+        self.tables = self.plan.device_tables()
+        self.arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(self.tables, name))).to(self.device)
+                       for name in _TABLE_ARRAYS}
+        self.weights = torch.as_tensor(self.plan.energy_weights(weights)).to(self.device).contiguous()
+        self._c = ctypes_tables(self.arrays, self.tables)
+
+    def energy_grad(self, A, species, status=None):
+        import ctypes
+
+        import torch
+        from . import _native as nat
+        A = A.to(self.device, torch.complex128).contiguous()
+        n = A.shape[0]
+        if A.shape[1:].numel() != self.tables.row_width:
+            raise ValueError(f"A rows must hold {self.tables.row_width} complex entries")
+        sp = species.to(self.device, torch.int32).contiguous()
+        nat.require_cuda(A, sp, what="recoupled energy_grad")
+        e = torch.empty(n, dtype=torch.float64, device=self.device)
+        G = torch.empty_like(A)
+        nat.check(nat.lib().y3b_ace_recoupled_energy_grad(
+            ctypes.byref(self._c), A.data_ptr(), n, sp.data_ptr(), self.weights.data_ptr(), self.weights.shape[0],
+            e.data_ptr(), G.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), "ace_recoupled_energy_grad")
+        return e, G
