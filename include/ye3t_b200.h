@@ -423,6 +423,12 @@ typedef struct {
   const int32_t* bp_gi;        /* [bp_count] component of the pass */
   const int32_t* bp_other;     /* [bp_count] A-row entry of the partner, -1 for a copied channel */
   const double* bp_value;      /* [bp_count] */
+  int64_t feature_count;       /* features of the bundle */
+  int64_t feat_count;          /* entries of feat_index and feat_weight */
+  const int32_t* dot_begin;    /* [pass_count + 1] contractions of each pass */
+  const int32_t* dot;          /* [dot_count, 4]: first local component of A, of B, feature range; 16-byte aligned */
+  const int32_t* feat_index;   /* [feat_count] feature of each weight */
+  const double* feat_weight;   /* [feat_count] W[f, d] */
 } y3b_recoupled_tables;
 
 /* Per-atom energies e_i = Re(sum_d k[z_i, d] T_d) and G = dE/dA (complex128,
@@ -435,6 +441,16 @@ int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables, const void
                                   const int32_t* species, const double* contraction_weights,
                                   int64_t species_count, double* energy, void* dEdA, int32_t* status,
                                   void* stream);
+
+/* Forward passes of the same plan: per-atom energies e_i = Re(sum_d k[z_i, d] T_d)
+ * (each contraction once), or the features F [atom_count, feature_count]
+ * complex128 in the bundle's feature order (ACEBundle.feature_offsets), with
+ * the same status conventions. */
+int y3b_ace_recoupled_energy(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                             const int32_t* species, const double* contraction_weights, int64_t species_count,
+                             double* energy, int32_t* status, void* stream);
+int y3b_ace_recoupled_features(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                               void* features, int32_t* status, void* stream);
 
 /* Forces F_k = -dE/dr_k = sum_{e in row k} (g_e - g_rev(e)) from the rows of
  * all atoms (deterministic gather; rev(e) is the reverse edge). */

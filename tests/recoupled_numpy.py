@@ -131,3 +131,36 @@ def walk_device_tables(tabs, A, species, k):
             partner = np.where(other[None, :] < 0, 1.0, row[:, np.maximum(other, 0)])
             G[:, t] += (val * gI[:, gi] * partner).sum(axis=1)
     return e, G.reshape(A.shape)
+
+
+def walk_forward(tabs, A, species=None, k=None):
+    """The forward device pass over ``RecoupledDeviceTables``: per L the components,
+    then each contraction ``T_d`` once; returns the energies ``Re(sum_d k[z, d] T_d)``
+    when ``k`` is given, else the features ``F [N, feature_count]``."""
+    N = A.shape[0]
+    W = tabs.row_width
+    row = A.reshape(N, W)
+    kz = None if k is None else np.asarray(k)[np.asarray(species)]
+    e = np.zeros(N)
+    F = np.zeros((N, tabs.feature_count), dtype=np.complex128)
+    for L in range(tabs.pass_count):
+        c0, c1 = int(tabs.pass_begin[L]), int(tabs.pass_begin[L + 1])
+        I = np.zeros((N, c1 - c0), dtype=np.complex128)
+        for c in range(c0, c1):
+            a, b, q0, qn = (int(v) for v in tabs.comp[c, :4])
+            if a < 0:
+                I[:, c - c0] = 1.0
+            elif qn == 0:
+                I[:, c - c0] = row[:, a]
+            else:
+                q = tabs.cg_index[q0:q0 + qn]
+                I[:, c - c0] = (tabs.cg_value[q0:q0 + qn] * row[:, a + (q & 255)] * row[:, b + (q >> 8)]).sum(axis=1)
+        M = np.arange(-L, L + 1)
+        for d in range(int(tabs.dot_begin[L]), int(tabs.dot_begin[L + 1])):
+            oa, ob, f0, fn = (int(v) for v in tabs.dot[d])
+            T = ((-1.0) ** M * I[:, oa + M + L] * I[:, ob + L - M]).sum(axis=1)
+            if kz is not None:
+                e += kz[:, d] * T.real
+            else:
+                F[:, tabs.feat_index[f0:f0 + fn]] += tabs.feat_weight[f0:f0 + fn][None, :] * T[:, None]
+    return e if k is not None else F

@@ -119,6 +119,7 @@ def test_device_tables_walk_matches_oracle_and_validation_catches_damage(plan5):
     tabs = plan.device_tables()
     assert (tabs.pass_count, tabs.max_pass_components, tabs.row_width, tabs.dot_count) == (7, 2184, 128, 41168)
     assert tabs.smem_bytes() == 16 * (2 * 128 + 2 * 2184)
+    assert tabs.dot_begin.tolist() == [0, 9260, 21018, 33932, 38500, 40888, 40958, 41168]
     rng = np.random.default_rng(12)
     A = rng.normal(size=(3, 8, 16)) + 1j * rng.normal(size=(3, 8, 16))
     species = np.array([1, 0, 2], dtype=np.int32)
@@ -128,7 +129,13 @@ def test_device_tables_walk_matches_oracle_and_validation_catches_damage(plan5):
     assert np.abs(e1 - e0).max() <= 1e-12 * np.abs(e0).max()
     assert np.abs(G1 - G0).max() <= 1e-12 * np.abs(G0).max()
     import copy
-    for field, row, col, value in (("own", 5, 0, 10 ** 6), ("bp_gi", 3, None, -2), ("comp", 0, 0, 10 ** 4)):
+    F0 = oracle.bundle_features(b, A, threads=4)
+    F1 = rn.walk_forward(tabs, A)
+    assert np.abs(F1 - F0).max() <= 1e-12 * np.abs(F0).max()
+    e2 = rn.walk_forward(tabs, A, species, plan.energy_weights(w))
+    assert np.abs(e2 - e0).max() <= 1e-12 * np.abs(e0).max()
+    for field, row, col, value in (("own", 5, 0, 10 ** 6), ("bp_gi", 3, None, -2), ("comp", 0, 0, 10 ** 4),
+                                   ("dot", 7, 1, 10 ** 5), ("feat_index", 2, None, 10 ** 7)):
         bad = copy.deepcopy(tabs)
         arr = getattr(bad, field)
         if col is None:
@@ -140,7 +147,7 @@ def test_device_tables_walk_matches_oracle_and_validation_catches_damage(plan5):
 
 
 def test_recoupled_entry_point_checks_arguments_without_gpu(plan3):
-    """The C entry point refuses null, misaligned and oversized tables before any CUDA call."""
+    """The C entry points refuse null, misaligned and oversized tables before any CUDA call."""
     import ctypes
 
     import torch
@@ -159,3 +166,11 @@ def test_recoupled_entry_point_checks_arguments_without_gpu(plan3):
     big = ctypes_tables(arrays, tabs)
     big.max_pass_components = 1 << 20
     assert f(ctypes.byref(big), 1, 4, 1, 1, 1, 1, 1, 0, 0) == -1 and b"shared memory" in lib.y3b_last_error()
+    fe = lib.y3b_ace_recoupled_energy
+    ff = lib.y3b_ace_recoupled_features
+    assert fe(ctypes.byref(ct), 0, 0, 0, 0, 1, 0, 0, 0) == 0 and ff(ctypes.byref(ct), 0, 0, 0, 0, 0) == 0
+    assert ff(ctypes.byref(ct), 1, 4, 0, 0, 0) == -1 and b"null features" in lib.y3b_last_error()
+    assert fe(ctypes.byref(big), 1, 4, 1, 1, 1, 1, 0, 0) == -1 and b"shared memory" in lib.y3b_last_error()
+    odd_dot = ctypes_tables(arrays, tabs)
+    odd_dot.dot = ct.dot + 8
+    assert ff(ctypes.byref(odd_dot), 1, 4, 1, 0, 0) == -1 and b"aligned" in lib.y3b_last_error()

@@ -60,6 +60,8 @@ class RecoupledTables(ctypes.Structure):
         ("component_count", I64), ("cg_count", I64), ("own_count", I64), ("bp_count", I64),
         ("pass_begin", VP), ("comp", VP), ("cg_index", VP), ("cg_value", VP), ("own", VP),
         ("bp_begin", VP), ("bp_gi", VP), ("bp_other", VP), ("bp_value", VP),
+        ("feature_count", I64), ("feat_count", I64), ("dot_begin", VP), ("dot", VP), ("feat_index", VP),
+        ("feat_weight", VP),
     ]
 
 
@@ -103,6 +105,9 @@ _SIGS = {
     "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP, VP]),
     "y3b_ace_recoupled_energy_grad": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, I64, VP,
                                                      VP, VP, VP]),
+    "y3b_ace_recoupled_energy": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, I64, VP, VP,
+                                                VP]),
+    "y3b_ace_recoupled_features": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, VP]),
     "y3b_ace_edge_grad": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                          VP, VP]),
     "y3b_forces_gather": (ctypes.c_int, [VP, VP, I64, VP, VP, VP, VP]),

@@ -39,7 +39,56 @@ struct RecTabs {
   const int32_t* bp_gi;
   const int32_t* bp_other;
   const double* bp_value;
+  int64_t feature_count, feat_count;
+  const int32_t* dot_begin;
+  const int4* dot;  // (A's first local component, B's, feature range begin, count)
+  const int32_t* feat_index;
+  const double* feat_weight;
 };
+
+// Step 1 of a pass: the components [c0, c0 + nc) of the pass into sI from the
+// A row in sA (unit, copied channel, or Clebsch-Gordan coupled pair).
+__device__ __forceinline__ void build_components(const RecTabs& t, const double2* sA, double2* sI, int c0, int nc,
+                                                 int W, bool& bad) {
+  for (int c = threadIdx.x; c < nc; c += kRecThreads) {
+    const int4 d = __ldg(t.comp + 2 * (c0 + c));
+    double2 v = make_double2(0.0, 0.0);
+    if (d.x < 0) {
+      v.x = 1.0;
+    } else if (d.w == 0) {
+      if (d.x < W) v = sA[d.x];
+      else bad = true;
+    } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
+      bad = true;
+    } else {
+      for (int q = d.z; q < d.z + d.w; ++q) {
+        const int ix = __ldg(t.cg_index + q);
+        const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
+        if (ia >= W || ib < 0 || ib >= W) {
+          bad = true;
+          continue;
+        }
+        const double cv = __ldg(t.cg_value + q);
+        const double2 p = mul(sA[ia], sA[ib]);
+        v.x = fma(cv, p.x, v.x);
+        v.y = fma(cv, p.y, v.y);
+      }
+    }
+    sI[c] = v;
+  }
+}
+
+// Fixed-order block sum of one double per thread (warp shuffles, then the
+// warps in order); the result is valid in thread 0.
+__device__ __forceinline__ double block_sum(double v, double* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double s = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < kRecThreads / 32; ++w) s += red[w];
+  return s;
+}
 
 __global__ void __launch_bounds__(kRecThreads)
 recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
@@ -78,32 +127,7 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
         continue;
       }
       // 1. components
-      for (int c = tid; c < nc; c += kRecThreads) {
-        const int4 d = __ldg(t.comp + 2 * (c0 + c));
-        double2 v = make_double2(0.0, 0.0);
-        if (d.x < 0) {
-          v.x = 1.0;
-        } else if (d.w == 0) {
-          if (d.x < W) v = sA[d.x];
-          else bad = true;
-        } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
-          bad = true;
-        } else {
-          for (int q = d.z; q < d.z + d.w; ++q) {
-            const int ix = __ldg(t.cg_index + q);
-            const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
-            if (ia >= W || ib < 0 || ib >= W) {
-              bad = true;
-              continue;
-            }
-            const double cv = __ldg(t.cg_value + q);
-            const double2 p = mul(sA[ia], sA[ib]);
-            v.x = fma(cv, p.x, v.x);
-            v.y = fma(cv, p.y, v.y);
-          }
-        }
-        sI[c] = v;
-      }
+      build_components(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       // 2. adjoints of the components and the energy share
       for (int c = tid; c < nc; c += kRecThreads) {
@@ -164,14 +188,98 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
     }
     if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
     for (int i = tid; i < W; i += kRecThreads) G[atom * W + i] = sGA[i];
-    // energy: warp sums, then the warps in order (fixed order)
-    for (int o = 16; o > 0; o >>= 1) ep += __shfl_xor_sync(0xffffffffu, ep, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ep;
+    const double total = block_sum(ep, red);
+    if (tid == 0) energy[atom] = 0.5 * total;
     __syncthreads();
-    if (tid == 0) {
-      double s = 0.0;
-      for (int w = 0; w < kRecThreads / 32; ++w) s += red[w];
-      energy[atom] = 0.5 * s;
+  }
+}
+
+// Forward pass: per L the components, then every contraction of the pass once,
+// T_d = sum_M (-1)^M I_A[M] I_B[-M]; the energies e = Re(sum_d k[z, d] T_d)
+// (kFeatures false) or the features F[f] += W[f, d] T_d (kFeatures true: a word
+// has at most one contraction per L and a feature belongs to one word, so each
+// feature has one writer per pass and the passes are ordered by barriers).
+template <bool kFeatures>
+__global__ void __launch_bounds__(kRecThreads)
+recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
+                         const int32_t* __restrict__ species, const double* __restrict__ k, int64_t species_count,
+                         double* __restrict__ energy, double2* __restrict__ features, int32_t* status) {
+  extern __shared__ double2 rec_smem[];
+  __shared__ double red[kRecThreads / 32];
+  const int W = t.row_width;
+  double2* sA = rec_smem;  // [W]
+  double2* sI = sA + W;    // [max_pass_components]
+  const int tid = threadIdx.x;
+  for (int64_t atom = blockIdx.x; atom < atom_count; atom += gridDim.x) {
+    const double* kz = nullptr;
+    double2* Frow = nullptr;
+    if constexpr (kFeatures) {
+      Frow = features + atom * t.feature_count;
+      for (int64_t f = tid; f < t.feature_count; f += kRecThreads) Frow[f] = make_double2(0.0, 0.0);
+    } else {
+      int z = species[atom];
+      if (z < 0 || z >= species_count) {
+        if (tid == 0 && status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        z = 0;
+      }
+      kz = k + int64_t(z) * t.dot_count;
+    }
+    for (int i = tid; i < W; i += kRecThreads) sA[i] = A[atom * W + i];
+    double ep = 0.0;
+    bool bad = false;
+    __syncthreads();
+    for (int L = 0; L < t.pass_count; ++L) {
+      const int c0 = t.pass_begin[L];
+      const int nc = t.pass_begin[L + 1] - c0;
+      const int d0 = t.dot_begin[L];
+      const int nd = t.dot_begin[L + 1] - d0;
+      if (c0 < 0 || nc < 0 || nc > t.max_pass_components || int64_t(c0) + nc > t.component_count || d0 < 0 ||
+          nd < 0 || int64_t(d0) + nd > t.dot_count) {
+        bad = true;  // uniform over the block
+        continue;
+      }
+      build_components(t, sA, sI, c0, nc, W, bad);
+      __syncthreads();
+      for (int j = tid; j < nd; j += kRecThreads) {
+        const int4 q = __ldg(t.dot + d0 + j);
+        if (q.x < 0 || q.y < 0 || q.x + 2 * L >= nc || q.y + 2 * L >= nc) {
+          bad = true;
+          continue;
+        }
+        double2 T = make_double2(0.0, 0.0);
+        for (int m = 0; m <= 2 * L; ++m) {  // m = M + L
+          const double2 p = mul(sI[q.x + m], sI[q.y + 2 * L - m]);
+          const double sgn = ((m - L) & 1) ? -1.0 : 1.0;
+          T.x = fma(sgn, p.x, T.x);
+          T.y = fma(sgn, p.y, T.y);
+        }
+        if constexpr (kFeatures) {
+          if (q.z < 0 || q.w < 0 || int64_t(q.z) + q.w > t.feat_count) {
+            bad = true;
+            continue;
+          }
+          for (int z = q.z; z < q.z + q.w; ++z) {
+            const int f = __ldg(t.feat_index + z);
+            if (f < 0 || f >= t.feature_count) {
+              bad = true;
+              continue;
+            }
+            const double wv = __ldg(t.feat_weight + z);
+            double2 v = Frow[f];
+            v.x = fma(wv, T.x, v.x);
+            v.y = fma(wv, T.y, v.y);
+            Frow[f] = v;
+          }
+        } else {
+          ep = fma(__ldg(kz + d0 + j), T.x, ep);
+        }
+      }
+      __syncthreads();
+    }
+    if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
+    if constexpr (!kFeatures) {
+      const double total = block_sum(ep, red);
+      if (tid == 0) energy[atom] = total;
     }
     __syncthreads();
   }
@@ -182,22 +290,84 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
 
 using namespace y3b;
 
-extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
-                                             const int32_t* species, const double* contraction_weights,
-                                             int64_t species_count, double* energy, void* dEdA, int32_t* status,
-                                             void* stream) {
+namespace {
+
+int check_tables(const y3b_recoupled_tables* tables) {
   Y3B_CHECK_ARG(tables != nullptr, "null tables");
   const y3b_recoupled_tables& t = *tables;
   Y3B_CHECK_ARG(t.pass_count >= 1 && t.pass_count <= 64, "pass_count must be in [1, 64]");
   Y3B_CHECK_ARG(t.row_width >= 1 && t.row_width <= 4096, "row_width must be in [1, 4096]");
-  Y3B_CHECK_ARG(t.max_pass_components >= 1 && t.dot_count >= 1, "empty recoupled tables");
-  Y3B_CHECK_ARG(t.component_count >= 1 && t.cg_count >= 0 && t.own_count >= 0 && t.bp_count >= 0,
+  Y3B_CHECK_ARG(t.max_pass_components >= 1 && t.dot_count >= 1 && t.feature_count >= 1, "empty recoupled tables");
+  Y3B_CHECK_ARG(t.component_count >= 1 && t.cg_count >= 0 && t.own_count >= 0 && t.bp_count >= 0 &&
+                    t.feat_count >= 0,
                 "negative table sizes");
   Y3B_CHECK_ARG(t.pass_begin && t.comp && t.own && t.bp_begin && t.bp_gi && t.bp_other && t.bp_value &&
-                    (t.cg_count == 0 || (t.cg_index && t.cg_value)),
+                    t.dot_begin && t.dot && (t.cg_count == 0 || (t.cg_index && t.cg_value)) &&
+                    (t.feat_count == 0 || (t.feat_index && t.feat_weight)),
                 "null table pointer");
-  Y3B_CHECK_ARG(reinterpret_cast<uintptr_t>(t.comp) % 16 == 0 && reinterpret_cast<uintptr_t>(t.own) % 8 == 0,
-                "comp must be 16-byte and own 8-byte aligned");
+  Y3B_CHECK_ARG(reinterpret_cast<uintptr_t>(t.comp) % 16 == 0 && reinterpret_cast<uintptr_t>(t.dot) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(t.own) % 8 == 0,
+                "comp and dot must be 16-byte and own 8-byte aligned");
+  return Y3B_OK;
+}
+
+RecTabs device_view(const y3b_recoupled_tables& t) {
+  return RecTabs{t.pass_count, t.max_pass_components, t.row_width, t.dot_count,
+                 t.component_count, t.cg_count, t.own_count, t.bp_count,
+                 t.pass_begin, reinterpret_cast<const int4*>(t.comp), t.cg_index, t.cg_value,
+                 reinterpret_cast<const int2*>(t.own), t.bp_begin, t.bp_gi, t.bp_other, t.bp_value,
+                 t.feature_count, t.feat_count, t.dot_begin, reinterpret_cast<const int4*>(t.dot), t.feat_index,
+                 t.feat_weight};
+}
+
+template <bool kFeatures>
+int launch_forward(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count, const int32_t* species,
+                   const double* weights, int64_t species_count, double* energy, void* features, int32_t* status,
+                   void* stream) {
+  if (int rc = check_tables(tables)) return rc;
+  const y3b_recoupled_tables& t = *tables;
+  Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
+  if (atom_count == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(A != nullptr, "null A");
+  if (kFeatures) {
+    Y3B_CHECK_ARG(features != nullptr, "null features");
+  } else {
+    Y3B_CHECK_ARG(species && weights && energy && species_count > 0, "null pointer argument");
+  }
+  const size_t smem = size_t(int64_t(t.row_width) + int64_t(t.max_pass_components)) * sizeof(double2);
+  Y3B_CHECK_ARG(smem <= 224 * 1024, "recoupled pass needs %lld bytes of shared memory (max 224 KB)",
+                (long long)smem);
+  const int64_t grid = std::min<int64_t>(atom_count, int64_t(kSMs) * 64);
+  cudaStream_t s = as_stream(stream);
+  Y3B_CUDA_TRY(cudaFuncSetAttribute(recoupled_forward_kernel<kFeatures>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  recoupled_forward_kernel<kFeatures><<<int(grid), kRecThreads, smem, s>>>(
+      device_view(t), static_cast<const double2*>(A), atom_count, species, weights, species_count, energy,
+      static_cast<double2*>(features), status);
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
+}  // namespace
+
+extern "C" int y3b_ace_recoupled_energy(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                                        const int32_t* species, const double* contraction_weights,
+                                        int64_t species_count, double* energy, int32_t* status, void* stream) {
+  return launch_forward<false>(tables, A, atom_count, species, contraction_weights, species_count, energy, nullptr,
+                               status, stream);
+}
+
+extern "C" int y3b_ace_recoupled_features(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                                          void* features, int32_t* status, void* stream) {
+  return launch_forward<true>(tables, A, atom_count, nullptr, nullptr, 0, nullptr, features, status, stream);
+}
+
+extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                                             const int32_t* species, const double* contraction_weights,
+                                             int64_t species_count, double* energy, void* dEdA, int32_t* status,
+                                             void* stream) {
+  if (int rc = check_tables(tables)) return rc;
+  const y3b_recoupled_tables& t = *tables;
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && contraction_weights && energy && dEdA && species_count > 0,
@@ -205,17 +375,13 @@ extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables,
   const size_t smem = size_t(2 * int64_t(t.row_width) + 2 * int64_t(t.max_pass_components)) * sizeof(double2);
   Y3B_CHECK_ARG(smem <= 224 * 1024, "recoupled pass needs %lld bytes of shared memory (max 224 KB)",
                 (long long)smem);
-  RecTabs rt{t.pass_count, t.max_pass_components, t.row_width, t.dot_count,
-             t.component_count, t.cg_count, t.own_count, t.bp_count,
-             t.pass_begin, reinterpret_cast<const int4*>(t.comp), t.cg_index, t.cg_value,
-             reinterpret_cast<const int2*>(t.own), t.bp_begin, t.bp_gi, t.bp_other, t.bp_value};
   const int64_t grid = std::min<int64_t>(atom_count, int64_t(kSMs) * 64);
   cudaStream_t s = as_stream(stream);
   Y3B_CUDA_TRY(cudaFuncSetAttribute(recoupled_energy_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(smem)));
   recoupled_energy_grad_kernel<<<int(grid), kRecThreads, smem, s>>>(
-      rt, static_cast<const double2*>(A), atom_count, species, contraction_weights, species_count, energy,
-      static_cast<double2*>(dEdA), status);
+      device_view(t), static_cast<const double2*>(A), atom_count, species, contraction_weights, species_count,
+      energy, static_cast<double2*>(dEdA), status);
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }

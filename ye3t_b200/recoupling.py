@@ -48,7 +48,7 @@ import numpy as np
 
 from .schedules import ACEBundle, ScheduleRecord, SymPowerTable
 
-__all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "RecoupledDeviceTables", "RecoupledEnergyGrad",
+__all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "RecoupledDeviceTables", "RecoupledEvaluator",
            "build_recoupled_plan", "ctypes_tables", "SEG_UNIT", "SEG_CHANNEL", "SEG_PAIR"]
 
 SEG_UNIT, SEG_CHANNEL, SEG_PAIR = 0, 1, 2
@@ -301,6 +301,11 @@ class RecoupledDeviceTables:
     bp_gi: np.ndarray       # int32 [Bp]
     bp_other: np.ndarray    # int32 [Bp]
     bp_value: np.ndarray    # float64 [Bp]
+    feature_count: int = 0
+    dot_begin: np.ndarray = None    # int32 [pass_count + 1] contractions of each pass
+    dot: np.ndarray = None          # int32 [D, 4]: first local component of A, of B, feature range
+    feat_index: np.ndarray = None   # int32 [Z]
+    feat_weight: np.ndarray = None  # float64 [Z]
 
     def validate(self) -> None:
         """Every index the device pass follows stays inside its array or its pass."""
@@ -348,6 +353,19 @@ class RecoupledDeviceTables:
             raise ValueError("back-propagation entry outside its pass")
         if np.any(self.bp_other >= W) or np.any(self.bp_other < -1):
             raise ValueError("back-propagation partner outside the A row")
+        db = self.dot_begin.astype(np.int64)
+        if db.shape != (P + 1,) or db[0] != 0 or np.any(np.diff(db) < 0) or db[-1] != self.dot_count \
+                or self.dot.shape != (self.dot_count, 4):
+            raise ValueError("dot_begin does not partition the contractions")
+        dt = self.dot.astype(np.int64)
+        Ld = np.repeat(np.arange(P), np.diff(db))
+        ncd = np.diff(pb)[Ld]
+        if np.any(dt[:, :2] < 0) or np.any(dt[:, 0] + 2 * Ld >= ncd) or np.any(dt[:, 1] + 2 * Ld >= ncd):
+            raise ValueError("contraction segment outside its pass")
+        if np.any(dt[:, 2] < 0) or np.any(dt[:, 3] < 0) or np.any(dt[:, 2] + dt[:, 3] > self.feat_index.shape[0]):
+            raise ValueError("contraction feature range outside the feature table")
+        if np.any(self.feat_index < 0) or np.any(self.feat_index >= self.feature_count):
+            raise ValueError("feature index outside the features")
 
     def smem_bytes(self) -> int:
         """Dynamic shared memory of the device pass: the A row and its adjoint, the pass's
@@ -418,7 +436,14 @@ def _device_tables(plan: "RecoupledPlan") -> RecoupledDeviceTables:
             comp[c] = row
     bp_flat = [e for L in range(P) for t in range(row_width) for e in bp[L][t]]
     bp_begin = np.concatenate([[0], np.cumsum([len(bp[L][t]) for L in range(P) for t in range(row_width)])])
+    dot_begin = np.searchsorted(plan.dot_L, np.arange(P + 1), side="left").astype(np.int64)
+    dot_pass = plan.dot_L.astype(np.int64)
+    dot = np.stack([seg_off[plan.dot_a] - pass_begin[dot_pass], seg_off[plan.dot_b] - pass_begin[dot_pass],
+                    plan.dot_feat_offset[:-1], np.diff(plan.dot_feat_offset)], axis=1) if plan.dot_count else \
+        np.zeros((0, 4), dtype=np.int64)
     tabs = RecoupledDeviceTables(
+        feature_count=plan.feature_count, dot_begin=dot_begin.astype(np.int32), dot=dot.astype(np.int32),
+        feat_index=plan.feat_index.astype(np.int32), feat_weight=np.ascontiguousarray(plan.feat_weight),
         pass_count=P, max_pass_components=int(np.diff(pass_begin).max(initial=0)), row_width=row_width,
         dot_count=plan.dot_count, pass_begin=pass_begin.astype(np.int32), comp=comp.astype(np.int32),
         cg_index=np.asarray(cg_index, dtype=np.int32), cg_value=np.asarray(cg_value, dtype=np.float64),
@@ -504,42 +529,90 @@ def ctypes_tables(arrays: Dict[str, "object"], tabs: RecoupledDeviceTables):
         pass_count=tabs.pass_count, max_pass_components=tabs.max_pass_components, row_width=tabs.row_width,
         dot_count=tabs.dot_count, component_count=int(tabs.comp.shape[0]), cg_count=int(tabs.cg_value.shape[0]),
         own_count=int(tabs.own.shape[0]), bp_count=int(tabs.bp_gi.shape[0]),
+        feature_count=tabs.feature_count, feat_count=int(tabs.feat_index.shape[0]),
         **{name: arrays[name].data_ptr() for name in _TABLE_ARRAYS})
 
 
-_TABLE_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value")
+_TABLE_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
+                 "dot_begin", "dot", "feat_index", "feat_weight")
 
 
-class RecoupledEnergyGrad:
-    """Per-atom energies and ``G = dE/dA`` through the recoupled plan on one GPU
-    (``y3b_ace_recoupled_energy_grad``): the tables and the per-species contraction
-    weights are uploaded once; each call takes ``A [n, nmax, (lmax+1)^2]`` complex128
-    and the atoms' species, like ``ACEEvaluator.energy_grad``."""
+class RecoupledEvaluator:
+    """The recoupled passes on one GPU: the tables and the per-species contraction weights
+    are uploaded once; each call takes ``A [n, nmax, (lmax+1)^2]`` complex128 (and the
+    atoms' species), like ``ACEEvaluator``'s ``energy_grad`` / ``energy_from_density`` /
+    ``features``."""
 
-    def __init__(self, bundle: ACEBundle, device, weights: np.ndarray, plan: "RecoupledPlan" = None):
+    def __init__(self, bundle: ACEBundle, device, weights: np.ndarray = None, plan: "RecoupledPlan" = None):
         import torch
         self.device = torch.device(device)
         self.plan = plan if plan is not None else build_recoupled_plan(bundle)
         self.tables = self.plan.device_tables()
         self.arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(self.tables, name))).to(self.device)
                        for name in _TABLE_ARRAYS}
-        self.weights = torch.as_tensor(self.plan.energy_weights(weights)).to(self.device).contiguous()
+        self.weights = None if weights is None else \
+            torch.as_tensor(self.plan.energy_weights(weights)).to(self.device).contiguous()
         self._c = ctypes_tables(self.arrays, self.tables)
 
+    def _rows(self, A):
+        import torch
+        from . import _native as nat
+        A = A.to(self.device, torch.complex128).contiguous()
+        if A.ndim < 1 or A.shape[1:].numel() != self.tables.row_width:
+            raise ValueError(f"A rows must hold {self.tables.row_width} complex entries")
+        nat.require_cuda(A, what="recoupled pass")
+        return A
+
+    def _species(self, species, n):
+        import torch
+        if self.weights is None:
+            raise ValueError("weights are required for the energy")
+        sp = species.to(self.device, torch.int32).contiguous()
+        if sp.shape != (n,):
+            raise ValueError("one species per atom is required")
+        return sp
+
     def energy_grad(self, A, species, status=None):
+        """(per-atom energies, ``G = dE/dA``)."""
         import ctypes
 
         import torch
         from . import _native as nat
-        A = A.to(self.device, torch.complex128).contiguous()
+        A = self._rows(A)
         n = A.shape[0]
-        if A.shape[1:].numel() != self.tables.row_width:
-            raise ValueError(f"A rows must hold {self.tables.row_width} complex entries")
-        sp = species.to(self.device, torch.int32).contiguous()
-        nat.require_cuda(A, sp, what="recoupled energy_grad")
+        sp = self._species(species, n)
         e = torch.empty(n, dtype=torch.float64, device=self.device)
         G = torch.empty_like(A)
         nat.check(nat.lib().y3b_ace_recoupled_energy_grad(
             ctypes.byref(self._c), A.data_ptr(), n, sp.data_ptr(), self.weights.data_ptr(), self.weights.shape[0],
             e.data_ptr(), G.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), "ace_recoupled_energy_grad")
         return e, G
+
+    def energy(self, A, species, status=None):
+        """Per-atom energies."""
+        import ctypes
+
+        import torch
+        from . import _native as nat
+        A = self._rows(A)
+        n = A.shape[0]
+        sp = self._species(species, n)
+        e = torch.empty(n, dtype=torch.float64, device=self.device)
+        nat.check(nat.lib().y3b_ace_recoupled_energy(
+            ctypes.byref(self._c), A.data_ptr(), n, sp.data_ptr(), self.weights.data_ptr(), self.weights.shape[0],
+            e.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), "ace_recoupled_energy")
+        return e
+
+    def features(self, A, status=None):
+        """Features ``[n, feature_count]`` complex128 in the bundle's order."""
+        import ctypes
+
+        import torch
+        from . import _native as nat
+        A = self._rows(A)
+        n = A.shape[0]
+        F = torch.empty((n, self.tables.feature_count), dtype=torch.complex128, device=self.device)
+        nat.check(nat.lib().y3b_ace_recoupled_features(
+            ctypes.byref(self._c), A.data_ptr(), n, F.data_ptr(), nat.ptr(status), nat.stream_of(self.device)),
+            "ace_recoupled_features")
+        return F
