@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--config", default="c5", choices=["c5", "c3", "c3f32", "c4"],
                     help="c5 (default): the headline 2^20-atom energy + forces step; c3/c3f32/c4: the "
                          "channel-diagonal descriptor configurations (mixed radial channels)")
+    ap.add_argument("--recoupled", action="store_true",
+                    help="B-basis through the recoupled passes (ye3t_b200.recoupling) instead of the "
+                         "term-level schedule kernels")
     ap.add_argument("--energy-only", action="store_true",
                     help="time the energy step alone (no adjoint, no forces)")
     return ap.parse_args()
@@ -205,6 +208,8 @@ def _config(args):
                         "linear readout",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
             "parallelism": f"atom-block x{args.gpus}",
+            "b_basis": "recoupled pair contractions" if getattr(args, "recoupled", False) else
+                       "term-level factorized schedules",
             "l2": "inputs larger than L2 (A-basis 2 GB, neighbour list 110 MB at 2^20 atoms)"}
 
 
@@ -245,7 +250,12 @@ def run_b200(args):
     # B-basis energy, or the B-basis adjoint (one launch per item class) + edge
     # gradients + force gather/scatter
     from ye3t_b200.packing import GRAD_CLASSES
-    launches_per_step = 8 + (GRAD_CLASSES + 2 if forces else 1)
+    rec = None
+    if args.recoupled:
+        from ye3t_b200.recoupling import RecoupledEvaluator
+        rec = RecoupledEvaluator(bundle, device, weights)
+    b_launches = 1 if rec is not None else GRAD_CLASSES
+    launches_per_step = 8 + (b_launches + 2 if forces else 1)
 
     def step(record):
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] if record else None
@@ -259,10 +269,11 @@ def run_b200(args):
         A = ev.density(pos_d, sp_d, box, row, nbr, begin)
         mark(2)
         if not forces:
-            e_at = ev.energy_from_density(A, sp_d[begin:end], out=e_buf)
+            e_at = rec.energy(A, sp_d[begin:end]) if rec is not None else \
+                ev.energy_from_density(A, sp_d[begin:end], out=e_buf)
             mark(3)
             return sum_over_ranks(e_at.sum()), None, marks
-        e_at, G = ev.energy_grad(A, sp_d[begin:end])
+        e_at, G = rec.energy_grad(A, sp_d[begin:end]) if rec is not None else ev.energy_grad(A, sp_d[begin:end])
         mark(3)
         g = ev.edge_grad(pos_d, sp_d, box, row, nbr, G, begin=begin)
         mark(4)
@@ -328,6 +339,9 @@ def run_b200(args):
     flops = ev.packed.flops_per_atom()
     kern_ms = statistics.mean(timers["energy_grad" if forces else "energy"])
     kern_flops = (flops["items_grad"] if forces else flops["items"]) + 2.0 * ev.feature_count
+    if rec is not None:
+        rflops = rec.tables.flops_per_atom()
+        kern_flops = rflops["energy_grad" if forces else "energy"]
     sched_flops_launch = kern_flops * n_local
     term_flops_launch = (flops["terms"] + 2.0 * ev.feature_count) * n_local
     achieved = sched_flops_launch / (kern_ms * 1e-3) / 1e12
@@ -344,7 +358,7 @@ def run_b200(args):
         hbm_peak, hbm_src = 6650.0, "fallback 6.65 TB/s"
     traffic = None
     tpath = os.path.join(REPO, "profiles", "ace_grad_traffic.json" if forces else "ace_energy_traffic.json")
-    if os.path.exists(tpath):
+    if rec is None and os.path.exists(tpath):
         with open(tpath) as fh:
             t = json.load(fh)
         traffic = t.get("dram_bytes_per_atom", 0) * n_local or None
@@ -367,15 +381,21 @@ def run_b200(args):
                 "d2h_bytes_per_step": 8 + (N * 24 if forces else 0)},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": "fp64",
-                     "kernel": ("ace_grad_kernel (B-basis energy + dE/dA)" if forces
-                                else "ace_eval_kernel<1> (B-basis energy, symmetric blocks on chip)"),
+                     "kernel": (("recoupled_energy_grad_kernel (B-basis energy + dE/dA, recoupled)" if forces
+                                 else "recoupled_forward_kernel<false> (B-basis energy, recoupled)")
+                                if rec is not None else
+                                ("ace_grad_kernel (B-basis energy + dE/dA)" if forces
+                                 else "ace_eval_kernel<1> (B-basis energy, symmetric blocks on chip)")),
                      "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "flops_per_launch": sched_flops_launch,
-                     "flops_note": "FP64 flops the item walk needs on valid tuples "
-                                   "(ye3t_b200.packing.item_grad_flops_per_atom with forces, "
-                                   "item_flops_per_atom without) plus the readout; the reference's "
-                                   "forward term-by-term count for the same features is "
+                     "flops_note": ("FP64 flops of the recoupled pass counted from its tables "
+                                    "(ye3t_b200.recoupling.RecoupledDeviceTables.flops_per_atom)"
+                                    if rec is not None else
+                                    "FP64 flops the item walk needs on valid tuples "
+                                    "(ye3t_b200.packing.item_grad_flops_per_atom with forces, "
+                                    "item_flops_per_atom without) plus the readout") +
+                                   "; the reference's forward term-by-term count for the same features is "
                                    f"{term_flops_launch:.4g} per launch",
                      "peak_source": "FP64 FMA microbenchmark (y3b_fma_peak_launch) measured in this run; "
                                     "MEASURED_PEAKS.json has no FP64 figure"},

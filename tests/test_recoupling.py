@@ -120,6 +120,9 @@ def test_device_tables_walk_matches_oracle_and_validation_catches_damage(plan5):
     assert (tabs.pass_count, tabs.max_pass_components, tabs.row_width, tabs.dot_count) == (7, 2184, 128, 41168)
     assert tabs.smem_bytes() == 16 * (2 * 128 + 2 * 2184)
     assert tabs.dot_begin.tolist() == [0, 9260, 21018, 33932, 38500, 40888, 40958, 41168]
+    # per-atom work of the passes, against 17.7 M (forward) / 33.7 M (adjoint) flops of the term-level walk
+    fl = tabs.flops_per_atom()
+    assert fl["energy"] < 1.7e6 and fl["energy_grad"] < 2.0e6 and fl["features"] < 1.8e6
     rng = np.random.default_rng(12)
     A = rng.normal(size=(3, 8, 16)) + 1j * rng.normal(size=(3, 8, 16))
     species = np.array([1, 0, 2], dtype=np.int32)

@@ -367,6 +367,22 @@ class RecoupledDeviceTables:
         if np.any(self.feat_index < 0) or np.any(self.feat_index >= self.feature_count):
             raise ValueError("feature index outside the features")
 
+    def flops_per_atom(self) -> Dict[str, float]:
+        """Real flops per atom of each pass, counted from the tables: a coupling term is a
+        complex product scaled and added (10), a contraction term a complex multiply-add (8),
+        an adjoint-list term a real weight times a complex value added (4), a coupled
+        back-propagation term 10 and a copied one 2; the energy takes 2 per contraction
+        (forward) or 4 per component (adjoint), a feature weight 4."""
+        terms = float(self.comp[:, 3].astype(np.int64).sum())
+        lists = float(self.comp[:, 6].astype(np.int64).sum())
+        dot_L = np.repeat(np.arange(self.pass_count), np.diff(self.dot_begin.astype(np.int64)))
+        macs = float((2 * dot_L + 1).sum())
+        coupled = float((self.bp_other >= 0).sum())
+        copied = float((self.bp_other < 0).sum())
+        return {"energy": 10 * terms + 8 * macs + 2 * self.dot_count,
+                "energy_grad": 10 * terms + 4 * lists + 4 * self.comp.shape[0] + 10 * coupled + 2 * copied,
+                "features": 10 * terms + 8 * macs + 4 * float(self.feat_index.shape[0])}
+
     def smem_bytes(self) -> int:
         """Dynamic shared memory of the device pass: the A row and its adjoint, the pass's
         components and theirs."""
