@@ -509,8 +509,14 @@ def build_recoupled_plan(bundle: ACEBundle, seed: int = 20260) -> RecoupledPlan:
                      if abs(W[d, c]) > 1e-14 * max(float(np.abs(W).max()), 1e-300)]
             dots.append((L, seg_of(sa, L), seg_of(sb, L), w, feats))
 
-    # segments ordered by L (then first appearance); contractions by L, then first segment
-    order = sorted(range(len(segs)), key=lambda s: (segs[s][1], s))
+    # segments ordered by L, then by how many contractions use them (longest first, so that
+    # a warp's components walk lists of similar length), then first appearance; contractions
+    # by L, then first segment
+    uses = np.zeros(len(segs), dtype=np.int64)
+    for _, a, b, _, _ in dots:
+        uses[a] += 1
+        uses[b] += 1
+    order = sorted(range(len(segs)), key=lambda s: (segs[s][1], -int(uses[s]), s))
     rank = np.empty(len(segs), dtype=np.int64)
     rank[np.asarray(order, dtype=np.int64)] = np.arange(len(segs))
     kinds = np.asarray([segs[s][0] for s in order], dtype=np.int8)
