@@ -177,3 +177,15 @@ def test_recoupled_entry_point_checks_arguments_without_gpu(plan3):
     odd_dot = ctypes_tables(arrays, tabs)
     odd_dot.dot = ct.dot + 8
     assert ff(ctypes.byref(odd_dot), 1, 4, 1, 0, 0) == -1 and b"aligned" in lib.y3b_last_error()
+
+
+def test_plan_covers_channel_diagonal_l4_bundle():
+    """The channel-diagonal nu <= 4, l <= 4 word set (intermediate L up to 8) recouples too."""
+    from oracle import oracle
+    b = _bundle("ace_diag_l4_nu4_L0")
+    tabs = build_recoupled_plan(b).device_tables()
+    assert tabs.pass_count == 7 and tabs.row_width == 25
+    rng = np.random.default_rng(13)
+    A = rng.normal(size=(6, 1, 25)) + 1j * rng.normal(size=(6, 1, 25))
+    F0 = oracle.bundle_features(b, A, threads=2)
+    assert np.abs(rn.walk_forward(tabs, A) - F0).max() <= 1e-12 * np.abs(F0).max()
