@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--recoupled", action="store_true",
                     help="B-basis through the recoupled passes (ye3t_b200.recoupling) instead of the "
                          "term-level schedule kernels")
+    ap.add_argument("--recoupled-atoms", type=int, default=1,
+                    help="atoms per CTA of the recoupled passes (1-4, within shared memory)")
     ap.add_argument("--energy-only", action="store_true",
                     help="time the energy step alone (no adjoint, no forces)")
     return ap.parse_args()
@@ -208,8 +210,8 @@ def _config(args):
                         "linear readout",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
             "parallelism": f"atom-block x{args.gpus}",
-            "b_basis": "recoupled pair contractions" if getattr(args, "recoupled", False) else
-                       "term-level factorized schedules",
+            "b_basis": (f"recoupled pair contractions ({args.recoupled_atoms} atoms per CTA)"
+                        if getattr(args, "recoupled", False) else "term-level factorized schedules"),
             "l2": "inputs larger than L2 (A-basis 2 GB, neighbour list 110 MB at 2^20 atoms)"}
 
 
@@ -253,7 +255,7 @@ def run_b200(args):
     rec = None
     if args.recoupled:
         from ye3t_b200.recoupling import RecoupledEvaluator
-        rec = RecoupledEvaluator(bundle, device, weights)
+        rec = RecoupledEvaluator(bundle, device, weights, atoms_per_cta=args.recoupled_atoms)
     b_launches = 1 if rec is not None else GRAD_CLASSES
     launches_per_step = 8 + (b_launches + 2 if forces else 1)
 

@@ -177,6 +177,27 @@ def test_recoupled_entry_point_checks_arguments_without_gpu(plan3):
     odd_dot = ctypes_tables(arrays, tabs)
     odd_dot.dot = ct.dot + 8
     assert ff(ctypes.byref(odd_dot), 1, 4, 1, 0, 0) == -1 and b"aligned" in lib.y3b_last_error()
+    many = ctypes_tables(arrays, tabs)
+    many.atoms_per_cta = 5
+    assert f(ctypes.byref(many), 1, 4, 1, 1, 1, 1, 1, 0, 0) == -1 and b"atoms_per_cta" in lib.y3b_last_error()
+
+
+def test_recoupled_atoms_per_cta_limited_by_shared_memory(plan5):
+    """Four C5 atoms per CTA would need 296 KB of shared memory for the adjoint: refused
+    before any CUDA call (three fit: 222 KB)."""
+    import ctypes
+
+    import torch
+    from ye3t_b200 import _native
+    from ye3t_b200.recoupling import _TABLE_ARRAYS, ctypes_tables
+    tabs = plan5[1].device_tables()
+    assert 3 * tabs.smem_bytes() <= 224 * 1024 < 4 * tabs.smem_bytes()
+    arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(tabs, name))) for name in _TABLE_ARRAYS}
+    ct = ctypes_tables(arrays, tabs)
+    ct.atoms_per_cta = 4
+    lib = _native.lib()
+    assert lib.y3b_ace_recoupled_energy_grad(ctypes.byref(ct), 1, 4, 1, 1, 1, 1, 1, 0, 0) == -1
+    assert b"4 atoms per CTA" in lib.y3b_last_error()
 
 
 def test_plan_covers_channel_diagonal_l4_bundle():

@@ -46,38 +46,6 @@ struct RecTabs {
   const double* feat_weight;
 };
 
-// Step 1 of a pass: the components [c0, c0 + nc) of the pass into sI from the
-// A row in sA (unit, copied channel, or Clebsch-Gordan coupled pair).
-__device__ __forceinline__ void build_components(const RecTabs& t, const double2* sA, double2* sI, int c0, int nc,
-                                                 int W, bool& bad) {
-  for (int c = threadIdx.x; c < nc; c += kRecThreads) {
-    const int4 d = __ldg(t.comp + 2 * (c0 + c));
-    double2 v = make_double2(0.0, 0.0);
-    if (d.x < 0) {
-      v.x = 1.0;
-    } else if (d.w == 0) {
-      if (d.x < W) v = sA[d.x];
-      else bad = true;
-    } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
-      bad = true;
-    } else {
-      for (int q = d.z; q < d.z + d.w; ++q) {
-        const int ix = __ldg(t.cg_index + q);
-        const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
-        if (ia >= W || ib < 0 || ib >= W) {
-          bad = true;
-          continue;
-        }
-        const double cv = __ldg(t.cg_value + q);
-        const double2 p = mul(sA[ia], sA[ib]);
-        v.x = fma(cv, p.x, v.x);
-        v.y = fma(cv, p.y, v.y);
-      }
-    }
-    sI[c] = v;
-  }
-}
-
 // Fixed-order block sum of one double per thread (warp shuffles, then the
 // warps in order); the result is valid in thread 0.
 __device__ __forceinline__ double block_sum(double v, double* red) {
@@ -90,6 +58,79 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   return s;
 }
 
+// Shared-memory arrays hold NA atoms side by side: entry e of atom a at
+// [e * NA + a].  A CTA takes atoms [g NA, g NA + NA); every table entry it
+// loads (coupling term, contraction-list entry, back-propagation entry,
+// contraction) serves all NA atoms, and the NA sums are independent chains.
+template <int NA>
+__device__ __forceinline__ void build_components(const RecTabs& t, const double2* sA, double2* sI, int c0, int nc,
+                                                 int W, bool& bad) {
+  for (int c = threadIdx.x; c < nc; c += kRecThreads) {
+    const int4 d = __ldg(t.comp + 2 * (c0 + c));
+    double2 v[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) v[a] = make_double2(d.x < 0 ? 1.0 : 0.0, 0.0);
+    if (d.x < 0) {
+    } else if (d.w == 0) {
+      if (d.x < W) {
+#pragma unroll
+        for (int a = 0; a < NA; ++a) v[a] = sA[d.x * NA + a];
+      } else {
+        bad = true;
+      }
+    } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
+      bad = true;
+    } else {
+      for (int q = d.z; q < d.z + d.w; ++q) {
+        const int ix = __ldg(t.cg_index + q);
+        const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
+        if (ia >= W || ib < 0 || ib >= W) {
+          bad = true;
+          continue;
+        }
+        const double cv = __ldg(t.cg_value + q);
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+          const double2 p = mul(sA[ia * NA + a], sA[ib * NA + a]);
+          v[a].x = fma(cv, p.x, v[a].x);
+          v[a].y = fma(cv, p.y, v[a].y);
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NA; ++a) sI[c * NA + a] = v[a];
+  }
+}
+
+// The CTA's atoms: count of valid ones, their weight rows (species outside
+// the range set the status and use species 0), and their A rows in sA.
+template <int NA>
+__device__ __forceinline__ int load_atoms(int64_t first, int64_t atom_count, int W, const double2* A,
+                                          const int32_t* species, const double* k, int64_t species_count,
+                                          int32_t dot_count, double2* sA, double2* sGA, const double** kz,
+                                          int32_t* status) {
+  const int nv = int(atom_count - first < NA ? atom_count - first : NA);
+#pragma unroll
+  for (int a = 0; a < NA; ++a) {
+    int z = 0;
+    if (species != nullptr && a < nv) {
+      z = species[first + a];
+      if (z < 0 || z >= species_count) {
+        if (threadIdx.x == 0 && status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        z = 0;
+      }
+    }
+    kz[a] = k == nullptr ? nullptr : k + int64_t(z) * dot_count;
+  }
+  for (int i = threadIdx.x; i < W * NA; i += kRecThreads) {
+    const int a = i % NA, e = i / NA;
+    sA[i] = a < nv ? A[(first + a) * W + e] : make_double2(0.0, 0.0);
+    if (sGA != nullptr) sGA[i] = make_double2(0.0, 0.0);
+  }
+  return nv;
+}
+
+template <int NA>
 __global__ void __launch_bounds__(kRecThreads)
 recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
                              const int32_t* __restrict__ species, const double* __restrict__ k,
@@ -99,24 +140,20 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
   __shared__ double red[kRecThreads / 32];
   const int W = t.row_width;
   const int maxc = t.max_pass_components;
-  double2* sA = rec_smem;      // [W] the atom's A row
-  double2* sGA = sA + W;       // [W] dE/dA of the row
-  double2* sI = sGA + W;       // [maxc] components of the pass
-  double2* sG = sI + maxc;     // [maxc] their adjoints
+  double2* sA = rec_smem;          // [W][NA] the atoms' A rows
+  double2* sGA = sA + W * NA;      // [W][NA] dE/dA of the rows
+  double2* sI = sGA + W * NA;      // [maxc][NA] components of the pass
+  double2* sG = sI + maxc * NA;    // [maxc][NA] their adjoints
   const int tid = threadIdx.x;
-  for (int64_t atom = blockIdx.x; atom < atom_count; atom += gridDim.x) {
-    int z = species[atom];
-    if (z < 0 || z >= species_count) {
-      if (tid == 0 && status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
-      z = 0;
-    }
-    const double* kz = k + int64_t(z) * t.dot_count;
-    const double2* Arow = A + atom * W;
-    for (int i = tid; i < W; i += kRecThreads) {
-      sA[i] = Arow[i];
-      sGA[i] = make_double2(0.0, 0.0);
-    }
-    double ep = 0.0;
+  const int64_t groups = (atom_count + NA - 1) / NA;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t first = grp * NA;
+    const double* kz[NA];
+    const int nv = load_atoms<NA>(first, atom_count, W, A, species, k, species_count, t.dot_count, sA, sGA, kz,
+                                  status);
+    double ep[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) ep[a] = 0.0;
     bool bad = false;
     __syncthreads();
     for (int L = 0; L < t.pass_count; ++L) {
@@ -127,12 +164,14 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
         continue;
       }
       // 1. components
-      build_components(t, sA, sI, c0, nc, W, bad);
+      build_components<NA>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
-      // 2. adjoints of the components and the energy share
+      // 2. adjoints of the components and the energy shares
       for (int c = tid; c < nc; c += kRecThreads) {
         const int4 d = __ldg(t.comp + 2 * (c0 + c) + 1);
-        double2 acc = make_double2(0.0, 0.0);
+        double2 acc[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) acc[a] = make_double2(0.0, 0.0);
         if (d.y < 0 || d.z < 0 || int64_t(d.y) + d.z > t.own_count) {
           bad = true;
         } else {
@@ -144,23 +183,28 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
               bad = true;
               continue;
             }
-            const double kk = __ldg(kz + e.y);
-            const double2 v = sI[p];
-            acc.x = fma(kk, v.x, acc.x);
-            acc.y = fma(kk, v.y, acc.y);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              const double kk = __ldg(kz[a] + e.y);
+              const double2 v = sI[p * NA + a];
+              acc[a].x = fma(kk, v.x, acc[a].x);
+              acc[a].y = fma(kk, v.y, acc[a].y);
+            }
           }
         }
-        if ((d.x - L) & 1) {
-          acc.x = -acc.x;
-          acc.y = -acc.y;
+        const double sgn = ((d.x - L) & 1) ? -1.0 : 1.0;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+          acc[a].x *= sgn;
+          acc[a].y *= sgn;
+          sG[c * NA + a] = acc[a];
+          const double2 iv = sI[c * NA + a];
+          ep[a] = fma(iv.x, acc[a].x, ep[a]);
+          ep[a] = fma(-iv.y, acc[a].y, ep[a]);
         }
-        sG[c] = acc;
-        const double2 iv = sI[c];
-        ep = fma(iv.x, acc.x, ep);
-        ep = fma(-iv.y, acc.y, ep);
       }
       __syncthreads();
-      // 3. back-propagation into the A row (each entry owns its sum)
+      // 3. back-propagation into the A rows (each entry owns its sum)
       for (int i = tid; i < W; i += kRecThreads) {
         const int64_t at = int64_t(L) * W + i;
         const int b0 = t.bp_begin[at], b1 = t.bp_begin[at + 1];
@@ -168,7 +212,9 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
           bad = true;
           continue;
         }
-        double2 ga = sGA[i];
+        double2 ga[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) ga[a] = sGA[i * NA + a];
         for (int q = b0; q < b1; ++q) {
           const int gi = __ldg(t.bp_gi + q);
           const int o = __ldg(t.bp_other + q);
@@ -177,20 +223,30 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
             continue;
           }
           const double cv = __ldg(t.bp_value + q);
-          const double2 g = sG[gi];
-          const double2 term = o < 0 ? g : mul(g, sA[o]);
-          ga.x = fma(cv, term.x, ga.x);
-          ga.y = fma(cv, term.y, ga.y);
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            const double2 g = sG[gi * NA + a];
+            const double2 term = o < 0 ? g : mul(g, sA[o * NA + a]);
+            ga[a].x = fma(cv, term.x, ga[a].x);
+            ga[a].y = fma(cv, term.y, ga[a].y);
+          }
         }
-        sGA[i] = ga;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) sGA[i * NA + a] = ga[a];
       }
       __syncthreads();
     }
     if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
-    for (int i = tid; i < W; i += kRecThreads) G[atom * W + i] = sGA[i];
-    const double total = block_sum(ep, red);
-    if (tid == 0) energy[atom] = 0.5 * total;
-    __syncthreads();
+    for (int i = tid; i < W * NA; i += kRecThreads) {
+      const int a = i % NA, e = i / NA;
+      if (a < nv) G[(first + a) * W + e] = sGA[i];
+    }
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      const double total = block_sum(ep[a], red);
+      if (tid == 0 && a < nv) energy[first + a] = 0.5 * total;
+      __syncthreads();
+    }
   }
 }
 
@@ -199,7 +255,7 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
 // (kFeatures false) or the features F[f] += W[f, d] T_d (kFeatures true: a word
 // has at most one contraction per L and a feature belongs to one word, so each
 // feature has one writer per pass and the passes are ordered by barriers).
-template <bool kFeatures>
+template <bool kFeatures, int NA>
 __global__ void __launch_bounds__(kRecThreads)
 recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
                          const int32_t* __restrict__ species, const double* __restrict__ k, int64_t species_count,
@@ -207,25 +263,22 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
   extern __shared__ double2 rec_smem[];
   __shared__ double red[kRecThreads / 32];
   const int W = t.row_width;
-  double2* sA = rec_smem;  // [W]
-  double2* sI = sA + W;    // [max_pass_components]
+  double2* sA = rec_smem;     // [W][NA]
+  double2* sI = sA + W * NA;  // [max_pass_components][NA]
   const int tid = threadIdx.x;
-  for (int64_t atom = blockIdx.x; atom < atom_count; atom += gridDim.x) {
-    const double* kz = nullptr;
-    double2* Frow = nullptr;
+  const int64_t groups = (atom_count + NA - 1) / NA;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t first = grp * NA;
+    const double* kz[NA];
+    const int nv = load_atoms<NA>(first, atom_count, W, A, kFeatures ? nullptr : species, kFeatures ? nullptr : k,
+                                  species_count, t.dot_count, sA, nullptr, kz, status);
     if constexpr (kFeatures) {
-      Frow = features + atom * t.feature_count;
-      for (int64_t f = tid; f < t.feature_count; f += kRecThreads) Frow[f] = make_double2(0.0, 0.0);
-    } else {
-      int z = species[atom];
-      if (z < 0 || z >= species_count) {
-        if (tid == 0 && status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
-        z = 0;
-      }
-      kz = k + int64_t(z) * t.dot_count;
+      for (int64_t i = tid; i < int64_t(nv) * t.feature_count; i += kRecThreads)
+        features[first * t.feature_count + i] = make_double2(0.0, 0.0);
     }
-    for (int i = tid; i < W; i += kRecThreads) sA[i] = A[atom * W + i];
-    double ep = 0.0;
+    double ep[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) ep[a] = 0.0;
     bool bad = false;
     __syncthreads();
     for (int L = 0; L < t.pass_count; ++L) {
@@ -238,7 +291,7 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
         bad = true;  // uniform over the block
         continue;
       }
-      build_components(t, sA, sI, c0, nc, W, bad);
+      build_components<NA>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       for (int j = tid; j < nd; j += kRecThreads) {
         const int4 q = __ldg(t.dot + d0 + j);
@@ -246,12 +299,17 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
           bad = true;
           continue;
         }
-        double2 T = make_double2(0.0, 0.0);
+        double2 T[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) T[a] = make_double2(0.0, 0.0);
         for (int m = 0; m <= 2 * L; ++m) {  // m = M + L
-          const double2 p = mul(sI[q.x + m], sI[q.y + 2 * L - m]);
           const double sgn = ((m - L) & 1) ? -1.0 : 1.0;
-          T.x = fma(sgn, p.x, T.x);
-          T.y = fma(sgn, p.y, T.y);
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            const double2 p = mul(sI[(q.x + m) * NA + a], sI[(q.y + 2 * L - m) * NA + a]);
+            T[a].x = fma(sgn, p.x, T[a].x);
+            T[a].y = fma(sgn, p.y, T[a].y);
+          }
         }
         if constexpr (kFeatures) {
           if (q.z < 0 || q.w < 0 || int64_t(q.z) + q.w > t.feat_count) {
@@ -265,23 +323,35 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
               continue;
             }
             const double wv = __ldg(t.feat_weight + z);
-            double2 v = Frow[f];
-            v.x = fma(wv, T.x, v.x);
-            v.y = fma(wv, T.y, v.y);
-            Frow[f] = v;
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              if (a < nv) {
+                double2* slot = features + (first + a) * t.feature_count + f;
+                double2 v = *slot;
+                v.x = fma(wv, T[a].x, v.x);
+                v.y = fma(wv, T[a].y, v.y);
+                *slot = v;
+              }
+            }
           }
         } else {
-          ep = fma(__ldg(kz + d0 + j), T.x, ep);
+#pragma unroll
+          for (int a = 0; a < NA; ++a) ep[a] = fma(__ldg(kz[a] + d0 + j), T[a].x, ep[a]);
         }
       }
       __syncthreads();
     }
     if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
     if constexpr (!kFeatures) {
-      const double total = block_sum(ep, red);
-      if (tid == 0) energy[atom] = total;
+#pragma unroll
+      for (int a = 0; a < NA; ++a) {
+        const double total = block_sum(ep[a], red);
+        if (tid == 0 && a < nv) energy[first + a] = total;
+        __syncthreads();
+      }
+    } else {
+      __syncthreads();
     }
-    __syncthreads();
   }
 }
 
@@ -320,12 +390,38 @@ RecTabs device_view(const y3b_recoupled_tables& t) {
                  t.feat_weight};
 }
 
+// Atoms per CTA: the tables' atoms_per_cta (0 means 1), in [1, 4].
+int atoms_per_cta(const y3b_recoupled_tables& t, int& na) {
+  na = t.atoms_per_cta == 0 ? 1 : t.atoms_per_cta;
+  Y3B_CHECK_ARG(na >= 1 && na <= 4, "atoms_per_cta must be 0 (one) or in [1, 4]");
+  return Y3B_OK;
+}
+
+template <typename Kernel>
+int launch_grouped(Kernel kernel, size_t smem_per_atom, int na, int64_t atom_count, cudaStream_t s,
+                   const RecTabs& rt, const void* A, const int32_t* species, const double* weights,
+                   int64_t species_count, double* energy, void* out, int32_t* status) {
+  const size_t smem = smem_per_atom * size_t(na);
+  Y3B_CHECK_ARG(smem <= 224 * 1024,
+                "recoupled pass needs %lld bytes of shared memory for %d atoms per CTA (max 224 KB)",
+                (long long)smem, na);
+  const int64_t groups = (atom_count + na - 1) / na;
+  const int64_t grid = std::min<int64_t>(groups, int64_t(kSMs) * 64);
+  Y3B_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  kernel<<<int(grid), kRecThreads, smem, s>>>(rt, static_cast<const double2*>(A), atom_count, species, weights,
+                                              species_count, energy, static_cast<double2*>(out), status);
+  Y3B_LAUNCH_CHECK();
+  return Y3B_OK;
+}
+
 template <bool kFeatures>
 int launch_forward(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count, const int32_t* species,
                    const double* weights, int64_t species_count, double* energy, void* features, int32_t* status,
                    void* stream) {
   if (int rc = check_tables(tables)) return rc;
   const y3b_recoupled_tables& t = *tables;
+  int na = 1;
+  if (int rc = atoms_per_cta(t, na)) return rc;
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A != nullptr, "null A");
@@ -334,18 +430,19 @@ int launch_forward(const y3b_recoupled_tables* tables, const void* A, int64_t at
   } else {
     Y3B_CHECK_ARG(species && weights && energy && species_count > 0, "null pointer argument");
   }
-  const size_t smem = size_t(int64_t(t.row_width) + int64_t(t.max_pass_components)) * sizeof(double2);
-  Y3B_CHECK_ARG(smem <= 224 * 1024, "recoupled pass needs %lld bytes of shared memory (max 224 KB)",
-                (long long)smem);
-  const int64_t grid = std::min<int64_t>(atom_count, int64_t(kSMs) * 64);
+  const size_t per_atom = size_t(int64_t(t.row_width) + int64_t(t.max_pass_components)) * sizeof(double2);
+  const RecTabs rt = device_view(t);
   cudaStream_t s = as_stream(stream);
-  Y3B_CUDA_TRY(cudaFuncSetAttribute(recoupled_forward_kernel<kFeatures>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  recoupled_forward_kernel<kFeatures><<<int(grid), kRecThreads, smem, s>>>(
-      device_view(t), static_cast<const double2*>(A), atom_count, species, weights, species_count, energy,
-      static_cast<double2*>(features), status);
-  Y3B_LAUNCH_CHECK();
-  return Y3B_OK;
+  switch (na) {
+    case 1: return launch_grouped(recoupled_forward_kernel<kFeatures, 1>, per_atom, 1, atom_count, s, rt, A,
+                                  species, weights, species_count, energy, features, status);
+    case 2: return launch_grouped(recoupled_forward_kernel<kFeatures, 2>, per_atom, 2, atom_count, s, rt, A,
+                                  species, weights, species_count, energy, features, status);
+    case 3: return launch_grouped(recoupled_forward_kernel<kFeatures, 3>, per_atom, 3, atom_count, s, rt, A,
+                                  species, weights, species_count, energy, features, status);
+    default: return launch_grouped(recoupled_forward_kernel<kFeatures, 4>, per_atom, 4, atom_count, s, rt, A,
+                                   species, weights, species_count, energy, features, status);
+  }
 }
 
 }  // namespace
@@ -368,20 +465,23 @@ extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables,
                                              void* stream) {
   if (int rc = check_tables(tables)) return rc;
   const y3b_recoupled_tables& t = *tables;
+  int na = 1;
+  if (int rc = atoms_per_cta(t, na)) return rc;
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && contraction_weights && energy && dEdA && species_count > 0,
                 "null pointer argument");
-  const size_t smem = size_t(2 * int64_t(t.row_width) + 2 * int64_t(t.max_pass_components)) * sizeof(double2);
-  Y3B_CHECK_ARG(smem <= 224 * 1024, "recoupled pass needs %lld bytes of shared memory (max 224 KB)",
-                (long long)smem);
-  const int64_t grid = std::min<int64_t>(atom_count, int64_t(kSMs) * 64);
+  const size_t per_atom = size_t(2 * int64_t(t.row_width) + 2 * int64_t(t.max_pass_components)) * sizeof(double2);
+  const RecTabs rt = device_view(t);
   cudaStream_t s = as_stream(stream);
-  Y3B_CUDA_TRY(cudaFuncSetAttribute(recoupled_energy_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(smem)));
-  recoupled_energy_grad_kernel<<<int(grid), kRecThreads, smem, s>>>(
-      device_view(t), static_cast<const double2*>(A), atom_count, species, contraction_weights, species_count,
-      energy, static_cast<double2*>(dEdA), status);
-  Y3B_LAUNCH_CHECK();
-  return Y3B_OK;
+  switch (na) {
+    case 1: return launch_grouped(recoupled_energy_grad_kernel<1>, per_atom, 1, atom_count, s, rt, A, species,
+                                  contraction_weights, species_count, energy, dEdA, status);
+    case 2: return launch_grouped(recoupled_energy_grad_kernel<2>, per_atom, 2, atom_count, s, rt, A, species,
+                                  contraction_weights, species_count, energy, dEdA, status);
+    case 3: return launch_grouped(recoupled_energy_grad_kernel<3>, per_atom, 3, atom_count, s, rt, A, species,
+                                  contraction_weights, species_count, energy, dEdA, status);
+    default: return launch_grouped(recoupled_energy_grad_kernel<4>, per_atom, 4, atom_count, s, rt, A, species,
+                                   contraction_weights, species_count, energy, dEdA, status);
+  }
 }

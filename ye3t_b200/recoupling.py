@@ -563,10 +563,14 @@ class RecoupledEvaluator:
     """The recoupled passes on one GPU: the tables and the per-species contraction weights
     are uploaded once; each call takes ``A [n, nmax, (lmax+1)^2]`` complex128 (and the
     atoms' species), like ``ACEEvaluator``'s ``energy_grad`` / ``energy_from_density`` /
-    ``features``."""
+    ``features``.  ``atoms_per_cta`` atoms share one CTA's walk of the tables (each table
+    entry loaded once for all of them), within the 224 KB of shared memory."""
 
-    def __init__(self, bundle: ACEBundle, device, weights: np.ndarray = None, plan: "RecoupledPlan" = None):
+    def __init__(self, bundle: ACEBundle, device, weights: np.ndarray = None, plan: "RecoupledPlan" = None,
+                 atoms_per_cta: int = 1):
         import torch
+        if not 1 <= int(atoms_per_cta) <= 4:
+            raise ValueError("atoms_per_cta must be in [1, 4]")
         self.device = torch.device(device)
         self.plan = plan if plan is not None else build_recoupled_plan(bundle)
         self.tables = self.plan.device_tables()
@@ -575,6 +579,7 @@ class RecoupledEvaluator:
         self.weights = None if weights is None else \
             torch.as_tensor(self.plan.energy_weights(weights)).to(self.device).contiguous()
         self._c = ctypes_tables(self.arrays, self.tables)
+        self._c.atoms_per_cta = int(atoms_per_cta)
 
     def _rows(self, A):
         import torch
