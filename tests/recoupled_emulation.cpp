@@ -1,0 +1,141 @@
+// CPU emulation harness for the recoupled device passes (test infrastructure).
+//
+// Compiles ye3t_b200/csrc/recoupled_kernels.cuh as host C++ and runs a kernel
+// as one CTA of kRecThreads OS threads: __syncthreads is a std::barrier over
+// the block, __shfl_xor_sync an exchange through a per-warp buffer between two
+// warp barriers, __shared__ arrays are function statics and the dynamic shared
+// memory one static buffer.  One CTA (gridDim.x = 1) walks every atom group, as
+// the grid-stride loop of the kernels allows, so the emulated run follows the
+// same source, barriers and index checks as the device run.
+#define Y3B_EMULATE 1
+
+#include <atomic>
+#include <barrier>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+struct double2 {
+  double x, y;
+};
+struct int2 {
+  int x, y;
+};
+struct int4 {
+  int x, y, z, w;
+};
+inline double2 make_double2(double x, double y) { return double2{x, y}; }
+struct Dim3 {
+  unsigned x = 0, y = 0, z = 0;
+};
+
+static thread_local Dim3 threadIdx;
+static thread_local Dim3 blockIdx;
+static Dim3 gridDim;
+static Dim3 blockDim;
+alignas(16) static unsigned char y3b_emulated_smem[256 * 1024];
+static std::barrier<>* g_block = nullptr;
+static std::barrier<>* g_warp[32];
+static double g_lanes[32][32];
+
+#define __global__
+#define __device__
+#define __host__
+#define __forceinline__ inline
+#define __launch_bounds__(n)
+#define __restrict__
+#define __shared__ static
+#define __syncthreads() g_block->arrive_and_wait()
+
+template <typename T>
+inline T __ldg(const T* p) {
+  return *p;
+}
+inline int atomicOr(int32_t* p, int v) { return __atomic_fetch_or(p, v, __ATOMIC_SEQ_CST); }
+inline double __shfl_xor_sync(unsigned, double v, int lane_mask) {
+  const int w = int(threadIdx.x) >> 5, lane = int(threadIdx.x) & 31;
+  g_lanes[w][lane] = v;
+  g_warp[w]->arrive_and_wait();
+  const double r = g_lanes[w][lane ^ lane_mask];
+  g_warp[w]->arrive_and_wait();
+  return r;
+}
+using std::fma;
+
+#include "recoupled_kernels.cuh"
+
+namespace {
+
+template <typename F>
+void run_block(F body) {
+  const int T = y3b::kRecThreads;
+  std::barrier<> block(T);
+  std::vector<std::barrier<>*> warps;
+  for (int w = 0; w < T / 32; ++w) warps.push_back(new std::barrier<>(32));
+  g_block = &block;
+  for (int w = 0; w < T / 32; ++w) g_warp[w] = warps[w];
+  gridDim.x = 1;
+  blockDim.x = T;
+  std::vector<std::thread> threads;
+  for (int i = 0; i < T; ++i)
+    threads.emplace_back([i, &body] {
+      threadIdx.x = unsigned(i);
+      blockIdx.x = 0;
+      body();
+    });
+  for (auto& t : threads) t.join();
+  for (auto* w : warps) delete w;
+  g_block = nullptr;
+}
+
+}  // namespace
+
+extern "C" int emu_recoupled_energy_grad(int na, const y3b_recoupled_tables* tables, const double* A,
+                                         int64_t atom_count, const int32_t* species, const double* k,
+                                         int64_t species_count, double* energy, double* G, int32_t* status) {
+  const y3b::RecTabs t = y3b::device_view(*tables);
+  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * t.max_pass_components) * 16;
+  if (smem > sizeof(y3b_emulated_smem) || na < 1 || na > 4) return -1;
+  const auto* a2 = reinterpret_cast<const double2*>(A);
+  auto* g2 = reinterpret_cast<double2*>(G);
+  switch (na) {
+    case 1: run_block([&] { y3b::recoupled_energy_grad_kernel<1>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
+    case 2: run_block([&] { y3b::recoupled_energy_grad_kernel<2>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
+    case 3: run_block([&] { y3b::recoupled_energy_grad_kernel<3>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
+    default: run_block([&] { y3b::recoupled_energy_grad_kernel<4>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
+  }
+  return 0;
+}
+
+extern "C" int emu_recoupled_forward(int na, int features_out, const y3b_recoupled_tables* tables, const double* A,
+                                     int64_t atom_count, const int32_t* species, const double* k,
+                                     int64_t species_count, double* energy, double* F, int32_t* status) {
+  const y3b::RecTabs t = y3b::device_view(*tables);
+  const size_t smem = size_t(na) * size_t(t.row_width + t.max_pass_components) * 16;
+  if (smem > sizeof(y3b_emulated_smem) || na < 1 || na > 4) return -1;
+  const auto* a2 = reinterpret_cast<const double2*>(A);
+  auto* f2 = reinterpret_cast<double2*>(F);
+#define EMU_FWD(FEAT, N)                                                                                   \
+  run_block([&] {                                                                                          \
+    y3b::recoupled_forward_kernel<FEAT, N>(t, a2, atom_count, species, k, species_count, energy, f2, status); \
+  })
+  if (features_out) {
+    switch (na) {
+      case 1: EMU_FWD(true, 1); break;
+      case 2: EMU_FWD(true, 2); break;
+      case 3: EMU_FWD(true, 3); break;
+      default: EMU_FWD(true, 4); break;
+    }
+  } else {
+    switch (na) {
+      case 1: EMU_FWD(false, 1); break;
+      case 2: EMU_FWD(false, 2); break;
+      case 3: EMU_FWD(false, 3); break;
+      default: EMU_FWD(false, 4); break;
+    }
+  }
+#undef EMU_FWD
+  return 0;
+}

@@ -210,3 +210,99 @@ def test_plan_covers_channel_diagonal_l4_bundle():
     A = rng.normal(size=(6, 1, 25)) + 1j * rng.normal(size=(6, 1, 25))
     F0 = oracle.bundle_features(b, A, threads=2)
     assert np.abs(rn.walk_forward(tabs, A) - F0).max() <= 1e-12 * np.abs(F0).max()
+
+
+@pytest.fixture(scope="module")
+def emulated(tmp_path_factory):
+    """The device source of the recoupled passes compiled as host C++ (tests/recoupled_emulation.cpp)."""
+    import ctypes
+    import shutil
+    import subprocess
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("no C++ compiler")
+    out = tmp_path_factory.mktemp("emu") / "recoupled_emulation.so"
+    subprocess.run([gxx, "-O2", "-std=c++20", "-pthread", "-fPIC", "-shared",
+                    "-I", os.path.join(REPO, "include"), "-I", os.path.join(REPO, "ye3t_b200", "csrc"),
+                    os.path.join(REPO, "tests", "recoupled_emulation.cpp"), "-o", str(out)], check=True)
+    lib = ctypes.CDLL(str(out))
+    P, I64 = ctypes.c_void_p, ctypes.c_int64
+    lib.emu_recoupled_energy_grad.argtypes = [ctypes.c_int, P, P, I64, P, P, I64, P, P, P]
+    lib.emu_recoupled_forward.argtypes = [ctypes.c_int, ctypes.c_int, P, P, I64, P, P, I64, P, P, P]
+    return lib
+
+
+def _emulate(lib, tabs, A, species, k, na):
+    import ctypes
+
+    import torch
+    from ye3t_b200.recoupling import _TABLE_ARRAYS, ctypes_tables
+    arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(tabs, name))) for name in _TABLE_ARRAYS}
+    ct = ctypes_tables(arrays, tabs)
+    n = A.shape[0]
+    A = np.ascontiguousarray(A)
+    sp = np.ascontiguousarray(species, dtype=np.int32)
+    k = np.ascontiguousarray(k)
+    e, G, e2 = np.zeros(n), np.zeros_like(A), np.zeros(n)
+    F = np.zeros((n, tabs.feature_count), dtype=np.complex128)
+    st = np.zeros(3, dtype=np.int32)
+    ptr = lambda x: x.ctypes.data  # noqa: E731
+    assert lib.emu_recoupled_energy_grad(na, ctypes.byref(ct), ptr(A), n, ptr(sp), ptr(k), k.shape[0], ptr(e),
+                                         ptr(G), ptr(st)) == 0
+    assert lib.emu_recoupled_forward(na, 0, ctypes.byref(ct), ptr(A), n, ptr(sp), ptr(k), k.shape[0], ptr(e2),
+                                     None, st[1:].ctypes.data) == 0
+    assert lib.emu_recoupled_forward(na, 1, ctypes.byref(ct), ptr(A), n, None, None, 0, None, ptr(F),
+                                     st[2:].ctypes.data) == 0
+    return e, G, e2, F, st
+
+
+@pytest.fixture(scope="module")
+def c5_case(plan5):
+    """Five atoms (one of an out-of-range species) with the oracle's results."""
+    from oracle import oracle
+    b, plan = plan5
+    rng = np.random.default_rng(30)
+    A = rng.normal(size=(5, 8, 16)) + 1j * rng.normal(size=(5, 8, 16))
+    species = np.array([0, 2, 1, 7, 1], dtype=np.int32)
+    w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
+    used = np.where(species >= 3, 0, species).astype(np.int32)
+    e0, G0 = oracle.bundle_energy_grad(b, A, used, w, threads=4)
+    F0 = oracle.bundle_features(b, A, threads=4)
+    return A, species, plan.energy_weights(w), e0, G0, F0
+
+
+@pytest.mark.parametrize("na", [1, 2, 3])
+def test_device_source_emulated_on_cpu_matches_oracle(emulated, plan5, c5_case, na):
+    """The recoupled kernels' own source (recoupled_kernels.cuh), run on the CPU as one CTA of
+    256 threads with real block barriers and warp exchanges, gives the oracle's energies, dE/dA
+    and features for 1-3 atoms per CTA, including a partial last group and a species out of
+    range (status INDEX_RANGE, species 0 used)."""
+    A, species, k, e0, G0, F0 = c5_case
+    e, G, e2, F, st = _emulate(emulated, plan5[1].device_tables(), A, species, k, na)
+    assert st.tolist() == [1, 1, 0]
+    assert np.abs(e - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(e2 - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G - G0).max() <= 1e-12 * np.abs(G0).max()
+    assert np.abs(F - F0).max() <= 1e-12 * np.abs(F0).max()
+
+
+def test_device_source_emulated_flags_damaged_tables(emulated, plan3):
+    """Table entries outside their pass or array (a list partner, a back-propagation
+    component, a contraction's segment, a coupling's A-row entry) set Y3B_STATUS_TABLE in
+    the emulated device source and are skipped; the undamaged run sets nothing."""
+    import copy
+
+    from ye3t_b200 import _native
+    tabs = plan3.device_tables()
+    rng = np.random.default_rng(40)
+    A = rng.normal(size=(2, 8, 16)) + 1j * rng.normal(size=(2, 8, 16))
+    k = plan3.energy_weights(rng.normal(size=(3, tabs.feature_count)))
+    species = np.array([0, 1], dtype=np.int32)
+    assert _emulate(emulated, tabs, A, species, k, 1)[4].tolist() == [0, 0, 0]
+    pair = int(np.nonzero(tabs.comp[:, 3] > 0)[0][0])
+    for field, index, value in (("own", (3, 0), 10 ** 6), ("bp_gi", (5,), 10 ** 6), ("dot", (2, 1), 10 ** 6),
+                                ("comp", (pair, 1), 10 ** 6)):
+        bad = copy.deepcopy(tabs)
+        getattr(bad, field)[index] = value
+        st = _emulate(emulated, bad, A, species, k, 2)[4]
+        assert st[0] & _native.STATUS_TABLE or st[1] & _native.STATUS_TABLE, field

@@ -1,0 +1,366 @@
+// Device code of the recoupled passes (see recoupled.cu for what they
+// compute).  Compiled by nvcc through recoupled.cu; with Y3B_EMULATE defined
+// it also compiles as host C++ for the CPU emulation harness of the tests,
+// which runs one OS thread per CUDA thread with std::barrier as the block
+// barrier, so that this exact source is checked against the oracle without a
+// GPU.
+#pragma once
+
+#include <stdint.h>
+
+#include "ye3t_b200.h"
+
+#ifdef Y3B_EMULATE
+#define Y3B_DYNAMIC_SMEM(T, name) T* name = reinterpret_cast<T*>(y3b_emulated_smem)
+#else
+#define Y3B_DYNAMIC_SMEM(T, name) extern __shared__ T name[]
+#endif
+
+namespace y3b {
+namespace {
+
+constexpr int kRecThreads = 256;
+
+__host__ __device__ inline double2 rmul(double2 a, double2 b) {
+  return make_double2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+struct RecTabs {
+  int32_t pass_count, max_pass_components, row_width, dot_count;
+  int64_t component_count, cg_count, own_count, bp_count;
+  const int32_t* pass_begin;
+  const int4* comp;  // two int4 per component: (a, b, cg_begin, cg_count), (m, own_begin, own_count, 0)
+  const int32_t* cg_index;
+  const double* cg_value;
+  const int2* own;  // (partner's first local component, contraction)
+  const int32_t* bp_begin;
+  const int32_t* bp_gi;
+  const int32_t* bp_other;
+  const double* bp_value;
+  int64_t feature_count, feat_count;
+  const int32_t* dot_begin;
+  const int4* dot;  // (A's first local component, B's, feature range begin, count)
+  const int32_t* feat_index;
+  const double* feat_weight;
+};
+
+inline RecTabs device_view(const y3b_recoupled_tables& t) {
+  return RecTabs{t.pass_count, t.max_pass_components, t.row_width, t.dot_count,
+                 t.component_count, t.cg_count, t.own_count, t.bp_count,
+                 t.pass_begin, reinterpret_cast<const int4*>(t.comp), t.cg_index, t.cg_value,
+                 reinterpret_cast<const int2*>(t.own), t.bp_begin, t.bp_gi, t.bp_other, t.bp_value,
+                 t.feature_count, t.feat_count, t.dot_begin, reinterpret_cast<const int4*>(t.dot), t.feat_index,
+                 t.feat_weight};
+}
+
+// Fixed-order block sum of one double per thread (warp shuffles, then the
+// warps in order); the result is valid in thread 0.
+__device__ __forceinline__ double block_sum(double v, double* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double s = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < kRecThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+// Shared-memory arrays hold NA atoms side by side: entry e of atom a at
+// [e * NA + a].  A CTA takes atoms [g NA, g NA + NA); every table entry it
+// loads (coupling term, contraction-list entry, back-propagation entry,
+// contraction) serves all NA atoms, and the NA sums are independent chains.
+template <int NA>
+__device__ __forceinline__ void build_components(const RecTabs& t, const double2* sA, double2* sI, int c0, int nc,
+                                                 int W, bool& bad) {
+  for (int c = threadIdx.x; c < nc; c += kRecThreads) {
+    const int4 d = __ldg(t.comp + 2 * (c0 + c));
+    double2 v[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) v[a] = make_double2(d.x < 0 ? 1.0 : 0.0, 0.0);
+    if (d.x < 0) {
+    } else if (d.w == 0) {
+      if (d.x < W) {
+#pragma unroll
+        for (int a = 0; a < NA; ++a) v[a] = sA[d.x * NA + a];
+      } else {
+        bad = true;
+      }
+    } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
+      bad = true;
+    } else {
+      for (int q = d.z; q < d.z + d.w; ++q) {
+        const int ix = __ldg(t.cg_index + q);
+        const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
+        if (ia >= W || ib < 0 || ib >= W) {
+          bad = true;
+          continue;
+        }
+        const double cv = __ldg(t.cg_value + q);
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+          const double2 p = rmul(sA[ia * NA + a], sA[ib * NA + a]);
+          v[a].x = fma(cv, p.x, v[a].x);
+          v[a].y = fma(cv, p.y, v[a].y);
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NA; ++a) sI[c * NA + a] = v[a];
+  }
+}
+
+// The CTA's atoms: count of valid ones, their weight rows (species outside
+// the range set the status and use species 0), and their A rows in sA.
+template <int NA>
+__device__ __forceinline__ int load_atoms(int64_t first, int64_t atom_count, int W, const double2* A,
+                                          const int32_t* species, const double* k, int64_t species_count,
+                                          int32_t dot_count, double2* sA, double2* sGA, const double** kz,
+                                          int32_t* status) {
+  const int nv = int(atom_count - first < NA ? atom_count - first : NA);
+#pragma unroll
+  for (int a = 0; a < NA; ++a) {
+    int z = 0;
+    if (species != nullptr && a < nv) {
+      z = species[first + a];
+      if (z < 0 || z >= species_count) {
+        if (threadIdx.x == 0 && status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        z = 0;
+      }
+    }
+    kz[a] = k == nullptr ? nullptr : k + int64_t(z) * dot_count;
+  }
+  for (int i = threadIdx.x; i < W * NA; i += kRecThreads) {
+    const int a = i % NA, e = i / NA;
+    sA[i] = a < nv ? A[(first + a) * W + e] : make_double2(0.0, 0.0);
+    if (sGA != nullptr) sGA[i] = make_double2(0.0, 0.0);
+  }
+  return nv;
+}
+
+template <int NA>
+__global__ void __launch_bounds__(kRecThreads)
+recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
+                             const int32_t* __restrict__ species, const double* __restrict__ k,
+                             int64_t species_count, double* __restrict__ energy, double2* __restrict__ G,
+                             int32_t* status) {
+  Y3B_DYNAMIC_SMEM(double2, rec_smem);
+  __shared__ double red[kRecThreads / 32];
+  const int W = t.row_width;
+  const int maxc = t.max_pass_components;
+  double2* sA = rec_smem;          // [W][NA] the atoms' A rows
+  double2* sGA = sA + W * NA;      // [W][NA] dE/dA of the rows
+  double2* sI = sGA + W * NA;      // [maxc][NA] components of the pass
+  double2* sG = sI + maxc * NA;    // [maxc][NA] their adjoints
+  const int tid = threadIdx.x;
+  const int64_t groups = (atom_count + NA - 1) / NA;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t first = grp * NA;
+    const double* kz[NA];
+    const int nv = load_atoms<NA>(first, atom_count, W, A, species, k, species_count, t.dot_count, sA, sGA, kz,
+                                  status);
+    double ep[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) ep[a] = 0.0;
+    bool bad = false;
+    __syncthreads();
+    for (int L = 0; L < t.pass_count; ++L) {
+      const int c0 = t.pass_begin[L];
+      const int nc = t.pass_begin[L + 1] - c0;
+      if (c0 < 0 || nc < 0 || nc > maxc || int64_t(c0) + nc > t.component_count) {
+        bad = true;  // uniform over the block: every thread reads the same entries
+        continue;
+      }
+      // 1. components
+      build_components<NA>(t, sA, sI, c0, nc, W, bad);
+      __syncthreads();
+      // 2. adjoints of the components and the energy shares
+      for (int c = tid; c < nc; c += kRecThreads) {
+        const int4 d = __ldg(t.comp + 2 * (c0 + c) + 1);
+        double2 acc[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) acc[a] = make_double2(0.0, 0.0);
+        if (d.y < 0 || d.z < 0 || int64_t(d.y) + d.z > t.own_count) {
+          bad = true;
+        } else {
+          const int r = 2 * L - d.x;
+          for (int q = d.y; q < d.y + d.z; ++q) {
+            const int2 e = __ldg(t.own + q);
+            const int p = e.x + r;
+            if (p < 0 || p >= nc || e.y < 0 || e.y >= t.dot_count) {
+              bad = true;
+              continue;
+            }
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              const double kk = __ldg(kz[a] + e.y);
+              const double2 v = sI[p * NA + a];
+              acc[a].x = fma(kk, v.x, acc[a].x);
+              acc[a].y = fma(kk, v.y, acc[a].y);
+            }
+          }
+        }
+        const double sgn = ((d.x - L) & 1) ? -1.0 : 1.0;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+          acc[a].x *= sgn;
+          acc[a].y *= sgn;
+          sG[c * NA + a] = acc[a];
+          const double2 iv = sI[c * NA + a];
+          ep[a] = fma(iv.x, acc[a].x, ep[a]);
+          ep[a] = fma(-iv.y, acc[a].y, ep[a]);
+        }
+      }
+      __syncthreads();
+      // 3. back-propagation into the A rows (each entry owns its sum)
+      for (int i = tid; i < W; i += kRecThreads) {
+        const int64_t at = int64_t(L) * W + i;
+        const int b0 = t.bp_begin[at], b1 = t.bp_begin[at + 1];
+        if (b0 < 0 || b1 < b0 || int64_t(b1) > t.bp_count) {
+          bad = true;
+          continue;
+        }
+        double2 ga[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) ga[a] = sGA[i * NA + a];
+        for (int q = b0; q < b1; ++q) {
+          const int gi = __ldg(t.bp_gi + q);
+          const int o = __ldg(t.bp_other + q);
+          if (gi < 0 || gi >= nc || o >= W) {
+            bad = true;
+            continue;
+          }
+          const double cv = __ldg(t.bp_value + q);
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            const double2 g = sG[gi * NA + a];
+            const double2 term = o < 0 ? g : rmul(g, sA[o * NA + a]);
+            ga[a].x = fma(cv, term.x, ga[a].x);
+            ga[a].y = fma(cv, term.y, ga[a].y);
+          }
+        }
+#pragma unroll
+        for (int a = 0; a < NA; ++a) sGA[i * NA + a] = ga[a];
+      }
+      __syncthreads();
+    }
+    if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
+    for (int i = tid; i < W * NA; i += kRecThreads) {
+      const int a = i % NA, e = i / NA;
+      if (a < nv) G[(first + a) * W + e] = sGA[i];
+    }
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      const double total = block_sum(ep[a], red);
+      if (tid == 0 && a < nv) energy[first + a] = 0.5 * total;
+      __syncthreads();
+    }
+  }
+}
+
+// Forward pass: per L the components, then every contraction of the pass once,
+// T_d = sum_M (-1)^M I_A[M] I_B[-M]; the energies e = Re(sum_d k[z, d] T_d)
+// (kFeatures false) or the features F[f] += W[f, d] T_d (kFeatures true: a word
+// has at most one contraction per L and a feature belongs to one word, so each
+// feature has one writer per pass and the passes are ordered by barriers).
+template <bool kFeatures, int NA>
+__global__ void __launch_bounds__(kRecThreads)
+recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
+                         const int32_t* __restrict__ species, const double* __restrict__ k, int64_t species_count,
+                         double* __restrict__ energy, double2* __restrict__ features, int32_t* status) {
+  Y3B_DYNAMIC_SMEM(double2, rec_smem);
+  __shared__ double red[kRecThreads / 32];
+  const int W = t.row_width;
+  double2* sA = rec_smem;     // [W][NA]
+  double2* sI = sA + W * NA;  // [max_pass_components][NA]
+  const int tid = threadIdx.x;
+  const int64_t groups = (atom_count + NA - 1) / NA;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t first = grp * NA;
+    const double* kz[NA];
+    const int nv = load_atoms<NA>(first, atom_count, W, A, kFeatures ? nullptr : species, kFeatures ? nullptr : k,
+                                  species_count, t.dot_count, sA, nullptr, kz, status);
+    if constexpr (kFeatures) {
+      for (int64_t i = tid; i < int64_t(nv) * t.feature_count; i += kRecThreads)
+        features[first * t.feature_count + i] = make_double2(0.0, 0.0);
+    }
+    double ep[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) ep[a] = 0.0;
+    bool bad = false;
+    __syncthreads();
+    for (int L = 0; L < t.pass_count; ++L) {
+      const int c0 = t.pass_begin[L];
+      const int nc = t.pass_begin[L + 1] - c0;
+      const int d0 = t.dot_begin[L];
+      const int nd = t.dot_begin[L + 1] - d0;
+      if (c0 < 0 || nc < 0 || nc > t.max_pass_components || int64_t(c0) + nc > t.component_count || d0 < 0 ||
+          nd < 0 || int64_t(d0) + nd > t.dot_count) {
+        bad = true;  // uniform over the block
+        continue;
+      }
+      build_components<NA>(t, sA, sI, c0, nc, W, bad);
+      __syncthreads();
+      for (int j = tid; j < nd; j += kRecThreads) {
+        const int4 q = __ldg(t.dot + d0 + j);
+        if (q.x < 0 || q.y < 0 || q.x + 2 * L >= nc || q.y + 2 * L >= nc) {
+          bad = true;
+          continue;
+        }
+        double2 T[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) T[a] = make_double2(0.0, 0.0);
+        for (int m = 0; m <= 2 * L; ++m) {  // m = M + L
+          const double sgn = ((m - L) & 1) ? -1.0 : 1.0;
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            const double2 p = rmul(sI[(q.x + m) * NA + a], sI[(q.y + 2 * L - m) * NA + a]);
+            T[a].x = fma(sgn, p.x, T[a].x);
+            T[a].y = fma(sgn, p.y, T[a].y);
+          }
+        }
+        if constexpr (kFeatures) {
+          if (q.z < 0 || q.w < 0 || int64_t(q.z) + q.w > t.feat_count) {
+            bad = true;
+            continue;
+          }
+          for (int z = q.z; z < q.z + q.w; ++z) {
+            const int f = __ldg(t.feat_index + z);
+            if (f < 0 || f >= t.feature_count) {
+              bad = true;
+              continue;
+            }
+            const double wv = __ldg(t.feat_weight + z);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              if (a < nv) {
+                double2* slot = features + (first + a) * t.feature_count + f;
+                double2 v = *slot;
+                v.x = fma(wv, T[a].x, v.x);
+                v.y = fma(wv, T[a].y, v.y);
+                *slot = v;
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int a = 0; a < NA; ++a) ep[a] = fma(__ldg(kz[a] + d0 + j), T[a].x, ep[a]);
+        }
+      }
+      __syncthreads();
+    }
+    if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
+    if constexpr (!kFeatures) {
+#pragma unroll
+      for (int a = 0; a < NA; ++a) {
+        const double total = block_sum(ep[a], red);
+        if (tid == 0 && a < nv) energy[first + a] = total;
+        __syncthreads();
+      }
+    } else {
+      __syncthreads();
+    }
+  }
+}
+
+}  // namespace
+}  // namespace y3b
