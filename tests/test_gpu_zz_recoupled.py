@@ -1,0 +1,91 @@
+"""Recoupled B-basis passes (y3b_ace_recoupled_*) on the GPU against the oracle and
+against the term-level adjoint kernels."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+_CASES = {}
+
+
+def _bundle(stem):
+    from ye3t_b200.schedules import ACEBundle
+    return ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", stem + ".npz"))
+
+
+def _case(stem):
+    """Bundle, plan, five atoms (one of a species outside the weights) and the oracle's results."""
+    if stem not in _CASES:
+        from oracle import oracle
+        from ye3t_b200.recoupling import build_recoupled_plan
+        b = _bundle(stem)
+        rng = np.random.default_rng(21)
+        A = rng.normal(size=(5, 8, 16)) + 1j * rng.normal(size=(5, 8, 16))
+        species = np.array([0, 1, 2, 1, 0], dtype=np.int32)
+        w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
+        e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=4)
+        F0 = oracle.bundle_features(b, A, threads=4)
+        _CASES[stem] = (b, build_recoupled_plan(b), A, species, w, e0, G0, F0)
+    return _CASES[stem]
+
+
+@pytest.mark.parametrize("stem, na", [("ace_n8_l3_nu3_L0", 1), ("ace_n8_l3_nu4_L0", 1), ("ace_n8_l3_nu4_L0", 2),
+                                      ("ace_n8_l3_nu4_L0", 3), ("ace_n8_l3_nu3_L0", 4)])
+def test_recoupled_passes_match_oracle(stem, na):
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    b, plan, A, species, w, e0, G0, F0 = _case(stem)
+    ev = RecoupledEvaluator(b, DEV, w, plan=plan, atoms_per_cta=na)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    Ad, sd = torch.as_tensor(A, device=DEV), torch.as_tensor(species, device=DEV)
+    F = ev.features(Ad, status=st).cpu().numpy()
+    e = ev.energy(Ad, sd, status=st).cpu().numpy()
+    e2, G = (x.cpu().numpy() for x in ev.energy_grad(Ad, sd, status=st))
+    assert int(st.item()) == 0
+    assert np.abs(F - F0).max() <= 1e-12 * np.abs(F0).max()
+    assert np.abs(e - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(e2 - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G - G0).max() <= 1e-12 * np.abs(G0).max()
+
+
+def test_recoupled_adjoint_matches_term_level_adjoint_and_repeats():
+    """3,000 atoms through the recoupled adjoint (one and three atoms per CTA) and through the
+    term-level adjoint (y3b_ace_energy_grad): same energies and dE/dA to 1e-12, and repeated
+    calls are bitwise identical."""
+    from ye3t_b200.ace import ACEConfig, ACEEvaluator
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    b, plan, _, _, _, _, _, _ = _case("ace_n8_l3_nu4_L0")
+    rng = np.random.default_rng(22)
+    n = 3000
+    A = torch.as_tensor(rng.normal(size=(n, 8, 16)) + 1j * rng.normal(size=(n, 8, 16)), device=DEV)
+    sp = torch.as_tensor(rng.integers(0, 3, n).astype(np.int32), device=DEV)
+    w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
+    ref = ACEEvaluator(b, DEV, config=ACEConfig(5.0, 5.0), species_prefactor=[1.0, 0.75, 1.25], weights=w)
+    e0, G0 = ref.energy_grad(A, sp)
+    for na in (1, 3):
+        rec = RecoupledEvaluator(b, DEV, w, plan=plan, atoms_per_cta=na)
+        e1, G1 = rec.energy_grad(A, sp)
+        e2, G2 = rec.energy_grad(A, sp)
+        assert torch.equal(e1, e2) and torch.equal(G1, G2)
+        assert float((e1 - e0).abs().max()) <= 1e-12 * float(e0.abs().max())
+        assert float((G1 - G0).abs().max()) <= 1e-12 * float(G0.abs().max())
+        e3 = rec.energy(A, sp)
+        assert float((e3 - e0).abs().max()) <= 1e-12 * float(e0.abs().max())
+
+
+def test_recoupled_species_out_of_range_sets_status():
+    from ye3t_b200 import _native
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    b, plan, A, _, _, _, _, _ = _case("ace_n8_l3_nu3_L0")
+    w = np.random.default_rng(23).normal(size=(2, b.feature_count))
+    ev = RecoupledEvaluator(b, DEV, w, plan=plan)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    e, G = ev.energy_grad(torch.as_tensor(A[:3], device=DEV), torch.tensor([0, 5, 1], dtype=torch.int32, device=DEV),
+                          status=st)
+    assert int(st.item()) & _native.STATUS_INDEX_RANGE
+    assert torch.isfinite(e).all() and torch.isfinite(G).all()
