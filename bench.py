@@ -57,6 +57,8 @@ def parse():
                          "term-level schedule kernels")
     ap.add_argument("--recoupled-atoms", type=int, default=1,
                     help="atoms per CTA of the recoupled passes (1-4, within shared memory)")
+    ap.add_argument("--recoupled-threads", type=int, default=256, choices=[256, 512],
+                    help="threads per CTA of the recoupled passes")
     ap.add_argument("--energy-only", action="store_true",
                     help="time the energy step alone (no adjoint, no forces)")
     return ap.parse_args()
@@ -210,7 +212,8 @@ def _config(args):
                         "linear readout",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
             "parallelism": f"atom-block x{args.gpus}",
-            "b_basis": (f"recoupled pair contractions ({args.recoupled_atoms} atoms per CTA)"
+            "b_basis": (f"recoupled pair contractions ({args.recoupled_atoms} atoms and "
+                        f"{args.recoupled_threads} threads per CTA)"
                         if getattr(args, "recoupled", False) else "term-level factorized schedules"),
             "l2": "inputs larger than L2 (A-basis 2 GB, neighbour list 110 MB at 2^20 atoms)"}
 
@@ -255,7 +258,8 @@ def run_b200(args):
     rec = None
     if args.recoupled:
         from ye3t_b200.recoupling import RecoupledEvaluator
-        rec = RecoupledEvaluator(bundle, device, weights, atoms_per_cta=args.recoupled_atoms)
+        rec = RecoupledEvaluator(bundle, device, weights, atoms_per_cta=args.recoupled_atoms,
+                                 threads_per_cta=args.recoupled_threads)
     b_launches = 1 if rec is not None else GRAD_CLASSES
     launches_per_step = 8 + (b_launches + 2 if forces else 1)
 

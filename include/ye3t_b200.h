@@ -430,7 +430,7 @@ typedef struct {
   const int32_t* feat_index;   /* [feat_count] feature of each weight */
   const double* feat_weight;   /* [feat_count] W[f, d] */
   int32_t atoms_per_cta;       /* atoms sharing one CTA's table walk: 0 (one) or 1..4, within shared memory */
-  int32_t reserved;            /* 0 */
+  int32_t threads_per_cta;     /* 0 (256), 256 or 512 */
 } y3b_recoupled_tables;
 
 /* Per-atom energies e_i = Re(sum_d k[z_i, d] T_d) and G = dE/dA (complex128,

@@ -1,7 +1,7 @@
 // CPU emulation harness for the recoupled device passes (test infrastructure).
 //
 // Compiles ye3t_b200/csrc/recoupled_kernels.cuh as host C++ and runs a kernel
-// as one CTA of kRecThreads OS threads: __syncthreads is a std::barrier over
+// as one CTA of 256 or 512 OS threads: __syncthreads is a std::barrier over
 // the block, __shfl_xor_sync an exchange through a per-warp buffer between two
 // warp barriers, __shared__ arrays are function statics and the dynamic shared
 // memory one static buffer.  One CTA (gridDim.x = 1) walks every atom group, as
@@ -69,8 +69,7 @@ using std::fma;
 namespace {
 
 template <typename F>
-void run_block(F body) {
-  const int T = y3b::kRecThreads;
+void run_block(int T, F body) {
   std::barrier<> block(T);
   std::vector<std::barrier<>*> warps;
   for (int w = 0; w < T / 32; ++w) warps.push_back(new std::barrier<>(32));
@@ -92,50 +91,58 @@ void run_block(F body) {
 
 }  // namespace
 
-extern "C" int emu_recoupled_energy_grad(int na, const y3b_recoupled_tables* tables, const double* A,
+#define EMU_SHAPES(CALL)                       \
+  switch (na * 1000 + th) {                    \
+    case 1256: CALL(1, 256); break;            \
+    case 2256: CALL(2, 256); break;            \
+    case 3256: CALL(3, 256); break;            \
+    case 4256: CALL(4, 256); break;            \
+    case 1512: CALL(1, 512); break;            \
+    case 2512: CALL(2, 512); break;            \
+    case 3512: CALL(3, 512); break;            \
+    case 4512: CALL(4, 512); break;            \
+    default: return -1;                        \
+  }
+
+extern "C" int emu_recoupled_energy_grad(int na, int th, const y3b_recoupled_tables* tables, const double* A,
                                          int64_t atom_count, const int32_t* species, const double* k,
                                          int64_t species_count, double* energy, double* G, int32_t* status) {
   const y3b::RecTabs t = y3b::device_view(*tables);
   const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * t.max_pass_components) * 16;
-  if (smem > sizeof(y3b_emulated_smem) || na < 1 || na > 4) return -1;
+  if (smem > sizeof(y3b_emulated_smem)) return -1;
   const auto* a2 = reinterpret_cast<const double2*>(A);
   auto* g2 = reinterpret_cast<double2*>(G);
-  switch (na) {
-    case 1: run_block([&] { y3b::recoupled_energy_grad_kernel<1>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
-    case 2: run_block([&] { y3b::recoupled_energy_grad_kernel<2>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
-    case 3: run_block([&] { y3b::recoupled_energy_grad_kernel<3>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
-    default: run_block([&] { y3b::recoupled_energy_grad_kernel<4>(t, a2, atom_count, species, k, species_count, energy, g2, status); }); break;
-  }
+#define EMU_GRAD(N, T)                                                                                        \
+  run_block(T, [&] {                                                                                          \
+    y3b::recoupled_energy_grad_kernel<N, T>(t, a2, atom_count, species, k, species_count, energy, g2, status); \
+  })
+  EMU_SHAPES(EMU_GRAD)
+#undef EMU_GRAD
   return 0;
 }
 
-extern "C" int emu_recoupled_forward(int na, int features_out, const y3b_recoupled_tables* tables, const double* A,
-                                     int64_t atom_count, const int32_t* species, const double* k,
+extern "C" int emu_recoupled_forward(int na, int th, int features_out, const y3b_recoupled_tables* tables,
+                                     const double* A, int64_t atom_count, const int32_t* species, const double* k,
                                      int64_t species_count, double* energy, double* F, int32_t* status) {
   const y3b::RecTabs t = y3b::device_view(*tables);
   const size_t smem = size_t(na) * size_t(t.row_width + t.max_pass_components) * 16;
-  if (smem > sizeof(y3b_emulated_smem) || na < 1 || na > 4) return -1;
+  if (smem > sizeof(y3b_emulated_smem)) return -1;
   const auto* a2 = reinterpret_cast<const double2*>(A);
   auto* f2 = reinterpret_cast<double2*>(F);
-#define EMU_FWD(FEAT, N)                                                                                   \
-  run_block([&] {                                                                                          \
-    y3b::recoupled_forward_kernel<FEAT, N>(t, a2, atom_count, species, k, species_count, energy, f2, status); \
+#define EMU_FEAT(N, T)                                                                                          \
+  run_block(T, [&] {                                                                                            \
+    y3b::recoupled_forward_kernel<true, N, T>(t, a2, atom_count, species, k, species_count, energy, f2, status); \
+  })
+#define EMU_ENER(N, T)                                                                                           \
+  run_block(T, [&] {                                                                                             \
+    y3b::recoupled_forward_kernel<false, N, T>(t, a2, atom_count, species, k, species_count, energy, f2, status); \
   })
   if (features_out) {
-    switch (na) {
-      case 1: EMU_FWD(true, 1); break;
-      case 2: EMU_FWD(true, 2); break;
-      case 3: EMU_FWD(true, 3); break;
-      default: EMU_FWD(true, 4); break;
-    }
+    EMU_SHAPES(EMU_FEAT)
   } else {
-    switch (na) {
-      case 1: EMU_FWD(false, 1); break;
-      case 2: EMU_FWD(false, 2); break;
-      case 3: EMU_FWD(false, 3); break;
-      default: EMU_FWD(false, 4); break;
-    }
+    EMU_SHAPES(EMU_ENER)
   }
-#undef EMU_FWD
+#undef EMU_FEAT
+#undef EMU_ENER
   return 0;
 }

@@ -54,7 +54,7 @@ def test_recoupled_passes_match_oracle(stem, na):
 
 
 def test_recoupled_adjoint_matches_term_level_adjoint_and_repeats():
-    """3,000 atoms through the recoupled adjoint (one and three atoms per CTA) and through the
+    """3,000 atoms through the recoupled adjoint (several CTA shapes) and through the
     term-level adjoint (y3b_ace_energy_grad): same energies and dE/dA to 1e-12, and repeated
     calls are bitwise identical."""
     from ye3t_b200.ace import ACEConfig, ACEEvaluator
@@ -67,8 +67,8 @@ def test_recoupled_adjoint_matches_term_level_adjoint_and_repeats():
     w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
     ref = ACEEvaluator(b, DEV, config=ACEConfig(5.0, 5.0), species_prefactor=[1.0, 0.75, 1.25], weights=w)
     e0, G0 = ref.energy_grad(A, sp)
-    for na in (1, 3):
-        rec = RecoupledEvaluator(b, DEV, w, plan=plan, atoms_per_cta=na)
+    for na, th in ((1, 256), (3, 256), (2, 512)):
+        rec = RecoupledEvaluator(b, DEV, w, plan=plan, atoms_per_cta=na, threads_per_cta=th)
         e1, G1 = rec.energy_grad(A, sp)
         e2, G2 = rec.energy_grad(A, sp)
         assert torch.equal(e1, e2) and torch.equal(G1, G2)

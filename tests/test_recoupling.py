@@ -227,12 +227,13 @@ def emulated(tmp_path_factory):
                     os.path.join(REPO, "tests", "recoupled_emulation.cpp"), "-o", str(out)], check=True)
     lib = ctypes.CDLL(str(out))
     P, I64 = ctypes.c_void_p, ctypes.c_int64
-    lib.emu_recoupled_energy_grad.argtypes = [ctypes.c_int, P, P, I64, P, P, I64, P, P, P]
-    lib.emu_recoupled_forward.argtypes = [ctypes.c_int, ctypes.c_int, P, P, I64, P, P, I64, P, P, P]
+    C = ctypes.c_int
+    lib.emu_recoupled_energy_grad.argtypes = [C, C, P, P, I64, P, P, I64, P, P, P]
+    lib.emu_recoupled_forward.argtypes = [C, C, C, P, P, I64, P, P, I64, P, P, P]
     return lib
 
 
-def _emulate(lib, tabs, A, species, k, na):
+def _emulate(lib, tabs, A, species, k, na, th=256):
     import ctypes
 
     import torch
@@ -247,11 +248,11 @@ def _emulate(lib, tabs, A, species, k, na):
     F = np.zeros((n, tabs.feature_count), dtype=np.complex128)
     st = np.zeros(3, dtype=np.int32)
     ptr = lambda x: x.ctypes.data  # noqa: E731
-    assert lib.emu_recoupled_energy_grad(na, ctypes.byref(ct), ptr(A), n, ptr(sp), ptr(k), k.shape[0], ptr(e),
-                                         ptr(G), ptr(st)) == 0
-    assert lib.emu_recoupled_forward(na, 0, ctypes.byref(ct), ptr(A), n, ptr(sp), ptr(k), k.shape[0], ptr(e2),
+    assert lib.emu_recoupled_energy_grad(na, th, ctypes.byref(ct), ptr(A), n, ptr(sp), ptr(k), k.shape[0],
+                                         ptr(e), ptr(G), ptr(st)) == 0
+    assert lib.emu_recoupled_forward(na, th, 0, ctypes.byref(ct), ptr(A), n, ptr(sp), ptr(k), k.shape[0], ptr(e2),
                                      None, st[1:].ctypes.data) == 0
-    assert lib.emu_recoupled_forward(na, 1, ctypes.byref(ct), ptr(A), n, None, None, 0, None, ptr(F),
+    assert lib.emu_recoupled_forward(na, th, 1, ctypes.byref(ct), ptr(A), n, None, None, 0, None, ptr(F),
                                      st[2:].ctypes.data) == 0
     return e, G, e2, F, st
 
@@ -271,14 +272,14 @@ def c5_case(plan5):
     return A, species, plan.energy_weights(w), e0, G0, F0
 
 
-@pytest.mark.parametrize("na", [1, 2, 3])
-def test_device_source_emulated_on_cpu_matches_oracle(emulated, plan5, c5_case, na):
+@pytest.mark.parametrize("na, th", [(1, 256), (2, 256), (3, 256), (3, 512)])
+def test_device_source_emulated_on_cpu_matches_oracle(emulated, plan5, c5_case, na, th):
     """The recoupled kernels' own source (recoupled_kernels.cuh), run on the CPU as one CTA of
-    256 threads with real block barriers and warp exchanges, gives the oracle's energies, dE/dA
-    and features for 1-3 atoms per CTA, including a partial last group and a species out of
-    range (status INDEX_RANGE, species 0 used)."""
+    256 or 512 threads with real block barriers and warp exchanges, gives the oracle's energies,
+    dE/dA and features for 1-3 atoms per CTA, including a partial last group and a species out
+    of range (status INDEX_RANGE, species 0 used)."""
     A, species, k, e0, G0, F0 = c5_case
-    e, G, e2, F, st = _emulate(emulated, plan5[1].device_tables(), A, species, k, na)
+    e, G, e2, F, st = _emulate(emulated, plan5[1].device_tables(), A, species, k, na, th)
     assert st.tolist() == [1, 1, 0]
     assert np.abs(e - e0).max() <= 1e-12 * np.abs(e0).max()
     assert np.abs(e2 - e0).max() <= 1e-12 * np.abs(e0).max()

@@ -61,7 +61,7 @@ class RecoupledTables(ctypes.Structure):
         ("pass_begin", VP), ("comp", VP), ("cg_index", VP), ("cg_value", VP), ("own", VP),
         ("bp_begin", VP), ("bp_gi", VP), ("bp_other", VP), ("bp_value", VP),
         ("feature_count", I64), ("feat_count", I64), ("dot_begin", VP), ("dot", VP), ("feat_index", VP),
-        ("feat_weight", VP), ("atoms_per_cta", I32), ("reserved", I32),
+        ("feat_weight", VP), ("atoms_per_cta", I32), ("threads_per_cta", I32),
     ]
 
 

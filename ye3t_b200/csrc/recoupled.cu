@@ -48,15 +48,18 @@ int check_tables(const y3b_recoupled_tables* tables) {
 }
 
 
-// Atoms per CTA: the tables' atoms_per_cta (0 means 1), in [1, 4].
-int atoms_per_cta(const y3b_recoupled_tables& t, int& na) {
+// Launch shape from the tables: atoms per CTA (0 means 1; 1..4) and threads
+// per CTA (0 means 256; 256 or 512).
+int launch_shape(const y3b_recoupled_tables& t, int& na, int& th) {
   na = t.atoms_per_cta == 0 ? 1 : t.atoms_per_cta;
+  th = t.threads_per_cta == 0 ? 256 : t.threads_per_cta;
   Y3B_CHECK_ARG(na >= 1 && na <= 4, "atoms_per_cta must be 0 (one) or in [1, 4]");
+  Y3B_CHECK_ARG(th == 256 || th == 512, "threads_per_cta must be 0 (256), 256 or 512");
   return Y3B_OK;
 }
 
 template <typename Kernel>
-int launch_grouped(Kernel kernel, size_t smem_per_atom, int na, int64_t atom_count, cudaStream_t s,
+int launch_grouped(Kernel kernel, int threads, size_t smem_per_atom, int na, int64_t atom_count, cudaStream_t s,
                    const RecTabs& rt, const void* A, const int32_t* species, const double* weights,
                    int64_t species_count, double* energy, void* out, int32_t* status) {
   const size_t smem = smem_per_atom * size_t(na);
@@ -66,11 +69,24 @@ int launch_grouped(Kernel kernel, size_t smem_per_atom, int na, int64_t atom_cou
   const int64_t groups = (atom_count + na - 1) / na;
   const int64_t grid = std::min<int64_t>(groups, int64_t(kSMs) * 64);
   Y3B_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  kernel<<<int(grid), kRecThreads, smem, s>>>(rt, static_cast<const double2*>(A), atom_count, species, weights,
-                                              species_count, energy, static_cast<double2*>(out), status);
+  kernel<<<int(grid), threads, smem, s>>>(rt, static_cast<const double2*>(A), atom_count, species, weights,
+                                          species_count, energy, static_cast<double2*>(out), status);
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }
+
+// One case per (atoms per CTA, threads per CTA) instance of a kernel template.
+#define Y3B_REC_DISPATCH(KERNEL, ...)                                                                   \
+  switch (na * 1000 + th) {                                                                             \
+    case 1256: return launch_grouped(KERNEL(1, 256), 256, __VA_ARGS__);                                 \
+    case 2256: return launch_grouped(KERNEL(2, 256), 256, __VA_ARGS__);                                 \
+    case 3256: return launch_grouped(KERNEL(3, 256), 256, __VA_ARGS__);                                 \
+    case 4256: return launch_grouped(KERNEL(4, 256), 256, __VA_ARGS__);                                 \
+    case 1512: return launch_grouped(KERNEL(1, 512), 512, __VA_ARGS__);                                 \
+    case 2512: return launch_grouped(KERNEL(2, 512), 512, __VA_ARGS__);                                 \
+    case 3512: return launch_grouped(KERNEL(3, 512), 512, __VA_ARGS__);                                 \
+    default: return launch_grouped(KERNEL(4, 512), 512, __VA_ARGS__);                                   \
+  }
 
 template <bool kFeatures>
 int launch_forward(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count, const int32_t* species,
@@ -78,8 +94,8 @@ int launch_forward(const y3b_recoupled_tables* tables, const void* A, int64_t at
                    void* stream) {
   if (int rc = check_tables(tables)) return rc;
   const y3b_recoupled_tables& t = *tables;
-  int na = 1;
-  if (int rc = atoms_per_cta(t, na)) return rc;
+  int na = 1, th = 256;
+  if (int rc = launch_shape(t, na, th)) return rc;
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A != nullptr, "null A");
@@ -91,16 +107,10 @@ int launch_forward(const y3b_recoupled_tables* tables, const void* A, int64_t at
   const size_t per_atom = size_t(int64_t(t.row_width) + int64_t(t.max_pass_components)) * sizeof(double2);
   const RecTabs rt = device_view(t);
   cudaStream_t s = as_stream(stream);
-  switch (na) {
-    case 1: return launch_grouped(recoupled_forward_kernel<kFeatures, 1>, per_atom, 1, atom_count, s, rt, A,
-                                  species, weights, species_count, energy, features, status);
-    case 2: return launch_grouped(recoupled_forward_kernel<kFeatures, 2>, per_atom, 2, atom_count, s, rt, A,
-                                  species, weights, species_count, energy, features, status);
-    case 3: return launch_grouped(recoupled_forward_kernel<kFeatures, 3>, per_atom, 3, atom_count, s, rt, A,
-                                  species, weights, species_count, energy, features, status);
-    default: return launch_grouped(recoupled_forward_kernel<kFeatures, 4>, per_atom, 4, atom_count, s, rt, A,
-                                   species, weights, species_count, energy, features, status);
-  }
+#define Y3B_FWD(N, T) recoupled_forward_kernel<kFeatures, N, T>
+  Y3B_REC_DISPATCH(Y3B_FWD, per_atom, na, atom_count, s, rt, A, species, weights, species_count, energy, features,
+                   status)
+#undef Y3B_FWD
 }
 
 }  // namespace
@@ -123,8 +133,8 @@ extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables,
                                              void* stream) {
   if (int rc = check_tables(tables)) return rc;
   const y3b_recoupled_tables& t = *tables;
-  int na = 1;
-  if (int rc = atoms_per_cta(t, na)) return rc;
+  int na = 1, th = 256;
+  if (int rc = launch_shape(t, na, th)) return rc;
   Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && contraction_weights && energy && dEdA && species_count > 0,
@@ -132,14 +142,8 @@ extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables,
   const size_t per_atom = size_t(2 * int64_t(t.row_width) + 2 * int64_t(t.max_pass_components)) * sizeof(double2);
   const RecTabs rt = device_view(t);
   cudaStream_t s = as_stream(stream);
-  switch (na) {
-    case 1: return launch_grouped(recoupled_energy_grad_kernel<1>, per_atom, 1, atom_count, s, rt, A, species,
-                                  contraction_weights, species_count, energy, dEdA, status);
-    case 2: return launch_grouped(recoupled_energy_grad_kernel<2>, per_atom, 2, atom_count, s, rt, A, species,
-                                  contraction_weights, species_count, energy, dEdA, status);
-    case 3: return launch_grouped(recoupled_energy_grad_kernel<3>, per_atom, 3, atom_count, s, rt, A, species,
-                                  contraction_weights, species_count, energy, dEdA, status);
-    default: return launch_grouped(recoupled_energy_grad_kernel<4>, per_atom, 4, atom_count, s, rt, A, species,
-                                   contraction_weights, species_count, energy, dEdA, status);
-  }
+#define Y3B_GRAD(N, T) recoupled_energy_grad_kernel<N, T>
+  Y3B_REC_DISPATCH(Y3B_GRAD, per_atom, na, atom_count, s, rt, A, species, contraction_weights, species_count,
+                   energy, dEdA, status)
+#undef Y3B_GRAD
 }

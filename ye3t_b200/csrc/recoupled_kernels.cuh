@@ -19,7 +19,6 @@
 namespace y3b {
 namespace {
 
-constexpr int kRecThreads = 256;
 
 __host__ __device__ inline double2 rmul(double2 a, double2 b) {
   return make_double2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
@@ -55,13 +54,14 @@ inline RecTabs device_view(const y3b_recoupled_tables& t) {
 
 // Fixed-order block sum of one double per thread (warp shuffles, then the
 // warps in order); the result is valid in thread 0.
+template <int TH>
 __device__ __forceinline__ double block_sum(double v, double* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   double s = 0.0;
   if (threadIdx.x == 0)
-    for (int w = 0; w < kRecThreads / 32; ++w) s += red[w];
+    for (int w = 0; w < TH / 32; ++w) s += red[w];
   return s;
 }
 
@@ -69,10 +69,10 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
 // [e * NA + a].  A CTA takes atoms [g NA, g NA + NA); every table entry it
 // loads (coupling term, contraction-list entry, back-propagation entry,
 // contraction) serves all NA atoms, and the NA sums are independent chains.
-template <int NA>
+template <int NA, int TH>
 __device__ __forceinline__ void build_components(const RecTabs& t, const double2* sA, double2* sI, int c0, int nc,
                                                  int W, bool& bad) {
-  for (int c = threadIdx.x; c < nc; c += kRecThreads) {
+  for (int c = threadIdx.x; c < nc; c += TH) {
     const int4 d = __ldg(t.comp + 2 * (c0 + c));
     double2 v[NA];
 #pragma unroll
@@ -111,7 +111,7 @@ __device__ __forceinline__ void build_components(const RecTabs& t, const double2
 
 // The CTA's atoms: count of valid ones, their weight rows (species outside
 // the range set the status and use species 0), and their A rows in sA.
-template <int NA>
+template <int NA, int TH>
 __device__ __forceinline__ int load_atoms(int64_t first, int64_t atom_count, int W, const double2* A,
                                           const int32_t* species, const double* k, int64_t species_count,
                                           int32_t dot_count, double2* sA, double2* sGA, const double** kz,
@@ -129,7 +129,7 @@ __device__ __forceinline__ int load_atoms(int64_t first, int64_t atom_count, int
     }
     kz[a] = k == nullptr ? nullptr : k + int64_t(z) * dot_count;
   }
-  for (int i = threadIdx.x; i < W * NA; i += kRecThreads) {
+  for (int i = threadIdx.x; i < W * NA; i += TH) {
     const int a = i % NA, e = i / NA;
     sA[i] = a < nv ? A[(first + a) * W + e] : make_double2(0.0, 0.0);
     if (sGA != nullptr) sGA[i] = make_double2(0.0, 0.0);
@@ -137,14 +137,14 @@ __device__ __forceinline__ int load_atoms(int64_t first, int64_t atom_count, int
   return nv;
 }
 
-template <int NA>
-__global__ void __launch_bounds__(kRecThreads)
+template <int NA, int TH>
+__global__ void __launch_bounds__(TH)
 recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
                              const int32_t* __restrict__ species, const double* __restrict__ k,
                              int64_t species_count, double* __restrict__ energy, double2* __restrict__ G,
                              int32_t* status) {
   Y3B_DYNAMIC_SMEM(double2, rec_smem);
-  __shared__ double red[kRecThreads / 32];
+  __shared__ double red[TH / 32];
   const int W = t.row_width;
   const int maxc = t.max_pass_components;
   double2* sA = rec_smem;          // [W][NA] the atoms' A rows
@@ -156,7 +156,7 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
     const int64_t first = grp * NA;
     const double* kz[NA];
-    const int nv = load_atoms<NA>(first, atom_count, W, A, species, k, species_count, t.dot_count, sA, sGA, kz,
+    const int nv = load_atoms<NA, TH>(first, atom_count, W, A, species, k, species_count, t.dot_count, sA, sGA, kz,
                                   status);
     double ep[NA];
 #pragma unroll
@@ -171,10 +171,10 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
         continue;
       }
       // 1. components
-      build_components<NA>(t, sA, sI, c0, nc, W, bad);
+      build_components<NA, TH>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       // 2. adjoints of the components and the energy shares
-      for (int c = tid; c < nc; c += kRecThreads) {
+      for (int c = tid; c < nc; c += TH) {
         const int4 d = __ldg(t.comp + 2 * (c0 + c) + 1);
         double2 acc[NA];
 #pragma unroll
@@ -212,7 +212,7 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
       }
       __syncthreads();
       // 3. back-propagation into the A rows (each entry owns its sum)
-      for (int i = tid; i < W; i += kRecThreads) {
+      for (int i = tid; i < W; i += TH) {
         const int64_t at = int64_t(L) * W + i;
         const int b0 = t.bp_begin[at], b1 = t.bp_begin[at + 1];
         if (b0 < 0 || b1 < b0 || int64_t(b1) > t.bp_count) {
@@ -244,13 +244,13 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
       __syncthreads();
     }
     if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
-    for (int i = tid; i < W * NA; i += kRecThreads) {
+    for (int i = tid; i < W * NA; i += TH) {
       const int a = i % NA, e = i / NA;
       if (a < nv) G[(first + a) * W + e] = sGA[i];
     }
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
-      const double total = block_sum(ep[a], red);
+      const double total = block_sum<TH>(ep[a], red);
       if (tid == 0 && a < nv) energy[first + a] = 0.5 * total;
       __syncthreads();
     }
@@ -262,13 +262,13 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
 // (kFeatures false) or the features F[f] += W[f, d] T_d (kFeatures true: a word
 // has at most one contraction per L and a feature belongs to one word, so each
 // feature has one writer per pass and the passes are ordered by barriers).
-template <bool kFeatures, int NA>
-__global__ void __launch_bounds__(kRecThreads)
+template <bool kFeatures, int NA, int TH>
+__global__ void __launch_bounds__(TH)
 recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_count,
                          const int32_t* __restrict__ species, const double* __restrict__ k, int64_t species_count,
                          double* __restrict__ energy, double2* __restrict__ features, int32_t* status) {
   Y3B_DYNAMIC_SMEM(double2, rec_smem);
-  __shared__ double red[kRecThreads / 32];
+  __shared__ double red[TH / 32];
   const int W = t.row_width;
   double2* sA = rec_smem;     // [W][NA]
   double2* sI = sA + W * NA;  // [max_pass_components][NA]
@@ -277,10 +277,10 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
     const int64_t first = grp * NA;
     const double* kz[NA];
-    const int nv = load_atoms<NA>(first, atom_count, W, A, kFeatures ? nullptr : species, kFeatures ? nullptr : k,
+    const int nv = load_atoms<NA, TH>(first, atom_count, W, A, kFeatures ? nullptr : species, kFeatures ? nullptr : k,
                                   species_count, t.dot_count, sA, nullptr, kz, status);
     if constexpr (kFeatures) {
-      for (int64_t i = tid; i < int64_t(nv) * t.feature_count; i += kRecThreads)
+      for (int64_t i = tid; i < int64_t(nv) * t.feature_count; i += TH)
         features[first * t.feature_count + i] = make_double2(0.0, 0.0);
     }
     double ep[NA];
@@ -298,9 +298,9 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
         bad = true;  // uniform over the block
         continue;
       }
-      build_components<NA>(t, sA, sI, c0, nc, W, bad);
+      build_components<NA, TH>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
-      for (int j = tid; j < nd; j += kRecThreads) {
+      for (int j = tid; j < nd; j += TH) {
         const int4 q = __ldg(t.dot + d0 + j);
         if (q.x < 0 || q.y < 0 || q.x + 2 * L >= nc || q.y + 2 * L >= nc) {
           bad = true;
@@ -352,7 +352,7 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
     if constexpr (!kFeatures) {
 #pragma unroll
       for (int a = 0; a < NA; ++a) {
-        const double total = block_sum(ep[a], red);
+        const double total = block_sum<TH>(ep[a], red);
         if (tid == 0 && a < nv) energy[first + a] = total;
         __syncthreads();
       }

@@ -564,13 +564,16 @@ class RecoupledEvaluator:
     are uploaded once; each call takes ``A [n, nmax, (lmax+1)^2]`` complex128 (and the
     atoms' species), like ``ACEEvaluator``'s ``energy_grad`` / ``energy_from_density`` /
     ``features``.  ``atoms_per_cta`` atoms share one CTA's walk of the tables (each table
-    entry loaded once for all of them), within the 224 KB of shared memory."""
+    entry loaded once for all of them), within the 224 KB of shared memory; a CTA has
+    ``threads_per_cta`` (256 or 512) threads."""
 
     def __init__(self, bundle: ACEBundle, device, weights: np.ndarray = None, plan: "RecoupledPlan" = None,
-                 atoms_per_cta: int = 1):
+                 atoms_per_cta: int = 1, threads_per_cta: int = 256):
         import torch
         if not 1 <= int(atoms_per_cta) <= 4:
             raise ValueError("atoms_per_cta must be in [1, 4]")
+        if int(threads_per_cta) not in (256, 512):
+            raise ValueError("threads_per_cta must be 256 or 512")
         self.device = torch.device(device)
         self.plan = plan if plan is not None else build_recoupled_plan(bundle)
         self.tables = self.plan.device_tables()
@@ -580,6 +583,7 @@ class RecoupledEvaluator:
             torch.as_tensor(self.plan.energy_weights(weights)).to(self.device).contiguous()
         self._c = ctypes_tables(self.arrays, self.tables)
         self._c.atoms_per_cta = int(atoms_per_cta)
+        self._c.threads_per_cta = int(threads_per_cta)
 
     def _rows(self, A):
         import torch
