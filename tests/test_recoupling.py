@@ -307,3 +307,27 @@ def test_device_source_emulated_flags_damaged_tables(emulated, plan3):
         getattr(bad, field)[index] = value
         st = _emulate(emulated, bad, A, species, k, 2)[4]
         assert st[0] & _native.STATUS_TABLE or st[1] & _native.STATUS_TABLE, field
+
+
+def test_device_source_emulated_channel_diagonal_bundle(emulated):
+    """A row of 25 entries (l <= 4, one channel) in the emulated device source: rows that do
+    not divide the block, and back-propagation without the split (too few components to stage
+    the parts)."""
+    from oracle import oracle
+    b = _bundle("ace_diag_l4_nu4_L0")
+    plan = build_recoupled_plan(b)
+    tabs = plan.device_tables()
+    assert tabs.max_pass_components < (256 // tabs.row_width) * tabs.row_width
+    rng = np.random.default_rng(50)
+    A = rng.normal(size=(5, 1, 25)) + 1j * rng.normal(size=(5, 1, 25))
+    species = np.array([0, 1, 0, 1, 1], dtype=np.int32)
+    w = rng.normal(size=(2, b.feature_count))
+    e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=2)
+    F0 = oracle.bundle_features(b, A, threads=2)
+    for na, th in ((2, 256), (4, 512)):
+        e, G, e2, F, st = _emulate(emulated, tabs, A, species, plan.energy_weights(w), na, th)
+        assert st.tolist() == [0, 0, 0]
+        assert np.abs(e - e0).max() <= 1e-12 * np.abs(e0).max()
+        assert np.abs(e2 - e0).max() <= 1e-12 * np.abs(e0).max()
+        assert np.abs(G - G0).max() <= 1e-12 * np.abs(G0).max()
+        assert np.abs(F - F0).max() <= 1e-12 * np.abs(F0).max()

@@ -14,7 +14,8 @@
 //      so no atomics and a fixed summation order; the energy share
 //      Re(I[c] gI[c]) accumulates per thread;
 //   3. each A-row entry adds its Clebsch-Gordan back-propagation terms
-//      (owner-computes again).
+//      (owner-computes again; a long list is split over the threads that
+//      step 3 would leave idle, and the parts are added in a fixed order).
 // Every table index the kernel follows is checked against the pass or the
 // array it addresses; an entry outside them sets Y3B_STATUS_TABLE and is
 // skipped, so a damaged table cannot reach outside shared memory.

@@ -211,35 +211,53 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
         }
       }
       __syncthreads();
-      // 3. back-propagation into the A rows (each entry owns its sum)
-      for (int i = tid; i < W; i += TH) {
+      // 3. back-propagation into the A rows.  Each entry's list is split into P
+      //    parts when the block has at least two threads per entry (P threads per
+      //    entry); the partial sums go to the component buffer, which step 2 no
+      //    longer needs, and are added to the entry in part order.
+      const int P = (2 * W <= TH && (TH / W) * W <= maxc) ? TH / W : 1;  // uniform
+      double2* part = sI;  // [P][W][NA]
+      for (int u = tid; u < W * P; u += TH) {
+        const int i = u % W, pi = u / W;
         const int64_t at = int64_t(L) * W + i;
         const int b0 = t.bp_begin[at], b1 = t.bp_begin[at + 1];
-        if (b0 < 0 || b1 < b0 || int64_t(b1) > t.bp_count) {
-          bad = true;
-          continue;
-        }
         double2 ga[NA];
 #pragma unroll
-        for (int a = 0; a < NA; ++a) ga[a] = sGA[i * NA + a];
-        for (int q = b0; q < b1; ++q) {
-          const int gi = __ldg(t.bp_gi + q);
-          const int o = __ldg(t.bp_other + q);
-          if (gi < 0 || gi >= nc || o >= W) {
-            bad = true;
-            continue;
-          }
-          const double cv = __ldg(t.bp_value + q);
+        for (int a = 0; a < NA; ++a) ga[a] = make_double2(0.0, 0.0);
+        if (b0 < 0 || b1 < b0 || int64_t(b1) > t.bp_count) {
+          bad = true;
+        } else {
+          const int len = b1 - b0;
+          const int q0 = b0 + (len * pi) / P, q1 = b0 + (len * (pi + 1)) / P;
+          for (int q = q0; q < q1; ++q) {
+            const int gi = __ldg(t.bp_gi + q);
+            const int o = __ldg(t.bp_other + q);
+            if (gi < 0 || gi >= nc || o >= W) {
+              bad = true;
+              continue;
+            }
+            const double cv = __ldg(t.bp_value + q);
 #pragma unroll
-          for (int a = 0; a < NA; ++a) {
-            const double2 g = sG[gi * NA + a];
-            const double2 term = o < 0 ? g : rmul(g, sA[o * NA + a]);
-            ga[a].x = fma(cv, term.x, ga[a].x);
-            ga[a].y = fma(cv, term.y, ga[a].y);
+            for (int a = 0; a < NA; ++a) {
+              const double2 g = sG[gi * NA + a];
+              const double2 term = o < 0 ? g : rmul(g, sA[o * NA + a]);
+              ga[a].x = fma(cv, term.x, ga[a].x);
+              ga[a].y = fma(cv, term.y, ga[a].y);
+            }
           }
         }
 #pragma unroll
-        for (int a = 0; a < NA; ++a) sGA[i * NA + a] = ga[a];
+        for (int a = 0; a < NA; ++a) part[(pi * W + i) * NA + a] = ga[a];
+      }
+      __syncthreads();
+      for (int u = tid; u < W * NA; u += TH) {
+        double2 acc = sGA[u];
+        for (int pi = 0; pi < P; ++pi) {
+          const double2 v = part[pi * W * NA + u];
+          acc.x += v.x;
+          acc.y += v.y;
+        }
+        sGA[u] = acc;
       }
       __syncthreads();
     }
