@@ -146,3 +146,53 @@ extern "C" int emu_recoupled_forward(int na, int th, int features_out, const y3b
 #undef EMU_ENER
   return 0;
 }
+
+// The library's entry points under their own names and C signatures, running the
+// emulated kernels on host memory: the Python wrapper (ye3t_b200.recoupling.
+// RecoupledEvaluator) can be driven through its real ctypes bindings on CPU
+// tensors.  The CTA shape comes from the tables as in the library.
+namespace {
+const char* g_error = "";
+int emu_shape(const y3b_recoupled_tables* t, int& na, int& th) {
+  if (t == nullptr) {
+    g_error = "null tables";
+    return -1;
+  }
+  na = t->atoms_per_cta == 0 ? 1 : t->atoms_per_cta;
+  th = t->threads_per_cta == 0 ? 256 : t->threads_per_cta;
+  if (na < 1 || na > 4 || (th != 256 && th != 512)) {
+    g_error = "bad CTA shape";
+    return -1;
+  }
+  return 0;
+}
+}  // namespace
+
+extern "C" const char* y3b_last_error(void) { return g_error; }
+
+extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                                             const int32_t* species, const double* contraction_weights,
+                                             int64_t species_count, double* energy, void* dEdA, int32_t* status,
+                                             void*) {
+  int na = 1, th = 256;
+  if (emu_shape(tables, na, th)) return -1;
+  return emu_recoupled_energy_grad(na, th, tables, static_cast<const double*>(A), atom_count, species,
+                                   contraction_weights, species_count, energy, static_cast<double*>(dEdA), status);
+}
+
+extern "C" int y3b_ace_recoupled_energy(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                                        const int32_t* species, const double* contraction_weights,
+                                        int64_t species_count, double* energy, int32_t* status, void*) {
+  int na = 1, th = 256;
+  if (emu_shape(tables, na, th)) return -1;
+  return emu_recoupled_forward(na, th, 0, tables, static_cast<const double*>(A), atom_count, species,
+                               contraction_weights, species_count, energy, nullptr, status);
+}
+
+extern "C" int y3b_ace_recoupled_features(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
+                                          void* features, int32_t* status, void*) {
+  int na = 1, th = 256;
+  if (emu_shape(tables, na, th)) return -1;
+  return emu_recoupled_forward(na, th, 1, tables, static_cast<const double*>(A), atom_count, nullptr, nullptr, 0,
+                               nullptr, static_cast<double*>(features), status);
+}

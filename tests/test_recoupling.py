@@ -269,7 +269,7 @@ def c5_case(plan5):
     used = np.where(species >= 3, 0, species).astype(np.int32)
     e0, G0 = oracle.bundle_energy_grad(b, A, used, w, threads=4)
     F0 = oracle.bundle_features(b, A, threads=4)
-    return A, species, plan.energy_weights(w), e0, G0, F0
+    return A, species, plan.energy_weights(w), e0, G0, F0, w
 
 
 @pytest.mark.parametrize("na, th", [(1, 256), (2, 256), (3, 256), (3, 512)])
@@ -278,7 +278,7 @@ def test_device_source_emulated_on_cpu_matches_oracle(emulated, plan5, c5_case, 
     256 or 512 threads with real block barriers and warp exchanges, gives the oracle's energies,
     dE/dA and features for 1-3 atoms per CTA, including a partial last group and a species out
     of range (status INDEX_RANGE, species 0 used)."""
-    A, species, k, e0, G0, F0 = c5_case
+    A, species, k, e0, G0, F0, _ = c5_case
     e, G, e2, F, st = _emulate(emulated, plan5[1].device_tables(), A, species, k, na, th)
     assert st.tolist() == [1, 1, 0]
     assert np.abs(e - e0).max() <= 1e-12 * np.abs(e0).max()
@@ -331,3 +331,38 @@ def test_device_source_emulated_channel_diagonal_bundle(emulated):
         assert np.abs(e2 - e0).max() <= 1e-12 * np.abs(e0).max()
         assert np.abs(G - G0).max() <= 1e-12 * np.abs(G0).max()
         assert np.abs(F - F0).max() <= 1e-12 * np.abs(F0).max()
+
+
+def test_evaluator_glue_through_emulated_entry_points(emulated, plan5, c5_case, monkeypatch):
+    """RecoupledEvaluator's energy_grad / energy / features with their real ctypes bindings
+    (_native._SIGS), the library swapped for the emulation harness, on CPU tensors: the same
+    argument order, table struct and shapes as on the GPU, against the oracle."""
+    import ctypes
+
+    import torch
+    from ye3t_b200 import _native
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    for name in ("y3b_ace_recoupled_energy_grad", "y3b_ace_recoupled_energy", "y3b_ace_recoupled_features"):
+        res, args = _native._SIGS[name]
+        getattr(emulated, name).restype = res
+        getattr(emulated, name).argtypes = args
+    emulated.y3b_last_error.restype = ctypes.c_char_p
+    monkeypatch.setattr(_native, "lib", lambda: emulated)
+    monkeypatch.setattr(_native, "require_cuda", lambda *t, what="": torch.device("cpu"))
+    monkeypatch.setattr(_native, "stream_of", lambda device: 0)
+    b, plan = plan5
+    A, species, _, e0, G0, F0, w = c5_case
+    used = np.where(species >= 3, 0, species).astype(np.int32)
+    ev = RecoupledEvaluator(b, "cpu", w, plan=plan, atoms_per_cta=2, threads_per_cta=512)
+    st = torch.zeros(1, dtype=torch.int32)
+    At, st_sp = torch.as_tensor(A), torch.as_tensor(used)
+    e, G = ev.energy_grad(At, st_sp, status=st)
+    e2 = ev.energy(At, st_sp, status=st)
+    F = ev.features(At, status=st)
+    assert int(st.item()) == 0
+    assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(e2.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()
+    assert np.abs(F.numpy() - F0).max() <= 1e-12 * np.abs(F0).max()
+    with pytest.raises(ValueError):
+        ev.energy_grad(At[:, :4], st_sp)
