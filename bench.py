@@ -59,6 +59,8 @@ def parse():
                     help="atoms per CTA of the recoupled passes (1-4, within shared memory)")
     ap.add_argument("--recoupled-threads", type=int, default=256, choices=[256, 512],
                     help="threads per CTA of the recoupled passes")
+    ap.add_argument("--recoupled-symmetric", action="store_true",
+                    help="the recoupled passes over M >= 0 components (physical densities)")
     ap.add_argument("--no-recoupled-probe", action="store_true",
                     help="skip the one-off look at the recoupled passes after the measurement")
     ap.add_argument("--energy-only", action="store_true",
@@ -238,8 +240,10 @@ def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces
             e0 = ev.energy_from_density(A, sp)
         plan = build_recoupled_plan(bundle)
         shapes, forward = {}, {}
-        for na, th in ((1, 256), (2, 256), (2, 512), (3, 512)):
-            rec = RecoupledEvaluator(bundle, device, weights, plan=plan, atoms_per_cta=na, threads_per_cta=th)
+        for na, th, symmetric in ((1, 256, False), (2, 256, False), (2, 512, False), (3, 512, False),
+                                  (1, 256, True), (2, 256, True), (4, 256, True), (3, 512, True)):
+            rec = RecoupledEvaluator(bundle, device, weights, plan=plan, atoms_per_cta=na, threads_per_cta=th,
+                                     symmetric=symmetric)
             if forces:
                 ms, (e1, G1) = timed(lambda: rec.energy_grad(A, sp))
                 gdiff = float((G1 - G0).abs().max() / G0.abs().max())
@@ -247,12 +251,12 @@ def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces
             else:
                 ms, e1 = timed(lambda: rec.energy(A, sp))
                 gdiff = None
-            shapes[f"{na}x{th}"] = {"ms": ms, "energy_max_rel_diff": float((e1 - e0).abs().max() / e0.abs().max()),
-                                    "dEdA_max_rel_diff": gdiff}
-            if forces and (na, th) in ((1, 256), (2, 512)):
+            key = f"{'symmetric ' if symmetric else ''}{na}x{th}"
+            shapes[key] = {"ms": ms, "energy_max_rel_diff": float((e1 - e0).abs().max() / e0.abs().max()),
+                           "dEdA_max_rel_diff": gdiff}
+            if forces and (na, th) in ((1, 256), (2, 512), (4, 256)):
                 fms, e2 = timed(lambda: rec.energy(A, sp))
-                forward[f"{na}x{th}"] = {"ms": fms,
-                                         "energy_max_rel_diff": float((e2 - e0).abs().max() / e0.abs().max())}
+                forward[key] = {"ms": fms, "energy_max_rel_diff": float((e2 - e0).abs().max() / e0.abs().max())}
         best = min(v["ms"] for v in shapes.values())
         return {"pass": "energy_grad" if forces else "energy", "atoms": int(N),
                 "term_level_ms": ref_ms, "shapes_atoms_x_threads": shapes, "speedup_vs_term_level": ref_ms / best,
@@ -269,8 +273,8 @@ def _config(args):
                         "linear readout",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
             "parallelism": f"atom-block x{args.gpus}",
-            "b_basis": (f"recoupled pair contractions ({args.recoupled_atoms} atoms and "
-                        f"{args.recoupled_threads} threads per CTA)"
+            "b_basis": (f"recoupled pair contractions ({'M >= 0 symmetric, ' if args.recoupled_symmetric else ''}"
+                        f"{args.recoupled_atoms} atoms and {args.recoupled_threads} threads per CTA)"
                         if getattr(args, "recoupled", False) else "term-level factorized schedules"),
             "l2": "inputs larger than L2 (A-basis 2 GB, neighbour list 110 MB at 2^20 atoms)"}
 
@@ -316,7 +320,7 @@ def run_b200(args):
     if args.recoupled:
         from ye3t_b200.recoupling import RecoupledEvaluator
         rec = RecoupledEvaluator(bundle, device, weights, atoms_per_cta=args.recoupled_atoms,
-                                 threads_per_cta=args.recoupled_threads)
+                                 threads_per_cta=args.recoupled_threads, symmetric=args.recoupled_symmetric)
     b_launches = 1 if rec is not None else GRAD_CLASSES
     launches_per_step = 8 + (b_launches + 2 if forces else 1)
 
@@ -458,7 +462,8 @@ def run_b200(args):
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "flops_per_launch": sched_flops_launch,
                      "flops_note": ("FP64 flops of the recoupled pass counted from its tables "
-                                    "(ye3t_b200.recoupling.RecoupledDeviceTables.flops_per_atom)"
+                                    "(ye3t_b200.recoupling.RecoupledDeviceTables / RecoupledSymTables"
+                                    ".flops_per_atom)"
                                     if rec is not None else
                                     "FP64 flops the item walk needs on valid tuples "
                                     "(ye3t_b200.packing.item_grad_flops_per_atom with forces, "

@@ -454,6 +454,46 @@ int y3b_ace_recoupled_energy(const y3b_recoupled_tables* tables, const void* A, 
 int y3b_ace_recoupled_features(const y3b_recoupled_tables* tables, const void* A, int64_t atom_count,
                                void* features, int32_t* status, void* stream);
 
+/* Symmetric passes of the same plan for physical densities, A[n, l, -m] =
+ * (-1)^m conj(A[n, l, m]) (real radial functions and prefactors, the densities
+ * y3b_ace_density produces): only the M >= 0 components are formed, and dE/dA
+ * is mirrored to m < 0.  Tables: ye3t_b200.recoupling.RecoupledSymTables
+ * (comp (a, b, cg_begin, cg_count), (M, own_begin, own_count, (-1)^p); bp_gi
+ * 2 * component + conj flag; mirror and dot as documented there).  A density
+ * without the symmetry gives wrong results: use the general passes for it. */
+typedef struct {
+  int32_t pass_count;
+  int32_t max_pass_components;
+  int32_t row_width;
+  int32_t dot_count;
+  int64_t component_count;
+  int64_t cg_count;
+  int64_t own_count;
+  int64_t bp_count;
+  const int32_t* pass_begin; /* [pass_count + 1] */
+  const int32_t* comp;       /* [component_count, 8], 16-byte aligned */
+  const int32_t* cg_index;   /* [cg_count] */
+  const double* cg_value;    /* [cg_count] */
+  const int32_t* own;        /* [own_count, 2], 8-byte aligned */
+  const int32_t* bp_begin;   /* [pass_count * row_width + 1] */
+  const int32_t* bp_gi;      /* [bp_count] */
+  const int32_t* bp_other;   /* [bp_count] */
+  const double* bp_value;    /* [bp_count] */
+  const int32_t* mirror;     /* [row_width] */
+  const int32_t* dot_begin;  /* [pass_count + 1] */
+  const int32_t* dot;        /* [dot_count, 4], 16-byte aligned */
+  int32_t atoms_per_cta;     /* 0 (one) or 1..4, within shared memory */
+  int32_t threads_per_cta;   /* 0 (256), 256 or 512 */
+} y3b_recoupled_sym_tables;
+
+int y3b_ace_recoupled_energy_grad_symmetric(const y3b_recoupled_sym_tables* tables, const void* A,
+                                            int64_t atom_count, const int32_t* species,
+                                            const double* contraction_weights, int64_t species_count,
+                                            double* energy, void* dEdA, int32_t* status, void* stream);
+int y3b_ace_recoupled_energy_symmetric(const y3b_recoupled_sym_tables* tables, const void* A, int64_t atom_count,
+                                       const int32_t* species, const double* contraction_weights,
+                                       int64_t species_count, double* energy, int32_t* status, void* stream);
+
 /* Forces F_k = -dE/dr_k = sum_{e in row k} (g_e - g_rev(e)) from the rows of
  * all atoms (deterministic gather; rev(e) is the reverse edge). */
 int y3b_forces_gather(const int64_t* row_offsets, const int32_t* neighbors, int64_t atom_count,

@@ -196,3 +196,46 @@ extern "C" int y3b_ace_recoupled_features(const y3b_recoupled_tables* tables, co
   return emu_recoupled_forward(na, th, 1, tables, static_cast<const double*>(A), atom_count, nullptr, nullptr, 0,
                                nullptr, static_cast<double*>(features), status);
 }
+
+// Symmetric passes (physical densities).
+extern "C" int y3b_ace_recoupled_energy_grad_symmetric(const y3b_recoupled_sym_tables* tables, const void* A,
+                                                       int64_t atom_count, const int32_t* species,
+                                                       const double* k, int64_t species_count, double* energy,
+                                                       void* dEdA, int32_t* status, void*) {
+  int na = 1, th = 256;
+  if (tables == nullptr) return -1;
+  na = tables->atoms_per_cta == 0 ? 1 : tables->atoms_per_cta;
+  th = tables->threads_per_cta == 0 ? 256 : tables->threads_per_cta;
+  const y3b::SymTabs t = y3b::sym_view(*tables);
+  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * t.max_pass_components) * 16;
+  if (smem > sizeof(y3b_emulated_smem)) return -1;
+  const auto* a2 = static_cast<const double2*>(A);
+  auto* g2 = static_cast<double2*>(dEdA);
+#define EMU_SGRAD(N, T)                                                                                            \
+  run_block(T, [&] {                                                                                               \
+    y3b::recoupled_sym_energy_grad_kernel<N, T>(t, a2, atom_count, species, k, species_count, energy, g2, status); \
+  })
+  EMU_SHAPES(EMU_SGRAD)
+#undef EMU_SGRAD
+  return 0;
+}
+
+extern "C" int y3b_ace_recoupled_energy_symmetric(const y3b_recoupled_sym_tables* tables, const void* A,
+                                                  int64_t atom_count, const int32_t* species, const double* k,
+                                                  int64_t species_count, double* energy, int32_t* status, void*) {
+  int na = 1, th = 256;
+  if (tables == nullptr) return -1;
+  na = tables->atoms_per_cta == 0 ? 1 : tables->atoms_per_cta;
+  th = tables->threads_per_cta == 0 ? 256 : tables->threads_per_cta;
+  const y3b::SymTabs t = y3b::sym_view(*tables);
+  const size_t smem = size_t(na) * size_t(t.row_width + t.max_pass_components) * 16;
+  if (smem > sizeof(y3b_emulated_smem)) return -1;
+  const auto* a2 = static_cast<const double2*>(A);
+#define EMU_SENER(N, T)                                                                                          \
+  run_block(T, [&] {                                                                                             \
+    y3b::recoupled_sym_energy_kernel<N, T>(t, a2, atom_count, species, k, species_count, energy, nullptr, status); \
+  })
+  EMU_SHAPES(EMU_SENER)
+#undef EMU_SENER
+  return 0;
+}

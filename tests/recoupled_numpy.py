@@ -164,3 +164,76 @@ def walk_forward(tabs, A, species=None, k=None):
             else:
                 F[:, tabs.feat_index[f0:f0 + fn]] += tabs.feat_weight[f0:f0 + fn][None, :] * T[:, None]
     return e if k is not None else F
+
+
+def walk_sym_tables(tabs, A, species, k):
+    """The symmetric device pass over ``RecoupledSymTables`` (physical densities), restated
+    loop for loop: per L the ``M >= 0`` components, their adjoints
+    ``(-1)^p conj(sum k I_partner[M])``, the energy share, the back-propagation into the
+    ``m >= 0`` half of the A row; then the mirror.  Returns (energies, G)."""
+    N = A.shape[0]
+    W = tabs.row_width
+    row = A.reshape(N, W)
+    kz = np.asarray(k)[np.asarray(species)]
+    G = np.zeros((N, W), dtype=np.complex128)
+    e = np.zeros(N)
+    for L in range(tabs.pass_count):
+        c0, c1 = int(tabs.pass_begin[L]), int(tabs.pass_begin[L + 1])
+        I = np.zeros((N, c1 - c0), dtype=np.complex128)
+        for c in range(c0, c1):
+            a, b, q0, qn = (int(v) for v in tabs.comp[c, :4])
+            if a < 0:
+                I[:, c - c0] = 1.0
+            elif qn == 0:
+                I[:, c - c0] = row[:, a]
+            else:
+                q = tabs.cg_index[q0:q0 + qn]
+                I[:, c - c0] = (tabs.cg_value[q0:q0 + qn] * row[:, a + (q & 255)] * row[:, b + (q >> 8)]).sum(axis=1)
+        gI = np.zeros_like(I)
+        for c in range(c0, c1):
+            M, o0, on, sgn = (int(v) for v in tabs.comp[c, 4:8])
+            ent = tabs.own[o0:o0 + on]
+            gI[:, c - c0] = sgn * np.conj((kz[:, ent[:, 1]] * I[:, ent[:, 0] + M]).sum(axis=1))
+            wM = 0.5 if M == 0 else 1.0
+            e += wM * (I[:, c - c0] * gI[:, c - c0]).real
+        for t in range(W):
+            b0, b1 = int(tabs.bp_begin[L * W + t]), int(tabs.bp_begin[L * W + t + 1])
+            if b1 == b0:
+                continue
+            code, other, val = tabs.bp_gi[b0:b1], tabs.bp_other[b0:b1], tabs.bp_value[b0:b1]
+            g = gI[:, code >> 1]
+            g = np.where((code & 1)[None, :] == 1, np.conj(g), g)
+            partner = np.where(other[None, :] < 0, 1.0, row[:, np.maximum(other, 0)])
+            G[:, t] += (val * g * partner).sum(axis=1)
+    for t in range(W):
+        m = int(tabs.mirror[t])
+        if m >= 0:
+            G[:, t] = (-1.0 if m & 1 else 1.0) * np.conj(G[:, m >> 1])
+    return e, G.reshape(A.shape)
+
+
+def walk_sym_forward(tabs, A, species, k):
+    """The symmetric forward energy: ``T_d = (-1)^p_B (Re(I_A[0] conj(I_B[0])) +
+    2 sum_{M > 0} Re(I_A[M] conj(I_B[M])))``, ``e = sum_d k[z, d] T_d``."""
+    N = A.shape[0]
+    row = A.reshape(N, tabs.row_width)
+    kz = np.asarray(k)[np.asarray(species)]
+    e = np.zeros(N)
+    for L in range(tabs.pass_count):
+        c0, c1 = int(tabs.pass_begin[L]), int(tabs.pass_begin[L + 1])
+        I = np.zeros((N, c1 - c0), dtype=np.complex128)
+        for c in range(c0, c1):
+            a, b, q0, qn = (int(v) for v in tabs.comp[c, :4])
+            if a < 0:
+                I[:, c - c0] = 1.0
+            elif qn == 0:
+                I[:, c - c0] = row[:, a]
+            else:
+                q = tabs.cg_index[q0:q0 + qn]
+                I[:, c - c0] = (tabs.cg_value[q0:q0 + qn] * row[:, a + (q & 255)] * row[:, b + (q >> 8)]).sum(axis=1)
+        wts = np.array([1.0] + [2.0] * L)
+        for d in range(int(tabs.dot_begin[L]), int(tabs.dot_begin[L + 1])):
+            oa, ob, sgn, _ = (int(v) for v in tabs.dot[d])
+            T = sgn * (wts * (I[:, oa:oa + L + 1] * np.conj(I[:, ob:ob + L + 1])).real).sum(axis=1)
+            e += kz[:, d] * T
+    return e

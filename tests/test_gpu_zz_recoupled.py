@@ -89,3 +89,44 @@ def test_recoupled_species_out_of_range_sets_status():
                           status=st)
     assert int(st.item()) & _native.STATUS_INDEX_RANGE
     assert torch.isfinite(e).all() and torch.isfinite(G).all()
+
+
+def test_symmetric_passes_on_physical_densities(golden):
+    """The symmetric passes (M >= 0 only) on densities from y3b_ace_density: against the oracle
+    on six atoms of the golden system, and against the general recoupled pass and the
+    term-level adjoint on 4,096 atoms of a random periodic system."""
+    from oracle import oracle
+    from ye3t_b200.ace import ACEConfig, ACEEvaluator
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    b, plan, _, _, _, _, _, _ = _case("ace_n8_l3_nu4_L0")
+    g = golden("ace_small")
+    A6 = np.ascontiguousarray(np.asarray(g["A"])[:6])
+    sp6 = np.asarray(g["species"])[:6].astype(np.int32)
+    rng = np.random.default_rng(24)
+    w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
+    e0, G0 = oracle.bundle_energy_grad(b, A6, sp6, w, threads=4)
+    for na, th in ((1, 256), (4, 256), (3, 512)):
+        sym = RecoupledEvaluator(b, DEV, w, plan=plan, atoms_per_cta=na, threads_per_cta=th, symmetric=True)
+        st = torch.zeros(1, dtype=torch.int32, device=DEV)
+        e1, G1 = (x.cpu().numpy() for x in sym.energy_grad(torch.as_tensor(A6, device=DEV),
+                                                            torch.as_tensor(sp6, device=DEV), status=st))
+        assert int(st.item()) == 0
+        assert np.abs(e1 - e0).max() <= 1e-12 * np.abs(e0).max()
+        assert np.abs(G1 - G0).max() <= 1e-12 * np.abs(G0).max()
+    n = 4096
+    box = (n / 0.05) ** (1.0 / 3.0)
+    pos = torch.as_tensor(rng.uniform(0, box, size=(n, 3)), device=DEV)
+    sp = torch.as_tensor(rng.integers(0, 3, n).astype(np.int32), device=DEV)
+    ev = ACEEvaluator(b, DEV, config=ACEConfig(5.0, 5.0), species_prefactor=[1.0, 0.75, 1.25], weights=w)
+    row, nbr = ev.neighbor_list(pos, box)
+    A = ev.density(pos, sp, box, row, nbr)
+    et, Gt = ev.energy_grad(A, sp)
+    gen = RecoupledEvaluator(b, DEV, w, plan=plan)
+    sym = RecoupledEvaluator(b, DEV, w, plan=plan, atoms_per_cta=2, threads_per_cta=512, symmetric=True)
+    eg, Gg = gen.energy_grad(A, sp)
+    es, Gs = sym.energy_grad(A, sp)
+    es2 = sym.energy(A, sp)
+    for e, G in ((eg, Gg), (es, Gs)):
+        assert float((e - et).abs().max()) <= 1e-12 * float(et.abs().max())
+        assert float((G - Gt).abs().max()) <= 1e-12 * float(Gt.abs().max())
+    assert float((es2 - et).abs().max()) <= 1e-12 * float(et.abs().max())

@@ -104,7 +104,8 @@ def test_torch_ops_registered_with_fake_kernels():
 
 
 @pytest.mark.parametrize("struct, c_name", [("AceTables", "y3b_ace_tables"),
-                                             ("RecoupledTables", "y3b_recoupled_tables")])
+                                             ("RecoupledTables", "y3b_recoupled_tables"),
+                                             ("RecoupledSymTables", "y3b_recoupled_sym_tables")])
 def test_tables_struct_layout_matches_header(tmp_path, struct, c_name):
     """The ctypes mirrors of the table structs (y3b_ace_tables is passed by value to every
     fused kernel) have the C structs' sizes and field offsets, read from include/ye3t_b200.h

@@ -366,3 +366,85 @@ def test_evaluator_glue_through_emulated_entry_points(emulated, plan5, c5_case, 
     assert np.abs(F.numpy() - F0).max() <= 1e-12 * np.abs(F0).max()
     with pytest.raises(ValueError):
         ev.energy_grad(At[:, :4], st_sp)
+
+
+@pytest.fixture(scope="module")
+def physical_case(plan5, golden):
+    """Six atoms of the golden 96-atom system (physical densities from the reference) with
+    the oracle's energies and dE/dA."""
+    from oracle import oracle
+    b, plan = plan5
+    g = golden("ace_small")
+    A = np.ascontiguousarray(np.asarray(g["A"])[:6])
+    species = np.asarray(g["species"])[:6].astype(np.int32)
+    w = np.random.default_rng(60).normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
+    e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=4)
+    return A, species, w, e0, G0
+
+
+def test_symmetric_tables_walk_matches_oracle_on_physical_densities(plan5, physical_case):
+    """The M >= 0 tables of the symmetric passes, walked loop for loop on the reference's own
+    densities, give the oracle's energies and dE/dA; they hold 59 % of the components."""
+    b, plan = plan5
+    tabs = plan.sym_device_tables()
+    assert (tabs.comp.shape[0], tabs.max_pass_components) == (4114, 1248)
+    assert 4 * tabs.smem_bytes() <= 224 * 1024
+    A, species, w, e0, G0 = physical_case
+    k = plan.energy_weights(w)
+    e1, G1 = rn.walk_sym_tables(tabs, A, species, k)
+    e2 = rn.walk_sym_forward(tabs, A, species, k)
+    assert np.abs(e1 - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(e2 - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G1 - G0).max() <= 1e-12 * np.abs(G0).max()
+
+
+def test_symmetric_tables_refuse_an_odd_parity_word_set(plan5):
+    """The symmetric passes need both segments of every contraction to share their parity,
+    which holds for parity-even word sets only: a contraction of an odd pair with an even
+    segment is refused."""
+    import copy
+
+    from ye3t_b200.recoupling import SEG_PAIR
+    plan = copy.deepcopy(plan5[1])
+    pairs = np.nonzero(plan.seg_kind == SEG_PAIR)[0]
+    odd = [int(s) for s in pairs if (plan.seg_a[s] % 4 + plan.seg_b[s] % 4 - plan.seg_L[s]) % 2]
+    assert odd
+    L = int(plan.seg_L[odd[0]])
+    even = [s for s in range(plan.segment_count) if s not in set(odd) and int(plan.seg_L[s]) == L]
+    d = int(np.nonzero(plan.dot_L == L)[0][0])
+    plan.dot_a[d], plan.dot_b[d] = odd[0], even[0]
+    with pytest.raises(ValueError, match="parity-even"):
+        plan.sym_device_tables()
+
+
+@pytest.mark.parametrize("na, th", [(1, 256), (4, 256), (3, 512)])
+def test_symmetric_device_source_emulated_matches_oracle(emulated, plan5, physical_case, na, th, monkeypatch):
+    """The symmetric kernels' own source, emulated on the CPU through RecoupledEvaluator's real
+    ctypes bindings (symmetric=True), on the reference's densities: the oracle's energies and
+    dE/dA, with dE/dA's m < 0 half mirrored."""
+    import ctypes
+
+    import torch
+    from ye3t_b200 import _native
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    for name in ("y3b_ace_recoupled_energy_grad_symmetric", "y3b_ace_recoupled_energy_symmetric"):
+        res, args = _native._SIGS[name]
+        getattr(emulated, name).restype = res
+        getattr(emulated, name).argtypes = args
+    emulated.y3b_last_error.restype = ctypes.c_char_p
+    monkeypatch.setattr(_native, "lib", lambda: emulated)
+    monkeypatch.setattr(_native, "require_cuda", lambda *t, what="": torch.device("cpu"))
+    monkeypatch.setattr(_native, "stream_of", lambda device: 0)
+    b, plan = plan5
+    A, species, w, e0, G0 = physical_case
+    ev = RecoupledEvaluator(b, "cpu", w, plan=plan, atoms_per_cta=na, threads_per_cta=th, symmetric=True)
+    st = torch.zeros(1, dtype=torch.int32)
+    At, sp = torch.as_tensor(A), torch.as_tensor(species)
+    e, G = ev.energy_grad(At, sp, status=st)
+    e2 = ev.energy(At, sp, status=st)
+    assert int(st.item()) == 0
+    assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(e2.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()
+    with pytest.raises(ValueError, match="general passes"):
+        ev.features(At)

@@ -65,6 +65,18 @@ class RecoupledTables(ctypes.Structure):
     ]
 
 
+class RecoupledSymTables(ctypes.Structure):
+    """``y3b_recoupled_sym_tables`` (include/ye3t_b200.h)."""
+
+    _fields_ = [
+        ("pass_count", I32), ("max_pass_components", I32), ("row_width", I32), ("dot_count", I32),
+        ("component_count", I64), ("cg_count", I64), ("own_count", I64), ("bp_count", I64),
+        ("pass_begin", VP), ("comp", VP), ("cg_index", VP), ("cg_value", VP), ("own", VP),
+        ("bp_begin", VP), ("bp_gi", VP), ("bp_other", VP), ("bp_value", VP), ("mirror", VP),
+        ("dot_begin", VP), ("dot", VP), ("atoms_per_cta", I32), ("threads_per_cta", I32),
+    ]
+
+
 _SIGS = {
     "y3b_abi_version": (I32, []),
     "y3b_last_error": (ctypes.c_char_p, []),
@@ -108,6 +120,10 @@ _SIGS = {
     "y3b_ace_recoupled_energy": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, I64, VP, VP,
                                                 VP]),
     "y3b_ace_recoupled_features": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, VP]),
+    "y3b_ace_recoupled_energy_grad_symmetric": (ctypes.c_int, [ctypes.POINTER(RecoupledSymTables), VP, I64, VP,
+                                                               VP, I64, VP, VP, VP, VP]),
+    "y3b_ace_recoupled_energy_symmetric": (ctypes.c_int, [ctypes.POINTER(RecoupledSymTables), VP, I64, VP, VP,
+                                                          I64, VP, VP, VP]),
     "y3b_ace_edge_grad": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                          VP, VP]),
     "y3b_forces_gather": (ctypes.c_int, [VP, VP, I64, VP, VP, VP, VP]),

@@ -51,7 +51,8 @@ int check_tables(const y3b_recoupled_tables* tables) {
 
 // Launch shape from the tables: atoms per CTA (0 means 1; 1..4) and threads
 // per CTA (0 means 256; 256 or 512).
-int launch_shape(const y3b_recoupled_tables& t, int& na, int& th) {
+template <typename T>
+int launch_shape(const T& t, int& na, int& th) {
   na = t.atoms_per_cta == 0 ? 1 : t.atoms_per_cta;
   th = t.threads_per_cta == 0 ? 256 : t.threads_per_cta;
   Y3B_CHECK_ARG(na >= 1 && na <= 4, "atoms_per_cta must be 0 (one) or in [1, 4]");
@@ -59,9 +60,9 @@ int launch_shape(const y3b_recoupled_tables& t, int& na, int& th) {
   return Y3B_OK;
 }
 
-template <typename Kernel>
+template <typename Kernel, typename Tabs>
 int launch_grouped(Kernel kernel, int threads, size_t smem_per_atom, int na, int64_t atom_count, cudaStream_t s,
-                   const RecTabs& rt, const void* A, const int32_t* species, const double* weights,
+                   const Tabs& rt, const void* A, const int32_t* species, const double* weights,
                    int64_t species_count, double* energy, void* out, int32_t* status) {
   const size_t smem = smem_per_atom * size_t(na);
   Y3B_CHECK_ARG(smem <= 224 * 1024,
@@ -147,4 +148,66 @@ extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables,
   Y3B_REC_DISPATCH(Y3B_GRAD, per_atom, na, atom_count, s, rt, A, species, contraction_weights, species_count,
                    energy, dEdA, status)
 #undef Y3B_GRAD
+}
+
+namespace {
+
+int check_sym_tables(const y3b_recoupled_sym_tables* tables) {
+  Y3B_CHECK_ARG(tables != nullptr, "null tables");
+  const y3b_recoupled_sym_tables& t = *tables;
+  Y3B_CHECK_ARG(t.pass_count >= 1 && t.pass_count <= 64, "pass_count must be in [1, 64]");
+  Y3B_CHECK_ARG(t.row_width >= 1 && t.row_width <= 4096, "row_width must be in [1, 4096]");
+  Y3B_CHECK_ARG(t.max_pass_components >= 1 && t.dot_count >= 1, "empty recoupled tables");
+  Y3B_CHECK_ARG(t.component_count >= 1 && t.cg_count >= 0 && t.own_count >= 0 && t.bp_count >= 0,
+                "negative table sizes");
+  Y3B_CHECK_ARG(t.pass_begin && t.comp && t.own && t.bp_begin && t.bp_gi && t.bp_other && t.bp_value &&
+                    t.mirror && t.dot_begin && t.dot && (t.cg_count == 0 || (t.cg_index && t.cg_value)),
+                "null table pointer");
+  Y3B_CHECK_ARG(reinterpret_cast<uintptr_t>(t.comp) % 16 == 0 && reinterpret_cast<uintptr_t>(t.dot) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(t.own) % 8 == 0,
+                "comp and dot must be 16-byte and own 8-byte aligned");
+  return Y3B_OK;
+}
+
+}  // namespace
+
+extern "C" int y3b_ace_recoupled_energy_grad_symmetric(const y3b_recoupled_sym_tables* tables, const void* A,
+                                                       int64_t atom_count, const int32_t* species,
+                                                       const double* contraction_weights, int64_t species_count,
+                                                       double* energy, void* dEdA, int32_t* status, void* stream) {
+  if (int rc = check_sym_tables(tables)) return rc;
+  const y3b_recoupled_sym_tables& t = *tables;
+  int na = 1, th = 256;
+  if (int rc = launch_shape(t, na, th)) return rc;
+  Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
+  if (atom_count == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(A && species && contraction_weights && energy && dEdA && species_count > 0,
+                "null pointer argument");
+  const size_t per_atom = size_t(2 * int64_t(t.row_width) + 2 * int64_t(t.max_pass_components)) * sizeof(double2);
+  const SymTabs rt = sym_view(t);
+  cudaStream_t s = as_stream(stream);
+#define Y3B_SGRAD(N, T) recoupled_sym_energy_grad_kernel<N, T>
+  Y3B_REC_DISPATCH(Y3B_SGRAD, per_atom, na, atom_count, s, rt, A, species, contraction_weights, species_count,
+                   energy, dEdA, status)
+#undef Y3B_SGRAD
+}
+
+extern "C" int y3b_ace_recoupled_energy_symmetric(const y3b_recoupled_sym_tables* tables, const void* A,
+                                                  int64_t atom_count, const int32_t* species,
+                                                  const double* contraction_weights, int64_t species_count,
+                                                  double* energy, int32_t* status, void* stream) {
+  if (int rc = check_sym_tables(tables)) return rc;
+  const y3b_recoupled_sym_tables& t = *tables;
+  int na = 1, th = 256;
+  if (int rc = launch_shape(t, na, th)) return rc;
+  Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
+  if (atom_count == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(A && species && contraction_weights && energy && species_count > 0, "null pointer argument");
+  const size_t per_atom = size_t(int64_t(t.row_width) + int64_t(t.max_pass_components)) * sizeof(double2);
+  const SymTabs rt = sym_view(t);
+  cudaStream_t s = as_stream(stream);
+#define Y3B_SENER(N, T) recoupled_sym_energy_kernel<N, T>
+  Y3B_REC_DISPATCH(Y3B_SENER, per_atom, na, atom_count, s, rt, A, species, contraction_weights, species_count,
+                   energy, nullptr, status)
+#undef Y3B_SENER
 }

@@ -65,12 +65,38 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   return s;
 }
 
+// Tables of the symmetric passes (physical densities, M >= 0 components only).
+struct SymTabs {
+  int32_t pass_count, max_pass_components, row_width, dot_count;
+  int64_t component_count, cg_count, own_count, bp_count;
+  const int32_t* pass_begin;
+  const int4* comp;  // (a, b, cg_begin, cg_count), (M, own_begin, own_count, (-1)^p)
+  const int32_t* cg_index;
+  const double* cg_value;
+  const int2* own;  // (partner's M = 0 local component, contraction)
+  const int32_t* bp_begin;
+  const int32_t* bp_gi;  // 2 * component + (1: conj(gI) of a negative M)
+  const int32_t* bp_other;
+  const double* bp_value;
+  const int32_t* mirror;  // 2 * (entry of -m) + (m & 1) for an entry of negative m, else -1
+  const int32_t* dot_begin;
+  const int4* dot;  // (A's M = 0 local component, B's, (-1)^p_B, 0)
+};
+
+inline SymTabs sym_view(const y3b_recoupled_sym_tables& t) {
+  return SymTabs{t.pass_count, t.max_pass_components, t.row_width, t.dot_count,
+                 t.component_count, t.cg_count, t.own_count, t.bp_count,
+                 t.pass_begin, reinterpret_cast<const int4*>(t.comp), t.cg_index, t.cg_value,
+                 reinterpret_cast<const int2*>(t.own), t.bp_begin, t.bp_gi, t.bp_other, t.bp_value,
+                 t.mirror, t.dot_begin, reinterpret_cast<const int4*>(t.dot)};
+}
+
 // Shared-memory arrays hold NA atoms side by side: entry e of atom a at
 // [e * NA + a].  A CTA takes atoms [g NA, g NA + NA); every table entry it
 // loads (coupling term, contraction-list entry, back-propagation entry,
 // contraction) serves all NA atoms, and the NA sums are independent chains.
-template <int NA, int TH>
-__device__ __forceinline__ void build_components(const RecTabs& t, const double2* sA, double2* sI, int c0, int nc,
+template <int NA, int TH, typename Tabs>
+__device__ __forceinline__ void build_components(const Tabs& t, const double2* sA, double2* sI, int c0, int nc,
                                                  int W, bool& bad) {
   for (int c = threadIdx.x; c < nc; c += TH) {
     const int4 d = __ldg(t.comp + 2 * (c0 + c));
@@ -375,6 +401,227 @@ recoupled_forward_kernel(RecTabs t, const double2* __restrict__ A, int64_t atom_
         __syncthreads();
       }
     } else {
+      __syncthreads();
+    }
+  }
+}
+
+// Symmetric adjoint (physical densities): per L the M >= 0 components, their
+// adjoints gI[M] = (-1)^p conj(sum_q k[d_q] I_partner[M]), the energy
+// 1/2 Re(I[0] gI[0]) + sum_{M>0} Re(I[M] gI[M]), and the back-propagation into
+// the m >= 0 half of each A row (entries of a negative M read conj(gI)); the
+// m < 0 half is mirrored at the end, G[-m] = (-1)^m conj(G[m]).
+template <int NA, int TH>
+__global__ void __launch_bounds__(TH)
+recoupled_sym_energy_grad_kernel(SymTabs t, const double2* __restrict__ A, int64_t atom_count,
+                                 const int32_t* __restrict__ species, const double* __restrict__ k,
+                                 int64_t species_count, double* __restrict__ energy, double2* __restrict__ G,
+                                 int32_t* status) {
+  Y3B_DYNAMIC_SMEM(double2, rec_smem);
+  __shared__ double red[TH / 32];
+  const int W = t.row_width;
+  const int maxc = t.max_pass_components;
+  double2* sA = rec_smem;
+  double2* sGA = sA + W * NA;
+  double2* sI = sGA + W * NA;
+  double2* sG = sI + maxc * NA;
+  const int tid = threadIdx.x;
+  const int64_t groups = (atom_count + NA - 1) / NA;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t first = grp * NA;
+    const double* kz[NA];
+    const int nv = load_atoms<NA, TH>(first, atom_count, W, A, species, k, species_count, t.dot_count, sA, sGA, kz,
+                                      status);
+    double ep[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) ep[a] = 0.0;
+    bool bad = false;
+    __syncthreads();
+    for (int L = 0; L < t.pass_count; ++L) {
+      const int c0 = t.pass_begin[L];
+      const int nc = t.pass_begin[L + 1] - c0;
+      if (c0 < 0 || nc < 0 || nc > maxc || int64_t(c0) + nc > t.component_count) {
+        bad = true;  // uniform over the block
+        continue;
+      }
+      build_components<NA, TH>(t, sA, sI, c0, nc, W, bad);
+      __syncthreads();
+      for (int c = tid; c < nc; c += TH) {
+        const int4 d = __ldg(t.comp + 2 * (c0 + c) + 1);  // (M, own_begin, own_count, sign)
+        double2 acc[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) acc[a] = make_double2(0.0, 0.0);
+        if (d.y < 0 || d.z < 0 || int64_t(d.y) + d.z > t.own_count) {
+          bad = true;
+        } else {
+          for (int q = d.y; q < d.y + d.z; ++q) {
+            const int2 e = __ldg(t.own + q);
+            const int p = e.x + d.x;
+            if (p < 0 || p >= nc || e.y < 0 || e.y >= t.dot_count) {
+              bad = true;
+              continue;
+            }
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              const double kk = __ldg(kz[a] + e.y);
+              const double2 v = sI[p * NA + a];
+              acc[a].x = fma(kk, v.x, acc[a].x);
+              acc[a].y = fma(kk, v.y, acc[a].y);
+            }
+          }
+        }
+        const double sg = d.w < 0 ? -1.0 : 1.0;
+        const double wm = d.x == 0 ? 0.5 : 1.0;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+          const double2 g = make_double2(sg * acc[a].x, -sg * acc[a].y);
+          sG[c * NA + a] = g;
+          const double2 iv = sI[c * NA + a];
+          ep[a] = fma(wm, iv.x * g.x - iv.y * g.y, ep[a]);
+        }
+      }
+      __syncthreads();
+      const int P = (2 * W <= TH && (TH / W) * W <= maxc) ? TH / W : 1;  // uniform
+      double2* part = sI;  // [P][W][NA]; step 2 is done with sI
+      for (int u = tid; u < W * P; u += TH) {
+        const int i = u % W, pi = u / W;
+        const int64_t at = int64_t(L) * W + i;
+        const int b0 = t.bp_begin[at], b1 = t.bp_begin[at + 1];
+        double2 ga[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) ga[a] = make_double2(0.0, 0.0);
+        if (b0 < 0 || b1 < b0 || int64_t(b1) > t.bp_count) {
+          bad = true;
+        } else {
+          const int len = b1 - b0;
+          const int q0 = b0 + (len * pi) / P, q1 = b0 + (len * (pi + 1)) / P;
+          for (int q = q0; q < q1; ++q) {
+            const int code = __ldg(t.bp_gi + q);
+            const int gi = code >> 1;
+            const int o = __ldg(t.bp_other + q);
+            if (code < 0 || gi >= nc || o >= W) {
+              bad = true;
+              continue;
+            }
+            const double cv = __ldg(t.bp_value + q);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              double2 g = sG[gi * NA + a];
+              if (code & 1) g.y = -g.y;
+              const double2 term = o < 0 ? g : rmul(g, sA[o * NA + a]);
+              ga[a].x = fma(cv, term.x, ga[a].x);
+              ga[a].y = fma(cv, term.y, ga[a].y);
+            }
+          }
+        }
+#pragma unroll
+        for (int a = 0; a < NA; ++a) part[(pi * W + i) * NA + a] = ga[a];
+      }
+      __syncthreads();
+      for (int u = tid; u < W * NA; u += TH) {
+        double2 acc = sGA[u];
+        for (int pi = 0; pi < P; ++pi) {
+          const double2 v = part[pi * W * NA + u];
+          acc.x += v.x;
+          acc.y += v.y;
+        }
+        sGA[u] = acc;
+      }
+      __syncthreads();
+    }
+    // the m < 0 half of each row from the m > 0 half (sources and targets are disjoint)
+    for (int u = tid; u < W * NA; u += TH) {
+      const int i = u / NA, a = u % NA;
+      const int mi = __ldg(t.mirror + i);
+      if (mi < 0) continue;
+      const int src = mi >> 1;
+      if (src >= W) {
+        bad = true;
+        continue;
+      }
+      const double2 v = sGA[src * NA + a];
+      const double sg = (mi & 1) ? -1.0 : 1.0;
+      sGA[u] = make_double2(sg * v.x, -sg * v.y);
+    }
+    __syncthreads();
+    if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
+    for (int i = tid; i < W * NA; i += TH) {
+      const int a = i % NA, e = i / NA;
+      if (a < nv) G[(first + a) * W + e] = sGA[i];
+    }
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      const double total = block_sum<TH>(ep[a], red);
+      if (tid == 0 && a < nv) energy[first + a] = total;
+      __syncthreads();
+    }
+  }
+}
+
+// Symmetric forward energy: T_d = (-1)^p_B (Re(I_A[0] conj(I_B[0])) +
+// 2 sum_{M>0} Re(I_A[M] conj(I_B[M]))), e = sum_d k[z, d] T_d.
+template <int NA, int TH>
+__global__ void __launch_bounds__(TH)
+recoupled_sym_energy_kernel(SymTabs t, const double2* __restrict__ A, int64_t atom_count,
+                            const int32_t* __restrict__ species, const double* __restrict__ k, int64_t species_count,
+                            double* __restrict__ energy, double2* __restrict__ unused, int32_t* status) {
+  Y3B_DYNAMIC_SMEM(double2, rec_smem);
+  __shared__ double red[TH / 32];
+  const int W = t.row_width;
+  double2* sA = rec_smem;
+  double2* sI = sA + W * NA;
+  const int tid = threadIdx.x;
+  const int64_t groups = (atom_count + NA - 1) / NA;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t first = grp * NA;
+    const double* kz[NA];
+    const int nv = load_atoms<NA, TH>(first, atom_count, W, A, species, k, species_count, t.dot_count, sA, nullptr,
+                                      kz, status);
+    double ep[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) ep[a] = 0.0;
+    bool bad = false;
+    __syncthreads();
+    for (int L = 0; L < t.pass_count; ++L) {
+      const int c0 = t.pass_begin[L];
+      const int nc = t.pass_begin[L + 1] - c0;
+      const int d0 = t.dot_begin[L];
+      const int nd = t.dot_begin[L + 1] - d0;
+      if (c0 < 0 || nc < 0 || nc > t.max_pass_components || int64_t(c0) + nc > t.component_count || d0 < 0 ||
+          nd < 0 || int64_t(d0) + nd > t.dot_count) {
+        bad = true;  // uniform over the block
+        continue;
+      }
+      build_components<NA, TH>(t, sA, sI, c0, nc, W, bad);
+      __syncthreads();
+      for (int j = tid; j < nd; j += TH) {
+        const int4 q = __ldg(t.dot + d0 + j);
+        if (q.x < 0 || q.y < 0 || q.x + L >= nc || q.y + L >= nc) {
+          bad = true;
+          continue;
+        }
+        double T[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) T[a] = 0.0;
+        for (int m = 0; m <= L; ++m) {
+          const double w = m == 0 ? 1.0 : 2.0;
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            const double2 x = sI[(q.x + m) * NA + a], y = sI[(q.y + m) * NA + a];
+            T[a] = fma(w, fma(x.x, y.x, x.y * y.y), T[a]);
+          }
+        }
+        const double sg = q.z < 0 ? -1.0 : 1.0;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) ep[a] = fma(__ldg(kz[a] + d0 + j), sg * T[a], ep[a]);
+      }
+      __syncthreads();
+    }
+    if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      const double total = block_sum<TH>(ep[a], red);
+      if (tid == 0 && a < nv) energy[first + a] = total;
       __syncthreads();
     }
   }

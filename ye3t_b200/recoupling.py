@@ -48,8 +48,9 @@ import numpy as np
 
 from .schedules import ACEBundle, ScheduleRecord, SymPowerTable
 
-__all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "RecoupledDeviceTables", "RecoupledEvaluator",
-           "build_recoupled_plan", "ctypes_tables", "SEG_UNIT", "SEG_CHANNEL", "SEG_PAIR"]
+__all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "RecoupledDeviceTables", "RecoupledSymTables",
+           "RecoupledEvaluator",
+           "build_recoupled_plan", "ctypes_tables", "ctypes_sym_tables", "SEG_UNIT", "SEG_CHANNEL", "SEG_PAIR"]
 
 SEG_UNIT, SEG_CHANNEL, SEG_PAIR = 0, 1, 2
 _FIT_TOL = 1e-11
@@ -269,6 +270,10 @@ class RecoupledPlan:
         """The plan packed for the device pass (validated)."""
         return _device_tables(self)
 
+    def sym_device_tables(self) -> "RecoupledSymTables":
+        """The plan packed for the symmetric pass over physical densities (validated)."""
+        return _sym_device_tables(self)
+
 
 @dataclass
 class RecoupledDeviceTables:
@@ -471,6 +476,219 @@ def _device_tables(plan: "RecoupledPlan") -> RecoupledDeviceTables:
     return tabs
 
 
+@dataclass
+class RecoupledSymTables:
+    """The plan packed for the symmetric device pass (``y3b_recoupled_sym_tables``), valid for
+    physical densities, ``A[n, l, -m] = (-1)^m conj(A[n, l, m])`` (real radial functions and
+    prefactors).  Then a segment of parity ``p`` (``l_a + l_b - L`` for a pair, 0 otherwise)
+    has ``I[-M] = (-1)^(p + M) conj(I[M])``, and in a parity-even word set both segments of a
+    contraction have the same parity, so only ``M >= 0`` is stored and
+
+        gI[M] = (-1)^p conj(sum_q k[d_q] I_partner[M]),
+        e = 1/2 Re(I[0] gI[0]) + sum_{M > 0} Re(I[M] gI[M]),
+
+    and dE/dA has the density's symmetry: the pass forms the ``m >= 0`` half of each A row
+    and mirrors the rest.  ``comp[c] = (a, b, cg_begin, cg_count, M, own_begin, own_count,
+    (-1)^p)``; ``own`` as in the general tables with partners' first (``M = 0``) components;
+    ``bp_gi`` is ``2 * component + (1 if the entry reads conj(gI) of a negative M)``;
+    ``mirror[t]`` is ``2 * t_plus + (m & 1)`` for an A entry of negative ``m`` (``t_plus``
+    the entry of ``-m``), else -1; ``dot[d] = (first local component of A, of B,
+    (-1)^p_B, 0)`` for the forward energy ``T_d = (-1)^p_B (Re(I_A[0] conj(I_B[0])) +
+    2 sum_{M > 0} Re(I_A[M] conj(I_B[M])))``."""
+
+    pass_count: int
+    max_pass_components: int
+    row_width: int
+    dot_count: int
+    pass_begin: np.ndarray  # int32 [pass_count + 1]
+    comp: np.ndarray        # int32 [C, 8]
+    cg_index: np.ndarray    # int32 [K]
+    cg_value: np.ndarray    # float64 [K]
+    own: np.ndarray         # int32 [O, 2]
+    bp_begin: np.ndarray    # int32 [pass_count * row_width + 1]
+    bp_gi: np.ndarray       # int32 [Bp]
+    bp_other: np.ndarray    # int32 [Bp]
+    bp_value: np.ndarray    # float64 [Bp]
+    mirror: np.ndarray      # int32 [row_width]
+    dot_begin: np.ndarray   # int32 [pass_count + 1]
+    dot: np.ndarray         # int32 [D, 4]
+
+    def validate(self) -> None:
+        P, W = self.pass_count, self.row_width
+        pb = self.pass_begin.astype(np.int64)
+        if pb.shape != (P + 1,) or pb[0] != 0 or np.any(np.diff(pb) < 0) or pb[-1] != self.comp.shape[0]:
+            raise ValueError("pass_begin does not partition the components")
+        if int(np.diff(pb).max(initial=0)) > self.max_pass_components:
+            raise ValueError("a pass holds more components than max_pass_components")
+        c = self.comp.astype(np.int64)
+        Lc = np.repeat(np.arange(P), np.diff(pb))
+        nc = np.diff(pb)[Lc]
+        if np.any((c[:, 4] < 0) | (c[:, 4] > Lc)) or np.any(np.abs(c[:, 7]) != 1):
+            raise ValueError("component M outside 0 .. L or parity sign not +-1")
+        if np.any(c[:, 2] < 0) or np.any(c[:, 2] + c[:, 3] > self.cg_value.shape[0]):
+            raise ValueError("coupling range outside the coupling table")
+        if np.any(c[:, 0] >= W) or np.any((c[:, 3] > 0) & ((c[:, 1] < 0) | (c[:, 1] >= W))):
+            raise ValueError("component channel outside the A row")
+        if np.any(c[:, 5] < 0) or np.any(c[:, 5] + c[:, 6] > self.own.shape[0]):
+            raise ValueError("adjoint list outside the list table")
+        own = self.own.astype(np.int64)
+        if own.size:
+            idx = np.repeat(np.arange(c.shape[0]), c[:, 6])
+            q = np.concatenate([np.arange(c[i, 5], c[i, 5] + c[i, 6]) for i in range(c.shape[0])])
+            rd = own[q, 0] + c[idx, 4]
+            if np.any(own[q, 0] < 0) or np.any(rd >= nc[idx]) or np.any(own[q, 1] < 0) or \
+                    np.any(own[q, 1] >= self.dot_count):
+                raise ValueError("adjoint partner outside its pass or weights")
+        bb = self.bp_begin.astype(np.int64)
+        if bb.shape != (P * W + 1,) or bb[0] != 0 or np.any(np.diff(bb) < 0) or bb[-1] != self.bp_gi.shape[0]:
+            raise ValueError("bp_begin does not partition the back-propagation entries")
+        Lq = np.repeat(np.arange(P * W) // W, np.diff(bb))
+        if np.any(self.bp_gi < 0) or np.any((self.bp_gi >> 1) >= np.diff(pb)[Lq]):
+            raise ValueError("back-propagation entry outside its pass")
+        if np.any(self.bp_other >= W) or np.any(self.bp_other < -1):
+            raise ValueError("back-propagation partner outside the A row")
+        m = self.mirror.astype(np.int64)
+        if m.shape != (W,) or np.any((m >= 0) & ((m >> 1) >= W)):
+            raise ValueError("mirror entry outside the A row")
+        db = self.dot_begin.astype(np.int64)
+        if db.shape != (P + 1,) or db[0] != 0 or db[-1] != self.dot_count or self.dot.shape != (self.dot_count, 4):
+            raise ValueError("dot_begin does not partition the contractions")
+        Ld = np.repeat(np.arange(P), np.diff(db))
+        dt = self.dot.astype(np.int64)
+        if np.any(dt[:, :2] < 0) or np.any(dt[:, 0] + Ld >= np.diff(pb)[Ld]) or \
+                np.any(dt[:, 1] + Ld >= np.diff(pb)[Ld]) or np.any(np.abs(dt[:, 2]) != 1):
+            raise ValueError("contraction segment outside its pass")
+
+    def smem_bytes(self) -> int:
+        """Dynamic shared memory per atom: the A row and its adjoint, the pass's components
+        and theirs."""
+        return 16 * (2 * self.row_width + 2 * self.max_pass_components)
+
+    def flops_per_atom(self) -> Dict[str, float]:
+        """Real flops per atom of the symmetric passes, counted as
+        ``RecoupledDeviceTables.flops_per_atom`` counts the general ones (a contraction term of
+        the forward energy, the real part of one complex product with its weight, counts 4)."""
+        terms = float(self.comp[:, 3].astype(np.int64).sum())
+        lists = float(self.comp[:, 6].astype(np.int64).sum())
+        dot_L = np.repeat(np.arange(self.pass_count), np.diff(self.dot_begin.astype(np.int64)))
+        halves = float((dot_L + 1).sum())
+        coupled = float((self.bp_other >= 0).sum())
+        copied = float((self.bp_other < 0).sum())
+        return {"energy": 10 * terms + 4 * halves + 2 * self.dot_count,
+                "energy_grad": 10 * terms + 4 * lists + 4 * self.comp.shape[0] + 10 * coupled + 2 * copied}
+
+
+def _sym_device_tables(plan: "RecoupledPlan") -> RecoupledSymTables:
+    L1 = plan.lmax + 1
+    W = L1 * L1
+    row_width = plan.nmax * W
+
+    def base(c):
+        l, n = c % L1, c // L1 + 1
+        return (n - 1) * W + l * l
+
+    def parity(s):
+        L, kind = int(plan.seg_L[s]), int(plan.seg_kind[s])
+        if kind != SEG_PAIR:
+            return 0
+        return (int(plan.seg_a[s]) % L1 + int(plan.seg_b[s]) % L1 - L) & 1
+
+    S = plan.segment_count
+    P = int(plan.seg_L.max()) + 1 if S else 0
+    for d in range(plan.dot_count):
+        if parity(int(plan.dot_a[d])) != parity(int(plan.dot_b[d])):
+            raise ValueError("the symmetric pass needs a parity-even word set")
+    # M >= 0 layout: segment s holds L + 1 components
+    half = (plan.seg_L.astype(np.int64) + 1)
+    off = np.concatenate([[0], np.cumsum(half)])
+    pass_begin = np.zeros(P + 1, dtype=np.int64)
+    for L in range(P):
+        sel = np.nonzero(plan.seg_L == L)[0]
+        pass_begin[L + 1] = off[sel[-1] + 1] if sel.size else pass_begin[L]
+    cg_index, cg_value, cg_at = [], [], {}
+
+    def cg_range(la, lb, L, M):
+        key = (la, lb, L, M)
+        if key not in cg_at:
+            idx, val = cg_table(la, lb, L)
+            rows = np.nonzero(idx[:, 2] == M + L)[0]
+            cg_at[key] = (len(cg_value), rows.shape[0])
+            cg_index.extend(int(idx[r, 0]) | (int(idx[r, 1]) << 8) for r in rows)
+            cg_value.extend(float(val[r]) for r in rows)
+        return cg_at[key]
+
+    lists: List[List[Tuple[int, int]]] = [[] for _ in range(S)]
+    for d in range(plan.dot_count):
+        a, b = int(plan.dot_a[d]), int(plan.dot_b[d])
+        L = int(plan.dot_L[d])
+        lists[a].append((int(off[b] - pass_begin[L]), d))
+        lists[b].append((int(off[a] - pass_begin[L]), d))
+    own, own_at = [], []
+    for s in range(S):
+        own_at.append(len(own))
+        own.extend(lists[s])
+    comp = np.zeros((int(off[-1]), 8), dtype=np.int64)
+    bp = [[[] for _ in range(row_width)] for _ in range(P)]
+    for s in range(S):
+        L, kind, p = int(plan.seg_L[s]), int(plan.seg_kind[s]), parity(s)
+        for M in range(L + 1):
+            c = int(off[s]) + M
+            local = c - int(pass_begin[L])
+            row = [-1, -1, 0, 0, M, own_at[s], len(lists[s]), -1 if p else 1]
+            if kind == SEG_CHANNEL:
+                row[0] = base(int(plan.seg_a[s])) + L + M
+            elif kind == SEG_PAIR:
+                ca, cb = int(plan.seg_a[s]), int(plan.seg_b[s])
+                la, lb = ca % L1, cb % L1
+                row[0], row[1] = base(ca), base(cb)
+                row[2], row[3] = cg_range(la, lb, L, M)
+            comp[c] = row
+        # back-propagation into the m >= 0 half of the A row, over every M of the segment
+        if kind == SEG_CHANNEL:
+            for M in range(L + 1):
+                t = base(int(plan.seg_a[s])) + L + M
+                bp[L][t].append((2 * (int(off[s]) + M - int(pass_begin[L])), -1, 1.0))
+        elif kind == SEG_PAIR:
+            ca, cb = int(plan.seg_a[s]), int(plan.seg_b[s])
+            la, lb = ca % L1, cb % L1
+            idx, val = cg_table(la, lb, L)
+            for (ia, ib, im), v in zip(idx, val):
+                M = int(im) - L
+                gi = int(off[s]) + abs(M) - int(pass_begin[L])
+                conj = 1 if M < 0 else 0
+                sign = (-1.0) ** ((p + M) & 1) if M < 0 else 1.0
+                ma, mb = int(ia) - la, int(ib) - lb
+                if ma >= 0:
+                    bp[L][base(ca) + int(ia)].append((2 * gi + conj, base(cb) + int(ib), sign * float(v)))
+                if mb >= 0:
+                    bp[L][base(cb) + int(ib)].append((2 * gi + conj, base(ca) + int(ia), sign * float(v)))
+    bp_flat = [e for L in range(P) for t in range(row_width) for e in bp[L][t]]
+    bp_begin = np.concatenate([[0], np.cumsum([len(bp[L][t]) for L in range(P) for t in range(row_width)])])
+    mirror = np.full(row_width, -1, dtype=np.int64)
+    for n in range(plan.nmax):
+        for l in range(L1):
+            for m in range(-l, 0):
+                t = n * W + l * l + l + m
+                mirror[t] = 2 * (n * W + l * l + l - m) + (m & 1)
+    dot_begin = np.searchsorted(plan.dot_L, np.arange(P + 1), side="left").astype(np.int64)
+    dot = np.zeros((plan.dot_count, 4), dtype=np.int64)
+    for d in range(plan.dot_count):
+        L = int(plan.dot_L[d])
+        a, b = int(plan.dot_a[d]), int(plan.dot_b[d])
+        dot[d] = (off[a] - pass_begin[L], off[b] - pass_begin[L], -1 if parity(b) else 1, 0)
+    tabs = RecoupledSymTables(
+        pass_count=P, max_pass_components=int(np.diff(pass_begin).max(initial=0)), row_width=row_width,
+        dot_count=plan.dot_count, pass_begin=pass_begin.astype(np.int32), comp=comp.astype(np.int32),
+        cg_index=np.asarray(cg_index, dtype=np.int32), cg_value=np.asarray(cg_value, dtype=np.float64),
+        own=np.asarray(own, dtype=np.int32).reshape(-1, 2), bp_begin=bp_begin.astype(np.int32),
+        bp_gi=np.asarray([e[0] for e in bp_flat], dtype=np.int32),
+        bp_other=np.asarray([e[1] for e in bp_flat], dtype=np.int32),
+        bp_value=np.asarray([e[2] for e in bp_flat], dtype=np.float64), mirror=mirror.astype(np.int32),
+        dot_begin=dot_begin.astype(np.int32), dot=dot.astype(np.int32))
+    tabs.validate()
+    return tabs
+
+
 def build_recoupled_plan(bundle: ACEBundle, seed: int = 20260) -> RecoupledPlan:
     """Recoupled plan of an L = 0 bundle (weights fitted once per pattern)."""
     if bundle.target_L != 0:
@@ -557,6 +775,18 @@ def ctypes_tables(arrays: Dict[str, "object"], tabs: RecoupledDeviceTables):
 
 _TABLE_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
                  "dot_begin", "dot", "feat_index", "feat_weight")
+_SYM_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
+               "mirror", "dot_begin", "dot")
+
+
+def ctypes_sym_tables(arrays: Dict[str, "object"], tabs: RecoupledSymTables):
+    """``y3b_recoupled_sym_tables`` over tensors holding ``tabs``' arrays (``arrays[name]``)."""
+    from . import _native as nat
+    return nat.RecoupledSymTables(
+        pass_count=tabs.pass_count, max_pass_components=tabs.max_pass_components, row_width=tabs.row_width,
+        dot_count=tabs.dot_count, component_count=int(tabs.comp.shape[0]), cg_count=int(tabs.cg_value.shape[0]),
+        own_count=int(tabs.own.shape[0]), bp_count=int(tabs.bp_gi.shape[0]),
+        **{name: arrays[name].data_ptr() for name in _SYM_ARRAYS})
 
 
 class RecoupledEvaluator:
@@ -565,23 +795,27 @@ class RecoupledEvaluator:
     atoms' species), like ``ACEEvaluator``'s ``energy_grad`` / ``energy_from_density`` /
     ``features``.  ``atoms_per_cta`` atoms share one CTA's walk of the tables (each table
     entry loaded once for all of them), within the 224 KB of shared memory; a CTA has
-    ``threads_per_cta`` (256 or 512) threads."""
+    ``threads_per_cta`` (256 or 512) threads.  ``symmetric`` selects the passes over the
+    ``M >= 0`` components (``RecoupledSymTables``), valid only for physical densities
+    ``A[n, l, -m] = (-1)^m conj(A[n, l, m])`` such as ``ACEEvaluator.density`` gives."""
 
     def __init__(self, bundle: ACEBundle, device, weights: np.ndarray = None, plan: "RecoupledPlan" = None,
-                 atoms_per_cta: int = 1, threads_per_cta: int = 256):
+                 atoms_per_cta: int = 1, threads_per_cta: int = 256, symmetric: bool = False):
         import torch
         if not 1 <= int(atoms_per_cta) <= 4:
             raise ValueError("atoms_per_cta must be in [1, 4]")
         if int(threads_per_cta) not in (256, 512):
             raise ValueError("threads_per_cta must be 256 or 512")
         self.device = torch.device(device)
+        self.symmetric = bool(symmetric)
         self.plan = plan if plan is not None else build_recoupled_plan(bundle)
-        self.tables = self.plan.device_tables()
+        self.tables = self.plan.sym_device_tables() if self.symmetric else self.plan.device_tables()
+        names = _SYM_ARRAYS if self.symmetric else _TABLE_ARRAYS
         self.arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(self.tables, name))).to(self.device)
-                       for name in _TABLE_ARRAYS}
+                       for name in names}
         self.weights = None if weights is None else \
             torch.as_tensor(self.plan.energy_weights(weights)).to(self.device).contiguous()
-        self._c = ctypes_tables(self.arrays, self.tables)
+        self._c = (ctypes_sym_tables if self.symmetric else ctypes_tables)(self.arrays, self.tables)
         self._c.atoms_per_cta = int(atoms_per_cta)
         self._c.threads_per_cta = int(threads_per_cta)
 
@@ -614,9 +848,10 @@ class RecoupledEvaluator:
         sp = self._species(species, n)
         e = torch.empty(n, dtype=torch.float64, device=self.device)
         G = torch.empty_like(A)
-        nat.check(nat.lib().y3b_ace_recoupled_energy_grad(
+        name = "y3b_ace_recoupled_energy_grad_symmetric" if self.symmetric else "y3b_ace_recoupled_energy_grad"
+        nat.check(getattr(nat.lib(), name)(
             ctypes.byref(self._c), A.data_ptr(), n, sp.data_ptr(), self.weights.data_ptr(), self.weights.shape[0],
-            e.data_ptr(), G.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), "ace_recoupled_energy_grad")
+            e.data_ptr(), G.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), name)
         return e, G
 
     def energy(self, A, species, status=None):
@@ -629,17 +864,20 @@ class RecoupledEvaluator:
         n = A.shape[0]
         sp = self._species(species, n)
         e = torch.empty(n, dtype=torch.float64, device=self.device)
-        nat.check(nat.lib().y3b_ace_recoupled_energy(
+        name = "y3b_ace_recoupled_energy_symmetric" if self.symmetric else "y3b_ace_recoupled_energy"
+        nat.check(getattr(nat.lib(), name)(
             ctypes.byref(self._c), A.data_ptr(), n, sp.data_ptr(), self.weights.data_ptr(), self.weights.shape[0],
-            e.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), "ace_recoupled_energy")
+            e.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), name)
         return e
 
     def features(self, A, status=None):
-        """Features ``[n, feature_count]`` complex128 in the bundle's order."""
+        """Features ``[n, feature_count]`` complex128 in the bundle's order (general passes only)."""
         import ctypes
 
         import torch
         from . import _native as nat
+        if self.symmetric:
+            raise ValueError("features need the general passes (symmetric=False)")
         A = self._rows(A)
         n = A.shape[0]
         F = torch.empty((n, self.tables.feature_count), dtype=torch.complex128, device=self.device)
