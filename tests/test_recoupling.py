@@ -448,3 +448,47 @@ def test_symmetric_device_source_emulated_matches_oracle(emulated, plan5, physic
     assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()
     with pytest.raises(ValueError, match="general passes"):
         ev.features(At)
+
+
+def _physical(rng, n, nmax, lmax):
+    """Random densities with the physical symmetry A[l, -m] = (-1)^m conj(A[l, m])."""
+    A = np.zeros((n, nmax, (lmax + 1) ** 2), dtype=np.complex128)
+    for l in range(lmax + 1):
+        for m in range(0, l + 1):
+            v = rng.normal(size=(n, nmax)) + (1j * rng.normal(size=(n, nmax)) if m else 0)
+            A[:, :, l * l + l + m] = v
+            A[:, :, l * l + l - m] = (-1) ** m * np.conj(v)
+    return A
+
+
+def test_symmetric_device_source_emulated_channel_diagonal(emulated, monkeypatch):
+    """The symmetric kernels' source on the 25-entry rows of the channel-diagonal l <= 4
+    bundle (back-propagation unsplit, rows that do not divide the block), emulated through
+    the real bindings, against the oracle."""
+    import ctypes
+
+    import torch
+    from oracle import oracle
+    from ye3t_b200 import _native
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    for name in ("y3b_ace_recoupled_energy_grad_symmetric", "y3b_ace_recoupled_energy_symmetric"):
+        res, args = _native._SIGS[name]
+        getattr(emulated, name).restype = res
+        getattr(emulated, name).argtypes = args
+    emulated.y3b_last_error.restype = ctypes.c_char_p
+    monkeypatch.setattr(_native, "lib", lambda: emulated)
+    monkeypatch.setattr(_native, "require_cuda", lambda *t, what="": torch.device("cpu"))
+    monkeypatch.setattr(_native, "stream_of", lambda device: 0)
+    b = _bundle("ace_diag_l4_nu4_L0")
+    rng = np.random.default_rng(70)
+    A = _physical(rng, 7, 1, 4)
+    species = np.array([0, 1, 1, 0, 1, 0, 0], dtype=np.int32)
+    w = rng.normal(size=(2, b.feature_count))
+    e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=2)
+    for na, th in ((3, 256), (4, 512)):
+        ev = RecoupledEvaluator(b, "cpu", w, atoms_per_cta=na, threads_per_cta=th, symmetric=True)
+        e, G = ev.energy_grad(torch.as_tensor(A), torch.as_tensor(species))
+        e2 = ev.energy(torch.as_tensor(A), torch.as_tensor(species))
+        assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+        assert np.abs(e2.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+        assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()
