@@ -209,7 +209,7 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces, ref_ms):
+def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces, ref_ms, F_ref=None, E_ref=None):
     """One look at the recoupled B-basis passes on this run's own system, after every timed
     region and outside the reported value: the pass's CUDA-event time in two CTA shapes
     (best of three after one warm-up call) against the term-level kernels' stage time of the
@@ -263,9 +263,34 @@ def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces
                 shapes[key] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
         timed_ms = [v["ms"] for v in shapes.values() if "ms" in v]
         best = min(timed_ms) if timed_ms else None
+        step = None
+        if best is not None:
+            try:  # one whole step with the fastest shape, its forces against the measured run's
+                key = min((k for k in shapes if "ms" in shapes[k]), key=lambda k: shapes[k]["ms"])
+                symmetric = key.startswith("symmetric")
+                na, th = (int(v) for v in key.split()[-1].split("x"))
+                rec = RecoupledEvaluator(bundle, device, weights, plan=plan, atoms_per_cta=na, threads_per_cta=th,
+                                         symmetric=symmetric)
+
+                def full_step():
+                    r, nb = ev.neighbor_list(pos_d, box, 0, N)
+                    Ad = ev.density(pos_d, sp_d, box, r, nb, 0)
+                    if not forces:
+                        return rec.energy(Ad, sp).sum(), None
+                    e, G = rec.energy_grad(Ad, sp)
+                    return e.sum(), ev.forces_from_edges(r, nb, ev.edge_grad(pos_d, sp_d, box, r, nb, G, begin=0))
+
+                sms, (E, F) = timed(full_step)
+                step = {"shape": key, "ms": sms, "atoms_per_s": N / (sms * 1e-3),
+                        "energy_rel_diff": None if E_ref is None else float(abs(float(E) - E_ref) / abs(E_ref)),
+                        "forces_max_rel_diff": None if F is None or F_ref is None else
+                        float((F - F_ref).abs().max() / F_ref.abs().max())}
+            except Exception as exc:
+                step = {"error": f"{type(exc).__name__}: {exc}"[:200]}
         return {"pass": "energy_grad" if forces else "energy", "atoms": int(N),
-                "term_level_ms": ref_ms, "shapes_atoms_x_threads": shapes, "speedup_vs_term_level": ref_ms / best if best else None,
-                "forward_energy_shapes": forward or None,
+                "term_level_ms": ref_ms, "shapes_atoms_x_threads": shapes,
+                "speedup_vs_term_level": ref_ms / best if best else None,
+                "forward_energy_shapes": forward or None, "whole_step_with_fastest_shape": step,
                 "note": "not part of value; timed after the timed regions, against the term-level stage time"}
     except Exception as exc:  # the probe must not take the measured line with it
         return {"error": f"{type(exc).__name__}: {exc}"[:300]}
@@ -439,7 +464,8 @@ def run_b200(args):
     probe = None
     if world == 1 and rec is None and not args.no_recoupled_probe:
         probe = recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces,
-                                statistics.mean(timers["energy_grad" if forces else "energy"]))
+                                statistics.mean(timers["energy_grad" if forces else "energy"]),
+                                F_ref=F_last if forces else None, E_ref=energy)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_sample, args.bundle, forces=not args.energy_only)
