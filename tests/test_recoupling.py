@@ -492,3 +492,17 @@ def test_symmetric_device_source_emulated_channel_diagonal(emulated, monkeypatch
         assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
         assert np.abs(e2.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
         assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()
+
+
+def test_symmetry_check_refuses_non_physical_densities(plan5, physical_case):
+    """RecoupledEvaluator.check_symmetry passes the reference's densities and refuses random
+    complex ones (for which the symmetric passes would be wrong)."""
+    import torch
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    b, plan = plan5
+    A, species, w, _, _ = physical_case
+    ev = RecoupledEvaluator(b, "cpu", w, plan=plan, symmetric=True)
+    ev.check_symmetry(torch.as_tensor(A))
+    rng = np.random.default_rng(80)
+    with pytest.raises(ValueError, match="physical symmetry"):
+        ev.check_symmetry(torch.as_tensor(rng.normal(size=(2, 8, 16)) + 1j * rng.normal(size=(2, 8, 16))))

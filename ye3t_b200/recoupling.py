@@ -828,6 +828,31 @@ class RecoupledEvaluator:
         nat.require_cuda(A, what="recoupled pass")
         return A
 
+    def check_symmetry(self, A, tol: float = 1e-12) -> None:
+        """Raise ``ValueError`` unless ``A[n, l, -m] = (-1)^m conj(A[n, l, m])`` holds to ``tol``
+        (relative to ``max |A|``): the condition of the symmetric passes."""
+        import torch
+        W = (self.plan.lmax + 1) ** 2
+        neg, pos, sign = [], [], []
+        for l in range(self.plan.lmax + 1):
+            for m in range(1, l + 1):
+                neg.append(l * l + l - m)
+                pos.append(l * l + l + m)
+                sign.append(-1.0 if m & 1 else 1.0)
+        rows = A.reshape(A.shape[0], -1, W)
+        scale = float(rows.abs().max()) if rows.numel() else 0.0
+        dev = 0.0
+        if neg:
+            idx_n = torch.as_tensor(neg, device=rows.device)
+            idx_p = torch.as_tensor(pos, device=rows.device)
+            sg = torch.as_tensor(sign, dtype=torch.float64, device=rows.device)
+            dev = float((rows[..., idx_n] - sg * rows[..., idx_p].conj()).abs().max())
+        zero = torch.as_tensor([l * l + l for l in range(self.plan.lmax + 1)], device=rows.device)
+        dev = max(dev, float(rows[..., zero].imag.abs().max()) if rows.numel() else 0.0)
+        if dev > tol * max(scale, 1e-300):
+            raise ValueError(f"A lacks the physical symmetry A[l,-m] = (-1)^m conj(A[l,m]) (deviation {dev:.3e}); "
+                             "use the general passes (symmetric=False)")
+
     def _species(self, species, n):
         import torch
         if self.weights is None:
