@@ -239,6 +239,11 @@ def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces
         else:
             e0 = ev.energy_from_density(A, sp)
         plan = build_recoupled_plan(bundle)
+        try:  # the symmetric shapes are valid only for densities with the physical symmetry
+            RecoupledEvaluator(bundle, device, None, plan=plan, symmetric=True).check_symmetry(A)
+            density_symmetric = True
+        except ValueError as exc:
+            density_symmetric = str(exc)[:200]
         shapes, forward = {}, {}
         for na, th, symmetric in ((1, 256, False), (2, 256, False), (2, 512, False), (3, 512, False),
                                   (1, 256, True), (2, 256, True), (4, 256, True), (3, 512, True)):
@@ -291,6 +296,7 @@ def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces
                 "term_level_ms": ref_ms, "shapes_atoms_x_threads": shapes,
                 "speedup_vs_term_level": ref_ms / best if best else None,
                 "forward_energy_shapes": forward or None, "whole_step_with_fastest_shape": step,
+                "density_symmetric": density_symmetric,
                 "note": "not part of value; timed after the timed regions, against the term-level stage time"}
     except Exception as exc:  # the probe must not take the measured line with it
         return {"error": f"{type(exc).__name__}: {exc}"[:300]}
