@@ -506,3 +506,75 @@ def test_symmetry_check_refuses_non_physical_densities(plan5, physical_case):
     rng = np.random.default_rng(80)
     with pytest.raises(ValueError, match="physical symmetry"):
         ev.check_symmetry(torch.as_tensor(rng.normal(size=(2, 8, 16)) + 1j * rng.normal(size=(2, 8, 16))))
+
+
+def test_bench_probe_runs_on_emulated_passes(emulated, plan5, physical_case, monkeypatch):
+    """bench.recoupled_probe end to end on the CPU: the library swapped for the emulation
+    harness, CUDA events stubbed, and a stand-in evaluator that returns the reference's
+    densities with the oracle's energies and dE/dA.  Every shape and the whole step must agree
+    with them, and the field must be plain JSON."""
+    import ctypes
+    import json
+    import sys
+
+    import torch
+    from ye3t_b200 import _native
+    for name in ("y3b_ace_recoupled_energy_grad", "y3b_ace_recoupled_energy", "y3b_ace_recoupled_features",
+                 "y3b_ace_recoupled_energy_grad_symmetric", "y3b_ace_recoupled_energy_symmetric"):
+        res, args = _native._SIGS[name]
+        getattr(emulated, name).restype = res
+        getattr(emulated, name).argtypes = args
+    emulated.y3b_last_error.restype = ctypes.c_char_p
+    monkeypatch.setattr(_native, "lib", lambda: emulated)
+    monkeypatch.setattr(_native, "require_cuda", lambda *t, what="": torch.device("cpu"))
+    monkeypatch.setattr(_native, "stream_of", lambda device: 0)
+
+    class Event:
+        def __init__(self, enable_timing=True):
+            pass
+
+        def record(self):
+            pass
+
+        def elapsed_time(self, other):
+            return 1.0
+
+    monkeypatch.setattr(torch.cuda, "Event", Event)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
+    if REPO not in sys.path:
+        sys.path.insert(0, REPO)
+    import bench
+    b, plan = plan5
+    A, species, w, e0, G0 = physical_case
+    At, sp = torch.as_tensor(A), torch.as_tensor(species)
+    e0t, G0t = torch.as_tensor(e0), torch.as_tensor(G0)
+    Fref = G0t.real.reshape(A.shape[0], -1)[:, :3].contiguous()
+
+    class Evaluator:  # the term-level side of the probe, from the oracle
+        def neighbor_list(self, pos, box, begin, end):
+            return None, None
+
+        def density(self, pos, species, box, row, nbr, begin):
+            return At
+
+        def energy_grad(self, A, species):
+            return e0t, G0t
+
+        def energy_from_density(self, A, species):
+            return e0t
+
+        def edge_grad(self, pos, species, box, row, nbr, G, begin=0):
+            return G.real.reshape(G.shape[0], -1)[:, :3].contiguous()
+
+        def forces_from_edges(self, row, nbr, g):
+            return g
+
+    out = bench.recoupled_probe(torch, Evaluator(), b, w, "cpu", torch.zeros(A.shape[0], 3), sp, 30.0, True,
+                                5000.0, F_ref=Fref, E_ref=float(e0.sum()))
+    json.dumps(out, allow_nan=False)
+    assert "error" not in out and out["density_symmetric"] is True
+    assert len(out["shapes_atoms_x_threads"]) == 8
+    for shape in out["shapes_atoms_x_threads"].values():
+        assert shape["energy_max_rel_diff"] <= 1e-12 and shape["dEdA_max_rel_diff"] <= 1e-12
+    step = out["whole_step_with_fastest_shape"]
+    assert step["energy_rel_diff"] <= 1e-12 and step["forces_max_rel_diff"] <= 1e-12
