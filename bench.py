@@ -49,20 +49,19 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="atoms in the CPU baseline sample (default 512 with forces, 1024 energy only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c5", choices=["c5", "c3", "c3f32", "c4"],
-                    help="c5 (default): the headline 2^20-atom energy + forces step; c3/c3f32/c4: the "
-                         "channel-diagonal descriptor configurations (mixed radial channels)")
-    ap.add_argument("--recoupled", action="store_true",
-                    help="B-basis through the recoupled passes (ye3t_b200.recoupling) instead of the "
-                         "term-level schedule kernels")
-    ap.add_argument("--recoupled-atoms", type=int, default=1,
-                    help="atoms per CTA of the recoupled passes (1-4, within shared memory)")
-    ap.add_argument("--recoupled-threads", type=int, default=256, choices=[256, 512],
-                    help="threads per CTA of the recoupled passes")
-    ap.add_argument("--recoupled-symmetric", action="store_true",
-                    help="the recoupled passes over M >= 0 components (physical densities)")
-    ap.add_argument("--no-recoupled-probe", action="store_true",
-                    help="skip the one-off look at the recoupled passes after the measurement")
+    ap.add_argument("--config", default="c5", choices=["c5", "c1", "c2", "c3", "c3f32", "c4"],
+                    help="c5 (default): the headline 2^20-atom energy + forces step; c1: the quickstart "
+                         "schedule over 4,096 atoms x 56 channel bindings; c2: 16,384-atom single-species "
+                         "nu<=3 descriptor; c3/c3f32/c4: the channel-diagonal descriptor configurations "
+                         "(mixed radial channels)")
+    ap.add_argument("--b-basis", default="recoupled", choices=["recoupled", "term"],
+                    help="B-basis of the C5 step: the recoupled passes (default) or the term-level kernels")
+    ap.add_argument("--recoupled-atoms", type=int, default=0,
+                    help="atoms per CTA of the recoupled passes (1-4; 0 = the evaluator's default)")
+    ap.add_argument("--recoupled-threads", type=int, default=0, choices=[0, 256, 512],
+                    help="threads per CTA of the recoupled passes (0 = the evaluator's default)")
+    ap.add_argument("--recoupled-general", action="store_true",
+                    help="the general recoupled passes instead of the M >= 0 (symmetric) ones")
     ap.add_argument("--energy-only", action="store_true",
                     help="time the energy step alone (no adjoint, no forces)")
     return ap.parse_args()
@@ -151,171 +150,118 @@ def measure_fp64_peak(torch, nat, device):
     return best
 
 
-def cpu_baseline(sample_atoms, bundle_stem, forces=True):
-    """The reference CPU path restated (oracle) on a bounded sample, all host cores."""
+def _cpu_sample(M, bundle_stem, forces, cores):
+    """One oracle evaluation of an M-atom periodic sample; returns its wall time."""
     import numpy as np
 
     from oracle import oracle
     from ye3t_b200.schedules import ACEBundle
-    cores = len(os.sched_getaffinity(0))
     b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", bundle_stem + ".npz"))
-    M = int(sample_atoms)
     rng = np.random.default_rng(0)
     box = (M / DENSITY) ** (1 / 3)
     pos = rng.uniform(0, box, (M, 3))
     sp = rng.integers(0, SPECIES, M).astype(np.int32)
-    w = np.random.default_rng(2).normal(size=(SPECIES, 41168 if bundle_stem == BUNDLE else b.feature_count))
+    w = np.random.default_rng(2).normal(size=(SPECIES, b.feature_count))
     t0 = time.perf_counter()
     if forces:
         e, F = oracle.energy_forces(b, pos, box, sp, np.asarray(PREFACTOR), w, CUTOFF, LAMBDA, threads=cores)
         assert np.isfinite(e) and np.isfinite(F).all()
-        what = ("then per word the reference block assembly (workflows.py:636-661), schedule evaluation "
-                "(factorized_runtime.cpp:252-287 restated) and its adjoint (autograd of couplings.py:552-567), the "
-                "symmetric-power adjoint, per-edge gradients and the force scatter")
     else:
         off, nbr, disp = oracle.neighbor_list(pos, box, CUTOFF)
         A = oracle.ace_density(disp, off, nbr, sp, np.asarray(PREFACTOR), b.nmax, b.lmax, CUTOFF, LAMBDA)
         e = oracle.bundle_energy(b, A, sp, w, threads=cores)
         assert np.isfinite(e).all()
-        what = ("then per word the reference block assembly (workflows.py:636-661) and schedule evaluation "
-                "(factorized_runtime.cpp:252-287 restated)")
-    dt = time.perf_counter() - t0
-    return {"value": M / dt, "unit": "atoms/s", "cores": cores, "kind": "port",
-            "sample": f"{M} atoms of the same density/species/cutoff in a {box:.1f} A periodic box; brute-force "
-                      f"neighbour list, A-basis, {what} ({cores} threads); {dt:.1f} s"}
+    return time.perf_counter() - t0
+
+
+# Atoms of the small sample that measures the oracle's fixed per-step host
+# cost (per-word block assembly and dispatch, which a full-size run amortises
+# over 2^20 atoms); its box (13.7 A) is still larger than twice the cutoff.
+CPU_FIXED_SAMPLE = 128
+
+
+def _cpu_what(forces):
+    if forces:
+        return ("brute-force neighbour list, A-basis, then per word the reference block assembly "
+                "(workflows.py:636-661), schedule evaluation (factorized_runtime.cpp:252-287 restated) and its "
+                "adjoint (autograd of couplings.py:552-567), the symmetric-power adjoint, per-edge gradients and "
+                "the force scatter")
+    return ("brute-force neighbour list, A-basis, then per word the reference block assembly (workflows.py:636-661) "
+            "and schedule evaluation (factorized_runtime.cpp:252-287 restated)")
+
+
+def cpu_baseline(sample_atoms, bundle_stem, forces=True):
+    """The reference CPU path restated (oracle) on all host cores, as a marginal per-atom rate:
+    the time of a ``sample_atoms`` sample minus that of a 128-atom sample (the fixed per-step host
+    cost), so that the rate is the one a full-size run would see."""
+    cores = len(os.sched_getaffinity(0))
+    M = int(sample_atoms)
+    t_fixed = _cpu_sample(CPU_FIXED_SAMPLE, bundle_stem, forces, cores)
+    t = _cpu_sample(M, bundle_stem, forces, cores)
+    rate = (M - CPU_FIXED_SAMPLE) / max(t - t_fixed, 1e-9)
+    return {"value": rate, "unit": "atoms/s", "cores": cores, "kind": "port",
+            "sample": f"marginal rate: ({M} - {CPU_FIXED_SAMPLE}) atoms / ({t:.1f} s - {t_fixed:.1f} s), two "
+                      f"periodic samples of the same density/species/cutoff; {_cpu_what(forces)} ({cores} "
+                      f"threads); the plain {M}-atom rate is {M / t:.1f} atoms/s"}
 
 
 def run_reference(args):
+    """The reference's CPU path (oracle restatement) on rank 0: the warm-up's first sample
+    measures the fixed per-step host cost on 128 atoms, every other step times a
+    ``--cpu-sample``-atom sample; value = marginal atoms/s."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    K, W = args.steps, args.warmup
-    base = None
-    times = []
-    for i in range(W + K):
-        cb = cpu_baseline(args.cpu_sample, args.bundle, forces=not args.energy_only)
-        if i >= W:
-            times.append(cb)
-        base = cb
-    vals = [t["value"] for t in times]
-    value = statistics.median(vals)
+    K, W = args.steps, max(1, args.warmup)
+    forces = not args.energy_only
+    cores = len(os.sched_getaffinity(0))
+    M = int(args.cpu_sample)
+    t_fixed = _cpu_sample(CPU_FIXED_SAMPLE, args.bundle, forces, cores)
+    for _ in range(W - 1):
+        _cpu_sample(M, args.bundle, forces, cores)
+    times = [_cpu_sample(M, args.bundle, forces, cores) for _ in range(K)]
+    t = statistics.median(times)
+    value = (M - CPU_FIXED_SAMPLE) / max(t - t_fixed, 1e-9)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": args.gpus,
-            "steps": K, "warmup": W, "ms_per_step": 1e3 * args.cpu_sample / value,
+            "steps": K, "warmup": args.warmup, "ms_per_step": 1e3 * args.atoms / value,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic", "config": _config(args),
-            "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": base["cores"], "kind": "port",
-                             "sample": base["sample"]},
+            "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": cores, "kind": "port",
+                             "sample": f"marginal rate: ({M} - {CPU_FIXED_SAMPLE}) atoms / (median {t:.1f} s of "
+                                       f"{K} samples - {t_fixed:.1f} s); {_cpu_what(forces)} ({cores} threads); "
+                                       f"ms_per_step is the {args.atoms}-atom step at that rate; the plain "
+                                       f"{M}-atom rate is {M / t:.1f} atoms/s"},
             "e2e": {"value": value, "unit": "atoms/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces, ref_ms, F_ref=None, E_ref=None):
-    """One look at the recoupled B-basis passes on this run's own system, after every timed
-    region and outside the reported value: the pass's CUDA-event time in two CTA shapes
-    (best of three after one warm-up call) against the term-level kernels' stage time of the
-    timed steps (``ref_ms``), and the largest relative difference of the energies (and of
-    dE/dA with forces) from the term-level kernels on the same A."""
-    try:
-        from ye3t_b200.recoupling import RecoupledEvaluator, build_recoupled_plan
-        N = pos_d.shape[0]
-        row, nbr = ev.neighbor_list(pos_d, box, 0, N)
-        A = ev.density(pos_d, sp_d, box, row, nbr, 0)
-        sp = sp_d[:N].contiguous()
-
-        def timed(fn):
-            fn()
-            best = None
-            for _ in range(3):
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record()
-                out = fn()
-                b.record()
-                torch.cuda.synchronize()
-                best = a.elapsed_time(b) if best is None else min(best, a.elapsed_time(b))
-            return best, out
-
-        if forces:
-            e0, G0 = ev.energy_grad(A, sp)
-        else:
-            e0 = ev.energy_from_density(A, sp)
-        plan = build_recoupled_plan(bundle)
-        try:  # the symmetric shapes are valid only for densities with the physical symmetry
-            RecoupledEvaluator(bundle, device, None, plan=plan, symmetric=True).check_symmetry(A)
-            density_symmetric = True
-        except ValueError as exc:
-            density_symmetric = str(exc)[:200]
-        shapes, forward = {}, {}
-        for na, th, symmetric in ((1, 256, False), (2, 256, False), (2, 512, False), (3, 512, False),
-                                  (1, 256, True), (2, 256, True), (4, 256, True), (3, 512, True)):
-            key = f"{'symmetric ' if symmetric else ''}{na}x{th}"
-            try:  # one shape's failure is recorded beside it and does not hide the others
-                rec = RecoupledEvaluator(bundle, device, weights, plan=plan, atoms_per_cta=na,
-                                         threads_per_cta=th, symmetric=symmetric)
-                if forces:
-                    ms, (e1, G1) = timed(lambda: rec.energy_grad(A, sp))
-                    gdiff = float((G1 - G0).abs().max() / G0.abs().max())
-                    del G1
-                else:
-                    ms, e1 = timed(lambda: rec.energy(A, sp))
-                    gdiff = None
-                shapes[key] = {"ms": ms, "energy_max_rel_diff": float((e1 - e0).abs().max() / e0.abs().max()),
-                               "dEdA_max_rel_diff": gdiff}
-                if forces and (na, th) in ((1, 256), (2, 512), (4, 256)):
-                    fms, e2 = timed(lambda: rec.energy(A, sp))
-                    forward[key] = {"ms": fms,
-                                    "energy_max_rel_diff": float((e2 - e0).abs().max() / e0.abs().max())}
-            except Exception as exc:
-                shapes[key] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
-        timed_ms = [v["ms"] for v in shapes.values() if "ms" in v]
-        best = min(timed_ms) if timed_ms else None
-        step = None
-        if best is not None:
-            try:  # one whole step with the fastest shape, its forces against the measured run's
-                key = min((k for k in shapes if "ms" in shapes[k]), key=lambda k: shapes[k]["ms"])
-                symmetric = key.startswith("symmetric")
-                na, th = (int(v) for v in key.split()[-1].split("x"))
-                rec = RecoupledEvaluator(bundle, device, weights, plan=plan, atoms_per_cta=na, threads_per_cta=th,
-                                         symmetric=symmetric)
-
-                def full_step():
-                    r, nb = ev.neighbor_list(pos_d, box, 0, N)
-                    Ad = ev.density(pos_d, sp_d, box, r, nb, 0)
-                    if not forces:
-                        return rec.energy(Ad, sp).sum(), None
-                    e, G = rec.energy_grad(Ad, sp)
-                    return e.sum(), ev.forces_from_edges(r, nb, ev.edge_grad(pos_d, sp_d, box, r, nb, G, begin=0))
-
-                sms, (E, F) = timed(full_step)
-                step = {"shape": key, "ms": sms, "atoms_per_s": N / (sms * 1e-3),
-                        "energy_rel_diff": None if E_ref is None else float(abs(float(E) - E_ref) / abs(E_ref)),
-                        "forces_max_rel_diff": None if F is None or F_ref is None else
-                        float((F - F_ref).abs().max() / F_ref.abs().max())}
-            except Exception as exc:
-                step = {"error": f"{type(exc).__name__}: {exc}"[:200]}
-        return {"pass": "energy_grad" if forces else "energy", "atoms": int(N),
-                "term_level_ms": ref_ms, "shapes_atoms_x_threads": shapes,
-                "speedup_vs_term_level": ref_ms / best if best else None,
-                "forward_energy_shapes": forward or None, "whole_step_with_fastest_shape": step,
-                "density_symmetric": density_symmetric,
-                "note": "not part of value; timed after the timed regions, against the term-level stage time"}
-    except Exception as exc:  # the probe must not take the measured line with it
-        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
-
-
 def _config(args):
     what = "energy" if getattr(args, "energy_only", False) else "energy + forces"
+    rec = getattr(args, "b_basis", "recoupled") == "recoupled"
+    sym = not getattr(args, "recoupled_general", False)
     return {"workload": f"C5 scalar ACE {what}: 2^20 atoms (periodic cubic box, 0.05/A^3, 3 species), "
                         "n_max 8, l_max 3, nu<=4 (25,328 words / 41,168 L=0 features), fp64, per-species "
                         "linear readout",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
             "parallelism": f"atom-block x{args.gpus}",
-            "b_basis": (f"recoupled pair contractions ({'M >= 0 symmetric, ' if args.recoupled_symmetric else ''}"
-                        f"{args.recoupled_atoms} atoms and {args.recoupled_threads} threads per CTA)"
-                        if getattr(args, "recoupled", False) else "term-level factorized schedules"),
+            "atom_order": "cell order (z, y, x) of a cell list with cells >= the cutoff, so each rank's atom "
+                          "block is a slab of the box",
+            "b_basis": (f"recoupled pair contractions ({'M >= 0 symmetric passes' if sym else 'general passes'})"
+                        if rec else "term-level factorized schedules"),
             "l2": "inputs larger than L2 (A-basis 2 GB, neighbour list 110 MB at 2^20 atoms)"}
 
 
+def cell_order(pos, box, cutoff):
+    """Permutation that sorts atoms by the (z, y, x) cell of a cell list whose cells are at
+    least ``cutoff`` wide (stable within a cell)."""
+    import numpy as np
+    n = max(1, int(box / cutoff))
+    c = np.clip(np.floor(np.mod(pos / box, 1.0) * n).astype(np.int64), 0, n - 1)
+    return np.lexsort((c[:, 0], c[:, 1], c[:, 2]))
+
+
 def run_b200(args):
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -332,32 +278,41 @@ def run_b200(args):
     rank, world = init_from_env("nccl", 300.0, device)
     N = int(args.atoms)
     pos, species, box = make_system(N)
+    order = torch.as_tensor(cell_order(pos.numpy(), box, CUTOFF))
+    pos, species = pos[order].contiguous(), species[order].contiguous()
     bundle = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", args.bundle + ".npz"))
     weights = make_weights(bundle.feature_count)
     ev = ACEEvaluator(bundle, device, config=ACEConfig(CUTOFF, LAMBDA), species_prefactor=PREFACTOR,
-                      weights=weights)
+                      weights=weights, b_basis=args.b_basis)
+    forces = not args.energy_only
+    physical = not args.recoupled_general
+    if args.b_basis == "recoupled":
+        if args.recoupled_atoms or args.recoupled_threads:
+            shape = (args.recoupled_atoms or 1, args.recoupled_threads or 256)
+            ev.RECOUPLED_GRAD_SHAPE = ev.RECOUPLED_ENERGY_SHAPE = shape
+        rec = ev.recoupled(physical, forces)
+    else:
+        rec = None
     begin, end = atom_block(rank, world, N)
     n_local = end - begin
     pos_h = pos.pin_memory()
     sp_h = species.pin_memory()
     pos_d = pos.to(device)
     sp_d = species.to(device)
+    sp_local = sp_d[begin:end]
     e_buf = torch.empty(n_local, dtype=torch.float64, device=device)
-    F_buf = torch.empty((N, 3), dtype=torch.float64, device=device)
-    forces = not args.energy_only
+    # forces: each rank scatters its rows' edge gradients into a full array, and
+    # a reduce-scatter leaves every rank the summed forces of its own block
+    chunk = (N + world - 1) // world
+    F_full = torch.empty((chunk * world, 3), dtype=torch.float64, device=device)
+    F_block = torch.empty((chunk, 3), dtype=torch.float64, device=device)
     stages = ("neighbors", "density", "energy_grad", "edge_grad", "forces") if forces else \
         ("neighbors", "density", "energy")
     timers = {k: [] for k in stages}
-    # our kernels per step: 6 neighbour-count, 1 fill, density, then the
-    # B-basis energy, or the B-basis adjoint (one launch per item class) + edge
-    # gradients + force gather/scatter
     from ye3t_b200.packing import GRAD_CLASSES
-    rec = None
-    if args.recoupled:
-        from ye3t_b200.recoupling import RecoupledEvaluator
-        rec = RecoupledEvaluator(bundle, device, weights, atoms_per_cta=args.recoupled_atoms,
-                                 threads_per_cta=args.recoupled_threads, symmetric=args.recoupled_symmetric)
     b_launches = 1 if rec is not None else GRAD_CLASSES
+    # our kernels per step: 6 neighbour-count, 1 fill, density, the B-basis
+    # pass(es), then edge gradients and the force gather/scatter
     launches_per_step = 8 + (b_launches + 2 if forces else 1)
 
     def step(record):
@@ -372,19 +327,20 @@ def run_b200(args):
         A = ev.density(pos_d, sp_d, box, row, nbr, begin)
         mark(2)
         if not forces:
-            e_at = rec.energy(A, sp_d[begin:end]) if rec is not None else \
-                ev.energy_from_density(A, sp_d[begin:end], out=e_buf)
+            e_at = ev.energy_from_density(A, sp_local, out=e_buf, physical=physical)
             mark(3)
             return sum_over_ranks(e_at.sum()), None, marks
-        e_at, G = rec.energy_grad(A, sp_d[begin:end]) if rec is not None else ev.energy_grad(A, sp_d[begin:end])
+        e_at, G = ev.energy_grad(A, sp_local, physical=physical)
         mark(3)
         g = ev.edge_grad(pos_d, sp_d, box, row, nbr, G, begin=begin)
         mark(4)
         if world == 1:
             F = ev.forces_from_edges(row, nbr, g)
         else:
-            F_buf.zero_()
-            F = sum_over_ranks(ev.partial_forces_from_edges(row, nbr, g, begin, N, out=F_buf))
+            F_full.zero_()
+            ev.partial_forces_from_edges(row, nbr, g, begin, N, out=F_full[:N])
+            dist.reduce_scatter_tensor(F_block, F_full, op=dist.ReduceOp.SUM)
+            F = F_block
         mark(5)
         return sum_over_ranks(e_at.sum()), F, marks
 
@@ -415,63 +371,68 @@ def run_b200(args):
         for k, a, b in zip(stages, m[:-1], m[1:]):
             timers[k].append(a.elapsed_time(b))
     energy = float(total.item())
+    forces_abs_sum = float(sum_over_ranks(F_last[:max(0, min(chunk, N - rank * chunk))].abs().sum()).item()) \
+        if forces else None
 
     # end to end through the public API with host buffers: H2D of positions
-    # and species every step, D2H of the total energy (and the forces)
-    for _ in range(max(1, args.warmup // 2)):
-        pos_d.copy_(pos_h, non_blocking=True)
-        sp_d.copy_(sp_h, non_blocking=True)
-        step(False)[0].to("cpu", non_blocking=False)
+    # and species every step, D2H of the total energy and this rank's forces
+    my_rows = max(0, min(chunk, N - rank * chunk)) if world > 1 else N
     host_total = torch.empty(1, dtype=torch.float64).pin_memory()
-    host_forces = torch.empty((N, 3), dtype=torch.float64).pin_memory() if forces else None
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
+    host_forces = torch.empty((max(my_rows, 1), 3), dtype=torch.float64).pin_memory() if forces else None
+
+    def e2e_step():
         pos_d.copy_(pos_h, non_blocking=True)
         sp_d.copy_(sp_h, non_blocking=True)
         tot, Fd, _ = step(False)
         host_total.copy_(tot.reshape(1), non_blocking=True)
-        if forces:
-            host_forces.copy_(Fd, non_blocking=True)
+        if forces and my_rows:
+            host_forces[:my_rows].copy_(Fd[:my_rows], non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
     e1.record()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
     peak = measure_fp64_peak(torch, nat, device)
-    flops = ev.packed.flops_per_atom()
     kern_ms = statistics.mean(timers["energy_grad" if forces else "energy"])
-    kern_flops = (flops["items_grad"] if forces else flops["items"]) + 2.0 * ev.feature_count
+    flops = ev.packed.flops_per_atom()
     if rec is not None:
-        rflops = rec.tables.flops_per_atom()
-        kern_flops = rflops["energy_grad" if forces else "energy"]
+        kern_flops = rec.tables.flops_per_atom()["energy_grad" if forces else "energy"]
+        kernel = ((f"recoupled_sym_energy_grad_kernel<{rec._c.atoms_per_cta}, {rec._c.threads_per_cta}>"
+                   if forces else
+                   f"recoupled_sym_energy_kernel<{rec._c.atoms_per_cta}, {rec._c.threads_per_cta}>")
+                  if physical else
+                  (f"recoupled_energy_grad_kernel<{rec._c.atoms_per_cta}, {rec._c.threads_per_cta}>" if forces
+                   else f"recoupled_forward_kernel<false, {rec._c.atoms_per_cta}, {rec._c.threads_per_cta}>"))
+        note = ("FP64 flops of the recoupled pass counted from its device tables "
+                "(ye3t_b200.recoupling RecoupledSymTables / RecoupledDeviceTables .flops_per_atom)")
+        tpath = os.path.join(REPO, "profiles", "recoupled_sym_grad_traffic.json" if forces and physical else "")
+    else:
+        kern_flops = (flops["items_grad"] if forces else flops["items"]) + 2.0 * ev.feature_count
+        kernel = "ace_grad_kernel (B-basis energy + dE/dA)" if forces else "ace_eval_kernel<1> (B-basis energy)"
+        note = ("FP64 flops the item walk needs on valid tuples (ye3t_b200.packing.item_grad_flops_per_atom with "
+                "forces, item_flops_per_atom without) plus the readout")
+        tpath = os.path.join(REPO, "profiles", "ace_grad_traffic.json" if forces else "ace_energy_traffic.json")
     sched_flops_launch = kern_flops * n_local
     term_flops_launch = (flops["terms"] + 2.0 * ev.feature_count) * n_local
     achieved = sched_flops_launch / (kern_ms * 1e-3) / 1e12
+    traffic = None
+    if os.path.isfile(tpath):
+        with open(tpath) as fh:
+            traffic = json.load(fh).get("dram_bytes_per_atom", 0) * n_local or None
     W = (bundle.lmax + 1) ** 2
     dens_ms = statistics.mean(timers["density"])
     avg_deg = float(0.05 * 4.0 / 3.0 * 3.141592653589793 * CUTOFF ** 3)
     dens_bytes_atom = 3 * 8 + 4 + 8 + 4 * avg_deg + bundle.nmax * W * 16
     dens_gbs = dens_bytes_atom * n_local / (dens_ms * 1e-3) / 1e9
-    try:
-        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
-            hbm_peak = float(json.load(fh)["hbm_gbs"])
-        hbm_src = "MEASURED_PEAKS.json hbm_gbs (measured copy)"
-    except (OSError, KeyError, ValueError):
-        hbm_peak, hbm_src = 6650.0, "fallback 6.65 TB/s"
-    traffic = None
-    tpath = os.path.join(REPO, "profiles", "ace_grad_traffic.json" if forces else "ace_energy_traffic.json")
-    if rec is None and os.path.exists(tpath):
-        with open(tpath) as fh:
-            t = json.load(fh)
-        traffic = t.get("dram_bytes_per_atom", 0) * n_local or None
+    hbm_peak, hbm_src = _hbm_peak()
 
-    forces_abs_sum = float(F_last.abs().sum().item()) if forces else None
-    probe = None
-    if world == 1 and rec is None and not args.no_recoupled_probe:
-        probe = recoupled_probe(torch, ev, bundle, weights, device, pos_d, sp_d, box, forces,
-                                statistics.mean(timers["energy_grad" if forces else "energy"]),
-                                F_ref=F_last if forces else None, E_ref=energy)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_sample, args.bundle, forces=not args.energy_only)
@@ -486,27 +447,14 @@ def run_b200(args):
         "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded uniform positions, random readout)",
         "config": _config(args),
-        "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
-                "d2h_bytes_per_step": 8 + (N * 24 if forces else 0)},
+        "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": world * N * (24 + 4),
+                "d2h_bytes_per_step": world * 8 + (N * 24 if forces else 0)},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": {"bound": "fp64",
-                     "kernel": (("recoupled_energy_grad_kernel (B-basis energy + dE/dA, recoupled)" if forces
-                                 else "recoupled_forward_kernel<false> (B-basis energy, recoupled)")
-                                if rec is not None else
-                                ("ace_grad_kernel (B-basis energy + dE/dA)" if forces
-                                 else "ace_eval_kernel<1> (B-basis energy, symmetric blocks on chip)")),
-                     "achieved": achieved,
+        "roofline": {"bound": "fp64", "kernel": kernel, "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "flops_per_launch": sched_flops_launch,
-                     "flops_note": ("FP64 flops of the recoupled pass counted from its tables "
-                                    "(ye3t_b200.recoupling.RecoupledDeviceTables / RecoupledSymTables"
-                                    ".flops_per_atom)"
-                                    if rec is not None else
-                                    "FP64 flops the item walk needs on valid tuples "
-                                    "(ye3t_b200.packing.item_grad_flops_per_atom with forces, "
-                                    "item_flops_per_atom without) plus the readout") +
-                                   "; the reference's forward term-by-term count for the same features is "
-                                   f"{term_flops_launch:.4g} per launch",
+                     "flops_note": note + "; the reference's forward term-by-term count for the same features is "
+                                          f"{term_flops_launch:.4g} per launch",
                      "peak_source": "FP64 FMA microbenchmark (y3b_fma_peak_launch) measured in this run; "
                                     "MEASURED_PEAKS.json has no FP64 figure"},
         "roofline_density": {"bound": "hbm", "kernel": "ace_density_kernel<3>", "achieved": dens_gbs,
@@ -515,11 +463,18 @@ def run_b200(args):
         "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
         "energy_total": energy,
         "forces_abs_sum": forces_abs_sum,
-        "recoupled_probe": probe,
         "clocks": clock_info,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
+
+
+def _hbm_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (measured copy)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
 
 
 # Channel-diagonal configurations: radial channels mixed per species pair,
@@ -726,20 +681,305 @@ def run_channels(args):
     print(json.dumps(line), flush=True)
 
 
+# -- C1: the quickstart schedule over supplied factor arrays ---------------------------------
+C1_WORKLOAD = ("C1 quickstart: compile_ace_factorized_schedules_by_L(content=(1,1,2), input_Ls=(1,1,0)), L = 0 "
+               "(hash 00112c9d4a6cb444), Sym^2(V_1) -> 0 block and a leaf, on seeded N(0,1) factor arrays of 4,096 "
+               "atoms x 8 radial channels (l = 1 and l = 0), all 56 ordered channel bindings (229,376 rows), fp64")
+
+
+def _c1_inputs():
+    """Seeded factor arrays (``torch.Generator().manual_seed(0)``: A1 then A0), the quickstart
+    schedule record and the Sym^2(V_1) -> 0 table."""
+    import numpy as np
+    import torch
+
+    from ye3t_b200.schedules import ACEBundle, ScheduleRecord
+    g = np.load(os.path.join(REPO, "tests", "golden", "quickstart.npz"))
+    specs = json.loads(bytes(g["q_specs"]).decode())
+    rec = ScheduleRecord(rank=0, block_count=int(g["q_bm"].shape[1]), L_R=0, n_tuple=(), l_tuple=(),
+                         block_specs=tuple(tuple(tuple(x) for x in label) for label in specs),
+                         component_offsets=g["q_off"], component_label_index=g["q_cli"],
+                         component_M_R=np.zeros_like(g["q_cli"]), block_m_tuples=g["q_bm"], coeffs=g["q_co"],
+                         convention_hash=bytes(g["convention_hash"]).decode())
+    gen = torch.Generator().manual_seed(0)
+    A1 = torch.randn(4096, 8, 3, dtype=torch.float64, generator=gen)
+    A0 = torch.randn(4096, 8, 1, dtype=torch.float64, generator=gen)
+    b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", BUNDLE + ".npz"))
+    pairs = [(n1, n2) for n1 in range(8) for n2 in range(8) if n1 != n2]
+    return rec, A1, A0, b.sym_tables[(1, 2, 0, 0)], pairs
+
+
+def _l2_flush(torch, device):
+    """A buffer twice the size of L2 (126 MB), written between timed steps of small configurations."""
+    buf = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    return lambda: buf.fill_(1)
+
+
+def _timed_steps(torch, step, steps, flush):
+    """Sum of CUDA-event times of ``steps`` calls of ``step``, L2 flushed before each."""
+    total = 0.0
+    for _ in range(steps):
+        flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return total / steps
+
+
+def cpu_c1(steps=1):
+    """The quickstart on the CPU oracle (the reference's grouped symmetric power and its C++ schedule
+    evaluator restated), all 56 bindings, one thread per the reference's serial loop."""
+    import numpy as np
+
+    from oracle import oracle
+    rec, A1, A0, t, pairs = _c1_inputs()
+    A1, A0 = A1.numpy(), A0.numpy()
+    best = None
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        sym = oracle.symmetric_power_monomial(A1.reshape(-1, 3), t.monomial_counts, t.output_offsets,
+                                              t.monomial_value.real).reshape(4096, 8)
+        bv = np.zeros((4096 * len(pairs), 1, 2, 1))
+        for r, (n1, n2) in enumerate(pairs):
+            bv[r * 4096:(r + 1) * 4096, 0, 0, 0] = sym[:, n1]
+            bv[r * 4096:(r + 1) * 4096, 0, 1, 0] = A0[:, n2, 0]
+        out = oracle.schedule_evaluate_record(bv, rec)
+        dt = time.perf_counter() - t0
+        assert np.isfinite(out).all()
+        best = dt if best is None else min(best, dt)
+    return {"value": 4096 / best, "unit": "atoms/s", "cores": 1, "kind": "port",
+            "sample": "the whole C1 workload (4,096 atoms x 56 bindings): grouped symmetric power "
+                      "(ye3t_runtime_core.cpp:5279 restated), block assembly (workflows.py:636-661) and the "
+                      f"schedule evaluation (factorized_runtime.cpp:252-287 restated), 1 thread; {best * 1e3:.1f} ms"}
+
+
+def run_c1(args):
+    import torch
+
+    from ye3t_b200 import _native as nat
+    from ye3t_b200.couplings import evaluate_factorized_schedule_torch
+    from ye3t_b200.runtime import symmetric_power_monomial_contraction
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    rec, A1h, A0h, t, pairs = _c1_inputs()
+    n1 = torch.tensor([p[0] for p in pairs], device=device)
+    n2 = torch.tensor([p[1] for p in pairs], device=device)
+    counts = torch.as_tensor(t.monomial_counts, device=device)
+    offsets = torch.as_tensor(t.output_offsets, device=device)
+    idx = torch.as_tensor(t.output_index, device=device)
+    vals = torch.as_tensor(t.monomial_value.real.copy(), device=device)
+    A1h, A0h = A1h.pin_memory(), A0h.pin_memory()
+    A1 = A1h.to(device)
+    A0 = A0h.to(device)
+    host_out = torch.empty((4096 * len(pairs), 1), dtype=torch.float64).pin_memory()
+
+    def step():
+        sym = symmetric_power_monomial_contraction(A1.reshape(-1, 3), counts, offsets, idx, vals).reshape(4096, 8)
+        bv = torch.stack((sym[:, n1].t().reshape(-1), A0[:, n2, 0].t().reshape(-1)), dim=1).reshape(-1, 1, 2, 1)
+        return evaluate_factorized_schedule_torch(bv, rec)
+
+    def e2e():
+        A1.copy_(A1h, non_blocking=True)
+        A0.copy_(A0h, non_blocking=True)
+        host_out.copy_(step(), non_blocking=True)
+
+    flush = _l2_flush(torch, device)
+    for _ in range(args.warmup):
+        step()
+        e2e()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    ms = _timed_steps(torch, step, args.steps, flush)
+    clock_info = clocks.stop()
+    e2e_ms = _timed_steps(torch, e2e, args.steps, flush)
+    rows = 4096 * len(pairs)
+    # algorithmic bytes: the factor arrays read once, the 229,376 outputs written once
+    nbytes = (4096 * 8 * 3 + 4096 * 8 + rows) * 8
+    hbm_peak, hbm_src = _hbm_peak()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    cpu = None if args.no_cpu_baseline else cpu_c1(3)
+    line = {"metric": "ACE quickstart schedule atoms/sec (c1)", "value": 4096 / (ms * 1e-3), "unit": "atoms/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded N(0,1) factors)",
+            "config": {"workload": C1_WORKLOAD, "atoms": 4096, "bindings": len(pairs),
+                       "l2": "L2 flushed (256 MB write) before every timed step"},
+            "e2e": {"value": 4096 / (e2e_ms * 1e-3), "unit": "atoms/s",
+                    "h2d_bytes_per_step": int(A1h.numel() + A0h.numel()) * 8, "d2h_bytes_per_step": rows * 8},
+            "gpu_launches": 2 * args.steps,  # symmetric power + schedule evaluation (the binding gather is torch)
+            "roofline": {"bound": "hbm", "kernel": "symmetric power + factorized schedule evaluation", "achieved": gbs,
+                         "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak, "traffic": None,
+                         "bytes_per_step": nbytes, "peak_source": hbm_src,
+                         "note": "a few MB per step: launch-bound, not bandwidth-bound"},
+            "clocks": clock_info, "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+
+
+# -- C2: single-species nu <= 3 descriptor ---------------------------------------------------
+C2_BUNDLE = "ace_n8_l3_nu3_L0"
+C2_WORKLOAD = ("C2 single-species scalar ACE descriptor: 16,384 atoms (periodic cubic box, 0.05/A^3), 1 species, "
+               "ChebExpCos n_max 8, l_max 3, nu<=3 (3,280 words -> 2,344 L=0 features per atom), cutoff 5 A, fp64")
+
+
+def cpu_c2(sample_atoms):
+    """The reference CPU path restated for the C2 descriptor, as a marginal per-atom rate."""
+    import numpy as np
+
+    from oracle import oracle
+    from ye3t_b200.schedules import ACEBundle
+    b = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", C2_BUNDLE + ".npz"))
+    cores = len(os.sched_getaffinity(0))
+
+    def sample(M):
+        rng = np.random.default_rng(0)
+        box = (M / DENSITY) ** (1 / 3)
+        pos = rng.uniform(0, box, (M, 3))
+        sp = np.zeros(M, dtype=np.int32)
+        t0 = time.perf_counter()
+        off, nbr, disp = oracle.neighbor_list(pos, box, CUTOFF)
+        A = oracle.ace_density(disp, off, nbr, sp, np.ones(1), b.nmax, b.lmax, CUTOFF, LAMBDA)
+        F = oracle.bundle_features(b, A, threads=cores)
+        assert np.isfinite(F).all()
+        return time.perf_counter() - t0
+
+    t_fixed, t = sample(CPU_FIXED_SAMPLE), sample(sample_atoms)
+    rate = (sample_atoms - CPU_FIXED_SAMPLE) / max(t - t_fixed, 1e-9)
+    return {"value": rate, "unit": "atoms/s", "cores": cores, "kind": "port",
+            "sample": f"marginal rate: ({sample_atoms} - {CPU_FIXED_SAMPLE}) atoms / ({t:.1f} s - {t_fixed:.1f} s); "
+                      "brute-force neighbour list, A-basis, then per word the reference block assembly "
+                      "(workflows.py:636-661) and schedule evaluation (factorized_runtime.cpp:252-287 restated) "
+                      f"({cores} threads)"}
+
+
+def run_c2(args):
+    import torch
+
+    from ye3t_b200 import _native as nat
+    from ye3t_b200.ace import ACEConfig, ACEEvaluator
+    from ye3t_b200.schedules import ACEBundle
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    N = 16384
+    box = (N / DENSITY) ** (1.0 / 3.0)
+    pos = torch.rand(N, 3, dtype=torch.float64, generator=torch.Generator().manual_seed(0)) * box
+    pos = pos[torch.as_tensor(cell_order(pos.numpy(), box, CUTOFF))].contiguous()
+    species = torch.zeros(N, dtype=torch.int32)
+    bundle = ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", C2_BUNDLE + ".npz"))
+    ev = ACEEvaluator(bundle, device, config=ACEConfig(CUTOFF, LAMBDA), species_prefactor=[1.0])
+    pos_h, sp_h = pos.pin_memory(), species.pin_memory()
+    pos_d, sp_d = pos.to(device), species.to(device)
+    F = torch.empty((N, ev.feature_count), dtype=torch.complex128, device=device)
+    host_F = torch.empty((N, ev.feature_count), dtype=torch.complex128).pin_memory()
+    stages = ("neighbors", "density", "features")
+    timers = {k: [] for k in stages}
+
+    def step(marks=None):
+        if marks:
+            marks[0].record()
+        row, nbr = ev.neighbor_list(pos_d, box)
+        if marks:
+            marks[1].record()
+        A = ev.density(pos_d, sp_d, box, row, nbr)
+        if marks:
+            marks[2].record()
+        ev.features(A, out=F)
+        if marks:
+            marks[3].record()
+        return F
+
+    def e2e():
+        pos_d.copy_(pos_h, non_blocking=True)
+        sp_d.copy_(sp_h, non_blocking=True)
+        host_F.copy_(step(), non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+        e2e()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    all_marks = []
+
+    def recorded():
+        m = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        all_marks.append(m)
+        step(m)
+
+    # the 614 MB feature output is larger than L2, so no flush is needed
+    ms = _timed_steps(torch, recorded, args.steps, lambda: None)
+    clock_info = clocks.stop()
+    for m in all_marks:
+        for k, a, b in zip(stages, m[:-1], m[1:]):
+            timers[k].append(a.elapsed_time(b))
+    e2e_ms = _timed_steps(torch, e2e, args.steps, lambda: None)
+    peak = measure_fp64_peak(torch, nat, device)
+    feat_ms = statistics.mean(timers["features"])
+    flops = ev.packed.flops_per_atom()["items"] * N
+    nbytes = (ev.feature_count + bundle.nmax * (bundle.lmax + 1) ** 2) * 16 * N
+    hbm_peak, hbm_src = _hbm_peak()
+    if flops / (peak * 1e12) >= nbytes / (hbm_peak * 1e9):
+        roof = {"bound": "fp64", "achieved": flops / (feat_ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                "peak_source": "FP64 FMA microbenchmark (y3b_fma_peak_launch) in this run"}
+    else:
+        roof = {"bound": "hbm", "achieved": nbytes / (feat_ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                "peak_source": hbm_src}
+    roof.update({"kernel": "ace_eval_kernel<double, 0> (features)", "frac": roof["achieved"] / roof["peak"],
+                 "traffic": None, "flops_per_launch": flops, "bytes_per_launch": nbytes})
+    cpu = None if args.no_cpu_baseline else cpu_c2(args.cpu_sample or 512)
+    line = {"metric": "ACE descriptor atoms/sec (c2)", "value": N / (ms * 1e-3), "unit": "atoms/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded uniform positions)",
+            "config": {"workload": C2_WORKLOAD, "atoms": N, "bundle": C2_BUNDLE, "cutoff_A": CUTOFF,
+                       "radial_lambda": LAMBDA, "l2": "feature output (614 MB) larger than L2"},
+            "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * 28,
+                    "d2h_bytes_per_step": N * ev.feature_count * 16},
+            "gpu_launches": 9 * args.steps,  # 7 neighbour-list, density, features
+            "roofline": roof, "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
+            "clocks": clock_info, "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+
+
+def _reference_line(args, metric, runs):
+    """The reference arm's line from per-step ``cpu_baseline``-style records."""
+    v = statistics.median([x["value"] for x in runs])
+    print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "atoms/s", "n_gpus": args.gpus,
+                      "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                      "cpu_baseline": dict(runs[-1], value=v),
+                      "e2e": {"value": v, "unit": "atoms/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
 def main():
     args = parse()
+    rank0 = int(os.environ.get("RANK", "0")) == 0
+    if args.config == "c1":
+        if args.impl == "reference":
+            if rank0:
+                _reference_line(args, "ACE quickstart schedule atoms/sec (c1)",
+                                [cpu_c1() for _ in range(args.warmup + args.steps)][args.warmup:])
+            return
+        run_c1(args)
+        return
+    if args.config == "c2":
+        if args.impl == "reference":
+            if rank0:
+                _reference_line(args, "ACE descriptor atoms/sec (c2)",
+                                [cpu_c2(args.cpu_sample or 512) for _ in range(args.steps)])
+            return
+        run_c2(args)
+        return
     if args.config != "c5":
         if args.impl == "reference":
-            if int(os.environ.get("RANK", "0")) == 0:
+            if rank0:
                 cfg = CHANNEL_CONFIGS[args.config]
-                vals = [cpu_channels_baseline(cfg, 512) for _ in range(args.warmup + args.steps)][args.warmup:]
-                v = statistics.median([x["value"] for x in vals])
-                print(json.dumps({"impl": "reference", "metric": f"ACE channel-diagonal features atoms/sec "
-                                                               f"({args.config})", "value": v, "unit": "atoms/s",
-                                  "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                                  "higher_is_better": True, "cpu_baseline": dict(vals[-1], value=v),
-                                  "e2e": {"value": v, "unit": "atoms/s", "h2d_bytes_per_step": 0,
-                                          "d2h_bytes_per_step": 0}}), flush=True)
+                _reference_line(args, f"ACE channel-diagonal features atoms/sec ({args.config})",
+                                [cpu_channels_baseline(cfg, 512) for _ in range(args.warmup + args.steps)]
+                                [args.warmup:])
             return
         run_channels(args)
         return

@@ -226,8 +226,10 @@ int y3b_density_accumulate_csr(int dtype, const void* edge_values, const int64_t
  * until exit, enough when y3b_density_accumulate_workspace_bytes(E, N) is at
  * most that size; larger problems are rejected with Y3B_ERR_WORKSPACE.  The
  * first call on a device looks up the array's device address (make it before
- * any stream capture).  All calls on a device share the array: calls that
- * overlap on the GPU race and must be serialised by the caller. */
+ * any stream capture) and keeps it for the life of the process, so a device
+ * reset (cudaDeviceReset) or a re-created primary context invalidates this
+ * entry point for that device.  All calls on a device share the array: calls
+ * that overlap on the GPU race and must be serialised by the caller. */
 #define Y3B_NOALLOC_SCRATCH_BYTES (16ll * 1024 * 1024)
 int y3b_density_accumulate_noalloc(int dtype, const void* edge_values, const int64_t* centers,
                                    int64_t edge_count, int64_t channel_count, int64_t atom_count,

@@ -9,6 +9,7 @@
 // same source, barriers and index checks as the device run.
 #define Y3B_EMULATE 1
 
+#include <algorithm>
 #include <atomic>
 #include <barrier>
 #include <cmath>
@@ -108,7 +109,7 @@ extern "C" int emu_recoupled_energy_grad(int na, int th, const y3b_recoupled_tab
                                          int64_t atom_count, const int32_t* species, const double* k,
                                          int64_t species_count, double* energy, double* G, int32_t* status) {
   const y3b::RecTabs t = y3b::device_view(*tables);
-  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * t.max_pass_components) * 16;
+  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * std::max(t.row_width, t.max_pass_components)) * 16;
   if (smem > sizeof(y3b_emulated_smem)) return -1;
   const auto* a2 = reinterpret_cast<const double2*>(A);
   auto* g2 = reinterpret_cast<double2*>(G);
@@ -207,7 +208,7 @@ extern "C" int y3b_ace_recoupled_energy_grad_symmetric(const y3b_recoupled_sym_t
   na = tables->atoms_per_cta == 0 ? 1 : tables->atoms_per_cta;
   th = tables->threads_per_cta == 0 ? 256 : tables->threads_per_cta;
   const y3b::SymTabs t = y3b::sym_view(*tables);
-  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * t.max_pass_components) * 16;
+  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * std::max(t.row_width, t.max_pass_components)) * 16;
   if (smem > sizeof(y3b_emulated_smem)) return -1;
   const auto* a2 = static_cast<const double2*>(A);
   auto* g2 = static_cast<double2*>(dEdA);

@@ -18,16 +18,21 @@ def _bundle(stem):
     return ACEBundle.load(os.path.join(REPO, "ye3t_b200", "bundles", stem + ".npz"))
 
 
-def _evaluator(small, stem, weights):
+def _evaluator(small, stem, weights, b_basis="recoupled"):
     from ye3t_b200.ace import ACEConfig, ACEEvaluator
     return ACEEvaluator(_bundle(stem), DEV, config=ACEConfig(float(small["rc"]), float(small["lam"])),
-                        species_prefactor=small["prefactor"], weights=weights)
+                        species_prefactor=small["prefactor"], weights=weights, b_basis=b_basis)
 
 
-def test_forces_match_reference_autograd(golden):
+# the B-basis adjoint of the product path (recoupled passes) and the term-level kernels
+B_BASES = pytest.mark.parametrize("b_basis", ["recoupled", "term"])
+
+
+@B_BASES
+def test_forces_match_reference_autograd(golden, b_basis):
     small = golden("ace_small")
     ref = golden("forces_small")
-    ev = _evaluator(small, "ace_n8_l3_nu3_L0", small["w3"])
+    ev = _evaluator(small, "ace_n8_l3_nu3_L0", small["w3"], b_basis)
     pos = torch.as_tensor(small["pos"], device=DEV)
     sp = torch.as_tensor(small["species"], device=DEV)
     E, F = ev.energy_forces(pos, sp, float(small["box"]))
@@ -37,7 +42,8 @@ def test_forces_match_reference_autograd(golden):
     assert err <= 1e-10, err
 
 
-def test_forces_nu4_bundle_match_reference_autograd(golden):
+@B_BASES
+def test_forces_nu4_bundle_match_reference_autograd(golden, b_basis):
     """The C5 bundle (nu <= 4, all four adjoint classes) with a readout on every 23rd word
     (1,102 words; every other feature weighted 0): total energy and forces against torch
     autograd through the reference ops on the 96-atom system."""
@@ -52,7 +58,7 @@ def test_forces_nu4_bundle_match_reference_autograd(golden):
         W[:, lo:hi] = ref["weights"][:, col:col + hi - lo]
         col += hi - lo
     assert col == ref["weights"].shape[1]
-    ev = _evaluator(small, "ace_n8_l3_nu4_L0", W)
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", W, b_basis)
     pos = torch.as_tensor(small["pos"], device=DEV)
     sp = torch.as_tensor(small["species"], device=DEV)
     E, F = ev.energy_forces(pos, sp, float(small["box"]))
@@ -61,10 +67,11 @@ def test_forces_nu4_bundle_match_reference_autograd(golden):
     assert err <= 1e-10, err
 
 
-def test_energy_grad_energy_equals_forward_and_gradient_is_exact(golden):
+@B_BASES
+def test_energy_grad_energy_equals_forward_and_gradient_is_exact(golden, b_basis):
     small = golden("ace_small")
     rng = np.random.default_rng(4)
-    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168), b_basis)
     N = 1024
     box = (N / 0.05) ** (1 / 3)
     pos = torch.as_tensor(rng.uniform(0, box, size=(N, 3)), device=DEV)
@@ -82,10 +89,11 @@ def test_energy_grad_energy_equals_forward_and_gradient_is_exact(golden):
     assert abs((ep - em) / 2 - lin) <= 1e-6 * abs(lin) + 1e-12
 
 
-def test_forces_sum_to_zero_and_match_finite_differences(golden):
+@B_BASES
+def test_forces_sum_to_zero_and_match_finite_differences(golden, b_basis):
     small = golden("ace_small")
     rng = np.random.default_rng(5)
-    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168), b_basis)
     N = 512
     box = (N / 0.05) ** (1 / 3)
     pos0 = rng.uniform(0, box, size=(N, 3))
@@ -122,13 +130,17 @@ def test_partial_forces_sum_to_gather_forces(golden):
     np.testing.assert_allclose(acc.cpu().numpy(), F.cpu().numpy(), rtol=1e-10, atol=1e-12)
 
 
-def test_energy_grad_many_ctas_matches_forward_and_repeats(golden):
+@B_BASES
+def test_energy_grad_many_ctas_matches_forward_and_repeats(golden, b_basis):
     """Thousands of CTAs (races between loading A and the item walk, or between
     warps adding to G, would show here): the adjoint's energies equal the
-    forward kernel's and a second run agrees with the first."""
+    forward kernel's and a second run agrees with the first (bit for bit on the
+    recoupled passes, whose sums have a fixed order; the term-level adjoint adds
+    gradients with shared-memory atomics, so its repeats may differ in the last
+    bits)."""
     small = golden("ace_small")
     rng = np.random.default_rng(11)
-    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168), b_basis)
     N = 8192
     box = (N / 0.05) ** (1 / 3)
     pos = torch.as_tensor(rng.uniform(0, box, size=(N, 3)), device=DEV)
@@ -142,6 +154,12 @@ def test_energy_grad_many_ctas_matches_forward_and_repeats(golden):
     np.testing.assert_allclose(e2.cpu().numpy(), e_fwd, rtol=1e-11, atol=1e-11)
     scale = G1.abs().max().item()
     assert (G1 - G2).abs().max().item() <= 1e-12 * scale
+    if b_basis == "recoupled":
+        assert torch.equal(G1, G2) and torch.equal(e1, e2)
+    # the symmetric passes on this physical density: the same energies and dE/dA
+    e3, G3 = ev.energy_grad(A, sp, physical=True)
+    np.testing.assert_allclose(e3.cpu().numpy(), e_fwd, rtol=1e-11, atol=1e-11)
+    assert (G3 - G1).abs().max().item() <= 1e-12 * scale
 
 
 @pytest.mark.parametrize("stem", ["ace_diag_l3_nu3_L0", "ace_diag_l4_nu4_L0"])
@@ -155,7 +173,7 @@ def test_energy_grad_single_slot_pool(golden, stem):
     b = _bundle(stem)
     rng = np.random.default_rng(5)
     ev = ACEEvaluator(b, DEV, config=ACEConfig(float(small["rc"]), float(small["lam"])),
-                      weights=rng.normal(size=(2, b.feature_count)))
+                      weights=rng.normal(size=(2, b.feature_count)), b_basis="term")
     N = 2048
     W = (b.lmax + 1) ** 2
     A = torch.complex(torch.randn(N, 1, W, dtype=torch.float64, device=DEV),
@@ -181,7 +199,7 @@ def test_energy_grad_flags_a_run_item_outside_its_bounds(golden):
     from ye3t_b200.packing import GRAD_CLASSES
     small = golden("ace_small")
     rng = np.random.default_rng(9)
-    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168))
+    ev = _evaluator(small, "ace_n8_l3_nu4_L0", rng.normal(size=(3, 41168)) / np.sqrt(41168), "term")
     items, groups = ev.packed.arrays["items"], ev.packed.arrays["groups"]
     P = ev.packed.arrays["phases"].shape[0]
     off = ev.packed.arrays["group_offsets"].cpu().numpy().reshape(GRAD_CLASSES, P + 1)

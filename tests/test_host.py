@@ -145,3 +145,37 @@ def test_ctypes_signatures_match_header_parameter_counts():
     assert counts and set(counts) == set(_native._SIGS)
     for name, (_, args) in _native._SIGS.items():
         assert len(args) == counts[name], (name, len(args), counts[name])
+
+
+def test_bench_cell_order_makes_rank_blocks_slabs():
+    """bench.cell_order sorts atoms by (z, y, x) cell, so that the contiguous atom blocks of
+    the ranks are slabs of the box: block r's z cells form one run, and consecutive blocks
+    meet at most in one cell layer."""
+    import sys
+
+    import numpy as np
+    if REPO not in sys.path:
+        sys.path.insert(0, REPO)
+    import bench
+    from ye3t_b200.distributed import atom_block
+    N = 20000
+    box = (N / 0.05) ** (1 / 3)
+    pos = np.random.default_rng(0).uniform(0, box, (N, 3))
+    order = bench.cell_order(pos, box, 5.0)
+    assert sorted(order.tolist()) == list(range(N))
+    n = int(box / 5.0)
+    cz = np.floor(pos[order, 2] / box * n).astype(int)
+    assert np.all(np.diff(cz) >= 0)
+    last = -1
+    for r in range(4):
+        b, e = atom_block(r, 4, N)
+        assert cz[b] >= last
+        last = cz[e - 1]
+    # the default C5 run takes the recoupled passes
+    argv = sys.argv
+    try:
+        sys.argv = ["bench.py"]
+        args = bench.parse()
+    finally:
+        sys.argv = argv
+    assert args.b_basis == "recoupled" and not args.recoupled_general and args.config == "c5"

@@ -508,19 +508,41 @@ def test_symmetry_check_refuses_non_physical_densities(plan5, physical_case):
         ev.check_symmetry(torch.as_tensor(rng.normal(size=(2, 8, 16)) + 1j * rng.normal(size=(2, 8, 16))))
 
 
-def test_bench_probe_runs_on_emulated_passes(emulated, plan5, physical_case, monkeypatch):
-    """bench.recoupled_probe end to end on the CPU: the library swapped for the emulation
-    harness, CUDA events stubbed, and a stand-in evaluator that returns the reference's
-    densities with the oracle's energies and dE/dA.  Every shape and the whole step must agree
-    with them, and the field must be plain JSON."""
+def _sub_bundle(b, keep):
+    """The words of ``b`` that ``keep(word)`` accepts, with ``b``'s own compiled patterns."""
+    import dataclasses
+    sel = np.asarray([i for i, w in enumerate(b.words) if keep(w)], dtype=np.int64)
+    return dataclasses.replace(b, words=[b.words[i] for i in sel], word_pattern_index=b.word_pattern_index[sel],
+                               word_n_map=b.word_n_map[sel])
+
+
+def test_emulated_adjoint_with_fewer_pass_components_than_row_entries(emulated, monkeypatch):
+    """The nu <= 2 words of the n_max 8, l_max 3 set have passes of at most 64 components
+    against rows of 128 entries; the adjoint's back-propagation still stages a part per row
+    entry in the component region, which the kernels and the launch size as at least a row
+    wide.  General and symmetric passes, emulated, against the oracle."""
     import ctypes
-    import json
-    import sys
 
     import torch
+    from oracle import oracle
     from ye3t_b200 import _native
-    for name in ("y3b_ace_recoupled_energy_grad", "y3b_ace_recoupled_energy", "y3b_ace_recoupled_features",
-                 "y3b_ace_recoupled_energy_grad_symmetric", "y3b_ace_recoupled_energy_symmetric"):
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    b = _sub_bundle(_bundle("ace_n8_l3_nu3_L0"), lambda w: len(w) <= 2)
+    plan = build_recoupled_plan(b)
+    gen, sym = plan.device_tables(), plan.sym_device_tables()
+    assert gen.max_pass_components < gen.row_width and sym.max_pass_components < sym.row_width
+    assert gen.smem_bytes() == 16 * 4 * gen.row_width
+    rng = np.random.default_rng(60)
+    A = _physical(rng, 5, 8, 3)
+    species = np.array([0, 1, 2, 1, 0], dtype=np.int32)
+    w = rng.normal(size=(3, b.feature_count))
+    e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=2)
+    for na, th in ((1, 256), (3, 512)):
+        e, G, _, _, st = _emulate(emulated, gen, A, species, plan.energy_weights(w), na, th)
+        assert st.tolist() == [0, 0, 0]
+        assert np.abs(e - e0).max() <= 1e-12 * np.abs(e0).max()
+        assert np.abs(G - G0).max() <= 1e-12 * np.abs(G0).max()
+    for name in ("y3b_ace_recoupled_energy_grad_symmetric", "y3b_ace_recoupled_energy_symmetric"):
         res, args = _native._SIGS[name]
         getattr(emulated, name).restype = res
         getattr(emulated, name).argtypes = args
@@ -528,53 +550,9 @@ def test_bench_probe_runs_on_emulated_passes(emulated, plan5, physical_case, mon
     monkeypatch.setattr(_native, "lib", lambda: emulated)
     monkeypatch.setattr(_native, "require_cuda", lambda *t, what="": torch.device("cpu"))
     monkeypatch.setattr(_native, "stream_of", lambda device: 0)
-
-    class Event:
-        def __init__(self, enable_timing=True):
-            pass
-
-        def record(self):
-            pass
-
-        def elapsed_time(self, other):
-            return 1.0
-
-    monkeypatch.setattr(torch.cuda, "Event", Event)
-    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
-    if REPO not in sys.path:
-        sys.path.insert(0, REPO)
-    import bench
-    b, plan = plan5
-    A, species, w, e0, G0 = physical_case
-    At, sp = torch.as_tensor(A), torch.as_tensor(species)
-    e0t, G0t = torch.as_tensor(e0), torch.as_tensor(G0)
-    Fref = G0t.real.reshape(A.shape[0], -1)[:, :3].contiguous()
-
-    class Evaluator:  # the term-level side of the probe, from the oracle
-        def neighbor_list(self, pos, box, begin, end):
-            return None, None
-
-        def density(self, pos, species, box, row, nbr, begin):
-            return At
-
-        def energy_grad(self, A, species):
-            return e0t, G0t
-
-        def energy_from_density(self, A, species):
-            return e0t
-
-        def edge_grad(self, pos, species, box, row, nbr, G, begin=0):
-            return G.real.reshape(G.shape[0], -1)[:, :3].contiguous()
-
-        def forces_from_edges(self, row, nbr, g):
-            return g
-
-    out = bench.recoupled_probe(torch, Evaluator(), b, w, "cpu", torch.zeros(A.shape[0], 3), sp, 30.0, True,
-                                5000.0, F_ref=Fref, E_ref=float(e0.sum()))
-    json.dumps(out, allow_nan=False)
-    assert "error" not in out and out["density_symmetric"] is True
-    assert len(out["shapes_atoms_x_threads"]) == 8
-    for shape in out["shapes_atoms_x_threads"].values():
-        assert shape["energy_max_rel_diff"] <= 1e-12 and shape["dEdA_max_rel_diff"] <= 1e-12
-    step = out["whole_step_with_fastest_shape"]
-    assert step["energy_rel_diff"] <= 1e-12 and step["forces_max_rel_diff"] <= 1e-12
+    ev = RecoupledEvaluator(b, "cpu", w, plan=plan, atoms_per_cta=2, threads_per_cta=256, symmetric=True)
+    st = torch.zeros(1, dtype=torch.int32)
+    e, G = ev.energy_grad(torch.as_tensor(A), torch.as_tensor(species), status=st)
+    assert int(st.item()) == 0
+    assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()

@@ -64,7 +64,8 @@ def test_noalloc_density_matches_workspace_entry_point_twice():
         ref = _with_workspace(lib, code, v, t, N)
         torch.cuda.synchronize()
         assert int(status.item()) == 0
-        np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), rtol=1e-12, atol=1e-12)
+        # both entry points run the same deterministic kernels on the same data
+        assert torch.equal(got, ref)
 
 
 def test_noalloc_density_rejects_problems_beyond_its_scratch():

@@ -9,13 +9,20 @@ Pipeline for the centres ``[begin, end)`` of a periodic cubic box:
    reference's radial table (``ye3t/runtime/execution_plan.py:7298``), complex
    harmonics (``:7479``), per-neighbour prefactor (``:7582``) and
    ``density_accumulate`` (``:7913``), fused;
-3. B-basis (kernel 2, ``y3b_ace_features`` / ``y3b_ace_energy``): the
-   symmetric blocks (``symmetric_power_product_plan_contraction``,
-   ``ye3t/runtime/symmetric_power.py:879``) formed on chip, then every word's
-   factorized schedule
+3. B-basis (kernel 2): every word's factorized schedule
    (``ACEFactorizedScheduleReport.evaluate``,
    ``ye3t/couplings/__init__.py:2574``) -- either written out as features or
    contracted with a per-species linear readout into per-atom energies.
+
+   For energies (and dE/dA) of a scalar bundle the default B-basis is the
+   recoupled plan (``ye3t_b200.recoupling``): each feature as contractions of
+   coupled channel pairs, evaluated by the recoupled passes, with the
+   ``M >= 0`` (symmetric) passes wherever A comes from this class's density
+   kernel (real radial functions and prefactors give
+   ``A[l, -m] = (-1)^m conj(A[l, m])``).  ``b_basis="term"`` selects the
+   term-level kernels (``y3b_ace_energy`` / ``y3b_ace_energy_grad``: the
+   symmetric blocks of ``ye3t/runtime/symmetric_power.py:879`` formed on chip,
+   then the schedule items), which also serve features and L > 0 bundles.
 """
 
 from __future__ import annotations
@@ -41,11 +48,17 @@ class ACEConfig:
 class ACEEvaluator:
     """Evaluates one :class:`ACEBundle` on one CUDA device."""
 
+    #: CTA shapes (atoms, threads) of the recoupled passes used by default
+    RECOUPLED_GRAD_SHAPE = (2, 256)
+    RECOUPLED_ENERGY_SHAPE = (1, 256)
+
     def __init__(self, bundle: ACEBundle, device, *, config: ACEConfig = ACEConfig(),
-                 species_prefactor=None, weights=None):
+                 species_prefactor=None, weights=None, b_basis: str = "recoupled"):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("ACEEvaluator runs on CUDA devices only")
+        if b_basis not in ("recoupled", "term"):
+            raise ValueError('b_basis must be "recoupled" or "term"')
         nat.lib()
         self.bundle = bundle
         self.config = config
@@ -58,6 +71,25 @@ class ACEEvaluator:
             weights, dtype=torch.float64, device=self.device).contiguous()
         if self.weights is not None and self.weights.shape[-1] != self.packed.feature_count:
             raise ValueError(f"weights need {self.packed.feature_count} features per species")
+        # energies and dE/dA of scalar bundles go through the recoupled passes
+        # unless the term-level kernels are asked for
+        self.b_basis = b_basis if bundle.target_L == 0 else "term"
+        self._recoupled = {}
+
+    def recoupled(self, symmetric: bool, grad: bool):
+        """The :class:`~ye3t_b200.recoupling.RecoupledEvaluator` used for energies (``grad``
+        False) or energies and dE/dA, built on first use (the plan is fitted once)."""
+        key = (bool(symmetric), bool(grad))
+        if key not in self._recoupled:
+            from .recoupling import RecoupledEvaluator, build_recoupled_plan
+            if self.weights is None:
+                raise ValueError("weights are required for the energy")
+            plan = next((r.plan for r in self._recoupled.values()), None) or build_recoupled_plan(self.bundle)
+            na, th = self.RECOUPLED_GRAD_SHAPE if grad else self.RECOUPLED_ENERGY_SHAPE
+            self._recoupled[key] = RecoupledEvaluator(self.bundle, self.device, self.weights.cpu().numpy(),
+                                                      plan=plan, atoms_per_cta=na, threads_per_cta=th,
+                                                      symmetric=symmetric)
+        return self._recoupled[key]
 
     @property
     def feature_count(self) -> int:
@@ -158,13 +190,23 @@ class ACEEvaluator:
         return out.reshape(n, C * self.packed.feature_count)
 
     def energy_from_density(self, A: torch.Tensor, species_centres: torch.Tensor,
-                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Per-atom energies ``sum_f w[z, f] Re(B_f)`` from the A-basis (B never stored)."""
+                            out: Optional[torch.Tensor] = None, physical: bool = False) -> torch.Tensor:
+        """Per-atom energies ``sum_f w[z, f] Re(B_f)`` from the A-basis (B never stored).
+
+        ``physical=True`` declares that A has the symmetry of a physical density
+        (as ``density`` gives), which lets the recoupled B-basis use its
+        ``M >= 0`` passes; any other A takes the general passes."""
         if self.weights is None:
             raise ValueError("weights are required for the energy")
         A = A.to(self.device, torch.complex128).contiguous()
         n = A.shape[0]
         sp = species_centres.to(self.device, torch.int32).contiguous()
+        if self.b_basis == "recoupled":
+            e = self.recoupled(physical, False).energy(A, sp, check_symmetry=False)
+            if out is not None:
+                out.copy_(e)
+                return out
+            return e
         if out is None:
             out = torch.empty(n, dtype=torch.float64, device=self.device)
         nat.check(nat.lib().y3b_ace_energy(ctypes_ref(self._tables), A.data_ptr(), n, sp.data_ptr(),
@@ -173,13 +215,18 @@ class ACEEvaluator:
         return out
 
     # -- force path ------------------------------------------------------------------
-    def energy_grad(self, A: torch.Tensor, species_centres: torch.Tensor, status: Optional[torch.Tensor] = None):
-        """(per-atom energies, G = dE/dA) from the A-basis (B is holomorphic in A: dE = Re(sum G dA))."""
+    def energy_grad(self, A: torch.Tensor, species_centres: torch.Tensor, status: Optional[torch.Tensor] = None,
+                    physical: bool = False):
+        """(per-atom energies, G = dE/dA) from the A-basis (B is holomorphic in A: dE = Re(sum G dA)).
+
+        ``physical`` as in ``energy_from_density``."""
         if self.weights is None:
             raise ValueError("weights are required for the energy")
         A = A.to(self.device, torch.complex128).contiguous()
         n = A.shape[0]
         sp = species_centres.to(self.device, torch.int32).contiguous()
+        if self.b_basis == "recoupled":
+            return self.recoupled(physical, True).energy_grad(A, sp, status=status, check_symmetry=False)
         e = torch.empty(n, dtype=torch.float64, device=self.device)
         G = torch.empty_like(A)
         nat.check(nat.lib().y3b_ace_energy_grad(ctypes_ref(self._tables), A.data_ptr(), n, sp.data_ptr(),
@@ -226,7 +273,7 @@ class ACEEvaluator:
         """(total energy, forces [N, 3]) of the whole system on this device."""
         row, nbr = self.neighbor_list(positions, box)
         A = self.density(positions, species, box, row, nbr)
-        e, G = self.energy_grad(A, species.to(self.device, torch.int32))
+        e, G = self.energy_grad(A, species.to(self.device, torch.int32), physical=True)
         g = self.edge_grad(positions, species, box, row, nbr, G)
         return e.sum(), self.forces_from_edges(row, nbr, g)
 
@@ -238,7 +285,7 @@ class ACEEvaluator:
         row, nbr = self.neighbor_list(positions, box, begin, end)
         A = self.density(positions, species, box, row, nbr, begin)
         sp = species.to(self.device, torch.int32)[begin:end]
-        return self.energy_from_density(A, sp)
+        return self.energy_from_density(A, sp, physical=True)
 
 
 def ctypes_ref(tables):

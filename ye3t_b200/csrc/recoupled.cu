@@ -60,6 +60,13 @@ int launch_shape(const T& t, int& na, int& th) {
   return Y3B_OK;
 }
 
+// Dynamic shared memory per atom of the adjoint passes: the A row and its
+// adjoint, and two component regions that also hold step 3's W parts.
+size_t grad_smem_per_atom(int64_t row_width, int64_t max_pass_components) {
+  const int64_t cw = std::max(row_width, max_pass_components);
+  return size_t(2 * row_width + 2 * cw) * sizeof(double2);
+}
+
 template <typename Kernel, typename Tabs>
 int launch_grouped(Kernel kernel, int threads, size_t smem_per_atom, int na, int64_t atom_count, cudaStream_t s,
                    const Tabs& rt, const void* A, const int32_t* species, const double* weights,
@@ -141,7 +148,7 @@ extern "C" int y3b_ace_recoupled_energy_grad(const y3b_recoupled_tables* tables,
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && contraction_weights && energy && dEdA && species_count > 0,
                 "null pointer argument");
-  const size_t per_atom = size_t(2 * int64_t(t.row_width) + 2 * int64_t(t.max_pass_components)) * sizeof(double2);
+  const size_t per_atom = grad_smem_per_atom(t.row_width, t.max_pass_components);
   const RecTabs rt = device_view(t);
   cudaStream_t s = as_stream(stream);
 #define Y3B_GRAD(N, T) recoupled_energy_grad_kernel<N, T>
@@ -183,7 +190,7 @@ extern "C" int y3b_ace_recoupled_energy_grad_symmetric(const y3b_recoupled_sym_t
   if (atom_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(A && species && contraction_weights && energy && dEdA && species_count > 0,
                 "null pointer argument");
-  const size_t per_atom = size_t(2 * int64_t(t.row_width) + 2 * int64_t(t.max_pass_components)) * sizeof(double2);
+  const size_t per_atom = grad_smem_per_atom(t.row_width, t.max_pass_components);
   const SymTabs rt = sym_view(t);
   cudaStream_t s = as_stream(stream);
 #define Y3B_SGRAD(N, T) recoupled_sym_energy_grad_kernel<N, T>

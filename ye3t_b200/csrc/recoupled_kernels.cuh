@@ -173,10 +173,12 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
   __shared__ double red[TH / 32];
   const int W = t.row_width;
   const int maxc = t.max_pass_components;
+  // the component regions also stage step 3's parts (at least W entries per atom)
+  const int cw = maxc > W ? maxc : W;
   double2* sA = rec_smem;          // [W][NA] the atoms' A rows
   double2* sGA = sA + W * NA;      // [W][NA] dE/dA of the rows
-  double2* sI = sGA + W * NA;      // [maxc][NA] components of the pass
-  double2* sG = sI + maxc * NA;    // [maxc][NA] their adjoints
+  double2* sI = sGA + W * NA;      // [cw][NA] components of the pass
+  double2* sG = sI + cw * NA;      // [cw][NA] their adjoints
   const int tid = threadIdx.x;
   const int64_t groups = (atom_count + NA - 1) / NA;
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
@@ -241,7 +243,7 @@ recoupled_energy_grad_kernel(RecTabs t, const double2* __restrict__ A, int64_t a
       //    parts when the block has at least two threads per entry (P threads per
       //    entry); the partial sums go to the component buffer, which step 2 no
       //    longer needs, and are added to the entry in part order.
-      const int P = (2 * W <= TH && (TH / W) * W <= maxc) ? TH / W : 1;  // uniform
+      const int P = (2 * W <= TH && (TH / W) * W <= cw) ? TH / W : 1;  // uniform
       double2* part = sI;  // [P][W][NA]
       for (int u = tid; u < W * P; u += TH) {
         const int i = u % W, pi = u / W;
@@ -421,10 +423,11 @@ recoupled_sym_energy_grad_kernel(SymTabs t, const double2* __restrict__ A, int64
   __shared__ double red[TH / 32];
   const int W = t.row_width;
   const int maxc = t.max_pass_components;
+  const int cw = maxc > W ? maxc : W;  // the component regions also stage step 3's parts
   double2* sA = rec_smem;
   double2* sGA = sA + W * NA;
   double2* sI = sGA + W * NA;
-  double2* sG = sI + maxc * NA;
+  double2* sG = sI + cw * NA;
   const int tid = threadIdx.x;
   const int64_t groups = (atom_count + NA - 1) / NA;
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
@@ -481,7 +484,7 @@ recoupled_sym_energy_grad_kernel(SymTabs t, const double2* __restrict__ A, int64
         }
       }
       __syncthreads();
-      const int P = (2 * W <= TH && (TH / W) * W <= maxc) ? TH / W : 1;  // uniform
+      const int P = (2 * W <= TH && (TH / W) * W <= cw) ? TH / W : 1;  // uniform
       double2* part = sI;  // [P][W][NA]; step 2 is done with sI
       for (int u = tid; u < W * P; u += TH) {
         const int i = u % W, pi = u / W;

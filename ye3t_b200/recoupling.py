@@ -389,9 +389,10 @@ class RecoupledDeviceTables:
                 "features": 10 * terms + 8 * macs + 4 * float(self.feat_index.shape[0])}
 
     def smem_bytes(self) -> int:
-        """Dynamic shared memory of the device pass: the A row and its adjoint, the pass's
-        components and theirs."""
-        return 16 * (2 * self.row_width + 2 * self.max_pass_components)
+        """Dynamic shared memory per atom of the adjoint pass: the A row and its adjoint, the
+        pass's components and theirs (each region at least a row wide, since the
+        back-propagation step stages its per-entry parts there)."""
+        return 16 * (2 * self.row_width + 2 * max(self.row_width, self.max_pass_components))
 
 
 def _device_tables(plan: "RecoupledPlan") -> RecoupledDeviceTables:
@@ -560,9 +561,10 @@ class RecoupledSymTables:
             raise ValueError("contraction segment outside its pass")
 
     def smem_bytes(self) -> int:
-        """Dynamic shared memory per atom: the A row and its adjoint, the pass's components
-        and theirs."""
-        return 16 * (2 * self.row_width + 2 * self.max_pass_components)
+        """Dynamic shared memory per atom of the adjoint pass: the A row and its adjoint, the
+        pass's components and theirs (each region at least a row wide, since the
+        back-propagation step stages its per-entry parts there)."""
+        return 16 * (2 * self.row_width + 2 * max(self.row_width, self.max_pass_components))
 
     def flops_per_atom(self) -> Dict[str, float]:
         """Real flops per atom of the symmetric passes, counted as
@@ -862,13 +864,18 @@ class RecoupledEvaluator:
             raise ValueError("one species per atom is required")
         return sp
 
-    def energy_grad(self, A, species, status=None):
-        """(per-atom energies, ``G = dE/dA``)."""
+    def energy_grad(self, A, species, status=None, check_symmetry: bool = True):
+        """(per-atom energies, ``G = dE/dA``).  With ``symmetric`` passes the density's
+        symmetry is checked first (``check_symmetry``, one pass over A and a host sync)
+        unless ``check_symmetry=False``; a caller whose A comes from a physical density
+        kernel (real radial functions and prefactors) may skip it."""
         import ctypes
 
         import torch
         from . import _native as nat
         A = self._rows(A)
+        if self.symmetric and check_symmetry:
+            self.check_symmetry(A)
         n = A.shape[0]
         sp = self._species(species, n)
         e = torch.empty(n, dtype=torch.float64, device=self.device)
@@ -879,13 +886,15 @@ class RecoupledEvaluator:
             e.data_ptr(), G.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), name)
         return e, G
 
-    def energy(self, A, species, status=None):
-        """Per-atom energies."""
+    def energy(self, A, species, status=None, check_symmetry: bool = True):
+        """Per-atom energies (the symmetry check as in ``energy_grad``)."""
         import ctypes
 
         import torch
         from . import _native as nat
         A = self._rows(A)
+        if self.symmetric and check_symmetry:
+            self.check_symmetry(A)
         n = A.shape[0]
         sp = self._species(species, n)
         e = torch.empty(n, dtype=torch.float64, device=self.device)
