@@ -496,6 +496,38 @@ int y3b_ace_recoupled_energy_symmetric(const y3b_recoupled_sym_tables* tables, c
                                        const int32_t* species, const double* contraction_weights,
                                        int64_t species_count, double* energy, int32_t* status, void* stream);
 
+/* The symmetric adjoint with the components' adjoints formed from dense tiles
+ * of the contraction weights (ye3t_b200.recoupling.RecoupledTiles): per pass,
+ * J[s] = sum_s' K[z][s, s'] I[s'] with K[z] symmetric, walked as tiles of
+ * `rows` segments by the union of their columns, so that each shared-memory
+ * read of a column component serves every row of the tile.  The same results
+ * as y3b_ace_recoupled_energy_grad_symmetric (replaces the same reference
+ * path: the autograd of ye3t/core/couplings.py:552-567 through the factorized
+ * schedules), with the tile weights kval [species_count, rows * step_count]
+ * (RecoupledTiles.tile_weights of the contraction weights) in place of the
+ * contraction weights.  A CTA holds 32 / rows atoms (rows 8 or 16) and
+ * threads_per_cta (256 or 512) threads; atoms_per_cta of `tables` is ignored.
+ * atom_order (nullable) gives the order in which atoms are grouped into CTAs
+ * (a species-sorted order lets a CTA's atoms share one species' weights);
+ * energy and dEdA are indexed by atom either way. */
+typedef struct {
+  int32_t rows;              /* segments per tile: 8 or 16 */
+  int32_t pass_count;        /* equal to the symmetric tables' */
+  int64_t tile_count;
+  int64_t step_count;
+  const int32_t* tile_begin;     /* [pass_count + 1] */
+  const int32_t* tile_row;       /* [tile_count, rows]: local component of the row's M = 0, or -1 */
+  const int32_t* tile_col_begin; /* [tile_count + 1], multiples of 4 */
+  const int32_t* col_comp;       /* [step_count], 16-byte aligned */
+  const double* kval;            /* [species_count, rows * step_count], 16-byte aligned */
+} y3b_recoupled_tile_tables;
+
+int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_tables* tables,
+                                        const y3b_recoupled_tile_tables* tiles, const void* A,
+                                        int64_t atom_count, const int32_t* atom_order, const int32_t* species,
+                                        int64_t species_count, double* energy, void* dEdA, int32_t* status,
+                                        void* stream);
+
 /* Forces F_k = -dE/dr_k = sum_{e in row k} (g_e - g_rev(e)) from the rows of
  * all atoms (deterministic gather; rev(e) is the reverse edge). */
 int y3b_forces_gather(const int64_t* row_offsets, const int32_t* neighbors, int64_t atom_count,

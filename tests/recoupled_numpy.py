@@ -212,6 +212,60 @@ def walk_sym_tables(tabs, A, species, k):
     return e, G.reshape(A.shape)
 
 
+def walk_sym_tiled(tabs, tiles, A, species, k):
+    """The symmetric pass with the adjoints of the components formed by the dense tiles
+    (``RecoupledTiles``) instead of the contraction lists, restated as the tiled kernel walks
+    them: per tile and row, the sum over the tile's columns of the row's weight times the
+    column's components; the rest as ``walk_sym_tables``.  Returns (energies, G)."""
+    N = A.shape[0]
+    W = tabs.row_width
+    row = A.reshape(N, W)
+    kval = tiles.tile_weights(k)[np.asarray(species)]  # [N, rows * steps]
+    R = tiles.rows
+    G = np.zeros((N, W), dtype=np.complex128)
+    e = np.zeros(N)
+    for L in range(tabs.pass_count):
+        c0, c1 = int(tabs.pass_begin[L]), int(tabs.pass_begin[L + 1])
+        I = np.zeros((N, c1 - c0), dtype=np.complex128)
+        for c in range(c0, c1):
+            a, b, q0, qn = (int(v) for v in tabs.comp[c, :4])
+            if a < 0:
+                I[:, c - c0] = 1.0
+            elif qn == 0:
+                I[:, c - c0] = row[:, a]
+            else:
+                q = tabs.cg_index[q0:q0 + qn]
+                I[:, c - c0] = (tabs.cg_value[q0:q0 + qn] * row[:, a + (q & 255)] * row[:, b + (q >> 8)]).sum(axis=1)
+        gI = np.zeros_like(I)
+        for t in range(int(tiles.tile_begin[L]), int(tiles.tile_begin[L + 1])):
+            q0, q1 = int(tiles.tile_col_begin[t]), int(tiles.tile_col_begin[t + 1])
+            cols = tiles.col_comp[q0:q1]
+            for r in range(R):
+                rc = int(tiles.tile_row[t, r])
+                if rc < 0:
+                    continue
+                kv = kval[:, R * q0 + r * (q1 - q0): R * q0 + (r + 1) * (q1 - q0)]  # [N, steps]
+                sgn = int(tabs.comp[c0 + rc, 7])
+                for M in range(L + 1):
+                    acc = (kv * I[:, cols + M]).sum(axis=1)
+                    gI[:, rc + M] = sgn * np.conj(acc)
+                    e += (0.5 if M == 0 else 1.0) * (I[:, rc + M] * gI[:, rc + M]).real
+        for t in range(W):
+            b0, b1 = int(tabs.bp_begin[L * W + t]), int(tabs.bp_begin[L * W + t + 1])
+            if b1 == b0:
+                continue
+            code, other, val = tabs.bp_gi[b0:b1], tabs.bp_other[b0:b1], tabs.bp_value[b0:b1]
+            g = gI[:, code >> 1]
+            g = np.where((code & 1)[None, :] == 1, np.conj(g), g)
+            partner = np.where(other[None, :] < 0, 1.0, row[:, np.maximum(other, 0)])
+            G[:, t] += (val * g * partner).sum(axis=1)
+    for t in range(W):
+        m = int(tabs.mirror[t])
+        if m >= 0:
+            G[:, t] = (-1.0 if m & 1 else 1.0) * np.conj(G[:, m >> 1])
+    return e, G.reshape(A.shape)
+
+
 def walk_sym_forward(tabs, A, species, k):
     """The symmetric forward energy: ``T_d = (-1)^p_B (Re(I_A[0] conj(I_B[0])) +
     2 sum_{M > 0} Re(I_A[M] conj(I_B[M])))``, ``e = sum_d k[z, d] T_d``."""

@@ -556,3 +556,24 @@ def test_emulated_adjoint_with_fewer_pass_components_than_row_entries(emulated, 
     assert int(st.item()) == 0
     assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
     assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()
+
+
+@pytest.mark.parametrize("rows", [8, 16])
+def test_symmetric_tiles_walk_matches_oracle(plan5, physical_case, rows):
+    """The contraction lists regrouped as dense tiles of 8 or 16 segments (every contraction
+    lands in exactly two tile entries, or twice in one on the diagonal): the tiled walk gives
+    the oracle's energies and dE/dA on the reference's densities, and the tiles keep most of
+    their entries nonzero."""
+    from ye3t_b200.recoupling import TILE_STEP
+    b, plan = plan5
+    tabs = plan.sym_device_tables()
+    tiles = plan.sym_tiles(rows)
+    assert tiles.efficiency() > (0.8 if rows == 8 else 0.65)
+    assert np.all(np.diff(tiles.tile_col_begin) % TILE_STEP == 0)
+    A, species, w, e0, G0 = physical_case
+    k = plan.energy_weights(w)
+    kv = tiles.tile_weights(k)
+    assert np.isclose(kv.sum(), 2 * k.sum())
+    e1, G1 = rn.walk_sym_tiled(tabs, tiles, A, species, k)
+    assert np.abs(e1 - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G1 - G0).max() <= 1e-12 * np.abs(G0).max()

@@ -77,6 +77,15 @@ class RecoupledSymTables(ctypes.Structure):
     ]
 
 
+class RecoupledTileTables(ctypes.Structure):
+    """``y3b_recoupled_tile_tables`` (include/ye3t_b200.h)."""
+
+    _fields_ = [
+        ("rows", I32), ("pass_count", I32), ("tile_count", I64), ("step_count", I64),
+        ("tile_begin", VP), ("tile_row", VP), ("tile_col_begin", VP), ("col_comp", VP), ("kval", VP),
+    ]
+
+
 _SIGS = {
     "y3b_abi_version": (I32, []),
     "y3b_last_error": (ctypes.c_char_p, []),
@@ -124,6 +133,9 @@ _SIGS = {
                                                                VP, I64, VP, VP, VP, VP]),
     "y3b_ace_recoupled_energy_symmetric": (ctypes.c_int, [ctypes.POINTER(RecoupledSymTables), VP, I64, VP, VP,
                                                           I64, VP, VP, VP]),
+    "y3b_ace_recoupled_energy_grad_tiled": (ctypes.c_int, [ctypes.POINTER(RecoupledSymTables),
+                                                           ctypes.POINTER(RecoupledTileTables), VP, I64, VP, VP,
+                                                           I64, VP, VP, VP, VP]),
     "y3b_ace_edge_grad": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                          VP, VP]),
     "y3b_forces_gather": (ctypes.c_int, [VP, VP, I64, VP, VP, VP, VP]),

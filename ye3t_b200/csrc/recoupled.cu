@@ -218,3 +218,64 @@ extern "C" int y3b_ace_recoupled_energy_symmetric(const y3b_recoupled_sym_tables
                    energy, nullptr, status)
 #undef Y3B_SENER
 }
+
+namespace {
+
+int check_tile_tables(const y3b_recoupled_sym_tables& t, const y3b_recoupled_tile_tables* tiles) {
+  Y3B_CHECK_ARG(tiles != nullptr, "null tile tables");
+  const y3b_recoupled_tile_tables& u = *tiles;
+  Y3B_CHECK_ARG(u.rows == 8 || u.rows == 16, "tile rows must be 8 or 16");
+  Y3B_CHECK_ARG(u.pass_count == t.pass_count, "tile tables cover %d passes, the symmetric tables %d", u.pass_count,
+                t.pass_count);
+  Y3B_CHECK_ARG(t.pass_count <= kTiledMaxLM1, "the tiled pass covers intermediate L up to %d", kTiledMaxLM1 - 1);
+  Y3B_CHECK_ARG(u.tile_count >= 0 && u.step_count >= 0, "negative tile table sizes");
+  Y3B_CHECK_ARG(u.tile_begin && u.tile_row && u.tile_col_begin && (u.step_count == 0 || (u.col_comp && u.kval)),
+                "null tile table pointer");
+  Y3B_CHECK_ARG(reinterpret_cast<uintptr_t>(u.col_comp) % 16 == 0 && reinterpret_cast<uintptr_t>(u.kval) % 16 == 0,
+                "col_comp and kval must be 16-byte aligned");
+  return Y3B_OK;
+}
+
+}  // namespace
+
+extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_tables* tables,
+                                                   const y3b_recoupled_tile_tables* tiles, const void* A,
+                                                   int64_t atom_count, const int32_t* atom_order,
+                                                   const int32_t* species, int64_t species_count, double* energy,
+                                                   void* dEdA, int32_t* status, void* stream) {
+  if (int rc = check_sym_tables(tables)) return rc;
+  const y3b_recoupled_sym_tables& t = *tables;
+  if (int rc = check_tile_tables(t, tiles)) return rc;
+  const int th = t.threads_per_cta == 0 ? 256 : t.threads_per_cta;
+  Y3B_CHECK_ARG(th == 256 || th == 512, "threads_per_cta must be 0 (256), 256 or 512");
+  Y3B_CHECK_ARG(atom_count >= 0, "negative atom count");
+  if (atom_count == 0) return Y3B_OK;
+  Y3B_CHECK_ARG(A && species && energy && dEdA && species_count > 0, "null pointer argument");
+  const int na = 32 / tiles->rows;
+  const size_t per_atom = grad_smem_per_atom(t.row_width, t.max_pass_components);
+  const SymTabs rt = sym_view(t);
+  const TileTabs tt = tile_view(*tiles);
+  const size_t smem = per_atom * size_t(na);
+  Y3B_CHECK_ARG(smem <= 224 * 1024,
+                "tiled recoupled pass needs %lld bytes of shared memory for %d atoms per CTA (max 224 KB)",
+                (long long)smem, na);
+  const int64_t groups = (atom_count + na - 1) / na;
+  const int64_t grid = std::min<int64_t>(groups, int64_t(kSMs) * 64);
+  cudaStream_t s = as_stream(stream);
+  const double2* Ad = static_cast<const double2*>(A);
+  double2* Gd = static_cast<double2*>(dEdA);
+#define Y3B_TILED_LAUNCH(NA, TH)                                                                         \
+  {                                                                                                      \
+    auto kernel = recoupled_sym_tiled_grad_kernel<NA, TH>;                                               \
+    Y3B_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));  \
+    kernel<<<int(grid), TH, smem, s>>>(rt, tt, Ad, atom_count, atom_order, species, species_count, energy, \
+                                       Gd, status);                                                      \
+    Y3B_LAUNCH_CHECK();                                                                                  \
+    return Y3B_OK;                                                                                       \
+  }
+  if (na == 4 && th == 256) Y3B_TILED_LAUNCH(4, 256)
+  if (na == 4 && th == 512) Y3B_TILED_LAUNCH(4, 512)
+  if (na == 2 && th == 256) Y3B_TILED_LAUNCH(2, 256)
+  Y3B_TILED_LAUNCH(2, 512)
+#undef Y3B_TILED_LAUNCH
+}

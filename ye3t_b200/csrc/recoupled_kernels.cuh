@@ -630,5 +630,254 @@ recoupled_sym_energy_kernel(SymTabs t, const double2* __restrict__ A, int64_t at
   }
 }
 
+// Dense tiles of the symmetric pass's contraction weights (RecoupledTiles).
+struct TileTabs {
+  int32_t rows, pass_count;
+  int64_t tile_count, step_count;
+  const int32_t* tile_begin;
+  const int32_t* tile_row;
+  const int32_t* tile_col_begin;
+  const int32_t* col_comp;
+  const double* kval;
+};
+
+inline TileTabs tile_view(const y3b_recoupled_tile_tables& t) {
+  return TileTabs{t.rows, t.pass_count, t.tile_count, t.step_count, t.tile_begin, t.tile_row, t.tile_col_begin,
+                  t.col_comp, t.kval};
+}
+
+// Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1: the warp's
+// tiles in a snake order over the warps (tiles are sorted by decreasing column
+// count); lane (r, a) walks its tile's columns four at a time and forms
+// acc[M] = sum_q K[z_a][row r, column q] I[column q + M] for its atom a, then
+// writes gI = (-1)^p conj(acc) and adds its energy share
+// w_M Re(I gI) (w_0 = 1/2).  A column or row outside the pass is skipped and
+// sets bad.
+template <int LM1, int NA, int TH>
+__device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileTabs& tt, int L, int c0, int nc,
+                                                   const double2* sI, double2* sG, const double* kz, double& ep,
+                                                   bool& bad) {
+  constexpr int R = 32 / NA;
+  constexpr int NW = TH / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r = lane / NA, a = lane % NA;
+  const int t0 = tt.tile_begin[L], t1 = tt.tile_begin[L + 1];
+  if (t0 < 0 || t1 < t0 || int64_t(t1) > tt.tile_count) {
+    bad = true;
+    return;
+  }
+  const int ntiles = t1 - t0;
+  for (int k = 0;; ++k) {
+    const int i = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;
+    if (i >= ntiles) break;
+    const int tile = t0 + i;
+    const int rowc = tt.tile_row[int64_t(tile) * R + r];
+    const int q0 = tt.tile_col_begin[tile], q1 = tt.tile_col_begin[tile + 1];
+    const int n = q1 - q0;
+    if (q0 < 0 || n < 0 || (n & 3) || (q0 & 3) || int64_t(q1) > tt.step_count) {
+      bad = true;
+      continue;  // uniform over the warp
+    }
+    const double* kr = kz + int64_t(R) * q0 + int64_t(r) * n;
+    double2 acc[LM1];
+#pragma unroll
+    for (int M = 0; M < LM1; ++M) acc[M] = make_double2(0.0, 0.0);
+    for (int q = 0; q < n; q += 4) {
+      const int4 c4 = __ldg(reinterpret_cast<const int4*>(tt.col_comp + q0 + q));
+      const double2 k01 = __ldg(reinterpret_cast<const double2*>(kr + q));
+      const double2 k23 = __ldg(reinterpret_cast<const double2*>(kr + q + 2));
+      const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
+      const double ks[4] = {k01.x, k01.y, k23.x, k23.y};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        int c = cs[j];
+        double kv = ks[j];
+        if (c < 0 || c + LM1 > nc) {  // uniform over the warp
+          bad = true;
+          c = 0;
+          kv = 0.0;
+        }
+#pragma unroll
+        for (int M = 0; M < LM1; ++M) {
+          const double2 v = sI[(c + M) * NA + a];
+          acc[M].x = fma(kv, v.x, acc[M].x);
+          acc[M].y = fma(kv, v.y, acc[M].y);
+        }
+      }
+    }
+    if (rowc < -1 || rowc + LM1 > nc) {
+      bad = true;
+    } else if (rowc >= 0) {
+      const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
+#pragma unroll
+      for (int M = 0; M < LM1; ++M) {
+        const double2 g = make_double2(sg * acc[M].x, -sg * acc[M].y);
+        sG[(rowc + M) * NA + a] = g;
+        const double2 iv = sI[(rowc + M) * NA + a];
+        ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
+      }
+    }
+  }
+}
+
+// Largest intermediate L + 1 the tiled kernel is instantiated for (l_max 4).
+constexpr int kTiledMaxLM1 = 9;
+
+// Symmetric adjoint with tiled step 2 (see y3b_ace_recoupled_energy_grad_tiled):
+// a CTA holds NA = 32 / rows atoms, taken from atom_order when given; steps 1
+// and 3 and the mirror are those of recoupled_sym_energy_grad_kernel.  Energies
+// are summed per atom over the lanes of that atom in a fixed order.
+template <int NA, int TH>
+__global__ void __launch_bounds__(TH, 1)
+recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restrict__ A, int64_t atom_count,
+                                const int32_t* __restrict__ order, const int32_t* __restrict__ species,
+                                int64_t species_count, double* __restrict__ energy, double2* __restrict__ G,
+                                int32_t* status) {
+  Y3B_DYNAMIC_SMEM(double2, rec_smem);
+  __shared__ double red[TH / 32][NA];
+  const int W = t.row_width;
+  const int maxc = t.max_pass_components;
+  const int cw = maxc > W ? maxc : W;
+  double2* sA = rec_smem;
+  double2* sGA = sA + W * NA;
+  double2* sI = sGA + W * NA;
+  double2* sG = sI + cw * NA;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, a_lane = lane % NA;
+  const int64_t groups = (atom_count + NA - 1) / NA;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t first = grp * NA;
+    const int nv = int(atom_count - first < NA ? atom_count - first : NA);
+    int64_t idx[NA];  // the CTA's atoms (a partial group repeats its first atom, never written)
+    int64_t mine = first;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      int64_t v = first + (a < nv ? a : 0);
+      if (order != nullptr) {
+        const int64_t o = order[v];
+        if (o < 0 || o >= atom_count) {
+          if (tid == 0 && status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        } else {
+          v = o;
+        }
+      }
+      idx[a] = v;
+      if (a == a_lane) mine = v;
+    }
+    int z = species[mine];
+    if (z < 0 || z >= species_count) {
+      if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+      z = 0;
+    }
+    const double* kz = tt.kval + int64_t(z) * int64_t(tt.rows) * tt.step_count;
+    for (int i = tid; i < W * NA; i += TH) {
+      const int a = i % NA, e = i / NA;
+      sA[i] = a < nv ? A[idx[a] * W + e] : make_double2(0.0, 0.0);
+      sGA[i] = make_double2(0.0, 0.0);
+    }
+    double ep = 0.0;
+    bool bad = false;
+    __syncthreads();
+    for (int L = 0; L < t.pass_count; ++L) {
+      const int c0 = t.pass_begin[L];
+      const int nc = t.pass_begin[L + 1] - c0;
+      if (c0 < 0 || nc < 0 || nc > maxc || int64_t(c0) + nc > t.component_count || L >= kTiledMaxLM1) {
+        bad = true;  // uniform over the block
+        continue;
+      }
+      build_components<NA, TH>(t, sA, sI, c0, nc, W, bad);
+      __syncthreads();
+      switch (L) {
+        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+      }
+      __syncthreads();
+      const int P = (2 * W <= TH && (TH / W) * W <= cw) ? TH / W : 1;  // uniform
+      double2* part = sI;  // [P][W][NA]; step 2 is done with sI
+      for (int u = tid; u < W * P; u += TH) {
+        const int i = u % W, pi = u / W;
+        const int64_t at = int64_t(L) * W + i;
+        const int b0 = t.bp_begin[at], b1 = t.bp_begin[at + 1];
+        double2 ga[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) ga[a] = make_double2(0.0, 0.0);
+        if (b0 < 0 || b1 < b0 || int64_t(b1) > t.bp_count) {
+          bad = true;
+        } else {
+          const int len = b1 - b0;
+          const int q0 = b0 + (len * pi) / P, q1 = b0 + (len * (pi + 1)) / P;
+          for (int q = q0; q < q1; ++q) {
+            const int code = __ldg(t.bp_gi + q);
+            const int gi = code >> 1;
+            const int o = __ldg(t.bp_other + q);
+            if (code < 0 || gi >= nc || o >= W) {
+              bad = true;
+              continue;
+            }
+            const double cv = __ldg(t.bp_value + q);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+              double2 g = sG[gi * NA + a];
+              if (code & 1) g.y = -g.y;
+              const double2 term = o < 0 ? g : rmul(g, sA[o * NA + a]);
+              ga[a].x = fma(cv, term.x, ga[a].x);
+              ga[a].y = fma(cv, term.y, ga[a].y);
+            }
+          }
+        }
+#pragma unroll
+        for (int a = 0; a < NA; ++a) part[(pi * W + i) * NA + a] = ga[a];
+      }
+      __syncthreads();
+      for (int u = tid; u < W * NA; u += TH) {
+        double2 acc = sGA[u];
+        for (int pi = 0; pi < P; ++pi) {
+          const double2 v = part[pi * W * NA + u];
+          acc.x += v.x;
+          acc.y += v.y;
+        }
+        sGA[u] = acc;
+      }
+      __syncthreads();
+    }
+    for (int u = tid; u < W * NA; u += TH) {
+      const int i = u / NA, a = u % NA;
+      const int mi = __ldg(t.mirror + i);
+      if (mi < 0) continue;
+      const int src = mi >> 1;
+      if (src >= W) {
+        bad = true;
+        continue;
+      }
+      const double2 v = sGA[src * NA + a];
+      const double sg = (mi & 1) ? -1.0 : 1.0;
+      sGA[u] = make_double2(sg * v.x, -sg * v.y);
+    }
+    // per-atom energy: lanes of one atom are NA apart; shuffle down to lanes
+    // 0..NA-1, then the warps in order
+    for (int o = 16; o >= NA; o >>= 1) ep += __shfl_xor_sync(0xffffffffu, ep, o);
+    if (lane < NA) red[tid >> 5][lane] = ep;
+    __syncthreads();
+    if (bad && status) atomicOr(status, Y3B_STATUS_TABLE);
+    for (int i = tid; i < W * NA; i += TH) {
+      const int a = i % NA, e = i / NA;
+      if (a < nv) G[idx[a] * W + e] = sGA[i];
+    }
+    if (tid < nv) {
+      double total = 0.0;
+      for (int w = 0; w < TH / 32; ++w) total += red[w][tid];
+      energy[idx[tid]] = total;
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
 }  // namespace y3b

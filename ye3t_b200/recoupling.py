@@ -49,6 +49,7 @@ import numpy as np
 from .schedules import ACEBundle, ScheduleRecord, SymPowerTable
 
 __all__ = ["clebsch_gordan", "cg_table", "RecoupledPlan", "RecoupledDeviceTables", "RecoupledSymTables",
+           "RecoupledTiles", "TILE_STEP",
            "RecoupledEvaluator",
            "build_recoupled_plan", "ctypes_tables", "ctypes_sym_tables", "SEG_UNIT", "SEG_CHANNEL", "SEG_PAIR"]
 
@@ -273,6 +274,10 @@ class RecoupledPlan:
     def sym_device_tables(self) -> "RecoupledSymTables":
         """The plan packed for the symmetric pass over physical densities (validated)."""
         return _sym_device_tables(self)
+
+    def sym_tiles(self, rows: int = 8) -> "RecoupledTiles":
+        """The symmetric pass's contraction lists as dense tiles of ``rows`` segments."""
+        return _tiles(self, self.sym_device_tables(), rows)
 
 
 @dataclass
@@ -578,6 +583,145 @@ class RecoupledSymTables:
         copied = float((self.bp_other < 0).sum())
         return {"energy": 10 * terms + 4 * halves + 2 * self.dot_count,
                 "energy_grad": 10 * terms + 4 * lists + 4 * self.comp.shape[0] + 10 * coupled + 2 * copied}
+
+
+# Steps of a tile's column walk are padded to a multiple of this, so that the kernel
+# reads four column offsets as one int4 and a row's four weights as two double2.
+TILE_STEP = 4
+
+
+@dataclass
+class RecoupledTiles:
+    """The contraction lists of the symmetric pass regrouped as dense tiles.
+
+    Per pass ``L`` the adjoint of the components is ``J[s] = sum_s' K[z][s, s'] I[s']``
+    over the pass's segments, with ``K[z]`` symmetric: a contraction ``d`` of segments
+    ``(a, b)`` adds ``k[z, d]`` to ``K[a, b]`` and to ``K[b, a]`` (``2 k`` on the diagonal
+    when ``a == b``).  A tile is ``rows`` segments (rows; ``-1`` pads a short tile) and
+    the union of their nonzero columns, walked column by column: every lane of a warp
+    holds one (row, atom), so one shared-memory read of a column component serves all the
+    tile's rows.  Rows with the same column set share a tile where they can; the rest are
+    merged greedily by the growth of the column union.  ``tile_row[t, r]`` and
+    ``col_comp[q]`` are local component offsets of the segments' ``M = 0`` components (the
+    symmetric layout, ``L + 1`` components per segment); a tile's columns
+    ``[tile_col_begin[t], tile_col_begin[t + 1])`` are padded to a multiple of
+    ``TILE_STEP`` with column 0 and weight 0.  The weights of species ``z`` are
+    ``kval[z, rows * tile_col_begin[t] + r * ncols_t + (q - tile_col_begin[t])]``
+    (``tile_weights``); ``dot_pos[d]`` are the two entries contraction ``d`` adds to.
+    Tiles within a pass are ordered by decreasing column count."""
+
+    rows: int
+    pass_count: int
+    tile_begin: np.ndarray      # int32 [pass_count + 1]
+    tile_row: np.ndarray        # int32 [T, rows]
+    tile_col_begin: np.ndarray  # int32 [T + 1]
+    col_comp: np.ndarray        # int32 [Q]
+    dot_pos: np.ndarray         # int64 [D, 2]
+    nonzero: int                # (row, column) pairs with a contraction
+
+    @property
+    def tile_count(self) -> int:
+        return int(self.tile_row.shape[0])
+
+    @property
+    def step_count(self) -> int:
+        return int(self.col_comp.shape[0])
+
+    def tile_weights(self, k: np.ndarray) -> np.ndarray:
+        """``kval [species, rows * step_count]`` from the contraction weights ``k [species, D]``."""
+        k = np.asarray(k, dtype=np.float64)
+        out = np.zeros((k.shape[0], self.rows * self.step_count), dtype=np.float64)
+        for z in range(k.shape[0]):
+            np.add.at(out[z], self.dot_pos[:, 0], k[z])
+            np.add.at(out[z], self.dot_pos[:, 1], k[z])
+        return out
+
+    def efficiency(self) -> float:
+        """Nonzero (row, column) pairs over the padded tile entries the kernel walks."""
+        return self.nonzero / max(1, self.rows * self.step_count)
+
+    def validate(self, sym: "RecoupledSymTables") -> None:
+        P, R = self.pass_count, self.rows
+        tb = self.tile_begin.astype(np.int64)
+        if tb.shape != (P + 1,) or tb[0] != 0 or np.any(np.diff(tb) < 0) or tb[-1] != self.tile_count:
+            raise ValueError("tile_begin does not partition the tiles")
+        if self.tile_row.shape != (self.tile_count, R):
+            raise ValueError("tile_row must be [tiles, rows]")
+        cb = self.tile_col_begin.astype(np.int64)
+        if cb.shape != (self.tile_count + 1,) or cb[0] != 0 or cb[-1] != self.step_count or \
+                np.any(np.diff(cb) < 0) or np.any(np.diff(cb) % TILE_STEP):
+            raise ValueError("tile_col_begin does not partition the steps in multiples of TILE_STEP")
+        nc = np.diff(sym.pass_begin.astype(np.int64))
+        Lt = np.repeat(np.arange(P), np.diff(tb))
+        rows = self.tile_row.astype(np.int64)
+        if np.any((rows >= 0) & (rows + Lt[:, None] >= nc[Lt][:, None])) or np.any(rows < -1):
+            raise ValueError("tile row outside its pass")
+        Lq = np.repeat(Lt, np.diff(cb))
+        if np.any(self.col_comp < 0) or np.any(self.col_comp.astype(np.int64) + Lq >= nc[Lq]):
+            raise ValueError("tile column outside its pass")
+        if np.any(self.dot_pos < 0) or np.any(self.dot_pos >= R * self.step_count):
+            raise ValueError("contraction position outside the weights")
+
+
+def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> RecoupledTiles:
+    if rows < 1 or rows > 32:
+        raise ValueError("rows per tile must be in [1, 32]")
+    half = plan.seg_L.astype(np.int64) + 1
+    off = np.concatenate([[0], np.cumsum(half)])
+    P = sym.pass_count
+    tile_begin, tile_row, col_begin, col_comp = [0], [], [0], []
+    pos_of = {}  # (global row segment, global column segment) -> flat weight index
+    nonzero = 0
+    for L in range(P):
+        segs = np.nonzero(plan.seg_L == L)[0]
+        support: Dict[int, set] = {int(s): set() for s in segs}
+        for d in np.nonzero(plan.dot_L == L)[0]:
+            a, b = int(plan.dot_a[d]), int(plan.dot_b[d])
+            support[a].add(b)
+            support[b].add(a)
+        nonzero += sum(len(v) for v in support.values())
+        groups: Dict[frozenset, List[int]] = {}
+        for s in segs:
+            groups.setdefault(frozenset(support[int(s)]), []).append(int(s))
+        tiles, left = [], []
+        for sig, members in sorted(groups.items(), key=lambda g: (-len(g[0]), min(g[1]))):
+            while len(members) >= rows:
+                tiles.append(members[:rows])
+                members = members[rows:]
+            left.extend(members)
+        left.sort(key=lambda s: (min(support[s], default=-1), len(support[s]), s))
+        while left:
+            t = [left.pop(0)]
+            union = set(support[t[0]])
+            while len(t) < rows and left:
+                best = min(range(len(left)), key=lambda i: (len(union | support[left[i]]) - len(union), i))
+                t.append(left.pop(best))
+                union |= support[t[-1]]
+            tiles.append(t)
+        cols_of = [sorted(set().union(*(support[s] for s in t))) for t in tiles]
+        order = sorted(range(len(tiles)), key=lambda i: (-len(cols_of[i]), i))
+        base = int(sym.pass_begin[L])
+        for i in order:
+            t, cols = tiles[i], cols_of[i]
+            n = len(cols)
+            npad = (n + TILE_STEP - 1) // TILE_STEP * TILE_STEP if n else 0
+            q0 = col_begin[-1]
+            for r, srow in enumerate(t):
+                for qi, scol in enumerate(cols):
+                    pos_of[(srow, scol)] = rows * q0 + r * npad + qi
+            tile_row.append([int(off[s]) - base for s in t] + [-1] * (rows - len(t)))
+            col_comp.extend(int(off[c]) - base for c in cols)
+            col_comp.extend([0] * (npad - n))
+            col_begin.append(q0 + npad)
+        tile_begin.append(len(tile_row))
+    dot_pos = np.asarray([(pos_of[(int(a), int(b))], pos_of[(int(b), int(a))])
+                          for a, b in zip(plan.dot_a, plan.dot_b)], dtype=np.int64).reshape(-1, 2)
+    tiles = RecoupledTiles(rows=rows, pass_count=P, tile_begin=np.asarray(tile_begin, dtype=np.int32),
+                           tile_row=np.asarray(tile_row, dtype=np.int32).reshape(-1, rows),
+                           tile_col_begin=np.asarray(col_begin, dtype=np.int32),
+                           col_comp=np.asarray(col_comp, dtype=np.int32), dot_pos=dot_pos, nonzero=nonzero)
+    tiles.validate(sym)
+    return tiles
 
 
 def _sym_device_tables(plan: "RecoupledPlan") -> RecoupledSymTables:
