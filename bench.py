@@ -60,6 +60,9 @@ def parse():
                     help="atoms per CTA of the recoupled passes (1-4; 0 = the evaluator's default)")
     ap.add_argument("--recoupled-threads", type=int, default=0, choices=[0, 256, 512],
                     help="threads per CTA of the recoupled passes (0 = the evaluator's default)")
+    ap.add_argument("--tile-rows", type=int, default=-1, choices=[-1, 0, 8, 16],
+                    help="segments per dense tile of the symmetric adjoint (0 = contraction lists; -1 = the "
+                         "evaluator's default)")
     ap.add_argument("--recoupled-general", action="store_true",
                     help="the general recoupled passes instead of the M >= 0 (symmetric) ones")
     ap.add_argument("--energy-only", action="store_true",
@@ -287,9 +290,13 @@ def run_b200(args):
     forces = not args.energy_only
     physical = not args.recoupled_general
     if args.b_basis == "recoupled":
-        if args.recoupled_atoms or args.recoupled_threads:
-            shape = (args.recoupled_atoms or 1, args.recoupled_threads or 256)
-            ev.RECOUPLED_GRAD_SHAPE = ev.RECOUPLED_ENERGY_SHAPE = shape
+        if args.recoupled_atoms or args.recoupled_threads or args.tile_rows >= 0:
+            base = (ev.RECOUPLED_TILED_SHAPE if physical else ev.RECOUPLED_GRAD_SHAPE) if forces else \
+                ev.RECOUPLED_ENERGY_SHAPE
+            rows = base[2] if args.tile_rows < 0 else args.tile_rows
+            shape = (args.recoupled_atoms or (32 // rows if rows else base[0]), args.recoupled_threads or base[1],
+                     rows)
+            ev.RECOUPLED_TILED_SHAPE = ev.RECOUPLED_GRAD_SHAPE = ev.RECOUPLED_ENERGY_SHAPE = shape
         rec = ev.recoupled(physical, forces)
     else:
         rec = None
@@ -404,7 +411,9 @@ def run_b200(args):
     flops = ev.packed.flops_per_atom()
     if rec is not None:
         kern_flops = rec.tables.flops_per_atom()["energy_grad" if forces else "energy"]
-        kernel = ((f"recoupled_sym_energy_grad_kernel<{rec._c.atoms_per_cta}, {rec._c.threads_per_cta}>"
+        kernel = ((f"recoupled_sym_tiled_grad_kernel<{32 // rec.tile_rows}, {rec._c.threads_per_cta}>"
+                   if rec.tiles is not None else
+                   f"recoupled_sym_energy_grad_kernel<{rec._c.atoms_per_cta}, {rec._c.threads_per_cta}>"
                    if forces else
                    f"recoupled_sym_energy_kernel<{rec._c.atoms_per_cta}, {rec._c.threads_per_cta}>")
                   if physical else

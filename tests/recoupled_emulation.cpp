@@ -45,7 +45,7 @@ static double g_lanes[32][32];
 #define __device__
 #define __host__
 #define __forceinline__ inline
-#define __launch_bounds__(n)
+#define __launch_bounds__(...)
 #define __restrict__
 #define __shared__ static
 #define __syncthreads() g_block->arrive_and_wait()
@@ -238,5 +238,34 @@ extern "C" int y3b_ace_recoupled_energy_symmetric(const y3b_recoupled_sym_tables
   })
   EMU_SHAPES(EMU_SENER)
 #undef EMU_SENER
+  return 0;
+}
+
+// Tiled symmetric adjoint: a CTA of 32 / rows atoms.
+extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_tables* tables,
+                                                   const y3b_recoupled_tile_tables* tiles, const void* A,
+                                                   int64_t atom_count, const int32_t* order, const int32_t* species,
+                                                   int64_t species_count, double* energy, void* dEdA,
+                                                   int32_t* status, void*) {
+  if (tables == nullptr || tiles == nullptr || (tiles->rows != 8 && tiles->rows != 16)) return -1;
+  const int th = tables->threads_per_cta == 0 ? 256 : tables->threads_per_cta;
+  const int na = 32 / tiles->rows;
+  const y3b::SymTabs t = y3b::sym_view(*tables);
+  const y3b::TileTabs tt = y3b::tile_view(*tiles);
+  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * std::max(t.row_width, t.max_pass_components)) * 16;
+  if (smem > sizeof(y3b_emulated_smem)) return -1;
+  const auto* a2 = static_cast<const double2*>(A);
+  auto* g2 = static_cast<double2*>(dEdA);
+#define EMU_TGRAD(N, T)                                                                                           \
+  run_block(T, [&] {                                                                                              \
+    y3b::recoupled_sym_tiled_grad_kernel<N, T>(t, tt, a2, atom_count, order, species, species_count, energy, g2,  \
+                                               status);                                                           \
+  })
+  if (na == 4 && th == 256) EMU_TGRAD(4, 256);
+  else if (na == 4 && th == 512) EMU_TGRAD(4, 512);
+  else if (na == 2 && th == 256) EMU_TGRAD(2, 256);
+  else if (na == 2 && th == 512) EMU_TGRAD(2, 512);
+  else return -1;
+#undef EMU_TGRAD
   return 0;
 }

@@ -65,7 +65,8 @@ def test_recoupled_adjoint_matches_term_level_adjoint_and_repeats():
     A = torch.as_tensor(rng.normal(size=(n, 8, 16)) + 1j * rng.normal(size=(n, 8, 16)), device=DEV)
     sp = torch.as_tensor(rng.integers(0, 3, n).astype(np.int32), device=DEV)
     w = rng.normal(size=(3, b.feature_count)) / np.sqrt(b.feature_count)
-    ref = ACEEvaluator(b, DEV, config=ACEConfig(5.0, 5.0), species_prefactor=[1.0, 0.75, 1.25], weights=w)
+    ref = ACEEvaluator(b, DEV, config=ACEConfig(5.0, 5.0), species_prefactor=[1.0, 0.75, 1.25], weights=w,
+                       b_basis="term")
     e0, G0 = ref.energy_grad(A, sp)
     for na, th in ((1, 256), (3, 256), (2, 512)):
         rec = RecoupledEvaluator(b, DEV, w, plan=plan, atoms_per_cta=na, threads_per_cta=th)
@@ -117,7 +118,8 @@ def test_symmetric_passes_on_physical_densities(golden):
     box = (n / 0.05) ** (1.0 / 3.0)
     pos = torch.as_tensor(rng.uniform(0, box, size=(n, 3)), device=DEV)
     sp = torch.as_tensor(rng.integers(0, 3, n).astype(np.int32), device=DEV)
-    ev = ACEEvaluator(b, DEV, config=ACEConfig(5.0, 5.0), species_prefactor=[1.0, 0.75, 1.25], weights=w)
+    ev = ACEEvaluator(b, DEV, config=ACEConfig(5.0, 5.0), species_prefactor=[1.0, 0.75, 1.25], weights=w,
+                      b_basis="term")
     row, nbr = ev.neighbor_list(pos, box)
     A = ev.density(pos, sp, box, row, nbr)
     et, Gt = ev.energy_grad(A, sp)
@@ -130,3 +132,20 @@ def test_symmetric_passes_on_physical_densities(golden):
         assert float((e - et).abs().max()) <= 1e-12 * float(et.abs().max())
         assert float((G - Gt).abs().max()) <= 1e-12 * float(Gt.abs().max())
     assert float((es2 - et).abs().max()) <= 1e-12 * float(et.abs().max())
+    # the dense-tile adjoint on the same densities: 8 and 16 rows per tile, both block
+    # sizes, species-sorted and index order; bitwise repeatable
+    for rows, th, sort in ((8, 256, True), (8, 512, True), (16, 512, False)):
+        tiled = RecoupledEvaluator(b, DEV, w, plan=plan, threads_per_cta=th, symmetric=True, tile_rows=rows,
+                                   sort_species=sort)
+        st = torch.zeros(1, dtype=torch.int32, device=DEV)
+        e1, G1 = tiled.energy_grad(A, sp, status=st)
+        e2, G2 = tiled.energy_grad(A, sp, status=st)
+        assert int(st.item()) == 0
+        assert torch.equal(e1, e2) and torch.equal(G1, G2)
+        assert float((e1 - et).abs().max()) <= 1e-12 * float(et.abs().max())
+        assert float((G1 - Gt).abs().max()) <= 1e-12 * float(Gt.abs().max())
+        e6, G6 = (x.cpu().numpy() for x in tiled.energy_grad(torch.as_tensor(A6, device=DEV),
+                                                              torch.as_tensor(sp6, device=DEV)))
+        assert np.abs(e6 - e0).max() <= 1e-12 * np.abs(e0).max()
+        assert np.abs(G6 - G0).max() <= 1e-12 * np.abs(G0).max()
+

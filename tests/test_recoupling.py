@@ -577,3 +577,43 @@ def test_symmetric_tiles_walk_matches_oracle(plan5, physical_case, rows):
     e1, G1 = rn.walk_sym_tiled(tabs, tiles, A, species, k)
     assert np.abs(e1 - e0).max() <= 1e-12 * np.abs(e0).max()
     assert np.abs(G1 - G0).max() <= 1e-12 * np.abs(G0).max()
+
+
+def _bind_emulated(emulated, monkeypatch, names):
+    import ctypes
+
+    import torch
+    from ye3t_b200 import _native
+    for name in names:
+        res, args = _native._SIGS[name]
+        getattr(emulated, name).restype = res
+        getattr(emulated, name).argtypes = args
+    emulated.y3b_last_error.restype = ctypes.c_char_p
+    monkeypatch.setattr(_native, "lib", lambda: emulated)
+    monkeypatch.setattr(_native, "require_cuda", lambda *t, what="": torch.device("cpu"))
+    monkeypatch.setattr(_native, "stream_of", lambda device: 0)
+
+
+@pytest.mark.parametrize("rows, th", [(8, 256), (8, 512), (16, 256)])
+def test_tiled_device_source_emulated_matches_oracle(emulated, plan5, physical_case, rows, th, monkeypatch):
+    """The tiled symmetric adjoint's own source (recoupled_sym_tiled_grad_kernel), emulated on
+    the CPU through RecoupledEvaluator's real bindings: 4 or 2 atoms per CTA grouped in species
+    order (a partial last group), lanes as (row, atom) walking the tiles' columns; the oracle's
+    energies and dE/dA, with no status set."""
+    import torch
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    _bind_emulated(emulated, monkeypatch, ["y3b_ace_recoupled_energy_grad_tiled"])
+    b, plan = plan5
+    A, species, w, e0, G0 = physical_case
+    ev = RecoupledEvaluator(b, "cpu", w, plan=plan, threads_per_cta=th, symmetric=True, tile_rows=rows)
+    st = torch.zeros(1, dtype=torch.int32)
+    e, G = ev.energy_grad(torch.as_tensor(A), torch.as_tensor(species), status=st)
+    assert int(st.item()) == 0
+    assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()
+    # a damaged tile column is skipped and reported
+    from ye3t_b200 import _native
+    ev.tile_arrays["col_comp"][5] = 1 << 20
+    st.zero_()
+    ev.energy_grad(torch.as_tensor(A), torch.as_tensor(species), status=st)
+    assert int(st.item()) & _native.STATUS_TABLE

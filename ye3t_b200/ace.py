@@ -48,9 +48,12 @@ class ACEConfig:
 class ACEEvaluator:
     """Evaluates one :class:`ACEBundle` on one CUDA device."""
 
-    #: CTA shapes (atoms, threads) of the recoupled passes used by default
-    RECOUPLED_GRAD_SHAPE = (2, 256)
-    RECOUPLED_ENERGY_SHAPE = (1, 256)
+    #: CTA shapes (atoms, threads, tile rows) of the recoupled passes used by default:
+    #: the adjoint of a physical density through the dense tiles (4 atoms, 8-segment
+    #: tiles), that of any other A through the general lists, and the energy alone
+    RECOUPLED_TILED_SHAPE = (4, 512, 8)
+    RECOUPLED_GRAD_SHAPE = (2, 256, 0)
+    RECOUPLED_ENERGY_SHAPE = (1, 256, 0)
 
     def __init__(self, bundle: ACEBundle, device, *, config: ACEConfig = ACEConfig(),
                  species_prefactor=None, weights=None, b_basis: str = "recoupled"):
@@ -85,10 +88,13 @@ class ACEEvaluator:
             if self.weights is None:
                 raise ValueError("weights are required for the energy")
             plan = next((r.plan for r in self._recoupled.values()), None) or build_recoupled_plan(self.bundle)
-            na, th = self.RECOUPLED_GRAD_SHAPE if grad else self.RECOUPLED_ENERGY_SHAPE
+            if grad:
+                na, th, rows = self.RECOUPLED_TILED_SHAPE if symmetric else self.RECOUPLED_GRAD_SHAPE
+            else:
+                na, th, rows = self.RECOUPLED_ENERGY_SHAPE
             self._recoupled[key] = RecoupledEvaluator(self.bundle, self.device, self.weights.cpu().numpy(),
-                                                      plan=plan, atoms_per_cta=na, threads_per_cta=th,
-                                                      symmetric=symmetric)
+                                                      plan=plan, atoms_per_cta=min(na, 4), threads_per_cta=th,
+                                                      symmetric=symmetric, tile_rows=rows)
         return self._recoupled[key]
 
     @property

@@ -943,17 +943,30 @@ class RecoupledEvaluator:
     entry loaded once for all of them), within the 224 KB of shared memory; a CTA has
     ``threads_per_cta`` (256 or 512) threads.  ``symmetric`` selects the passes over the
     ``M >= 0`` components (``RecoupledSymTables``), valid only for physical densities
-    ``A[n, l, -m] = (-1)^m conj(A[n, l, m])`` such as ``ACEEvaluator.density`` gives."""
+    ``A[n, l, -m] = (-1)^m conj(A[n, l, m])`` such as ``ACEEvaluator.density`` gives.
+
+    ``tile_rows`` (8 or 16; symmetric passes only) makes ``energy_grad`` form the
+    components' adjoints from dense tiles of the contraction weights
+    (``RecoupledTiles``, ``y3b_ace_recoupled_energy_grad_tiled``): a CTA then holds
+    ``32 // tile_rows`` atoms, grouped in species order so that a CTA's atoms share one
+    species' tile weights (``sort_species``)."""
 
     def __init__(self, bundle: ACEBundle, device, weights: np.ndarray = None, plan: "RecoupledPlan" = None,
-                 atoms_per_cta: int = 1, threads_per_cta: int = 256, symmetric: bool = False):
+                 atoms_per_cta: int = 1, threads_per_cta: int = 256, symmetric: bool = False,
+                 tile_rows: int = 0, sort_species: bool = True):
         import torch
         if not 1 <= int(atoms_per_cta) <= 4:
             raise ValueError("atoms_per_cta must be in [1, 4]")
         if int(threads_per_cta) not in (256, 512):
             raise ValueError("threads_per_cta must be 256 or 512")
+        if int(tile_rows) not in (0, 8, 16):
+            raise ValueError("tile_rows must be 0 (lists), 8 or 16")
+        if tile_rows and not symmetric:
+            raise ValueError("the tiled adjoint is a form of the symmetric passes (symmetric=True)")
         self.device = torch.device(device)
         self.symmetric = bool(symmetric)
+        self.tile_rows = int(tile_rows)
+        self.sort_species = bool(sort_species)
         self.plan = plan if plan is not None else build_recoupled_plan(bundle)
         self.tables = self.plan.sym_device_tables() if self.symmetric else self.plan.device_tables()
         names = _SYM_ARRAYS if self.symmetric else _TABLE_ARRAYS
@@ -964,6 +977,19 @@ class RecoupledEvaluator:
         self._c = (ctypes_sym_tables if self.symmetric else ctypes_tables)(self.arrays, self.tables)
         self._c.atoms_per_cta = int(atoms_per_cta)
         self._c.threads_per_cta = int(threads_per_cta)
+        self.tiles = None
+        if self.tile_rows:
+            from . import _native as nat
+            self.tiles = self.plan.sym_tiles(self.tile_rows)
+            self.tile_arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(self.tiles, name))).to(self.device)
+                                for name in ("tile_begin", "tile_row", "tile_col_begin", "col_comp")}
+            self.kval = None if weights is None else torch.as_tensor(
+                self.tiles.tile_weights(self.plan.energy_weights(weights))).to(self.device).contiguous()
+            self._t = nat.RecoupledTileTables(
+                rows=self.tiles.rows, pass_count=self.tiles.pass_count, tile_count=self.tiles.tile_count,
+                step_count=self.tiles.step_count,
+                **{name: self.tile_arrays[name].data_ptr() for name in self.tile_arrays},
+                kval=0 if self.kval is None else self.kval.data_ptr())
 
     def _rows(self, A):
         import torch
@@ -1024,6 +1050,13 @@ class RecoupledEvaluator:
         sp = self._species(species, n)
         e = torch.empty(n, dtype=torch.float64, device=self.device)
         G = torch.empty_like(A)
+        if self.tiles is not None:
+            order = torch.sort(sp, stable=True).indices.to(torch.int32) if self.sort_species else None
+            nat.check(nat.lib().y3b_ace_recoupled_energy_grad_tiled(
+                ctypes.byref(self._c), ctypes.byref(self._t), A.data_ptr(), n, nat.ptr(order), sp.data_ptr(),
+                self.kval.shape[0], e.data_ptr(), G.data_ptr(), nat.ptr(status), nat.stream_of(self.device)),
+                "y3b_ace_recoupled_energy_grad_tiled")
+            return e, G
         name = "y3b_ace_recoupled_energy_grad_symmetric" if self.symmetric else "y3b_ace_recoupled_energy_grad"
         nat.check(getattr(nat.lib(), name)(
             ctypes.byref(self._c), A.data_ptr(), n, sp.data_ptr(), self.weights.data_ptr(), self.weights.shape[0],
