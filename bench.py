@@ -246,7 +246,8 @@ def _config(args):
                         "n_max 8, l_max 3, nu<=4 (25,328 words / 41,168 L=0 features), fp64, per-species "
                         "linear readout",
             "atoms": args.atoms, "bundle": args.bundle, "cutoff_A": CUTOFF, "radial_lambda": LAMBDA,
-            "parallelism": f"atom-block x{args.gpus}",
+            "parallelism": f"atom-block x{args.gpus} (each rank bins its slab and a one-cell halo; forces "
+                           "reduce-scattered)" if args.gpus > 1 else "atom-block x1",
             "atom_order": "cell order (z, y, x) of a cell list with cells >= the cutoff, so each rank's atom "
                           "block is a slab of the box",
             "b_basis": (f"recoupled pair contractions ({'M >= 0 symmetric passes' if sym else 'general passes'})"
@@ -273,7 +274,7 @@ def run_b200(args):
     from ye3t_b200.schedules import ACEBundle
 
     from ye3t_b200.distributed import atom_block, init_from_env, max_over_ranks as _max_over_ranks
-    from ye3t_b200.distributed import sum_over_ranks
+    from ye3t_b200.distributed import block_forces, sum_over_ranks
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)
@@ -302,6 +303,13 @@ def run_b200(args):
         rec = None
     begin, end = atom_block(rank, world, N)
     n_local = end - begin
+    # this rank's slab of the box (cell-ordered atoms) with one cell layer of halo,
+    # and a bound on its edge count (26.2 neighbours on average at this density),
+    # so that the neighbour build neither bins the whole system nor syncs the host
+    z_window = ev.slab_window(pos, box, begin, end)
+    avg_deg = DENSITY * 4.0 / 3.0 * 3.141592653589793 * CUTOFF ** 3
+    capacity = int(1.25 * avg_deg * n_local) + 4096
+    nstatus = torch.zeros(1, dtype=torch.int32, device=device)
     pos_h = pos.pin_memory()
     sp_h = species.pin_memory()
     pos_d = pos.to(device)
@@ -320,7 +328,7 @@ def run_b200(args):
     b_launches = 1 if rec is not None else GRAD_CLASSES
     # our kernels per step: 6 neighbour-count, 1 fill, density, the B-basis
     # pass(es), then edge gradients and the force gather/scatter
-    launches_per_step = 8 + (b_launches + 2 if forces else 1)
+    launches_per_step = 8 + (b_launches + 2 if forces else 1) + (1 if world > 1 and forces else 0)
 
     def step(record):
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] if record else None
@@ -329,7 +337,7 @@ def run_b200(args):
             if record:
                 marks[i].record()
         mark(0)
-        row, nbr = ev.neighbor_list(pos_d, box, begin, end)
+        row, nbr = ev.neighbor_list(pos_d, box, begin, end, z_window=z_window, capacity=capacity, status=nstatus)
         mark(1)
         A = ev.density(pos_d, sp_d, box, row, nbr, begin)
         mark(2)
@@ -346,8 +354,7 @@ def run_b200(args):
         else:
             F_full.zero_()
             ev.partial_forces_from_edges(row, nbr, g, begin, N, out=F_full[:N])
-            dist.reduce_scatter_tensor(F_block, F_full, op=dist.ReduceOp.SUM)
-            F = F_block
+            F = block_forces(F_full, F_block)
         mark(5)
         return sum_over_ranks(e_at.sum()), F, marks
 
@@ -378,6 +385,8 @@ def run_b200(args):
         for k, a, b in zip(stages, m[:-1], m[1:]):
             timers[k].append(a.elapsed_time(b))
     energy = float(total.item())
+    if int(nstatus.item()) != 0:
+        raise RuntimeError(f"neighbour build status {int(nstatus.item())}: slab window or edge capacity exceeded")
     forces_abs_sum = float(sum_over_ranks(F_last[:max(0, min(chunk, N - rank * chunk))].abs().sum()).item()) \
         if forces else None
 

@@ -262,6 +262,28 @@ int y3b_neighbor_fill(const double* positions, int64_t atom_count, int64_t cente
                       int64_t workspace_bytes, const int64_t* row_offsets, int32_t* neighbors,
                       void* stream);
 
+/* The same two passes for an atom block that is a slab of the box (atoms
+ * stored in cell order, one rank's block of a spatial decomposition): only
+ * atoms in the z cell layers [z_cell_begin, z_cell_begin + z_cell_count)
+ * (periodic, layers of y3b_neighbor_cells_per_side cells) are binned, so the
+ * binning costs the slab and its halo instead of the whole system.  Every
+ * centre's z layer and its two neighbours must lie in the window; a centre
+ * outside sets Y3B_STATUS_INDEX_RANGE (its row is incomplete).  A window of
+ * z_cell_count <= 0 or >= the layer count is the whole box.  The fill writes
+ * at most neighbor_capacity indices: a list longer than that sets
+ * Y3B_STATUS_CAPACITY, so a caller can size the neighbour array from a bound
+ * instead of reading row_offsets[count] back to the host first. */
+int64_t y3b_neighbor_cells_per_side(double box, double cutoff);
+int y3b_neighbor_count_window(const double* positions, int64_t atom_count, int64_t center_begin,
+                              int64_t center_end, double box, double cutoff, int64_t z_cell_begin,
+                              int64_t z_cell_count, void* workspace, int64_t workspace_bytes,
+                              int64_t* row_offsets, int32_t* status, void* stream);
+int y3b_neighbor_fill_window(const double* positions, int64_t atom_count, int64_t center_begin,
+                             int64_t center_end, double box, double cutoff, int64_t z_cell_begin,
+                             int64_t z_cell_count, const void* workspace, int64_t workspace_bytes,
+                             const int64_t* row_offsets, int64_t neighbor_capacity, int32_t* neighbors,
+                             int32_t* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * Radial channel mixing.
  * ---------------------------------------------------------------------- */

@@ -100,6 +100,14 @@ def _rank_forces(rank, world, port, out_path):
     total = sum_over_ranks(torch.tensor(np.concatenate([[e.sum()], F.reshape(-1)]), dtype=torch.float64))
     if r == 0:
         np.save(out_path, total.numpy())
+    # the bench's collective: a reduce-scatter of the partial arrays (padded to
+    # world * chunk rows) leaves each rank the forces of its own chunk
+    from ye3t_b200.distributed import block_forces
+    chunk = (N + w - 1) // w
+    padded = torch.zeros((chunk * w, 3), dtype=torch.float64)
+    padded[:N] = torch.as_tensor(F)
+    mine = block_forces(padded, torch.empty((chunk, 3), dtype=torch.float64))
+    np.save(f"{out_path}.block{r}.npy", mine.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -115,3 +123,5 @@ def test_rank_partial_forces_sum_to_reference(tmp_path, golden, world):
     assert abs(total[0] - float(ref["energy"])) <= 1e-12 * abs(float(ref["energy"]))
     F = total[1:].reshape(-1, 3)
     assert np.abs(F - F_ref).max() <= 1e-10 * max(1.0, np.abs(F_ref).max())
+    blocks = np.concatenate([np.load(f"{out}.block{r}.npy") for r in range(world)])[:F_ref.shape[0]]
+    assert np.abs(blocks - F_ref).max() <= 1e-10 * max(1.0, np.abs(F_ref).max())

@@ -65,6 +65,38 @@ def test_neighbor_list_matches_oracle(ev3, N, begin, end):
     np.testing.assert_array_equal(got.cpu().numpy(), nbr[off[begin]:off[end]])
 
 
+def test_neighbor_list_slab_windows_match_full_build(ev3):
+    """Atoms in cell order, four atom blocks: each block's rows built from its slab window
+    (plus halo) with a capacity-sized neighbour array equal the full build bit for bit; a
+    window one layer short flags the centres outside it, and a capacity one short flags the
+    overflow."""
+    import sys
+    from ye3t_b200 import _native as nat
+    sys.path.insert(0, REPO)
+    import bench
+    N = 20000
+    box = (N / 0.05) ** (1 / 3)
+    pos = np.random.default_rng(77).uniform(0, box, size=(N, 3))
+    pos = pos[bench.cell_order(pos, box, 5.0)]
+    pd = torch.as_tensor(pos, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for r in range(4):
+        b, e = (N * r) // 4, (N * (r + 1)) // 4
+        win = ev3.slab_window(pos, box, b, e)
+        assert win is not None and win[1] < int(nat.lib().y3b_neighbor_cells_per_side(box, 5.0))
+        row0, nbr0 = ev3.neighbor_list(pd, box, b, e)
+        row1, nbr1 = ev3.neighbor_list(pd, box, b, e, z_window=win, capacity=nbr0.shape[0] + 100, status=status)
+        assert int(status.item()) == 0
+        assert torch.equal(row0, row1)
+        assert torch.equal(nbr0, nbr1[:nbr0.shape[0]])
+    short = (win[0] + 1, win[1] - 1)
+    ev3.neighbor_list(pd, box, b, e, z_window=short, capacity=nbr0.shape[0], status=status)
+    assert int(status.item()) & nat.STATUS_INDEX_RANGE
+    status.zero_()
+    ev3.neighbor_list(pd, box, b, e, z_window=win, capacity=nbr0.shape[0] - 1, status=status)
+    assert int(status.item()) & nat.STATUS_CAPACITY
+
+
 def test_density_matches_reference(small, ev3):
     pos = torch.as_tensor(small["pos"], device=DEV)
     sp = torch.as_tensor(small["species"], device=DEV)

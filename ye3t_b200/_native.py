@@ -115,6 +115,10 @@ _SIGS = {
     "y3b_neighbor_workspace_bytes": (I64, [I64, DBL, DBL]),
     "y3b_neighbor_count": (ctypes.c_int, [VP, I64, I64, I64, DBL, DBL, VP, I64, VP, VP]),
     "y3b_neighbor_fill": (ctypes.c_int, [VP, I64, I64, I64, DBL, DBL, VP, I64, VP, VP, VP]),
+    "y3b_neighbor_cells_per_side": (I64, [DBL, DBL]),
+    "y3b_neighbor_count_window": (ctypes.c_int, [VP, I64, I64, I64, DBL, DBL, I64, I64, VP, I64, VP, VP, VP]),
+    "y3b_neighbor_fill_window": (ctypes.c_int, [VP, I64, I64, I64, DBL, DBL, I64, I64, VP, I64, VP, I64, VP, VP,
+                                                VP]),
     "y3b_ace_density": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, DBL, DBL, VP, VP,
                                        VP]),
     "y3b_ace_features": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP]),

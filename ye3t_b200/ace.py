@@ -106,24 +106,68 @@ class ACEEvaluator:
 
     # -- neighbour list --------------------------------------------------------
     def neighbor_list(self, positions: torch.Tensor, box: float, begin: int = 0,
-                      end: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-        """CSR rows ``(row_offsets [n+1] int64, neighbors [E] int32)`` for centres [begin, end)."""
+                      end: Optional[int] = None, z_window: Optional[Tuple[int, int]] = None,
+                      capacity: Optional[int] = None,
+                      status: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """CSR rows ``(row_offsets [n+1] int64, neighbors [E] int32)`` for centres [begin, end).
+
+        ``z_window = (first z cell layer, layer count)`` bins only that slab of the box
+        (``y3b_neighbor_count_window``): the centres must be a slab inside it, one layer
+        in from each side (``slab_window`` computes it).  With ``capacity`` the neighbour
+        array is allocated at that size without reading the edge total back to the host
+        (no device sync); ``neighbors`` is then the whole buffer, of which
+        ``row_offsets[-1]`` entries are used, and an overflow sets
+        ``Y3B_STATUS_CAPACITY`` in ``status``."""
         pos = positions.to(self.device, torch.float64).contiguous()
         N = pos.shape[0]
         end = N if end is None else int(end)
         lib = nat.lib()
         rc = float(self.config.cutoff)
         ws_bytes = int(lib.y3b_neighbor_workspace_bytes(N, float(box), rc))
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=self.device)
+        key = (N, ws_bytes)
+        if getattr(self, "_nbr_ws_key", None) != key:
+            self._nbr_ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=self.device)
+            self._nbr_ws_key = key
+        ws = self._nbr_ws
         row = torch.empty(end - begin + 1, dtype=torch.int64, device=self.device)
         s = self._stream()
-        nat.check(lib.y3b_neighbor_count(pos.data_ptr(), N, begin, end, float(box), rc, ws.data_ptr(), ws_bytes,
-                                         row.data_ptr(), s), "neighbor_count")
-        E = int(row[-1].item())
-        nbr = torch.empty(max(E, 1), dtype=torch.int32, device=self.device)
-        nat.check(lib.y3b_neighbor_fill(pos.data_ptr(), N, begin, end, float(box), rc, ws.data_ptr(), ws_bytes,
-                                        row.data_ptr(), nbr.data_ptr(), s), "neighbor_fill")
+        zb, zc = (0, 0) if z_window is None else (int(z_window[0]), int(z_window[1]))
+        nat.check(lib.y3b_neighbor_count_window(pos.data_ptr(), N, begin, end, float(box), rc, zb, zc,
+                                                ws.data_ptr(), ws_bytes, row.data_ptr(), nat.ptr(status), s),
+                  "neighbor_count")
+        if capacity is None:
+            E = int(row[-1].item())
+            cap = E
+        else:
+            E = cap = int(capacity)
+        nbr = torch.empty(max(cap, 1), dtype=torch.int32, device=self.device)
+        nat.check(lib.y3b_neighbor_fill_window(pos.data_ptr(), N, begin, end, float(box), rc, zb, zc,
+                                               ws.data_ptr(), ws_bytes, row.data_ptr(), cap, nbr.data_ptr(),
+                                               nat.ptr(status), s), "neighbor_fill")
         return row, nbr[:E]
+
+    def slab_window(self, positions, box: float, begin: int, end: int) -> Optional[Tuple[int, int]]:
+        """The z window ``(first layer, count)`` of the cell list that holds the centres
+        ``[begin, end)`` with one layer of halo on each side, or None when that is the whole
+        box.  Read from host positions; meant for atoms stored in cell order, where an atom
+        block is a slab."""
+        import numpy as np
+        n = int(nat.lib().y3b_neighbor_cells_per_side(float(box), float(self.config.cutoff)))
+        if n < 3 or end <= begin:
+            return None
+        z = np.asarray(positions[begin:end, 2].cpu() if hasattr(positions, "cpu") else positions[begin:end, 2],
+                       dtype=np.float64)
+        f = z / box
+        cz = np.clip(((f - np.floor(f)) * n).astype(np.int64), 0, n - 1)
+        layers = np.unique(cz)
+        # the smallest periodic run of layers that holds every centre layer
+        gaps = np.diff(np.concatenate([layers, [layers[0] + n]]))
+        g = int(np.argmax(gaps))
+        first = int(layers[(g + 1) % layers.shape[0]])
+        span = int(n - gaps[g] + 1)
+        if span + 2 >= n:
+            return None
+        return ((first - 1) % n, span + 2)
 
     # -- kernel 1 ----------------------------------------------------------------
     def density(self, positions, species, box, row_offsets, neighbors, begin: int = 0,

@@ -41,14 +41,26 @@ __device__ __forceinline__ int cell_coord(double x, double box, int n) {
   return c < 0 ? 0 : (c >= n ? n - 1 : c);
 }
 
-__global__ void assign_cells_kernel(const double* __restrict__ pos, int64_t N, double box, int n,
+// A window of z cell layers [zb, zb + zc) (periodic; zc == n is the whole
+// box): only atoms inside it are binned, in window-local cells
+// ((z - zb) mod n, y, x).  Returns -1 for a z layer outside the window.
+__device__ __forceinline__ int window_z(int cz, int n, int zb, int zc) {
+  const int wz = (cz - zb + n) % n;
+  return wz < zc ? wz : -1;
+}
+
+__global__ void assign_cells_kernel(const double* __restrict__ pos, int64_t N, double box, int n, int zb, int zc,
                                     int32_t* __restrict__ atom_cell,
                                     unsigned long long* __restrict__ counts) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < N;
        i += int64_t(gridDim.x) * blockDim.x) {
     const int cx = cell_coord(pos[3 * i], box, n), cy = cell_coord(pos[3 * i + 1], box, n),
-              cz = cell_coord(pos[3 * i + 2], box, n);
-    const int c = (cz * n + cy) * n + cx;
+              wz = window_z(cell_coord(pos[3 * i + 2], box, n), n, zb, zc);
+    if (wz < 0) {
+      atom_cell[i] = -1;
+      continue;
+    }
+    const int c = (wz * n + cy) * n + cx;
     atom_cell[i] = c;
     atomicAdd(counts + c + 1, 1ull);
   }
@@ -60,6 +72,7 @@ __global__ void fill_cells_kernel(int64_t N, const int32_t* __restrict__ atom_ce
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < N;
        i += int64_t(gridDim.x) * blockDim.x) {
     const int c = atom_cell[i];
+    if (c < 0) continue;
     const int slot = atomicAdd(cursor + c, 1);
     cell_atoms[cell_start[c] + slot] = int32_t(i);
   }
@@ -83,19 +96,28 @@ __global__ void sort_cells_kernel(int64_t nc, const int64_t* __restrict__ cell_s
   }
 }
 
-// Visit every candidate neighbour j of centre i exactly once.
+// Visit every candidate neighbour j of centre i exactly once.  A centre whose
+// neighbouring z layers leave the binned window returns false (its row is
+// incomplete); the caller reports it.
 template <typename F>
-__device__ __forceinline__ void for_each_neighbor(const double* __restrict__ pos, int64_t i, double box,
-                                                  double rc2, int n, const int64_t* __restrict__ cell_start,
+__device__ __forceinline__ bool for_each_neighbor(const double* __restrict__ pos, int64_t i, double box,
+                                                  double rc2, int n, int zb, int zc,
+                                                  const int64_t* __restrict__ cell_start,
                                                   const int32_t* __restrict__ cell_atoms, F&& f) {
   const double xi = pos[3 * i], yi = pos[3 * i + 1], zi = pos[3 * i + 2];
   const int span = n >= 3 ? 1 : 0;
   const int cx = cell_coord(xi, box, n), cy = cell_coord(yi, box, n), cz = cell_coord(zi, box, n);
-  for (int dz = -span; dz <= span; ++dz)
+  bool inside = true;
+  for (int dz = -span; dz <= span; ++dz) {
+    const int wz = window_z((cz + dz + n) % n, n, zb, zc);
+    if (wz < 0) {
+      inside = false;
+      continue;
+    }
     for (int dy = -span; dy <= span; ++dy)
       for (int dx = -span; dx <= span; ++dx) {
-        const int x = (cx + dx + n) % n, y = (cy + dy + n) % n, z = (cz + dz + n) % n;
-        const int c = (z * n + y) * n + x;
+        const int x = (cx + dx + n) % n, y = (cy + dy + n) % n;
+        const int c = (wz * n + y) * n + x;
         for (int64_t k = cell_start[c]; k < cell_start[c + 1]; ++k) {
           const int32_t j = cell_atoms[k];
           if (j == i) continue;
@@ -104,33 +126,42 @@ __device__ __forceinline__ void for_each_neighbor(const double* __restrict__ pos
           if (dist2(d) <= rc2) f(j);
         }
       }
+  }
+  return inside;
 }
 
 __global__ void count_neighbors_kernel(const double* __restrict__ pos, int64_t begin, int64_t end,
-                                       double box, double rc2, int n,
+                                       double box, double rc2, int n, int zb, int zc,
                                        const int64_t* __restrict__ cell_start,
                                        const int32_t* __restrict__ cell_atoms,
-                                       int64_t* __restrict__ row_offsets) {
+                                       int64_t* __restrict__ row_offsets, int32_t* status) {
   for (int64_t i = begin + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < end;
        i += int64_t(gridDim.x) * blockDim.x) {
     int64_t cnt = 0;
-    for_each_neighbor(pos, i, box, rc2, n, cell_start, cell_atoms, [&](int32_t) { ++cnt; });
+    if (!for_each_neighbor(pos, i, box, rc2, n, zb, zc, cell_start, cell_atoms, [&](int32_t) { ++cnt; }) &&
+        status)
+      atomicOr(status, Y3B_STATUS_INDEX_RANGE);
     row_offsets[i - begin + 1] = cnt;
     if (i == begin) row_offsets[0] = 0;
   }
 }
 
 __global__ void fill_neighbors_kernel(const double* __restrict__ pos, int64_t begin, int64_t end,
-                                      double box, double rc2, int n,
+                                      double box, double rc2, int n, int zb, int zc,
                                       const int64_t* __restrict__ cell_start,
                                       const int32_t* __restrict__ cell_atoms,
-                                      const int64_t* __restrict__ row_offsets,
-                                      int32_t* __restrict__ nbr) {
+                                      const int64_t* __restrict__ row_offsets, int64_t capacity,
+                                      int32_t* __restrict__ nbr, int32_t* status) {
   for (int64_t i = begin + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < end;
        i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t b = row_offsets[i - begin], e = row_offsets[i - begin + 1];
+    const int64_t b = row_offsets[i - begin];
+    int64_t e = row_offsets[i - begin + 1];
+    if (e > capacity) {
+      if (status) atomicOr(status, Y3B_STATUS_CAPACITY);
+      e = capacity;
+    }
     int64_t k = b;
-    for_each_neighbor(pos, i, box, rc2, n, cell_start, cell_atoms, [&](int32_t j) {
+    for_each_neighbor(pos, i, box, rc2, n, zb, zc, cell_start, cell_atoms, [&](int32_t j) {
       if (k < e) nbr[k] = j;
       ++k;
     });
@@ -186,29 +217,44 @@ extern "C" int64_t y3b_neighbor_workspace_bytes(int64_t atom_count, double box, 
   return carve_cells(nullptr, atom_count, n * n * n).bytes;
 }
 
-extern "C" int y3b_neighbor_count(const double* positions, int64_t atom_count, int64_t center_begin,
-                                  int64_t center_end, double box, double cutoff, void* workspace,
-                                  int64_t workspace_bytes, int64_t* row_offsets, void* stream) {
+namespace {
+
+// z window of the cell list: zc >= n (or a box of fewer than 3 cells) bins the
+// whole box.
+void clamp_window(int n, int64_t z_begin, int64_t z_count, int& zb, int& zc) {
+  if (z_count <= 0 || z_count >= n || n < 3) {
+    zb = 0;
+    zc = n;
+  } else {
+    zb = int(((z_begin % n) + n) % n);
+    zc = int(z_count);
+  }
+}
+
+int neighbor_count_impl(const double* positions, int64_t atom_count, int64_t center_begin, int64_t center_end,
+                        double box, double cutoff, int64_t z_begin, int64_t z_count, void* workspace,
+                        int64_t workspace_bytes, int64_t* row_offsets, int32_t* status, cudaStream_t s) {
   Y3B_CHECK_ARG(atom_count >= 0 && atom_count < (int64_t(1) << 31), "atom count out of range");
   Y3B_CHECK_ARG(0 <= center_begin && center_begin <= center_end && center_end <= atom_count,
                 "bad centre range [%lld, %lld)", (long long)center_begin, (long long)center_end);
   Y3B_CHECK_ARG(box > 0 && cutoff > 0, "box and cutoff must be positive");
   Y3B_CHECK_ARG(row_offsets != nullptr, "null row_offsets");
-  cudaStream_t s = as_stream(stream);
   if (center_end == center_begin) {
     Y3B_CUDA_TRY(cudaMemsetAsync(row_offsets, 0, 8, s));
     return Y3B_OK;
   }
   Y3B_CHECK_ARG(positions != nullptr, "null positions");
   const int n = cells_per_side(box, cutoff);
-  const int64_t nc = int64_t(n) * n * n;
+  int zb = 0, zc = n;
+  clamp_window(n, z_begin, z_count, zb, zc);
+  const int64_t nc = int64_t(zc) * n * n;
   const CellWorkspace w = carve_cells(workspace, atom_count, nc);
   Y3B_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "neighbour workspace too small: need %lld",
                 (long long)w.bytes);
   Y3B_CUDA_TRY(cudaMemsetAsync(w.cell_start, 0, (nc + 1) * 8, s));
   Y3B_CUDA_TRY(cudaMemsetAsync(w.cursor, 0, nc * 4, s));
   assign_cells_kernel<<<grid_for(atom_count, 256), 256, 0, s>>>(
-      positions, atom_count, box, n, w.atom_cell, reinterpret_cast<unsigned long long*>(w.cell_start));
+      positions, atom_count, box, n, zb, zc, w.atom_cell, reinterpret_cast<unsigned long long*>(w.cell_start));
   Y3B_LAUNCH_CHECK();
   scan_i64_kernel<<<1, 1024, 0, s>>>(w.cell_start, nc + 1);
   Y3B_LAUNCH_CHECK();
@@ -219,30 +265,70 @@ extern "C" int y3b_neighbor_count(const double* positions, int64_t atom_count, i
   Y3B_LAUNCH_CHECK();
   const int64_t count = center_end - center_begin;
   count_neighbors_kernel<<<grid_for(count, 128), 128, 0, s>>>(
-      positions, center_begin, center_end, box, cutoff * cutoff, n, w.cell_start, w.cell_atoms,
-      row_offsets);
+      positions, center_begin, center_end, box, cutoff * cutoff, n, zb, zc, w.cell_start, w.cell_atoms,
+      row_offsets, status);
   Y3B_LAUNCH_CHECK();
   scan_i64_kernel<<<1, 1024, 0, s>>>(row_offsets, count + 1);
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }
 
-extern "C" int y3b_neighbor_fill(const double* positions, int64_t atom_count, int64_t center_begin,
-                                 int64_t center_end, double box, double cutoff, const void* workspace,
-                                 int64_t workspace_bytes, const int64_t* row_offsets, int32_t* neighbors,
-                                 void* stream) {
+int neighbor_fill_impl(const double* positions, int64_t atom_count, int64_t center_begin, int64_t center_end,
+                       double box, double cutoff, int64_t z_begin, int64_t z_count, const void* workspace,
+                       int64_t workspace_bytes, const int64_t* row_offsets, int64_t capacity, int32_t* neighbors,
+                       int32_t* status, cudaStream_t s) {
   Y3B_CHECK_ARG(0 <= center_begin && center_begin <= center_end && center_end <= atom_count,
                 "bad centre range");
   if (center_end == center_begin) return Y3B_OK;
   Y3B_CHECK_ARG(positions && row_offsets && neighbors, "null pointer argument");
+  Y3B_CHECK_ARG(capacity >= 0, "negative neighbour capacity");
   const int n = cells_per_side(box, cutoff);
-  const int64_t nc = int64_t(n) * n * n;
+  int zb = 0, zc = n;
+  clamp_window(n, z_begin, z_count, zb, zc);
+  const int64_t nc = int64_t(zc) * n * n;
   const CellWorkspace w = carve_cells(const_cast<void*>(workspace), atom_count, nc);
   Y3B_CHECK_ARG(workspace && workspace_bytes >= w.bytes, "neighbour workspace too small");
   const int64_t count = center_end - center_begin;
-  fill_neighbors_kernel<<<grid_for(count, 128), 128, 0, as_stream(stream)>>>(
-      positions, center_begin, center_end, box, cutoff * cutoff, n, w.cell_start, w.cell_atoms,
-      row_offsets, neighbors);
+  fill_neighbors_kernel<<<grid_for(count, 128), 128, 0, s>>>(
+      positions, center_begin, center_end, box, cutoff * cutoff, n, zb, zc, w.cell_start, w.cell_atoms,
+      row_offsets, capacity, neighbors, status);
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }
+
+}  // namespace
+
+extern "C" int y3b_neighbor_count(const double* positions, int64_t atom_count, int64_t center_begin,
+                                  int64_t center_end, double box, double cutoff, void* workspace,
+                                  int64_t workspace_bytes, int64_t* row_offsets, void* stream) {
+  return neighbor_count_impl(positions, atom_count, center_begin, center_end, box, cutoff, 0, 0, workspace,
+                             workspace_bytes, row_offsets, nullptr, as_stream(stream));
+}
+
+extern "C" int y3b_neighbor_fill(const double* positions, int64_t atom_count, int64_t center_begin,
+                                 int64_t center_end, double box, double cutoff, const void* workspace,
+                                 int64_t workspace_bytes, const int64_t* row_offsets, int32_t* neighbors,
+                                 void* stream) {
+  return neighbor_fill_impl(positions, atom_count, center_begin, center_end, box, cutoff, 0, 0, workspace,
+                            workspace_bytes, row_offsets, INT64_MAX, neighbors, nullptr, as_stream(stream));
+}
+
+extern "C" int y3b_neighbor_count_window(const double* positions, int64_t atom_count, int64_t center_begin,
+                                         int64_t center_end, double box, double cutoff, int64_t z_cell_begin,
+                                         int64_t z_cell_count, void* workspace, int64_t workspace_bytes,
+                                         int64_t* row_offsets, int32_t* status, void* stream) {
+  return neighbor_count_impl(positions, atom_count, center_begin, center_end, box, cutoff, z_cell_begin,
+                             z_cell_count, workspace, workspace_bytes, row_offsets, status, as_stream(stream));
+}
+
+extern "C" int y3b_neighbor_fill_window(const double* positions, int64_t atom_count, int64_t center_begin,
+                                        int64_t center_end, double box, double cutoff, int64_t z_cell_begin,
+                                        int64_t z_cell_count, const void* workspace, int64_t workspace_bytes,
+                                        const int64_t* row_offsets, int64_t neighbor_capacity,
+                                        int32_t* neighbors, int32_t* status, void* stream) {
+  return neighbor_fill_impl(positions, atom_count, center_begin, center_end, box, cutoff, z_cell_begin,
+                            z_cell_count, workspace, workspace_bytes, row_offsets, neighbor_capacity, neighbors,
+                            status, as_stream(stream));
+}
+
+extern "C" int64_t y3b_neighbor_cells_per_side(double box, double cutoff) { return cells_per_side(box, cutoff); }

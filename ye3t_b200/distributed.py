@@ -3,9 +3,11 @@
 Each atom's A- and B-basis depend only on its own neighbour row, so rank r of
 P evaluates the centres ``[r N / P, (r + 1) N / P)`` from the replicated
 positions; the collectives are sums of the per-rank energies and, with forces,
-of the per-rank partial force arrays (each rank scatters its rows' edge
-gradients into a full ``[N, 3]`` array).  The reference has no distributed
-code; this is new.
+a reduce-scatter of the per-rank partial force arrays (each rank scatters its
+rows' edge gradients into a full ``[N, 3]`` array and keeps the summed forces
+of its own block).  With atoms stored in cell order a block is a slab of the
+box, and each rank bins only its slab and a one-cell halo for its neighbour
+lists.  The reference has no distributed code; this is new.
 """
 
 from __future__ import annotations
@@ -17,7 +19,7 @@ from typing import Tuple
 import torch
 import torch.distributed as dist
 
-__all__ = ["atom_block", "init_from_env", "sum_over_ranks", "max_over_ranks"]
+__all__ = ["atom_block", "init_from_env", "sum_over_ranks", "max_over_ranks", "block_forces"]
 
 
 def atom_block(rank: int, world: int, atom_count: int) -> Tuple[int, int]:
@@ -51,3 +53,23 @@ def max_over_ranks(x: float, device) -> float:
     if dist.is_initialized() and dist.get_world_size() > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def block_forces(partial: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """Sum the ranks' partial force arrays ``partial [P * chunk, 3]`` and keep this rank's
+    ``chunk`` rows in ``out [chunk, 3]`` (a reduce-scatter; on a backend without one,
+    such as gloo on CPU, an all-reduce and a slice give the same rows)."""
+    if not (dist.is_initialized() and dist.get_world_size() > 1):
+        out.copy_(partial[:out.shape[0]])
+        return out
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if partial.shape[0] != world * out.shape[0]:
+        raise ValueError("partial forces must hold world_size * chunk rows")
+    if dist.get_backend() == "nccl":
+        dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM)
+    else:
+        full = partial.clone()
+        dist.all_reduce(full, op=dist.ReduceOp.SUM)
+        out.copy_(full[rank * out.shape[0]:(rank + 1) * out.shape[0]])
+    return out
+
