@@ -537,10 +537,18 @@ typedef struct {
   int32_t pass_count;        /* equal to the symmetric tables' */
   int64_t tile_count;
   int64_t step_count;
+  int64_t item_count;
   const int32_t* tile_begin;     /* [pass_count + 1] */
   const int32_t* tile_row;       /* [tile_count, rows]: local component of the row's M = 0, or -1 */
   const int32_t* tile_col_begin; /* [tile_count + 1], multiples of 4 */
   const int32_t* col_comp;       /* [step_count], 16-byte aligned */
+  /* back-propagation work items: per pass, chunks (t, q0, q1, 0) of the
+   * A-row entries' lists in the symmetric tables; each entry adds its items'
+   * partial sums in the order t_item lists them */
+  const int32_t* bp_item_begin;  /* [pass_count + 1] */
+  const int32_t* bp_item;        /* [item_count, 4], 16-byte aligned */
+  const int32_t* t_item_begin;   /* [pass_count * row_width + 1] */
+  const int32_t* t_item;         /* [item_count]: item index within its pass */
   const double* kval;            /* [species_count, rows * step_count], 16-byte aligned */
 } y3b_recoupled_tile_tables;
 

@@ -617,3 +617,32 @@ def test_tiled_device_source_emulated_matches_oracle(emulated, plan5, physical_c
     st.zero_()
     ev.energy_grad(torch.as_tensor(A), torch.as_tensor(species), status=st)
     assert int(st.item()) & _native.STATUS_TABLE
+
+
+@pytest.mark.parametrize("stem", ["ace_diag_l4_nu4_L0", "nu2"])
+def test_tiled_device_source_emulated_small_rows(emulated, stem, monkeypatch):
+    """The tiled adjoint on rows of 25 entries (l_max 4, intermediate L up to 8) and on the
+    nu <= 2 words of the n_max 8 set (passes smaller than the row), emulated through the real
+    bindings, against the oracle."""
+    import torch
+    from oracle import oracle
+    from ye3t_b200.recoupling import RecoupledEvaluator
+    _bind_emulated(emulated, monkeypatch, ["y3b_ace_recoupled_energy_grad_tiled"])
+    if stem == "nu2":
+        b = _sub_bundle(_bundle("ace_n8_l3_nu3_L0"), lambda w: len(w) <= 2)
+        nmax, lmax, S = 8, 3, 3
+    else:
+        b = _bundle(stem)
+        nmax, lmax, S = 1, 4, 2
+    plan = build_recoupled_plan(b)
+    rng = np.random.default_rng(61)
+    A = _physical(rng, 6, nmax, lmax)
+    species = rng.integers(0, S, 6).astype(np.int32)
+    w = rng.normal(size=(S, b.feature_count))
+    e0, G0 = oracle.bundle_energy_grad(b, A, species, w, threads=2)
+    ev = RecoupledEvaluator(b, "cpu", w, plan=plan, threads_per_cta=256, symmetric=True, tile_rows=8)
+    st = torch.zeros(1, dtype=torch.int32)
+    e, G = ev.energy_grad(torch.as_tensor(A), torch.as_tensor(species), status=st)
+    assert int(st.item()) == 0
+    assert np.abs(e.numpy() - e0).max() <= 1e-12 * np.abs(e0).max()
+    assert np.abs(G.numpy() - G0).max() <= 1e-12 * np.abs(G0).max()

@@ -81,8 +81,9 @@ class RecoupledTileTables(ctypes.Structure):
     """``y3b_recoupled_tile_tables`` (include/ye3t_b200.h)."""
 
     _fields_ = [
-        ("rows", I32), ("pass_count", I32), ("tile_count", I64), ("step_count", I64),
-        ("tile_begin", VP), ("tile_row", VP), ("tile_col_begin", VP), ("col_comp", VP), ("kval", VP),
+        ("rows", I32), ("pass_count", I32), ("tile_count", I64), ("step_count", I64), ("item_count", I64),
+        ("tile_begin", VP), ("tile_row", VP), ("tile_col_begin", VP), ("col_comp", VP),
+        ("bp_item_begin", VP), ("bp_item", VP), ("t_item_begin", VP), ("t_item", VP), ("kval", VP),
     ]
 
 

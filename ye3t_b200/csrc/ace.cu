@@ -8,32 +8,41 @@ namespace y3b {
 
 constexpr int kMaxNmax = 16;
 
-// Warps per CTA of the density kernel, sized to keep its static shared memory
-// under 48 KB.
-template <int LMAX>
-struct DensityWarps {
-  static constexpr int value = LMAX >= 3 ? 2 : 4;
-};
+// Radial table size the density kernels are instantiated for: the smallest
+// of 8, 12, 16 that holds nmax, so that the radial values stay in registers
+// (the runtime nmax <= NMAXT selects the outputs).
+inline int radial_table_size(int64_t nmax) { return nmax <= 8 ? 8 : (nmax <= 12 ? 12 : 16); }
 
 // ---------------------------------------------------------------------------
-// Kernel 1: A-basis density.  One warp per centre atom.  Pass 1: lanes over
-// up to 32 edges of the row compute p[z_j] R_n(r) and Yc_lm(r_hat) into
-// warp-private shared memory.  Pass 2: lanes over the nmax*(lmax+1)^2 outputs
-// accumulate those edges in CSR order.  A is written once per atom with
-// coalesced stores; no atomics.
+// Kernel 1: A-basis density.  One warp per centre atom, DensityWarps warps per
+// CTA.  Pass 1: lanes over up to 32 edges of the row compute p[z_j] R_n(r)
+// (n = 1..NMAXT) and the complex harmonics Yc_lm(r_hat) into warp-private
+// shared memory.  Pass 2: lane (lm, g) owns one harmonic column lm and the
+// radial channels n = g, g + G, ... (G = 32 / W lane groups): per edge it
+// reads its harmonic once and its radial values, and accumulates in CSR
+// order.  A is written once per atom; no atomics.
 // ---------------------------------------------------------------------------
-template <int LMAX>
-__global__ void __launch_bounds__(32 * DensityWarps<LMAX>::value) ace_density_kernel(
+template <int LMAX, int NMAXT>
+struct DensityWarps {  // up to 4 warps within 48 KB of static shared memory
+  static constexpr int kPerWarp = 32 * ((NMAXT + 1) * 8 + ((LMAX + 1) * (LMAX + 1) + 1) * 16);
+  static constexpr int value = 4 * kPerWarp <= 48 * 1024 ? 4 : (2 * kPerWarp <= 48 * 1024 ? 2 : 1);
+};
+
+template <int LMAX, int NMAXT>
+__global__ void __launch_bounds__(32 * DensityWarps<LMAX, NMAXT>::value) ace_density_kernel(
     const double* __restrict__ pos, const int32_t* __restrict__ species, int64_t N,
     int64_t center_begin, int64_t count, double box, const int64_t* __restrict__ row_off,
     const int32_t* __restrict__ nbr, const double* __restrict__ pref, int64_t S, int nmax,
     double rc, double lam, ShNorm nrm, double2* __restrict__ A, int32_t* status) {
   constexpr int W = (LMAX + 1) * (LMAX + 1);
-  constexpr int kOutPerLane = (kMaxNmax * W + 31) / 32;
-  constexpr int kDensityWarps = DensityWarps<LMAX>::value;
-  __shared__ double s_rad[kDensityWarps][32][kMaxNmax + 1];
-  __shared__ double2 s_y[kDensityWarps][32][W];
+  constexpr int G = W <= 16 ? 32 / W : 1;                 // lane groups over the radial channels
+  constexpr int NPL = (NMAXT + G - 1) / G;                // radial channels per lane
+  constexpr int kDensityWarps = DensityWarps<LMAX, NMAXT>::value;
+  __shared__ double s_rad[kDensityWarps][32][NMAXT + 1];  // +1: conflict-free pass-1 stores
+  __shared__ double2 s_y[kDensityWarps][32][W + 1];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int lm = lane % W, grp = lane / W;
+  const bool owner = lane < G * W;
   const int nout = nmax * W;
   const int64_t row0 = row_off[0];
   const int64_t warp = blockIdx.x * int64_t(kDensityWarps) + wib;
@@ -41,19 +50,20 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX>::value) ace_density_ke
   for (int64_t a = warp; a < count; a += nwarps) {
     const int64_t i = center_begin + a;
     const int64_t b = row_off[a] - row0, e = row_off[a + 1] - row0;
-    double2 acc[kOutPerLane];
+    double2 acc[NPL];
 #pragma unroll
-    for (int k = 0; k < kOutPerLane; ++k) acc[k] = make_double2(0.0, 0.0);
+    for (int k = 0; k < NPL; ++k) acc[k] = make_double2(0.0, 0.0);
     for (int64_t c0 = b; c0 < e; c0 += 32) {
       const int nedge = (e - c0) < 32 ? int(e - c0) : 32;
       if (lane < nedge) {
         const int64_t j = nbr[c0 + lane];
-        double rv[kMaxNmax + 1];
+        double rv[NMAXT + 1];
         double2 yc[W];
         double p = 0.0;
         if (j < 0 || j >= N) {
           if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
-          for (int k = 0; k <= nmax; ++k) rv[k] = 0.0;
+#pragma unroll
+          for (int k = 0; k <= NMAXT; ++k) rv[k] = 0.0;
 #pragma unroll
           for (int k = 0; k < W; ++k) yc[k] = make_double2(0.0, 0.0);
         } else {
@@ -62,7 +72,7 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX>::value) ace_density_ke
           const double r = sqrt(dist2(d));
           const int zj = species[j];
           p = (zj >= 0 && zj < S) ? pref[zj] : 0.0;
-          radial_basis<double>(r, rc, lam, nmax, rv, nullptr);
+          radial_basis<double>(r, rc, lam, NMAXT, rv, nullptr);
           const double sr = r > 1e-12 ? r : 1e-12;
           double v[W];
           real_sh_unit<double, LMAX>(d[0] / sr, d[1] / sr, d[2] / sr, nrm, v, nullptr);
@@ -79,31 +89,35 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX>::value) ace_density_ke
             }
           }
         }
-        for (int n = 0; n < nmax; ++n) s_rad[wib][lane][n] = p * rv[n + 1];
+#pragma unroll
+        for (int n = 0; n < NMAXT; ++n) s_rad[wib][lane][n] = p * rv[n + 1];
 #pragma unroll
         for (int k = 0; k < W; ++k) s_y[wib][lane][k] = yc[k];
       }
       __syncwarp();
-      for (int q = 0; q < nedge; ++q) {
+      if (owner) {
+        for (int q = 0; q < nedge; ++q) {
+          const double2 y = s_y[wib][q][lm];
 #pragma unroll
-        for (int k = 0; k < kOutPerLane; ++k) {
-          const int o = lane + 32 * k;
-          if (o < nout) {
-            const int n = o / W, lm = o - n * W;
-            const double rp = s_rad[wib][q][n];
-            const double2 y = s_y[wib][q][lm];
-            acc[k].x += rp * y.x;
-            acc[k].y += rp * y.y;
+          for (int k = 0; k < NPL; ++k) {
+            const int n = grp + G * k;
+            if (n < NMAXT) {
+              const double rp = s_rad[wib][q][n];
+              acc[k].x += rp * y.x;
+              acc[k].y += rp * y.y;
+            }
           }
         }
       }
       __syncwarp();
     }
-    double2* Ai = A + a * int64_t(nout);
+    if (owner) {
+      double2* Ai = A + a * int64_t(nout);
 #pragma unroll
-    for (int k = 0; k < kOutPerLane; ++k) {
-      const int o = lane + 32 * k;
-      if (o < nout) Ai[o] = acc[k];
+      for (int k = 0; k < NPL; ++k) {
+        const int n = grp + G * k;
+        if (n < nmax) Ai[n * W + lm] = acc[k];
+      }
     }
   }
 }
@@ -478,17 +492,20 @@ extern "C" int y3b_ace_density(const double* positions, const int32_t* species, 
   Y3B_CHECK_ARG(positions && species && row_offsets && species_prefactor && A, "null pointer argument");
   const ShNorm nrm = make_sh_norm();
   cudaStream_t s = as_stream(stream);
-#define Y3B_DENSITY_CASE(L)                                                                     \
-  case L:                                                                                       \
-    ace_density_kernel<L><<<int(std::min<int64_t>((center_count + DensityWarps<L>::value - 1) / \
-                                                      DensityWarps<L>::value,                   \
-                                                  int64_t(kSMs) * 128)),                        \
-                            32 * DensityWarps<L>::value, 0, s>>>(positions, species, atom_count, center_begin, \
-                                                   center_count, box, row_offsets, neighbors,    \
-                                                   species_prefactor, species_count, int(nmax),  \
-                                                   cutoff, lambda, nrm,                          \
-                                                   static_cast<double2*>(A), status);            \
+#define Y3B_DENSITY_LAUNCH(L, NT)                                                                    \
+  ace_density_kernel<L, NT><<<int(std::min<int64_t>((center_count + DensityWarps<L, NT>::value - 1) /      \
+                                                        DensityWarps<L, NT>::value,                        \
+                                                    int64_t(kSMs) * 128)),                                 \
+                              32 * DensityWarps<L, NT>::value, 0, s>>>(                                    \
+      positions, species, atom_count, center_begin, center_count, box, row_offsets, neighbors,            \
+      species_prefactor, species_count, int(nmax), cutoff, lambda, nrm, static_cast<double2*>(A), status)
+#define Y3B_DENSITY_CASE(L)                                                                            \
+  case L:                                                                                              \
+    if (nt == 8) Y3B_DENSITY_LAUNCH(L, 8);                                                             \
+    else if (nt == 12) Y3B_DENSITY_LAUNCH(L, 12);                                                      \
+    else Y3B_DENSITY_LAUNCH(L, 16);                                                                    \
     break;
+  const int nt = radial_table_size(nmax);
   switch (lmax) {
     Y3B_DENSITY_CASE(0)
     Y3B_DENSITY_CASE(1)
@@ -498,6 +515,7 @@ extern "C" int y3b_ace_density(const double* positions, const int32_t* species, 
     default:
       return fail(Y3B_ERR_UNSUPPORTED, "ace_density: lmax %lld not built (0..4)", (long long)lmax);
   }
+#undef Y3B_DENSITY_LAUNCH
 #undef Y3B_DENSITY_CASE
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;

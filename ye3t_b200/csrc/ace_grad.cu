@@ -988,24 +988,28 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
 // ---------------------------------------------------------------------------
 // Edge gradients: one warp per centre i; lanes over its edges.  With
 // A[n, lm] = sum_j p_j R_n(r) Yc_lm(d),  g_e = dE_i/dd_e =
-//   p_j ( d_hat sum_n R'_n Re(sum_lm G[n,lm] Yc_lm) + sum_n R_n Re(sum_lm G[n,lm] grad Yc_lm) ).
+//   p_j ( d_hat sum_lm Re(Q_lm Yc_lm) + sum_lm Re(P_lm grad Yc_lm) ),
+//   P_lm = sum_n R_n G[n, lm],  Q_lm = sum_n R'_n G[n, lm].
+// The radial table is instantiated at NMAXT >= nmax entries (G is zero
+// beyond nmax in shared memory), so radial values and derivatives stay in
+// registers; P and Q are formed per harmonic column and used at once.
 // ---------------------------------------------------------------------------
-constexpr int kEdgeWarps = 2;
+constexpr int kEdgeWarps = 4;
 
-template <int LMAX>
+template <int LMAX, int NMAXT>
 __global__ void __launch_bounds__(32 * kEdgeWarps) ace_edge_grad_kernel(
     const double* __restrict__ pos, const int32_t* __restrict__ species, int64_t N, int64_t center_begin,
     int64_t count, double box, const int64_t* __restrict__ row_off, const int32_t* __restrict__ nbr,
     const double* __restrict__ pref, int64_t S, int nmax, double rc, double lam, ShNorm nrm,
     const double2* __restrict__ dEdA, double* __restrict__ edge_grad, int32_t* status) {
   constexpr int W = (LMAX + 1) * (LMAX + 1);
-  __shared__ double2 sG[kEdgeWarps][16 * W];
+  __shared__ double2 sG[kEdgeWarps][NMAXT * W];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int na = nmax * W;
   const int64_t row0 = row_off[0];
   for (int64_t c = blockIdx.x * int64_t(kEdgeWarps) + wib; c < count; c += int64_t(gridDim.x) * kEdgeWarps) {
     const int64_t i = center_begin + c;
-    for (int k = lane; k < na; k += 32) sG[wib][k] = dEdA[c * na + k];
+    for (int k = lane; k < NMAXT * W; k += 32) sG[wib][k] = k < na ? dEdA[c * na + k] : make_double2(0.0, 0.0);
     __syncwarp();
     const int64_t b = row_off[c] - row0, e_end = row_off[c + 1] - row0;
     for (int64_t e = b + lane; e < e_end; e += 32) {
@@ -1019,8 +1023,8 @@ __global__ void __launch_bounds__(32 * kEdgeWarps) ace_edge_grad_kernel(
         const double r = sqrt(dist2(d));
         const int zj = species[j];
         const double p = (zj >= 0 && zj < S) ? pref[zj] : 0.0;
-        double rv[17], rd[17];
-        radial_basis<double>(r, rc, lam, nmax, rv, rd);
+        double rv[NMAXT + 1], rd[NMAXT + 1];
+        radial_basis<double>(r, rc, lam, NMAXT, rv, rd);
         const double eps = 1e-12;
         const double sr = r > eps ? r : eps;
         const double u[3] = {d[0] / sr, d[1] / sr, d[2] / sr};
@@ -1073,13 +1077,18 @@ __global__ void __launch_bounds__(32 * kEdgeWarps) ace_edge_grad_kernel(
               }
             }
             const int lm = cidx + m;
-            for (int n = 0; n < nmax; ++n) {
-              const double2 G = sG[wib][n * W + lm];
-              acc_r += rd[n + 1] * (G.x * yr - G.y * yi);
-              const double Rn = rv[n + 1];
+            double2 P = make_double2(0.0, 0.0), Q = make_double2(0.0, 0.0);
 #pragma unroll
-              for (int ax = 0; ax < 3; ++ax) acc_v[ax] += Rn * (G.x * dr[ax] - G.y * di[ax]);
+            for (int n = 0; n < NMAXT; ++n) {
+              const double2 Gv = sG[wib][n * W + lm];
+              P.x = fma(rv[n + 1], Gv.x, P.x);
+              P.y = fma(rv[n + 1], Gv.y, P.y);
+              Q.x = fma(rd[n + 1], Gv.x, Q.x);
+              Q.y = fma(rd[n + 1], Gv.y, Q.y);
             }
+            acc_r += Q.x * yr - Q.y * yi;
+#pragma unroll
+            for (int ax = 0; ax < 3; ++ax) acc_v[ax] += P.x * dr[ax] - P.y * di[ax];
           }
         }
         gx = p * (acc_r * u[0] + acc_v[0]);
@@ -1224,12 +1233,16 @@ extern "C" int y3b_ace_edge_grad(const double* positions, const int32_t* species
   const ShNorm nrm = make_sh_norm();
   const int grid = int(std::min<int64_t>((center_count + kEdgeWarps - 1) / kEdgeWarps, int64_t(kSMs) * 64));
   cudaStream_t s = as_stream(stream);
+#define Y3B_EDGE_LAUNCH(L, NT)                                                                              \
+  ace_edge_grad_kernel<L, NT><<<grid, 32 * kEdgeWarps, 0, s>>>(                                             \
+      positions, species, atom_count, center_begin, center_count, box, row_offsets, neighbors,              \
+      species_prefactor, species_count, int(nmax), cutoff, lambda, nrm, static_cast<const double2*>(dEdA),   \
+      edge_grad, status)
 #define Y3B_EDGE_CASE(L)                                                                                    \
   case L:                                                                                                   \
-    ace_edge_grad_kernel<L><<<grid, 32 * kEdgeWarps, 0, s>>>(                                               \
-        positions, species, atom_count, center_begin, center_count, box, row_offsets, neighbors,            \
-        species_prefactor, species_count, int(nmax), cutoff, lambda, nrm, static_cast<const double2*>(dEdA), \
-        edge_grad, status);                                                                                  \
+    if (nmax <= 8) Y3B_EDGE_LAUNCH(L, 8);                                                                   \
+    else if (nmax <= 12) Y3B_EDGE_LAUNCH(L, 12);                                                            \
+    else Y3B_EDGE_LAUNCH(L, 16);                                                                            \
     break;
   switch (lmax) {
     Y3B_EDGE_CASE(0)
@@ -1240,6 +1253,7 @@ extern "C" int y3b_ace_edge_grad(const double* positions, const int32_t* species
     default:
       return fail(Y3B_ERR_UNSUPPORTED, "ace_edge_grad: lmax %lld not built (0..4)", (long long)lmax);
   }
+#undef Y3B_EDGE_LAUNCH
 #undef Y3B_EDGE_CASE
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;

@@ -41,6 +41,7 @@ __device__ __forceinline__ void radial_basis(R r, R rc_in, R lam, int kmax, R* v
   const R eps = sizeof(R) == 8 ? R(2.220446049250313e-16) : R(1.1920929e-07);
   const R rc = rc_in > eps ? rc_in : eps;
   const R s = r / rc;
+#pragma unroll
   for (int k = 0; k <= kmax; ++k) {
     val[k] = R(0);
     if (der) der[k] = R(0);
@@ -70,6 +71,7 @@ __device__ __forceinline__ void radial_basis(R r, R rc_in, R lam, int kmax, R* v
   const R x = R(1) - R(2) * em / den;
   const R dx = R(2) * lam * exp(arg) / (den * rc);
   R t0 = R(1), t1 = x, u0 = R(1), u1 = R(2) * x;
+#pragma unroll
   for (int k = 2; k <= kmax; ++k) {
     const R t2 = R(2) * x * t1 - t0;
     t0 = t1;

@@ -633,17 +633,64 @@ recoupled_sym_energy_kernel(SymTabs t, const double2* __restrict__ A, int64_t at
 // Dense tiles of the symmetric pass's contraction weights (RecoupledTiles).
 struct TileTabs {
   int32_t rows, pass_count;
-  int64_t tile_count, step_count;
+  int64_t tile_count, step_count, item_count;
   const int32_t* tile_begin;
   const int32_t* tile_row;
   const int32_t* tile_col_begin;
   const int32_t* col_comp;
+  const int32_t* bp_item_begin;
+  const int4* bp_item;
+  const int32_t* t_item_begin;
+  const int32_t* t_item;
   const double* kval;
 };
 
 inline TileTabs tile_view(const y3b_recoupled_tile_tables& t) {
-  return TileTabs{t.rows, t.pass_count, t.tile_count, t.step_count, t.tile_begin, t.tile_row, t.tile_col_begin,
-                  t.col_comp, t.kval};
+  return TileTabs{t.rows, t.pass_count, t.tile_count, t.step_count, t.item_count, t.tile_begin, t.tile_row,
+                  t.tile_col_begin, t.col_comp, t.bp_item_begin, reinterpret_cast<const int4*>(t.bp_item),
+                  t.t_item_begin, t.t_item, t.kval};
+}
+
+// Step 1 of the tiled adjoint with lanes as (component, atom): a warp builds
+// 32 / NA consecutive components for its NA atoms at a time, so each table
+// entry it loads serves NA lanes and its A-row reads are whole [entry][NA]
+// rows.
+template <int NA, int TH>
+__device__ __forceinline__ void build_components_lanes(const SymTabs& t, const double2* sA, double2* sI, int c0,
+                                                       int nc, int W, bool& bad) {
+  constexpr int R = 32 / NA;
+  constexpr int NW = TH / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int a = lane % NA;
+  for (int g = warp; g * R < nc; g += NW) {
+    const int c = g * R + lane / NA;
+    if (c >= nc) continue;
+    const int4 d = __ldg(t.comp + 2 * (c0 + c));
+    double2 v = make_double2(d.x < 0 ? 1.0 : 0.0, 0.0);
+    if (d.x < 0) {
+    } else if (d.w == 0) {
+      if (d.x < W)
+        v = sA[d.x * NA + a];
+      else
+        bad = true;
+    } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
+      bad = true;
+    } else {
+      for (int q = d.z; q < d.z + d.w; ++q) {
+        const int ix = __ldg(t.cg_index + q);
+        const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
+        if (ia >= W || ib < 0 || ib >= W) {
+          bad = true;
+          continue;
+        }
+        const double cv = __ldg(t.cg_value + q);
+        const double2 p = rmul(sA[ia * NA + a], sA[ib * NA + a]);
+        v.x = fma(cv, p.x, v.x);
+        v.y = fma(cv, p.y, v.y);
+      }
+    }
+    sI[c * NA + a] = v;
+  }
 }
 
 // Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1: the warp's
@@ -785,7 +832,7 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
         bad = true;  // uniform over the block
         continue;
       }
-      build_components<NA, TH>(t, sA, sI, c0, nc, W, bad);
+      build_components_lanes<NA, TH>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       switch (L) {
         case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
@@ -799,53 +846,68 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
         default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
       }
       __syncthreads();
-      const int P = (2 * W <= TH && (TH / W) * W <= cw) ? TH / W : 1;  // uniform
-      double2* part = sI;  // [P][W][NA]; step 2 is done with sI
-      for (int u = tid; u < W * P; u += TH) {
-        const int i = u % W, pi = u / W;
-        const int64_t at = int64_t(L) * W + i;
-        const int b0 = t.bp_begin[at], b1 = t.bp_begin[at + 1];
-        double2 ga[NA];
-#pragma unroll
-        for (int a = 0; a < NA; ++a) ga[a] = make_double2(0.0, 0.0);
-        if (b0 < 0 || b1 < b0 || int64_t(b1) > t.bp_count) {
-          bad = true;
+      // 3. back-propagation: lanes (work item, atom) sum their item's chunk of an
+      //    A-row entry's list into a part (the component buffer is free now); each
+      //    entry then adds its parts in the order t_item lists them
+      {
+        constexpr int R = 32 / NA;
+        constexpr int NW = TH / 32;
+        const int warp = tid >> 5;
+        const int i0 = tt.bp_item_begin[L], i1 = tt.bp_item_begin[L + 1];
+        const int ni = i1 - i0;
+        double2* part = sI;  // [ni][NA]
+        if (i0 < 0 || ni < 0 || ni > cw || int64_t(i1) > tt.item_count) {
+          bad = true;  // uniform over the block
         } else {
-          const int len = b1 - b0;
-          const int q0 = b0 + (len * pi) / P, q1 = b0 + (len * (pi + 1)) / P;
-          for (int q = q0; q < q1; ++q) {
-            const int code = __ldg(t.bp_gi + q);
-            const int gi = code >> 1;
-            const int o = __ldg(t.bp_other + q);
-            if (code < 0 || gi >= nc || o >= W) {
+          for (int g = warp; g * R < ni; g += NW) {
+            const int it = g * R + lane / NA;
+            if (it >= ni) continue;
+            const int4 w = __ldg(tt.bp_item + i0 + it);  // (t, q0, q1, 0)
+            double2 ga = make_double2(0.0, 0.0);
+            if (w.x < 0 || w.x >= W || w.y < 0 || w.z < w.y || int64_t(w.z) > t.bp_count) {
               bad = true;
-              continue;
+            } else {
+              for (int q = w.y; q < w.z; ++q) {
+                const int code = __ldg(t.bp_gi + q);
+                const int gi = code >> 1;
+                const int o = __ldg(t.bp_other + q);
+                if (code < 0 || gi >= nc || o >= W) {
+                  bad = true;
+                  continue;
+                }
+                const double cv = __ldg(t.bp_value + q);
+                double2 gg = sG[gi * NA + a_lane];
+                if (code & 1) gg.y = -gg.y;
+                const double2 term = o < 0 ? gg : rmul(gg, sA[o * NA + a_lane]);
+                ga.x = fma(cv, term.x, ga.x);
+                ga.y = fma(cv, term.y, ga.y);
+              }
             }
-            const double cv = __ldg(t.bp_value + q);
-#pragma unroll
-            for (int a = 0; a < NA; ++a) {
-              double2 g = sG[gi * NA + a];
-              if (code & 1) g.y = -g.y;
-              const double2 term = o < 0 ? g : rmul(g, sA[o * NA + a]);
-              ga[a].x = fma(cv, term.x, ga[a].x);
-              ga[a].y = fma(cv, term.y, ga[a].y);
-            }
+            part[it * NA + a_lane] = ga;
           }
         }
-#pragma unroll
-        for (int a = 0; a < NA; ++a) part[(pi * W + i) * NA + a] = ga[a];
-      }
-      __syncthreads();
-      for (int u = tid; u < W * NA; u += TH) {
-        double2 acc = sGA[u];
-        for (int pi = 0; pi < P; ++pi) {
-          const double2 v = part[pi * W * NA + u];
-          acc.x += v.x;
-          acc.y += v.y;
+        __syncthreads();
+        if (!(i0 < 0 || ni < 0 || ni > cw || int64_t(i1) > tt.item_count)) {
+          for (int u = tid; u < W * NA; u += TH) {
+            const int i = u / NA, a = u % NA;
+            const int64_t at = int64_t(L) * W + i;
+            const int j0 = tt.t_item_begin[at], j1 = tt.t_item_begin[at + 1];
+            double2 acc = sGA[u];
+            for (int j = j0; j < j1; ++j) {
+              const int it = tt.t_item[j];
+              if (it < 0 || it >= ni) {
+                bad = true;
+                continue;
+              }
+              const double2 v = part[it * NA + a];
+              acc.x += v.x;
+              acc.y += v.y;
+            }
+            sGA[u] = acc;
+          }
         }
-        sGA[u] = acc;
+        __syncthreads();
       }
-      __syncthreads();
     }
     for (int u = tid; u < W * NA; u += TH) {
       const int i = u / NA, a = u % NA;

@@ -618,6 +618,14 @@ class RecoupledTiles:
     col_comp: np.ndarray        # int32 [Q]
     dot_pos: np.ndarray         # int64 [D, 2]
     nonzero: int                # (row, column) pairs with a contraction
+    # back-propagation work items: each A-row entry's list of a pass cut into chunks of at
+    # most ``bp_chunk`` entries, (entry t, first, end) into the symmetric tables' bp
+    # arrays, longest first within a pass; t_item lists each entry's items in list order
+    bp_chunk: int = 0
+    bp_item_begin: np.ndarray = None  # int32 [pass_count + 1]
+    bp_item: np.ndarray = None        # int32 [I, 4]: (t, q0, q1, 0)
+    t_item_begin: np.ndarray = None   # int32 [pass_count * row_width + 1]
+    t_item: np.ndarray = None         # int32 [I]: item index within its pass
 
     @property
     def tile_count(self) -> int:
@@ -661,6 +669,25 @@ class RecoupledTiles:
             raise ValueError("tile column outside its pass")
         if np.any(self.dot_pos < 0) or np.any(self.dot_pos >= R * self.step_count):
             raise ValueError("contraction position outside the weights")
+        W = sym.row_width
+        ib = self.bp_item_begin.astype(np.int64)
+        if ib.shape != (P + 1,) or ib[0] != 0 or np.any(np.diff(ib) < 0) or ib[-1] != self.bp_item.shape[0]:
+            raise ValueError("bp_item_begin does not partition the work items")
+        cwidth = max(sym.max_pass_components, W)
+        if np.any(np.diff(ib) > cwidth):
+            raise ValueError("a pass has more back-propagation items than its part buffer holds")
+        it = self.bp_item.astype(np.int64)
+        Li = np.repeat(np.arange(P), np.diff(ib))
+        bb = sym.bp_begin.astype(np.int64)
+        if it.size and (np.any(it[:, 0] < 0) or np.any(it[:, 0] >= W) or np.any(it[:, 1] > it[:, 2]) or
+                        np.any(it[:, 1] < bb[Li * W + it[:, 0]]) or np.any(it[:, 2] > bb[Li * W + it[:, 0] + 1])):
+            raise ValueError("work item outside its entry's back-propagation list")
+        tb = self.t_item_begin.astype(np.int64)
+        if tb.shape != (P * W + 1,) or tb[0] != 0 or tb[-1] != self.t_item.shape[0] or np.any(np.diff(tb) < 0):
+            raise ValueError("t_item_begin does not partition the items")
+        Lt = np.repeat(np.arange(P * W) // W, np.diff(tb))
+        if np.any(self.t_item < 0) or np.any(self.t_item >= np.diff(ib)[Lt]):
+            raise ValueError("entry item outside its pass")
 
 
 def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> RecoupledTiles:
@@ -716,10 +743,44 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
         tile_begin.append(len(tile_row))
     dot_pos = np.asarray([(pos_of[(int(a), int(b))], pos_of[(int(b), int(a))])
                           for a, b in zip(plan.dot_a, plan.dot_b)], dtype=np.int64).reshape(-1, 2)
+    # back-propagation work items: the largest chunk (16, 12, 8 ... entries) whose item
+    # count still fits each pass's part buffer
+    W = sym.row_width
+    cwidth = max(sym.max_pass_components, W)
+    bb = sym.bp_begin.astype(np.int64)
+    chunk = 16
+    while True:
+        items_per_pass = [int(sum(max(1, -(-int(bb[L * W + t + 1] - bb[L * W + t]) // chunk)) if
+                                  bb[L * W + t + 1] > bb[L * W + t] else 0 for t in range(W))) for L in range(P)]
+        if max(items_per_pass, default=0) <= cwidth or chunk >= 1 << 20:
+            break
+        chunk *= 2
+    item_begin, items, t_begin, t_items = [0], [], [0], []
+    for L in range(P):
+        pass_items = []
+        for t in range(W):
+            q0, q1 = int(bb[L * W + t]), int(bb[L * W + t + 1])
+            for q in range(q0, q1, chunk):
+                pass_items.append((t, q, min(q1, q + chunk)))
+        order = sorted(range(len(pass_items)), key=lambda i: (-(pass_items[i][2] - pass_items[i][1]), i))
+        where = np.empty(len(pass_items), dtype=np.int64)
+        where[np.asarray(order, dtype=np.int64)] = np.arange(len(pass_items))
+        items.extend((pass_items[i][0], pass_items[i][1], pass_items[i][2], 0) for i in order)
+        item_begin.append(len(items))
+        per_t: List[List[int]] = [[] for _ in range(W)]
+        for i, (t, _, _) in enumerate(pass_items):
+            per_t[t].append(int(where[i]))
+        for t in range(W):
+            t_items.extend(per_t[t])
+            t_begin.append(len(t_items))
     tiles = RecoupledTiles(rows=rows, pass_count=P, tile_begin=np.asarray(tile_begin, dtype=np.int32),
                            tile_row=np.asarray(tile_row, dtype=np.int32).reshape(-1, rows),
                            tile_col_begin=np.asarray(col_begin, dtype=np.int32),
-                           col_comp=np.asarray(col_comp, dtype=np.int32), dot_pos=dot_pos, nonzero=nonzero)
+                           col_comp=np.asarray(col_comp, dtype=np.int32), dot_pos=dot_pos, nonzero=nonzero,
+                           bp_chunk=chunk, bp_item_begin=np.asarray(item_begin, dtype=np.int32),
+                           bp_item=np.asarray(items, dtype=np.int32).reshape(-1, 4),
+                           t_item_begin=np.asarray(t_begin, dtype=np.int32),
+                           t_item=np.asarray(t_items, dtype=np.int32))
     tiles.validate(sym)
     return tiles
 
@@ -921,6 +982,8 @@ def ctypes_tables(arrays: Dict[str, "object"], tabs: RecoupledDeviceTables):
 
 _TABLE_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
                  "dot_begin", "dot", "feat_index", "feat_weight")
+_TILE_ARRAYS = ("tile_begin", "tile_row", "tile_col_begin", "col_comp", "bp_item_begin", "bp_item", "t_item_begin",
+                "t_item")
 _SYM_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
                "mirror", "dot_begin", "dot")
 
@@ -982,12 +1045,12 @@ class RecoupledEvaluator:
             from . import _native as nat
             self.tiles = self.plan.sym_tiles(self.tile_rows)
             self.tile_arrays = {name: torch.as_tensor(np.ascontiguousarray(getattr(self.tiles, name))).to(self.device)
-                                for name in ("tile_begin", "tile_row", "tile_col_begin", "col_comp")}
+                                for name in _TILE_ARRAYS}
             self.kval = None if weights is None else torch.as_tensor(
                 self.tiles.tile_weights(self.plan.energy_weights(weights))).to(self.device).contiguous()
             self._t = nat.RecoupledTileTables(
                 rows=self.tiles.rows, pass_count=self.tiles.pass_count, tile_count=self.tiles.tile_count,
-                step_count=self.tiles.step_count,
+                step_count=self.tiles.step_count, item_count=int(self.tiles.bp_item.shape[0]),
                 **{name: self.tile_arrays[name].data_ptr() for name in self.tile_arrays},
                 kval=0 if self.kval is None else self.kval.data_ptr())
 
