@@ -538,17 +538,24 @@ typedef struct {
   int64_t tile_count;
   int64_t step_count;
   int64_t item_count;
+  int64_t group_count;
+  int64_t pack_count;
   const int32_t* tile_begin;     /* [pass_count + 1] */
   const int32_t* tile_row;       /* [tile_count, rows]: local component of the row's M = 0, or -1 */
   const int32_t* tile_col_begin; /* [tile_count + 1], multiples of 4 */
   const int32_t* col_comp;       /* [step_count], 16-byte aligned */
-  /* back-propagation work items: per pass, chunks (t, q0, q1, 0) of the
-   * A-row entries' lists in the symmetric tables; each entry adds its items'
-   * partial sums in the order t_item lists them */
+  /* back-propagation work items: per pass, chunks of the A-row entries'
+   * lists; item i of a pass (groups of `rows` items) writes a partial sum that
+   * its entry adds in the order t_item lists them.  The items' records
+   * (code, other, value as two int32) are packed per group, entry k of the
+   * group's item j at bp_group_off[g] + k * rows + j, padded with null
+   * records (other -1, value 0). */
   const int32_t* bp_item_begin;  /* [pass_count + 1] */
-  const int32_t* bp_item;        /* [item_count, 4], 16-byte aligned */
   const int32_t* t_item_begin;   /* [pass_count * row_width + 1] */
   const int32_t* t_item;         /* [item_count]: item index within its pass */
+  const int32_t* bp_group_begin; /* [pass_count + 1] */
+  const int32_t* bp_group_off;   /* [group_count + 1] */
+  const int32_t* bp_pack;        /* [pack_count, 4], 16-byte aligned */
   const double* kval;            /* [species_count, rows * step_count], 16-byte aligned */
 } y3b_recoupled_tile_tables;
 

@@ -55,6 +55,12 @@ inline T __ldg(const T* p) {
   return *p;
 }
 inline int atomicOr(int32_t* p, int v) { return __atomic_fetch_or(p, v, __ATOMIC_SEQ_CST); }
+inline double __hiloint2double(int hi, int lo) {
+  const uint64_t bits = (uint64_t(uint32_t(hi)) << 32) | uint64_t(uint32_t(lo));
+  double d;
+  std::memcpy(&d, &bits, sizeof d);
+  return d;
+}
 inline double __shfl_xor_sync(unsigned, double v, int lane_mask) {
   const int w = int(threadIdx.x) >> 5, lane = int(threadIdx.x) & 31;
   g_lanes[w][lane] = v;

@@ -244,7 +244,7 @@ def walk_sym_tiled(tabs, tiles, A, species, k):
                 rc = int(tiles.tile_row[t, r])
                 if rc < 0:
                     continue
-                kv = kval[:, R * q0 + r * (q1 - q0): R * q0 + (r + 1) * (q1 - q0)]  # [N, steps]
+                kv = kval[:, R * q0 + r: R * q1: R]  # [N, steps]
                 sgn = int(tabs.comp[c0 + rc, 7])
                 for M in range(L + 1):
                     acc = (kv * I[:, cols + M]).sum(axis=1)

@@ -82,8 +82,10 @@ class RecoupledTileTables(ctypes.Structure):
 
     _fields_ = [
         ("rows", I32), ("pass_count", I32), ("tile_count", I64), ("step_count", I64), ("item_count", I64),
+        ("group_count", I64), ("pack_count", I64),
         ("tile_begin", VP), ("tile_row", VP), ("tile_col_begin", VP), ("col_comp", VP),
-        ("bp_item_begin", VP), ("bp_item", VP), ("t_item_begin", VP), ("t_item", VP), ("kval", VP),
+        ("bp_item_begin", VP), ("t_item_begin", VP), ("t_item", VP), ("bp_group_begin", VP), ("bp_group_off", VP),
+        ("bp_pack", VP), ("kval", VP),
     ]
 
 

@@ -633,22 +633,24 @@ recoupled_sym_energy_kernel(SymTabs t, const double2* __restrict__ A, int64_t at
 // Dense tiles of the symmetric pass's contraction weights (RecoupledTiles).
 struct TileTabs {
   int32_t rows, pass_count;
-  int64_t tile_count, step_count, item_count;
+  int64_t tile_count, step_count, item_count, group_count, pack_count;
   const int32_t* tile_begin;
   const int32_t* tile_row;
   const int32_t* tile_col_begin;
   const int32_t* col_comp;
   const int32_t* bp_item_begin;
-  const int4* bp_item;
   const int32_t* t_item_begin;
   const int32_t* t_item;
+  const int32_t* bp_group_begin;
+  const int32_t* bp_group_off;
+  const int4* bp_pack;
   const double* kval;
 };
 
 inline TileTabs tile_view(const y3b_recoupled_tile_tables& t) {
-  return TileTabs{t.rows, t.pass_count, t.tile_count, t.step_count, t.item_count, t.tile_begin, t.tile_row,
-                  t.tile_col_begin, t.col_comp, t.bp_item_begin, reinterpret_cast<const int4*>(t.bp_item),
-                  t.t_item_begin, t.t_item, t.kval};
+  return TileTabs{t.rows, t.pass_count, t.tile_count, t.step_count, t.item_count, t.group_count, t.pack_count,
+                  t.tile_begin, t.tile_row, t.tile_col_begin, t.col_comp, t.bp_item_begin, t.t_item_begin,
+                  t.t_item, t.bp_group_begin, t.bp_group_off, reinterpret_cast<const int4*>(t.bp_pack), t.kval};
 }
 
 // Step 1 of the tiled adjoint with lanes as (component, atom): a warp builds
@@ -693,75 +695,95 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
   }
 }
 
-// Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1: the warp's
-// tiles in a snake order over the warps (tiles are sorted by decreasing column
-// count); lane (r, a) walks its tile's columns four at a time and forms
-// acc[M] = sum_q K[z_a][row r, column q] I[column q + M] for its atom a, then
-// writes gI = (-1)^p conj(acc) and adds its energy share
+// Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1.  A lane
+// owns one (atom a, component M) of a tile and all R = 32 / NA rows of it in
+// registers: per column step it reads I[column + M] for its atom once from
+// shared memory and the R row weights (contiguous, the same for every lane of
+// the tile), and adds acc[r] += K[r] I.  A warp holds 32 / (NA * MC) tiles at
+// a time (slots), MC = min(LM1, 32 / NA) components per slot; passes with
+// more components run the tile again for the next MC of them.  Work units
+// (tile, component chunk) go to the warps in a snake order (tiles are sorted
+// by decreasing column count).  At the end of a unit each lane writes
+// gI = (-1)^p conj(acc[r]) for its rows and adds its energy shares
 // w_M Re(I gI) (w_0 = 1/2).  A column or row outside the pass is skipped and
 // sets bad.
 template <int LM1, int NA, int TH>
 __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileTabs& tt, int L, int c0, int nc,
                                                    const double2* sI, double2* sG, const double* kz, double& ep,
                                                    bool& bad) {
-  constexpr int R = 32 / NA;
+  constexpr int R = 32 / NA;                       // rows per tile
+  constexpr int MC = LM1 < R ? LM1 : R;            // components per slot
+  constexpr int NCH = (LM1 + MC - 1) / MC;         // component chunks per tile
+  constexpr int SLOTS = 32 / (NA * MC);            // tiles per warp at a time
   constexpr int NW = TH / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r = lane / NA, a = lane % NA;
+  const int slot = lane / (NA * MC);
+  const int mloc = (lane / NA) % MC, a = lane % NA;
+  const bool active = slot < SLOTS;
   const int t0 = tt.tile_begin[L], t1 = tt.tile_begin[L + 1];
   if (t0 < 0 || t1 < t0 || int64_t(t1) > tt.tile_count) {
     bad = true;
     return;
   }
-  const int ntiles = t1 - t0;
+  const int units = (t1 - t0) * NCH;
+  const int rounds = (units + SLOTS - 1) / SLOTS;  // warp rounds of SLOTS units
   for (int k = 0;; ++k) {
-    const int i = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;
-    if (i >= ntiles) break;
-    const int tile = t0 + i;
-    const int rowc = tt.tile_row[int64_t(tile) * R + r];
+    const int rnd = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;
+    if (rnd >= rounds) break;
+    const int unit = rnd * SLOTS + slot;
+    const bool live = active && unit < units;
+    const int tile = t0 + (live ? unit / NCH : 0);
+    const int M = (live ? unit % NCH : 0) * MC + mloc;
+    const bool mine = live && M < LM1;
     const int q0 = tt.tile_col_begin[tile], q1 = tt.tile_col_begin[tile + 1];
-    const int n = q1 - q0;
-    if (q0 < 0 || n < 0 || (n & 3) || (q0 & 3) || int64_t(q1) > tt.step_count) {
+    const int n = live ? q1 - q0 : 0;
+    if (live && (q0 < 0 || n < 0 || (n & 3) || (q0 & 3) || int64_t(q1) > tt.step_count)) {
       bad = true;
-      continue;  // uniform over the warp
+      continue;
     }
-    const double* kr = kz + int64_t(R) * q0 + int64_t(r) * n;
-    double2 acc[LM1];
+    const double* kq = kz + int64_t(R) * q0;
+    double2 acc[R];
 #pragma unroll
-    for (int M = 0; M < LM1; ++M) acc[M] = make_double2(0.0, 0.0);
+    for (int r = 0; r < R; ++r) acc[r] = make_double2(0.0, 0.0);
+    const int Mc = mine ? M : 0;
     for (int q = 0; q < n; q += 4) {
       const int4 c4 = __ldg(reinterpret_cast<const int4*>(tt.col_comp + q0 + q));
-      const double2 k01 = __ldg(reinterpret_cast<const double2*>(kr + q));
-      const double2 k23 = __ldg(reinterpret_cast<const double2*>(kr + q + 2));
       const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
-      const double ks[4] = {k01.x, k01.y, k23.x, k23.y};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         int c = cs[j];
-        double kv = ks[j];
-        if (c < 0 || c + LM1 > nc) {  // uniform over the warp
+        bool ok = true;
+        if (c < 0 || c + LM1 > nc) {
           bad = true;
+          ok = false;
           c = 0;
-          kv = 0.0;
         }
+        const double2 v = sI[(c + Mc) * NA + a];
+        const double2* kr = reinterpret_cast<const double2*>(kq + int64_t(q + j) * R);
 #pragma unroll
-        for (int M = 0; M < LM1; ++M) {
-          const double2 v = sI[(c + M) * NA + a];
-          acc[M].x = fma(kv, v.x, acc[M].x);
-          acc[M].y = fma(kv, v.y, acc[M].y);
+        for (int r = 0; r < R; r += 2) {
+          const double2 k2 = __ldg(kr + r / 2);
+          const double k0 = ok ? k2.x : 0.0, k1 = ok ? k2.y : 0.0;
+          acc[r].x = fma(k0, v.x, acc[r].x);
+          acc[r].y = fma(k0, v.y, acc[r].y);
+          acc[r + 1].x = fma(k1, v.x, acc[r + 1].x);
+          acc[r + 1].y = fma(k1, v.y, acc[r + 1].y);
         }
       }
     }
-    if (rowc < -1 || rowc + LM1 > nc) {
-      bad = true;
-    } else if (rowc >= 0) {
-      const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
+    if (mine) {
 #pragma unroll
-      for (int M = 0; M < LM1; ++M) {
-        const double2 g = make_double2(sg * acc[M].x, -sg * acc[M].y);
-        sG[(rowc + M) * NA + a] = g;
-        const double2 iv = sI[(rowc + M) * NA + a];
-        ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
+      for (int r = 0; r < R; ++r) {
+        const int rowc = tt.tile_row[int64_t(tile) * R + r];
+        if (rowc < -1 || rowc + LM1 > nc) {
+          bad = true;
+        } else if (rowc >= 0) {
+          const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
+          const double2 g = make_double2(sg * acc[r].x, -sg * acc[r].y);
+          sG[(rowc + M) * NA + a] = g;
+          const double2 iv = sI[(rowc + M) * NA + a];
+          ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
+        }
       }
     }
   }
@@ -855,39 +877,42 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
         const int warp = tid >> 5;
         const int i0 = tt.bp_item_begin[L], i1 = tt.bp_item_begin[L + 1];
         const int ni = i1 - i0;
+        const int g0 = tt.bp_group_begin[L], g1 = tt.bp_group_begin[L + 1];
         double2* part = sI;  // [ni][NA]
-        if (i0 < 0 || ni < 0 || ni > cw || int64_t(i1) > tt.item_count) {
+        if (i0 < 0 || ni < 0 || ni > cw || int64_t(i1) > tt.item_count || g0 < 0 || g1 < g0 ||
+            int64_t(g1) > tt.group_count || int64_t(g1 - g0) * R < ni) {
           bad = true;  // uniform over the block
         } else {
-          for (int g = warp; g * R < ni; g += NW) {
-            const int it = g * R + lane / NA;
-            if (it >= ni) continue;
-            const int4 w = __ldg(tt.bp_item + i0 + it);  // (t, q0, q1, 0)
-            double2 ga = make_double2(0.0, 0.0);
-            if (w.x < 0 || w.x >= W || w.y < 0 || w.z < w.y || int64_t(w.z) > t.bp_count) {
-              bad = true;
-            } else {
-              for (int q = w.y; q < w.z; ++q) {
-                const int code = __ldg(t.bp_gi + q);
-                const int gi = code >> 1;
-                const int o = __ldg(t.bp_other + q);
-                if (code < 0 || gi >= nc || o >= W) {
-                  bad = true;
-                  continue;
-                }
-                const double cv = __ldg(t.bp_value + q);
-                double2 gg = sG[gi * NA + a_lane];
-                if (code & 1) gg.y = -gg.y;
-                const double2 term = o < 0 ? gg : rmul(gg, sA[o * NA + a_lane]);
-                ga.x = fma(cv, term.x, ga.x);
-                ga.y = fma(cv, term.y, ga.y);
-              }
+          for (int g = g0 + warp; g < g1; g += NW) {
+            const int e0 = tt.bp_group_off[g], e1 = tt.bp_group_off[g + 1];
+            const int j = lane / NA;
+            const int it = (g - g0) * R + j;
+            if (e0 < 0 || e1 < e0 || int64_t(e1) > tt.pack_count || ((e1 - e0) % R)) {
+              bad = true;  // uniform over the warp
+              continue;
             }
-            part[it * NA + a_lane] = ga;
+            double2 ga = make_double2(0.0, 0.0);
+            for (int e = e0 + j; e < e1; e += R) {
+              const int4 rec = __ldg(tt.bp_pack + e);  // (code, other, value lo, value hi)
+              const int gi = rec.x >> 1;
+              const int o = rec.y;
+              if (rec.x < 0 || gi >= nc || o >= W) {
+                bad = true;
+                continue;
+              }
+              const double cv = __hiloint2double(rec.w, rec.z);
+              double2 gg = sG[gi * NA + a_lane];
+              if (rec.x & 1) gg.y = -gg.y;
+              const double2 term = o < 0 ? gg : rmul(gg, sA[o * NA + a_lane]);
+              ga.x = fma(cv, term.x, ga.x);
+              ga.y = fma(cv, term.y, ga.y);
+            }
+            if (it < ni) part[it * NA + a_lane] = ga;
           }
         }
         __syncthreads();
-        if (!(i0 < 0 || ni < 0 || ni > cw || int64_t(i1) > tt.item_count)) {
+        if (!(i0 < 0 || ni < 0 || ni > cw || int64_t(i1) > tt.item_count || g0 < 0 || g1 < g0 ||
+              int64_t(g1) > tt.group_count || int64_t(g1 - g0) * R < ni)) {
           for (int u = tid; u < W * NA; u += TH) {
             const int i = u / NA, a = u % NA;
             const int64_t at = int64_t(L) * W + i;

@@ -606,8 +606,9 @@ class RecoupledTiles:
     symmetric layout, ``L + 1`` components per segment); a tile's columns
     ``[tile_col_begin[t], tile_col_begin[t + 1])`` are padded to a multiple of
     ``TILE_STEP`` with column 0 and weight 0.  The weights of species ``z`` are
-    ``kval[z, rows * tile_col_begin[t] + r * ncols_t + (q - tile_col_begin[t])]``
-    (``tile_weights``); ``dot_pos[d]`` are the two entries contraction ``d`` adds to.
+    ``kval[z, rows * q + r]`` for column step ``q`` and tile row ``r`` (one step's
+    weights of all rows contiguous; ``tile_weights``); ``dot_pos[d]`` are the two
+    entries contraction ``d`` adds to.
     Tiles within a pass are ordered by decreasing column count."""
 
     rows: int
@@ -626,6 +627,13 @@ class RecoupledTiles:
     bp_item: np.ndarray = None        # int32 [I, 4]: (t, q0, q1, 0)
     t_item_begin: np.ndarray = None   # int32 [pass_count * row_width + 1]
     t_item: np.ndarray = None         # int32 [I]: item index within its pass
+    # the items' entries as 16-byte records (code, other, value) interleaved per group
+    # of ``rows`` consecutive items of a pass: entry k of item j of group g at
+    # bp_group_off[g] + k * rows + j, padded with null records (other -1, value 0) to
+    # the group's longest item, so that a warp reads one contiguous row of records
+    bp_group_begin: np.ndarray = None  # int32 [pass_count + 1]
+    bp_group_off: np.ndarray = None    # int32 [groups + 1]
+    bp_pack: np.ndarray = None         # int32 [packed, 4]: (code, other, value bits lo, hi)
 
     @property
     def tile_count(self) -> int:
@@ -688,6 +696,20 @@ class RecoupledTiles:
         Lt = np.repeat(np.arange(P * W) // W, np.diff(tb))
         if np.any(self.t_item < 0) or np.any(self.t_item >= np.diff(ib)[Lt]):
             raise ValueError("entry item outside its pass")
+        gb = self.bp_group_begin.astype(np.int64)
+        go = self.bp_group_off.astype(np.int64)
+        if gb.shape != (P + 1,) or gb[0] != 0 or gb[-1] != go.shape[0] - 1 or np.any(np.diff(gb) < 0):
+            raise ValueError("bp_group_begin does not partition the groups")
+        if go[0] != 0 or go[-1] != self.bp_pack.shape[0] or np.any(np.diff(go) % R) or np.any(np.diff(go) < 0):
+            raise ValueError("bp_group_off does not cut the records into rows of whole groups")
+        if np.any(np.diff(gb) * R < np.diff(ib)) or np.any((np.diff(gb) - 1) * R >= np.maximum(np.diff(ib), 1)):
+            raise ValueError("the groups of a pass do not hold its items")
+        pk = self.bp_pack.astype(np.int64)
+        Lg = np.repeat(np.arange(P), np.diff(gb))
+        Lr = np.repeat(Lg, np.diff(go))
+        if pk.size and (np.any(pk[:, 0] < 0) or np.any((pk[:, 0] >> 1) >= nc[Lr]) or np.any(pk[:, 1] < -1) or
+                        np.any(pk[:, 1] >= W)):
+            raise ValueError("packed back-propagation record outside its pass or row")
 
 
 def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> RecoupledTiles:
@@ -735,7 +757,7 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
             q0 = col_begin[-1]
             for r, srow in enumerate(t):
                 for qi, scol in enumerate(cols):
-                    pos_of[(srow, scol)] = rows * q0 + r * npad + qi
+                    pos_of[(srow, scol)] = rows * (q0 + qi) + r
             tile_row.append([int(off[s]) - base for s in t] + [-1] * (rows - len(t)))
             col_comp.extend(int(off[c]) - base for c in cols)
             col_comp.extend([0] * (npad - n))
@@ -773,6 +795,23 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
         for t in range(W):
             t_items.extend(per_t[t])
             t_begin.append(len(t_items))
+    # pack the items' entries per group of ``rows`` items
+    group_begin, group_off, pack = [0], [0], []
+    vbits = sym.bp_value.astype(np.float64).view(np.int32).reshape(-1, 2)
+    for L in range(P):
+        pass_items = items[item_begin[L]:item_begin[L + 1]]
+        for g0 in range(0, len(pass_items), rows):
+            grp = pass_items[g0:g0 + rows]
+            longest = max(q1 - q0 for _, q0, q1, _ in grp)
+            for k in range(longest):
+                for j in range(rows):
+                    if j < len(grp) and grp[j][1] + k < grp[j][2]:
+                        q = grp[j][1] + k
+                        pack.append((int(sym.bp_gi[q]), int(sym.bp_other[q]), int(vbits[q, 0]), int(vbits[q, 1])))
+                    else:
+                        pack.append((0, -1, 0, 0))
+            group_off.append(len(pack))
+        group_begin.append(len(group_off) - 1)
     tiles = RecoupledTiles(rows=rows, pass_count=P, tile_begin=np.asarray(tile_begin, dtype=np.int32),
                            tile_row=np.asarray(tile_row, dtype=np.int32).reshape(-1, rows),
                            tile_col_begin=np.asarray(col_begin, dtype=np.int32),
@@ -780,7 +819,10 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
                            bp_chunk=chunk, bp_item_begin=np.asarray(item_begin, dtype=np.int32),
                            bp_item=np.asarray(items, dtype=np.int32).reshape(-1, 4),
                            t_item_begin=np.asarray(t_begin, dtype=np.int32),
-                           t_item=np.asarray(t_items, dtype=np.int32))
+                           t_item=np.asarray(t_items, dtype=np.int32),
+                           bp_group_begin=np.asarray(group_begin, dtype=np.int32),
+                           bp_group_off=np.asarray(group_off, dtype=np.int32),
+                           bp_pack=np.asarray(pack, dtype=np.int32).reshape(-1, 4))
     tiles.validate(sym)
     return tiles
 
@@ -982,8 +1024,8 @@ def ctypes_tables(arrays: Dict[str, "object"], tabs: RecoupledDeviceTables):
 
 _TABLE_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
                  "dot_begin", "dot", "feat_index", "feat_weight")
-_TILE_ARRAYS = ("tile_begin", "tile_row", "tile_col_begin", "col_comp", "bp_item_begin", "bp_item", "t_item_begin",
-                "t_item")
+_TILE_ARRAYS = ("tile_begin", "tile_row", "tile_col_begin", "col_comp", "bp_item_begin", "t_item_begin", "t_item",
+                "bp_group_begin", "bp_group_off", "bp_pack")
 _SYM_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
                "mirror", "dot_begin", "dot")
 
@@ -1051,6 +1093,7 @@ class RecoupledEvaluator:
             self._t = nat.RecoupledTileTables(
                 rows=self.tiles.rows, pass_count=self.tiles.pass_count, tile_count=self.tiles.tile_count,
                 step_count=self.tiles.step_count, item_count=int(self.tiles.bp_item.shape[0]),
+                group_count=int(self.tiles.bp_group_off.shape[0] - 1), pack_count=int(self.tiles.bp_pack.shape[0]),
                 **{name: self.tile_arrays[name].data_ptr() for name in self.tile_arrays},
                 kval=0 if self.kval is None else self.kval.data_ptr())
 
