@@ -1028,67 +1028,64 @@ __global__ void __launch_bounds__(32 * kEdgeWarps) ace_edge_grad_kernel(
         const double eps = 1e-12;
         const double sr = r > eps ? r : eps;
         const double u[3] = {d[0] / sr, d[1] / sr, d[2] / sr};
-        double v[W], g[W][3];
-        real_sh_unit<double, LMAX>(u[0], u[1], u[2], nrm, v, g);
-        // Cartesian gradients of the real harmonics, in place: J = (I - u u^T) / |d|
-        // (I / eps below eps), as ye3t_runtime_core.cpp:819-834
-#pragma unroll
-        for (int k = 0; k < W; ++k) {
-          const double gu = r > eps ? g[k][0] * u[0] + g[k][1] * u[1] + g[k][2] * u[2] : 0.0;
-#pragma unroll
-          for (int ax = 0; ax < 3; ++ax) g[k][ax] = (g[k][ax] - gu * u[ax]) / sr;
-        }
+        ShState<double, LMAX> st;
+        sh_state<double, LMAX>(u[0], u[1], u[2], st);
+        // Cartesian gradients of the real harmonics: J = (I - u u^T) / |d| (I / eps
+        // below eps), as ye3t_runtime_core.cpp:819-834; the division by |d| is one
+        // reciprocal and a product per entry
+        const double inv_sr = 1.0 / sr;
         double acc_r = 0.0, acc_v[3] = {0.0, 0.0, 0.0};
         const double inv2 = 0.70710678118654752440084436210484903;
+        // one complex harmonic column lm with its gradient: add
+        // Re(Q_lm Yc_lm) and Re(P_lm grad Yc_lm)
+        auto column = [&](int lm, double yr, double yi, const double (&dr)[3], const double (&di)[3]) {
+          double2 P = make_double2(0.0, 0.0), Q = make_double2(0.0, 0.0);
+#pragma unroll
+          for (int n = 0; n < NMAXT; ++n) {
+            const double2 Gv = sG[wib][n * W + lm];
+            P.x = fma(rv[n + 1], Gv.x, P.x);
+            P.y = fma(rv[n + 1], Gv.y, P.y);
+            Q.x = fma(rd[n + 1], Gv.x, Q.x);
+            Q.y = fma(rd[n + 1], Gv.y, Q.y);
+          }
+          acc_r += Q.x * yr - Q.y * yi;
+#pragma unroll
+          for (int ax = 0; ax < 3; ++ax) acc_v[ax] += P.x * dr[ax] - P.y * di[ax];
+        };
 #pragma unroll
         for (int l = 0; l <= LMAX; ++l) {
           const int cidx = l * l + l;
 #pragma unroll
-          for (int m = -l; m <= l; ++m) {
-            // complex harmonic and its gradient from the real ones
+          for (int m = 0; m <= l; ++m) {
+            double v[2], g[2][3];
+            real_sh_pair<double, LMAX>(l, m, st, nrm, v, g);
+#pragma unroll
+            for (int h = 0; h < (m == 0 ? 1 : 2); ++h) {
+              const double gu = r > eps ? g[h][0] * u[0] + g[h][1] * u[1] + g[h][2] * u[2] : 0.0;
+#pragma unroll
+              for (int ax = 0; ax < 3; ++ax) g[h][ax] = (g[h][ax] - gu * u[ax]) * inv_sr;
+            }
+            // complex harmonics and gradients from the real pair
             // (Yc_{l,-m} = (R_{+m} + i R_{-m}) / sqrt2, Yc_{l,+m} = (-1)^m (R_{+m} - i R_{-m}) / sqrt2)
-            double yr, yi, dr[3], di[3];
             if (m == 0) {
-              yr = v[cidx];
-              yi = 0.0;
-#pragma unroll
-              for (int ax = 0; ax < 3; ++ax) {
-                dr[ax] = g[cidx][ax];
-                di[ax] = 0.0;
-              }
-            } else if (m < 0) {
-              const int pp = cidx - m, nn = cidx + m;
-              yr = inv2 * v[pp];
-              yi = inv2 * v[nn];
-#pragma unroll
-              for (int ax = 0; ax < 3; ++ax) {
-                dr[ax] = inv2 * g[pp][ax];
-                di[ax] = inv2 * g[nn][ax];
-              }
+              const double dr[3] = {g[0][0], g[0][1], g[0][2]}, di[3] = {0.0, 0.0, 0.0};
+              column(cidx, v[0], 0.0, dr, di);
             } else {
               const double sg = (m & 1) ? -1.0 : 1.0;
-              const int pp = cidx + m, nn = cidx - m;
-              yr = sg * (inv2 * v[pp]);
-              yi = sg * (inv2 * -v[nn]);
+              double dr[3], di[3];
 #pragma unroll
               for (int ax = 0; ax < 3; ++ax) {
-                dr[ax] = sg * (inv2 * g[pp][ax]);
-                di[ax] = sg * (inv2 * -g[nn][ax]);
+                dr[ax] = inv2 * g[0][ax];
+                di[ax] = inv2 * g[1][ax];
               }
-            }
-            const int lm = cidx + m;
-            double2 P = make_double2(0.0, 0.0), Q = make_double2(0.0, 0.0);
+              column(cidx - m, inv2 * v[0], inv2 * v[1], dr, di);
 #pragma unroll
-            for (int n = 0; n < NMAXT; ++n) {
-              const double2 Gv = sG[wib][n * W + lm];
-              P.x = fma(rv[n + 1], Gv.x, P.x);
-              P.y = fma(rv[n + 1], Gv.y, P.y);
-              Q.x = fma(rd[n + 1], Gv.x, Q.x);
-              Q.y = fma(rd[n + 1], Gv.y, Q.y);
+              for (int ax = 0; ax < 3; ++ax) {
+                dr[ax] = sg * (inv2 * g[0][ax]);
+                di[ax] = sg * (inv2 * -g[1][ax]);
+              }
+              column(cidx + m, sg * (inv2 * v[0]), sg * (inv2 * -v[1]), dr, di);
             }
-            acc_r += Q.x * yr - Q.y * yi;
-#pragma unroll
-            for (int ax = 0; ax < 3; ++ax) acc_v[ax] += P.x * dr[ax] - P.y * di[ax];
           }
         }
         gx = p * (acc_r * u[0] + acc_v[0]);

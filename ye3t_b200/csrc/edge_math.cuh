@@ -110,6 +110,56 @@ __device__ __forceinline__ void legendre_derivs(R z, R* q) {
   }
 }
 
+// The per-edge state of the real tesseral harmonics below: the Legendre
+// derivative table and the powers (ux + i uy)^m.  real_sh_pair turns it into
+// the values and gradients of the pair (l, +m), (l, -m) with the same
+// arithmetic as real_sh_unit, so that a caller can form one pair at a time.
+template <typename R, int LMAX>
+struct ShState {
+  R q[(LMAX + 1) * (LMAX + 2) / 2];
+  R pr[LMAX + 1], pi_[LMAX + 1];
+};
+
+template <typename R, int LMAX>
+__device__ __forceinline__ void sh_state(R ux, R uy, R uz, ShState<R, LMAX>& st) {
+  legendre_derivs<R, LMAX>(uz, st.q);
+  st.pr[0] = R(1);
+  st.pi_[0] = R(0);
+#pragma unroll
+  for (int m = 1; m <= LMAX; ++m) {
+    st.pr[m] = st.pr[m - 1] * ux - st.pi_[m - 1] * uy;
+    st.pi_[m] = st.pr[m - 1] * uy + st.pi_[m - 1] * ux;
+  }
+}
+
+// Values and polynomial gradients of (l, +m) [index 0] and (l, -m) [index 1]
+// (for m = 0 only index 0 is set).
+template <typename R, int LMAX>
+__device__ __forceinline__ void real_sh_pair(int l, int m, const ShState<R, LMAX>& st, const ShNorm& nrm, R v[2],
+                                             R g[2][3]) {
+  const R rt2 = R(1.4142135623730950488016887242096981);
+  if (m == 0) {
+    const R n0 = R(nrm.n[norm_index(l, 0)]);
+    v[0] = n0 * st.q[norm_index(l, 0)];
+    g[0][0] = R(0);
+    g[0][1] = R(0);
+    g[0][2] = l >= 1 ? n0 * st.q[norm_index(l, 1)] : R(0);
+    return;
+  }
+  const R sc = rt2 * R(nrm.n[norm_index(l, m)]);
+  const R qq = st.q[norm_index(l, m)];
+  const R dq = (m + 1 <= l) ? st.q[norm_index(l, m + 1)] : R(0);
+  const R mr = R(m) * st.pr[m - 1], mi = R(m) * st.pi_[m - 1];
+  v[0] = sc * qq * st.pr[m];
+  v[1] = -sc * qq * st.pi_[m];
+  g[0][0] = sc * qq * mr;
+  g[0][1] = sc * qq * (-mi);
+  g[0][2] = sc * dq * st.pr[m];
+  g[1][0] = -sc * qq * mi;
+  g[1][1] = -sc * qq * mr;
+  g[1][2] = -sc * dq * st.pi_[m];
+}
+
 // Real tesseral harmonics (ye3t_runtime_core.cpp:226-290 convention) for all
 // l <= LMAX at a unit vector u, with the gradient g[.][3] of their polynomial
 // extension in (ux, uy, uz) when g != nullptr.  Packed columns [l^2, (l+1)^2).
