@@ -696,29 +696,34 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
 }
 
 // Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1.  A lane
-// owns one (atom a, component M) of a tile and all R = 32 / NA rows of it in
+// owns one (atom a, component M) of a tile and RL of its R = 32 / NA rows in
 // registers: per column step it reads I[column + M] for its atom once from
-// shared memory and the R row weights (contiguous, the same for every lane of
-// the tile), and adds acc[r] += K[r] I.  A warp holds 32 / (NA * MC) tiles at
-// a time (slots), MC = min(LM1, 32 / NA) components per slot; passes with
-// more components run the tile again for the next MC of them.  Work units
-// (tile, component chunk) go to the warps in a snake order (tiles are sorted
-// by decreasing column count).  At the end of a unit each lane writes
-// gI = (-1)^p conj(acc[r]) for its rows and adds its energy shares
-// w_M Re(I gI) (w_0 = 1/2).  A column or row outside the pass is skipped and
-// sets bad.
+// shared memory and its rows' weights (contiguous, the same for all lanes of a
+// row group), and adds acc[i] += K[row i] I.  A tile spreads over
+// NA * MC * RG lanes: MC = min(LM1, R) components and RG = R / RL row groups,
+// with RL the fewest rows per lane that keep a tile within one warp, so that
+// small L still give one tile per warp (the warps' work stays even) and large
+// L reuse each read for up to R rows.  Passes with more than MC components
+// run a tile again for the next MC of them.  Work units (tile, component
+// chunk) go to the warps in a snake order (tiles are sorted by decreasing
+// column count).  At the end of a unit each lane writes gI = (-1)^p
+// conj(acc[i]) for its rows and adds its energy shares w_M Re(I gI)
+// (w_0 = 1/2).  A column or row outside the pass is skipped and sets bad.
 template <int LM1, int NA, int TH>
 __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileTabs& tt, int L, int c0, int nc,
                                                    const double2* sI, double2* sG, const double* kz, double& ep,
                                                    bool& bad) {
-  constexpr int R = 32 / NA;                       // rows per tile
-  constexpr int MC = LM1 < R ? LM1 : R;            // components per slot
-  constexpr int NCH = (LM1 + MC - 1) / MC;         // component chunks per tile
-  constexpr int SLOTS = 32 / (NA * MC);            // tiles per warp at a time
+  constexpr int R = 32 / NA;                                   // rows per tile
+  constexpr int MC = LM1 < R ? LM1 : R;                        // components per unit
+  constexpr int NCH = (LM1 + MC - 1) / MC;                     // component chunks per tile
+  constexpr int RG0 = 32 / (NA * MC);                          // row groups that fit a warp
+  constexpr int RG = RG0 >= R ? R : (RG0 >= 4 ? 4 : (RG0 >= 2 ? 2 : 1));
+  constexpr int RL = R / RG;                                   // rows per lane
+  constexpr int SLOTS = 32 / (NA * MC * RG);                   // units per warp at a time
   constexpr int NW = TH / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int slot = lane / (NA * MC);
-  const int mloc = (lane / NA) % MC, a = lane % NA;
+  const int a = lane % NA, mloc = (lane / NA) % MC, rg = (lane / (NA * MC)) % RG;
+  const int slot = lane / (NA * MC * RG);
   const bool active = slot < SLOTS;
   const int t0 = tt.tile_begin[L], t1 = tt.tile_begin[L + 1];
   if (t0 < 0 || t1 < t0 || int64_t(t1) > tt.tile_count) {
@@ -741,10 +746,10 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
       bad = true;
       continue;
     }
-    const double* kq = kz + int64_t(R) * q0;
-    double2 acc[R];
+    const double* kq = kz + int64_t(R) * q0 + rg * RL;
+    double2 acc[RL];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = make_double2(0.0, 0.0);
+    for (int i = 0; i < RL; ++i) acc[i] = make_double2(0.0, 0.0);
     const int Mc = mine ? M : 0;
     for (int q = 0; q < n; q += 4) {
       const int4 c4 = __ldg(reinterpret_cast<const int4*>(tt.col_comp + q0 + q));
@@ -759,27 +764,33 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
           c = 0;
         }
         const double2 v = sI[(c + Mc) * NA + a];
-        const double2* kr = reinterpret_cast<const double2*>(kq + int64_t(q + j) * R);
+        const double* kr = kq + int64_t(q + j) * R;
+        if constexpr (RL == 1) {
+          const double k0 = ok ? __ldg(kr) : 0.0;
+          acc[0].x = fma(k0, v.x, acc[0].x);
+          acc[0].y = fma(k0, v.y, acc[0].y);
+        } else {
 #pragma unroll
-        for (int r = 0; r < R; r += 2) {
-          const double2 k2 = __ldg(kr + r / 2);
-          const double k0 = ok ? k2.x : 0.0, k1 = ok ? k2.y : 0.0;
-          acc[r].x = fma(k0, v.x, acc[r].x);
-          acc[r].y = fma(k0, v.y, acc[r].y);
-          acc[r + 1].x = fma(k1, v.x, acc[r + 1].x);
-          acc[r + 1].y = fma(k1, v.y, acc[r + 1].y);
+          for (int i = 0; i < RL; i += 2) {
+            const double2 k2 = __ldg(reinterpret_cast<const double2*>(kr + i));
+            const double k0 = ok ? k2.x : 0.0, k1 = ok ? k2.y : 0.0;
+            acc[i].x = fma(k0, v.x, acc[i].x);
+            acc[i].y = fma(k0, v.y, acc[i].y);
+            acc[i + 1].x = fma(k1, v.x, acc[i + 1].x);
+            acc[i + 1].y = fma(k1, v.y, acc[i + 1].y);
+          }
         }
       }
     }
     if (mine) {
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int rowc = tt.tile_row[int64_t(tile) * R + r];
+      for (int i = 0; i < RL; ++i) {
+        const int rowc = tt.tile_row[int64_t(tile) * R + rg * RL + i];
         if (rowc < -1 || rowc + LM1 > nc) {
           bad = true;
         } else if (rowc >= 0) {
           const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
-          const double2 g = make_double2(sg * acc[r].x, -sg * acc[r].y);
+          const double2 g = make_double2(sg * acc[i].x, -sg * acc[i].y);
           sG[(rowc + M) * NA + a] = g;
           const double2 iv = sI[(rowc + M) * NA + a];
           ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
