@@ -28,6 +28,7 @@ struct int4 {
   int x, y, z, w;
 };
 inline double2 make_double2(double x, double y) { return double2{x, y}; }
+inline int4 make_int4(int x, int y, int z, int w) { return int4{x, y, z, w}; }
 struct Dim3 {
   unsigned x = 0, y = 0, z = 0;
 };
@@ -49,6 +50,7 @@ static double g_lanes[32][32];
 #define __restrict__
 #define __shared__ static
 #define __syncthreads() g_block->arrive_and_wait()
+#define __syncwarp(...) g_warp[int(threadIdx.x) >> 5]->arrive_and_wait()
 
 template <typename T>
 inline T __ldg(const T* p) {
@@ -253,12 +255,13 @@ extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_table
                                                    int64_t atom_count, const int32_t* order, const int32_t* species,
                                                    int64_t species_count, double* energy, void* dEdA,
                                                    int32_t* status, void*) {
-  if (tables == nullptr || tiles == nullptr || (tiles->rows != 8 && tiles->rows != 16)) return -1;
+  if (tables == nullptr || tiles == nullptr || tiles->rows != 8) return -1;
   const int th = tables->threads_per_cta == 0 ? 256 : tables->threads_per_cta;
   const int na = 32 / tiles->rows;
   const y3b::SymTabs t = y3b::sym_view(*tables);
   const y3b::TileTabs tt = y3b::tile_view(*tiles);
-  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * std::max(t.row_width, t.max_pass_components)) * 16;
+  const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * std::max(t.row_width, t.max_pass_components)) * 16 +
+                     size_t(th / 32) * y3b::kTileStages * y3b::kStageBytes;
   if (smem > sizeof(y3b_emulated_smem)) return -1;
   const auto* a2 = static_cast<const double2*>(A);
   auto* g2 = static_cast<double2*>(dEdA);
@@ -269,8 +272,6 @@ extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_table
   })
   if (na == 4 && th == 256) EMU_TGRAD(4, 256);
   else if (na == 4 && th == 512) EMU_TGRAD(4, 512);
-  else if (na == 2 && th == 256) EMU_TGRAD(2, 256);
-  else if (na == 2 && th == 512) EMU_TGRAD(2, 512);
   else return -1;
 #undef EMU_TGRAD
   return 0;

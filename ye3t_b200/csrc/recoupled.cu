@@ -224,7 +224,7 @@ namespace {
 int check_tile_tables(const y3b_recoupled_sym_tables& t, const y3b_recoupled_tile_tables* tiles) {
   Y3B_CHECK_ARG(tiles != nullptr, "null tile tables");
   const y3b_recoupled_tile_tables& u = *tiles;
-  Y3B_CHECK_ARG(u.rows == 8 || u.rows == 16, "tile rows must be 8 or 16");
+  Y3B_CHECK_ARG(u.rows == 8, "tile rows must be 8");
   Y3B_CHECK_ARG(u.pass_count == t.pass_count, "tile tables cover %d passes, the symmetric tables %d", u.pass_count,
                 t.pass_count);
   Y3B_CHECK_ARG(t.pass_count <= kTiledMaxLM1, "the tiled pass covers intermediate L up to %d", kTiledMaxLM1 - 1);
@@ -255,7 +255,7 @@ extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_table
   const size_t per_atom = grad_smem_per_atom(t.row_width, t.max_pass_components);
   const SymTabs rt = sym_view(t);
   const TileTabs tt = tile_view(*tiles);
-  const size_t smem = per_atom * size_t(na);
+  const size_t smem = per_atom * size_t(na) + size_t(th / 32) * kTileStages * kStageBytes;
   Y3B_CHECK_ARG(smem <= 224 * 1024,
                 "tiled recoupled pass needs %lld bytes of shared memory for %d atoms per CTA (max 224 KB)",
                 (long long)smem, na);
@@ -273,9 +273,7 @@ extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_table
     Y3B_LAUNCH_CHECK();                                                                                  \
     return Y3B_OK;                                                                                       \
   }
-  if (na == 4 && th == 256) Y3B_TILED_LAUNCH(4, 256)
-  if (na == 4 && th == 512) Y3B_TILED_LAUNCH(4, 512)
-  if (na == 2 && th == 256) Y3B_TILED_LAUNCH(2, 256)
-  Y3B_TILED_LAUNCH(2, 512)
+  if (th == 256) Y3B_TILED_LAUNCH(4, 256)
+  Y3B_TILED_LAUNCH(4, 512)
 #undef Y3B_TILED_LAUNCH
 }

@@ -8,6 +8,8 @@
 
 #include <stdint.h>
 
+#include <cstring>
+
 #include "ye3t_b200.h"
 
 #ifdef Y3B_EMULATE
@@ -22,6 +24,28 @@ namespace {
 
 __host__ __device__ inline double2 rmul(double2 a, double2 b) {
   return make_double2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+// 16-byte asynchronous global-to-shared copies (cp.async, completion tracked
+// per thread in commit groups).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+#ifdef Y3B_EMULATE
+  std::memcpy(smem_dst, gmem_src, 16);
+#else
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src) : "memory");
+#endif
+}
+__device__ __forceinline__ void cp_async_commit() {
+#ifndef Y3B_EMULATE
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+#endif
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+#ifndef Y3B_EMULATE
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+#endif
 }
 
 struct RecTabs {
@@ -695,64 +719,91 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
   }
 }
 
-// Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1.  A lane
-// owns one (atom a, component M) of a tile and RL of its R = 32 / NA rows in
-// registers: per column step it reads I[column + M] for its atom once from
-// shared memory and its rows' weights (contiguous, the same for all lanes of a
-// row group), and adds acc[i] += K[row i] I.  A tile spreads over
-// NA * MC * RG lanes: MC = min(LM1, R) components and RG = R / RL row groups,
-// with RL the fewest rows per lane that keep a tile within one warp, so that
-// small L still give one tile per warp (the warps' work stays even) and large
-// L reuse each read for up to R rows.  Passes with more than MC components
-// run a tile again for the next MC of them.  Work units (tile, component
-// chunk) go to the warps in a snake order (tiles are sorted by decreasing
-// column count).  At the end of a unit each lane writes gI = (-1)^p
-// conj(acc[i]) for its rows and adds its energy shares w_M Re(I gI)
-// (w_0 = 1/2).  A column or row outside the pass is skipped and sets bad.
+// Per-warp staging ring of step 2: each stage holds four column steps of the
+// warp's current tile, their column offsets (16 bytes) and the weights of all
+// rows (4 x 8 doubles) for the species of the CTA's first atom, copied from
+// global memory kTileStages stages ahead of their use so that the weights' L2
+// latency overlaps the arithmetic.  A lane whose atom has another species
+// (rare in species-sorted groups) reads its weights from global memory.
+constexpr int kTileStages = 8;
+constexpr int kStageBytes = 16 + 4 * 8 * 8;
+
+// Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1 (tiles of
+// 8 rows, NA = 4 atoms).  A lane owns one (atom a, component M) of the warp's
+// tile and RL of its 8 rows in registers: per column step it reads
+// I[column + M] for its atom once from shared memory and its rows' weights
+// from the warp's staging ring, and adds acc[i] += K[row i] I.  A tile spreads
+// over NA * MC * RG lanes: MC = min(LM1, 8) components and RG = 8 / RL row
+// groups, with RL the fewest rows per lane that keep a tile within one warp,
+// so that small L still give one tile per warp (the warps' work stays even)
+// and large L reuse each read for up to 8 rows.  Passes with more than MC
+// components run a tile again for the next MC of them.  Work units (tile,
+// component chunk) go to the warps in a snake order (tiles are sorted by
+// decreasing column count).  At the end of a unit each lane writes
+// gI = (-1)^p conj(acc[i]) for its rows and adds its energy shares
+// w_M Re(I gI) (w_0 = 1/2).  A column or row outside the pass is skipped and
+// sets bad.
 template <int LM1, int NA, int TH>
 __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileTabs& tt, int L, int c0, int nc,
-                                                   const double2* sI, double2* sG, const double* kz, double& ep,
+                                                   const double2* sI, double2* sG, const double* kz,
+                                                   const double* kz_staged, unsigned char* ring, double& ep,
                                                    bool& bad) {
   constexpr int R = 32 / NA;                                   // rows per tile
+  static_assert(R == 8, "the staged step 2 takes tiles of 8 rows");
   constexpr int MC = LM1 < R ? LM1 : R;                        // components per unit
   constexpr int NCH = (LM1 + MC - 1) / MC;                     // component chunks per tile
   constexpr int RG0 = 32 / (NA * MC);                          // row groups that fit a warp
   constexpr int RG = RG0 >= R ? R : (RG0 >= 4 ? 4 : (RG0 >= 2 ? 2 : 1));
   constexpr int RL = R / RG;                                   // rows per lane
-  constexpr int SLOTS = 32 / (NA * MC * RG);                   // units per warp at a time
+  static_assert(NA * MC * RG <= 32 && 2 * NA * MC * RG > 32, "one unit per warp");
   constexpr int NW = TH / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int a = lane % NA, mloc = (lane / NA) % MC, rg = (lane / (NA * MC)) % RG;
-  const int slot = lane / (NA * MC * RG);
-  const bool active = slot < SLOTS;
+  const bool used = lane < NA * MC * RG;
   const int t0 = tt.tile_begin[L], t1 = tt.tile_begin[L + 1];
   if (t0 < 0 || t1 < t0 || int64_t(t1) > tt.tile_count) {
     bad = true;
     return;
   }
   const int units = (t1 - t0) * NCH;
-  const int rounds = (units + SLOTS - 1) / SLOTS;  // warp rounds of SLOTS units
   for (int k = 0;; ++k) {
-    const int rnd = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;
-    if (rnd >= rounds) break;
-    const int unit = rnd * SLOTS + slot;
-    const bool live = active && unit < units;
-    const int tile = t0 + (live ? unit / NCH : 0);
-    const int M = (live ? unit % NCH : 0) * MC + mloc;
-    const bool mine = live && M < LM1;
+    const int unit = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;  // uniform over the warp
+    if (unit >= units) break;
+    const int tile = t0 + unit / NCH;
+    const int M = (unit % NCH) * MC + mloc;
+    const bool mine = used && M < LM1;
     const int q0 = tt.tile_col_begin[tile], q1 = tt.tile_col_begin[tile + 1];
-    const int n = live ? q1 - q0 : 0;
-    if (live && (q0 < 0 || n < 0 || (n & 3) || (q0 & 3) || int64_t(q1) > tt.step_count)) {
+    const int n = q1 - q0;
+    if (q0 < 0 || n < 0 || (n & 3) || (q0 & 3) || int64_t(q1) > tt.step_count) {
       bad = true;
       continue;
     }
-    const double* kq = kz + int64_t(R) * q0 + rg * RL;
+    const int nq = n / 4;
+    const double* kq = kz_staged + int64_t(R) * q0;          // the staged species' weights
+    const double* kl = kz + int64_t(R) * q0 + rg * RL;         // this lane's species' weights
+    const bool staged = kz == kz_staged;
+    auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
+      unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
+      if (Q < nq) {
+        if (lane < 16)
+          cp_async16(st + 16 + 16 * lane, kq + int64_t(R) * 4 * Q + 2 * lane);
+        else if (lane == 16)
+          cp_async16(st, tt.col_comp + q0 + 4 * Q);
+      }
+      cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < kTileStages; ++s) issue(s);
     double2 acc[RL];
 #pragma unroll
     for (int i = 0; i < RL; ++i) acc[i] = make_double2(0.0, 0.0);
     const int Mc = mine ? M : 0;
-    for (int q = 0; q < n; q += 4) {
-      const int4 c4 = __ldg(reinterpret_cast<const int4*>(tt.col_comp + q0 + q));
+    for (int Q = 0; Q < nq; ++Q) {
+      cp_async_wait<kTileStages - 1>();
+      __syncwarp();
+      const unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
+      const int4 c4 = *reinterpret_cast<const int4*>(st);
+      const double* kst = reinterpret_cast<const double*>(st + 16) + rg * RL;
       const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -764,24 +815,28 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
           c = 0;
         }
         const double2 v = sI[(c + Mc) * NA + a];
-        const double* kr = kq + int64_t(q + j) * R;
-        if constexpr (RL == 1) {
-          const double k0 = ok ? __ldg(kr) : 0.0;
-          acc[0].x = fma(k0, v.x, acc[0].x);
-          acc[0].y = fma(k0, v.y, acc[0].y);
-        } else {
+        double kk[RL];
+        if (staged) {
+          const double* kr = kst + j * R;
 #pragma unroll
-          for (int i = 0; i < RL; i += 2) {
-            const double2 k2 = __ldg(reinterpret_cast<const double2*>(kr + i));
-            const double k0 = ok ? k2.x : 0.0, k1 = ok ? k2.y : 0.0;
-            acc[i].x = fma(k0, v.x, acc[i].x);
-            acc[i].y = fma(k0, v.y, acc[i].y);
-            acc[i + 1].x = fma(k1, v.x, acc[i + 1].x);
-            acc[i + 1].y = fma(k1, v.y, acc[i + 1].y);
-          }
+          for (int i = 0; i < RL; ++i) kk[i] = kr[i];
+        } else {
+          const double* kr = kl + int64_t(R) * (4 * Q + j);
+#pragma unroll
+          for (int i = 0; i < RL; ++i) kk[i] = __ldg(kr + i);
+        }
+#pragma unroll
+        for (int i = 0; i < RL; ++i) {
+          const double k0 = ok ? kk[i] : 0.0;
+          acc[i].x = fma(k0, v.x, acc[i].x);
+          acc[i].y = fma(k0, v.y, acc[i].y);
         }
       }
+      __syncwarp();
+      issue(Q + kTileStages);
     }
+    cp_async_wait<0>();
+    __syncwarp();
     if (mine) {
 #pragma unroll
       for (int i = 0; i < RL; ++i) {
@@ -824,6 +879,8 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
   double2* sG = sI + cw * NA;
   const int tid = threadIdx.x;
   const int lane = tid & 31, a_lane = lane % NA;
+  // this warp's staging ring for step 2, after the component regions
+  unsigned char* ring = reinterpret_cast<unsigned char*>(sG + cw * NA) + (tid >> 5) * kTileStages * kStageBytes;
   const int64_t groups = (atom_count + NA - 1) / NA;
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
     const int64_t first = grp * NA;
@@ -850,6 +907,9 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
       z = 0;
     }
     const double* kz = tt.kval + int64_t(z) * int64_t(tt.rows) * tt.step_count;
+    int z0 = species[idx[0]];  // the species whose weights the staging rings hold
+    if (z0 < 0 || z0 >= species_count) z0 = 0;
+    const double* kz0 = tt.kval + int64_t(z0) * int64_t(tt.rows) * tt.step_count;
     for (int i = tid; i < W * NA; i += TH) {
       const int a = i % NA, e = i / NA;
       sA[i] = a < nv ? A[idx[a] * W + e] : make_double2(0.0, 0.0);
@@ -868,15 +928,15 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
       build_components_lanes<NA, TH>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       switch (L) {
-        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
-        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, ep, bad); break;
+        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
       }
       __syncthreads();
       // 3. back-propagation: lanes (work item, atom) sum their item's chunk of an
@@ -903,20 +963,27 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
               continue;
             }
             double2 ga = make_double2(0.0, 0.0);
-            for (int e = e0 + j; e < e1; e += R) {
-              const int4 rec = __ldg(tt.bp_pack + e);  // (code, other, value lo, value hi)
-              const int gi = rec.x >> 1;
-              const int o = rec.y;
-              if (rec.x < 0 || gi >= nc || o >= W) {
-                bad = true;
-                continue;
+            for (int e = e0 + j; e < e1; e += 4 * R) {  // four records in flight per lane
+              int4 recs[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                recs[u] = e + u * R < e1 ? __ldg(tt.bp_pack + e + u * R) : make_int4(0, -1, 0, 0);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int4 rec = recs[u];  // (code, other, value lo, value hi)
+                const int gi = rec.x >> 1;
+                const int o = rec.y;
+                if (rec.x < 0 || gi >= nc || o >= W) {
+                  bad = true;
+                  continue;
+                }
+                const double cv = __hiloint2double(rec.w, rec.z);
+                double2 gg = sG[gi * NA + a_lane];
+                if (rec.x & 1) gg.y = -gg.y;
+                const double2 term = o < 0 ? gg : rmul(gg, sA[o * NA + a_lane]);
+                ga.x = fma(cv, term.x, ga.x);
+                ga.y = fma(cv, term.y, ga.y);
               }
-              const double cv = __hiloint2double(rec.w, rec.z);
-              double2 gg = sG[gi * NA + a_lane];
-              if (rec.x & 1) gg.y = -gg.y;
-              const double2 term = o < 0 ? gg : rmul(gg, sA[o * NA + a_lane]);
-              ga.x = fma(cv, term.x, ga.x);
-              ga.y = fma(cv, term.y, ga.y);
             }
             if (it < ni) part[it * NA + a_lane] = ga;
           }

@@ -1050,11 +1050,11 @@ class RecoupledEvaluator:
     ``M >= 0`` components (``RecoupledSymTables``), valid only for physical densities
     ``A[n, l, -m] = (-1)^m conj(A[n, l, m])`` such as ``ACEEvaluator.density`` gives.
 
-    ``tile_rows`` (8 or 16; symmetric passes only) makes ``energy_grad`` form the
+    ``tile_rows`` (8; symmetric passes only) makes ``energy_grad`` form the
     components' adjoints from dense tiles of the contraction weights
     (``RecoupledTiles``, ``y3b_ace_recoupled_energy_grad_tiled``): a CTA then holds
-    ``32 // tile_rows`` atoms, grouped in species order so that a CTA's atoms share one
-    species' tile weights (``sort_species``)."""
+    4 atoms, grouped in species order so that a CTA's atoms share one species' tile
+    weights (``sort_species``)."""
 
     def __init__(self, bundle: ACEBundle, device, weights: np.ndarray = None, plan: "RecoupledPlan" = None,
                  atoms_per_cta: int = 1, threads_per_cta: int = 256, symmetric: bool = False,
@@ -1064,8 +1064,8 @@ class RecoupledEvaluator:
             raise ValueError("atoms_per_cta must be in [1, 4]")
         if int(threads_per_cta) not in (256, 512):
             raise ValueError("threads_per_cta must be 256 or 512")
-        if int(tile_rows) not in (0, 8, 16):
-            raise ValueError("tile_rows must be 0 (lists), 8 or 16")
+        if int(tile_rows) not in (0, 8):
+            raise ValueError("tile_rows must be 0 (lists) or 8")
         if tile_rows and not symmetric:
             raise ValueError("the tiled adjoint is a form of the symmetric passes (symmetric=True)")
         self.device = torch.device(device)
