@@ -72,6 +72,8 @@ inline double __shfl_xor_sync(unsigned, double v, int lane_mask) {
   return r;
 }
 using std::fma;
+using std::max;
+using std::min;
 
 #include "recoupled_kernels.cuh"
 

@@ -743,11 +743,87 @@ constexpr int kStageBytes = 16 + 4 * 8 * 8;
 // gI = (-1)^p conj(acc[i]) for its rows and adds its energy shares
 // w_M Re(I gI) (w_0 = 1/2).  A column or row outside the pass is skipped and
 // sets bad.
+// Column walk of one unit: acc[i] += K[row i, q] I[column q + M] for the
+// unit's column steps, four per stage of the staging ring (STAGED: the weights
+// of the CTA's one species from the ring; otherwise this lane's species'
+// weights from global memory).  A quad of columns outside the pass is skipped
+// and sets bad (the columns are the same for every lane of the warp).
+template <bool STAGED, int LM1, int R, int RL, int NA>
+__device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, int nc, const double2* sIa,
+                                          const double* kq, const double* kl, int rg, unsigned char* ring,
+                                          double2 (&acc)[RL], bool& bad) {
+  const int lane = threadIdx.x & 31;
+  auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
+    unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
+    if (Q < nq) {
+      if (STAGED && lane < 16)
+        cp_async16(st + 16 + 16 * lane, kq + int64_t(R) * 4 * Q + 2 * lane);
+      else if (lane == 16)
+        cp_async16(st, tt.col_comp + q0 + 4 * Q);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < kTileStages; ++s) issue(s);
+  for (int Q = 0; Q < nq; ++Q) {
+    cp_async_wait<kTileStages - 1>();
+    __syncwarp();
+    const unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
+    const int4 c4 = *reinterpret_cast<const int4*>(st);
+    const int cmin = min(min(c4.x, c4.y), min(c4.z, c4.w)), cmax = max(max(c4.x, c4.y), max(c4.z, c4.w));
+    if (cmin < 0 || cmax + LM1 > nc) {
+      bad = true;
+    } else {
+      const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
+      const double* kst = reinterpret_cast<const double*>(st + 16) + rg * RL;
+      const double* kg = kl + int64_t(R) * 4 * Q;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const double2 v = sIa[cs[j] * NA];
+        const double* kr = STAGED ? kst + j * R : kg + j * R;
+        if constexpr (RL == 1) {
+          const double k0 = STAGED ? kr[0] : __ldg(kr);
+          acc[0].x = fma(k0, v.x, acc[0].x);
+          acc[0].y = fma(k0, v.y, acc[0].y);
+        } else {
+#pragma unroll
+          for (int i = 0; i < RL; i += 2) {
+            const double2 k2 = STAGED ? *reinterpret_cast<const double2*>(kr + i)
+                                      : __ldg(reinterpret_cast<const double2*>(kr + i));
+            acc[i].x = fma(k2.x, v.x, acc[i].x);
+            acc[i].y = fma(k2.x, v.y, acc[i].y);
+            acc[i + 1].x = fma(k2.y, v.x, acc[i + 1].x);
+            acc[i + 1].y = fma(k2.y, v.y, acc[i + 1].y);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    issue(Q + kTileStages);
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+}
+
+// Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1 (tiles of
+// 8 rows, NA = 4 atoms).  A lane owns one (atom a, component M) of the warp's
+// tile and RL of its 8 rows in registers: per column step it reads
+// I[column + M] for its atom once from shared memory and its rows' weights
+// (tile_walk), and adds acc[i] += K[row i] I.  A tile spreads over
+// NA * MC * RG lanes: MC = min(LM1, 8) components and RG = 8 / RL row groups,
+// with RL the fewest rows per lane that keep a tile within one warp, so that
+// small L still give one tile per warp (the warps' work stays even) and large
+// L reuse each read for up to 8 rows.  Passes with more than MC components
+// run a tile again for the next MC of them.  Work units (tile, component
+// chunk) go to the warps in a snake order (tiles are sorted by decreasing
+// column count).  At the end of a unit each lane writes gI = (-1)^p
+// conj(acc[i]) for its rows and adds its energy shares w_M Re(I gI)
+// (w_0 = 1/2).  A column or row outside the pass is skipped and sets bad.
 template <int LM1, int NA, int TH>
 __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileTabs& tt, int L, int c0, int nc,
                                                    const double2* sI, double2* sG, const double* kz,
-                                                   const double* kz_staged, unsigned char* ring, double& ep,
-                                                   bool& bad) {
+                                                   const double* kz_staged, bool staged, unsigned char* ring,
+                                                   double& ep, bool& bad) {
   constexpr int R = 32 / NA;                                   // rows per tile
   static_assert(R == 8, "the staged step 2 takes tiles of 8 rows");
   constexpr int MC = LM1 < R ? LM1 : R;                        // components per unit
@@ -778,65 +854,16 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
       bad = true;
       continue;
     }
-    const int nq = n / 4;
-    const double* kq = kz_staged + int64_t(R) * q0;          // the staged species' weights
-    const double* kl = kz + int64_t(R) * q0 + rg * RL;         // this lane's species' weights
-    const bool staged = kz == kz_staged;
-    auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
-      unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
-      if (Q < nq) {
-        if (lane < 16)
-          cp_async16(st + 16 + 16 * lane, kq + int64_t(R) * 4 * Q + 2 * lane);
-        else if (lane == 16)
-          cp_async16(st, tt.col_comp + q0 + 4 * Q);
-      }
-      cp_async_commit();
-    };
-#pragma unroll
-    for (int s = 0; s < kTileStages; ++s) issue(s);
     double2 acc[RL];
 #pragma unroll
     for (int i = 0; i < RL; ++i) acc[i] = make_double2(0.0, 0.0);
-    const int Mc = mine ? M : 0;
-    for (int Q = 0; Q < nq; ++Q) {
-      cp_async_wait<kTileStages - 1>();
-      __syncwarp();
-      const unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
-      const int4 c4 = *reinterpret_cast<const int4*>(st);
-      const double* kst = reinterpret_cast<const double*>(st + 16) + rg * RL;
-      const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        int c = cs[j];
-        bool ok = true;
-        if (c < 0 || c + LM1 > nc) {
-          bad = true;
-          ok = false;
-          c = 0;
-        }
-        const double2 v = sI[(c + Mc) * NA + a];
-        double kk[RL];
-        if (staged) {
-          const double* kr = kst + j * R;
-#pragma unroll
-          for (int i = 0; i < RL; ++i) kk[i] = kr[i];
-        } else {
-          const double* kr = kl + int64_t(R) * (4 * Q + j);
-#pragma unroll
-          for (int i = 0; i < RL; ++i) kk[i] = __ldg(kr + i);
-        }
-#pragma unroll
-        for (int i = 0; i < RL; ++i) {
-          const double k0 = ok ? kk[i] : 0.0;
-          acc[i].x = fma(k0, v.x, acc[i].x);
-          acc[i].y = fma(k0, v.y, acc[i].y);
-        }
-      }
-      __syncwarp();
-      issue(Q + kTileStages);
-    }
-    cp_async_wait<0>();
-    __syncwarp();
+    const double2* sIa = sI + (mine ? M : 0) * NA + a;
+    const double* kq = kz_staged + int64_t(R) * q0;       // the staged species' weights
+    const double* kl = kz + int64_t(R) * q0 + rg * RL;    // this lane's species' weights
+    if (staged)  // uniform over the CTA
+      tile_walk<true, LM1, R, RL, NA>(tt, q0, n / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
+    else
+      tile_walk<false, LM1, R, RL, NA>(tt, q0, n / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
     if (mine) {
 #pragma unroll
       for (int i = 0; i < RL; ++i) {
@@ -907,8 +934,17 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
       z = 0;
     }
     const double* kz = tt.kval + int64_t(z) * int64_t(tt.rows) * tt.step_count;
-    int z0 = species[idx[0]];  // the species whose weights the staging rings hold
-    if (z0 < 0 || z0 >= species_count) z0 = 0;
+    // the staging rings hold one species' weights: those of the CTA's atoms when
+    // they all share it (species-sorted groups), else each lane reads its own
+    bool uniform_z = true;
+    int z0 = 0;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      int za = species[idx[a]];
+      if (za < 0 || za >= species_count) za = 0;
+      if (a == 0) z0 = za;
+      uniform_z = uniform_z && za == z0;
+    }
     const double* kz0 = tt.kval + int64_t(z0) * int64_t(tt.rows) * tt.step_count;
     for (int i = tid; i < W * NA; i += TH) {
       const int a = i % NA, e = i / NA;
@@ -928,15 +964,15 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
       build_components_lanes<NA, TH>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       switch (L) {
-        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
-        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, ring, ep, bad); break;
+        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
       }
       __syncthreads();
       // 3. back-propagation: lanes (work item, atom) sum their item's chunk of an
