@@ -702,6 +702,7 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
     } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
       bad = true;
     } else {
+      double2 v2 = make_double2(0.0, 0.0);  // odd terms, added at the end
       for (int q = d.z; q < d.z + d.w; ++q) {
         const int ix = __ldg(t.cg_index + q);
         const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
@@ -711,9 +712,12 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
         }
         const double cv = __ldg(t.cg_value + q);
         const double2 p = rmul(sA[ia * NA + a], sA[ib * NA + a]);
-        v.x = fma(cv, p.x, v.x);
-        v.y = fma(cv, p.y, v.y);
+        double2& vv = ((q - d.z) & 1) ? v2 : v;
+        vv.x = fma(cv, p.x, vv.x);
+        vv.y = fma(cv, p.y, vv.y);
       }
+      v.x += v2.x;
+      v.y += v2.y;
     }
     sI[c * NA + a] = v;
   }
@@ -753,6 +757,12 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
                                           const double* kq, const double* kl, int rg, unsigned char* ring,
                                           double2 (&acc)[RL], bool& bad) {
   const int lane = threadIdx.x & 31;
+  // with up to 4 rows per lane, even and odd column steps accumulate
+  // separately (two independent FMA chains per output), added at the end
+  constexpr bool kTwo = RL <= 4;
+  double2 acc2[RL];
+#pragma unroll
+  for (int i = 0; i < RL; ++i) acc2[i] = make_double2(0.0, 0.0);
   auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
     unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
     if (Q < nq) {
@@ -779,21 +789,22 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
       const double* kg = kl + int64_t(R) * 4 * Q;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
+        double2(&ac)[RL] = (kTwo && (j & 1)) ? acc2 : acc;
         const double2 v = sIa[cs[j] * NA];
         const double* kr = STAGED ? kst + j * R : kg + j * R;
         if constexpr (RL == 1) {
           const double k0 = STAGED ? kr[0] : __ldg(kr);
-          acc[0].x = fma(k0, v.x, acc[0].x);
-          acc[0].y = fma(k0, v.y, acc[0].y);
+          ac[0].x = fma(k0, v.x, ac[0].x);
+          ac[0].y = fma(k0, v.y, ac[0].y);
         } else {
 #pragma unroll
           for (int i = 0; i < RL; i += 2) {
             const double2 k2 = STAGED ? *reinterpret_cast<const double2*>(kr + i)
                                       : __ldg(reinterpret_cast<const double2*>(kr + i));
-            acc[i].x = fma(k2.x, v.x, acc[i].x);
-            acc[i].y = fma(k2.x, v.y, acc[i].y);
-            acc[i + 1].x = fma(k2.y, v.x, acc[i + 1].x);
-            acc[i + 1].y = fma(k2.y, v.y, acc[i + 1].y);
+            ac[i].x = fma(k2.x, v.x, ac[i].x);
+            ac[i].y = fma(k2.x, v.y, ac[i].y);
+            ac[i + 1].x = fma(k2.y, v.x, ac[i + 1].x);
+            ac[i + 1].y = fma(k2.y, v.y, ac[i + 1].y);
           }
         }
       }
@@ -803,6 +814,13 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
   }
   cp_async_wait<0>();
   __syncwarp();
+  if constexpr (kTwo) {
+#pragma unroll
+    for (int i = 0; i < RL; ++i) {
+      acc[i].x += acc2[i].x;
+      acc[i].y += acc2[i].y;
+    }
+  }
 }
 
 // Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1 (tiles of
@@ -998,7 +1016,9 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
               bad = true;  // uniform over the warp
               continue;
             }
-            double2 ga = make_double2(0.0, 0.0);
+            double2 gp[4];  // four partial sums (records u = 0..3 of each row), added in order
+#pragma unroll
+            for (int u = 0; u < 4; ++u) gp[u] = make_double2(0.0, 0.0);
             for (int e = e0 + j; e < e1; e += 4 * R) {  // four records in flight per lane
               int4 recs[4];
 #pragma unroll
@@ -1017,10 +1037,12 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
                 double2 gg = sG[gi * NA + a_lane];
                 if (rec.x & 1) gg.y = -gg.y;
                 const double2 term = o < 0 ? gg : rmul(gg, sA[o * NA + a_lane]);
-                ga.x = fma(cv, term.x, ga.x);
-                ga.y = fma(cv, term.y, ga.y);
+                gp[u].x = fma(cv, term.x, gp[u].x);
+                gp[u].y = fma(cv, term.y, gp[u].y);
               }
             }
+            const double2 ga = make_double2((gp[0].x + gp[1].x) + (gp[2].x + gp[3].x),
+                                            (gp[0].y + gp[1].y) + (gp[2].y + gp[3].y));
             if (it < ni) part[it * NA + a_lane] = ga;
           }
         }
