@@ -25,7 +25,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 os.environ.setdefault("YE3T_ENABLE_CPP_RUNTIME_JIT", "1")
-os.environ.setdefault("TORCH_EXTENSIONS_DIR", os.path.join(REPO, "_work", "torch_ext"))
+os.environ.setdefault("TORCH_EXTENSIONS_DIR", os.path.join(REPO, "oracle", "_build", "torch_ext"))
 
 from ye3t.couplings import compile_ace_factorized_schedules_by_L  # noqa: E402
 from ye3t import couplings  # noqa: E402
@@ -36,8 +36,12 @@ from ye3t.runtime.symmetric_power import symmetric_power_product_plan_contractio
 
 from ye3t_b200.schedules import ACEBundle, ScheduleRecord  # noqa: E402
 
-REF_FIXTURE = os.path.join(os.environ.get("YE3T_REFERENCE", "/root/reference"), "tests", "fixtures",
-                           "shared_monomial_plan_v1.txt")
+from oracle.reference import reference_dir  # noqa: E402
+
+REF_DIR = reference_dir()
+if REF_DIR is None:
+    raise SystemExit("the reference checkout is needed: set YE3T_REFERENCE (oracle/reference.py)")
+REF_FIXTURE = os.path.join(REF_DIR, "tests", "fixtures", "shared_monomial_plan_v1.txt")
 
 
 def _record_arrays(prefix, rec: ScheduleRecord, out: dict):
@@ -524,8 +528,7 @@ def hierarchical_fixture():
     complex block inputs (``ye3t/runtime/hierarchical.py:514``)."""
     import importlib.util
     import tempfile
-    ref = os.environ.get("YE3T_REFERENCE", "/root/reference")
-    sys.path.insert(0, os.path.join(ref, "tests"))
+    sys.path.insert(0, os.path.join(REF_DIR, "tests"))
     import test_execution_plan as te
     import test_hierarchical_runtime as th
     from ye3t.runtime import YE3THierarchicalRepeatedBlockModule
