@@ -263,7 +263,7 @@ extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_table
   const y3b::SymTabs t = y3b::sym_view(*tables);
   const y3b::TileTabs tt = y3b::tile_view(*tiles);
   const size_t smem = size_t(na) * size_t(2 * t.row_width + 2 * std::max(t.row_width, t.max_pass_components)) * 16 +
-                     size_t(th / 32) * y3b::kTileStages * y3b::kStageBytes;
+                     size_t(th / 32) * y3b::kTileStages * y3b::kStageBytes + size_t(tiles->scratch_slots) * 512;
   if (smem > sizeof(y3b_emulated_smem)) return -1;
   const auto* a2 = static_cast<const double2*>(A);
   auto* g2 = static_cast<double2*>(dEdA);

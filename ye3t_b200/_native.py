@@ -85,7 +85,8 @@ class RecoupledTileTables(ctypes.Structure):
         ("group_count", I64), ("pack_count", I64),
         ("tile_begin", VP), ("tile_row", VP), ("tile_col_begin", VP), ("col_comp", VP),
         ("bp_item_begin", VP), ("t_item_begin", VP), ("t_item", VP), ("bp_group_begin", VP), ("bp_group_off", VP),
-        ("bp_pack", VP), ("kval", VP),
+        ("bp_pack", VP), ("unit_count", I64), ("fix_count", I64), ("scratch_slots", I32), ("unit_begin", VP),
+        ("unit", VP), ("fix_begin", VP), ("fix", VP), ("kval", VP),
     ]
 
 

@@ -229,8 +229,11 @@ int check_tile_tables(const y3b_recoupled_sym_tables& t, const y3b_recoupled_til
                 t.pass_count);
   Y3B_CHECK_ARG(t.pass_count <= kTiledMaxLM1, "the tiled pass covers intermediate L up to %d", kTiledMaxLM1 - 1);
   Y3B_CHECK_ARG(u.tile_count >= 0 && u.step_count >= 0, "negative tile table sizes");
-  Y3B_CHECK_ARG(u.tile_begin && u.tile_row && u.tile_col_begin && (u.step_count == 0 || (u.col_comp && u.kval)),
+  Y3B_CHECK_ARG(u.tile_begin && u.tile_row && u.tile_col_begin && (u.step_count == 0 || (u.col_comp && u.kval)) &&
+                    u.unit_begin && u.fix_begin && (u.unit_count == 0 || u.unit) && (u.fix_count == 0 || u.fix),
                 "null tile table pointer");
+  Y3B_CHECK_ARG(reinterpret_cast<uintptr_t>(u.unit) % 16 == 0 && reinterpret_cast<uintptr_t>(u.fix) % 16 == 0,
+                "unit and fix must be 16-byte aligned");
   Y3B_CHECK_ARG(reinterpret_cast<uintptr_t>(u.col_comp) % 16 == 0 && reinterpret_cast<uintptr_t>(u.kval) % 16 == 0,
                 "col_comp and kval must be 16-byte aligned");
   return Y3B_OK;
@@ -255,7 +258,9 @@ extern "C" int y3b_ace_recoupled_energy_grad_tiled(const y3b_recoupled_sym_table
   const size_t per_atom = grad_smem_per_atom(t.row_width, t.max_pass_components);
   const SymTabs rt = sym_view(t);
   const TileTabs tt = tile_view(*tiles);
-  const size_t smem = per_atom * size_t(na) + size_t(th / 32) * kTileStages * kStageBytes;
+  Y3B_CHECK_ARG(tiles->scratch_slots >= 0 && tiles->scratch_slots <= 64, "scratch_slots must be in [0, 64]");
+  const size_t smem = per_atom * size_t(na) + size_t(th / 32) * kTileStages * kStageBytes +
+                      size_t(tiles->scratch_slots) * 512;
   Y3B_CHECK_ARG(smem <= 224 * 1024,
                 "tiled recoupled pass needs %lld bytes of shared memory for %d atoms per CTA (max 224 KB)",
                 (long long)smem, na);

@@ -668,13 +668,21 @@ struct TileTabs {
   const int32_t* bp_group_begin;
   const int32_t* bp_group_off;
   const int4* bp_pack;
+  int64_t unit_count, fix_count;
+  int32_t scratch_slots;
+  const int32_t* unit_begin;
+  const int4* unit;
+  const int32_t* fix_begin;
+  const int4* fix;
   const double* kval;
 };
 
 inline TileTabs tile_view(const y3b_recoupled_tile_tables& t) {
   return TileTabs{t.rows, t.pass_count, t.tile_count, t.step_count, t.item_count, t.group_count, t.pack_count,
                   t.tile_begin, t.tile_row, t.tile_col_begin, t.col_comp, t.bp_item_begin, t.t_item_begin,
-                  t.t_item, t.bp_group_begin, t.bp_group_off, reinterpret_cast<const int4*>(t.bp_pack), t.kval};
+                  t.t_item, t.bp_group_begin, t.bp_group_off, reinterpret_cast<const int4*>(t.bp_pack),
+                  t.unit_count, t.fix_count, t.scratch_slots, t.unit_begin, reinterpret_cast<const int4*>(t.unit),
+                  t.fix_begin, reinterpret_cast<const int4*>(t.fix), t.kval};
 }
 
 // Step 1 of the tiled adjoint with lanes as (component, atom): a warp builds
@@ -702,7 +710,6 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
     } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
       bad = true;
     } else {
-      double2 v2 = make_double2(0.0, 0.0);  // odd terms, added at the end
       for (int q = d.z; q < d.z + d.w; ++q) {
         const int ix = __ldg(t.cg_index + q);
         const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
@@ -712,12 +719,9 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
         }
         const double cv = __ldg(t.cg_value + q);
         const double2 p = rmul(sA[ia * NA + a], sA[ib * NA + a]);
-        double2& vv = ((q - d.z) & 1) ? v2 : v;
-        vv.x = fma(cv, p.x, vv.x);
-        vv.y = fma(cv, p.y, vv.y);
+        v.x = fma(cv, p.x, v.x);
+        v.y = fma(cv, p.y, v.y);
       }
-      v.x += v2.x;
-      v.y += v2.y;
     }
     sI[c * NA + a] = v;
   }
@@ -732,21 +736,6 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
 constexpr int kTileStages = 8;
 constexpr int kStageBytes = 16 + 4 * 8 * 8;
 
-// Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1 (tiles of
-// 8 rows, NA = 4 atoms).  A lane owns one (atom a, component M) of the warp's
-// tile and RL of its 8 rows in registers: per column step it reads
-// I[column + M] for its atom once from shared memory and its rows' weights
-// from the warp's staging ring, and adds acc[i] += K[row i] I.  A tile spreads
-// over NA * MC * RG lanes: MC = min(LM1, 8) components and RG = 8 / RL row
-// groups, with RL the fewest rows per lane that keep a tile within one warp,
-// so that small L still give one tile per warp (the warps' work stays even)
-// and large L reuse each read for up to 8 rows.  Passes with more than MC
-// components run a tile again for the next MC of them.  Work units (tile,
-// component chunk) go to the warps in a snake order (tiles are sorted by
-// decreasing column count).  At the end of a unit each lane writes
-// gI = (-1)^p conj(acc[i]) for its rows and adds its energy shares
-// w_M Re(I gI) (w_0 = 1/2).  A column or row outside the pass is skipped and
-// sets bad.
 // Column walk of one unit: acc[i] += K[row i, q] I[column q + M] for the
 // unit's column steps, four per stage of the staging ring (STAGED: the weights
 // of the CTA's one species from the ring; otherwise this lane's species'
@@ -757,12 +746,6 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
                                           const double* kq, const double* kl, int rg, unsigned char* ring,
                                           double2 (&acc)[RL], bool& bad) {
   const int lane = threadIdx.x & 31;
-  // with up to 4 rows per lane, even and odd column steps accumulate
-  // separately (two independent FMA chains per output), added at the end
-  constexpr bool kTwo = RL <= 4;
-  double2 acc2[RL];
-#pragma unroll
-  for (int i = 0; i < RL; ++i) acc2[i] = make_double2(0.0, 0.0);
   auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
     unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
     if (Q < nq) {
@@ -789,22 +772,21 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
       const double* kg = kl + int64_t(R) * 4 * Q;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        double2(&ac)[RL] = (kTwo && (j & 1)) ? acc2 : acc;
         const double2 v = sIa[cs[j] * NA];
         const double* kr = STAGED ? kst + j * R : kg + j * R;
         if constexpr (RL == 1) {
           const double k0 = STAGED ? kr[0] : __ldg(kr);
-          ac[0].x = fma(k0, v.x, ac[0].x);
-          ac[0].y = fma(k0, v.y, ac[0].y);
+          acc[0].x = fma(k0, v.x, acc[0].x);
+          acc[0].y = fma(k0, v.y, acc[0].y);
         } else {
 #pragma unroll
           for (int i = 0; i < RL; i += 2) {
             const double2 k2 = STAGED ? *reinterpret_cast<const double2*>(kr + i)
                                       : __ldg(reinterpret_cast<const double2*>(kr + i));
-            ac[i].x = fma(k2.x, v.x, ac[i].x);
-            ac[i].y = fma(k2.x, v.y, ac[i].y);
-            ac[i + 1].x = fma(k2.y, v.x, ac[i + 1].x);
-            ac[i + 1].y = fma(k2.y, v.y, ac[i + 1].y);
+            acc[i].x = fma(k2.x, v.x, acc[i].x);
+            acc[i].y = fma(k2.x, v.y, acc[i].y);
+            acc[i + 1].x = fma(k2.y, v.x, acc[i + 1].x);
+            acc[i + 1].y = fma(k2.y, v.y, acc[i + 1].y);
           }
         }
       }
@@ -814,13 +796,6 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
   }
   cp_async_wait<0>();
   __syncwarp();
-  if constexpr (kTwo) {
-#pragma unroll
-    for (int i = 0; i < RL; ++i) {
-      acc[i].x += acc2[i].x;
-      acc[i].y += acc2[i].y;
-    }
-  }
 }
 
 // Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1 (tiles of
@@ -830,18 +805,22 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
 // (tile_walk), and adds acc[i] += K[row i] I.  A tile spreads over
 // NA * MC * RG lanes: MC = min(LM1, 8) components and RG = 8 / RL row groups,
 // with RL the fewest rows per lane that keep a tile within one warp, so that
-// small L still give one tile per warp (the warps' work stays even) and large
-// L reuse each read for up to 8 rows.  Passes with more than MC components
-// run a tile again for the next MC of them.  Work units (tile, component
-// chunk) go to the warps in a snake order (tiles are sorted by decreasing
-// column count).  At the end of a unit each lane writes gI = (-1)^p
-// conj(acc[i]) for its rows and adds its energy shares w_M Re(I gI)
-// (w_0 = 1/2).  A column or row outside the pass is skipped and sets bad.
+// small L still give one tile per warp and large L reuse each read for up to
+// 8 rows.  Passes with more than MC components run a tile again for the next
+// MC of them.  The work units (a tile, or a chunk of a long tile's columns,
+// ordered by decreasing length) go to the warps in a snake order.  A whole
+// tile ends by writing gI = (-1)^p conj(acc[i]) for its rows and adding the
+// energy shares w_M Re(I gI) (w_0 = 1/2); the first chunk of a cut tile
+// leaves its sums in the adjoint slots and a later chunk in its scratch slot,
+// and after a barrier each cut tile's fix-up adds the later chunks in slot
+// order and finishes as a whole tile does.  Every sum has a fixed order, so
+// the results do not depend on which warp runs what.  A column, row or unit
+// outside the pass is skipped and sets bad.
 template <int LM1, int NA, int TH>
 __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileTabs& tt, int L, int c0, int nc,
                                                    const double2* sI, double2* sG, const double* kz,
                                                    const double* kz_staged, bool staged, unsigned char* ring,
-                                                   double& ep, bool& bad) {
+                                                   double2* scratch, double& ep, bool& bad) {
   constexpr int R = 32 / NA;                                   // rows per tile
   static_assert(R == 8, "the staged step 2 takes tiles of 8 rows");
   constexpr int MC = LM1 < R ? LM1 : R;                        // components per unit
@@ -849,26 +828,50 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
   constexpr int RG0 = 32 / (NA * MC);                          // row groups that fit a warp
   constexpr int RG = RG0 >= R ? R : (RG0 >= 4 ? 4 : (RG0 >= 2 ? 2 : 1));
   constexpr int RL = R / RG;                                   // rows per lane
+  constexpr int SLOT = R * MC * NA;                            // double2 per scratch slot
   static_assert(NA * MC * RG <= 32 && 2 * NA * MC * RG > 32, "one unit per warp");
   constexpr int NW = TH / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int a = lane % NA, mloc = (lane / NA) % MC, rg = (lane / (NA * MC)) % RG;
   const bool used = lane < NA * MC * RG;
   const int t0 = tt.tile_begin[L], t1 = tt.tile_begin[L + 1];
-  if (t0 < 0 || t1 < t0 || int64_t(t1) > tt.tile_count) {
+  const int u0 = tt.unit_begin[L], u1 = tt.unit_begin[L + 1];
+  if (t0 < 0 || t1 < t0 || int64_t(t1) > tt.tile_count || u0 < 0 || u1 < u0 || int64_t(u1) > tt.unit_count) {
     bad = true;
     return;
   }
-  const int units = (t1 - t0) * NCH;
+  // a whole tile's ending: gI and the energy shares from the lane's sums
+  auto finish = [&](int tile, int M, const double2 (&acc)[RL]) {
+#pragma unroll
+    for (int i = 0; i < RL; ++i) {
+      const int rowc = tt.tile_row[int64_t(tile) * R + rg * RL + i];
+      if (rowc < -1 || rowc + LM1 > nc) {
+        bad = true;
+      } else if (rowc >= 0) {
+        const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
+        const double2 g = make_double2(sg * acc[i].x, -sg * acc[i].y);
+        sG[(rowc + M) * NA + a] = g;
+        const double2 iv = sI[(rowc + M) * NA + a];
+        ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
+      }
+    }
+  };
+  const int items = (u1 - u0) * NCH;
   for (int k = 0;; ++k) {
-    const int unit = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;  // uniform over the warp
-    if (unit >= units) break;
-    const int tile = t0 + unit / NCH;
-    const int M = (unit % NCH) * MC + mloc;
+    const int item = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;  // uniform over the warp
+    if (item >= items) break;
+    const int4 u = __ldg(tt.unit + u0 + item / NCH);  // (tile, first step, end step, kind)
+    const int tile = u.x;
+    const int M = (item % NCH) * MC + mloc;
     const bool mine = used && M < LM1;
+    if (tile < t0 || tile >= t1 || u.w < -2 || (u.w >= 0 && (NCH > 1 || (u.w + 1) * MC > tt.scratch_slots))) {
+      bad = true;
+      continue;
+    }
     const int q0 = tt.tile_col_begin[tile], q1 = tt.tile_col_begin[tile + 1];
-    const int n = q1 - q0;
-    if (q0 < 0 || n < 0 || (n & 3) || (q0 & 3) || int64_t(q1) > tt.step_count) {
+    const int qs = q0 + u.y, qe = q0 + u.z;
+    if (q0 < 0 || q1 < q0 || (q0 & 3) || u.y < 0 || u.z < u.y || ((u.z - u.y) & 3) || (u.y & 3) || qe > q1 ||
+        int64_t(q1) > tt.step_count) {
       bad = true;
       continue;
     }
@@ -876,26 +879,54 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
 #pragma unroll
     for (int i = 0; i < RL; ++i) acc[i] = make_double2(0.0, 0.0);
     const double2* sIa = sI + (mine ? M : 0) * NA + a;
-    const double* kq = kz_staged + int64_t(R) * q0;       // the staged species' weights
-    const double* kl = kz + int64_t(R) * q0 + rg * RL;    // this lane's species' weights
+    const double* kq = kz_staged + int64_t(R) * qs;       // the staged species' weights
+    const double* kl = kz + int64_t(R) * qs + rg * RL;    // this lane's species' weights
     if (staged)  // uniform over the CTA
-      tile_walk<true, LM1, R, RL, NA>(tt, q0, n / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
+      tile_walk<true, LM1, R, RL, NA>(tt, qs, (qe - qs) / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
     else
-      tile_walk<false, LM1, R, RL, NA>(tt, q0, n / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
-    if (mine) {
+      tile_walk<false, LM1, R, RL, NA>(tt, qs, (qe - qs) / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
+    if (!mine) continue;
+    if (u.w == -1) {
+      finish(tile, M, acc);
+    } else {
 #pragma unroll
       for (int i = 0; i < RL; ++i) {
         const int rowc = tt.tile_row[int64_t(tile) * R + rg * RL + i];
         if (rowc < -1 || rowc + LM1 > nc) {
           bad = true;
-        } else if (rowc >= 0) {
-          const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
-          const double2 g = make_double2(sg * acc[i].x, -sg * acc[i].y);
-          sG[(rowc + M) * NA + a] = g;
-          const double2 iv = sI[(rowc + M) * NA + a];
-          ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
+        } else if (u.w == -2) {
+          if (rowc >= 0) sG[(rowc + M) * NA + a] = acc[i];  // the first chunk's sums, unsigned
+        } else {
+          scratch[u.w * SLOT + ((rg * RL + i) * MC + mloc) * NA + a] = acc[i];
         }
       }
+    }
+  }
+  const int f0 = tt.fix_begin[L], f1 = tt.fix_begin[L + 1];
+  if (f1 > f0) {  // uniform over the CTA
+    __syncthreads();
+    if (f0 < 0 || int64_t(f1) > tt.fix_count) {
+      bad = true;
+      return;
+    }
+    for (int f = f0 + warp; f < f1; f += NW) {
+      const int4 fx = __ldg(tt.fix + f);  // (tile, first slot, slot count, 0)
+      if (!used || fx.x < t0 || fx.x >= t1 || fx.y < 0 || fx.z < 1 || (fx.y + fx.z) * MC > tt.scratch_slots) {
+        if (used) bad = true;
+        continue;
+      }
+      double2 acc[RL];
+#pragma unroll
+      for (int i = 0; i < RL; ++i) {
+        const int rowc = tt.tile_row[int64_t(fx.x) * R + rg * RL + i];
+        acc[i] = (rowc >= 0 && rowc + LM1 <= nc) ? sG[(rowc + mloc) * NA + a] : make_double2(0.0, 0.0);
+        for (int sl = fx.y; sl < fx.y + fx.z; ++sl) {
+          const double2 v = scratch[sl * SLOT + ((rg * RL + i) * MC + mloc) * NA + a];
+          acc[i].x += v.x;
+          acc[i].y += v.y;
+        }
+      }
+      finish(fx.x, mloc, acc);
     }
   }
 }
@@ -924,8 +955,11 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
   double2* sG = sI + cw * NA;
   const int tid = threadIdx.x;
   const int lane = tid & 31, a_lane = lane % NA;
-  // this warp's staging ring for step 2, after the component regions
+  // this warp's staging ring for step 2, after the component regions, and the
+  // CTA's scratch for the partial sums of cut tiles after the rings
   unsigned char* ring = reinterpret_cast<unsigned char*>(sG + cw * NA) + (tid >> 5) * kTileStages * kStageBytes;
+  double2* scratch =
+      reinterpret_cast<double2*>(reinterpret_cast<unsigned char*>(sG + cw * NA) + (TH / 32) * kTileStages * kStageBytes);
   const int64_t groups = (atom_count + NA - 1) / NA;
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
     const int64_t first = grp * NA;
@@ -982,15 +1016,15 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
       build_components_lanes<NA, TH>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       switch (L) {
-        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
-        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, ep, bad); break;
+        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
       }
       __syncthreads();
       // 3. back-propagation: lanes (work item, atom) sum their item's chunk of an
@@ -1016,9 +1050,7 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
               bad = true;  // uniform over the warp
               continue;
             }
-            double2 gp[4];  // four partial sums (records u = 0..3 of each row), added in order
-#pragma unroll
-            for (int u = 0; u < 4; ++u) gp[u] = make_double2(0.0, 0.0);
+            double2 ga = make_double2(0.0, 0.0);
             for (int e = e0 + j; e < e1; e += 4 * R) {  // four records in flight per lane
               int4 recs[4];
 #pragma unroll
@@ -1037,12 +1069,10 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
                 double2 gg = sG[gi * NA + a_lane];
                 if (rec.x & 1) gg.y = -gg.y;
                 const double2 term = o < 0 ? gg : rmul(gg, sA[o * NA + a_lane]);
-                gp[u].x = fma(cv, term.x, gp[u].x);
-                gp[u].y = fma(cv, term.y, gp[u].y);
+                ga.x = fma(cv, term.x, ga.x);
+                ga.y = fma(cv, term.y, ga.y);
               }
             }
-            const double2 ga = make_double2((gp[0].x + gp[1].x) + (gp[2].x + gp[3].x),
-                                            (gp[0].y + gp[1].y) + (gp[2].y + gp[3].y));
             if (it < ni) part[it * NA + a_lane] = ga;
           }
         }

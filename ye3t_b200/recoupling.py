@@ -634,6 +634,18 @@ class RecoupledTiles:
     bp_group_begin: np.ndarray = None  # int32 [pass_count + 1]
     bp_group_off: np.ndarray = None    # int32 [groups + 1]
     bp_pack: np.ndarray = None         # int32 [packed, 4]: (code, other, value bits lo, hi)
+    # step-2 work units: a tile's column steps cut into chunks of at most about
+    # ``unit_quads`` quads of TILE_STEP steps, so that the warps of a CTA get even shares;
+    # unit (tile, first step, end step, kind): kind -1 a whole tile, -2 the first chunk
+    # of a cut tile (its sums go to the components' adjoint slots), s >= 0 a later chunk
+    # (its sums go to scratch slot s); fix[f] = (tile, first slot, slot count, 0) adds a
+    # cut tile's later chunks in slot order.  Units are ordered by decreasing length.
+    unit_quads: int = 0
+    scratch_slots: int = 0
+    unit_begin: np.ndarray = None  # int32 [pass_count + 1]
+    unit: np.ndarray = None        # int32 [U, 4]
+    fix_begin: np.ndarray = None   # int32 [pass_count + 1]
+    fix: np.ndarray = None         # int32 [F, 4]
 
     @property
     def tile_count(self) -> int:
@@ -658,7 +670,7 @@ class RecoupledTiles:
 
     def validate(self, sym: "RecoupledSymTables") -> None:
         P, R = self.pass_count, self.rows
-        tb = self.tile_begin.astype(np.int64)
+        tb = tb_ = self.tile_begin.astype(np.int64)
         if tb.shape != (P + 1,) or tb[0] != 0 or np.any(np.diff(tb) < 0) or tb[-1] != self.tile_count:
             raise ValueError("tile_begin does not partition the tiles")
         if self.tile_row.shape != (self.tile_count, R):
@@ -704,6 +716,27 @@ class RecoupledTiles:
             raise ValueError("bp_group_off does not cut the records into rows of whole groups")
         if np.any(np.diff(gb) * R < np.diff(ib)) or np.any((np.diff(gb) - 1) * R >= np.maximum(np.diff(ib), 1)):
             raise ValueError("the groups of a pass do not hold its items")
+        ub = self.unit_begin.astype(np.int64)
+        if ub.shape != (P + 1,) or ub[0] != 0 or ub[-1] != self.unit.shape[0] or np.any(np.diff(ub) < 0):
+            raise ValueError("unit_begin does not partition the work units")
+        un = self.unit.astype(np.int64)
+        Lu = np.repeat(np.arange(P), np.diff(ub))
+        if un.size and (np.any(un[:, 0] < tb_[Lu]) or np.any(un[:, 0] >= tb_[Lu + 1]) or
+                        np.any(un[:, 1] < 0) or np.any(un[:, 2] < un[:, 1]) or np.any(un[:, 1] % TILE_STEP) or
+                        np.any(un[:, 2] % TILE_STEP) or np.any(un[:, 2] > np.diff(cb)[un[:, 0]]) or
+                        np.any(un[:, 3] < -2) or np.any(un[:, 3] >= self.scratch_slots)):
+            raise ValueError("work unit outside its pass, tile or scratch")
+        fb = self.fix_begin.astype(np.int64)
+        if fb.shape != (P + 1,) or fb[0] != 0 or fb[-1] != self.fix.shape[0] or np.any(np.diff(fb) < 0):
+            raise ValueError("fix_begin does not partition the fix-ups")
+        fx = self.fix.astype(np.int64)
+        Lf = np.repeat(np.arange(P), np.diff(fb))
+        mc = np.minimum(np.arange(P) + 1, 8)
+        if fx.size and (np.any(fx[:, 1] < 0) or np.any(fx[:, 2] < 1) or
+                        np.any((fx[:, 1] + fx[:, 2]) * mc[Lf] > self.scratch_slots)):
+            raise ValueError("fix-up outside the scratch")
+        if un.size and np.any((un[:, 3] >= 0) & ((un[:, 3] + 1) * mc[Lu] > self.scratch_slots)):
+            raise ValueError("work unit's slot outside the scratch")
         pk = self.bp_pack.astype(np.int64)
         Lg = np.repeat(np.arange(P), np.diff(gb))
         Lr = np.repeat(Lg, np.diff(go))
@@ -823,8 +856,62 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
                            bp_group_begin=np.asarray(group_begin, dtype=np.int32),
                            bp_group_off=np.asarray(group_off, dtype=np.int32),
                            bp_pack=np.asarray(pack, dtype=np.int32).reshape(-1, 4))
+    _plan_units(tiles)
     tiles.validate(sym)
     return tiles
+
+
+# Step-2 work units: warps per CTA the cuts aim at, and the scratch bytes a CTA
+# holds for the partial sums of cut tiles (a slot of a pass holds one chunk's
+# sums: 8 rows x min(L + 1, 8) components x 4 atoms, complex, 512 (L + 1) bytes).
+UNIT_WARPS = 16
+SCRATCH_BYTES = 12 * 1024
+
+
+def _plan_units(tiles: RecoupledTiles) -> None:
+    """Cut each pass's tiles into work units of at most ``q`` quads, the smallest ``q``
+    that gives about two units per warp and fits the cut tiles' later chunks into the
+    scratch slots (tiles of more than 8 components per pass are not cut)."""
+    P = tiles.pass_count
+    quads = np.diff(tiles.tile_col_begin.astype(np.int64)) // TILE_STEP
+    unit_begin, units, fix_begin, fixes = [0], [], [0], []
+    qmax_all = 0
+    for L in range(P):
+        t0, t1 = int(tiles.tile_begin[L]), int(tiles.tile_begin[L + 1])
+        n = quads[t0:t1]
+        total = int(n.sum())
+        cut_ok = L + 1 <= 8
+        slots = SCRATCH_BYTES // (512 * min(L + 1, 8))
+        q = max(1, -(-total // (2 * UNIT_WARPS))) if cut_ok else max(1, int(n.max(initial=1)))
+        while True:
+            extra = int(sum(max(0, -(-int(x) // q) - 1) for x in n))
+            if extra <= slots or q >= int(n.max(initial=1)):
+                break
+            q += 1
+        pass_units, slot = [], 0
+        for i, x in enumerate(n):
+            tile = t0 + i
+            k = max(1, -(-int(x) // q))
+            if k == 1:
+                pass_units.append((tile, 0, int(x) * TILE_STEP, -1))
+                continue
+            cuts = [int(x) * j // k for j in range(k + 1)]
+            fixes.append((tile, slot, k - 1, 0))
+            for j in range(k):
+                kind = -2 if j == 0 else slot + j - 1
+                pass_units.append((tile, cuts[j] * TILE_STEP, cuts[j + 1] * TILE_STEP, kind))
+            slot += k - 1
+        pass_units.sort(key=lambda u: (-(u[2] - u[1]), u[0], u[1]))
+        units.extend(pass_units)
+        unit_begin.append(len(units))
+        fix_begin.append(len(fixes))
+        qmax_all = max(qmax_all, q)
+    tiles.unit_quads = qmax_all
+    tiles.scratch_slots = SCRATCH_BYTES // 512
+    tiles.unit_begin = np.asarray(unit_begin, dtype=np.int32)
+    tiles.unit = np.asarray(units, dtype=np.int32).reshape(-1, 4)
+    tiles.fix_begin = np.asarray(fix_begin, dtype=np.int32)
+    tiles.fix = np.asarray(fixes, dtype=np.int32).reshape(-1, 4)
 
 
 def _sym_device_tables(plan: "RecoupledPlan") -> RecoupledSymTables:
@@ -1025,7 +1112,7 @@ def ctypes_tables(arrays: Dict[str, "object"], tabs: RecoupledDeviceTables):
 _TABLE_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
                  "dot_begin", "dot", "feat_index", "feat_weight")
 _TILE_ARRAYS = ("tile_begin", "tile_row", "tile_col_begin", "col_comp", "bp_item_begin", "t_item_begin", "t_item",
-                "bp_group_begin", "bp_group_off", "bp_pack")
+                "bp_group_begin", "bp_group_off", "bp_pack", "unit_begin", "unit", "fix_begin", "fix")
 _SYM_ARRAYS = ("pass_begin", "comp", "cg_index", "cg_value", "own", "bp_begin", "bp_gi", "bp_other", "bp_value",
                "mirror", "dot_begin", "dot")
 
@@ -1094,6 +1181,8 @@ class RecoupledEvaluator:
                 rows=self.tiles.rows, pass_count=self.tiles.pass_count, tile_count=self.tiles.tile_count,
                 step_count=self.tiles.step_count, item_count=int(self.tiles.bp_item.shape[0]),
                 group_count=int(self.tiles.bp_group_off.shape[0] - 1), pack_count=int(self.tiles.bp_pack.shape[0]),
+                unit_count=int(self.tiles.unit.shape[0]), fix_count=int(self.tiles.fix.shape[0]),
+                scratch_slots=int(self.tiles.scratch_slots),
                 **{name: self.tile_arrays[name].data_ptr() for name in self.tile_arrays},
                 kval=0 if self.kval is None else self.kval.data_ptr())
 
