@@ -2,7 +2,7 @@
 //
 // Compiles ye3t_b200/csrc/recoupled_kernels.cuh as host C++ and runs a kernel
 // as one CTA of 256 or 512 OS threads: __syncthreads is a std::barrier over
-// the block, __shfl_xor_sync an exchange through a per-warp buffer between two
+// the block, __shfl_xor_sync / __shfl_sync an exchange through a per-warp buffer between two
 // warp barriers, __shared__ arrays are function statics and the dynamic shared
 // memory one static buffer.  One CTA (gridDim.x = 1) walks every atom group, as
 // the grid-stride loop of the kernels allows, so the emulated run follows the
@@ -68,6 +68,14 @@ inline double __shfl_xor_sync(unsigned, double v, int lane_mask) {
   g_lanes[w][lane] = v;
   g_warp[w]->arrive_and_wait();
   const double r = g_lanes[w][lane ^ lane_mask];
+  g_warp[w]->arrive_and_wait();
+  return r;
+}
+inline double __shfl_sync(unsigned, double v, int src_lane) {
+  const int w = int(threadIdx.x) >> 5, lane = int(threadIdx.x) & 31;
+  g_lanes[w][lane] = v;
+  g_warp[w]->arrive_and_wait();
+  const double r = g_lanes[w][src_lane & 31];
   g_warp[w]->arrive_and_wait();
   return r;
 }

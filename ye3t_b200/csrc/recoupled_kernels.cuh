@@ -736,21 +736,59 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
 constexpr int kTileStages = 8;
 constexpr int kStageBytes = 16 + 4 * 8 * 8;
 
-// Column walk of one unit: acc[i] += K[row i, q] I[column q + M] for the
-// unit's column steps, four per stage of the staging ring (STAGED: the weights
-// of the CTA's one species from the ring; otherwise this lane's species'
-// weights from global memory).  A quad of columns outside the pass is skipped
-// and sets bad (the columns are the same for every lane of the warp).
-template <bool STAGED, int LM1, int R, int RL, int NA>
-__device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, int nc, const double2* sIa,
-                                          const double* kq, const double* kl, int rg, unsigned char* ring,
-                                          double2 (&acc)[RL], bool& bad) {
+// One FP64 tensor-core step D = A B + C of shape m8n8k4 (mma.sync: tcgen05 has
+// no FP64 kind, so this is the FP64 matrix path of sm_100).  Fragments of lane
+// l: a = A[l / 4][l % 4], b = B[l % 4][l / 4], (d0, d1) = C, D[l / 4][2 (l % 4)
+// + {0, 1}].  The CPU emulation gathers the fragments through warp exchanges
+// and forms each output as C + sum_k A[r][k] B[k][n] with fma in k order.
+__device__ __forceinline__ void dmma_m8n8k4(double& d0, double& d1, double a, double b) {
+#ifdef Y3B_EMULATE
+  const int lane = threadIdx.x & 31, r = lane >> 2, tg = lane & 3;
+  double av[4], b0[4], b1[4];
+  for (int k = 0; k < 4; ++k) {
+    av[k] = __shfl_sync(0xffffffffu, a, r * 4 + k);
+    b0[k] = __shfl_sync(0xffffffffu, b, 4 * (2 * tg) + k);
+    b1[k] = __shfl_sync(0xffffffffu, b, 4 * (2 * tg + 1) + k);
+  }
+  for (int k = 0; k < 4; ++k) {
+    d0 = fma(av[k], b0[k], d0);
+    d1 = fma(av[k], b1[k], d1);
+  }
+#else
+  asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};\n"
+      : "+d"(d0), "+d"(d1)
+      : "d"(a), "d"(b));
+#endif
+}
+
+// Column walk of one unit on the FP64 tensor cores.  Each stage of the ring is
+// the k = 4 of one m8n8k4 step: acc[M] += K[8 rows, 4 steps] x I[4 steps, 8]
+// for every M of the pass, where the 8 columns of I are (atom, real or
+// imaginary part) of the column's component + M.  Lane l holds the weight
+// K[row l / 4, step l % 4], the I value of step l % 4 for atom l / 8 (real
+// part when l / 4 is even), and the sums of row l / 4 and atom l % 4 (real,
+// imaginary) in acc[M].  STAGED: the CTA's one species' weights come from the
+// ring; otherwise each species among the CTA's atoms takes its own step with
+// its weights read from global memory and the I values of the other species'
+// atoms set to zero.  A quad of columns outside the pass is skipped and sets
+// bad (the columns are the same for every lane of the warp).
+template <bool STAGED, int LM1, int NA>
+__device__ __forceinline__ void tile_walk_mma(const TileTabs& tt, int q0, int nq, int nc, const double* sId,
+                                              const double* const (&kw)[NA], const int (&za)[NA],
+                                              unsigned char* ring, double (&acc)[LM1][2], bool& bad) {
+  constexpr int R = 8;
   const int lane = threadIdx.x & 31;
+  const int kk = lane & 3, row = lane >> 2;
+  const int ab = lane >> 3, part = (lane >> 2) & 1;  // the lane's I value: atom, real/imaginary
+  int zb = za[0];
+#pragma unroll
+  for (int s = 1; s < NA; ++s)
+    if (ab == s) zb = za[s];
   auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
     unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
     if (Q < nq) {
       if (STAGED && lane < 16)
-        cp_async16(st + 16 + 16 * lane, kq + int64_t(R) * 4 * Q + 2 * lane);
+        cp_async16(st + 16 + 16 * lane, kw[0] + int64_t(R) * 4 * Q + 2 * lane);
       else if (lane == 16)
         cp_async16(st, tt.col_comp + q0 + 4 * Q);
     }
@@ -767,73 +805,55 @@ __device__ __forceinline__ void tile_walk(const TileTabs& tt, int q0, int nq, in
     if (cmin < 0 || cmax + LM1 > nc) {
       bad = true;
     } else {
-      const int cs[4] = {c4.x, c4.y, c4.z, c4.w};
-      const double* kst = reinterpret_cast<const double*>(st + 16) + rg * RL;
-      const double* kg = kl + int64_t(R) * 4 * Q;
+      const int col = kk == 0 ? c4.x : (kk == 1 ? c4.y : (kk == 2 ? c4.z : c4.w));
+      const double* bI = sId + (col * NA + ab) * 2 + part;  // I[col + M] at bI[2 NA M]
+      if (STAGED) {
+        const double av = reinterpret_cast<const double*>(st + 16)[kk * R + row];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const double2 v = sIa[cs[j] * NA];
-        const double* kr = STAGED ? kst + j * R : kg + j * R;
-        if constexpr (RL == 1) {
-          const double k0 = STAGED ? kr[0] : __ldg(kr);
-          acc[0].x = fma(k0, v.x, acc[0].x);
-          acc[0].y = fma(k0, v.y, acc[0].y);
-        } else {
+        for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, bI[2 * NA * M]);
+      } else {
 #pragma unroll
-          for (int i = 0; i < RL; i += 2) {
-            const double2 k2 = STAGED ? *reinterpret_cast<const double2*>(kr + i)
-                                      : __ldg(reinterpret_cast<const double2*>(kr + i));
-            acc[i].x = fma(k2.x, v.x, acc[i].x);
-            acc[i].y = fma(k2.x, v.y, acc[i].y);
-            acc[i + 1].x = fma(k2.y, v.x, acc[i + 1].x);
-            acc[i + 1].y = fma(k2.y, v.y, acc[i + 1].y);
-          }
+        for (int s = 0; s < NA; ++s) {
+          bool first = true;
+#pragma unroll
+          for (int j = 0; j < s; ++j) first = first && za[j] != za[s];
+          if (!first) continue;  // uniform over the warp
+          const double av = __ldg(kw[s] + int64_t(R) * (4 * Q + kk) + row);
+          const bool on = zb == za[s];
+#pragma unroll
+          for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, on ? bI[2 * NA * M] : 0.0);
         }
       }
     }
     __syncwarp();
     issue(Q + kTileStages);
   }
-  cp_async_wait<0>();
-  __syncwarp();
 }
 
 // Step 2 of the tiled symmetric adjoint for one pass of L = LM1 - 1 (tiles of
-// 8 rows, NA = 4 atoms).  A lane owns one (atom a, component M) of the warp's
-// tile and RL of its 8 rows in registers: per column step it reads
-// I[column + M] for its atom once from shared memory and its rows' weights
-// (tile_walk), and adds acc[i] += K[row i] I.  A tile spreads over
-// NA * MC * RG lanes: MC = min(LM1, 8) components and RG = 8 / RL row groups,
-// with RL the fewest rows per lane that keep a tile within one warp, so that
-// small L still give one tile per warp and large L reuse each read for up to
-// 8 rows.  Passes with more than MC components run a tile again for the next
-// MC of them.  The work units (a tile, or a chunk of a long tile's columns,
-// ordered by decreasing length) go to the warps in a snake order.  A whole
-// tile ends by writing gI = (-1)^p conj(acc[i]) for its rows and adding the
-// energy shares w_M Re(I gI) (w_0 = 1/2); the first chunk of a cut tile
-// leaves its sums in the adjoint slots and a later chunk in its scratch slot,
-// and after a barrier each cut tile's fix-up adds the later chunks in slot
-// order and finishes as a whole tile does.  Every sum has a fixed order, so
-// the results do not depend on which warp runs what.  A column, row or unit
-// outside the pass is skipped and sets bad.
+// 8 rows, NA = 4 atoms).  A warp takes a work unit (a tile, or a chunk of a
+// long tile's columns; units ordered by decreasing length go to the warps in a
+// snake order) and walks its columns on the FP64 tensor cores for all LM1
+// components at once (tile_walk_mma), so that lane l ends with the sums of row
+// l / 4 and atom l % 4.  A whole tile ends by writing gI = (-1)^p conj(acc)
+// for its rows and adding the energy shares w_M Re(I gI) (w_0 = 1/2).  The
+// first chunk of a cut tile leaves its sums in sG, each later chunk in its
+// scratch slot, and after a barrier each cut tile's fix-up adds the later
+// chunks in slot order and finishes as a whole tile does.  Every sum has a
+// fixed order, so the results do not depend on which warp runs what.  A
+// column, row or unit outside the pass is skipped and sets bad.
 template <int LM1, int NA, int TH>
 __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileTabs& tt, int L, int c0, int nc,
-                                                   const double2* sI, double2* sG, const double* kz,
-                                                   const double* kz_staged, bool staged, unsigned char* ring,
+                                                   const double2* sI, double2* sG, const double* const (&kw)[NA],
+                                                   const int (&za)[NA], bool staged, unsigned char* ring,
                                                    double2* scratch, double& ep, bool& bad) {
-  constexpr int R = 32 / NA;                                   // rows per tile
-  static_assert(R == 8, "the staged step 2 takes tiles of 8 rows");
-  constexpr int MC = LM1 < R ? LM1 : R;                        // components per unit
-  constexpr int NCH = (LM1 + MC - 1) / MC;                     // component chunks per tile
-  constexpr int RG0 = 32 / (NA * MC);                          // row groups that fit a warp
-  constexpr int RG = RG0 >= R ? R : (RG0 >= 4 ? 4 : (RG0 >= 2 ? 2 : 1));
-  constexpr int RL = R / RG;                                   // rows per lane
-  constexpr int SLOT = R * MC * NA;                            // double2 per scratch slot
-  static_assert(NA * MC * RG <= 32 && 2 * NA * MC * RG > 32, "one unit per warp");
+  constexpr int R = 8;
+  static_assert(NA == 4, "one m8n8k4 step holds 8 rows of 4 atoms");
+  constexpr int SLOT = R * LM1 * NA;  // double2 per scratch slot
   constexpr int NW = TH / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int a = lane % NA, mloc = (lane / NA) % MC, rg = (lane / (NA * MC)) % RG;
-  const bool used = lane < NA * MC * RG;
+  const int a = lane & 3, row = lane >> 2;
+  const double* sId = reinterpret_cast<const double*>(sI);
   const int t0 = tt.tile_begin[L], t1 = tt.tile_begin[L + 1];
   const int u0 = tt.unit_begin[L], u1 = tt.unit_begin[L + 1];
   if (t0 < 0 || t1 < t0 || int64_t(t1) > tt.tile_count || u0 < 0 || u1 < u0 || int64_t(u1) > tt.unit_count) {
@@ -841,30 +861,29 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
     return;
   }
   // a whole tile's ending: gI and the energy shares from the lane's sums
-  auto finish = [&](int tile, int M, const double2 (&acc)[RL]) {
+  auto finish = [&](int tile, const double (&acc)[LM1][2]) {
+    const int rowc = tt.tile_row[int64_t(tile) * R + row];
+    if (rowc < -1 || rowc + LM1 > nc) {
+      bad = true;
+      return;
+    }
+    if (rowc < 0) return;
+    const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
 #pragma unroll
-    for (int i = 0; i < RL; ++i) {
-      const int rowc = tt.tile_row[int64_t(tile) * R + rg * RL + i];
-      if (rowc < -1 || rowc + LM1 > nc) {
-        bad = true;
-      } else if (rowc >= 0) {
-        const double sg = __ldg(t.comp + 2 * (c0 + rowc) + 1).w < 0 ? -1.0 : 1.0;
-        const double2 g = make_double2(sg * acc[i].x, -sg * acc[i].y);
-        sG[(rowc + M) * NA + a] = g;
-        const double2 iv = sI[(rowc + M) * NA + a];
-        ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
-      }
+    for (int M = 0; M < LM1; ++M) {
+      const double2 g = make_double2(sg * acc[M][0], -sg * acc[M][1]);
+      sG[(rowc + M) * NA + a] = g;
+      const double2 iv = sI[(rowc + M) * NA + a];
+      ep = fma(M == 0 ? 0.5 : 1.0, iv.x * g.x - iv.y * g.y, ep);
     }
   };
-  const int items = (u1 - u0) * NCH;
+  const int units = u1 - u0;
   for (int k = 0;; ++k) {
     const int item = (k & 1) ? k * NW + (NW - 1 - warp) : k * NW + warp;  // uniform over the warp
-    if (item >= items) break;
-    const int4 u = __ldg(tt.unit + u0 + item / NCH);  // (tile, first step, end step, kind)
+    if (item >= units) break;
+    const int4 u = __ldg(tt.unit + u0 + item);  // (tile, first step, end step, kind)
     const int tile = u.x;
-    const int M = (item % NCH) * MC + mloc;
-    const bool mine = used && M < LM1;
-    if (tile < t0 || tile >= t1 || u.w < -2 || (u.w >= 0 && (NCH > 1 || (u.w + 1) * MC > tt.scratch_slots))) {
+    if (tile < t0 || tile >= t1 || u.w < -2 || (u.w >= 0 && (u.w + 1) * LM1 > tt.scratch_slots)) {
       bad = true;
       continue;
     }
@@ -875,30 +894,32 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
       bad = true;
       continue;
     }
-    double2 acc[RL];
+    double acc[LM1][2];
 #pragma unroll
-    for (int i = 0; i < RL; ++i) acc[i] = make_double2(0.0, 0.0);
-    const double2* sIa = sI + (mine ? M : 0) * NA + a;
-    const double* kq = kz_staged + int64_t(R) * qs;       // the staged species' weights
-    const double* kl = kz + int64_t(R) * qs + rg * RL;    // this lane's species' weights
+    for (int M = 0; M < LM1; ++M) acc[M][0] = acc[M][1] = 0.0;
+    const double* kwu[NA];
+#pragma unroll
+    for (int s = 0; s < NA; ++s) kwu[s] = kw[s] + int64_t(R) * qs;
     if (staged)  // uniform over the CTA
-      tile_walk<true, LM1, R, RL, NA>(tt, qs, (qe - qs) / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
+      tile_walk_mma<true, LM1, NA>(tt, qs, (qe - qs) / 4, nc, sId, kwu, za, ring, acc, bad);
     else
-      tile_walk<false, LM1, R, RL, NA>(tt, qs, (qe - qs) / 4, nc, sIa, kq, kl, rg, ring, acc, bad);
-    if (!mine) continue;
+      tile_walk_mma<false, LM1, NA>(tt, qs, (qe - qs) / 4, nc, sId, kwu, za, ring, acc, bad);
     if (u.w == -1) {
-      finish(tile, M, acc);
+      finish(tile, acc);
     } else {
+      const int rowc = tt.tile_row[int64_t(tile) * R + row];
+      if (rowc < -1 || rowc + LM1 > nc) {
+        bad = true;
+      } else if (u.w == -2) {
+        if (rowc >= 0) {
 #pragma unroll
-      for (int i = 0; i < RL; ++i) {
-        const int rowc = tt.tile_row[int64_t(tile) * R + rg * RL + i];
-        if (rowc < -1 || rowc + LM1 > nc) {
-          bad = true;
-        } else if (u.w == -2) {
-          if (rowc >= 0) sG[(rowc + M) * NA + a] = acc[i];  // the first chunk's sums, unsigned
-        } else {
-          scratch[u.w * SLOT + ((rg * RL + i) * MC + mloc) * NA + a] = acc[i];
+          for (int M = 0; M < LM1; ++M)
+            sG[(rowc + M) * NA + a] = make_double2(acc[M][0], acc[M][1]);  // the first chunk's sums, unsigned
         }
+      } else {
+#pragma unroll
+        for (int M = 0; M < LM1; ++M)
+          scratch[u.w * SLOT + (row * LM1 + M) * NA + a] = make_double2(acc[M][0], acc[M][1]);
       }
     }
   }
@@ -911,22 +932,25 @@ __device__ __forceinline__ void tiled_adjoint_pass(const SymTabs& t, const TileT
     }
     for (int f = f0 + warp; f < f1; f += NW) {
       const int4 fx = __ldg(tt.fix + f);  // (tile, first slot, slot count, 0)
-      if (!used || fx.x < t0 || fx.x >= t1 || fx.y < 0 || fx.z < 1 || (fx.y + fx.z) * MC > tt.scratch_slots) {
-        if (used) bad = true;
+      if (fx.x < t0 || fx.x >= t1 || fx.y < 0 || fx.z < 1 || (fx.y + fx.z) * LM1 > tt.scratch_slots) {
+        bad = true;
         continue;
       }
-      double2 acc[RL];
+      const int rowc = tt.tile_row[int64_t(fx.x) * R + row];
+      const bool in = rowc >= 0 && rowc + LM1 <= nc;
+      double acc[LM1][2];
 #pragma unroll
-      for (int i = 0; i < RL; ++i) {
-        const int rowc = tt.tile_row[int64_t(fx.x) * R + rg * RL + i];
-        acc[i] = (rowc >= 0 && rowc + LM1 <= nc) ? sG[(rowc + mloc) * NA + a] : make_double2(0.0, 0.0);
+      for (int M = 0; M < LM1; ++M) {
+        const double2 v0 = in ? sG[(rowc + M) * NA + a] : make_double2(0.0, 0.0);
+        acc[M][0] = v0.x;
+        acc[M][1] = v0.y;
         for (int sl = fx.y; sl < fx.y + fx.z; ++sl) {
-          const double2 v = scratch[sl * SLOT + ((rg * RL + i) * MC + mloc) * NA + a];
-          acc[i].x += v.x;
-          acc[i].y += v.y;
+          const double2 v = scratch[sl * SLOT + (row * LM1 + M) * NA + a];
+          acc[M][0] += v.x;
+          acc[M][1] += v.y;
         }
       }
-      finish(fx.x, mloc, acc);
+      finish(fx.x, acc);
     }
   }
 }
@@ -965,7 +989,6 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
     const int64_t first = grp * NA;
     const int nv = int(atom_count - first < NA ? atom_count - first : NA);
     int64_t idx[NA];  // the CTA's atoms (a partial group repeats its first atom, never written)
-    int64_t mine = first;
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
       int64_t v = first + (a < nv ? a : 0);
@@ -978,26 +1001,22 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
         }
       }
       idx[a] = v;
-      if (a == a_lane) mine = v;
     }
-    int z = species[mine];
-    if (z < 0 || z >= species_count) {
-      if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
-      z = 0;
-    }
-    const double* kz = tt.kval + int64_t(z) * int64_t(tt.rows) * tt.step_count;
-    // the staging rings hold one species' weights: those of the CTA's atoms when
-    // they all share it (species-sorted groups), else each lane reads its own
+    // the CTA's species and weights; the staging rings hold one species'
+    // weights, used when all the CTA's atoms share it (species-sorted groups)
+    int za[NA];
+    const double* kw[NA];
     bool uniform_z = true;
-    int z0 = 0;
 #pragma unroll
     for (int a = 0; a < NA; ++a) {
-      int za = species[idx[a]];
-      if (za < 0 || za >= species_count) za = 0;
-      if (a == 0) z0 = za;
-      uniform_z = uniform_z && za == z0;
+      za[a] = species[idx[a]];
+      if (za[a] < 0 || za[a] >= species_count) {
+        if (tid == 0 && status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+        za[a] = 0;
+      }
+      kw[a] = tt.kval + int64_t(za[a]) * int64_t(tt.rows) * tt.step_count;
+      uniform_z = uniform_z && za[a] == za[0];
     }
-    const double* kz0 = tt.kval + int64_t(z0) * int64_t(tt.rows) * tt.step_count;
     for (int i = tid; i < W * NA; i += TH) {
       const int a = i % NA, e = i / NA;
       sA[i] = a < nv ? A[idx[a] * W + e] : make_double2(0.0, 0.0);
@@ -1016,15 +1035,15 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
       build_components_lanes<NA, TH>(t, sA, sI, c0, nc, W, bad);
       __syncthreads();
       switch (L) {
-        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
-        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kz, kz0, uniform_z, ring, scratch, ep, bad); break;
+        case 0: tiled_adjoint_pass<1, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        case 1: tiled_adjoint_pass<2, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        case 2: tiled_adjoint_pass<3, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        case 3: tiled_adjoint_pass<4, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        case 4: tiled_adjoint_pass<5, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        case 5: tiled_adjoint_pass<6, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        case 6: tiled_adjoint_pass<7, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        case 7: tiled_adjoint_pass<8, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
+        default: tiled_adjoint_pass<9, NA, TH>(t, tt, L, c0, nc, sI, sG, kw, za, uniform_z, ring, scratch, ep, bad); break;
       }
       __syncthreads();
       // 3. back-propagation: lanes (work item, atom) sum their item's chunk of an

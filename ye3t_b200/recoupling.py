@@ -863,7 +863,7 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
 
 # Step-2 work units: warps per CTA the cuts aim at, and the scratch bytes a CTA
 # holds for the partial sums of cut tiles (a slot of a pass holds one chunk's
-# sums: 8 rows x min(L + 1, 8) components x 4 atoms, complex, 512 (L + 1) bytes).
+# sums: 8 rows x (L + 1) components x 4 atoms, complex, 512 (L + 1) bytes).
 UNIT_WARPS = 16
 SCRATCH_BYTES = 12 * 1024
 
@@ -871,7 +871,7 @@ SCRATCH_BYTES = 12 * 1024
 def _plan_units(tiles: RecoupledTiles) -> None:
     """Cut each pass's tiles into work units of at most ``q`` quads, the smallest ``q``
     that gives about two units per warp and fits the cut tiles' later chunks into the
-    scratch slots (tiles of more than 8 components per pass are not cut)."""
+    scratch slots."""
     P = tiles.pass_count
     quads = np.diff(tiles.tile_col_begin.astype(np.int64)) // TILE_STEP
     unit_begin, units, fix_begin, fixes = [0], [], [0], []
@@ -880,9 +880,8 @@ def _plan_units(tiles: RecoupledTiles) -> None:
         t0, t1 = int(tiles.tile_begin[L]), int(tiles.tile_begin[L + 1])
         n = quads[t0:t1]
         total = int(n.sum())
-        cut_ok = L + 1 <= 8
-        slots = SCRATCH_BYTES // (512 * min(L + 1, 8))
-        q = max(1, -(-total // (2 * UNIT_WARPS))) if cut_ok else max(1, int(n.max(initial=1)))
+        slots = SCRATCH_BYTES // (512 * (L + 1))
+        q = max(1, -(-total // (2 * UNIT_WARPS)))
         while True:
             extra = int(sum(max(0, -(-int(x) // q) - 1) for x in n))
             if extra <= slots or q >= int(n.max(initial=1)):
