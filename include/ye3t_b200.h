@@ -41,6 +41,7 @@ extern "C" {
 #define Y3B_STATUS_INDEX_RANGE 1
 #define Y3B_STATUS_CAPACITY 2
 #define Y3B_STATUS_TABLE 4 /* a table entry outside the kernel's bounds was skipped */
+#define Y3B_STATUS_TIMEOUT 8 /* a bounded wait on the tensor cores ran out; the output is incomplete */
 
 /* ABI version; the reference's gate is core_abi_version()
  * (ye3t/runtime/csrc/execution_plan_torch.cpp:7925, checked at
@@ -312,6 +313,25 @@ int y3b_ace_density_mixed(int dtype, const double* positions, const int32_t* spe
                           const int64_t* row_offsets, const int32_t* neighbors, const void* mixing,
                           int64_t species_count, int64_t channel_count, int64_t nmax, int64_t lmax,
                           double cutoff, double lambda, void* A, int32_t* status, void* stream);
+
+/* The same A-basis in fp32 with the mixing on the tensor cores (tcgen05,
+ * kind::tf32 with a 3xTF32 split): per centre and neighbour species the edge
+ * sums S[i, lm, z, n] = sum_{z_j = z} R_n Yc_lm (CUDA cores), then
+ * A[i, c, lm] = sum_{z, n} W[z_i, z, c, n] S[i, lm, z, n] as a product of 128
+ * rows (i, lm, part) by every centre species' table at once.  mixing is f32
+ * [S, S, C, nmax]; A is complex64 [center_count, C, (lmax+1)^2].  Supported:
+ * lmax <= 4, nmax <= 16, C a multiple of 16, S * nmax <= 64, S * C <= 256,
+ * else Y3B_ERR_UNSUPPORTED (use y3b_ace_density_mixed).  The workspace (16-byte
+ * aligned) holds S for a chunk of centres; the full size is
+ * y3b_ace_density_mixed_tc_workspace_bytes, a smaller one runs in chunks (at
+ * least one centre).  Bad indices set Y3B_STATUS_INDEX_RANGE and give 0. */
+int64_t y3b_ace_density_mixed_tc_workspace_bytes(int64_t center_count, int64_t species_count, int64_t nmax,
+                                                 int64_t lmax);
+int y3b_ace_density_mixed_tc(const double* positions, const int32_t* species, int64_t atom_count,
+                             int64_t center_begin, int64_t center_count, double box, const int64_t* row_offsets,
+                             const int32_t* neighbors, const float* mixing, int64_t species_count,
+                             int64_t channel_count, int64_t nmax, int64_t lmax, double cutoff, double lambda,
+                             void* workspace, int64_t workspace_bytes, void* A, int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------
  * Fused ACE evaluation over a packed multi-word bundle.

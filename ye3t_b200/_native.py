@@ -21,6 +21,7 @@ F32, F64, C64, C128 = 0, 1, 2, 3
 STATUS_INDEX_RANGE = 1
 STATUS_CAPACITY = 2
 STATUS_TABLE = 4
+STATUS_TIMEOUT = 8
 
 _DTYPE_CODE = {torch.float32: F32, torch.float64: F64, torch.complex64: C64, torch.complex128: C128}
 
@@ -131,6 +132,9 @@ _SIGS = {
     "y3b_radial_channel_contraction": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, I64, VP, VP, VP]),
     "y3b_ace_density_mixed": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64,
                                              I64, DBL, DBL, VP, VP, VP]),
+    "y3b_ace_density_mixed_tc_workspace_bytes": (I64, [I64, I64, I64, I64]),
+    "y3b_ace_density_mixed_tc": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, I64, DBL, DBL,
+                                                VP, I64, VP, VP, VP]),
     "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP, VP]),
     "y3b_ace_recoupled_energy_grad": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, I64, VP,
                                                      VP, VP, VP]),

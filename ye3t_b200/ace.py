@@ -104,6 +104,14 @@ class ACEEvaluator:
     def _stream(self):
         return nat.stream_of(self.device)
 
+    def _workspace(self, nbytes: int) -> torch.Tensor:
+        """A device scratch buffer of at least ``nbytes`` (kept and grown between calls)."""
+        ws = getattr(self, "_scratch", None)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=self.device)
+            self._scratch = ws
+        return ws
+
     # -- neighbour list --------------------------------------------------------
     def neighbor_list(self, positions: torch.Tensor, box: float, begin: int = 0,
                       end: Optional[int] = None, z_window: Optional[Tuple[int, int]] = None,
@@ -187,12 +195,16 @@ class ACEEvaluator:
         return A
 
     def density_mixed(self, positions, species, box, row_offsets, neighbors, mixing, begin: int = 0,
-                      dtype=torch.float64, status: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      dtype=torch.float64, status: Optional[torch.Tensor] = None,
+                      tensor_cores: Optional[bool] = None) -> torch.Tensor:
         """A-basis ``[n_centres, C, (lmax+1)^2]`` with radial channels mixed per species pair.
 
         ``mixing [S, S, C, nmax]``: channel c of a pair (z_i, z_j) is
         ``sum_n mixing[z_i, z_j, c, n-1] R_n``.  ``dtype`` float64 gives
-        complex128, float32 complex64 (computed in that precision).
+        complex128, float32 complex64 (computed in that precision).  In fp32 the
+        mixing runs on the tensor cores (``y3b_ace_density_mixed_tc``) wherever
+        its shape allows (``tensor_cores`` None); True requires that path, False
+        uses the per-edge CUDA-core kernel.
         """
         pos = positions.to(self.device, torch.float64).contiguous()
         sp = species.to(self.device, torch.int32).contiguous()
@@ -202,6 +214,21 @@ class ACEEvaluator:
         count = int(row_offsets.shape[0]) - 1
         cdt = torch.complex128 if dtype == torch.float64 else torch.complex64
         A = torch.empty((count, W.shape[2], self.W), dtype=cdt, device=self.device)
+        S, C, nmax = W.shape[0], W.shape[2], W.shape[3]
+        tc_ok = (dtype == torch.float32 and self.bundle.lmax <= 4 and nmax <= 16 and C % 16 == 0
+                 and -(-S * nmax // 8) * 8 <= 64 and -(-S * C // 16) * 16 <= 256)
+        if tensor_cores and not tc_ok:
+            raise ValueError("the tensor-core mixing needs fp32, lmax <= 4, nmax <= 16, C a multiple of 16, "
+                             "S * nmax <= 64 and S * C <= 256")
+        if tc_ok and tensor_cores is not False:
+            need = int(nat.lib().y3b_ace_density_mixed_tc_workspace_bytes(count, S, nmax, self.bundle.lmax))
+            ws = self._workspace(min(need, 1 << 30))
+            nat.check(nat.lib().y3b_ace_density_mixed_tc(
+                pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box), row_offsets.data_ptr(),
+                neighbors.data_ptr(), W.data_ptr(), S, C, nmax, self.bundle.lmax, float(self.config.cutoff),
+                float(self.config.radial_lambda), ws.data_ptr(), ws.numel(), A.data_ptr(), nat.ptr(status),
+                self._stream()), "ace_density_mixed_tc")
+            return A
         nat.check(nat.lib().y3b_ace_density_mixed(
             nat.dtype_code(dtype), pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box),
             row_offsets.data_ptr(), neighbors.data_ptr(), W.data_ptr(), W.shape[0], W.shape[2], W.shape[3],
