@@ -577,6 +577,7 @@ def run_channels(args):
     pos_h, sp_h = pos.pin_memory(), species.pin_memory()
     pos_d, sp_d = pos.to(device), species.to(device)
     mix_d = mix.to(device, rdt)
+    tc_mix = evs[0].mixing_on_tensor_cores(mix.shape[0], mix.shape[2], mix.shape[3], rdt)
     stages = ("neighbors", "density", "features")
     timers = {k: [] for k in stages}
 
@@ -689,7 +690,9 @@ def run_channels(args):
         "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
                 "d2h_bytes_per_step": 8,
                 "note": "features stay on the device (sharded descriptor); a checksum is read back"},
-        "gpu_launches": (8 + len(evs)) * args.steps,  # 7 neighbour-list, mixed density, one per bundle
+        # 7 neighbour-list launches, the mixed density (species sums + tensor-core product in
+        # fp32, one fused kernel in fp64), one feature launch per bundle
+        "gpu_launches": (7 + (2 if tc_mix else 1) + len(evs)) * args.steps,
         "roofline": roof,
         "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
         "checksum": float(check.item()),

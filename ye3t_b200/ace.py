@@ -104,6 +104,13 @@ class ACEEvaluator:
     def _stream(self):
         return nat.stream_of(self.device)
 
+    def mixing_on_tensor_cores(self, species_count: int, channel_count: int, nmax: int, dtype) -> bool:
+        """Whether ``density_mixed`` runs this shape on the tensor cores by default (fp32,
+        l_max <= 4, n_max <= 16, C a multiple of 16, S * n_max <= 64, S * C <= 256)."""
+        S, C = int(species_count), int(channel_count)
+        return (dtype == torch.float32 and self.bundle.lmax <= 4 and int(nmax) <= 16 and C % 16 == 0
+                and -(-S * int(nmax) // 8) * 8 <= 64 and -(-S * C // 16) * 16 <= 256)
+
     def _workspace(self, nbytes: int) -> torch.Tensor:
         """A device scratch buffer of at least ``nbytes`` (kept and grown between calls)."""
         ws = getattr(self, "_scratch", None)
@@ -215,8 +222,7 @@ class ACEEvaluator:
         cdt = torch.complex128 if dtype == torch.float64 else torch.complex64
         A = torch.empty((count, W.shape[2], self.W), dtype=cdt, device=self.device)
         S, C, nmax = W.shape[0], W.shape[2], W.shape[3]
-        tc_ok = (dtype == torch.float32 and self.bundle.lmax <= 4 and nmax <= 16 and C % 16 == 0
-                 and -(-S * nmax // 8) * 8 <= 64 and -(-S * C // 16) * 16 <= 256)
+        tc_ok = self.mixing_on_tensor_cores(S, C, nmax, dtype)
         if tensor_cores and not tc_ok:
             raise ValueError("the tensor-core mixing needs fp32, lmax <= 4, nmax <= 16, C a multiple of 16, "
                              "S * nmax <= 64 and S * C <= 256")
