@@ -16,15 +16,20 @@ inline int radial_table_size(int64_t nmax) { return nmax <= 8 ? 8 : (nmax <= 12 
 // ---------------------------------------------------------------------------
 // Kernel 1: A-basis density.  One warp per centre atom, DensityWarps warps per
 // CTA.  Pass 1: lanes over up to 32 edges of the row compute p[z_j] R_n(r)
-// (n = 1..NMAXT) and the complex harmonics Yc_lm(r_hat) into warp-private
-// shared memory.  Pass 2: lane (lm, g) owns one harmonic column lm and the
-// radial channels n = g, g + G, ... (G = 32 / W lane groups): per edge it
-// reads its harmonic once and its radial values, and accumulates in CSR
-// order.  A is written once per atom; no atomics.
+// (n = 1..NMAXT) and the real harmonics Y_k(r_hat) into warp-private shared
+// memory.  Pass 2: lane (k, g) owns one real harmonic k and the radial channels
+// n = g, g + G, ... (G = 32 / W lane groups): per edge it reads its harmonic
+// once and its radial values, and accumulates in CSR order.  The complex
+// Condon-Shortley harmonics are fixed combinations of two real ones
+// (Yc_{l,0} = Y_{l,0}; Yc_{l,-m} = (Y_{l,m} + i Y_{l,-m}) / sqrt 2;
+// Yc_{l,m} = (-1)^m (Y_{l,m} - i Y_{l,-m}) / sqrt 2), so the sums are real (half
+// the multiply-adds of a complex accumulation) and lane k forms A[n, k] from its
+// own sum and that of the lane of the mirrored harmonic (one shuffle per
+// channel).  A is written once per atom; no atomics.
 // ---------------------------------------------------------------------------
 template <int LMAX, int NMAXT>
 struct DensityWarps {  // up to 4 warps within 48 KB of static shared memory
-  static constexpr int kPerWarp = 32 * ((NMAXT + 1) * 8 + ((LMAX + 1) * (LMAX + 1) + 1) * 16);
+  static constexpr int kPerWarp = 32 * ((NMAXT + 1) * 8 + ((LMAX + 1) * (LMAX + 1) + 1) * 8);
   static constexpr int value = 4 * kPerWarp <= 48 * 1024 ? 4 : (2 * kPerWarp <= 48 * 1024 ? 2 : 1);
 };
 
@@ -39,10 +44,17 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX, NMAXT>::value) ace_den
   constexpr int NPL = (NMAXT + G - 1) / G;                // radial channels per lane
   constexpr int kDensityWarps = DensityWarps<LMAX, NMAXT>::value;
   __shared__ double s_rad[kDensityWarps][32][NMAXT + 1];  // +1: conflict-free pass-1 stores
-  __shared__ double2 s_y[kDensityWarps][32][W + 1];
+  __shared__ double s_y[kDensityWarps][32][W + 1];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  const int lm = lane % W, grp = lane / W;
+  const int k = lane % W, grp = lane / W;
   const bool owner = lane < G * W;
+  // the lane's harmonic (l, m) and the lane holding the mirrored real harmonic (l, -m)
+  int l = 0;
+  while ((l + 1) * (l + 1) <= k) ++l;
+  const int cc = l * l + l, m = k - cc;
+  const int partner = lane - k + (cc - m);
+  const double inv2 = 0.70710678118654752440084436210484903;
+  const double sgn = (m > 0 && (m & 1)) ? -1.0 : 1.0;
   const int nout = nmax * W;
   const int64_t row0 = row_off[0];
   const int64_t warp = blockIdx.x * int64_t(kDensityWarps) + wib;
@@ -50,22 +62,22 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX, NMAXT>::value) ace_den
   for (int64_t a = warp; a < count; a += nwarps) {
     const int64_t i = center_begin + a;
     const int64_t b = row_off[a] - row0, e = row_off[a + 1] - row0;
-    double2 acc[NPL];
+    double acc[NPL];
 #pragma unroll
-    for (int k = 0; k < NPL; ++k) acc[k] = make_double2(0.0, 0.0);
+    for (int t = 0; t < NPL; ++t) acc[t] = 0.0;
     for (int64_t c0 = b; c0 < e; c0 += 32) {
       const int nedge = (e - c0) < 32 ? int(e - c0) : 32;
       if (lane < nedge) {
         const int64_t j = nbr[c0 + lane];
         double rv[NMAXT + 1];
-        double2 yc[W];
+        double v[W];
         double p = 0.0;
         if (j < 0 || j >= N) {
           if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
 #pragma unroll
-          for (int k = 0; k <= NMAXT; ++k) rv[k] = 0.0;
+          for (int t = 0; t <= NMAXT; ++t) rv[t] = 0.0;
 #pragma unroll
-          for (int k = 0; k < W; ++k) yc[k] = make_double2(0.0, 0.0);
+          for (int t = 0; t < W; ++t) v[t] = 0.0;
         } else {
           double d[3];
           min_image(pos, i, j, box, d);
@@ -74,49 +86,41 @@ __global__ void __launch_bounds__(32 * DensityWarps<LMAX, NMAXT>::value) ace_den
           p = (zj >= 0 && zj < S) ? pref[zj] : 0.0;
           radial_basis<double>(r, rc, lam, NMAXT, rv, nullptr);
           const double sr = r > 1e-12 ? r : 1e-12;
-          double v[W];
           real_sh_unit<double, LMAX>(d[0] / sr, d[1] / sr, d[2] / sr, nrm, v, nullptr);
-          const double inv2 = 0.70710678118654752440084436210484903;
-#pragma unroll
-          for (int l = 0; l <= LMAX; ++l) {
-            const int c = l * l + l;
-            yc[c] = make_double2(v[c], 0.0);
-#pragma unroll
-            for (int m = 1; m <= l; ++m) {
-              const double sg = (m & 1) ? -1.0 : 1.0;
-              yc[c - m] = make_double2(inv2 * v[c + m], inv2 * v[c - m]);
-              yc[c + m] = make_double2(sg * (inv2 * v[c + m]), sg * (inv2 * -v[c - m]));
-            }
-          }
         }
 #pragma unroll
         for (int n = 0; n < NMAXT; ++n) s_rad[wib][lane][n] = p * rv[n + 1];
 #pragma unroll
-        for (int k = 0; k < W; ++k) s_y[wib][lane][k] = yc[k];
+        for (int t = 0; t < W; ++t) s_y[wib][lane][t] = v[t];
       }
       __syncwarp();
       if (owner) {
         for (int q = 0; q < nedge; ++q) {
-          const double2 y = s_y[wib][q][lm];
+          const double y = s_y[wib][q][k];
 #pragma unroll
-          for (int k = 0; k < NPL; ++k) {
-            const int n = grp + G * k;
-            if (n < NMAXT) {
-              const double rp = s_rad[wib][q][n];
-              acc[k].x += rp * y.x;
-              acc[k].y += rp * y.y;
-            }
+          for (int t = 0; t < NPL; ++t) {
+            const int n = grp + G * t;
+            if (n < NMAXT) acc[t] = fma(s_rad[wib][q][n], y, acc[t]);
           }
         }
       }
       __syncwarp();
     }
-    if (owner) {
-      double2* Ai = A + a * int64_t(nout);
+    double2* Ai = A + a * int64_t(nout);
 #pragma unroll
-      for (int k = 0; k < NPL; ++k) {
-        const int n = grp + G * k;
-        if (n < nmax) Ai[n * W + lm] = acc[k];
+    for (int t = 0; t < NPL; ++t) {
+      const double other = __shfl_sync(0xffffffffu, acc[t], partner < 32 ? partner : lane);
+      const int n = grp + G * t;
+      if (owner && n < nmax) {
+        double2 out;
+        if (m == 0) {
+          out = make_double2(acc[t], 0.0);
+        } else if (m < 0) {  // (Y_{l,|m|} + i Y_{l,-|m|}) / sqrt 2
+          out = make_double2(inv2 * other, inv2 * acc[t]);
+        } else {             // (-1)^m (Y_{l,m} - i Y_{l,-m}) / sqrt 2
+          out = make_double2(sgn * (inv2 * acc[t]), -sgn * (inv2 * other));
+        }
+        Ai[n * W + k] = out;
       }
     }
   }

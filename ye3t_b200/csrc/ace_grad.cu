@@ -997,19 +997,42 @@ __global__ void __launch_bounds__(32 * ClassWarps<CLS>::value, 1) ace_grad_kerne
 constexpr int kEdgeWarps = 4;
 
 template <int LMAX, int NMAXT>
-__global__ void __launch_bounds__(32 * kEdgeWarps) ace_edge_grad_kernel(
+__global__ void __launch_bounds__(32 * kEdgeWarps, 3) ace_edge_grad_kernel(
     const double* __restrict__ pos, const int32_t* __restrict__ species, int64_t N, int64_t center_begin,
     int64_t count, double box, const int64_t* __restrict__ row_off, const int32_t* __restrict__ nbr,
     const double* __restrict__ pref, int64_t S, int nmax, double rc, double lam, ShNorm nrm,
     const double2* __restrict__ dEdA, double* __restrict__ edge_grad, int32_t* status) {
   constexpr int W = (LMAX + 1) * (LMAX + 1);
-  __shared__ double2 sG[kEdgeWarps][NMAXT * W];
+  // dE/dA of the centre folded into the real-harmonic basis: with Yc_lm = sum_k
+  // T[lm, k] Y_k (Yc_{l,0} = Y_{l,0}; Yc_{l,-m} = (Y_{l,m} + i Y_{l,-m}) / sqrt 2;
+  // Yc_{l,m} = (-1)^m (Y_{l,m} - i Y_{l,-m}) / sqrt 2), sum_lm Re(G[n, lm] Yc_lm) =
+  // sum_k Gr[n, k] Y_k with Gr[n, k] = Re(sum_lm G[n, lm] T[lm, k]), so every edge
+  // contracts real channels (half the multiply-adds of the complex form)
+  __shared__ double sG[kEdgeWarps][NMAXT * W];
+  __shared__ double2 sGc[kEdgeWarps][NMAXT * W];  // the centre's dE/dA row as read
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int na = nmax * W;
   const int64_t row0 = row_off[0];
+  const double inv2 = 0.70710678118654752440084436210484903;
   for (int64_t c = blockIdx.x * int64_t(kEdgeWarps) + wib; c < count; c += int64_t(gridDim.x) * kEdgeWarps) {
     const int64_t i = center_begin + c;
-    for (int k = lane; k < NMAXT * W; k += 32) sG[wib][k] = k < na ? dEdA[c * na + k] : make_double2(0.0, 0.0);
+    for (int q = lane; q < NMAXT * W; q += 32) sGc[wib][q] = q < na ? dEdA[c * na + q] : make_double2(0.0, 0.0);
+    __syncwarp();
+    for (int q = lane; q < NMAXT * W; q += 32) {
+      const int n = q / W, k = q - n * W;
+      const int l = int(sqrtf(float(k)));
+      const int cc = l * l + l, m = k - cc, am = m < 0 ? -m : m;
+      const double2* Gn = sGc[wib] + n * W;
+      double gr;
+      if (m == 0) {
+        gr = Gn[cc].x;
+      } else {
+        const double sg = (am & 1) ? -1.0 : 1.0;
+        const double2 gm = Gn[cc - am], gp = Gn[cc + am];
+        gr = m > 0 ? inv2 * (gm.x + sg * gp.x) : inv2 * (sg * gp.y - gm.y);
+      }
+      sG[wib][q] = gr;
+    }
     __syncwarp();
     const int64_t b = row_off[c] - row0, e_end = row_off[c + 1] - row0;
     for (int64_t e = b + lane; e < e_end; e += 32) {
@@ -1035,22 +1058,19 @@ __global__ void __launch_bounds__(32 * kEdgeWarps) ace_edge_grad_kernel(
         // reciprocal and a product per entry
         const double inv_sr = 1.0 / sr;
         double acc_r = 0.0, acc_v[3] = {0.0, 0.0, 0.0};
-        const double inv2 = 0.70710678118654752440084436210484903;
-        // one complex harmonic column lm with its gradient: add
-        // Re(Q_lm Yc_lm) and Re(P_lm grad Yc_lm)
-        auto column = [&](int lm, double yr, double yi, const double (&dr)[3], const double (&di)[3]) {
-          double2 P = make_double2(0.0, 0.0), Q = make_double2(0.0, 0.0);
+        // one real harmonic k with its gradient: add Q_k Y_k and P_k grad Y_k with
+        // P_k = sum_n R_n Gr[n, k], Q_k = sum_n R'_n Gr[n, k]
+        auto column = [&](int k, double y, const double (&dy)[3]) {
+          double P = 0.0, Q = 0.0;
 #pragma unroll
           for (int n = 0; n < NMAXT; ++n) {
-            const double2 Gv = sG[wib][n * W + lm];
-            P.x = fma(rv[n + 1], Gv.x, P.x);
-            P.y = fma(rv[n + 1], Gv.y, P.y);
-            Q.x = fma(rd[n + 1], Gv.x, Q.x);
-            Q.y = fma(rd[n + 1], Gv.y, Q.y);
+            const double gv = sG[wib][n * W + k];
+            P = fma(rv[n + 1], gv, P);
+            Q = fma(rd[n + 1], gv, Q);
           }
-          acc_r += Q.x * yr - Q.y * yi;
+          acc_r = fma(Q, y, acc_r);
 #pragma unroll
-          for (int ax = 0; ax < 3; ++ax) acc_v[ax] += P.x * dr[ax] - P.y * di[ax];
+          for (int ax = 0; ax < 3; ++ax) acc_v[ax] = fma(P, dy[ax], acc_v[ax]);
         };
 #pragma unroll
         for (int l = 0; l <= LMAX; ++l) {
@@ -1065,27 +1085,8 @@ __global__ void __launch_bounds__(32 * kEdgeWarps) ace_edge_grad_kernel(
 #pragma unroll
               for (int ax = 0; ax < 3; ++ax) g[h][ax] = (g[h][ax] - gu * u[ax]) * inv_sr;
             }
-            // complex harmonics and gradients from the real pair
-            // (Yc_{l,-m} = (R_{+m} + i R_{-m}) / sqrt2, Yc_{l,+m} = (-1)^m (R_{+m} - i R_{-m}) / sqrt2)
-            if (m == 0) {
-              const double dr[3] = {g[0][0], g[0][1], g[0][2]}, di[3] = {0.0, 0.0, 0.0};
-              column(cidx, v[0], 0.0, dr, di);
-            } else {
-              const double sg = (m & 1) ? -1.0 : 1.0;
-              double dr[3], di[3];
-#pragma unroll
-              for (int ax = 0; ax < 3; ++ax) {
-                dr[ax] = inv2 * g[0][ax];
-                di[ax] = inv2 * g[1][ax];
-              }
-              column(cidx - m, inv2 * v[0], inv2 * v[1], dr, di);
-#pragma unroll
-              for (int ax = 0; ax < 3; ++ax) {
-                dr[ax] = sg * (inv2 * g[0][ax]);
-                di[ax] = sg * (inv2 * -g[1][ax]);
-              }
-              column(cidx + m, sg * (inv2 * v[0]), sg * (inv2 * -v[1]), dr, di);
-            }
+            column(cidx + m, v[0], g[0]);
+            if (m > 0) column(cidx - m, v[1], g[1]);
           }
         }
         gx = p * (acc_r * u[0] + acc_v[0]);

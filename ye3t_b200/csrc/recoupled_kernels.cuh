@@ -770,8 +770,9 @@ __device__ __forceinline__ void dmma_m8n8k4(double& d0, double& d1, double a, do
 // imaginary) in acc[M].  STAGED: the CTA's one species' weights come from the
 // ring; otherwise each species among the CTA's atoms takes its own step with
 // its weights read from global memory and the I values of the other species'
-// atoms set to zero.  A quad of columns outside the pass is skipped and sets
-// bad (the columns are the same for every lane of the warp).
+// atoms set to zero.  Each lane reads its own column of the stage; one outside
+// the pass sets bad and is replaced by column 0, so every read stays inside the
+// component region.
 template <bool STAGED, int LM1, int NA>
 __device__ __forceinline__ void tile_walk_mma(const TileTabs& tt, int q0, int nq, int nc, const double* sId,
                                               const double* const (&kw)[NA], const int (&za)[NA],
@@ -780,18 +781,22 @@ __device__ __forceinline__ void tile_walk_mma(const TileTabs& tt, int q0, int nq
   const int lane = threadIdx.x & 31;
   const int kk = lane & 3, row = lane >> 2;
   const int ab = lane >> 3, part = (lane >> 2) & 1;  // the lane's I value: atom, real/imaginary
+  const double* sIl = sId + ab * 2 + part;            // I[c + M] of this lane at sIl[2 NA (c + M)]
+  const int lim = nc - LM1;                           // a column c needs c + LM1 <= nc
   int zb = za[0];
 #pragma unroll
   for (int s = 1; s < NA; ++s)
     if (ab == s) zb = za[s];
+  // the lane's share of a stage copy: lanes 0-15 16 bytes of weights, lane 16 the columns
+  const bool wl = STAGED && lane < 16, cl = lane == 16;
+  const bool copier = wl || cl;
+  const char* src = wl ? reinterpret_cast<const char*>(kw[0] + 2 * lane)
+                       : reinterpret_cast<const char*>(tt.col_comp + q0);
+  const int64_t src_step = wl ? int64_t(R) * 4 * 8 : 16;  // bytes per stage
+  const int dst_off = wl ? 16 + 16 * lane : 0;
   auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
-    unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
-    if (Q < nq) {
-      if (STAGED && lane < 16)
-        cp_async16(st + 16 + 16 * lane, kw[0] + int64_t(R) * 4 * Q + 2 * lane);
-      else if (lane == 16)
-        cp_async16(st, tt.col_comp + q0 + 4 * Q);
-    }
+    if (copier && Q < nq)
+      cp_async16(ring + (Q & (kTileStages - 1)) * kStageBytes + dst_off, src + int64_t(Q) * src_step);
     cp_async_commit();
   };
 #pragma unroll
@@ -799,30 +804,27 @@ __device__ __forceinline__ void tile_walk_mma(const TileTabs& tt, int q0, int nq
   for (int Q = 0; Q < nq; ++Q) {
     cp_async_wait<kTileStages - 1>();
     __syncwarp();
-    const unsigned char* st = ring + (Q % kTileStages) * kStageBytes;
-    const int4 c4 = *reinterpret_cast<const int4*>(st);
-    const int cmin = min(min(c4.x, c4.y), min(c4.z, c4.w)), cmax = max(max(c4.x, c4.y), max(c4.z, c4.w));
-    if (cmin < 0 || cmax + LM1 > nc) {
-      bad = true;
+    const unsigned char* st = ring + (Q & (kTileStages - 1)) * kStageBytes;
+    const int col = reinterpret_cast<const int*>(st)[kk];
+    // a column outside the pass sets bad and reads column 0 instead
+    const bool ok = col >= 0 && col <= lim;
+    bad = bad || !ok;
+    const double* bI = sIl + (ok ? col : 0) * (2 * NA);
+    if (STAGED) {
+      const double av = reinterpret_cast<const double*>(st + 16)[kk * R + row];
+#pragma unroll
+      for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, bI[2 * NA * M]);
     } else {
-      const int col = kk == 0 ? c4.x : (kk == 1 ? c4.y : (kk == 2 ? c4.z : c4.w));
-      const double* bI = sId + (col * NA + ab) * 2 + part;  // I[col + M] at bI[2 NA M]
-      if (STAGED) {
-        const double av = reinterpret_cast<const double*>(st + 16)[kk * R + row];
 #pragma unroll
-        for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, bI[2 * NA * M]);
-      } else {
+      for (int s = 0; s < NA; ++s) {
+        bool first = true;
 #pragma unroll
-        for (int s = 0; s < NA; ++s) {
-          bool first = true;
+        for (int j = 0; j < s; ++j) first = first && za[j] != za[s];
+        if (!first) continue;  // uniform over the warp
+        const double av = __ldg(kw[s] + int64_t(R) * (4 * Q + kk) + row);
+        const bool on = zb == za[s];
 #pragma unroll
-          for (int j = 0; j < s; ++j) first = first && za[j] != za[s];
-          if (!first) continue;  // uniform over the warp
-          const double av = __ldg(kw[s] + int64_t(R) * (4 * Q + kk) + row);
-          const bool on = zb == za[s];
-#pragma unroll
-          for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, on ? bI[2 * NA * M] : 0.0);
-        }
+        for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, on ? bI[2 * NA * M] : 0.0);
       }
     }
     __syncwarp();

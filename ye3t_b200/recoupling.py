@@ -745,6 +745,21 @@ class RecoupledTiles:
             raise ValueError("packed back-propagation record outside its pass or row")
 
 
+def _parity_interleave(cols, off, base) -> list:
+    """A tile's columns ordered so that consecutive columns alternate between even and odd
+    component indices while both remain: the kernel reads the 4 columns of a step as 64-byte
+    rows of shared memory, and rows of one parity share a half of the banks."""
+    even = [c for c in cols if (int(off[c]) - base) % 2 == 0]
+    odd = [c for c in cols if (int(off[c]) - base) % 2 == 1]
+    out = []
+    while even or odd:
+        if even:
+            out.append(even.pop(0))
+        if odd:
+            out.append(odd.pop(0))
+    return out
+
+
 def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> RecoupledTiles:
     if rows < 1 or rows > 32:
         raise ValueError("rows per tile must be in [1, 32]")
@@ -784,7 +799,7 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
         order = sorted(range(len(tiles)), key=lambda i: (-len(cols_of[i]), i))
         base = int(sym.pass_begin[L])
         for i in order:
-            t, cols = tiles[i], cols_of[i]
+            t, cols = tiles[i], _parity_interleave(cols_of[i], off, base)
             n = len(cols)
             npad = (n + TILE_STEP - 1) // TILE_STEP * TILE_STEP if n else 0
             q0 = col_begin[-1]
