@@ -578,9 +578,9 @@ typedef struct {
   const int32_t* bp_pack;        /* [pack_count, 4], 16-byte aligned */
   /* step-2 work units per pass: (tile, first step, end step, kind), kind -1 a
    * whole tile, -2 the first column chunk of a cut tile, s >= 0 a later
-   * chunk whose sums go to scratch slot s (slots of 512 * min(L + 1, 8)
-   * bytes, scratch_slots * 512 bytes in all); fix (tile, first slot, slot
-   * count, 0) adds a cut tile's later chunks in slot order */
+   * chunk whose sums go to scratch slot s (slots of 512 * (L + 1) bytes,
+   * scratch_slots * 512 bytes in all); fix (tile, first slot, slot count, 0)
+   * adds a cut tile's later chunks in slot order */
   int64_t unit_count;
   int64_t fix_count;
   int32_t scratch_slots;

@@ -727,14 +727,16 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
   }
 }
 
-// Per-warp staging ring of step 2: each stage holds four column steps of the
-// warp's current tile, their column offsets (16 bytes) and the weights of all
-// rows (4 x 8 doubles) for the species of the CTA's first atom, copied from
-// global memory kTileStages stages ahead of their use so that the weights' L2
-// latency overlaps the arithmetic.  A lane whose atom has another species
-// (rare in species-sorted groups) reads its weights from global memory.
-constexpr int kTileStages = 8;
-constexpr int kStageBytes = 16 + 4 * 8 * 8;
+// Per-warp staging ring of step 2: each stage holds eight column steps (two
+// k = 4 steps of the tile product) of the warp's current unit, their column
+// offsets (32 bytes) and the weights of all rows (8 x 8 doubles) for the
+// species of the CTA's first atom, copied from global memory kTileStages
+// stages ahead of their use so that the weights' L2 latency overlaps the
+// arithmetic.  A CTA whose atoms have several species reads each species'
+// weights from global memory instead.
+constexpr int kTileStages = 4;
+constexpr int kStageSteps = 8;
+constexpr int kStageBytes = 4 * kStageSteps + kStageSteps * 8 * 8;
 
 // One FP64 tensor-core step D = A B + C of shape m8n8k4 (mma.sync: tcgen05 has
 // no FP64 kind, so this is the FP64 matrix path of sm_100).  Fragments of lane
@@ -783,35 +785,33 @@ __device__ __forceinline__ void tile_walk_mma(const TileTabs& tt, int q0, int nq
   const int ab = lane >> 3, part = (lane >> 2) & 1;  // the lane's I value: atom, real/imaginary
   const double* sIl = sId + ab * 2 + part;            // I[c + M] of this lane at sIl[2 NA (c + M)]
   const int lim = nc - LM1;                           // a column c needs c + LM1 <= nc
+  const int ns = (nq + 1) >> 1;                       // stages of two quads
   int zb = za[0];
 #pragma unroll
   for (int s = 1; s < NA; ++s)
     if (ab == s) zb = za[s];
-  // the lane's share of a stage copy: lanes 0-15 16 bytes of weights, lane 16 the columns
-  const bool wl = STAGED && lane < 16, cl = lane == 16;
-  const bool copier = wl || cl;
-  const char* src = wl ? reinterpret_cast<const char*>(kw[0] + 2 * lane)
-                       : reinterpret_cast<const char*>(tt.col_comp + q0);
-  const int64_t src_step = wl ? int64_t(R) * 4 * 8 : 16;  // bytes per stage
-  const int dst_off = wl ? 16 + 16 * lane : 0;
-  auto issue = [&](int Q) {  // stage of steps 4Q .. 4Q + 3 (every lane commits a group)
-    if (copier && Q < nq)
-      cp_async16(ring + (Q & (kTileStages - 1)) * kStageBytes + dst_off, src + int64_t(Q) * src_step);
+  // the lane's share of a stage copy: 16 bytes of weights (lane < 16 for the
+  // stage's first quad, lane >= 16 for its second), and lanes 0 / 1 the columns
+  // of the first / second quad
+  const int half = lane >> 4;
+  const char* wsrc = reinterpret_cast<const char*>(kw[0] + 2 * lane);
+  const char* csrc = reinterpret_cast<const char*>(tt.col_comp + q0 + 4 * (lane & 1));
+  auto issue = [&](int Q) {  // stage Q: quads 2Q and 2Q + 1 (every lane commits a group)
+    unsigned char* st = ring + (Q & (kTileStages - 1)) * kStageBytes;
+    if (STAGED && 2 * Q + half < nq)
+      cp_async16(st + 4 * kStageSteps + 16 * lane, wsrc + int64_t(Q) * (R * kStageSteps * 8));
+    if (lane < 2 && 2 * Q + lane < nq) cp_async16(st + 16 * lane, csrc + int64_t(Q) * (4 * kStageSteps));
     cp_async_commit();
   };
-#pragma unroll
-  for (int s = 0; s < kTileStages; ++s) issue(s);
-  for (int Q = 0; Q < nq; ++Q) {
-    cp_async_wait<kTileStages - 1>();
-    __syncwarp();
-    const unsigned char* st = ring + (Q & (kTileStages - 1)) * kStageBytes;
-    const int col = reinterpret_cast<const int*>(st)[kk];
-    // a column outside the pass sets bad and reads column 0 instead
+  // one k = 4 step: quad h of the stage
+  auto kstep = [&](const unsigned char* st, int Q, int h) {
+    const int col = reinterpret_cast<const int*>(st)[4 * h + kk];
+    // a column outside the pass sets bad and is replaced by column 0
     const bool ok = col >= 0 && col <= lim;
     bad = bad || !ok;
     const double* bI = sIl + (ok ? col : 0) * (2 * NA);
     if (STAGED) {
-      const double av = reinterpret_cast<const double*>(st + 16)[kk * R + row];
+      const double av = reinterpret_cast<const double*>(st + 4 * kStageSteps)[(4 * h + kk) * R + row];
 #pragma unroll
       for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, bI[2 * NA * M]);
     } else {
@@ -821,12 +821,21 @@ __device__ __forceinline__ void tile_walk_mma(const TileTabs& tt, int q0, int nq
 #pragma unroll
         for (int j = 0; j < s; ++j) first = first && za[j] != za[s];
         if (!first) continue;  // uniform over the warp
-        const double av = __ldg(kw[s] + int64_t(R) * (4 * Q + kk) + row);
+        const double av = __ldg(kw[s] + int64_t(R) * (kStageSteps * Q + 4 * h + kk) + row);
         const bool on = zb == za[s];
 #pragma unroll
         for (int M = 0; M < LM1; ++M) dmma_m8n8k4(acc[M][0], acc[M][1], av, on ? bI[2 * NA * M] : 0.0);
       }
     }
+  };
+#pragma unroll
+  for (int s = 0; s < kTileStages; ++s) issue(s);
+  for (int Q = 0; Q < ns; ++Q) {
+    cp_async_wait<kTileStages - 1>();
+    __syncwarp();
+    const unsigned char* st = ring + (Q & (kTileStages - 1)) * kStageBytes;
+    kstep(st, Q, 0);
+    if (2 * Q + 1 < nq) kstep(st, Q, 1);  // uniform over the warp
     __syncwarp();
     issue(Q + kTileStages);
   }

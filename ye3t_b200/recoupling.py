@@ -731,7 +731,7 @@ class RecoupledTiles:
             raise ValueError("fix_begin does not partition the fix-ups")
         fx = self.fix.astype(np.int64)
         Lf = np.repeat(np.arange(P), np.diff(fb))
-        mc = np.minimum(np.arange(P) + 1, 8)
+        mc = np.arange(P) + 1
         if fx.size and (np.any(fx[:, 1] < 0) or np.any(fx[:, 2] < 1) or
                         np.any((fx[:, 1] + fx[:, 2]) * mc[Lf] > self.scratch_slots)):
             raise ValueError("fix-up outside the scratch")
