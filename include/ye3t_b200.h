@@ -314,24 +314,29 @@ int y3b_ace_density_mixed(int dtype, const double* positions, const int32_t* spe
                           int64_t species_count, int64_t channel_count, int64_t nmax, int64_t lmax,
                           double cutoff, double lambda, void* A, int32_t* status, void* stream);
 
-/* The same A-basis in fp32 with the mixing on the tensor cores (tcgen05,
- * kind::tf32 with a 3xTF32 split): per centre and neighbour species the edge
- * sums S[i, lm, z, n] = sum_{z_j = z} R_n Yc_lm (CUDA cores), then
- * A[i, c, lm] = sum_{z, n} W[z_i, z, c, n] S[i, lm, z, n] as a product of 128
- * rows (i, lm, part) by every centre species' table at once.  mixing is f32
- * [S, S, C, nmax]; A is complex64 [center_count, C, (lmax+1)^2].  Supported:
- * lmax <= 4, nmax <= 16, C a multiple of 16, S * nmax <= 64, S * C <= 256,
- * else Y3B_ERR_UNSUPPORTED (use y3b_ace_density_mixed).  The workspace (16-byte
- * aligned) holds S for a chunk of centres; the full size is
- * y3b_ace_density_mixed_tc_workspace_bytes, a smaller one runs in chunks (at
- * least one centre).  Bad indices set Y3B_STATUS_INDEX_RANGE and give 0. */
-int64_t y3b_ace_density_mixed_tc_workspace_bytes(int64_t center_count, int64_t species_count, int64_t nmax,
-                                                 int64_t lmax);
-int y3b_ace_density_mixed_tc(const double* positions, const int32_t* species, int64_t atom_count,
-                             int64_t center_begin, int64_t center_count, double box, const int64_t* row_offsets,
-                             const int32_t* neighbors, const float* mixing, int64_t species_count,
-                             int64_t channel_count, int64_t nmax, int64_t lmax, double cutoff, double lambda,
-                             void* workspace, int64_t workspace_bytes, void* A, int32_t* status, void* stream);
+/* The same A-basis with the mixing as a matrix product on the tensor cores:
+ * per centre and neighbour species the edge sums S[i, lm, z, n] = sum_{z_j = z}
+ * R_n Yc_lm (CUDA cores, in the real-harmonic basis), then A[i, c, lm] =
+ * sum_{z, n} W[z_i, z, c, n] S[i, lm, z, n].  dtype F32: tcgen05 kind::tf32
+ * with a 3xTF32 split, 128 rows (i, lm, part) by every centre species' table at
+ * once (needs C a multiple of 16, S * nmax <= 64, S * C <= 256); F64: FP64
+ * mma.sync m8n8k4 (tcgen05 has no FP64 kind; needs C a multiple of 8 up to
+ * 64).  Both need lmax <= 4 and nmax <= 16, else Y3B_ERR_UNSUPPORTED (use
+ * y3b_ace_density_mixed).  mixing is [S, S, C, nmax] in dtype; A is complex64
+ * / complex128 [center_count, C, (lmax+1)^2].  The workspace (16-byte aligned)
+ * holds S for a chunk of centres; the full size is
+ * y3b_ace_density_mixed_split_workspace_bytes (-1 for an unsupported shape), a
+ * smaller one runs in chunks (at least one centre).  Bad indices set
+ * Y3B_STATUS_INDEX_RANGE and give 0; a tensor-core wait that runs out sets
+ * Y3B_STATUS_TIMEOUT. */
+int64_t y3b_ace_density_mixed_split_workspace_bytes(int dtype, int64_t center_count, int64_t species_count,
+                                                    int64_t channel_count, int64_t nmax, int64_t lmax);
+int y3b_ace_density_mixed_split(int dtype, const double* positions, const int32_t* species, int64_t atom_count,
+                                int64_t center_begin, int64_t center_count, double box,
+                                const int64_t* row_offsets, const int32_t* neighbors, const void* mixing,
+                                int64_t species_count, int64_t channel_count, int64_t nmax, int64_t lmax,
+                                double cutoff, double lambda, void* workspace, int64_t workspace_bytes, void* A,
+                                int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------
  * Fused ACE evaluation over a packed multi-word bundle.

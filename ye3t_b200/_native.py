@@ -132,9 +132,9 @@ _SIGS = {
     "y3b_radial_channel_contraction": (ctypes.c_int, [ctypes.c_int, VP, VP, VP, I64, I64, I64, VP, VP, VP]),
     "y3b_ace_density_mixed": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64,
                                              I64, DBL, DBL, VP, VP, VP]),
-    "y3b_ace_density_mixed_tc_workspace_bytes": (I64, [I64, I64, I64, I64]),
-    "y3b_ace_density_mixed_tc": (ctypes.c_int, [VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64, I64, I64, DBL, DBL,
-                                                VP, I64, VP, VP, VP]),
+    "y3b_ace_density_mixed_split_workspace_bytes": (I64, [ctypes.c_int, I64, I64, I64, I64, I64]),
+    "y3b_ace_density_mixed_split": (ctypes.c_int, [ctypes.c_int, VP, VP, I64, I64, I64, DBL, VP, VP, VP, I64, I64,
+                                                   I64, I64, DBL, DBL, VP, I64, VP, VP, VP]),
     "y3b_ace_energy_grad": (ctypes.c_int, [ctypes.POINTER(AceTables), VP, I64, VP, VP, I64, VP, VP, VP, VP]),
     "y3b_ace_recoupled_energy_grad": (ctypes.c_int, [ctypes.POINTER(RecoupledTables), VP, I64, VP, VP, I64, VP,
                                                      VP, VP, VP]),

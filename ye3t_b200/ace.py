@@ -105,11 +105,15 @@ class ACEEvaluator:
         return nat.stream_of(self.device)
 
     def mixing_on_tensor_cores(self, species_count: int, channel_count: int, nmax: int, dtype) -> bool:
-        """Whether ``density_mixed`` runs this shape on the tensor cores by default (fp32,
-        l_max <= 4, n_max <= 16, C a multiple of 16, S * n_max <= 64, S * C <= 256)."""
-        S, C = int(species_count), int(channel_count)
-        return (dtype == torch.float32 and self.bundle.lmax <= 4 and int(nmax) <= 16 and C % 16 == 0
-                and -(-S * int(nmax) // 8) * 8 <= 64 and -(-S * C // 16) * 16 <= 256)
+        """Whether ``density_mixed`` runs the mixing of this shape as a tensor-core product by
+        default: fp32 (tcgen05, 3xTF32) needs C a multiple of 16, S * n_max <= 64 and
+        S * C <= 256; fp64 (FP64 mma.sync) C a multiple of 8 up to 64; both l_max <= 4 and
+        n_max <= 16."""
+        code = nat.F64 if dtype == torch.float64 else (nat.F32 if dtype == torch.float32 else None)
+        if code is None:
+            return False
+        return int(nat.lib().y3b_ace_density_mixed_split_workspace_bytes(
+            code, 1, int(species_count), int(channel_count), int(nmax), self.bundle.lmax)) > 0
 
     def _workspace(self, nbytes: int) -> torch.Tensor:
         """A device scratch buffer of at least ``nbytes`` (kept and grown between calls)."""
@@ -208,10 +212,11 @@ class ACEEvaluator:
 
         ``mixing [S, S, C, nmax]``: channel c of a pair (z_i, z_j) is
         ``sum_n mixing[z_i, z_j, c, n-1] R_n``.  ``dtype`` float64 gives
-        complex128, float32 complex64 (computed in that precision).  In fp32 the
-        mixing runs on the tensor cores (``y3b_ace_density_mixed_tc``) wherever
-        its shape allows (``tensor_cores`` None); True requires that path, False
-        uses the per-edge CUDA-core kernel.
+        complex128, float32 complex64 (computed in that precision).  The mixing runs
+        as a tensor-core product after per-species edge sums
+        (``y3b_ace_density_mixed_split``: tcgen05 in fp32, FP64 mma.sync in fp64)
+        wherever its shape allows (``tensor_cores`` None); True requires that path,
+        False uses the fused per-edge CUDA-core kernel.
         """
         pos = positions.to(self.device, torch.float64).contiguous()
         sp = species.to(self.device, torch.int32).contiguous()
@@ -224,16 +229,18 @@ class ACEEvaluator:
         S, C, nmax = W.shape[0], W.shape[2], W.shape[3]
         tc_ok = self.mixing_on_tensor_cores(S, C, nmax, dtype)
         if tensor_cores and not tc_ok:
-            raise ValueError("the tensor-core mixing needs fp32, lmax <= 4, nmax <= 16, C a multiple of 16, "
-                             "S * nmax <= 64 and S * C <= 256")
+            raise ValueError("the tensor-core mixing needs l_max <= 4, n_max <= 16 and (fp32) C a multiple of 16, "
+                             "S * n_max <= 64, S * C <= 256 or (fp64) C a multiple of 8 up to 64")
         if tc_ok and tensor_cores is not False:
-            need = int(nat.lib().y3b_ace_density_mixed_tc_workspace_bytes(count, S, nmax, self.bundle.lmax))
+            code = nat.dtype_code(dtype)
+            need = int(nat.lib().y3b_ace_density_mixed_split_workspace_bytes(code, count, S, C, nmax,
+                                                                            self.bundle.lmax))
             ws = self._workspace(min(need, 1 << 30))
-            nat.check(nat.lib().y3b_ace_density_mixed_tc(
-                pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box), row_offsets.data_ptr(),
-                neighbors.data_ptr(), W.data_ptr(), S, C, nmax, self.bundle.lmax, float(self.config.cutoff),
-                float(self.config.radial_lambda), ws.data_ptr(), ws.numel(), A.data_ptr(), nat.ptr(status),
-                self._stream()), "ace_density_mixed_tc")
+            nat.check(nat.lib().y3b_ace_density_mixed_split(
+                code, pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box),
+                row_offsets.data_ptr(), neighbors.data_ptr(), W.data_ptr(), S, C, nmax, self.bundle.lmax,
+                float(self.config.cutoff), float(self.config.radial_lambda), ws.data_ptr(), ws.numel(), A.data_ptr(),
+                nat.ptr(status), self._stream()), "ace_density_mixed_split")
             return A
         nat.check(nat.lib().y3b_ace_density_mixed(
             nat.dtype_code(dtype), pos.data_ptr(), sp.data_ptr(), pos.shape[0], int(begin), count, float(box),

@@ -42,39 +42,40 @@ constexpr int kWaitLimit = 1 << 22;   // polls of an mbarrier before the kernel 
 // shared memory across the chunks of rows longer than 32 edges.  The complex
 // harmonics are fixed combinations of the real ones (Yc_{l,0} = Y_{l,0};
 // Yc_{l,-m} = (Y_{l,m} + i Y_{l,-m}) / sqrt 2; Yc_{l,m} = (-1)^m (Y_{l,m} -
-// i Y_{l,-m}) / sqrt 2), so the complex rows (a, lm, part) of Kp floats (column
+// i Y_{l,-m}) / sqrt 2), so the complex rows (a, lm, part) of Kp values (column
 // z * nmax + n, zero padded) are formed from the summed real rows as they are
-// written out, consecutive lanes on consecutive floats.
-template <int LMAX>
+// written out, consecutive lanes on consecutive values.
+template <typename T, int LMAX>
 __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
     const double* __restrict__ pos, const int32_t* __restrict__ species, int64_t N, int64_t center_begin,
     int64_t a_begin, int64_t a_count, double box, const int64_t* __restrict__ row_off,
-    const int32_t* __restrict__ nbr, int S, int nmax, int Kp, float rc, float lam, ShNorm nrm,
-    float* __restrict__ Sout, int32_t* status) {
+    const int32_t* __restrict__ nbr, int S, int nmax, int Kp, T rc, T lam, ShNorm nrm,
+    T* __restrict__ Sout, int32_t* status) {
   constexpr int W = (LMAX + 1) * (LMAX + 1);
   constexpr int W2 = 2 * W;
   constexpr int G = 32 / W;
   constexpr int NPL = (kTcMaxRadial + G - 1) / G;  // radial indices per lane
   constexpr int RS = kTcMaxRadial + 4;             // radial row (16-byte multiple)
-  __shared__ __align__(16) float s_r[kSpWarps][32 * RS];
-  __shared__ float s_y[kSpWarps][32 * W];
+  __shared__ __align__(16) T s_r[kSpWarps][32 * RS];
+  __shared__ T s_y[kSpWarps][32 * W];
   __shared__ int s_z[kSpWarps][32];
-  extern __shared__ float s_rows[];  // [warp][W][Kp + 1], real basis
+  extern __shared__ __align__(16) unsigned char sp_dyn[];
+  T* s_rows = reinterpret_cast<T*>(sp_dyn);  // [warp][W][Kp + 1], real basis
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  float* r_w = s_r[wib];
-  float* y_w = s_y[wib];
+  T* r_w = s_r[wib];
+  T* y_w = s_y[wib];
   int* z_w = s_z[wib];
   const int KS = Kp + 1;
-  float* o_w = s_rows + wib * W * KS;
+  T* o_w = s_rows + wib * W * KS;
   const int k = lane % W, g = lane / W;
   const bool owner = lane < G * W;
   const int64_t row0 = row_off[0];
-  const float inv2 = 0.70710678118654752440f;
+  const T inv2 = T(0.70710678118654752440084436210484903);
   for (int64_t al = blockIdx.x * int64_t(kSpWarps) + wib; al < a_count; al += int64_t(gridDim.x) * kSpWarps) {
     const int64_t a = a_begin + al;  // index within the centre range
     const int64_t i = center_begin + a;
     const int64_t b = row_off[a] - row0, e = row_off[a + 1] - row0;
-    for (int u = lane; u < W * KS; u += 32) o_w[u] = 0.0f;
+    for (int u = lane; u < W * KS; u += 32) o_w[u] = T(0);
     __syncwarp();
     for (int64_t c0 = b; c0 < e; c0 += 32) {
       const int nedge = (e - c0) < 32 ? int(e - c0) : 32;
@@ -88,14 +89,14 @@ __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
           double dd[3];
           min_image(pos, i, j, box, dd);
           const double r2 = dist2(dd);
-          const float d[3] = {float(dd[0]), float(dd[1]), float(dd[2])};
-          const float r = sqrtf(float(r2));
-          float rv[kTcMaxRadial + 1];
-          radial_basis<float>(r, rc, lam, nmax, rv, nullptr);
+          const T d[3] = {T(dd[0]), T(dd[1]), T(dd[2])};
+          const T r = sqrt(T(r2));
+          T rv[kTcMaxRadial + 1];
+          radial_basis<T>(r, rc, lam, nmax, rv, nullptr);
           for (int n = 0; n < nmax; ++n) r_w[lane * RS + n] = rv[n + 1];
-          const float sr = r > 1e-12f ? r : 1e-12f;
-          float v[W];
-          real_sh_unit<float, LMAX>(d[0] / sr, d[1] / sr, d[2] / sr, nrm, v, nullptr);
+          const T sr = r > T(1e-12) ? r : T(1e-12);
+          T v[W];
+          real_sh_unit<T, LMAX>(d[0] / sr, d[1] / sr, d[2] / sr, nrm, v, nullptr);
 #pragma unroll
           for (int q = 0; q < W; ++q) y_w[lane * W + q] = v[q];
           z_w[lane] = zj;
@@ -103,29 +104,29 @@ __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
       }
       __syncwarp();
       for (int z = 0; z < S; ++z) {
-        float acc[NPL];
+        T acc[NPL];
 #pragma unroll
-        for (int t = 0; t < NPL; ++t) acc[t] = 0.0f;
+        for (int t = 0; t < NPL; ++t) acc[t] = T(0);
         for (int q = 0; q < nedge; ++q) {
           if (z_w[q] != z) continue;  // uniform over the warp
-          const float y = y_w[q * W + k];
-          const float* rq = r_w + q * RS;
-          if constexpr (G == 1) {
+          const T y = y_w[q * W + k];
+          const T* rq = r_w + q * RS;
+          if constexpr (G == 1 && sizeof(T) == 4) {
 #pragma unroll
             for (int t = 0; t < NPL; t += 4) {
               if (t < nmax) {
                 const float4 r4 = *reinterpret_cast<const float4*>(rq + t);
-                acc[t] = fmaf(r4.x, y, acc[t]);
-                acc[t + 1] = fmaf(r4.y, y, acc[t + 1]);
-                acc[t + 2] = fmaf(r4.z, y, acc[t + 2]);
-                acc[t + 3] = fmaf(r4.w, y, acc[t + 3]);
+                acc[t] = fma(T(r4.x), y, acc[t]);
+                acc[t + 1] = fma(T(r4.y), y, acc[t + 1]);
+                acc[t + 2] = fma(T(r4.z), y, acc[t + 2]);
+                acc[t + 3] = fma(T(r4.w), y, acc[t + 3]);
               }
             }
           } else {
 #pragma unroll
             for (int t = 0; t < NPL; ++t) {
               const int n = g + t * G;
-              if (n < nmax) acc[t] = fmaf(rq[n], y, acc[t]);
+              if (n < nmax) acc[t] = fma(rq[n], y, acc[t]);
             }
           }
         }
@@ -139,20 +140,20 @@ __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
       }
       __syncwarp();
     }
-    float* So = Sout + al * int64_t(W2) * Kp;
+    T* So = Sout + al * int64_t(W2) * Kp;
     for (int u = lane; u < W2 * Kp; u += 32) {
       const int row = u / Kp, col = u - row * Kp;
       const int lm = row >> 1, part = row & 1;
       int l = 0;
       while ((l + 1) * (l + 1) <= lm) ++l;
       const int m = lm - l * l - l, cc = l * l + l, am = m < 0 ? -m : m;
-      float val;
+      T val;
       if (m == 0) {
-        val = part ? 0.0f : o_w[cc * KS + col];
+        val = part ? T(0) : o_w[cc * KS + col];
       } else {
-        const float sg = (m > 0 && (am & 1)) ? -1.0f : 1.0f;
+        const T sg = (m > 0 && (am & 1)) ? T(-1) : T(1);
         // m < 0: (Y_{l,|m|} + i Y_{l,-|m|}) / sqrt 2; m > 0: (-1)^m (Y_{l,m} - i Y_{l,-m}) / sqrt 2
-        val = part ? (m < 0 ? 1.0f : -1.0f) * sg * inv2 * o_w[(cc - am) * KS + col]
+        val = part ? (m < 0 ? T(1) : T(-1)) * sg * inv2 * o_w[(cc - am) * KS + col]
                    : sg * inv2 * o_w[(cc + am) * KS + col];
       }
       So[u] = val;
@@ -363,6 +364,82 @@ __global__ void __launch_bounds__(kTcThreads) mixing_tf32_kernel(
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(tmem_cols) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Mixing product in fp64 on the FP64 tensor cores (mma.sync m8n8k4; tcgen05 has
+// no FP64 kind).  A warp takes 8 rows (a, lm, part) of one centre (a centre's rows
+// padded to a multiple of 8) and the C channels of the centre's species: per K step
+// of 4, the A fragment S[row l/4][4 ks + l%4] (global memory, through L1) and for
+// each block of 8 channels the B fragment W[z_i][k][c] from shared memory (rows of
+// C + 8 doubles, so that the four k rows of a fragment fall in two halves of the
+// banks); lane l ends with D[row l/4][c = 8 nb + 2 (l%4) + {0, 1}].
+constexpr int kF64Warps = 8;
+constexpr int kF64MaxNB = 8;  // C <= 64
+
+__device__ __forceinline__ void dmma_f64(double& d0, double& d1, double a, double b) {
+  asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};\n"
+      : "+d"(d0), "+d"(d1)
+      : "d"(a), "d"(b));
+}
+
+__global__ void __launch_bounds__(32 * kF64Warps) mixing_f64_kernel(
+    const double* __restrict__ Sin, int64_t atom_count, int W2, int Kp, const double* __restrict__ mix, int S, int C,
+    int nmax, const int32_t* __restrict__ species, double* __restrict__ A, int32_t* status) {
+  extern __shared__ __align__(16) unsigned char f64_smem[];
+  double* sW = reinterpret_cast<double*>(f64_smem);  // [s][k][C + 8]
+  const int CS = C + 8;
+  for (int u = threadIdx.x; u < S * Kp * C; u += blockDim.x) {
+    const int sz = u / (Kp * C), rem = u - sz * Kp * C, k = rem / C, c = rem - k * C;
+    double v = 0.0;
+    if (k < S * nmax) {
+      const int z = k / nmax, n = k - z * nmax;
+      v = mix[((int64_t(sz) * S + z) * C + c) * nmax + n];
+    }
+    sW[(sz * Kp + k) * CS + c] = v;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int kk = lane & 3, r = lane >> 2;
+  const int RB = (W2 + 7) / 8;  // row blocks per centre
+  const int64_t tasks = atom_count * RB;
+  const int nbs = C / 8;
+  for (int64_t task = blockIdx.x * int64_t(kF64Warps) + warp; task < tasks;
+       task += int64_t(gridDim.x) * kF64Warps) {
+    const int64_t a = task / RB;
+    const int rb = int(task - a * RB);
+    int zi = species[a];
+    const bool zok = zi >= 0 && zi < S;
+    if (!zok) {
+      if (status && lane == 0 && rb == 0) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
+      zi = 0;
+    }
+    const int row = rb * 8 + r;
+    const bool rok = row < W2;
+    const double* Srow = Sin + (a * W2 + (rok ? row : 0)) * Kp + kk;
+    const double* Wz = sW + (int64_t(zi) * Kp + kk) * CS + r;  // B[k = 4 ks + kk][c = 8 nb + r]
+    double acc[kF64MaxNB][2];
+#pragma unroll
+    for (int nb = 0; nb < kF64MaxNB; ++nb) acc[nb][0] = acc[nb][1] = 0.0;
+    for (int ks = 0; ks < Kp / 4; ++ks) {
+      const double av = rok ? Srow[4 * ks] : 0.0;
+      const double* Wk = Wz + 4 * ks * CS;
+#pragma unroll
+      for (int nb = 0; nb < kF64MaxNB; ++nb)
+        if (nb < nbs) dmma_f64(acc[nb][0], acc[nb][1], av, Wk[8 * nb]);  // uniform over the warp
+    }
+    if (rok) {
+      double* Ao = A + a * int64_t(C) * W2 + row;
+#pragma unroll
+      for (int nb = 0; nb < kF64MaxNB; ++nb) {
+        if (nb < nbs) {
+          const int c = 8 * nb + 2 * kk;
+          Ao[int64_t(c) * W2] = zok ? acc[nb][0] : 0.0;
+          Ao[int64_t(c + 1) * W2] = zok ? acc[nb][1] : 0.0;
+        }
+      }
+    }
+  }
+}
+
 int tc_dims(int64_t S, int64_t C, int64_t nmax, int64_t lmax, int& Kp, int& Np, int& cols) {
   Kp = int((S * nmax + 7) / 8 * 8);
   Np = int((S * C + 15) / 16 * 16);
@@ -379,75 +456,130 @@ int tc_dims(int64_t S, int64_t C, int64_t nmax, int64_t lmax, int& Kp, int& Np, 
 
 using namespace y3b;
 
-extern "C" int64_t y3b_ace_density_mixed_tc_workspace_bytes(int64_t center_count, int64_t species_count,
-                                                            int64_t nmax, int64_t lmax) {
-  if (center_count < 0 || species_count < 1 || nmax < 1 || lmax < 0) return -1;
-  const int64_t Kp = (species_count * nmax + 7) / 8 * 8;
-  return center_count * 2 * (lmax + 1) * (lmax + 1) * Kp * int64_t(sizeof(float));
+namespace y3b {
+namespace {
+
+int f64_dims(int64_t S, int64_t C, int64_t nmax, int64_t lmax, int& Kp) {
+  Kp = int((S * nmax + 3) / 4 * 4);
+  if (lmax < 0 || lmax > 4 || nmax < 1 || nmax > kTcMaxRadial || S < 1 || C < 8 || C % 8 || C > 8 * kF64MaxNB ||
+      size_t(S) * Kp * (C + 8) * sizeof(double) > 200 * 1024)
+    return -1;
+  return 0;
 }
 
-extern "C" int y3b_ace_density_mixed_tc(const double* positions, const int32_t* species, int64_t atom_count,
-                                        int64_t center_begin, int64_t center_count, double box,
-                                        const int64_t* row_offsets, const int32_t* neighbors, const float* mixing,
-                                        int64_t species_count, int64_t channel_count, int64_t nmax, int64_t lmax,
-                                        double cutoff, double lambda, void* workspace, int64_t workspace_bytes,
-                                        void* A, int32_t* status, void* stream) {
+int split_dims(int dtype, int64_t S, int64_t C, int64_t nmax, int64_t lmax, int& Kp, int& Np, int& cols) {
+  Np = cols = 0;
+  if (dtype == Y3B_F32) return tc_dims(S, C, nmax, lmax, Kp, Np, cols);
+  if (dtype == Y3B_F64) return f64_dims(S, C, nmax, lmax, Kp);
+  return -1;
+}
+
+}  // namespace
+}  // namespace y3b
+
+extern "C" int64_t y3b_ace_density_mixed_split_workspace_bytes(int dtype, int64_t center_count,
+                                                               int64_t species_count, int64_t channel_count,
+                                                               int64_t nmax, int64_t lmax) {
   int Kp = 0, Np = 0, cols = 0;
-  if (tc_dims(species_count, channel_count, nmax, lmax, Kp, Np, cols))
+  if (center_count < 0 || split_dims(dtype, species_count, channel_count, nmax, lmax, Kp, Np, cols)) return -1;
+  const int64_t real = dtype == Y3B_F64 ? 8 : 4;
+  return center_count * 2 * (lmax + 1) * (lmax + 1) * Kp * real;
+}
+
+extern "C" int y3b_ace_density_mixed_split(int dtype, const double* positions, const int32_t* species,
+                                           int64_t atom_count, int64_t center_begin, int64_t center_count,
+                                           double box, const int64_t* row_offsets, const int32_t* neighbors,
+                                           const void* mixing, int64_t species_count, int64_t channel_count,
+                                           int64_t nmax, int64_t lmax, double cutoff, double lambda,
+                                           void* workspace, int64_t workspace_bytes, void* A, int32_t* status,
+                                           void* stream) {
+  int Kp = 0, Np = 0, cols = 0;
+  Y3B_CHECK_ARG(dtype == Y3B_F32 || dtype == Y3B_F64, "ace_density_mixed_split: dtype must be F32 or F64");
+  if (split_dims(dtype, species_count, channel_count, nmax, lmax, Kp, Np, cols))
     return fail(Y3B_ERR_UNSUPPORTED,
-                "ace_density_mixed_tc: needs lmax <= 4, nmax <= %d, C a multiple of 16, S * nmax <= %d and "
-                "S * C <= %d",
-                kTcMaxRadial, kTcMaxK, kTcMaxN);
+                dtype == Y3B_F32
+                    ? "ace_density_mixed_split (fp32, tcgen05): needs lmax <= 4, nmax <= 16, C a multiple of 16, "
+                      "S * nmax <= 64 and S * C <= 256"
+                    : "ace_density_mixed_split (fp64): needs lmax <= 4, nmax <= 16, C a multiple of 8 up to 64 "
+                      "and S * Kp * (C + 8) doubles within 200 KB");
   Y3B_CHECK_ARG(center_begin >= 0 && center_count >= 0 && center_begin + center_count <= atom_count,
                 "bad centre range");
   Y3B_CHECK_ARG(box > 0 && cutoff > 0, "box and cutoff must be positive");
   if (center_count == 0) return Y3B_OK;
   Y3B_CHECK_ARG(positions && species && row_offsets && mixing && A && workspace, "null pointer argument");
   Y3B_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, "workspace must be 16-byte aligned");
+  const bool f64 = dtype == Y3B_F64;
+  const size_t real = f64 ? sizeof(double) : sizeof(float);
   const int W2 = int(2 * (lmax + 1) * (lmax + 1));
-  const int64_t per_atom = int64_t(W2) * Kp * int64_t(sizeof(float));
+  const int64_t per_atom = int64_t(W2) * Kp * int64_t(real);
   const int64_t chunk = workspace_bytes / per_atom;
-  if (chunk < 1) return fail(Y3B_ERR_WORKSPACE, "ace_density_mixed_tc: workspace below one atom (%lld bytes)",
-                             (long long)per_atom);
+  if (chunk < 1)
+    return fail(Y3B_ERR_WORKSPACE, "ace_density_mixed_split: workspace below one atom (%lld bytes)",
+                (long long)per_atom);
   const ShNorm nrm = make_sh_norm();
   cudaStream_t s = as_stream(stream);
-  // residency: at most 512 / cols CTAs per SM, so that every CTA's tensor memory fits
-  const size_t need = size_t(2 * kTcRows + 2 * Np) * Kp * sizeof(float);
-  const int per_sm = 512 / cols < 4 ? 512 / cols : 4;
-  const size_t floor_bytes = size_t(228 * 1024) / size_t(per_sm + 1) + 1024;
-  const size_t smem = need > floor_bytes ? need : floor_bytes;
-  Y3B_CHECK_ARG(smem <= 200 * 1024, "mixing operands need %zu bytes of shared memory", smem);
-  Y3B_CUDA_TRY(cudaFuncSetAttribute(mixing_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  float* Sbuf = static_cast<float*>(workspace);
-  float* Af = static_cast<float*>(A);
   const int C = int(channel_count), S = int(species_count);
+  // the product kernel's launch shape
+  size_t prod_smem = 0;
+  int per_sm = 1;
+  if (f64) {
+    prod_smem = size_t(S) * Kp * (C + 8) * sizeof(double);
+    per_sm = int(std::max<size_t>(1, std::min<size_t>(4, size_t(220 * 1024) / (prod_smem + 1024))));
+    Y3B_CUDA_TRY(cudaFuncSetAttribute(mixing_f64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(prod_smem)));
+  } else {
+    // residency: at most 512 / cols CTAs per SM, so that every CTA's tensor memory fits
+    const size_t need = size_t(2 * kTcRows + 2 * Np) * Kp * sizeof(float);
+    per_sm = 512 / cols < 4 ? 512 / cols : 4;
+    const size_t floor_bytes = size_t(228 * 1024) / size_t(per_sm + 1) + 1024;
+    prod_smem = need > floor_bytes ? need : floor_bytes;
+    Y3B_CHECK_ARG(prod_smem <= 200 * 1024, "mixing operands need %zu bytes of shared memory", prod_smem);
+    Y3B_CUDA_TRY(cudaFuncSetAttribute(mixing_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(prod_smem)));
+  }
   for (int64_t a0 = 0; a0 < center_count; a0 += chunk) {
     const int64_t n = center_count - a0 < chunk ? center_count - a0 : chunk;
     const int grid_s = int(std::min<int64_t>((n + kSpWarps - 1) / kSpWarps, int64_t(kSMs) * 32));
-    const size_t sp_smem = size_t(kSpWarps) * (W2 / 2) * (Kp + 1) * sizeof(float);
-#define Y3B_SP_CASE(L)                                                                                            \
-  case L:                                                                                                         \
-    Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_species_density_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                      int(sp_smem)));                                                             \
-    ace_species_density_kernel<L><<<grid_s, 32 * kSpWarps, sp_smem, s>>>(                                               \
-        positions, species, atom_count, center_begin, a0, n, box, row_offsets, neighbors, S, int(nmax), Kp,      \
-        float(cutoff), float(lambda), nrm, Sbuf, status);                                                         \
+    const size_t sp_smem = size_t(kSpWarps) * (W2 / 2) * (Kp + 1) * real;
+#define Y3B_SP_CASE(T, L)                                                                                     \
+  case L:                                                                                                     \
+    Y3B_CUDA_TRY(cudaFuncSetAttribute(ace_species_density_kernel<T, L>,                                       \
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, int(sp_smem)));            \
+    ace_species_density_kernel<T, L><<<grid_s, 32 * kSpWarps, sp_smem, s>>>(                                  \
+        positions, species, atom_count, center_begin, a0, n, box, row_offsets, neighbors, S, int(nmax), Kp,  \
+        T(cutoff), T(lambda), nrm, static_cast<T*>(workspace), status);                                       \
     break;
-    switch (lmax) {
-      Y3B_SP_CASE(0)
-      Y3B_SP_CASE(1)
-      Y3B_SP_CASE(2)
-      Y3B_SP_CASE(3)
-      Y3B_SP_CASE(4)
-      default:
-        return fail(Y3B_ERR_UNSUPPORTED, "ace_density_mixed_tc: lmax %lld not built (0..4)", (long long)lmax);
+#define Y3B_SP_L(T)                                                                                           \
+  switch (lmax) {                                                                                             \
+    Y3B_SP_CASE(T, 0)                                                                                         \
+    Y3B_SP_CASE(T, 1)                                                                                         \
+    Y3B_SP_CASE(T, 2)                                                                                         \
+    Y3B_SP_CASE(T, 3)                                                                                         \
+    Y3B_SP_CASE(T, 4)                                                                                         \
+    default:                                                                                                  \
+      return fail(Y3B_ERR_UNSUPPORTED, "ace_density_mixed_split: lmax %lld not built (0..4)", (long long)lmax); \
+  }
+    if (f64) {
+      Y3B_SP_L(double)
+    } else {
+      Y3B_SP_L(float)
     }
+#undef Y3B_SP_L
 #undef Y3B_SP_CASE
     Y3B_LAUNCH_CHECK();
-    const int64_t tiles = (n * W2 + kTcRows - 1) / kTcRows;
-    const int grid_t = int(std::min<int64_t>(tiles, int64_t(kSMs) * per_sm));
-    mixing_tf32_kernel<<<grid_t, kTcThreads, smem, s>>>(Sbuf, n, W2, Kp, mixing, S, C, int(nmax), Np, cols,
-                                                        species + center_begin + a0, Af + a0 * C * W2, status);
+    if (f64) {
+      const int64_t tasks = n * ((W2 + 7) / 8);
+      const int grid_t = int(std::min<int64_t>((tasks + kF64Warps - 1) / kF64Warps, int64_t(kSMs) * per_sm));
+      mixing_f64_kernel<<<grid_t, 32 * kF64Warps, prod_smem, s>>>(
+          static_cast<const double*>(workspace), n, W2, Kp, static_cast<const double*>(mixing), S, C, int(nmax),
+          species + center_begin + a0, static_cast<double*>(A) + a0 * C * W2, status);
+    } else {
+      const int64_t tiles = (n * W2 + kTcRows - 1) / kTcRows;
+      const int grid_t = int(std::min<int64_t>(tiles, int64_t(kSMs) * per_sm));
+      mixing_tf32_kernel<<<grid_t, kTcThreads, prod_smem, s>>>(
+          static_cast<const float*>(workspace), n, W2, Kp, static_cast<const float*>(mixing), S, C, int(nmax), Np,
+          cols, species + center_begin + a0, static_cast<float*>(A) + a0 * C * W2, status);
+    }
     Y3B_LAUNCH_CHECK();
   }
   return Y3B_OK;
