@@ -696,10 +696,14 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
   constexpr int NW = TH / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int a = lane % NA;
+  // the record of the lane's component in the warp's next group is loaded a group ahead
+  int4 dn = make_int4(-1, 0, 0, 0);
+  if (warp * R + lane / NA < nc) dn = __ldg(t.comp + 2 * (c0 + warp * R + lane / NA));
   for (int g = warp; g * R < nc; g += NW) {
     const int c = g * R + lane / NA;
+    const int4 d = dn;
+    if (c + NW * R < nc) dn = __ldg(t.comp + 2 * (c0 + c + NW * R));
     if (c >= nc) continue;
-    const int4 d = __ldg(t.comp + 2 * (c0 + c));
     double2 v = make_double2(d.x < 0 ? 1.0 : 0.0, 0.0);
     if (d.x < 0) {
     } else if (d.w == 0) {
