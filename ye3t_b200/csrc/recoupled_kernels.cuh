@@ -1085,13 +1085,13 @@ recoupled_sym_tiled_grad_kernel(SymTabs t, TileTabs tt, const double2* __restric
               continue;
             }
             double2 ga = make_double2(0.0, 0.0);
-            for (int e = e0 + j; e < e1; e += 4 * R) {  // four records in flight per lane
-              int4 recs[4];
+            for (int e = e0 + j; e < e1; e += 8 * R) {  // eight records in flight per lane
+              int4 recs[8];
 #pragma unroll
-              for (int u = 0; u < 4; ++u)
+              for (int u = 0; u < 8; ++u)
                 recs[u] = e + u * R < e1 ? __ldg(tt.bp_pack + e + u * R) : make_int4(0, -1, 0, 0);
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
+              for (int u = 0; u < 8; ++u) {
                 const int4 rec = recs[u];  // (code, other, value lo, value hi)
                 const int gi = rec.x >> 1;
                 const int o = rec.y;
