@@ -714,17 +714,27 @@ __device__ __forceinline__ void build_components_lanes(const SymTabs& t, const d
     } else if (d.z < 0 || int64_t(d.z) + d.w > t.cg_count || d.y < 0) {
       bad = true;
     } else {
-      for (int q = d.z; q < d.z + d.w; ++q) {
-        const int ix = __ldg(t.cg_index + q);
-        const int ia = d.x + (ix & 255), ib = d.y + (ix >> 8);
-        if (ia >= W || ib < 0 || ib >= W) {
-          bad = true;
-          continue;
+      for (int qb = d.z; qb < d.z + d.w; qb += 4) {  // four terms' table entries in flight
+        int ix[4];
+        double cv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const bool in = qb + u < d.z + d.w;
+          ix[u] = in ? __ldg(t.cg_index + qb + u) : 0;
+          cv[u] = in ? __ldg(t.cg_value + qb + u) : 0.0;
         }
-        const double cv = __ldg(t.cg_value + q);
-        const double2 p = rmul(sA[ia * NA + a], sA[ib * NA + a]);
-        v.x = fma(cv, p.x, v.x);
-        v.y = fma(cv, p.y, v.y);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (qb + u >= d.z + d.w) break;
+          const int ia = d.x + (ix[u] & 255), ib = d.y + (ix[u] >> 8);
+          if (ia >= W || ib < 0 || ib >= W) {
+            bad = true;
+            continue;
+          }
+          const double2 p = rmul(sA[ia * NA + a], sA[ib * NA + a]);
+          v.x = fma(cv[u], p.x, v.x);
+          v.y = fma(cv[u], p.y, v.y);
+        }
       }
     }
     sI[c * NA + a] = v;
