@@ -97,6 +97,16 @@ class ACEEvaluator:
                                                       symmetric=symmetric, tile_rows=rows)
         return self._recoupled[key]
 
+    def recoupled_features(self):
+        """The general recoupled passes used for fp64 features (built on first use; no readout
+        weights needed)."""
+        if "features" not in self._recoupled:
+            from .recoupling import RecoupledEvaluator, build_recoupled_plan
+            plan = next((r.plan for r in self._recoupled.values()), None) or build_recoupled_plan(self.bundle)
+            self._recoupled["features"] = RecoupledEvaluator(self.bundle, self.device, None, plan=plan,
+                                                             atoms_per_cta=1, threads_per_cta=256)
+        return self._recoupled["features"]
+
     @property
     def feature_count(self) -> int:
         return self.packed.feature_count
@@ -254,13 +264,25 @@ class ACEEvaluator:
         """B-basis features ``[n, feature_count]`` from the A-basis.
 
         complex128 A gives complex128 features; complex64 A is evaluated in
-        fp32 and gives complex64 features.
+        fp32 and gives complex64 features.  For a scalar bundle in fp64 with the
+        recoupled B-basis (the default) the features come from the recoupled
+        forward pass (``y3b_ace_recoupled_features``: each feature as its
+        contractions of coupled channel pairs, about half the time of the
+        term-level kernel at C2); otherwise from the term-level kernel.
         """
         dt = torch.complex64 if A.dtype == torch.complex64 else torch.complex128
         A = A.to(self.device, dt).contiguous()
         n = A.shape[0]
         if out is None:
             out = torch.empty((n, self.packed.feature_count), dtype=dt, device=self.device)
+        if self.b_basis == "recoupled" and dt == torch.complex128:
+            return self.recoupled_features().features(A, out=out)
+        return self._term_features(A, out)
+
+    def _term_features(self, A: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Features of contiguous device rows ``A`` into ``out`` by the term-level kernel."""
+        n = A.shape[0]
+        dt = A.dtype
         code = nat.C64 if dt == torch.complex64 else nat.C128
         nat.check(nat.lib().y3b_ace_features_typed(code, ctypes_ref(self._tables), A.data_ptr(), n, out.data_ptr(),
                                                    self._stream()), "ace_features")
@@ -276,7 +298,11 @@ class ACEEvaluator:
         if self.bundle.nmax != 1:
             raise ValueError("channel_features needs a channel-diagonal bundle (nmax == 1)")
         n, C, W = A.shape
-        out = self.features(A.reshape(n * C, 1, W))
+        dt = torch.complex64 if A.dtype == torch.complex64 else torch.complex128
+        rows = A.to(self.device, dt).reshape(n * C, 1, W).contiguous()
+        # the term-level kernel: on rows of one channel it is faster than the recoupled pass
+        out = torch.empty((n * C, self.packed.feature_count), dtype=dt, device=self.device)
+        self._term_features(rows, out)
         return out.reshape(n, C * self.packed.feature_count)
 
     def energy_from_density(self, A: torch.Tensor, species_centres: torch.Tensor,

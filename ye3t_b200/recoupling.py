@@ -1290,8 +1290,9 @@ class RecoupledEvaluator:
             e.data_ptr(), nat.ptr(status), nat.stream_of(self.device)), name)
         return e
 
-    def features(self, A, status=None):
-        """Features ``[n, feature_count]`` complex128 in the bundle's order (general passes only)."""
+    def features(self, A, status=None, out=None):
+        """Features ``[n, feature_count]`` complex128 in the bundle's order (general passes only),
+        into ``out`` when given (contiguous, complex128, that shape)."""
         import ctypes
 
         import torch
@@ -1300,7 +1301,11 @@ class RecoupledEvaluator:
             raise ValueError("features need the general passes (symmetric=False)")
         A = self._rows(A)
         n = A.shape[0]
-        F = torch.empty((n, self.tables.feature_count), dtype=torch.complex128, device=self.device)
+        shape = (n, self.tables.feature_count)
+        if out is not None and (tuple(out.shape) != shape or out.dtype != torch.complex128 or
+                                not out.is_contiguous() or out.device != self.device):
+            raise ValueError(f"out must be a contiguous complex128 tensor of shape {shape} on {self.device}")
+        F = out if out is not None else torch.empty(shape, dtype=torch.complex128, device=self.device)
         nat.check(nat.lib().y3b_ace_recoupled_features(
             ctypes.byref(self._c), A.data_ptr(), n, F.data_ptr(), nat.ptr(status), nat.stream_of(self.device)),
             "ace_recoupled_features")
