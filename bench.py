@@ -100,10 +100,21 @@ class ClockSampler:
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "25"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # wait (at most 3 s) for the first sample, so that a short timed region that starts
+        # right after this call is sampled from its beginning
+        deadline = time.time() + 3.0
+        while time.time() < deadline and self.proc.poll() is None:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.01)
 
     def stop(self):
         if self.proc is None:
@@ -371,6 +382,7 @@ def run_b200(args):
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    barrier()  # the ranks start the timed steps together (the samplers start at different times)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     marks = []
     t0.record()
@@ -608,6 +620,7 @@ def run_channels(args):
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    barrier()  # the ranks start the timed steps together (the samplers start at different times)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     marks = []
     t0.record()
