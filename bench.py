@@ -337,9 +337,10 @@ def run_b200(args):
     timers = {k: [] for k in stages}
     from ye3t_b200.packing import GRAD_CLASSES
     b_launches = 1 if rec is not None else GRAD_CLASSES
-    # our kernels per step: 6 neighbour-count, 1 fill, density, the B-basis
-    # pass(es), then edge gradients and the force gather/scatter
-    launches_per_step = 8 + (b_launches + 2 if forces else 1) + (1 if world > 1 and forces else 0)
+    # our kernels per step: 8 neighbour-count (cell binning and two two-launch prefix
+    # sums included), 1 fill, density, the B-basis pass(es), then edge gradients and the
+    # force gather/scatter
+    launches_per_step = 10 + (b_launches + 2 if forces else 1) + (1 if world > 1 and forces else 0)
 
     def step(record):
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)] if record else None
@@ -703,9 +704,9 @@ def run_channels(args):
         "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * (24 + 4),
                 "d2h_bytes_per_step": 8,
                 "note": "features stay on the device (sharded descriptor); a checksum is read back"},
-        # 7 neighbour-list launches, the mixed density (species sums + tensor-core product in
+        # 9 neighbour-list launches, the mixed density (species sums + tensor-core product in
         # fp32, one fused kernel in fp64), one feature launch per bundle
-        "gpu_launches": (7 + (2 if tc_mix else 1) + len(evs)) * args.steps,
+        "gpu_launches": (9 + (2 if tc_mix else 1) + len(evs)) * args.steps,
         "roofline": roof,
         "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
         "checksum": float(check.item()),
@@ -1016,7 +1017,7 @@ def run_c2(args):
                        "radial_lambda": LAMBDA, "l2": "feature output (614 MB) larger than L2"},
             "e2e": {"value": N / (e2e_ms * 1e-3), "unit": "atoms/s", "h2d_bytes_per_step": N * 28,
                     "d2h_bytes_per_step": N * ev.feature_count * 16},
-            "gpu_launches": 9 * args.steps,  # 7 neighbour-list, density, features
+            "gpu_launches": 11 * args.steps,  # 9 neighbour-list, density, features
             "roofline": roof, "stage_ms": {k: statistics.mean(v) for k, v in timers.items()},
             "clocks": clock_info, "cpu_baseline": cpu}
     print(json.dumps(line), flush=True)

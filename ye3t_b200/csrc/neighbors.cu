@@ -17,8 +17,12 @@ struct CellWorkspace {
   int32_t* cursor;      // [nc]
   int32_t* atom_cell;   // [N]
   int32_t* cell_atoms;  // [N]
+  int64_t* block_sums;  // [kScanBlocks]: segment totals of the prefix sums
   int64_t bytes;
 };
+
+constexpr int kScanBlocks = 256;   // segments of a prefix sum, one CTA each
+constexpr int kScanThreads = 256;
 
 inline int64_t al(int64_t x) { return (x + 255) & ~int64_t(255); }
 
@@ -30,6 +34,7 @@ inline CellWorkspace carve_cells(void* base, int64_t N, int64_t nc) {
   w.cursor = reinterpret_cast<int32_t*>(p + o); o += al(nc * 4);
   w.atom_cell = reinterpret_cast<int32_t*>(p + o); o += al(N * 4);
   w.cell_atoms = reinterpret_cast<int32_t*>(p + o); o += al(N * 4);
+  w.block_sums = reinterpret_cast<int64_t*>(p + o); o += al(kScanBlocks * 8);
   w.bytes = o;
   return w;
 }
@@ -177,26 +182,59 @@ __global__ void fill_neighbors_kernel(const double* __restrict__ pos, int64_t be
   }
 }
 
-__global__ void __launch_bounds__(1024) scan_i64_kernel(int64_t* __restrict__ a, int64_t n) {
-  __shared__ int64_t sums[1024];
-  const int t = threadIdx.x;
-  const int64_t chunk = (n + 1023) / 1024;
-  const int64_t b = t * chunk, e = min(n, b + chunk);
-  int64_t s = 0;
-  for (int64_t i = b; i < e; ++i) s += a[i];
-  sums[t] = s;
+// In-place inclusive prefix sum of n int64 values in two launches over kScanBlocks
+// segments of ceil(n / kScanBlocks) values: the segments' totals, then each segment
+// scanned in tiles of kScanThreads values (warp shuffles, then the warps' totals),
+// starting from the total of the segments before it.  Coalesced and exact.
+__device__ __forceinline__ int64_t block_inclusive_scan(int64_t v, int64_t* warp_tot, int64_t& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  if (lane == 31) warp_tot[warp] = v;
   __syncthreads();
-  for (int off = 1; off < 1024; off <<= 1) {
-    const int64_t v = t >= off ? sums[t - off] : 0;
-    __syncthreads();
-    sums[t] += v;
-    __syncthreads();
+  int64_t before = 0;
+  total = 0;
+  for (int w = 0; w < kScanThreads / 32; ++w) {
+    if (w < warp) before += warp_tot[w];
+    total += warp_tot[w];
   }
-  int64_t run = t > 0 ? sums[t - 1] : 0;
-  for (int64_t i = b; i < e; ++i) {
-    run += a[i];
-    a[i] = run;
+  __syncthreads();
+  return before + v;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_sums_kernel(const int64_t* __restrict__ a, int64_t n,
+                                                                 int64_t seg, int64_t* __restrict__ sums) {
+  __shared__ int64_t warp_tot[kScanThreads / 32];
+  const int64_t b = blockIdx.x * seg, e = b + seg < n ? b + seg : n;
+  int64_t s = 0;
+  for (int64_t i = b + threadIdx.x; i < e; i += kScanThreads) s += a[i];
+  int64_t total;
+  block_inclusive_scan(s, warp_tot, total);
+  if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(int64_t* __restrict__ a, int64_t n, int64_t seg,
+                                                                  const int64_t* __restrict__ sums) {
+  __shared__ int64_t warp_tot[kScanThreads / 32];
+  int64_t carry;  // the total of the segments before this one
+  block_inclusive_scan(threadIdx.x < blockIdx.x ? sums[threadIdx.x] : 0, warp_tot, carry);
+  const int64_t b = blockIdx.x * seg, e = b + seg < n ? b + seg : n;
+  for (int64_t t = b; t < e; t += kScanThreads) {
+    const int64_t i = t + threadIdx.x;
+    int64_t tile;
+    const int64_t v = block_inclusive_scan(i < e ? a[i] : 0, warp_tot, tile);
+    if (i < e) a[i] = carry + v;
+    carry += tile;
   }
+}
+
+void scan_i64(int64_t* a, int64_t n, int64_t* sums, cudaStream_t s) {
+  const int64_t seg = (n + kScanBlocks - 1) / kScanBlocks;
+  scan_sums_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(a, n, seg, sums);
+  scan_apply_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(a, n, seg, sums);
 }
 
 }  // namespace
@@ -256,7 +294,7 @@ int neighbor_count_impl(const double* positions, int64_t atom_count, int64_t cen
   assign_cells_kernel<<<grid_for(atom_count, 256), 256, 0, s>>>(
       positions, atom_count, box, n, zb, zc, w.atom_cell, reinterpret_cast<unsigned long long*>(w.cell_start));
   Y3B_LAUNCH_CHECK();
-  scan_i64_kernel<<<1, 1024, 0, s>>>(w.cell_start, nc + 1);
+  scan_i64(w.cell_start, nc + 1, w.block_sums, s);
   Y3B_LAUNCH_CHECK();
   fill_cells_kernel<<<grid_for(atom_count, 256), 256, 0, s>>>(atom_count, w.atom_cell, w.cell_start,
                                                               w.cursor, w.cell_atoms);
@@ -268,7 +306,7 @@ int neighbor_count_impl(const double* positions, int64_t atom_count, int64_t cen
       positions, center_begin, center_end, box, cutoff * cutoff, n, zb, zc, w.cell_start, w.cell_atoms,
       row_offsets, status);
   Y3B_LAUNCH_CHECK();
-  scan_i64_kernel<<<1, 1024, 0, s>>>(row_offsets, count + 1);
+  scan_i64(row_offsets, count + 1, w.block_sums, s);
   Y3B_LAUNCH_CHECK();
   return Y3B_OK;
 }
