@@ -321,7 +321,7 @@ int y3b_ace_density_mixed(int dtype, const double* positions, const int32_t* spe
  * with a 3xTF32 split, 128 rows (i, lm, part) by every centre species' table at
  * once (needs C a multiple of 16, S * nmax <= 64, S * C <= 256); F64: FP64
  * mma.sync m8n8k4 (tcgen05 has no FP64 kind; needs C a multiple of 8 up to
- * 64).  Both need lmax <= 4 and nmax <= 16, else Y3B_ERR_UNSUPPORTED (use
+ * 64 and S * nmax <= 64).  Both need lmax <= 4 and nmax <= 16, else Y3B_ERR_UNSUPPORTED (use
  * y3b_ace_density_mixed).  mixing is [S, S, C, nmax] in dtype; A is complex64
  * / complex128 [center_count, C, (lmax+1)^2].  The workspace (16-byte aligned)
  * holds S for a chunk of centres; the full size is

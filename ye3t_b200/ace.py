@@ -117,8 +117,8 @@ class ACEEvaluator:
     def mixing_on_tensor_cores(self, species_count: int, channel_count: int, nmax: int, dtype) -> bool:
         """Whether ``density_mixed`` runs the mixing of this shape as a tensor-core product by
         default: fp32 (tcgen05, 3xTF32) needs C a multiple of 16, S * n_max <= 64 and
-        S * C <= 256; fp64 (FP64 mma.sync) C a multiple of 8 up to 64; both l_max <= 4 and
-        n_max <= 16."""
+        S * C <= 256; fp64 (FP64 mma.sync) C a multiple of 8 up to 64 and S * n_max <= 64; both
+        l_max <= 4 and n_max <= 16."""
         code = nat.F64 if dtype == torch.float64 else (nat.F32 if dtype == torch.float32 else None)
         if code is None:
             return False
@@ -240,7 +240,7 @@ class ACEEvaluator:
         tc_ok = self.mixing_on_tensor_cores(S, C, nmax, dtype)
         if tensor_cores and not tc_ok:
             raise ValueError("the tensor-core mixing needs l_max <= 4, n_max <= 16 and (fp32) C a multiple of 16, "
-                             "S * n_max <= 64, S * C <= 256 or (fp64) C a multiple of 8 up to 64")
+                             "S * n_max <= 64, S * C <= 256 or (fp64) C a multiple of 8 up to 64 and S * n_max <= 64")
         if tc_ok and tensor_cores is not False:
             code = nat.dtype_code(dtype)
             need = int(nat.lib().y3b_ace_density_mixed_split_workspace_bytes(code, count, S, C, nmax,

@@ -419,12 +419,17 @@ __global__ void __launch_bounds__(32 * kF64Warps) mixing_f64_kernel(
     double acc[kF64MaxNB][2];
 #pragma unroll
     for (int nb = 0; nb < kF64MaxNB; ++nb) acc[nb][0] = acc[nb][1] = 0.0;
-    for (int ks = 0; ks < Kp / 4; ++ks) {
-      const double av = rok ? Srow[4 * ks] : 0.0;
+    // the lane's A fragments of every K step, loaded together ahead of the products
+    double av[kTcMaxK / 4];
+#pragma unroll
+    for (int ks = 0; ks < kTcMaxK / 4; ++ks) av[ks] = (rok && ks < Kp / 4) ? Srow[4 * ks] : 0.0;
+#pragma unroll
+    for (int ks = 0; ks < kTcMaxK / 4; ++ks) {
+      if (ks >= Kp / 4) break;  // uniform over the warp
       const double* Wk = Wz + 4 * ks * CS;
 #pragma unroll
       for (int nb = 0; nb < kF64MaxNB; ++nb)
-        if (nb < nbs) dmma_f64(acc[nb][0], acc[nb][1], av, Wk[8 * nb]);  // uniform over the warp
+        if (nb < nbs) dmma_f64(acc[nb][0], acc[nb][1], av[ks], Wk[8 * nb]);  // uniform over the warp
     }
     if (rok) {
       double* Ao = A + a * int64_t(C) * W2 + row;
@@ -462,6 +467,7 @@ namespace {
 int f64_dims(int64_t S, int64_t C, int64_t nmax, int64_t lmax, int& Kp) {
   Kp = int((S * nmax + 3) / 4 * 4);
   if (lmax < 0 || lmax > 4 || nmax < 1 || nmax > kTcMaxRadial || S < 1 || C < 8 || C % 8 || C > 8 * kF64MaxNB ||
+      Kp > kTcMaxK ||
       size_t(S) * Kp * (C + 8) * sizeof(double) > 200 * 1024)
     return -1;
   return 0;
