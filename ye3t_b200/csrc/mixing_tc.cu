@@ -35,10 +35,10 @@ constexpr int kWaitLimit = 1 << 22;   // polls of an mbarrier before the kernel 
 
 // ---------------------------------------------------------------------------
 // Species-split densities S: one warp per centre.  Pass 1: lanes over up to 32
-// edges form R_n, the real harmonics Y_k and the neighbour species in
-// warp-private shared memory.  Pass 2: lane (k, g) owns real harmonic k and every
+// edges form R_n and the real harmonics Y_k in warp-private shared memory (each
+// lane keeps its edge's species).  Pass 2: lane (k, g) owns real harmonic k and every
 // G-th radial index, G = 32 / (lmax+1)^2, and for each species sums the chunk's
-// edges of that species in CSR order into the centre's real-basis rows, kept in
+// edges of that species (a warp ballot) in CSR order into the centre's real-basis rows, kept in
 // shared memory across the chunks of rows longer than 32 edges.  The complex
 // harmonics are fixed combinations of the real ones (Yc_{l,0} = Y_{l,0};
 // Yc_{l,-m} = (Y_{l,m} + i Y_{l,-m}) / sqrt 2; Yc_{l,m} = (-1)^m (Y_{l,m} -
@@ -58,13 +58,11 @@ __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
   constexpr int RS = kTcMaxRadial + 4;             // radial row (16-byte multiple)
   __shared__ __align__(16) T s_r[kSpWarps][32 * RS];
   __shared__ T s_y[kSpWarps][32 * W];
-  __shared__ int s_z[kSpWarps][32];
   extern __shared__ __align__(16) unsigned char sp_dyn[];
   T* s_rows = reinterpret_cast<T*>(sp_dyn);  // [warp][W][Kp + 1], real basis
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   T* r_w = s_r[wib];
   T* y_w = s_y[wib];
-  int* z_w = s_z[wib];
   const int KS = Kp + 1;
   T* o_w = s_rows + wib * W * KS;
   const int k = lane % W, g = lane / W;
@@ -79,13 +77,14 @@ __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
     __syncwarp();
     for (int64_t c0 = b; c0 < e; c0 += 32) {
       const int nedge = (e - c0) < 32 ? int(e - c0) : 32;
+      int my_z = -1;  // the species of this lane's edge (-1: none or out of range)
       if (lane < nedge) {
         const int64_t j = nbr[c0 + lane];
         const int zj = (j >= 0 && j < N) ? species[j] : -1;
         if (j < 0 || j >= N || zj < 0 || zj >= S) {
           if (status) atomicOr(status, Y3B_STATUS_INDEX_RANGE);
-          z_w[lane] = -1;
         } else {
+          my_z = zj;
           double dd[3];
           min_image(pos, i, j, box, dd);
           const double r2 = dist2(dd);
@@ -99,7 +98,6 @@ __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
           real_sh_unit<T, LMAX>(d[0] / sr, d[1] / sr, d[2] / sr, nrm, v, nullptr);
 #pragma unroll
           for (int q = 0; q < W; ++q) y_w[lane * W + q] = v[q];
-          z_w[lane] = zj;
         }
       }
       __syncwarp();
@@ -107,8 +105,9 @@ __global__ void __launch_bounds__(32 * kSpWarps) ace_species_density_kernel(
         T acc[NPL];
 #pragma unroll
         for (int t = 0; t < NPL; ++t) acc[t] = T(0);
-        for (int q = 0; q < nedge; ++q) {
-          if (z_w[q] != z) continue;  // uniform over the warp
+        // the chunk's edges of species z, in CSR order (the same mask in every lane)
+        for (unsigned m = __ballot_sync(0xffffffffu, my_z == z); m != 0u; m &= m - 1u) {
+          const int q = __ffs(int(m)) - 1;
           const T y = y_w[q * W + k];
           const T* rq = r_w + q * RS;
           if constexpr (G == 1 && sizeof(T) == 4) {
