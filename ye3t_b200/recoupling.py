@@ -876,10 +876,12 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
     return tiles
 
 
-# Step-2 work units: warps per CTA the cuts aim at, and the scratch bytes a CTA
-# holds for the partial sums of cut tiles (a slot of a pass holds one chunk's
-# sums: 8 rows x (L + 1) components x 4 atoms, complex, 512 (L + 1) bytes).
-UNIT_WARPS = 16
+# Step-2 work units: the cuts aim at about two units for each of UNIT_WARPS warps (of
+# the CTA's 16: coarser units than one pair per warp need fewer cut tiles and fix-ups,
+# which measured 1 % faster at 8 than at 16 or 4), and the scratch bytes a CTA holds
+# for the partial sums of cut tiles (a slot of a pass holds one chunk's sums: 8 rows x
+# (L + 1) components x 4 atoms, complex, 512 (L + 1) bytes).
+UNIT_WARPS = 8
 SCRATCH_BYTES = 12 * 1024
 
 
