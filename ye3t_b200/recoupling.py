@@ -813,12 +813,12 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
         tile_begin.append(len(tile_row))
     dot_pos = np.asarray([(pos_of[(int(a), int(b))], pos_of[(int(b), int(a))])
                           for a, b in zip(plan.dot_a, plan.dot_b)], dtype=np.int64).reshape(-1, 2)
-    # back-propagation work items: the largest chunk (16, 12, 8 ... entries) whose item
-    # count still fits each pass's part buffer
+    # back-propagation work items: chunks of BP_CHUNK entries, doubled while a pass's item
+    # count would exceed its part buffer
     W = sym.row_width
     cwidth = max(sym.max_pass_components, W)
     bb = sym.bp_begin.astype(np.int64)
-    chunk = 16
+    chunk = BP_CHUNK
     while True:
         items_per_pass = [int(sum(max(1, -(-int(bb[L * W + t + 1] - bb[L * W + t]) // chunk)) if
                                   bb[L * W + t + 1] > bb[L * W + t] else 0 for t in range(W))) for L in range(P)]
@@ -883,6 +883,10 @@ def _tiles(plan: "RecoupledPlan", sym: RecoupledSymTables, rows: int) -> Recoupl
 # (L + 1) components x 4 atoms, complex, 512 (L + 1) bytes).
 UNIT_WARPS = 8
 SCRATCH_BYTES = 12 * 1024
+
+# Entries per back-propagation work item (step 3), doubled for a pass whose items
+# would not fit its part buffer; 16 measured faster than 8, 24 or 32.
+BP_CHUNK = 16
 
 
 def _plan_units(tiles: RecoupledTiles) -> None:
