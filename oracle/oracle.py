@@ -7,7 +7,8 @@ never by the ye3t_b200 product path.
 ``lib()`` loads the restatement (``ye3t_oracle.cpp``, built by ``make`` in this
 directory on first use); ``refcore()`` loads the reference's own runtime core
 compiled from its sources into ``_ref/`` (absent where the reference tree was
-not available at build time).
+not available at build time); ``refeval()`` imports the reference's compiled
+schedule evaluator (factorized_runtime.cpp, a torch extension) built there too.
 """
 
 from __future__ import annotations
@@ -22,6 +23,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB = None
 _REF = None
+_REFEVAL = None
 
 I64 = ctypes.c_int64
 VP = ctypes.c_void_p
@@ -59,6 +61,25 @@ def refcore() -> Optional[ctypes.CDLL]:
             return None
         _REF = ctypes.CDLL(path)
     return _REF
+
+
+def refeval():
+    """The reference's compiled schedule evaluator (``ye3t_factorized_ref``, whose
+    ``evaluate_factorized_schedule_cpu`` is factorized_runtime.cpp:426-548), or None if it
+    was not built."""
+    global _REFEVAL
+    if _REFEVAL is None:
+        path = os.path.join(HERE, "_ref", "ye3t_factorized_ref.so")
+        if not os.path.exists(path):
+            return None
+        import importlib.util
+
+        import torch  # noqa: F401  (the extension resolves its libtorch symbols through torch)
+        spec = importlib.util.spec_from_file_location("ye3t_factorized_ref", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        _REFEVAL = mod
+    return _REFEVAL
 
 
 def _c(a, dtype=None):
@@ -109,6 +130,46 @@ def symmetric_power_monomial(x, monomial_counts, output_offsets, monomial_values
     lib().yo_symmetric_power_monomial(ctypes.c_int(_DT[x.dtype]), _p(x2), I64(x2.shape[0]), I64(x2.shape[1]),
                                       _p(counts), _p(off), _p(vals), I64(out_dim), _p(out))
     return out.reshape(*lead, out_dim)
+
+
+def ref_symmetric_power_monomial(x, monomial_counts, output_offsets, monomial_values, threads=1):
+    """The reference core's own ``symmetric_power_monomial_forward`` (ye3t_runtime_core.h:1227),
+    real fp64, from the ``_ref`` build; the caller checks ``refcore()`` first."""
+    x = _c(x, np.float64)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    counts = _c(monomial_counts, np.int64)
+    off = _c(output_offsets, np.int64).reshape(-1)
+    vals = _c(monomial_values, np.float64).reshape(-1)
+    out_dim = off.shape[0] - 1
+    out = np.zeros((x2.shape[0], out_dim))
+    refcore().yr_symmetric_power_monomial_f64(_p(x2), I64(x2.shape[0]), I64(x2.shape[1]), _p(counts), _p(off),
+                                              _p(vals), I64(vals.shape[0]), I64(out_dim), _p(out),
+                                              ctypes.c_int(threads))
+    return out.reshape(*lead, out_dim)
+
+
+def ref_schedule_evaluate_record(block_values, record):
+    """A ``ScheduleRecord`` through the reference's compiled evaluator
+    (``evaluate_factorized_schedule_cpu``, factorized_runtime.cpp:426-548, on torch CPU
+    tensors), with the dtype rule of ``schedule_evaluate_record``; the caller checks
+    ``refeval()`` first.  The extension runs its batch loop under ``at::parallel_for``, so it
+    uses torch's intra-op threads (``torch.set_num_threads``)."""
+    import torch
+    bv = _c(block_values)
+    coeffs = record.coeffs
+    if not np.iscomplexobj(bv):
+        rc = record.real_coeffs()
+        if rc is None:
+            bv = bv.astype(np.complex128)
+        else:
+            coeffs = rc
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    out = refeval().evaluate_factorized_schedule_cpu(
+        t(bv), t(np.asarray(record.component_offsets, np.int64)),
+        t(np.asarray(record.component_label_index, np.int64)), t(record.block_m_indices()),
+        t(np.asarray(coeffs).astype(bv.dtype)), int(record.component_count), False)
+    return out.numpy()
 
 
 def symmetric_power_shared_monomial(x, monomial_counts, output_offsets, coefficient_terms, coefficient_values):

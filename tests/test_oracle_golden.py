@@ -153,6 +153,27 @@ def test_oracle_matches_reference_core_build():
     np.testing.assert_allclose(cd1, cd2, rtol=1e-11, atol=1e-12)
 
 
+def test_reference_evaluator_build_matches_oracle_and_golden(golden):
+    """The reference's compiled schedule evaluator and symmetric power, built from their
+    sources into oracle/_ref, give the quickstart golden (out_cpp, written by the reference's
+    own evaluate(backend="cpp")) and agree with the restatement, so the C1 CPU arm may time
+    either."""
+    if oracle.refeval() is None or oracle.refcore() is None:
+        pytest.skip("reference builds absent (make -C oracle ref)")
+    g = golden("quickstart")
+    rec = _record(g, "q_")
+    out = oracle.ref_schedule_evaluate_record(g["bv"], rec)
+    np.testing.assert_allclose(out, g["out_cpp"], rtol=1e-13, atol=1e-13)
+    np.testing.assert_allclose(out, oracle.schedule_evaluate_record(g["bv"], rec), rtol=1e-13, atol=1e-13)
+    b = ACEBundle.load(_bundle_path("ace_n8_l3_nu4_L0"))
+    t = b.sym_tables[(1, 2, 0, 0)]
+    x = np.random.default_rng(3).normal(size=(257, 3))
+    y = oracle.ref_symmetric_power_monomial(x, t.monomial_counts, t.output_offsets, t.monomial_value.real,
+                                            threads=2)
+    np.testing.assert_allclose(y, oracle.symmetric_power_monomial(x, t.monomial_counts, t.output_offsets,
+                                                                  t.monomial_value.real), rtol=1e-14, atol=1e-14)
+
+
 def _bundle_path(stem):
     import os
     return os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "ye3t_b200", "bundles",
